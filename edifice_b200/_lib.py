@@ -1,0 +1,67 @@
+"""ctypes binding of libedifice_b200.so (the C ABI in include/edifice_b200.h).
+
+The library is loaded from the package directory (built in-tree by
+``python -m edifice_b200.build``).  There is no fallback: if the library is
+missing or fails to load, every op raises.
+"""
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libedifice_b200.so")
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_f = ctypes.c_float
+_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes); every entry point declared in include/edifice_b200.h
+SIGNATURES = {
+    "edb_version": (ctypes.c_char_p, []),
+    "edb_status_string": (ctypes.c_char_p, [_i]),
+    "edb_get_device_errors": (_i, [ctypes.POINTER(ctypes.c_uint), _i]),
+    "edb_linear_scan_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "edb_linear_scan_bwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "edb_mingru_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "edb_mingru_bwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+}
+
+EDB_F32, EDB_BF16 = 0, 1
+
+_lib = None
+
+
+class EdbError(RuntimeError):
+    pass
+
+
+def load():
+    """Load the native library (once) and attach prototypes.  Raises if absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise EdbError("libedifice_b200.so not built (run `python -m edifice_b200.build`); "
+                       "there is no CPU fallback")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def status_string(st):
+    return load().edb_status_string(int(st)).decode()
+
+
+def check(st, what):
+    if st != 0:
+        raise EdbError("%s failed: %s (status %d)" % (what, status_string(st), st))
+
+
+def device_errors(clear=True):
+    flags = ctypes.c_uint(0)
+    check(load().edb_get_device_errors(ctypes.byref(flags), int(bool(clear))), "edb_get_device_errors")
+    return int(flags.value)

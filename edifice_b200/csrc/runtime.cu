@@ -1,0 +1,91 @@
+// runtime.cu -- library-wide host utilities of libedifice_b200.so: version and
+// status strings, the per-device error word, tensor-map encoding through the
+// runtime's driver entry point, and the per-device SM-count cache.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "edb_common.cuh"
+
+__device__ unsigned int g_edb_device_errors = 0;
+
+namespace edb {
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static std::once_flag g_encode_once;
+
+CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t rank, void* gaddr,
+                      const cuuint64_t* dims, const cuuint64_t* strides_bytes,
+                      const cuuint32_t* box, CUtensorMapSwizzle swizzle) {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (!g_encode) return CUDA_ERROR_NOT_SUPPORTED;
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    return g_encode(map, dtype, rank, gaddr, dims, strides_bytes, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+unsigned int* device_error_word() {
+    static unsigned int* cache[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!cache[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_edb_device_errors) == cudaSuccess)
+            cache[dev] = static_cast<unsigned int*>(p);
+    }
+    return cache[dev];
+}
+
+int sm_count() {
+    static int cache[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+            n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+}  // namespace edb
+
+extern "C" const char* edb_version(void) { return "edifice_b200 0.1 sm_100a"; }
+
+extern "C" const char* edb_status_string(int status) {
+    switch (status) {
+        case EDB_OK: return "ok";
+        case EDB_ERR_NULL_POINTER: return "null pointer argument";
+        case EDB_ERR_BAD_SHAPE: return "invalid shape";
+        case EDB_ERR_BAD_DTYPE: return "invalid dtype";
+        case EDB_ERR_MISALIGNED: return "pointer not aligned as required";
+        case EDB_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+        case EDB_ERR_UNSUPPORTED: return "configuration not supported";
+        case EDB_ERR_DEVICE_TIMEOUT: return "a bounded device wait gave up";
+        default:
+            if (status > 0 && status < 1000) return cudaGetErrorString((cudaError_t)status);
+            return "unknown status";
+    }
+}
+
+extern "C" int edb_get_device_errors(unsigned int* flags_out, int clear) {
+    if (!flags_out) return EDB_ERR_NULL_POINTER;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return (int)e;
+    e = cudaMemcpyFromSymbol(flags_out, g_edb_device_errors, sizeof(unsigned int));
+    if (e != cudaSuccess) return (int)e;
+    if (clear) {
+        unsigned int zero = 0;
+        e = cudaMemcpyToSymbol(g_edb_device_errors, &zero, sizeof(unsigned int));
+    }
+    return (int)e;
+}

@@ -1,0 +1,142 @@
+"""Host-side mirror of ``Edifice.CUDA.FusedScan`` for the fused sequence-mixing path.
+
+Same op names, argument meaning and error behaviour as the reference module
+(lib/edifice/cuda/fused_scan.ex), over torch CUDA tensors as the device-memory
+plumbing, calling libedifice_b200.so through its C ABI.  There is no fallback
+tier: a missing library, a CPU tensor or a failed launch raises, the way the
+reference's NIF tier raises ``"CUDA fused ... failed: reason"``
+(e.g. fused_scan.ex:2804-2806).
+
+Forward ops return new tensors; ``*_backward`` functions return the gradient
+tuple of the reference's backward dispatch; the ``*_fn`` autograd Functions
+reproduce the reference's ``custom_grad`` wiring (which inputs get gradients,
+and the sigmoid chain rule applied outside the kernel for MinGRU).
+"""
+import torch
+
+from . import _lib
+
+_DT = {torch.float32: _lib.EDB_F32, torch.bfloat16: _lib.EDB_BF16}
+
+
+def _dtype_code(t, what):
+    if t.dtype not in _DT:
+        raise _lib.EdbError("%s: unsupported dtype %s (f32 or bf16)" % (what, t.dtype))
+    return _DT[t.dtype]
+
+
+def _dev(*ts, what="op"):
+    for t in ts:
+        if t is not None and (not t.is_cuda or not t.is_contiguous()):
+            raise _lib.EdbError("%s: inputs must be contiguous CUDA tensors "
+                                "(there is no CPU path)" % what)
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _same(shape_a, shape_b, what):
+    if tuple(shape_a) != tuple(shape_b):
+        raise _lib.EdbError("%s: shape mismatch %s vs %s" % (what, tuple(shape_a), tuple(shape_b)))
+
+
+# ------------------------------------------------------------------ linear scan
+def linear_scan(a_vals, b_vals, h0=None):
+    """h_t = a_t * h_{t-1} + b_t, h_{-1} = h0 (zeros if None).  [B, L, H] -> [B, L, H].
+    Mirrors FusedScan.linear_scan/2 (fused_scan.ex:171-185)."""
+    _dev(a_vals, b_vals, h0, what="linear_scan")
+    _same(a_vals.shape, b_vals.shape, "linear_scan")
+    B, L, H = a_vals.shape
+    out = torch.empty_like(a_vals)
+    lib = _lib.load()
+    _lib.check(lib.edb_linear_scan_fwd(_dtype_code(a_vals, "linear_scan"), _p(a_vals), _p(b_vals),
+                                       _p(h0), _p(out), B, L, H, _stream()), "CUDA linear scan")
+    return out
+
+
+def linear_scan_backward(a_vals, h0, forward_out, grad_output):
+    """Returns (grad_a, grad_b, grad_h0).  Mirrors linear_scan_backward_dispatch/4
+    (fused_scan.ex:852-867); h0 None means zeros."""
+    _dev(a_vals, h0, forward_out, grad_output, what="linear_scan_backward")
+    B, L, H = a_vals.shape
+    ga, gb = torch.empty_like(a_vals), torch.empty_like(a_vals)
+    gh0 = torch.empty((B, H), dtype=a_vals.dtype, device=a_vals.device)
+    lib = _lib.load()
+    _lib.check(lib.edb_linear_scan_bwd(_dtype_code(a_vals, "linear_scan_backward"), _p(a_vals),
+                                       _p(h0), _p(forward_out), _p(grad_output), _p(ga), _p(gb),
+                                       _p(gh0), B, L, H, _stream()), "CUDA linear scan backward")
+    return ga, gb, gh0
+
+
+class LinearScanFn(torch.autograd.Function):
+    """custom_grad wiring of linear_scan_custom_call/2 (fused_scan.ex:834-850):
+    gradients flow to a_vals and b_vals."""
+
+    @staticmethod
+    def forward(ctx, a_vals, b_vals):
+        out = linear_scan(a_vals, b_vals)
+        ctx.save_for_backward(a_vals, out)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        a_vals, out = ctx.saved_tensors
+        ga, gb, _ = linear_scan_backward(a_vals, None, out, grad_output.contiguous())
+        return ga, gb
+
+
+# ------------------------------------------------------------------------ MinGRU
+def mingru_scan(z, candidates, h0=None):
+    """Kernel-level MinGRU on post-sigmoid gates: h = (1 - z) h + z c."""
+    _dev(z, candidates, h0, what="mingru")
+    _same(z.shape, candidates.shape, "mingru")
+    B, L, H = z.shape
+    out = torch.empty_like(z)
+    lib = _lib.load()
+    _lib.check(lib.edb_mingru_fwd(_dtype_code(z, "mingru"), _p(z), _p(candidates), _p(h0),
+                                  _p(out), B, L, H, _stream()), "CUDA fused MinGRU scan")
+    return out
+
+
+def mingru(gates, candidates):
+    """FusedScan.mingru/2 (fused_scan.ex:60-74): z = sigmoid(gates) is computed
+    outside the kernel (as the reference does on the XLA side, :2777), h0 = 0."""
+    return mingru_scan(torch.sigmoid(gates), candidates)
+
+
+def mingru_backward(z, candidates, h0, forward_out, grad_output):
+    """Returns (grad_z, grad_cand, grad_h0) w.r.t. post-sigmoid z.  Mirrors
+    mingru_backward_dispatch/5 (fused_scan.ex:530-545)."""
+    _dev(z, candidates, h0, forward_out, grad_output, what="mingru_backward")
+    B, L, H = z.shape
+    gz, gc = torch.empty_like(z), torch.empty_like(z)
+    gh0 = torch.empty((B, H), dtype=z.dtype, device=z.device)
+    lib = _lib.load()
+    _lib.check(lib.edb_mingru_bwd(_dtype_code(z, "mingru_backward"), _p(z), _p(candidates), _p(h0),
+                                  _p(forward_out), _p(grad_output), _p(gz), _p(gc), _p(gh0), B, L,
+                                  H, _stream()), "CUDA fused MinGRU scan backward")
+    return gz, gc, gh0
+
+
+class MinGRUFn(torch.autograd.Function):
+    """custom_grad wiring of mingru_custom_call/2 (fused_scan.ex:454-481):
+    gradients to the raw gates (sigmoid chain rule applied outside the kernel,
+    :477-479) and to the candidates."""
+
+    @staticmethod
+    def forward(ctx, gates, candidates):
+        z = torch.sigmoid(gates)
+        out = mingru_scan(z, candidates)
+        ctx.save_for_backward(z, candidates, out)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        z, cand, out = ctx.saved_tensors
+        gz, gc, _ = mingru_backward(z, cand, None, out, grad_output.contiguous())
+        return gz * z * (1 - z), gc

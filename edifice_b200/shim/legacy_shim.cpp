@@ -1,0 +1,55 @@
+// legacy_shim.cpp -- reference-named launch symbols forwarding to libedifice_b200.
+//
+// Built twice by edifice_b200/build.py: without EDB_SHIM_BF16 into
+// libedifice_cuda_kernels.so (f32 io) and with it into
+// libedifice_cuda_kernels_bf16.so (bf16 io), the two file names the
+// reference's NIF dlopen()s (c_src/edifice_cuda_nif.c:4052-4230).  The
+// concatenated backward outputs keep the reference's layouts.
+#include "edifice_b200.h"
+#include "edifice_cuda_kernels.h"
+
+namespace {
+#ifdef EDB_SHIM_BF16
+constexpr int kDtype = EDB_BF16;
+#else
+constexpr int kDtype = EDB_F32;
+#endif
+}  // namespace
+
+extern "C" {
+
+int fused_linear_scan_launch(cudaStream_t stream, const edb_io_t* a_vals, const edb_io_t* b_vals,
+                             const edb_io_t* h0, edb_io_t* output, int batch, int seq_len,
+                             int hidden) {
+    return edb_linear_scan_fwd(kDtype, a_vals, b_vals, h0, output, batch, seq_len, hidden,
+                               stream);
+}
+
+int fused_linear_scan_backward_launch(cudaStream_t stream, const edb_io_t* a_vals,
+                                      const edb_io_t* h0, const edb_io_t* forward_out,
+                                      const edb_io_t* grad_output, edb_io_t* output_concat,
+                                      int batch, int seq_len, int hidden) {
+    const long long bth = (long long)batch * seq_len * hidden;
+    return edb_linear_scan_bwd(kDtype, a_vals, h0, forward_out, grad_output, output_concat,
+                               output_concat + bth, output_concat + 2 * bth, batch, seq_len,
+                               hidden, stream);
+}
+
+int fused_mingru_scan_launch(cudaStream_t stream, const edb_io_t* gates,
+                             const edb_io_t* candidates, const edb_io_t* h0, edb_io_t* output,
+                             int batch, int seq_len, int hidden) {
+    return edb_mingru_fwd(kDtype, gates, candidates, h0, output, batch, seq_len, hidden, stream);
+}
+
+int fused_mingru_scan_backward_launch(cudaStream_t stream, const edb_io_t* z,
+                                      const edb_io_t* candidates, const edb_io_t* h0,
+                                      const edb_io_t* forward_out, const edb_io_t* grad_output,
+                                      edb_io_t* output_concat, int batch, int seq_len,
+                                      int hidden) {
+    const long long bth = (long long)batch * seq_len * hidden;
+    return edb_mingru_bwd(kDtype, z, candidates, h0, forward_out, grad_output, output_concat,
+                          output_concat + bth, output_concat + 2 * bth, batch, seq_len, hidden,
+                          stream);
+}
+
+}  // extern "C"

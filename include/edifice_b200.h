@@ -1,0 +1,105 @@
+/*
+ * edifice_b200.h -- C ABI of libedifice_b200.so, the B200 (sm_100a) kernels for
+ * Edifice's fused sequence-mixing path.
+ *
+ * This ABI replaces the reference's two boundaries for the path:
+ *   - the per-op C launch wrappers that c_src/edifice_cuda_nif.c dlsym()s out of
+ *     priv/cuda/libedifice_cuda_kernels{,_bf16}.so (edifice_cuda_nif.c:4052-4230);
+ *   - the XLA FFI handlers "exla_fused_<op>_{f32,bf16}" registered by
+ *     native/cuda/fused_*.cu under -DEXLA_FFI.
+ * The reference-named launch symbols themselves (fused_<op>_launch with the
+ * reference's exact signatures) are exported by the two shim libraries
+ * declared in edifice_cuda_kernels.h; they forward to the entry points below.
+ *
+ * Conventions
+ *   - Every tensor is a plain device pointer to a dense row-major array in the
+ *     reference's layout; the caller owns every buffer, outputs included.
+ *   - dtype (EDB_F32 / EDB_BF16) selects the storage type of the op's io
+ *     tensors; arithmetic is f32 (recurrent state f32) in both cases.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream).  Everything is stream-ordered; no entry point synchronises the
+ *     device or allocates memory unless its comment says so.
+ *   - Return value: 0 on success; a cudaError_t value (1..999) passes through
+ *     unchanged; ABI validation errors are >= 1000 (edb_status).  Nothing
+ *     aborts, traps or throws across this boundary.
+ *   - Waits inside kernels are bounded.  A wait that gives up sets a bit in a
+ *     per-device error word which edb_get_device_errors() returns.
+ */
+#ifndef EDIFICE_B200_H
+#define EDIFICE_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    EDB_OK = 0,
+    EDB_ERR_NULL_POINTER = 1000,
+    EDB_ERR_BAD_SHAPE = 1001,
+    EDB_ERR_BAD_DTYPE = 1002,
+    EDB_ERR_MISALIGNED = 1003,
+    EDB_ERR_WORKSPACE_TOO_SMALL = 1004,
+    EDB_ERR_UNSUPPORTED = 1005,
+    EDB_ERR_DEVICE_TIMEOUT = 1006
+} edb_status;
+
+typedef enum { EDB_F32 = 0, EDB_BF16 = 1 } edb_dtype;
+
+/* bits of the per-device error word */
+#define EDB_DEVERR_SCAN_PIPE 0x1u   /* diagonal-scan TMA pipeline wait gave up */
+#define EDB_DEVERR_SSM_PIPE 0x2u    /* selective-scan pipeline wait gave up */
+#define EDB_DEVERR_ATTN_PIPE 0x4u   /* attention pipeline wait gave up */
+#define EDB_DEVERR_DELTA_PIPE 0x8u  /* delta-rule pipeline wait gave up */
+
+/* Library version string, e.g. "edifice_b200 0.1 sm_100a". */
+const char* edb_version(void);
+
+/* Human-readable text for a status returned by any entry point. */
+const char* edb_status_string(int status);
+
+/* Read (and, if clear != 0, reset) the current device's error word.
+ * Synchronises the current device.  Returns 0 or a cudaError_t. */
+int edb_get_device_errors(unsigned int* flags_out, int clear);
+
+/* ------------------------------------------------------------------------
+ * Diagonal linear recurrence  h_t = a_t * h_{t-1} + b_t   (h_{-1} = h0)
+ * a, b, h: [batch, seq_len, hidden]; h0: [batch, hidden] or NULL (= zeros).
+ * Replaces fused_linear_scan_launch (native/cuda/fused_linear_scan.cu:78-94)
+ * and the "exla_fused_linear_scan_<dtype>" FFI handler (:100-160); Nx
+ * semantics of lib/edifice/cuda/fused_scan.ex:4429-4444 / :869-882.
+ * ---------------------------------------------------------------------- */
+int edb_linear_scan_fwd(int dtype, const void* a, const void* b, const void* h0, void* h,
+                        int batch, int seq_len, int hidden, void* stream);
+
+/* Backward of the above given dY = dL/dh:
+ *   g = dY_t + acc;  ga_t = g * h_{t-1};  gb_t = g;  acc = g * a_t;  gh0 = acc.
+ * h is the forward output; gh0 may be NULL.
+ * Replaces fused_linear_scan_backward_launch
+ * (native/cuda/fused_linear_scan_backward.cu:96-120; fused_scan.ex:884-916). */
+int edb_linear_scan_bwd(int dtype, const void* a, const void* h0, const void* h, const void* dy,
+                        void* ga, void* gb, void* gh0, int batch, int seq_len, int hidden,
+                        void* stream);
+
+/* ------------------------------------------------------------------------
+ * MinGRU  h_t = (1 - z_t) h_{t-1} + z_t c_t  with z already sigmoided.
+ * Replaces fused_mingru_scan_launch (native/cuda/fused_mingru_scan.cu:82-101);
+ * Nx semantics fused_scan.ex:516-528 / lib/edifice/recurrent/min_gru.ex:305-326.
+ * ---------------------------------------------------------------------- */
+int edb_mingru_fwd(int dtype, const void* z, const void* c, const void* h0, void* h,
+                   int batch, int seq_len, int hidden, void* stream);
+
+/* Backward: g = dY_t + acc; gz_t = g (c_t - h_{t-1}); gc_t = g z_t; acc = g (1 - z_t).
+ * The sigmoid chain rule (fused_scan.ex:477-479) stays with the caller.
+ * Replaces fused_mingru_scan_backward_launch
+ * (native/cuda/fused_mingru_scan_backward.cu:95-120; fused_scan.ex:548-581). */
+int edb_mingru_bwd(int dtype, const void* z, const void* c, const void* h0, const void* h,
+                   const void* dy, void* gz, void* gc, void* gh0, int batch, int seq_len,
+                   int hidden, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EDIFICE_B200_H */

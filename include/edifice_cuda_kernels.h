@@ -1,0 +1,57 @@
+/*
+ * edifice_cuda_kernels.h -- the reference-named launch symbols, exported by the
+ * two shim libraries
+ *     edifice_b200/shim/libedifice_cuda_kernels.so       (io = f32)
+ *     edifice_b200/shim/libedifice_cuda_kernels_bf16.so  (io = bf16)
+ * with exactly the names and argument lists that c_src/edifice_cuda_nif.c
+ * dlsym()s from priv/cuda/libedifice_cuda_kernels{,_bf16}.so
+ * (edifice_cuda_nif.c:4052-4230).  Dropping these two files in place of the
+ * reference's libraries switches the NIF to the B200 kernels unchanged.  Each
+ * forwards to the edb_* entry point of edifice_b200.h.
+ *
+ * io pointers are float* in the f32 shim and __nv_bfloat16* in the bf16 shim
+ * (same C ABI: a pointer).  Return: cudaError_t as int, or an edb_status.
+ */
+#ifndef EDIFICE_CUDA_KERNELS_H
+#define EDIFICE_CUDA_KERNELS_H
+
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#ifdef EDB_SHIM_BF16
+typedef unsigned short edb_io_t; /* bit pattern of __nv_bfloat16 */
+#else
+typedef float edb_io_t;
+#endif
+
+/* native/cuda/fused_linear_scan.cu:78-94 */
+int fused_linear_scan_launch(cudaStream_t stream, const edb_io_t* a_vals, const edb_io_t* b_vals,
+                             const edb_io_t* h0, edb_io_t* output, int batch, int seq_len,
+                             int hidden);
+
+/* native/cuda/fused_linear_scan_backward.cu:96-120; output_concat = [ga | gb | gh0] */
+int fused_linear_scan_backward_launch(cudaStream_t stream, const edb_io_t* a_vals,
+                                      const edb_io_t* h0, const edb_io_t* forward_out,
+                                      const edb_io_t* grad_output, edb_io_t* output_concat,
+                                      int batch, int seq_len, int hidden);
+
+/* native/cuda/fused_mingru_scan.cu:82-101 */
+int fused_mingru_scan_launch(cudaStream_t stream, const edb_io_t* gates,
+                             const edb_io_t* candidates, const edb_io_t* h0, edb_io_t* output,
+                             int batch, int seq_len, int hidden);
+
+/* native/cuda/fused_mingru_scan_backward.cu:95-120; output_concat = [gz | gc | gh0] */
+int fused_mingru_scan_backward_launch(cudaStream_t stream, const edb_io_t* z,
+                                      const edb_io_t* candidates, const edb_io_t* h0,
+                                      const edb_io_t* forward_out, const edb_io_t* grad_output,
+                                      edb_io_t* output_concat, int batch, int seq_len,
+                                      int hidden);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EDIFICE_CUDA_KERNELS_H */

@@ -1,0 +1,225 @@
+"""CPU oracle for the fused sequence-mixing path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference
+arm import this package, and only as the checker (or the timed CPU baseline).
+The product library never routes through it.
+
+Every function takes numpy arrays (any float dtype; they are widened to f32,
+which is exact for bf16-rounded values) and returns f32 numpy arrays.
+``prec="f64"`` (default) is the parity oracle with f64 accumulation;
+``prec="f32"`` is the Nx-like f32 arithmetic used for the timed CPU baseline.
+
+Reference citations (edifice project paths) live beside each C function in
+oracle_body.h.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+from . import build as _build
+
+_lib = None
+_ref_cpu = None
+
+_F = ctypes.POINTER(ctypes.c_float)
+_I = ctypes.c_int
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = _build.ORACLE_SO
+        if not os.path.exists(path):
+            _build.build_oracle()
+        _lib = ctypes.CDLL(path)
+    return _lib
+
+
+def ref_cpu_lib():
+    """The reference's own CPU references (oracle/_ref), or None when absent."""
+    global _ref_cpu
+    if _ref_cpu is None and os.path.exists(_build.REF_CPU_SO):
+        _ref_cpu = ctypes.CDLL(_build.REF_CPU_SO)
+    return _ref_cpu
+
+
+def set_threads(n):
+    lib().orc_set_num_threads(int(n))
+
+
+def num_threads():
+    return int(lib().orc_num_threads())
+
+
+def _f32(x):
+    return np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+
+
+def _p(x):
+    return None if x is None else x.ctypes.data_as(_F)
+
+
+def _fn(name, prec):
+    return getattr(lib(), "orc_%s_%s" % (name, prec))
+
+
+# ----------------------------------------------------------------- scans
+def linear_scan_fwd(a, b, h0=None, prec="f64"):
+    a, b = _f32(a), _f32(b)
+    B, L, H = a.shape
+    h0 = None if h0 is None else _f32(h0)
+    out = np.empty_like(a)
+    _fn("linear_scan_fwd", prec)(_p(a), _p(b), _p(h0), _p(out), _I(B), _I(L), _I(H))
+    return out
+
+
+def linear_scan_bwd(a, h0, fwd, dy, prec="f64"):
+    a, fwd, dy = _f32(a), _f32(fwd), _f32(dy)
+    B, L, H = a.shape
+    h0 = None if h0 is None else _f32(h0)
+    ga, gb = np.empty_like(a), np.empty_like(a)
+    gh0 = np.empty((B, H), np.float32)
+    _fn("linear_scan_bwd", prec)(_p(a), _p(h0), _p(fwd), _p(dy), _p(ga), _p(gb), _p(gh0),
+                                 _I(B), _I(L), _I(H))
+    return ga, gb, gh0
+
+
+def mingru_fwd(z, c, h0=None, prec="f64"):
+    z, c = _f32(z), _f32(c)
+    B, L, H = z.shape
+    h0 = None if h0 is None else _f32(h0)
+    out = np.empty_like(z)
+    _fn("mingru_fwd", prec)(_p(z), _p(c), _p(h0), _p(out), _I(B), _I(L), _I(H))
+    return out
+
+
+def mingru_bwd(z, c, h0, fwd, dy, prec="f64"):
+    z, c, fwd, dy = _f32(z), _f32(c), _f32(fwd), _f32(dy)
+    B, L, H = z.shape
+    h0 = None if h0 is None else _f32(h0)
+    gz, gc = np.empty_like(z), np.empty_like(z)
+    gh0 = np.empty((B, H), np.float32)
+    _fn("mingru_bwd", prec)(_p(z), _p(c), _p(h0), _p(fwd), _p(dy), _p(gz), _p(gc), _p(gh0),
+                            _I(B), _I(L), _I(H))
+    return gz, gc, gh0
+
+
+# ------------------------------------------------------- selective scan
+DT_MIN, DT_MAX = 0.001, 0.1
+
+
+def selective_scan_fwd(x, dt, A, Bm, Cm, prec="f64", dt_min=DT_MIN, dt_max=DT_MAX):
+    x, dt, A, Bm, Cm = map(_f32, (x, dt, A, Bm, Cm))
+    B, L, D = x.shape
+    N = A.shape[1]
+    if N > 64:
+        raise ValueError("oracle supports d_state <= 64")
+    y = np.empty_like(x)
+    _fn("selective_scan_fwd", prec)(_p(x), _p(dt), _p(A), _p(Bm), _p(Cm), _p(y), _I(B), _I(L),
+                                    _I(D), _I(N), ctypes.c_float(dt_min), ctypes.c_float(dt_max))
+    return y
+
+
+def selective_scan_bwd(x, dt, A, Bm, Cm, dy, prec="f64", dt_min=DT_MIN, dt_max=DT_MAX):
+    x, dt, A, Bm, Cm, dy = map(_f32, (x, dt, A, Bm, Cm, dy))
+    B, L, D = x.shape
+    N = A.shape[1]
+    gx, gdt = np.empty_like(x), np.empty_like(x)
+    gB, gC = np.empty((B, L, N), np.float32), np.empty((B, L, N), np.float32)
+    _fn("selective_scan_bwd", prec)(_p(x), _p(dt), _p(A), _p(Bm), _p(Cm), _p(dy), _p(gx),
+                                    _p(gdt), _p(gB), _p(gC), _I(B), _I(L), _I(D), _I(N),
+                                    ctypes.c_float(dt_min), ctypes.c_float(dt_max))
+    return gx, gdt, gB, gC
+
+
+def selective_scan_model_fwd(x, dt, Bm, Cm, prec="f64", dt_min=DT_MIN, dt_max=DT_MAX):
+    x, dt, Bm, Cm = map(_f32, (x, dt, Bm, Cm))
+    B, L, D = x.shape
+    N = Bm.shape[2]
+    y = np.empty_like(x)
+    _fn("selective_scan_model_fwd", prec)(_p(x), _p(dt), _p(Bm), _p(Cm), _p(y), _I(B), _I(L),
+                                          _I(D), _I(N), ctypes.c_float(dt_min),
+                                          ctypes.c_float(dt_max))
+    return y
+
+
+# ------------------------------------------------------------ delta rule
+def delta_net_fwd(q, k, v, beta, prec="f64"):
+    q, k, v, beta = map(_f32, (q, k, v, beta))
+    B, L, H, d = q.shape
+    scalar = int(beta.ndim == 3)
+    o = np.empty_like(q)
+    _fn("delta_net_fwd", prec)(_p(q), _p(k), _p(v), _p(beta), _p(o), _I(B), _I(L), _I(H),
+                               _I(d), _I(scalar))
+    return o
+
+
+def delta_net_bwd(q, k, v, beta, dO, prec="f64"):
+    q, k, v, beta, dO = map(_f32, (q, k, v, beta, dO))
+    B, L, H, d = q.shape
+    scalar = int(beta.ndim == 3)
+    gq, gk, gv = np.empty_like(q), np.empty_like(q), np.empty_like(q)
+    gbeta = np.empty_like(beta)
+    _fn("delta_net_bwd", prec)(_p(q), _p(k), _p(v), _p(beta), _p(dO), _p(gq), _p(gk), _p(gv),
+                               _p(gbeta), _I(B), _I(L), _I(H), _I(d), _I(scalar))
+    return gq, gk, gv, gbeta
+
+
+# ------------------------------------------------------------- attention
+def attention_fwd(q, k, v, causal=True, prec="f64", want_lse=False):
+    q, k, v = map(_f32, (q, k, v))
+    B, Hq, L, d = q.shape
+    Hkv = k.shape[1]
+    o = np.empty_like(q)
+    lse = np.empty((B, Hq, L), np.float32) if want_lse else None
+    _fn("attention_fwd", prec)(_p(q), _p(k), _p(v), _p(o), _p(lse), _I(B), _I(Hq), _I(Hkv),
+                               _I(L), _I(d), _I(int(bool(causal))))
+    return (o, lse) if want_lse else o
+
+
+def attention_bwd(q, k, v, dO, causal=True, prec="f64"):
+    q, k, v, dO = map(_f32, (q, k, v, dO))
+    B, Hq, L, d = q.shape
+    Hkv = k.shape[1]
+    dq, dk, dv = np.empty_like(q), np.empty_like(k), np.empty_like(v)
+    _fn("attention_bwd", prec)(_p(q), _p(k), _p(v), _p(dO), _p(dq), _p(dk), _p(dv), _I(B),
+                               _I(Hq), _I(Hkv), _I(L), _I(d), _I(int(bool(causal))))
+    return dq, dk, dv
+
+
+# ---------------------------------------------- the reference's own C refs
+def ref_linear_scan_cpu(a, b, h0):
+    r = ref_cpu_lib()
+    a, b, h0 = map(_f32, (a, b, h0))
+    B, L, H = a.shape
+    out = np.empty_like(a)
+    r.ref_linear_scan_cpu(_p(a), _p(b), _p(h0), _p(out), _I(B), _I(L), _I(H))
+    return out
+
+
+def ref_mingru_scan_cpu(z, c, h0):
+    r = ref_cpu_lib()
+    z, c, h0 = map(_f32, (z, c, h0))
+    B, L, H = z.shape
+    out = np.empty_like(z)
+    r.ref_mingru_scan_cpu(_p(z), _p(c), _p(h0), _p(out), _I(B), _I(L), _I(H))
+    return out
+
+
+def ref_delta_net_scan_cpu(q, k, v, beta):
+    r = ref_cpu_lib()
+    q, k, v, beta = map(_f32, (q, k, v, beta))
+    B, L, H, d = q.shape
+    out = np.empty_like(q)
+    r.ref_delta_net_scan_cpu(_p(q), _p(k), _p(v), _p(beta), _p(out), _I(B), _I(L), _I(H), _I(d))
+    return out
+
+
+def norm_rel(x, ref):
+    """||x - ref||_2 / ||ref||_2 computed in f64 (the parity metric)."""
+    x = np.asarray(x, np.float64)
+    ref = np.asarray(ref, np.float64)
+    den = np.linalg.norm(ref.ravel())
+    num = np.linalg.norm((x - ref).ravel())
+    return float(num / den) if den > 0 else float(num)
