@@ -9,7 +9,7 @@ from ._lib import EdbError, LIB_PATH, load, device_errors  # noqa: F401
 from . import fused_scan  # noqa: F401
 from .fused_scan import (  # noqa: F401
     linear_scan, linear_scan_backward, mingru, mingru_scan, mingru_backward,
-    LinearScanFn, MinGRUFn,
+    LinearScanFn, MinGRUFn, selective_scan, selective_scan_backward, SelectiveScanFn,
 )
 
 __version__ = "0.1.0"

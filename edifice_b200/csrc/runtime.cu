@@ -26,6 +26,16 @@ CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t ra
             g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     });
     if (!g_encode) return CUDA_ERROR_NOT_SUPPORTED;
+    // The driver call needs a current context on this thread.  A thread that
+    // has only ever asked the runtime for the device number (e.g. an autograd
+    // worker) has none yet; cudaSetDevice makes the primary context current.
+    thread_local int ctx_dev = -1;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return CUDA_ERROR_INVALID_CONTEXT;
+    if (dev != ctx_dev) {
+        if (cudaSetDevice(dev) != cudaSuccess) return CUDA_ERROR_INVALID_CONTEXT;
+        ctx_dev = dev;
+    }
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     return g_encode(map, dtype, rank, gaddr, dims, strides_bytes, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,

@@ -140,3 +140,69 @@ class MinGRUFn(torch.autograd.Function):
         z, cand, out = ctx.saved_tensors
         gz, gc, _ = mingru_backward(z, cand, None, out, grad_output.contiguous())
         return gz * z * (1 - z), gc
+
+
+# ---------------------------------------------------------------- selective scan
+DT_MIN, DT_MAX = 0.001, 0.1  # lib/edifice/ssm/common.ex:58-63
+
+
+def _ssm_shapes(x, a, b):
+    Bsz, L, D = x.shape
+    if a.shape[0] != D or tuple(b.shape[:2]) != (Bsz, L) or b.shape[2] != a.shape[1]:
+        raise _lib.EdbError("selective_scan: shape mismatch x%s A%s B%s"
+                            % (tuple(x.shape), tuple(a.shape), tuple(b.shape)))
+    return Bsz, L, D, a.shape[1]
+
+
+def selective_scan(x, dt, a, b, c, with_ckpt=False):
+    """FusedScan.selective_scan/5 (fused_scan.ex:370-384), kernel semantics:
+    x, dt [B, L, D]; A [D, N]; B, C [B, L, N] -> y [B, L, D].
+    with_ckpt=True also returns the f32 chunk-start states the backward can reuse."""
+    _dev(x, dt, a, b, c, what="selective_scan")
+    Bsz, L, D, N = _ssm_shapes(x, a, b)
+    y = torch.empty_like(x)
+    lib = _lib.load()
+    ck = None
+    if with_ckpt:
+        nbytes = lib.edb_selective_scan_ckpt_bytes(Bsz, L, D, N)
+        ck = torch.empty(nbytes // 4, dtype=torch.float32, device=x.device)
+    _lib.check(lib.edb_selective_scan_fwd(_dtype_code(x, "selective_scan"), _p(x), _p(dt), _p(a),
+                                          _p(b), _p(c), _p(y), _p(ck), Bsz, L, D, N, DT_MIN,
+                                          DT_MAX, _stream()), "CUDA fused selective scan")
+    return (y, ck) if with_ckpt else y
+
+
+def selective_scan_backward(x, dt, a, b, c, grad_output, h_ckpt=None):
+    """Returns (grad_x, grad_dt, grad_B, grad_C); grad_B/grad_C are f32 as in
+    selective_scan_backward_dispatch/7 (fused_scan.ex:1433-1450)."""
+    _dev(x, dt, a, b, c, grad_output, h_ckpt, what="selective_scan_backward")
+    Bsz, L, D, N = _ssm_shapes(x, a, b)
+    lib = _lib.load()
+    gx, gdt = torch.empty_like(x), torch.empty_like(x)
+    gB = torch.empty((Bsz, L, N), dtype=torch.float32, device=x.device)
+    gC = torch.empty_like(gB)
+    wsb = lib.edb_selective_scan_bwd_workspace(Bsz, L, D, N, int(h_ckpt is not None))
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=x.device)
+    _lib.check(lib.edb_selective_scan_bwd(_dtype_code(x, "selective_scan_backward"), _p(x), _p(dt),
+                                          _p(a), _p(b), _p(c), _p(grad_output), _p(h_ckpt),
+                                          _p(gx), _p(gdt), _p(gB), _p(gC), Bsz, L, D, N, DT_MIN,
+                                          DT_MAX, _p(ws), wsb, _stream()),
+               "CUDA fused selective scan backward")
+    return gx, gdt, gB, gC
+
+
+class SelectiveScanFn(torch.autograd.Function):
+    """custom_grad wiring of selective_scan_custom_call/5 (fused_scan.ex:2595-2611):
+    gradients to x, dt, B, C; A gets none."""
+
+    @staticmethod
+    def forward(ctx, x, dt, a, b, c):
+        y, ck = selective_scan(x, dt, a, b, c, with_ckpt=True)
+        ctx.save_for_backward(x, dt, a, b, c, ck)
+        return y
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        x, dt, a, b, c, ck = ctx.saved_tensors
+        gx, gdt, gB, gC = selective_scan_backward(x, dt, a, b, c, grad_output.contiguous(), ck)
+        return gx, gdt, None, gB.to(b.dtype), gC.to(c.dtype)

@@ -52,4 +52,35 @@ int fused_mingru_scan_backward_launch(cudaStream_t stream, const edb_io_t* z,
                           stream);
 }
 
+int fused_selective_scan_launch(cudaStream_t stream, const edb_io_t* x, const edb_io_t* dt,
+                                const edb_io_t* A, const edb_io_t* B, const edb_io_t* C,
+                                edb_io_t* out, int batch, int seq_len, int hidden, int state) {
+    return edb_selective_scan_fwd(kDtype, x, dt, A, B, C, out, nullptr, batch, seq_len, hidden,
+                                  state, 0.001f, 0.1f, stream);
+}
+
+int fused_selective_scan_backward_launch(cudaStream_t stream, const edb_io_t* x,
+                                         const edb_io_t* dt, const edb_io_t* A,
+                                         const edb_io_t* B, const edb_io_t* C,
+                                         const edb_io_t* grad_output, edb_io_t* output_concat,
+                                         int batch, int seq_len, int hidden, int state_size) {
+    const long long bth = (long long)batch * seq_len * hidden;
+    const long long bts = (long long)batch * seq_len * state_size;
+    edb_io_t* gx = output_concat;
+    edb_io_t* gdt = output_concat + bth;
+    float* gB = reinterpret_cast<float*>(output_concat + 2 * bth);
+    float* gC = gB + bts;
+    const size_t wsb = edb_selective_scan_bwd_workspace(batch, seq_len, hidden, state_size, 0);
+    void* ws = nullptr;
+    if (wsb) {
+        cudaError_t e = cudaMallocAsync(&ws, wsb, stream);
+        if (e != cudaSuccess) return (int)e;
+    }
+    int st = edb_selective_scan_bwd(kDtype, x, dt, A, B, C, grad_output, nullptr, gx, gdt, gB, gC,
+                                    batch, seq_len, hidden, state_size, 0.001f, 0.1f, ws, wsb,
+                                    stream);
+    if (ws) cudaFreeAsync(ws, stream);
+    return st;
+}
+
 }  // extern "C"

@@ -98,6 +98,44 @@ int edb_mingru_bwd(int dtype, const void* z, const void* c, const void* h0, cons
                    const void* dy, void* gz, void* gc, void* gh0, int batch, int seq_len,
                    int hidden, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Mamba selective scan, kernel semantics (given A, per-channel clamped dt):
+ *   dtc = clip(dt, dt_min, dt_max);  h_n = exp(dtc A[d,n]) h_n + dtc B[b,t,n] x;
+ *   y = sum_n C[b,t,n] h_n   (h_{-1} = 0).
+ * x, dt, y: [batch, seq_len, d_inner]; A: [d_inner, d_state];
+ * B, C: [batch, seq_len, d_state]; all in `dtype`.  d_state <= 16.
+ * The reference uses dt_min = 0.001, dt_max = 0.1.
+ * h_ckpt (optional, f32, edb_selective_scan_ckpt_bytes() bytes, 16-byte
+ * aligned): the forward also writes the state at the start of every chunk, so
+ * the backward can skip recomputing them.
+ * Replaces fused_selective_scan_launch (native/cuda/fused_selective_scan.cu:105-124)
+ * and "exla_fused_selective_scan_<dtype>"; Nx semantics
+ * test/edifice/cuda/backward_kernels_test.exs:1563-1586.
+ * ---------------------------------------------------------------------- */
+size_t edb_selective_scan_ckpt_bytes(int batch, int seq_len, int d_inner, int d_state);
+
+int edb_selective_scan_fwd(int dtype, const void* x, const void* dt, const void* A, const void* B,
+                           const void* C, void* y, float* h_ckpt, int batch, int seq_len,
+                           int d_inner, int d_state, float dt_min, float dt_max, void* stream);
+
+/* Workspace bytes edb_selective_scan_bwd needs (have_ckpt: a forward h_ckpt
+ * will be passed). */
+size_t edb_selective_scan_bwd_workspace(int batch, int seq_len, int d_inner, int d_state,
+                                        int have_ckpt);
+
+/* Backward given dY: gx, gdt in `dtype`; gB, gC f32 [batch, seq_len, d_state]
+ * (sums over d_inner, reduced deterministically).  A gets no gradient and gdt
+ * is 0 where dt lies outside [dt_min, dt_max], as in
+ * lib/edifice/cuda/fused_scan.ex:1453-1531.  The caller provides the workspace
+ * (16-byte aligned).  Replaces fused_selective_scan_backward_launch
+ * (native/cuda/fused_selective_scan_backward.cu:198-238), whose [B,D,L,N]
+ * f32 workspace and atomics are not used. */
+int edb_selective_scan_bwd(int dtype, const void* x, const void* dt, const void* A, const void* B,
+                           const void* C, const void* dy, const float* h_ckpt, void* gx, void* gdt,
+                           float* gB, float* gC, int batch, int seq_len, int d_inner, int d_state,
+                           float dt_min, float dt_max, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
 #ifdef __cplusplus
 }
 #endif

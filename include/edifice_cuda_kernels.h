@@ -50,6 +50,23 @@ int fused_mingru_scan_backward_launch(cudaStream_t stream, const edb_io_t* z,
                                       edb_io_t* output_concat, int batch, int seq_len,
                                       int hidden);
 
+/* native/cuda/fused_selective_scan.cu:105-124 (dt clamp [0.001, 0.1]) */
+int fused_selective_scan_launch(cudaStream_t stream, const edb_io_t* x, const edb_io_t* dt,
+                                const edb_io_t* A, const edb_io_t* B, const edb_io_t* C,
+                                edb_io_t* out, int batch, int seq_len, int hidden, int state);
+
+/* native/cuda/fused_selective_scan_backward.cu:198-238;
+ * output_concat = [gx io (B*L*H) | gdt io (B*L*H) | gB f32 (B*L*S) | gC f32 (B*L*S)]
+ * -- the byte layout the reference kernel writes (the reference NIF under-sizes
+ * this buffer in bf16, c_src/edifice_cuda_nif.c:3758; size it per tensor dtype).
+ * The workspace is taken stream-ordered (cudaMallocAsync / cudaFreeAsync), as
+ * the reference launcher does. */
+int fused_selective_scan_backward_launch(cudaStream_t stream, const edb_io_t* x,
+                                         const edb_io_t* dt, const edb_io_t* A,
+                                         const edb_io_t* B, const edb_io_t* C,
+                                         const edb_io_t* grad_output, edb_io_t* output_concat,
+                                         int batch, int seq_len, int hidden, int state_size);
+
 #ifdef __cplusplus
 }
 #endif
