@@ -88,7 +88,7 @@ def build(force=False, jobs=None, verbose_ptxas=False):
                 ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", *define,
                  "-I", os.path.join(ROOT, "include"), "-I", "/usr/local/cuda/include",
                  shim_src, "-o", out, "-L", PKG, "-ledifice_b200",
-                 "-Wl,-rpath,$ORIGIN/..", "-L/usr/local/cuda/lib64", "-lcudart"],
+                 "-Wl,-rpath,$ORIGIN/..:$ORIGIN", "-L/usr/local/cuda/lib64", "-lcudart"],
                 capture_output=True, text=True)
             if r.returncode != 0:
                 raise RuntimeError("shim build failed:\n%s\n%s" % (r.stdout, r.stderr))
