@@ -30,6 +30,8 @@ SIGNATURES = {
     "edb_selective_scan_bwd_workspace": (_sz, [_i, _i, _i, _i, _i]),
     "edb_selective_scan_bwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _i, _i, _i, _i, _f, _f, _vp, _sz, _vp]),
+    "edb_selective_scan_bwd_noalloc": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                            _vp, _vp, _i, _i, _i, _i, _f, _f, _vp]),
 }
 
 EDB_F32, EDB_BF16 = 0, 1

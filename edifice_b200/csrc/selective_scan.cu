@@ -25,6 +25,8 @@
 //     transpose-reduce, cross-warp sum in shared memory, one partial per
 //     (channel block, b, t, n) to the workspace, then a second kernel sums the
 //     channel-block partials in a fixed order.  No atomics.
+#include <atomic>
+
 #include "edb_common.cuh"
 
 namespace {
@@ -465,4 +467,54 @@ extern "C" int edb_selective_scan_bwd(int dtype, const void* x, const void* dt, 
                                           seq_len, d_inner, d_state, dt_min, dt_max, st)
                    : launch_bwd<float, 16>(x, dt, A, B, C, dy, ck, gx, gdt, gB, gC, gpart, batch,
                                            seq_len, d_inner, d_state, dt_min, dt_max, st);
+}
+
+// ---------------------------------------------------------------- no-alloc variant
+// Scratch of edb_selective_scan_bwd_noalloc: a fixed array inside the library,
+// one per device, so that callers which must not allocate device memory can
+// still run the backward.  Host code cannot use the symbol itself as a device
+// address (on the host it names a host-side stand-in); the address is looked
+// up once per device with cudaGetSymbolAddress, the device being current.
+static __device__ __align__(256) unsigned char g_ssm_noalloc_scratch[EDB_SSM_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::atomic<void*> g_ssm_noalloc_addr[kMaxDevices];
+
+int ssm_noalloc_scratch(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= kMaxDevices) return EDB_ERR_UNSUPPORTED;
+    void* p = g_ssm_noalloc_addr[dev].load(std::memory_order_acquire);
+    if (p == nullptr) {
+        e = cudaGetSymbolAddress(&p, g_ssm_noalloc_scratch);
+        if (e != cudaSuccess) return (int)e;
+        if (p == nullptr) return EDB_ERR_UNSUPPORTED;
+        g_ssm_noalloc_addr[dev].store(p, std::memory_order_release);
+    }
+    *out = p;
+    return EDB_OK;
+}
+
+}  // namespace
+
+extern "C" int edb_selective_scan_bwd_noalloc(int dtype, const void* x, const void* dt,
+                                              const void* A, const void* B, const void* C,
+                                              const void* dy, const float* h_ckpt, void* gx,
+                                              void* gdt, float* gB, float* gC, int batch,
+                                              int seq_len, int d_inner, int d_state, float dt_min,
+                                              float dt_max, void* stream) {
+    if (int s = check_args(dtype, batch, seq_len, d_inner, d_state, dt_min, dt_max)) return s;
+    if (!x || !dt || !A || !B || !C || !dy || !gx || !gdt || !gB || !gC)
+        return EDB_ERR_NULL_POINTER;
+    const size_t need =
+        edb_selective_scan_bwd_workspace(batch, seq_len, d_inner, d_state, h_ckpt != nullptr);
+    if (need > (size_t)EDB_SSM_NOALLOC_SCRATCH_BYTES) return EDB_ERR_WORKSPACE_TOO_SMALL;
+    void* ws = nullptr;
+    if (int s = ssm_noalloc_scratch(&ws)) return s;
+    return edb_selective_scan_bwd(dtype, x, dt, A, B, C, dy, h_ckpt, gx, gdt, gB, gC, batch,
+                                  seq_len, d_inner, d_state, dt_min, dt_max, ws,
+                                  (size_t)EDB_SSM_NOALLOC_SCRATCH_BYTES, stream);
 }

@@ -136,6 +136,35 @@ int edb_selective_scan_bwd(int dtype, const void* x, const void* dt, const void*
                            float dt_min, float dt_max, void* workspace, size_t workspace_bytes,
                            void* stream);
 
+/* Capacity of the library's built-in scratch array used by
+ * edb_selective_scan_bwd_noalloc (16 MiB; every GPU that loads the library
+ * holds it until the process exits). */
+#define EDB_SSM_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* Same backward as edb_selective_scan_bwd, for callers that must not allocate
+ * device memory -- above all an XLA/EXLA custom-call handler: XLA reserves most
+ * of the GPU for its own allocator up front, so a cudaMalloc made from inside
+ * the handler can fail for lack of memory, and XLA hands these handlers no
+ * scratch buffer.  This entry point allocates nothing: its scratch is a
+ * fixed-size array inside the library (EDB_SSM_NOALLOC_SCRATCH_BYTES).  The
+ * caller still passes every input and output.
+ *   - Problems whose workspace (edb_selective_scan_bwd_workspace) exceeds the
+ *     array are rejected with EDB_ERR_WORKSPACE_TOO_SMALL before any GPU work.
+ *   - The first call on a device looks up the array's device address (once
+ *     per device, with that device current); make that first call before any
+ *     stream capture.
+ *   - All calls share the one array per device and it keeps the last call's
+ *     contents (every byte this backward reads is written first, so nothing
+ *     needs clearing); calls that overlap on the GPU -- different streams, or
+ *     different host threads on one device -- race on it and must be ordered
+ *     by the caller.
+ * No counterpart in the reference. */
+int edb_selective_scan_bwd_noalloc(int dtype, const void* x, const void* dt, const void* A,
+                                   const void* B, const void* C, const void* dy,
+                                   const float* h_ckpt, void* gx, void* gdt, float* gB, float* gC,
+                                   int batch, int seq_len, int d_inner, int d_state, float dt_min,
+                                   float dt_max, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
