@@ -32,6 +32,8 @@ SIGNATURES = {
                                     _i, _i, _i, _i, _f, _f, _vp, _sz, _vp]),
     "edb_selective_scan_bwd_noalloc": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                             _vp, _vp, _i, _i, _i, _i, _f, _f, _vp]),
+    "edb_flash_attention_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f,
+                                     _vp]),
 }
 
 EDB_F32, EDB_BF16 = 0, 1

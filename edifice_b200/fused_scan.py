@@ -191,6 +191,33 @@ def selective_scan_backward(x, dt, a, b, c, grad_output, h_ckpt=None):
     return gx, gdt, gB, gC
 
 
+def _attn_shapes(q, k, v):
+    if q.dim() != 4 or k.dim() != 4 or k.shape != v.shape:
+        raise _lib.EdbError("flash_attention: expected [B, H, L, d] q and equal k/v shapes")
+    B, Hq, L, d = q.shape
+    if k.shape[0] != B or k.shape[2] != L or k.shape[3] != d or Hq % k.shape[1] != 0:
+        raise _lib.EdbError("flash_attention: q %s incompatible with k/v %s"
+                            % (tuple(q.shape), tuple(k.shape)))
+    return B, Hq, k.shape[1], L, d
+
+
+def flash_attention(q, k, v, causal=False, scale=None, return_lse=False):
+    """FusedScan.flash_attention/4 (fused_scan.ex:3398-3414) with GQA:
+    q [B, Hq, L, d], k/v [B, Hkv, L, d] -> o [B, Hq, L, d].  `causal` masks
+    j > i; scale defaults to 1/sqrt(d).  return_lse adds the f32 [B, Hq, L]
+    row log-sum-exp the backward can reuse."""
+    _dev(q, k, v, what="flash_attention")
+    B, Hq, Hkv, L, d = _attn_shapes(q, k, v)
+    o = torch.empty_like(q)
+    lse = torch.empty((B, Hq, L), dtype=torch.float32, device=q.device) if return_lse else None
+    lib = _lib.load()
+    _lib.check(lib.edb_flash_attention_fwd(_dtype_code(q, "flash_attention"), _p(q), _p(k), _p(v),
+                                           _p(o), _p(lse), B, Hq, Hkv, L, d, int(bool(causal)),
+                                           float(scale or 0.0), _stream()),
+               "CUDA flash attention")
+    return (o, lse) if return_lse else o
+
+
 class SelectiveScanFn(torch.autograd.Function):
     """custom_grad wiring of selective_scan_custom_call/5 (fused_scan.ex:2595-2611):
     gradients to x, dt, B, C; A gets none."""

@@ -83,4 +83,11 @@ int fused_selective_scan_backward_launch(cudaStream_t stream, const edb_io_t* x,
     return st;
 }
 
+int fused_flash_attention_launch(cudaStream_t stream, const edb_io_t* q, const edb_io_t* k,
+                                 const edb_io_t* v, edb_io_t* output, int batch, int num_heads,
+                                 int seq_len, int head_dim, int causal) {
+    return edb_flash_attention_fwd(kDtype, q, k, v, output, nullptr, batch, num_heads, num_heads,
+                                   seq_len, head_dim, causal, 0.0f, stream);
+}
+
 }  // extern "C"

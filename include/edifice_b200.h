@@ -136,6 +136,22 @@ int edb_selective_scan_bwd(int dtype, const void* x, const void* dt, const void*
                            float dt_min, float dt_max, void* workspace, size_t workspace_bytes,
                            void* stream);
 
+/* ------------------------------------------------------------------------
+ * Scaled-dot-product attention, causal or full, with grouped KV heads (GQA).
+ *   O = softmax(Q K^T * scale [+ -inf above the diagonal if causal]) V
+ * q, o: [batch, q_heads, seq_len, head_dim]; k, v: [batch, kv_heads, seq_len,
+ * head_dim]; q head h reads kv head h / (q_heads / kv_heads).  head_dim <= 128
+ * (bf16 with head_dim 64/128 runs on tcgen05 tensor cores).  scale <= 0 means
+ * 1/sqrt(head_dim).  lse (optional, f32 [batch, q_heads, seq_len]): natural-log
+ * row log-sum-exp of the scaled scores, for the backward.
+ * Replaces fused_flash_attention_launch (native/cuda/fused_flash_attention.cu:
+ * 168-191; equal heads only there) and "exla_fused_flash_attention_<dtype>";
+ * Nx semantics lib/edifice/cuda/fused_scan.ex:3476-3508.
+ * ---------------------------------------------------------------------- */
+int edb_flash_attention_fwd(int dtype, const void* q, const void* k, const void* v, void* o,
+                            float* lse, int batch, int q_heads, int kv_heads, int seq_len,
+                            int head_dim, int causal, float scale, void* stream);
+
 /* Capacity of the library's built-in scratch array used by
  * edb_selective_scan_bwd_noalloc (16 MiB; every GPU that loads the library
  * holds it until the process exits). */

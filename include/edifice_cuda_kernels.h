@@ -67,6 +67,12 @@ int fused_selective_scan_backward_launch(cudaStream_t stream, const edb_io_t* x,
                                          const edb_io_t* grad_output, edb_io_t* output_concat,
                                          int batch, int seq_len, int hidden, int state_size);
 
+/* native/cuda/fused_flash_attention.cu:168-191: q, k, v, output [B, H, T, d],
+ * equal heads, scale 1/sqrt(d), causal 0/1. */
+int fused_flash_attention_launch(cudaStream_t stream, const edb_io_t* q, const edb_io_t* k,
+                                 const edb_io_t* v, edb_io_t* output, int batch, int num_heads,
+                                 int seq_len, int head_dim, int causal);
+
 #ifdef __cplusplus
 }
 #endif

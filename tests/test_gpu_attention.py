@@ -1,0 +1,129 @@
+"""GPU parity of causal/full GQA attention against the CPU oracle (f64), the
+golden GQA vectors, and the reference's own flash-attention CUDA kernels."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from oracle import build as ob
+from edifice_b200 import fused_scan as fs
+from edifice_b200 import build, device_errors
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: 1e-4, torch.bfloat16: 2e-2}
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def attn_inputs(B, Hq, Hkv, L, d, dtype, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    q = torch.randn(B, Hq, L, d, generator=g)
+    k = torch.randn(B, Hkv, L, d, generator=g)
+    v = torch.randn(B, Hkv, L, d, generator=g)
+    do = torch.randn(B, Hq, L, d, generator=g)
+    return [t.to(dtype).cuda() for t in (q, k, v, do)]
+
+
+FWD_CASES = [
+    # (B, Hq, Hkv, L, d)
+    (1, 2, 2, 128, 128),
+    (2, 4, 2, 256, 128),
+    (1, 8, 2, 300, 128),   # partial last tile
+    (2, 4, 4, 64, 128),    # L < tile
+    (1, 2, 1, 1000, 64),   # head_dim 64
+    (1, 1, 1, 1, 128),     # single token
+    (2, 4, 2, 37, 8),      # small head_dim: SIMT path
+    (1, 4, 1, 200, 96),    # other head_dim: SIMT path
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("case", FWD_CASES)
+@pytest.mark.parametrize("causal", [True, False])
+def test_attention_forward(cuda, dtype, case, causal):
+    q, k, v, _ = attn_inputs(*case, dtype, seed=41)
+    o, lse = fs.flash_attention(q, k, v, causal=causal, return_lse=True)
+    torch.cuda.synchronize()
+    ro, rl = O.attention_fwd(_np(q), _np(k), _np(v), causal=causal, want_lse=True)
+    assert O.norm_rel(_np(o), ro) <= TOL[dtype]
+    assert O.norm_rel(_np(lse), rl) <= 1e-4
+    assert device_errors() == 0
+
+
+@pytest.mark.parametrize("layer", [0, 1])
+def test_attention_golden_gqa(cuda, layer):
+    g = np.load(os.path.join(GOLD, "gqa_fixture.npz"))
+    q, k, v = (torch.tensor(g["%s%d" % (n, layer)]).cuda() for n in ("q", "k", "v"))
+    o = fs.flash_attention(q, k, v, causal=True)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(_np(o), g["o%d" % layer], atol=2e-5)
+
+
+def test_config3_forward_rows(cuda):
+    """B4 Hq32 Hkv8 L8192 d128 causal bf16; a sample of
+    query rows (first and last 96 of three heads) against the f64 oracle."""
+    B, Hq, Hkv, L, d = 4, 32, 8, 8192, 128
+    q, k, v, _ = attn_inputs(B, Hq, Hkv, L, d, torch.bfloat16, seed=0)
+    o = fs.flash_attention(q, k, v, causal=True)
+    torch.cuda.synchronize()
+    assert device_errors() == 0
+    kn, vn = _np(k), _np(v)
+    for (b, h) in ((0, 0), (1, 13), (3, 31)):
+        hk = h // (Hq // Hkv)
+        for sl in (slice(0, 96), slice(L - 96, L)):
+            rows = np.arange(L)[sl]
+            # oracle on the needed prefix of keys for these rows
+            qq = _np(q[b:b + 1, h:h + 1, sl])
+            kk = kn[b:b + 1, hk:hk + 1, :rows[-1] + 1]
+            vv = vn[b:b + 1, hk:hk + 1, :rows[-1] + 1]
+            ref = _ref_rows(qq, kk, vv, rows)
+            assert O.norm_rel(_np(o[b, h, sl]), ref) <= 2e-2
+
+
+def _ref_rows(q, k, v, rows):
+    """causal attention for query rows `rows` (f64 numpy)."""
+    qd, kd, vd = (x[0, 0].astype(np.float64) for x in (q, k, v))
+    s = qd @ kd.T / np.sqrt(qd.shape[-1])
+    s[rows[:, None] < np.arange(kd.shape[0])[None, :]] = -np.inf
+    s -= s.max(-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(-1, keepdims=True)
+    return p @ vd
+
+
+@pytest.mark.skipif(not os.path.exists(ob.REF_KERNELS_SO["f32"]), reason="oracle/_ref not built")
+@pytest.mark.parametrize("causal", [0, 1])
+def test_oracle_matches_reference_cuda_flash(cuda, causal):
+    """Pin the oracle's attention against the reference's own
+    fused_flash_attention_launch (f32 build for sm_100a, equal heads).
+    L is a multiple of the reference's 32-row tile: for other L the reference
+    kernel's threads past the end skip the cooperative K/V tile load and the
+    block barrier (native/cuda/fused_flash_attention.cu:75-77, `continue`
+    before the loads), so its output is wrong there (seen at L = 70)."""
+    lib = ctypes.CDLL(ob.REF_KERNELS_SO["f32"])
+    B, H, L, d = 2, 3, 96, 32
+    q, k, v, _ = attn_inputs(B, H, H, L, d, torch.float32, seed=7)
+    o = torch.empty_like(q)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    assert lib.fused_flash_attention_launch(None, P(q), P(k), P(v), P(o), B, H, L, d, causal) == 0
+    torch.cuda.synchronize()
+    assert O.norm_rel(_np(o), O.attention_fwd(_np(q), _np(k), _np(v), causal=bool(causal))) <= 1e-5
+
+
+@pytest.mark.parametrize("prec,dtype", [("f32", torch.float32), ("bf16", torch.bfloat16)])
+def test_legacy_shim_forward(cuda, prec, dtype):
+    lib = ctypes.CDLL(build.SHIMS[prec])
+    B, H, L, d = 2, 4, 256, 128
+    q, k, v, _ = attn_inputs(B, H, H, L, d, dtype, seed=9)
+    o = torch.empty_like(q)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    assert lib.fused_flash_attention_launch(None, P(q), P(k), P(v), P(o), B, H, L, d, 1) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(o, fs.flash_attention(q, k, v, causal=True))
