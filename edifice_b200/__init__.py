@@ -10,7 +10,7 @@ from . import fused_scan  # noqa: F401
 from .fused_scan import (  # noqa: F401
     linear_scan, linear_scan_backward, mingru, mingru_scan, mingru_backward,
     LinearScanFn, MinGRUFn, selective_scan, selective_scan_backward, SelectiveScanFn,
-    flash_attention,
+    flash_attention, flash_attention_backward, FlashAttentionFn,
 )
 
 __version__ = "0.1.0"

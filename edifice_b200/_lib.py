@@ -34,6 +34,9 @@ SIGNATURES = {
                                             _vp, _vp, _i, _i, _i, _i, _f, _f, _vp]),
     "edb_flash_attention_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f,
                                      _vp]),
+    "edb_flash_attention_bwd_workspace": (_sz, [_i, _i, _i, _i, _i, _i, _i]),
+    "edb_flash_attention_bwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i,
+                                     _i, _i, _i, _i, _f, _vp, _sz, _vp]),
 }
 
 EDB_F32, EDB_BF16 = 0, 1

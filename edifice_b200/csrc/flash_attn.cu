@@ -62,7 +62,9 @@ struct FwdSmem {
 };
 
 // ------------------------------------------------------------ tcgen05 forward
-template <int HD, bool CAUSAL>
+// STORE_O = false: only the row log-sum-exp is written (the backward's
+// recompute when the caller has no lse from the forward).
+template <int HD, bool CAUSAL, bool STORE_O = true>
 __global__ void __launch_bounds__(kFwdThreads, 2)
     attn_fwd_tc_kernel(const __grid_constant__ AttnMaps maps, float* __restrict__ lse, int L,
                        int Hq, int Hkv, float scale_log2, unsigned* err) {
@@ -296,7 +298,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
             tc::fence_after_sync();
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
 #pragma unroll
-            for (int cc = 0; cc < HD / 32; ++cc) {
+            for (int cc = 0; cc < (STORE_O ? HD / 32 : 0); ++cc) {
                 uint32_t o[32];
                 tc::tmem_ld32(tO + cc * 32, o);
                 tc::tmem_wait_ld();
@@ -316,7 +318,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                 lse[(long long)bh * L + qrow] = (m_used + log2f(l)) * kLn2;
             fence_proxy_async();
             tc::named_bar(1, 128);
-            if (tid == 0) {
+            if (STORE_O && tid == 0) {
                 prefetch_tmap(&maps.o);
                 for (int bx = 0; bx < NB; ++bx)
                     tc::tma_store_3d(&maps.o, sQ + bx * (BM * 128), bx * 64, q0, bh);
@@ -392,15 +394,10 @@ __global__ void __launch_bounds__(128)
 
 // ------------------------------------------------------------ launch
 int make_map3(CUtensorMap* m, const void* p, int d, int L, int nbh, int box_rows) {
-    const cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)L, (cuuint64_t)nbh};
-    const cuuint64_t strides[2] = {(cuuint64_t)d * 2, (cuuint64_t)L * d * 2};
-    const cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
-    CUresult r = edb::encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(p),
-                                   dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-    return r == CUDA_SUCCESS ? EDB_OK : EDB_ERR_UNSUPPORTED;
+    return tc::make_attn_map(m, p, d, L, nbh, box_rows);
 }
 
-template <int HD, bool CAUSAL>
+template <int HD, bool CAUSAL, bool STORE_O = true>
 int launch_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
                   int Hkv, int L, float scale, cudaStream_t st) {
     AttnMaps maps;
@@ -409,7 +406,7 @@ int launch_fwd_tc(const void* q, const void* k, const void* v, void* o, float* l
     if ((s = make_map3(&maps.k, k, HD, L, B * Hkv, BN))) return s;
     if ((s = make_map3(&maps.v, v, HD, L, B * Hkv, BN))) return s;
     if ((s = make_map3(&maps.o, o, HD, L, B * Hq, BM))) return s;
-    auto kern = attn_fwd_tc_kernel<HD, CAUSAL>;
+    auto kern = attn_fwd_tc_kernel<HD, CAUSAL, STORE_O>;
     const int smem = FwdSmem<HD>::TOTAL;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
@@ -436,6 +433,22 @@ int launch_fwd_simt(const void* q, const void* k, const void* v, void* o, float*
 }
 
 }  // namespace
+
+// Row log-sum-exp only (bf16, head_dim 64/128), for the backward when the
+// caller did not keep the forward's lse.  Library-internal.
+int edb_attn_fwd_lse_only(int head_dim, int causal, const void* q, const void* k, float* lse,
+                          int B, int Hq, int Hkv, int L, float scale, cudaStream_t st) {
+    // the V operand is read by the PV MMAs; K stands in for it (O is not stored)
+    if (head_dim == 128)
+        return causal ? launch_fwd_tc<128, true, false>(q, k, k, const_cast<void*>(q), lse, B, Hq,
+                                                        Hkv, L, scale, st)
+                      : launch_fwd_tc<128, false, false>(q, k, k, const_cast<void*>(q), lse, B,
+                                                         Hq, Hkv, L, scale, st);
+    return causal ? launch_fwd_tc<64, true, false>(q, k, k, const_cast<void*>(q), lse, B, Hq, Hkv,
+                                                   L, scale, st)
+                  : launch_fwd_tc<64, false, false>(q, k, k, const_cast<void*>(q), lse, B, Hq,
+                                                    Hkv, L, scale, st);
+}
 
 extern "C" int edb_flash_attention_fwd(int dtype, const void* q, const void* k, const void* v,
                                        void* o, float* lse, int batch, int q_heads, int kv_heads,

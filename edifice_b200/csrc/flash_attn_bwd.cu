@@ -1,0 +1,679 @@
+// flash_attn_bwd.cu -- backward of causal/full GQA attention.
+//
+// Reference semantics (edifice project paths):
+//   lib/edifice/cuda/fused_scan.ex:3527-3574 (flash_attention_backward_fallback):
+//     P = softmax(QK^T*scale); dV = P^T dO; dP = dO V^T;
+//     dS = P (.) (dP - rowsum(dP (.) P)) * scale; dQ = dS K; dK = dS^T Q
+//   native/cuda/fused_flash_attention_backward.cu:49-408 (equal heads).
+// rowsum(dP (.) P) equals D = rowsum(dO (.) O), which a prep kernel computes.
+// GQA: dK, dV of kv head hk sum over its Hq/Hkv query heads.
+//
+// B200 path (bf16, head_dim 64/128) -- one CTA per (kv tile of 128 rows,
+// kv head, batch), longest causal work first; per (query head of the group,
+// query tile of 64 rows) five tcgen05 MMAs with TMEM accumulators:
+//   S^T  = K Q^T    (128x64, K-major x K-major)        TMEM cols [2D, 2D+64)
+//   dP^T = V dO^T   (128x64)                            TMEM cols [2D+64, 2D+128)
+//   dV  += P^T dO   (128xD, P^T from smem, dO MN-major) TMEM cols [0, D)
+//   dK  += dS^T Q   (128xD)                             TMEM cols [D, 2D)
+//   dQ_i = dS K     (64xD, dS^T read as an MN-major A)  TMEM cols [2D+128, 3D+128)
+// Warps 0-3 turn S^T, dP^T (TMEM lane = kv row) into P^T and dS^T (bf16,
+// 128-byte swizzled smem); warps 4-7 add each dQ_i into an f32 accumulator with
+// red.global.add.v4.f32 and at the end write dK, dV; warp 8 streams Q_i / dO_i
+// / lse / D through a 2-stage TMA ring; warp 9 issues the MMAs.  S^T/dP^T of
+// the next tile is issued as soon as the compute warps have read the current
+// one, so it overlaps their exponentials.  A last kernel converts dQ to the io
+// dtype.  Other shapes run SIMT kernels with the same math.
+#include <math.h>
+
+#include "tc_common.cuh"
+
+namespace {
+
+constexpr int BKV = 128;
+constexpr int BQ = 64;
+constexpr int QD_STAGES = 2;
+constexpr int kBwdThreads = 320;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct BwdMaps {
+    CUtensorMap q, k, v, dO;
+};
+
+template <int HD>
+struct BwdSmem {
+    static constexpr int NB = HD / 64;
+    static constexpr int KV_BYTES = BKV * HD * 2;
+    static constexpr int QD_BYTES = BQ * HD * 2;
+    static constexpr int T_BYTES = BKV * BQ * 2;  // P^T or dS^T tile
+    static constexpr int OFF_K = 0;
+    static constexpr int OFF_V = OFF_K + KV_BYTES;
+    static constexpr int OFF_Q = OFF_V + KV_BYTES;
+    static constexpr int OFF_DO = OFF_Q + QD_STAGES * QD_BYTES;
+    static constexpr int OFF_PT = OFF_DO + QD_STAGES * QD_BYTES;
+    static constexpr int OFF_DS = OFF_PT + T_BYTES;
+    static constexpr int OFF_LSE = OFF_DS + T_BYTES;
+    static constexpr int OFF_D = OFF_LSE + QD_STAGES * BQ * 4;
+    static constexpr int OFF_BAR = OFF_D + QD_STAGES * BQ * 4;
+    // kv_full, qd_full[2], qd_empty[2], sdp_full, sdp_free, pds_full, mm2_done,
+    // dq_full, dq_free, all_done
+    static constexpr int NBAR = 1 + 2 * QD_STAGES + 7;
+    static constexpr int TOTAL = OFF_BAR + NBAR * 8 + 16;
+    static constexpr int TM_DV = 0, TM_DK = HD, TM_S = 2 * HD, TM_DP = 2 * HD + 64,
+                         TM_DQ = 2 * HD + 128;
+    static constexpr int TMEM_COLS = 512;
+};
+
+static __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+                 "f"(d)
+                 : "memory");
+}
+
+template <int HD, bool CAUSAL>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const float* __restrict__ lse,
+                       const float* __restrict__ Dv, float* __restrict__ dq_acc,
+                       __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv, int L,
+                       int Hq, int Hkv, float scale, unsigned* err) {
+    using S = BwdSmem<HD>;
+    constexpr int NB = S::NB;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t* sK = smem + S::OFF_K;
+    uint8_t* sV = smem + S::OFF_V;
+    uint8_t* sQ = smem + S::OFF_Q;
+    uint8_t* sdO = smem + S::OFF_DO;
+    uint8_t* sPt = smem + S::OFF_PT;
+    uint8_t* sDs = smem + S::OFF_DS;
+    float* sLse = reinterpret_cast<float*>(smem + S::OFF_LSE);
+    float* sD = reinterpret_cast<float*>(smem + S::OFF_D);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
+    uint64_t* kv_full = bars;
+    uint64_t* qd_full = bars + 1;
+    uint64_t* qd_empty = bars + 1 + QD_STAGES;
+    uint64_t* sdp_full = bars + 1 + 2 * QD_STAGES;
+    uint64_t* sdp_free = sdp_full + 1;
+    uint64_t* pds_full = sdp_full + 2;
+    uint64_t* mm2_done = sdp_full + 3;
+    uint64_t* dq_full = sdp_full + 4;
+    uint64_t* dq_free = sdp_full + 5;
+    uint64_t* all_done = sdp_full + 6;
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + S::NBAR);
+    int* s_abort = reinterpret_cast<int*>(s_tmem + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int kt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+    const int G = Hq / Hkv;
+    const int bhk = b * Hkv + hk;
+    const int nq = (L + BQ - 1) / BQ;
+    const int i0 = CAUSAL ? (kt * BKV) / BQ : 0;
+    const int nqi = nq - i0;
+    const int N = G * nqi;
+    const float scale_log2 = scale * kLog2e;
+
+    if ((smem_u32(smem) & 1023u) != 0) {
+        if (tid == 0) edb_flag_error(err, EDB_DEVERR_ATTN_PIPE);
+        return;
+    }
+    if (warp == 9) {
+        tc::tmem_alloc(s_tmem, S::TMEM_COLS);
+        tc::tmem_relinquish();
+    }
+    if (tid == 256) {
+        mbar_init(kv_full, 1);
+        for (int s = 0; s < QD_STAGES; ++s) {
+            mbar_init(&qd_full[s], 1);
+            mbar_init(&qd_empty[s], 1);
+        }
+        mbar_init(sdp_full, 1);
+        mbar_init(sdp_free, 4);
+        mbar_init(pds_full, 4);
+        mbar_init(mm2_done, 1);
+        mbar_init(dq_full, 1);
+        mbar_init(dq_free, 4);
+        mbar_init(all_done, 1);
+        *s_abort = 0;
+        fence_mbar_init();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *s_tmem;
+    volatile int* abort_flag = s_abort;
+
+    if (warp == 8) {
+        // ------------------------------------------------ producer (whole warp)
+        if (lane == 0) {
+            prefetch_tmap(&maps.q);
+            prefetch_tmap(&maps.k);
+            prefetch_tmap(&maps.v);
+            prefetch_tmap(&maps.dO);
+            mbar_arrive_expect_tx(kv_full, 2 * S::KV_BYTES);
+            for (int bx = 0; bx < NB; ++bx) {
+                tma_load_3d(sK + bx * (BKV * 128), &maps.k, kv_full, bx * 64, kt * BKV, bhk);
+                tma_load_3d(sV + bx * (BKV * 128), &maps.v, kv_full, bx * 64, kt * BKV, bhk);
+            }
+        }
+        int issued = 0;
+        for (int n = 0; n < N; ++n) {
+            const int s = n % QD_STAGES;
+            int go = 1;
+            if (lane == 0 && n >= QD_STAGES) {
+                if (*abort_flag ||
+                    !mbar_wait_bounded(&qd_empty[s], ((n / QD_STAGES) - 1) & 1, err,
+                                       EDB_DEVERR_ATTN_PIPE)) {
+                    *abort_flag = 1;
+                    go = 0;
+                }
+            }
+            go = __shfl_sync(0xffffffffu, go, 0);
+            if (!go) break;
+            const int g = n / nqi, i = i0 + n % nqi;
+            const int bh = b * Hq + hk * G + g;
+            for (int c = lane; c < BQ; c += 32) {
+                const int qr = i * BQ + c;
+                const bool ok = qr < L;
+                sLse[s * BQ + c] = ok ? lse[(long long)bh * L + qr] * kLog2e : INFINITY;
+                sD[s * BQ + c] = ok ? Dv[(long long)bh * L + qr] : 0.0f;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&qd_full[s], 2 * S::QD_BYTES);
+                for (int bx = 0; bx < NB; ++bx) {
+                    tma_load_3d(sQ + s * S::QD_BYTES + bx * (BQ * 128), &maps.q, &qd_full[s],
+                                bx * 64, i * BQ, bh);
+                    tma_load_3d(sdO + s * S::QD_BYTES + bx * (BQ * 128), &maps.dO, &qd_full[s],
+                                bx * 64, i * BQ, bh);
+                }
+            }
+            issued = n + 1;
+        }
+        if (lane == 0) {
+            for (int n = max(0, issued - QD_STAGES); n < issued; ++n)
+                mbar_wait_bounded(&qd_full[n % QD_STAGES], (n / QD_STAGES) & 1, err,
+                                  EDB_DEVERR_ATTN_PIPE);
+            mbar_wait_bounded(kv_full, 0, err, EDB_DEVERR_ATTN_PIPE);
+        }
+    } else if (warp == 9) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idSP = tc::idesc_bf16(BKV, BQ, 0, 0);   // S^T, dP^T
+            constexpr uint32_t idKV = tc::idesc_bf16(BKV, HD, 0, 1);   // dV, dK
+            constexpr uint32_t idQ = tc::idesc_bf16(BQ, HD, 1, 1);     // dQ
+            auto issue_sdp = [&](int n) {
+                const int s = n % QD_STAGES;
+                const uint8_t* q = sQ + s * S::QD_BYTES;
+                const uint8_t* o = sdO + s * S::QD_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk) {
+                    const int off_kv = (kk >> 2) * (BKV * 128) + (kk & 3) * 32;
+                    const int off_q = (kk >> 2) * (BQ * 128) + (kk & 3) * 32;
+                    tc::mma_bf16_ss(tmem + S::TM_S, tc::sdesc_sw128(sK + off_kv, 16, 1024),
+                                    tc::sdesc_sw128(q + off_q, 16, 1024), idSP, kk > 0);
+                    tc::mma_bf16_ss(tmem + S::TM_DP, tc::sdesc_sw128(sV + off_kv, 16, 1024),
+                                    tc::sdesc_sw128(o + off_q, 16, 1024), idSP, kk > 0);
+                }
+                tc::commit(sdp_full);
+            };
+            bool ok = mbar_wait_bounded(kv_full, 0, err, EDB_DEVERR_ATTN_PIPE) &&
+                      (N == 0 || mbar_wait_bounded(&qd_full[0], 0, err, EDB_DEVERR_ATTN_PIPE));
+            if (ok && N > 0) {
+                tc::fence_after_sync();
+                issue_sdp(0);
+            }
+            for (int n = 0; ok && n < N; ++n) {
+                if (n + 1 < N) {
+                    ok = !*abort_flag &&
+                         mbar_wait_bounded(&qd_full[(n + 1) % QD_STAGES],
+                                           ((n + 1) / QD_STAGES) & 1, err, EDB_DEVERR_ATTN_PIPE) &&
+                         mbar_wait_bounded(sdp_free, n & 1, err, EDB_DEVERR_ATTN_PIPE);
+                    if (!ok) break;
+                    tc::fence_after_sync();
+                    issue_sdp(n + 1);
+                }
+                ok = mbar_wait_bounded(pds_full, n & 1, err, EDB_DEVERR_ATTN_PIPE) &&
+                     (n == 0 || mbar_wait_bounded(dq_free, (n - 1) & 1, err, EDB_DEVERR_ATTN_PIPE));
+                if (!ok) break;
+                tc::fence_after_sync();
+                const int s = n % QD_STAGES;
+                const uint8_t* q = sQ + s * S::QD_BYTES;
+                const uint8_t* o = sdO + s * S::QD_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < BQ / 16; ++kk) {
+                    tc::mma_bf16_ss(tmem + S::TM_DV, tc::sdesc_sw128(sPt + kk * 32, 16, 1024),
+                                    tc::sdesc_sw128(o + kk * 2048, BQ * 128, 1024), idKV,
+                                    (n > 0 || kk > 0));
+                    tc::mma_bf16_ss(tmem + S::TM_DK, tc::sdesc_sw128(sDs + kk * 32, 16, 1024),
+                                    tc::sdesc_sw128(q + kk * 2048, BQ * 128, 1024), idKV,
+                                    (n > 0 || kk > 0));
+                }
+#pragma unroll
+                for (int kk = 0; kk < BKV / 16; ++kk)
+                    tc::mma_bf16_ss(tmem + S::TM_DQ, tc::sdesc_sw128(sDs + kk * 2048, BQ * 128, 1024),
+                                    tc::sdesc_sw128(sK + kk * 2048, BKV * 128, 1024), idQ, kk > 0);
+                tc::commit(mm2_done);
+                tc::commit(&qd_empty[s]);
+                tc::commit(dq_full);
+            }
+            if (!ok) *abort_flag = 1;
+            tc::commit(all_done);
+            mbar_wait_bounded(all_done, 0, err, EDB_DEVERR_ATTN_PIPE);
+        }
+    } else if (warp < 4) {
+        // ------------------------------------------------ P^T / dS^T compute
+        const int r = warp * 32 + lane;
+        const int kv_idx = kt * BKV + r;
+        const uint32_t lb = (uint32_t)(warp * 32) << 16;
+        for (int n = 0; n < N; ++n) {
+            const int s = n % QD_STAGES;
+            const int i = i0 + n % nqi;
+            if (*abort_flag ||
+                !mbar_wait_bounded(&qd_full[s], (n / QD_STAGES) & 1, err, EDB_DEVERR_ATTN_PIPE) ||
+                !mbar_wait_bounded(sdp_full, n & 1, err, EDB_DEVERR_ATTN_PIPE)) {
+                *abort_flag = 1;
+                break;
+            }
+            tc::fence_after_sync();
+            uint32_t sr[2][32], dr[2][32];
+            tc::tmem_ld32(tmem + S::TM_S + lb, sr[0]);
+            tc::tmem_ld32(tmem + S::TM_S + lb + 32, sr[1]);
+            tc::tmem_ld32(tmem + S::TM_DP + lb, dr[0]);
+            tc::tmem_ld32(tmem + S::TM_DP + lb + 32, dr[1]);
+            tc::tmem_wait_ld();
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sdp_free);
+            if (n > 0 && !mbar_wait_bounded(mm2_done, (n - 1) & 1, err, EDB_DEVERR_ATTN_PIPE)) {
+                *abort_flag = 1;
+                break;
+            }
+            const float* l2 = sLse + s * BQ;
+            const float* dd = sD + s * BQ;
+#pragma unroll
+            for (int ch = 0; ch < BQ / 8; ++ch) {
+                float p[8], ds[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const int c = ch * 8 + e;
+                    const int q_idx = i * BQ + c;
+                    const bool valid = kv_idx < L && (!CAUSAL || q_idx >= kv_idx);
+                    const float sv = __uint_as_float(sr[c >> 5][c & 31]);
+                    const float dpv = __uint_as_float(dr[c >> 5][c & 31]);
+                    p[e] = valid ? tc::ex2(fmaf(sv, scale_log2, -l2[c])) : 0.0f;
+                    ds[e] = p[e] * (dpv - dd[c]) * scale;
+                }
+                *reinterpret_cast<uint4*>(sPt + tc::sw128_off(r, ch)) =
+                    make_uint4(tc::pack_bf16x2(p[0], p[1]), tc::pack_bf16x2(p[2], p[3]),
+                               tc::pack_bf16x2(p[4], p[5]), tc::pack_bf16x2(p[6], p[7]));
+                *reinterpret_cast<uint4*>(sDs + tc::sw128_off(r, ch)) =
+                    make_uint4(tc::pack_bf16x2(ds[0], ds[1]), tc::pack_bf16x2(ds[2], ds[3]),
+                               tc::pack_bf16x2(ds[4], ds[5]), tc::pack_bf16x2(ds[6], ds[7]));
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(pds_full);
+        }
+    } else {
+        // ------------------------------------------------ dQ reduction + dK/dV epilogue (warps 4-7)
+        const int w = warp - 4;
+        const uint32_t lb = (uint32_t)(w * 32) << 16;
+        bool ok = true;
+        for (int n = 0; n < N; ++n) {
+            const int g = n / nqi, i = i0 + n % nqi;
+            const int bh = b * Hq + hk * G + g;
+            if (*abort_flag || !mbar_wait_bounded(dq_full, n & 1, err, EDB_DEVERR_ATTN_PIPE)) {
+                *abort_flag = 1;
+                ok = false;
+                break;
+            }
+            tc::fence_after_sync();
+            uint32_t qv[HD / 32][32];
+#pragma unroll
+            for (int cc = 0; cc < HD / 32; ++cc) tc::tmem_ld32(tmem + S::TM_DQ + lb + cc * 32, qv[cc]);
+            tc::tmem_wait_ld();
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(dq_free);
+            // M = 64 accumulator: lanes 32w + t (t < 16) hold query row 16w + t
+            const int q_row = i * BQ + 16 * w + lane;
+            if (lane < 16 && q_row < L) {
+                float* dst = dq_acc + ((long long)bh * L + q_row) * HD;
+#pragma unroll
+                for (int cc = 0; cc < HD / 32; ++cc)
+#pragma unroll
+                    for (int e = 0; e < 32; e += 4)
+                        red_add_v4(dst + cc * 32 + e, __uint_as_float(qv[cc][e]),
+                                   __uint_as_float(qv[cc][e + 1]), __uint_as_float(qv[cc][e + 2]),
+                                   __uint_as_float(qv[cc][e + 3]));
+            }
+        }
+        if (ok && mbar_wait_bounded(all_done, 0, err, EDB_DEVERR_ATTN_PIPE)) {
+            tc::fence_after_sync();
+            const int r = w * 32 + lane;
+            const int kv_idx = kt * BKV + r;
+#pragma unroll
+            for (int which = 0; which < 2; ++which) {
+                __nv_bfloat16* dst = (which == 0 ? dv : dk) + ((long long)bhk * L + kv_idx) * HD;
+                const uint32_t col = which == 0 ? S::TM_DV : S::TM_DK;
+#pragma unroll
+                for (int cc = 0; cc < HD / 32; ++cc) {
+                    uint32_t x[32];
+                    tc::tmem_ld32(tmem + col + lb + cc * 32, x);
+                    tc::tmem_wait_ld();
+                    if (kv_idx < L) {
+#pragma unroll
+                        for (int e = 0; e < 32; e += 8)
+                            st_global_v4(dst + cc * 32 + e,
+                                         make_uint4(tc::pack_bf16x2(__uint_as_float(x[e]), __uint_as_float(x[e + 1])),
+                                                    tc::pack_bf16x2(__uint_as_float(x[e + 2]), __uint_as_float(x[e + 3])),
+                                                    tc::pack_bf16x2(__uint_as_float(x[e + 4]), __uint_as_float(x[e + 5])),
+                                                    tc::pack_bf16x2(__uint_as_float(x[e + 6]), __uint_as_float(x[e + 7]))));
+                    }
+                }
+            }
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 9) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, S::TMEM_COLS);
+    }
+}
+
+// D = rowsum(dO (.) O), one warp per 4 rows (8 lanes x 16 bytes per 128-wide row)
+template <typename T>
+__global__ void attn_bwd_rowdot_kernel(const T* __restrict__ o, const T* __restrict__ dO,
+                                       float* __restrict__ D, long long rows, int d) {
+    const long long row = (long long)blockIdx.x * blockDim.y + threadIdx.y;
+    if (row >= rows) return;
+    float acc = 0.0f;
+    for (int e = threadIdx.x; e < d; e += blockDim.x)
+        acc = fmaf(ld_scalar<T>(o + row * d + e), ld_scalar<T>(dO + row * d + e), acc);
+    for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (threadIdx.x == 0) D[row] = acc;
+}
+
+template <typename T>
+__global__ void dq_convert_kernel(const float* __restrict__ acc, T* __restrict__ dq, long long n) {
+    const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i + 3 < n) {
+        const float4 v = *reinterpret_cast<const float4*>(acc + i);
+        st_scalar<T>(dq + i, v.x);
+        st_scalar<T>(dq + i + 1, v.y);
+        st_scalar<T>(dq + i + 2, v.z);
+        st_scalar<T>(dq + i + 3, v.w);
+    } else {
+        for (long long j = i; j < n; ++j) st_scalar<T>(dq + j, acc[j]);
+    }
+}
+
+// ------------------------------------------------------------ SIMT backward
+// lse of every query row (natural log), one thread per row
+template <typename T, int HDMAX>
+__global__ void attn_lse_simt_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                                     float* __restrict__ lse, int L, int Hq, int Hkv, int d,
+                                     int causal, float scale) {
+    const int hq = blockIdx.y, b = blockIdx.z;
+    const int hk = hq / (Hq / Hkv);
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= L) return;
+    const T* qi = q + (((long long)b * Hq + hq) * L + i) * d;
+    const T* kb = k + ((long long)b * Hkv + hk) * L * d;
+    float qv[HDMAX];
+    for (int e = 0; e < HDMAX; ++e) qv[e] = e < d ? ld_scalar<T>(qi + e) * scale * kLog2e : 0.0f;
+    float m = -INFINITY, l = 0.0f;
+    const int jend = causal ? i + 1 : L;
+    for (int j = 0; j < jend; ++j) {
+        float s = 0.0f;
+        for (int e = 0; e < d; ++e) s = fmaf(qv[e], ld_scalar<T>(kb + (long long)j * d + e), s);
+        const float mn = fmaxf(m, s);
+        l = l * exp2f(m - mn) + exp2f(s - mn);
+        m = mn;
+    }
+    lse[((long long)b * Hq + hq) * L + i] = (m + log2f(l)) / kLog2e;
+}
+
+template <typename T, int HDMAX>
+__global__ void attn_bwd_dq_simt_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                                        const T* __restrict__ v, const T* __restrict__ dO,
+                                        const float* __restrict__ lse, const float* __restrict__ Dv,
+                                        T* __restrict__ dq, int L, int Hq, int Hkv, int d,
+                                        int causal, float scale) {
+    const int hq = blockIdx.y, b = blockIdx.z;
+    const int hk = hq / (Hq / Hkv);
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= L) return;
+    const long long row = ((long long)b * Hq + hq) * L + i;
+    const T* kb = k + ((long long)b * Hkv + hk) * L * d;
+    const T* vb = v + ((long long)b * Hkv + hk) * L * d;
+    float qv[HDMAX], dov[HDMAX], acc[HDMAX];
+    for (int e = 0; e < HDMAX; ++e) {
+        qv[e] = e < d ? ld_scalar<T>(q + row * d + e) : 0.0f;
+        dov[e] = e < d ? ld_scalar<T>(dO + row * d + e) : 0.0f;
+        acc[e] = 0.0f;
+    }
+    const float l2 = lse[row] * kLog2e, Di = Dv[row];
+    const int jend = causal ? i + 1 : L;
+    for (int j = 0; j < jend; ++j) {
+        float s = 0.0f, dp = 0.0f;
+        for (int e = 0; e < d; ++e) {
+            s = fmaf(qv[e], ld_scalar<T>(kb + (long long)j * d + e), s);
+            dp = fmaf(dov[e], ld_scalar<T>(vb + (long long)j * d + e), dp);
+        }
+        const float p = exp2f(s * scale * kLog2e - l2);
+        const float ds = p * (dp - Di) * scale;
+        for (int e = 0; e < d; ++e) acc[e] = fmaf(ds, ld_scalar<T>(kb + (long long)j * d + e), acc[e]);
+    }
+    for (int e = 0; e < d; ++e) st_scalar<T>(dq + row * d + e, acc[e]);
+}
+
+template <typename T, int HDMAX>
+__global__ void attn_bwd_dkdv_simt_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                                          const T* __restrict__ v, const T* __restrict__ dO,
+                                          const float* __restrict__ lse,
+                                          const float* __restrict__ Dv, T* __restrict__ dk,
+                                          T* __restrict__ dvo, int L, int Hq, int Hkv, int d,
+                                          int causal, float scale) {
+    const int hk = blockIdx.y, b = blockIdx.z;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= L) return;
+    const int G = Hq / Hkv;
+    const long long krow = ((long long)b * Hkv + hk) * L + j;
+    float kv[HDMAX], vv[HDMAX], ak[HDMAX], av[HDMAX];
+    for (int e = 0; e < HDMAX; ++e) {
+        kv[e] = e < d ? ld_scalar<T>(k + krow * d + e) : 0.0f;
+        vv[e] = e < d ? ld_scalar<T>(v + krow * d + e) : 0.0f;
+        ak[e] = 0.0f;
+        av[e] = 0.0f;
+    }
+    for (int g = 0; g < G; ++g) {
+        const long long bh = (long long)b * Hq + hk * G + g;
+        for (int i = causal ? j : 0; i < L; ++i) {
+            const long long row = bh * L + i;
+            float s = 0.0f, dp = 0.0f;
+            for (int e = 0; e < d; ++e) {
+                s = fmaf(ld_scalar<T>(q + row * d + e), kv[e], s);
+                dp = fmaf(ld_scalar<T>(dO + row * d + e), vv[e], dp);
+            }
+            const float p = exp2f(s * scale * kLog2e - lse[row] * kLog2e);
+            const float ds = p * (dp - Dv[row]) * scale;
+            for (int e = 0; e < d; ++e) {
+                ak[e] = fmaf(ds, ld_scalar<T>(q + row * d + e), ak[e]);
+                av[e] = fmaf(p, ld_scalar<T>(dO + row * d + e), av[e]);
+            }
+        }
+    }
+    for (int e = 0; e < d; ++e) {
+        st_scalar<T>(dk + krow * d + e, ak[e]);
+        st_scalar<T>(dvo + krow * d + e, av[e]);
+    }
+}
+
+size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+bool tc_shape(int dtype, int head_dim) {
+    return dtype == EDB_BF16 && (head_dim == 64 || head_dim == 128);
+}
+
+template <int HD, bool CAUSAL>
+int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dO, const float* lse,
+                  const float* D, float* dq_acc, void* dk, void* dv, int B, int Hq, int Hkv, int L,
+                  float scale, cudaStream_t st) {
+    BwdMaps maps;
+    int s;
+    if ((s = tc::make_attn_map(&maps.q, q, HD, L, B * Hq, BQ))) return s;
+    if ((s = tc::make_attn_map(&maps.dO, dO, HD, L, B * Hq, BQ))) return s;
+    if ((s = tc::make_attn_map(&maps.k, k, HD, L, B * Hkv, BKV))) return s;
+    if ((s = tc::make_attn_map(&maps.v, v, HD, L, B * Hkv, BKV))) return s;
+    auto kern = attn_bwd_tc_kernel<HD, CAUSAL>;
+    const int smem = BwdSmem<HD>::TOTAL;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return (int)e;
+    dim3 grid((L + BKV - 1) / BKV, Hkv, B);
+    kern<<<grid, kBwdThreads, smem, st>>>(maps, lse, D, dq_acc, (__nv_bfloat16*)dk,
+                                          (__nv_bfloat16*)dv, L, Hq, Hkv, scale,
+                                          edb::device_error_word());
+    return edb::status_from_cuda(cudaGetLastError());
+}
+
+template <typename T>
+int launch_bwd_simt(const void* q, const void* k, const void* v, const void* dO, const float* lse,
+                    const float* D, void* dq, void* dk, void* dv, int B, int Hq, int Hkv, int L,
+                    int d, int causal, float scale, cudaStream_t st) {
+    dim3 gq((L + 63) / 64, Hq, B), gk((L + 63) / 64, Hkv, B);
+#define EDB_SIMT_BWD(HDM)                                                                        \
+    attn_bwd_dq_simt_kernel<T, HDM><<<gq, 64, 0, st>>>((const T*)q, (const T*)k, (const T*)v,   \
+                                                       (const T*)dO, lse, D, (T*)dq, L, Hq, Hkv, \
+                                                       d, causal, scale);                        \
+    attn_bwd_dkdv_simt_kernel<T, HDM><<<gk, 64, 0, st>>>((const T*)q, (const T*)k, (const T*)v, \
+                                                         (const T*)dO, lse, D, (T*)dk, (T*)dv,  \
+                                                         L, Hq, Hkv, d, causal, scale);
+    if (d <= 32) {
+        EDB_SIMT_BWD(32)
+    } else if (d <= 64) {
+        EDB_SIMT_BWD(64)
+    } else {
+        EDB_SIMT_BWD(128)
+    }
+#undef EDB_SIMT_BWD
+    return edb::status_from_cuda(cudaGetLastError());
+}
+
+template <typename T>
+int launch_lse_simt(const void* q, const void* k, float* lse, int B, int Hq, int Hkv, int L, int d,
+                    int causal, float scale, cudaStream_t st) {
+    dim3 g((L + 63) / 64, Hq, B);
+    if (d <= 32)
+        attn_lse_simt_kernel<T, 32><<<g, 64, 0, st>>>((const T*)q, (const T*)k, lse, L, Hq, Hkv, d,
+                                                      causal, scale);
+    else if (d <= 64)
+        attn_lse_simt_kernel<T, 64><<<g, 64, 0, st>>>((const T*)q, (const T*)k, lse, L, Hq, Hkv, d,
+                                                      causal, scale);
+    else
+        attn_lse_simt_kernel<T, 128><<<g, 64, 0, st>>>((const T*)q, (const T*)k, lse, L, Hq, Hkv,
+                                                       d, causal, scale);
+    return edb::status_from_cuda(cudaGetLastError());
+}
+
+}  // namespace
+
+// forward entry with the row log-sum-exp only (flash_attn.cu)
+int edb_attn_fwd_lse_only(int head_dim, int causal, const void* q, const void* k, float* lse,
+                          int B, int Hq, int Hkv, int L, float scale, cudaStream_t st);
+
+extern "C" size_t edb_flash_attention_bwd_workspace(int dtype, int batch, int q_heads,
+                                                    int kv_heads, int seq_len, int head_dim,
+                                                    int have_lse) {
+    if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || seq_len <= 0 || head_dim <= 0) return 0;
+    const size_t rows = (size_t)batch * q_heads * seq_len;
+    size_t ws = a256(rows * 4);                      // D
+    if (!have_lse) ws += a256(rows * 4);             // lse
+    if (tc_shape(dtype, head_dim)) ws += a256(rows * head_dim * 4);  // f32 dQ accumulator
+    return ws;
+}
+
+extern "C" int edb_flash_attention_bwd(int dtype, const void* q, const void* k, const void* v,
+                                       const void* o, const void* dO, const float* lse, void* dq,
+                                       void* dk, void* dv, int batch, int q_heads, int kv_heads,
+                                       int seq_len, int head_dim, int causal, float scale,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
+    if (dtype != EDB_F32 && dtype != EDB_BF16) return EDB_ERR_BAD_DTYPE;
+    if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || seq_len <= 0 || head_dim <= 0)
+        return EDB_ERR_BAD_SHAPE;
+    if (q_heads % kv_heads != 0) return EDB_ERR_BAD_SHAPE;
+    if (head_dim > 128) return EDB_ERR_UNSUPPORTED;
+    if (!q || !k || !v || !o || !dO || !dq || !dk || !dv) return EDB_ERR_NULL_POINTER;
+    const size_t need = edb_flash_attention_bwd_workspace(dtype, batch, q_heads, kv_heads,
+                                                          seq_len, head_dim, lse != nullptr);
+    if (workspace_bytes < need || !workspace) return EDB_ERR_WORKSPACE_TOO_SMALL;
+    if (!edb::aligned16(workspace)) return EDB_ERR_MISALIGNED;
+    if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)head_dim);
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t rows = (size_t)batch * q_heads * seq_len;
+    char* w = static_cast<char*>(workspace);
+    float* D = reinterpret_cast<float*>(w);
+    w += a256(rows * 4);
+    const float* L_ = lse;
+    float* lse_ws = nullptr;
+    if (!lse) {
+        lse_ws = reinterpret_cast<float*>(w);
+        w += a256(rows * 4);
+        L_ = lse_ws;
+    }
+    const bool use_tc = tc_shape(dtype, head_dim) && edb::aligned16(q) && edb::aligned16(k) &&
+                        edb::aligned16(v) && edb::aligned16(dO) && edb::aligned16(dk) &&
+                        edb::aligned16(dv);
+    // D = rowsum(dO * O)
+    {
+        dim3 blk(32, 4);
+        const unsigned nb = (unsigned)((rows + 3) / 4);
+        if (dtype == EDB_BF16)
+            attn_bwd_rowdot_kernel<__nv_bfloat16><<<nb, blk, 0, st>>>(
+                (const __nv_bfloat16*)o, (const __nv_bfloat16*)dO, D, (long long)rows, head_dim);
+        else
+            attn_bwd_rowdot_kernel<float><<<nb, blk, 0, st>>>((const float*)o, (const float*)dO, D,
+                                                              (long long)rows, head_dim);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return (int)e;
+    }
+    if (lse_ws) {
+        int s;
+        if (use_tc)
+            s = edb_attn_fwd_lse_only(head_dim, causal, q, k, lse_ws, batch, q_heads, kv_heads,
+                                      seq_len, scale, st);
+        else
+            s = dtype == EDB_BF16
+                    ? launch_lse_simt<__nv_bfloat16>(q, k, lse_ws, batch, q_heads, kv_heads,
+                                                     seq_len, head_dim, causal, scale, st)
+                    : launch_lse_simt<float>(q, k, lse_ws, batch, q_heads, kv_heads, seq_len,
+                                             head_dim, causal, scale, st);
+        if (s) return s;
+    }
+    if (use_tc) {
+        float* acc = reinterpret_cast<float*>(w);
+        const size_t nel = rows * head_dim;
+        cudaError_t e = cudaMemsetAsync(acc, 0, nel * 4, st);
+        if (e != cudaSuccess) return (int)e;
+        int s;
+        if (head_dim == 128)
+            s = causal ? launch_bwd_tc<128, true>(q, k, v, dO, L_, D, acc, dk, dv, batch, q_heads,
+                                                  kv_heads, seq_len, scale, st)
+                       : launch_bwd_tc<128, false>(q, k, v, dO, L_, D, acc, dk, dv, batch, q_heads,
+                                                   kv_heads, seq_len, scale, st);
+        else
+            s = causal ? launch_bwd_tc<64, true>(q, k, v, dO, L_, D, acc, dk, dv, batch, q_heads,
+                                                 kv_heads, seq_len, scale, st)
+                       : launch_bwd_tc<64, false>(q, k, v, dO, L_, D, acc, dk, dv, batch, q_heads,
+                                                  kv_heads, seq_len, scale, st);
+        if (s) return s;
+        const unsigned nb = (unsigned)((nel / 4 + 255) / 256);
+        dq_convert_kernel<__nv_bfloat16><<<nb, 256, 0, st>>>(acc, (__nv_bfloat16*)dq,
+                                                            (long long)nel);
+        return edb::status_from_cuda(cudaGetLastError());
+    }
+    return dtype == EDB_BF16
+               ? launch_bwd_simt<__nv_bfloat16>(q, k, v, dO, L_, D, dq, dk, dv, batch, q_heads,
+                                                kv_heads, seq_len, head_dim, causal, scale, st)
+               : launch_bwd_simt<float>(q, k, v, dO, L_, D, dq, dk, dv, batch, q_heads, kv_heads,
+                                        seq_len, head_dim, causal, scale, st);
+}

@@ -164,4 +164,15 @@ static __device__ __forceinline__ void named_bar(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// 3D bf16 tensor map [nbh][L][d] (d contiguous) with SWIZZLE_128B boxes of
+// 64 columns x box_rows rows; rows past L read as zero and are not written.
+inline int make_attn_map(CUtensorMap* m, const void* p, int d, int L, int nbh, int box_rows) {
+    const cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)L, (cuuint64_t)nbh};
+    const cuuint64_t strides[2] = {(cuuint64_t)d * 2, (cuuint64_t)L * d * 2};
+    const cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+    CUresult r = edb::encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(p),
+                                   dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    return r == CUDA_SUCCESS ? EDB_OK : EDB_ERR_UNSUPPORTED;
+}
+
 }  // namespace tc

@@ -218,6 +218,43 @@ def flash_attention(q, k, v, causal=False, scale=None, return_lse=False):
     return (o, lse) if return_lse else o
 
 
+def flash_attention_backward(q, k, v, causal, forward_out, grad_output, lse=None, scale=None):
+    """Returns (grad_q, grad_k, grad_v).  Mirrors flash_attention_backward_dispatch/6
+    (fused_scan.ex:3510-3525); lse (from flash_attention(return_lse=True)) is
+    optional and recomputed when absent."""
+    _dev(q, k, v, forward_out, grad_output, lse, what="flash_attention_backward")
+    B, Hq, Hkv, L, d = _attn_shapes(q, k, v)
+    lib = _lib.load()
+    code = _dtype_code(q, "flash_attention_backward")
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    wsb = lib.edb_flash_attention_bwd_workspace(code, B, Hq, Hkv, L, d, int(lse is not None))
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=q.device)
+    _lib.check(lib.edb_flash_attention_bwd(code, _p(q), _p(k), _p(v), _p(forward_out),
+                                           _p(grad_output), _p(lse), _p(dq), _p(dk), _p(dv), B,
+                                           Hq, Hkv, L, d, int(bool(causal)), float(scale or 0.0),
+                                           _p(ws), wsb, _stream()),
+               "CUDA flash attention backward")
+    return dq, dk, dv
+
+
+class FlashAttentionFn(torch.autograd.Function):
+    """custom_grad wiring of flash_attention_custom_call/4 (fused_scan.ex:3427-3443):
+    gradients to q, k, v."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, causal=False):
+        o, lse = flash_attention(q, k, v, causal=causal, return_lse=True)
+        ctx.causal = causal
+        ctx.save_for_backward(q, k, v, o, lse)
+        return o
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        q, k, v, o, lse = ctx.saved_tensors
+        dq, dk, dv = flash_attention_backward(q, k, v, ctx.causal, o, grad_output.contiguous(), lse)
+        return dq, dk, dv, None
+
+
 class SelectiveScanFn(torch.autograd.Function):
     """custom_grad wiring of selective_scan_custom_call/5 (fused_scan.ex:2595-2611):
     gradients to x, dt, B, C; A gets none."""

@@ -90,4 +90,22 @@ int fused_flash_attention_launch(cudaStream_t stream, const edb_io_t* q, const e
                                    seq_len, head_dim, causal, 0.0f, stream);
 }
 
+int fused_flash_attention_backward_launch(cudaStream_t stream, const edb_io_t* q,
+                                          const edb_io_t* k, const edb_io_t* v,
+                                          const edb_io_t* o, const edb_io_t* grad_o,
+                                          edb_io_t* output_concat, int batch, int num_heads,
+                                          int seq_len, int head_dim, int causal) {
+    const long long n = (long long)batch * num_heads * seq_len * head_dim;
+    const size_t wsb = edb_flash_attention_bwd_workspace(kDtype, batch, num_heads, num_heads,
+                                                         seq_len, head_dim, 0);
+    void* ws = nullptr;
+    cudaError_t e = cudaMallocAsync(&ws, wsb, stream);
+    if (e != cudaSuccess) return (int)e;
+    int st = edb_flash_attention_bwd(kDtype, q, k, v, o, grad_o, nullptr, output_concat,
+                                     output_concat + n, output_concat + 2 * n, batch, num_heads,
+                                     num_heads, seq_len, head_dim, causal, 0.0f, ws, wsb, stream);
+    cudaFreeAsync(ws, stream);
+    return st;
+}
+
 }  // extern "C"

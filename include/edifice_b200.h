@@ -152,6 +152,24 @@ int edb_flash_attention_fwd(int dtype, const void* q, const void* k, const void*
                             float* lse, int batch, int q_heads, int kv_heads, int seq_len,
                             int head_dim, int causal, float scale, void* stream);
 
+/* Workspace bytes edb_flash_attention_bwd needs (have_lse: the forward's lse
+ * will be passed). */
+size_t edb_flash_attention_bwd_workspace(int dtype, int batch, int q_heads, int kv_heads,
+                                         int seq_len, int head_dim, int have_lse);
+
+/* Backward given o (forward output) and dO: dq [B,Hq,L,d], dk/dv [B,Hkv,L,d]
+ * in `dtype` (dk, dv of a kv head sum over its query heads).  lse may be NULL
+ * (recomputed).  Caller-provided workspace, 16-byte aligned.
+ * Replaces fused_flash_attention_backward_launch
+ * (native/cuda/fused_flash_attention_backward.cu:355-408, which cudaMallocs and
+ * cudaFrees its scratch synchronously on every call); Nx semantics
+ * lib/edifice/cuda/fused_scan.ex:3527-3574. */
+int edb_flash_attention_bwd(int dtype, const void* q, const void* k, const void* v, const void* o,
+                            const void* dO, const float* lse, void* dq, void* dk, void* dv,
+                            int batch, int q_heads, int kv_heads, int seq_len, int head_dim,
+                            int causal, float scale, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
 /* Capacity of the library's built-in scratch array used by
  * edb_selective_scan_bwd_noalloc (16 MiB; every GPU that loads the library
  * holds it until the process exits). */

@@ -73,6 +73,15 @@ int fused_flash_attention_launch(cudaStream_t stream, const edb_io_t* q, const e
                                  const edb_io_t* v, edb_io_t* output, int batch, int num_heads,
                                  int seq_len, int head_dim, int causal);
 
+/* native/cuda/fused_flash_attention_backward.cu:355-408;
+ * output_concat = [dq | dk | dv], each B*H*T*d io elements.  Scratch is taken
+ * stream-ordered (cudaMallocAsync / cudaFreeAsync). */
+int fused_flash_attention_backward_launch(cudaStream_t stream, const edb_io_t* q,
+                                          const edb_io_t* k, const edb_io_t* v,
+                                          const edb_io_t* o, const edb_io_t* grad_o,
+                                          edb_io_t* output_concat, int batch, int num_heads,
+                                          int seq_len, int head_dim, int causal);
+
 #ifdef __cplusplus
 }
 #endif

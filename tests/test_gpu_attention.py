@@ -127,3 +127,106 @@ def test_legacy_shim_forward(cuda, prec, dtype):
     assert lib.fused_flash_attention_launch(None, P(q), P(k), P(v), P(o), B, H, L, d, 1) == 0
     torch.cuda.synchronize()
     assert torch.equal(o, fs.flash_attention(q, k, v, causal=True))
+
+
+# ------------------------------------------------------------------ backward
+BWD_CASES = [
+    (1, 2, 2, 128, 128),
+    (2, 4, 2, 256, 128),
+    (1, 8, 2, 300, 128),   # partial tiles
+    (2, 4, 4, 64, 128),
+    (1, 2, 1, 1000, 64),
+    (2, 4, 2, 37, 8),      # SIMT path
+    (1, 4, 1, 130, 96),    # SIMT path
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("case", BWD_CASES)
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("with_lse", [True, False])
+def test_attention_backward(cuda, dtype, case, causal, with_lse):
+    q, k, v, do = attn_inputs(*case, dtype, seed=43)
+    o, lse = fs.flash_attention(q, k, v, causal=causal, return_lse=True)
+    dq, dk, dv = fs.flash_attention_backward(q, k, v, causal, o, do, lse if with_lse else None)
+    torch.cuda.synchronize()
+    ref = O.attention_bwd(_np(q), _np(k), _np(v), _np(do), causal=causal)
+    for got, r in zip((dq, dk, dv), ref):
+        assert O.norm_rel(_np(got), r) <= TOL[dtype], O.norm_rel(_np(got), r)
+    assert device_errors() == 0
+
+
+@pytest.mark.parametrize("layer", [0, 1])
+def test_attention_backward_golden_gqa(cuda, layer):
+    g = np.load(os.path.join(GOLD, "gqa_fixture.npz"))
+    q, k, v, do = (torch.tensor(g["%s%d" % (n, layer)]).cuda() for n in ("q", "k", "v", "do"))
+    o = fs.flash_attention(q, k, v, causal=True)
+    dq, dk, dv = fs.flash_attention_backward(q, k, v, True, o, do)
+    torch.cuda.synchronize()
+    for got, n in zip((dq, dk, dv), ("dq", "dk", "dv")):
+        np.testing.assert_allclose(_np(got), g["%s%d" % (n, layer)], atol=5e-5)
+
+
+def test_attention_backward_mid_size_full_oracle(cuda):
+    """B1 Hq8 Hkv2 L2048 d128 causal bf16: every gradient against the f64 oracle."""
+    q, k, v, do = attn_inputs(1, 8, 2, 2048, 128, torch.bfloat16, seed=44)
+    o, lse = fs.flash_attention(q, k, v, causal=True, return_lse=True)
+    dq, dk, dv = fs.flash_attention_backward(q, k, v, True, o, do, lse)
+    torch.cuda.synchronize()
+    O.set_threads(os.cpu_count() or 8)
+    ref = O.attention_bwd(_np(q), _np(k), _np(v), _np(do), causal=True)
+    for got, r in zip((dq, dk, dv), ref):
+        assert O.norm_rel(_np(got), r) <= 2e-2
+
+
+def test_config3_backward_vs_torch_fp32(cuda):
+    """BASELINE configs[3] at full size (B4 Hq32 Hkv8 L8192 d128, causal):
+    forward + backward against torch's fp32 SDPA (memory-efficient backend, K/V
+    repeated over the group, dK/dV summed back) on the same bf16-rounded inputs."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    B, Hq, Hkv, L, d = 4, 32, 8, 8192, 128
+    q, k, v, do = attn_inputs(B, Hq, Hkv, L, d, torch.bfloat16, seed=0)
+    o, lse = fs.flash_attention(q, k, v, causal=True, return_lse=True)
+    dq, dk, dv = fs.flash_attention_backward(q, k, v, True, o, do, lse)
+    torch.cuda.synchronize()
+    assert device_errors() == 0
+    G = Hq // Hkv
+    qf = q.float().requires_grad_(True)
+    kf = k.float().requires_grad_(True)
+    vf = v.float().requires_grad_(True)
+    with sdpa_kernel(SDPBackend.EFFICIENT_ATTENTION):
+        of = torch.nn.functional.scaled_dot_product_attention(
+            qf, kf.repeat_interleave(G, 1), vf.repeat_interleave(G, 1), is_causal=True)
+    of.backward(do.float())
+    rel = lambda a, b: ((a.float() - b).norm() / b.norm()).item()
+    assert rel(o, of.detach()) <= 2e-2
+    assert rel(dq, qf.grad) <= 2e-2
+    assert rel(dk, kf.grad) <= 2e-2
+    assert rel(dv, vf.grad) <= 2e-2
+
+
+@pytest.mark.parametrize("prec,dtype", [("f32", torch.float32), ("bf16", torch.bfloat16)])
+def test_legacy_shim_backward(cuda, prec, dtype):
+    lib = ctypes.CDLL(build.SHIMS[prec])
+    B, H, L, d = 2, 4, 256, 128
+    q, k, v, do = attn_inputs(B, H, H, L, d, dtype, seed=45)
+    o = fs.flash_attention(q, k, v, causal=True)
+    cat = torch.empty(3 * q.numel(), dtype=dtype, device="cuda")
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    assert lib.fused_flash_attention_backward_launch(None, P(q), P(k), P(v), P(o), P(do), P(cat),
+                                                     B, H, L, d, 1) == 0
+    torch.cuda.synchronize()
+    ref = O.attention_bwd(_np(q), _np(k), _np(v), _np(do), causal=True)
+    n = q.numel()
+    for idx, r in enumerate(ref):
+        assert O.norm_rel(_np(cat[idx * n:(idx + 1) * n]).reshape(r.shape), r) <= TOL[dtype]
+
+
+def test_autograd_fn(cuda):
+    q, k, v, do = attn_inputs(1, 4, 2, 200, 128, torch.bfloat16, seed=46)
+    leaves = [t.clone().requires_grad_(True) for t in (q, k, v)]
+    o = fs.FlashAttentionFn.apply(*leaves, True)
+    o.backward(do)
+    ref = O.attention_bwd(_np(q), _np(k), _np(v), _np(do), causal=True)
+    for leaf, r in zip(leaves, ref):
+        assert O.norm_rel(_np(leaf.grad), r) <= 2e-2
