@@ -2,26 +2,32 @@
 """Benchmark of the fused sequence-mixing hot path on B200 (one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config linear|mingru]
+                    [--config linear|mingru|ssm|attn] [--no-paths]
 
-Default workload: BASELINE configs[1] -- the diagonal linear-RNN scan
-h_t = a_t h_{t-1} + b_t, forward + backward, bf16 io / f32 state,
-batch 8 x seq 4096 x hidden 2048 per GPU (weak scaling: rank r owns batch
-rows [8r, 8r+8) of a global batch of 8N, no collective on the data path).
-A step = one forward + one backward pass over the shard; tokens = batch*seq.
+Headline (default --config linear): BASELINE configs[1] -- the diagonal
+linear-RNN scan h_t = a_t h_{t-1} + b_t, forward + backward, bf16 io / f32
+state, batch 8 x seq 4096 x hidden 2048 per GPU.  A step = one forward + one
+backward pass over the rank's shard; tokens = batch * seq.  Weak scaling: rank r
+owns units [rU, (r+1)U) of a global problem of N shards (batch rows; (batch,
+kv-group) pairs for attention), inputs seeded per unit, no collective on the
+data path.
 
---impl ours       our kernels (libedifice_b200.so); device-timed with CUDA
-                  events, max over ranks; plus e2e through the public API with
-                  host buffers, roofline of the dominant kernel, CPU baseline.
---impl reference  the reference algorithm on the host CPU (the oracle port of
-                  Edifice's Nx fallbacks, f32, OpenMP over all host cores);
+The headline line also carries `paths`: the other implemented configs
+(MinGRU form of configs[1], configs[3] causal GQA attention, configs[4] Mamba
+selective scan), each timed the same way over min(K, 20) steps.
+
+--impl ours       our kernels (libedifice_b200.so): device-timed with CUDA
+                  events, max over ranks; e2e through the public API with host
+                  buffers; roofline of the dominant kernel; CPU baseline.
+--impl reference  the reference algorithm on the host CPU (the oracle's f32
+                  port of Edifice's Nx fallbacks, OpenMP over all host cores);
                   rank 0 only.
-
 Under torchrun every rank joins an NCCL group used only for the barrier and
 the max-over-ranks reduction of the elapsed time.
 """
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -39,9 +45,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["linear", "mingru"], default="linear")
+    ap.add_argument("--config", choices=["linear", "mingru", "ssm", "attn"], default="linear")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-paths", action="store_true")
     return ap.parse_args()
 
 
@@ -52,7 +59,7 @@ def dist_env():
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampler for the timed region (100 ms period)."""
+    """nvidia-smi clocks/throttle sampler for the timed region (20 ms period)."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -67,7 +74,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
-                 "-i", str(self.gpu), "-lms", "100"],
+                 "-i", str(self.gpu), "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
@@ -94,13 +101,16 @@ class ClockSampler:
             return None
         inside = [r for t, r in self.rows if t0 <= t <= t1]
         used = inside if inside else [r for _, r in self.rows]
-        sm = [float(r[1]) for r in used if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in used if r[2].replace(".", "").isdigit()]
+        num = lambda s: s.replace(".", "", 1).isdigit()
+        sm = [float(r[1]) for r in used if len(r) > 1 and num(r[1])]
+        mx = [float(r[2]) for r in used if len(r) > 2 and num(r[2])]
+        pw = [float(r[3]) for r in used if len(r) > 3 and num(r[3])]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in used for i in range(4)
                           if len(r) > 5 + i and r[5 + i].lower().startswith("active")})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "power_w_max": max(pw) if pw else None,
                 "samples": len(inside), "window": "timed" if inside else "whole run"}
 
 
@@ -109,8 +119,12 @@ def measured_peaks():
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
-    return 6650.0, "fallback (6.65 TB/s pool measurement)"
+        return {"hbm": (float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"),
+                "tensor": (float(d["bf16_tflops_sustained"]),
+                           "measured (MEASURED_PEAKS.json bf16_tflops_sustained: the kernel runs "
+                           "back to back inside a seconds-long step loop)")}
+    return {"hbm": (6650.0, "fallback (6.65 TB/s pool measurement)"),
+            "tensor": (1400.0, "fallback (1.4 PFLOP/s sustained pool measurement)")}
 
 
 def ncu_traffic(kernel_key):
@@ -124,27 +138,6 @@ def ncu_traffic(kernel_key):
     return None if e is None else e.get("traffic_bytes_per_launch")
 
 
-# ------------------------------------------------------------- CPU baseline
-def cpu_scan_step(cfg, a, b, dy, prec="f32"):
-    import oracle as O
-    if cfg.mingru:
-        h = O.mingru_fwd(a, b, prec=prec)
-        O.mingru_bwd(a, b, None, h, dy, prec=prec)
-    else:
-        h = O.linear_scan_fwd(a, b, prec=prec)
-        O.linear_scan_bwd(a, None, h, dy, prec=prec)
-
-
-def cpu_sample(cfg, rows, seed=0):
-    import numpy as np
-    rng = np.random.default_rng(seed)
-    shp = (rows, cfg.seq_len, cfg.hidden)
-    a = (1 / (1 + np.exp(-rng.standard_normal(shp, dtype=np.float32)))).astype(np.float32)
-    b = rng.standard_normal(shp, dtype=np.float32)
-    dy = rng.standard_normal(shp, dtype=np.float32)
-    return a, b, dy
-
-
 def cpu_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -152,116 +145,359 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
-def time_cpu_baseline(cfg, budget_s=15.0):
-    """Oracle f32 port, all host threads, on `rows` batch rows of the config;
-    repeats until ~budget_s of CPU work.  Returns the cpu_baseline object."""
+# ---------------------------------------------------------------- workloads
+class ScanWorkload:
+    """linear scan (or its MinGRU form) fwd + bwd."""
+
+    def __init__(self, mingru=False):
+        from edifice_b200.shard import ScanConfig
+        self.cfg = ScanConfig(name="mingru_cfg1", mingru=True) if mingru else ScanConfig()
+        self.kname = "mingru" if mingru else "linear_scan"
+        self.dtype = "bf16"
+
+    def describe(self, world):
+        c = self.cfg
+        return {"workload": "%s fwd+bwd (BASELINE configs[1]%s)" %
+                            (c.name, ", MinGRU form" if c.mingru else ""),
+                "batch_per_gpu": c.batch, "global_batch": c.batch * world, "seq_len": c.seq_len,
+                "hidden": c.hidden, "parallelism": "dp%d (batch-row shards, no collective)" % world,
+                "l2": "inputs larger than L2 (%.2f GB touched per step > 126 MB)"
+                      % ((c.bytes_fwd() + c.bytes_bwd()) / 1e9)}
+
+    def setup(self, dev, rank):
+        from edifice_b200 import shard
+        self.units = shard.plan_units(self.cfg.units, rank, self._world)
+        self.a, self.b, self.dy = shard.scan_inputs(self.cfg, self.units, dev)
+
+    def kernels(self):
+        return {"fwd": ("hbm", self.cfg.bytes_fwd()), "bwd": ("hbm", self.cfg.bytes_bwd())}
+
+    launches_per_step = 2
+    tokens = property(lambda self: self.cfg.tokens)
+
+    def _fwd(self, a, b):
+        from edifice_b200 import fused_scan as fs
+        return fs.mingru_scan(a, b) if self.cfg.mingru else fs.linear_scan(a, b)
+
+    def _bwd(self, a, b, h, dy):
+        from edifice_b200 import fused_scan as fs
+        if self.cfg.mingru:
+            return fs.mingru_backward(a, b, None, h, dy)
+        return fs.linear_scan_backward(a, None, h, dy)
+
+    def step(self, ev=None):
+        if ev:
+            ev[0].record()
+        h = self._fwd(self.a, self.b)
+        if ev:
+            ev[1].record()
+        self._bwd(self.a, self.b, h, self.dy)
+        if ev:
+            ev[2].record()
+
+    def host_inputs(self):
+        return [self.a, self.b, self.dy]
+
+    def e2e_step(self, dev_in):
+        a, b, dy = dev_in
+        h = self._fwd(a, b)
+        return (h,) + tuple(self._bwd(a, b, h, dy))
+
+    api = property(lambda self: "edifice_b200.fused_scan.%s + backward" %
+                   ("mingru_scan" if self.cfg.mingru else "linear_scan"))
+
+    def cpu_step(self, rows=None, prec="f32"):
+        import numpy as np
+        import oracle as O
+        c = self.cfg
+        rows = rows or c.batch
+        if not hasattr(self, "_cpu") or self._cpu[0] != rows:
+            rng = np.random.default_rng(0)
+            shp = (rows, c.seq_len, c.hidden)
+            a = (1 / (1 + np.exp(-rng.standard_normal(shp, dtype=np.float32)))).astype(np.float32)
+            self._cpu = (rows, a, rng.standard_normal(shp, dtype=np.float32),
+                         rng.standard_normal(shp, dtype=np.float32))
+        _, a, b, dy = self._cpu
+        if c.mingru:
+            h = O.mingru_fwd(a, b, prec=prec)
+            O.mingru_bwd(a, b, None, h, dy, prec=prec)
+        else:
+            h = O.linear_scan_fwd(a, b, prec=prec)
+            O.linear_scan_bwd(a, None, h, dy, prec=prec)
+        return rows * c.seq_len  # tokens processed
+
+    cpu_what = ("oracle f32 port of the Nx fallbacks (fused_scan.ex:4429-4444, 884-916; "
+                "MinGRU :516-528, 548-581)")
+
+
+class SsmWorkload:
+    """Mamba selective scan fwd (with chunk checkpoints) + bwd."""
+
+    def __init__(self):
+        from edifice_b200.shard import SsmConfig
+        self.cfg = SsmConfig()
+        self.kname = "selective_scan"
+        self.dtype = "bf16"
+
+    def describe(self, world):
+        c = self.cfg
+        return {"workload": "%s fwd+bwd (BASELINE configs[4])" % c.name,
+                "batch_per_gpu": c.batch, "global_batch": c.batch * world, "seq_len": c.seq_len,
+                "d_inner": c.d_inner, "d_state": c.d_state,
+                "parallelism": "dp%d (batch-row shards, no collective)" % world,
+                "l2": "inputs larger than L2 (%.1f GB per step)"
+                      % ((c.bytes_fwd() + c.bytes_bwd()) / 1e9)}
+
+    def setup(self, dev, rank):
+        from edifice_b200 import shard
+        self.units = shard.plan_units(self.cfg.units, rank, self._world)
+        self.x, self.dt, self.A, self.B, self.C, self.dy = shard.ssm_inputs(self.cfg, self.units, dev)
+
+    def kernels(self):
+        return {"fwd": ("hbm", self.cfg.bytes_fwd()), "bwd": ("hbm", self.cfg.bytes_bwd())}
+
+    launches_per_step = 3  # fwd, bwd, dB/dC reduce
+    tokens = property(lambda self: self.cfg.tokens)
+
+    def step(self, ev=None):
+        from edifice_b200 import fused_scan as fs
+        if ev:
+            ev[0].record()
+        _, ck = fs.selective_scan(self.x, self.dt, self.A, self.B, self.C, with_ckpt=True)
+        if ev:
+            ev[1].record()
+        fs.selective_scan_backward(self.x, self.dt, self.A, self.B, self.C, self.dy, ck)
+        if ev:
+            ev[2].record()
+
+    def host_inputs(self):
+        return [self.x, self.dt, self.A, self.B, self.C, self.dy]
+
+    def e2e_step(self, dev_in):
+        from edifice_b200 import fused_scan as fs
+        x, dt, A, B, C, dy = dev_in
+        y, ck = fs.selective_scan(x, dt, A, B, C, with_ckpt=True)
+        return (y,) + tuple(fs.selective_scan_backward(x, dt, A, B, C, dy, ck))
+
+    api = "edifice_b200.fused_scan.selective_scan + backward"
+
+    def extra(self, fwd_ms, bwd_ms):
+        e = self.cfg.exps_fwd()
+        return {"fwd_exp_per_s": e / (fwd_ms / 1000.0),
+                "note": "exp-bound: one ex2 per (t,d,n) in the forward; the MUFU rate "
+                        "(16/clk/SM) caps the config-4 forward near 7.6 ms at 1.9 GHz"}
+
+    def cpu_step(self, rows=None, prec="f32"):
+        import numpy as np
+        import oracle as O
+        c = self.cfg
+        ch = 128
+        if not hasattr(self, "_cpu"):
+            rng = np.random.default_rng(0)
+            x = rng.standard_normal((1, c.seq_len, ch), dtype=np.float32)
+            dt = np.log1p(np.exp(rng.standard_normal((1, c.seq_len, ch)) * 0.5 - 2)).astype(np.float32)
+            A = (-np.exp(rng.uniform(0, math.log(16), (ch, c.d_state)))).astype(np.float32)
+            B = rng.standard_normal((1, c.seq_len, c.d_state), dtype=np.float32)
+            C = rng.standard_normal((1, c.seq_len, c.d_state), dtype=np.float32)
+            dy = rng.standard_normal((1, c.seq_len, ch), dtype=np.float32)
+            self._cpu = (x, dt, A, B, C, dy)
+        x, dt, A, B, C, dy = self._cpu
+        O.selective_scan_fwd(x, dt, A, B, C, prec=prec)
+        O.selective_scan_bwd(x, dt, A, B, C, dy, prec=prec)
+        return c.seq_len * ch / c.d_inner  # token-equivalents (one row, 128 of 4096 channels)
+
+    cpu_what = ("oracle f32 port (kernel semantics, backward_kernels_test.exs:1563-1586 + "
+                "fused_scan.ex:1453-1531) on 1 batch row x 128 of 4096 channels, scaled")
+
+
+class AttnWorkload:
+    """causal GQA attention fwd (with lse) + bwd."""
+
+    def __init__(self):
+        from edifice_b200.shard import AttnConfig
+        self.cfg = AttnConfig()
+        self.kname = "flash_attention"
+        self.dtype = "bf16"
+
+    def describe(self, world):
+        c = self.cfg
+        return {"workload": "%s fwd+bwd (BASELINE configs[3])" % c.name,
+                "batch_per_gpu": c.batch, "global_batch": c.batch * world, "q_heads": c.q_heads,
+                "kv_heads": c.kv_heads, "seq_len": c.seq_len, "head_dim": c.head_dim,
+                "causal": c.causal,
+                "parallelism": "dp%d ((batch, kv-group) shards, no collective)" % world,
+                "l2": "tensor-bound; q/k/v/dO 0.67 GB per step"}
+
+    def setup(self, dev, rank):
+        from edifice_b200 import shard
+        self.units = shard.plan_units(self.cfg.units, rank, self._world)
+        self.q, self.k, self.v, self.do = shard.attn_inputs(self.cfg, self.units, dev)
+
+    def kernels(self):
+        return {"fwd": ("tensor", self.cfg.flops_fwd()), "bwd": ("tensor", self.cfg.flops_bwd())}
+
+    launches_per_step = 4  # fwd, rowdot, bwd, dq convert
+    tokens = property(lambda self: self.cfg.tokens)
+
+    def step(self, ev=None):
+        from edifice_b200 import fused_scan as fs
+        if ev:
+            ev[0].record()
+        o, lse = fs.flash_attention(self.q, self.k, self.v, causal=True, return_lse=True)
+        if ev:
+            ev[1].record()
+        fs.flash_attention_backward(self.q, self.k, self.v, True, o, self.do, lse)
+        if ev:
+            ev[2].record()
+
+    def host_inputs(self):
+        return [self.q, self.k, self.v, self.do]
+
+    def e2e_step(self, dev_in):
+        from edifice_b200 import fused_scan as fs
+        q, k, v, do = dev_in
+        o, lse = fs.flash_attention(q, k, v, causal=True, return_lse=True)
+        return (o,) + tuple(fs.flash_attention_backward(q, k, v, True, o, do, lse))
+
+    api = "edifice_b200.fused_scan.flash_attention + flash_attention_backward"
+
+    def cpu_step(self, rows=None, prec="f32"):
+        import numpy as np
+        import oracle as O
+        c = self.cfg
+        Ls = 1024
+        if not hasattr(self, "_cpu"):
+            rng = np.random.default_rng(0)
+            q = rng.standard_normal((1, 4, Ls, c.head_dim), dtype=np.float32)
+            k = rng.standard_normal((1, 1, Ls, c.head_dim), dtype=np.float32)
+            v = rng.standard_normal((1, 1, Ls, c.head_dim), dtype=np.float32)
+            do = rng.standard_normal((1, 4, Ls, c.head_dim), dtype=np.float32)
+            self._cpu = (q, k, v, do)
+        q, k, v, do = self._cpu
+        O.attention_fwd(q, k, v, causal=True, prec=prec)
+        O.attention_bwd(q, k, v, do, causal=True, prec=prec)
+        # token-equivalents by FLOP share of one full step
+        f_sample = 4.0 * 4 * Ls * Ls * c.head_dim / 2 * 3.5
+        f_step = (c.flops_fwd() + c.flops_bwd())
+        return c.tokens * f_sample / f_step
+
+    cpu_what = ("oracle f32 port (fused_scan.ex:3476-3508, 3527-3574) on one kv group "
+                "(4 q heads) at L=1024, scaled to the step by FLOP share")
+
+
+WORKLOADS = {"linear": lambda: ScanWorkload(False), "mingru": lambda: ScanWorkload(True),
+             "ssm": SsmWorkload, "attn": AttnWorkload}
+
+
+def roofline(wl, kern_ms):
+    peaks = measured_peaks()
+    work = wl.kernels()
+    dom = max(kern_ms, key=kern_ms.get)
+    bound, amount = work[dom]
+    peak, src = peaks[bound]
+    if bound == "hbm":
+        achieved, unit = amount / (kern_ms[dom] / 1e3) / 1e9, "GB/s"
+    else:
+        achieved, unit = amount / (kern_ms[dom] / 1e3) / 1e12, "TFLOP/s"
+    kname = "%s_%s" % (wl.kname, dom)
+    roof = {"bound": bound, "kernel": kname, "achieved": round(achieved, 2), "peak": peak,
+            "unit": unit, "frac": round(achieved / peak, 4), "peak_source": src,
+            ("algorithmic_bytes_per_launch" if bound == "hbm" else "algorithmic_flops_per_launch"):
+                amount,
+            "traffic": ncu_traffic(kname)}
+    per = {}
+    for k, ms in kern_ms.items():
+        b_, a_ = work[k]
+        rate = a_ / (ms / 1e3) / (1e9 if b_ == "hbm" else 1e12)
+        per[k] = {"ms": round(ms, 4), ("GB/s" if b_ == "hbm" else "TFLOP/s"): round(rate, 2),
+                  "frac_of_peak": round(rate / peaks[b_][0], 4)}
+    return roof, per
+
+
+def time_steps(wl, K, W, world, dist, torch):
+    for _ in range(max(3, W)):
+        wl.step()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.time()
+    start.record()
+    for i in range(K):
+        wl.step(evs[i])
+    end.record()
+    torch.cuda.synchronize()
+    t1 = time.time()
+    if world > 1:
+        dist.barrier()
+    el = start.elapsed_time(end)
+    fwd = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    bwd = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    if world > 1:
+        t = torch.tensor([el, fwd, bwd], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        el, fwd, bwd = t.tolist()
+    return el, {"fwd": fwd, "bwd": bwd}, t0, t1
+
+
+def time_cpu(wl, budget_s=12.0):
     import oracle as O
     n = cpu_threads()
     O.set_threads(n)
-    rows = cfg.batch
-    a, b, dy = cpu_sample(cfg, rows)
-    cpu_scan_step(cfg, a, b, dy)  # warm
+    wl.cpu_step()  # warm
     t0 = time.perf_counter()
-    reps = 0
+    reps, tok = 0, 0.0
     while True:
-        cpu_scan_step(cfg, a, b, dy)
+        tok += wl.cpu_step()
         reps += 1
         el = time.perf_counter() - t0
         if el >= budget_s or reps >= 200:
             break
-    tok_s = reps * rows * cfg.seq_len / el
-    return {"value": tok_s, "unit": "tokens/s", "cores": n, "kind": "port",
-            "sample": "%d x fwd+bwd of the full %d-row config (%s), %.1f s of CPU work, "
-                      "oracle f32 port of the Nx fallbacks (fused_scan.ex:4429-4444, 884-916)"
-                      % (reps, rows, cfg.name, el)}
+    return {"value": tok / el, "unit": "tokens/s", "cores": n, "kind": "port",
+            "sample": "%d repetitions, %.1f s of CPU work: %s" % (reps, el, wl.cpu_what)}
 
 
 # ------------------------------------------------------------------ ours
-def run_ours(args, cfg):
+def run_ours(args):
     import torch
     import torch.distributed as dist
-    from edifice_b200 import fused_scan as fs
-    from edifice_b200 import shard, device_errors
+    from edifice_b200 import device_errors
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
-    units = shard.plan_units(cfg.units, rank, world)
-    a, b, dy = shard.scan_inputs(cfg, units, dev)
-    fwd = fs.mingru_scan if cfg.mingru else fs.linear_scan
-    bwd_fn = (lambda a_, h_, dy_: fs.mingru_backward(a_, b, None, h_, dy_)) if cfg.mingru else \
-        (lambda a_, h_, dy_: fs.linear_scan_backward(a_, None, h_, dy_))
-
-    def step(ev=None):
-        if ev is not None:
-            ev[0].record()
-        h = fwd(a, b)
-        if ev is not None:
-            ev[1].record()
-        g = bwd_fn(a, h, dy)
-        if ev is not None:
-            ev[2].record()
-        return h, g
-
-    for _ in range(max(3, args.warmup)):
-        step()
-    torch.cuda.synchronize()
-    K = args.steps
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-
+    wl = WORKLOADS[args.config]()
+    wl._world = world
+    wl.setup(dev, rank)
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    t_wall0 = time.time()
-    start.record()
-    for i in range(K):
-        step(evs[i])
-    end.record()
-    torch.cuda.synchronize()
-    t_wall1 = time.time()
-    if world > 1:
-        dist.barrier()
+    K = args.steps
+    elapsed, kern_ms, t0, t1 = time_steps(wl, K, args.warmup, world, dist, torch)
     sampler.stop()
-    elapsed = start.elapsed_time(end)  # ms
-    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
-    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
-    if world > 1:
-        t = torch.tensor([elapsed, fwd_ms, bwd_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed, fwd_ms, bwd_ms = t.tolist()
     errs = device_errors()
 
     # ---- e2e through the public API with host buffers
     e2e = None
     if args.e2e_steps > 0:
-        pin = [x.cpu().pin_memory() for x in (a, b, dy)]
-        dev_in = [torch.empty_like(x) for x in (a, b, dy)]
-        outs_host = None
+        pin = [x.cpu().pin_memory() for x in wl.host_inputs()]
+        dev_in = [torch.empty_like(x) for x in wl.host_inputs()]
+        outs_host = []
 
         def e2e_step():
-            nonlocal outs_host
             for d_, h_ in zip(dev_in, pin):
                 d_.copy_(h_, non_blocking=True)
-            h = fwd(dev_in[0], dev_in[1])
-            if cfg.mingru:
-                g = fs.mingru_backward(dev_in[0], dev_in[1], None, h, dev_in[2])
-            else:
-                g = fs.linear_scan_backward(dev_in[0], None, h, dev_in[2])
-            res = (h,) + tuple(g)
-            if outs_host is None:
-                outs_host = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
+            res = wl.e2e_step(dev_in)
+            if not outs_host:
+                outs_host.extend(torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res)
             for o_, r_ in zip(outs_host, res):
                 o_.copy_(r_, non_blocking=True)
-            return res
 
         e2e_step()
         e2e_step()
@@ -279,13 +515,34 @@ def run_ours(args, cfg):
             t = torch.tensor([el2], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             el2 = t.item()
-        h2d = sum(x.numel() * x.element_size() for x in pin)
-        d2h = sum(x.numel() * x.element_size() for x in outs_host)
-        e2e = {"value": world * cfg.tokens * args.e2e_steps / (el2 / 1000.0), "unit": "tokens/s",
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "ms_per_step": el2 / args.e2e_steps, "steps": args.e2e_steps,
-               "api": "edifice_b200.fused_scan (%s + backward)" %
-                      ("mingru_scan" if cfg.mingru else "linear_scan")}
+        e2e = {"value": world * wl.tokens * args.e2e_steps / (el2 / 1000.0), "unit": "tokens/s",
+               "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in pin),
+               "d2h_bytes_per_step": sum(x.numel() * x.element_size() for x in outs_host),
+               "ms_per_step": el2 / args.e2e_steps, "steps": args.e2e_steps, "api": wl.api}
+        del pin, dev_in, outs_host
+
+    # ---- other paths (same process, smaller step count)
+    paths = {}
+    if args.config == "linear" and not args.no_paths:
+        del wl.a, wl.b, wl.dy
+        torch.cuda.empty_cache()
+        for name in ("mingru", "attn", "ssm"):
+            pw = WORKLOADS[name]()
+            pw._world = world
+            pw.setup(dev, rank)
+            kp = max(2, min(K, 20))
+            el_p, km, _, _ = time_steps(pw, kp, 3, world, dist, torch)
+            roof_p, per_p = roofline(pw, km)
+            entry = {"value": world * pw.tokens * kp / (el_p / 1000.0), "unit": "tokens/s",
+                     "ms_per_step": el_p / kp, "steps": kp, "config": pw.describe(world),
+                     "roofline": roof_p, "kernels": per_p,
+                     "gpu_launches": pw.launches_per_step * kp}
+            if hasattr(pw, "extra"):
+                entry.update(pw.extra(km["fwd"], km["bwd"]))
+            paths[pw.cfg.name] = entry
+            del pw
+            torch.cuda.empty_cache()
+        errs |= device_errors()
 
     if world > 1:
         dist.barrier()
@@ -293,90 +550,66 @@ def run_ours(args, cfg):
     if rank != 0:
         return
 
-    peak, peak_src = measured_peaks()
-    kern_bytes = {"fwd": cfg.bytes_fwd(), "bwd": cfg.bytes_bwd()}
-    kern_ms = {"fwd": fwd_ms, "bwd": bwd_ms}
-    dom = max(kern_ms, key=kern_ms.get)
-    achieved = kern_bytes[dom] / (kern_ms[dom] / 1000.0) / 1e9
-    kname = "%s_%s" % ("mingru" if cfg.mingru else "linear_scan", dom)
-    traffic = ncu_traffic(kname)
-    roof = {"bound": "hbm", "kernel": kname, "achieved": round(achieved, 1),
-            "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-            "peak_source": peak_src,
-            "algorithmic_bytes_per_launch": kern_bytes[dom],
-            "traffic": traffic}
-    per_kernel = {k: {"ms": round(kern_ms[k], 4),
-                      "GB/s": round(kern_bytes[k] / (kern_ms[k] / 1000.0) / 1e9, 1),
-                      "frac_of_peak": round(kern_bytes[k] / (kern_ms[k] / 1000.0) / 1e9 / peak, 4)}
-                  for k in kern_ms}
+    roof, per_kernel = roofline(wl, kern_ms)
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        cpu = time_cpu_baseline(cfg)
-    ms_step = elapsed / K
-    value = world * cfg.tokens * K / (elapsed / 1000.0)
+        cpu = time_cpu(wl)
     line = {
         "metric": "scan/delta/attn fwd+bwd tokens/s",
-        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
-        "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "%s fwd+bwd (BASELINE configs[1]%s)" %
-                               (cfg.name, ", MinGRU form" if cfg.mingru else ""),
-                   "batch_per_gpu": cfg.batch, "global_batch": cfg.batch * world,
-                   "seq_len": cfg.seq_len, "hidden": cfg.hidden,
-                   "parallelism": "dp%d (batch-row shards, no collective)" % world,
-                   "l2": "inputs larger than L2 (%.2f GB touched per step > 126 MB)"
-                         % ((kern_bytes["fwd"] + kern_bytes["bwd"]) / 1e9)},
+        "value": world * wl.tokens * K / (elapsed / 1000.0), "unit": "tokens/s",
+        "n_gpus": world, "steps": K, "warmup": max(3, args.warmup),
+        "ms_per_step": elapsed / K, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
+        "config": wl.describe(world),
         "roofline": roof, "kernels": per_kernel, "cpu_baseline": cpu, "e2e": e2e,
-        "gpu_launches": 2 * K,
-        "clocks": sampler.summary(t_wall0, t_wall1),
+        "gpu_launches": wl.launches_per_step * K,
+        "clocks": sampler.summary(t0, t1),
         "device_errors": errs,
     }
+    if hasattr(wl, "extra"):
+        line.update(wl.extra(kern_ms["fwd"], kern_ms["bwd"]))
+    if paths:
+        line["paths"] = paths
     print(json.dumps(line), flush=True)
 
 
 # --------------------------------------------------------------- reference
-def run_reference(args, cfg):
+def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
     import oracle as O
+    wl = WORKLOADS[args.config]()
+    wl._world = 1
     n = cpu_threads()
     O.set_threads(n)
-    # size the per-step sample so W+K steps fit in ~150 s
-    rows = cfg.batch
-    a, b, dy = cpu_sample(cfg, rows)
     t0 = time.perf_counter()
-    cpu_scan_step(cfg, a, b, dy)
+    wl.cpu_step()
     one = time.perf_counter() - t0
-    total = (args.steps + args.warmup) * one
-    if total > 150.0:
-        frac = 150.0 / total
-        hs = max(64, int(cfg.hidden * frac) // 64 * 64)
-        a, b, dy = a[:1, :, :hs].copy(), b[:1, :, :hs].copy(), dy[:1, :, :hs].copy()
-        rows, sample = 1, "1 batch row x %d of %d channels" % (hs, cfg.hidden)
-        tok_per_step = cfg.seq_len * hs / cfg.hidden
-    else:
-        sample = "the full %d-row config" % rows
-        tok_per_step = rows * cfg.seq_len
+    rows = None
+    if isinstance(wl, ScanWorkload) and (args.steps + args.warmup) * one > 150.0:
+        rows = 1  # keep the whole run within a few minutes
     for _ in range(args.warmup):
-        cpu_scan_step(cfg, a, b, dy)
+        wl.cpu_step(rows)
     t0 = time.perf_counter()
+    tok = 0.0
     for _ in range(args.steps):
-        cpu_scan_step(cfg, a, b, dy)
+        tok += wl.cpu_step(rows)
     el = time.perf_counter() - t0
-    value = tok_per_step * args.steps / el
+    value = tok / el
+    sample = ("1 batch row per step" if rows == 1 else "the full config per step") \
+        if isinstance(wl, ScanWorkload) else wl.cpu_what
     line = {
         "impl": "reference",
         "metric": "scan/delta/attn fwd+bwd tokens/s", "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": el * 1000.0 / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "%s fwd+bwd (BASELINE configs[1])" % cfg.name,
-                   "batch_per_gpu": cfg.batch, "seq_len": cfg.seq_len, "hidden": cfg.hidden},
+        "config": wl.describe(1),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": n, "kind": "port",
-                         "sample": sample + "; tokens scaled by the sampled fraction; oracle "
-                                   "f32 restatement of the Nx fallbacks (the reference's Nx/EXLA "
-                                   "host path itself needs Erlang/Elixir, absent here)"},
+                         "sample": sample + "; oracle f32 restatement of the Nx fallbacks (the "
+                                   "reference's Nx/EXLA host path needs Erlang/Elixir, absent "
+                                   "here)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -385,12 +618,10 @@ def run_reference(args, cfg):
 
 def main():
     args = parse()
-    from edifice_b200.shard import ScanConfig
-    cfg = ScanConfig(name="mingru_cfg1", mingru=True) if args.config == "mingru" else ScanConfig()
     if args.impl == "reference":
-        run_reference(args, cfg)
+        run_reference(args)
     else:
-        run_ours(args, cfg)
+        run_ours(args)
 
 
 if __name__ == "__main__":

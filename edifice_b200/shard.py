@@ -45,6 +45,66 @@ class ScanConfig:
         return (n_in + 2) * e * es + self.batch * self.hidden * es
 
 
+@dataclasses.dataclass(frozen=True)
+class SsmConfig:
+    """Mamba selective scan fwd+bwd, bf16 io, f32 state."""
+    name: str = "selective_scan_cfg4"
+    batch: int = 64
+    seq_len: int = 8192
+    d_inner: int = 4096
+    d_state: int = 16
+    dtype: torch.dtype = torch.bfloat16
+
+    @property
+    def units(self):
+        return self.batch
+
+    @property
+    def tokens(self):
+        return self.batch * self.seq_len
+
+    def bytes_fwd(self):
+        e = self.batch * self.seq_len * self.d_inner
+        bc = self.batch * self.seq_len * self.d_state
+        return 3 * e * 2 + 2 * bc * 2 + self.d_inner * self.d_state * 2
+
+    def bytes_bwd(self):
+        e = self.batch * self.seq_len * self.d_inner
+        bc = self.batch * self.seq_len * self.d_state
+        return 5 * e * 2 + 2 * bc * 2 + 2 * bc * 4 + self.d_inner * self.d_state * 2
+
+    def exps_fwd(self):
+        return self.batch * self.seq_len * self.d_inner * self.d_state
+
+
+@dataclasses.dataclass(frozen=True)
+class AttnConfig:
+    """causal GQA attention fwd+bwd, bf16."""
+    name: str = "flash_attention_cfg3"
+    batch: int = 4
+    q_heads: int = 32
+    kv_heads: int = 8
+    seq_len: int = 8192
+    head_dim: int = 128
+    causal: bool = True
+    dtype: torch.dtype = torch.bfloat16
+
+    @property
+    def units(self):
+        return self.batch * self.kv_heads  # (batch, kv-group) pairs
+
+    @property
+    def tokens(self):
+        return self.batch * self.seq_len
+
+    def flops_fwd(self):
+        f = 4.0 * self.batch * self.q_heads * self.seq_len ** 2 * self.head_dim
+        return f / 2 if self.causal else f
+
+    def flops_bwd(self):
+        return 2.5 * self.flops_fwd()
+
+
 def unit_seed(base_seed, unit):
     return (int(base_seed) * 1_000_003 + int(unit)) & 0x7FFFFFFFFFFF
 
@@ -82,6 +142,49 @@ def scan_inputs(cfg, units, device, base_seed=0):
         b[i].copy_(torch.randn((L, H), generator=g, device=device))
         dy[i].copy_(torch.randn((L, H), generator=g, device=device))
     return a, b, dy
+
+
+def ssm_inputs(cfg, units, device, base_seed=0):
+    """configs[0]/[4] distributions per batch-row unit: x ~ N(0,1);
+    dt = softplus(0.5 N(0,1) - 2); B, C, dY ~ N(0,1); A = -exp(U(log 1, log 16))
+    shared by all units (its own seed).  Returns x, dt, A, B, C, dy."""
+    L, D, N = cfg.seq_len, cfg.d_inner, cfg.d_state
+    U = len(units)
+    x = torch.empty((U, L, D), dtype=cfg.dtype, device=device)
+    dt, dy = torch.empty_like(x), torch.empty_like(x)
+    Bm = torch.empty((U, L, N), dtype=cfg.dtype, device=device)
+    Cm = torch.empty_like(Bm)
+    for i, u in enumerate(units):
+        g = torch.Generator(device=device).manual_seed(unit_seed(base_seed, u))
+        x[i].copy_(torch.randn((L, D), generator=g, device=device))
+        dt[i].copy_(torch.nn.functional.softplus(
+            torch.randn((L, D), generator=g, device=device) * 0.5 - 2))
+        Bm[i].copy_(torch.randn((L, N), generator=g, device=device))
+        Cm[i].copy_(torch.randn((L, N), generator=g, device=device))
+        dy[i].copy_(torch.randn((L, D), generator=g, device=device))
+    g = torch.Generator(device=device).manual_seed(unit_seed(base_seed, 1 << 40))
+    A = (-torch.exp(torch.rand((D, N), generator=g, device=device) * math.log(16.0))).to(cfg.dtype)
+    return x, dt, A, Bm, Cm, dy
+
+
+def attn_inputs(cfg, units, device, base_seed=0):
+    """configs[3] per (batch, kv-group) unit: q, k, v, dO ~ N(0,1).  The rank's
+    units are laid out as a [len(units)/kv_heads, heads, L, d] batch."""
+    G = cfg.q_heads // cfg.kv_heads
+    L, d = cfg.seq_len, cfg.head_dim
+    nb = len(units) // cfg.kv_heads
+    q = torch.empty((nb, cfg.q_heads, L, d), dtype=cfg.dtype, device=device)
+    do = torch.empty_like(q)
+    k = torch.empty((nb, cfg.kv_heads, L, d), dtype=cfg.dtype, device=device)
+    v = torch.empty_like(k)
+    for i, u in enumerate(units):
+        b, hk = divmod(i, cfg.kv_heads)
+        g = torch.Generator(device=device).manual_seed(unit_seed(base_seed, u))
+        q[b, hk * G:(hk + 1) * G].copy_(torch.randn((G, L, d), generator=g, device=device))
+        k[b, hk].copy_(torch.randn((L, d), generator=g, device=device))
+        v[b, hk].copy_(torch.randn((L, d), generator=g, device=device))
+        do[b, hk * G:(hk + 1) * G].copy_(torch.randn((G, L, d), generator=g, device=device))
+    return q, k, v, do
 
 
 def ceil_div(a, b):
