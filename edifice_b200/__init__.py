@@ -11,6 +11,7 @@ from .fused_scan import (  # noqa: F401
     linear_scan, linear_scan_backward, mingru, mingru_scan, mingru_backward,
     LinearScanFn, MinGRUFn, selective_scan, selective_scan_backward, SelectiveScanFn,
     flash_attention, flash_attention_backward, FlashAttentionFn,
+    delta_net_scan, delta_rule_backward, DeltaNetFn,
 )
 
 __version__ = "0.1.0"

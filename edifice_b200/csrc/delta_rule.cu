@@ -1,0 +1,310 @@
+// delta_rule.cu -- DeltaNet delta rule, forward + backward (recurrent path).
+//
+// Reference semantics (edifice project paths):
+//   forward   lib/edifice/cuda/fused_scan.ex:2212-2236 (delta_net_scan_fallback)
+//             == lib/edifice/recurrent/delta_net.ex:231-273:
+//             r = S_{t-1} k_t;  S_t = S_{t-1} + (beta_t (.) (v_t - r)) k_t^T;  o_t = S_t q_t
+//   backward  fused_scan.ex:1257-1326 (delta_rule_backward_fallback), with the
+//             through-retrieval key gradient taken as S_{t-1}^T (beta (.) dS k) --
+//             the exact gradient, as in native/cuda/fused_delta_rule_scan_backward.cu
+//             and torch autograd of test/fixtures/numerical/delta_net_random; the Nx
+//             fallback scales S_{t-1}^T dS k by beta over the key index instead,
+//             which only agrees when beta is the same for every row.
+// q, k, v, o: [B, L, H, d]; beta: [B, L, H, d] (per element, the model's form,
+// delta_net.ex:285-297) or [B, L, H] (one gate per token and head).
+//
+// This file is the general path (any d <= 128, either beta form, f32 or bf16
+// io): one CTA per (b, h) holding S (and dS) in shared memory as f32, token
+// order.  The forward can write S at the start of every CK-token chunk (plus
+// the final state); the backward walks chunks in reverse, recomputes each
+// chunk's retrievals r_t from its checkpoint, and undoes the updates
+// (S_{t-1} = S_t - u_t k_t^T with the stored r_t) instead of storing every state.
+#include <math.h>
+
+#include "edb_common.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int CK = 64;  // tokens per checkpoint chunk
+
+template <typename T>
+static __device__ __forceinline__ float ldv(const T* p) {
+    return ld_scalar<T>(p);
+}
+
+// shared layout: S [d][d+1] | q k v beta o-scratch [5][DMAX] (| dS [d][d+1] | r [CK][d] | vec [4][DMAX])
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+    delta_fwd_rec_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                         const T* __restrict__ beta, T* __restrict__ o, float* __restrict__ ckpt,
+                         int L, int H, int d, int beta_scalar) {
+    extern __shared__ float sm[];
+    const int sd = d + 1;
+    float* S = sm;
+    float* sq = S + d * sd;
+    float* sk = sq + d;
+    float* su = sk + d;  // beta (.) (v - r)
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int tid = threadIdx.x;
+    const int nck = (L + CK - 1) / CK;
+    for (int i = tid; i < d * sd; i += kThreads) S[i] = 0.0f;
+    __syncthreads();
+    const long long rs = (long long)H * d;  // token stride
+    const long long base = (long long)b * L * rs + (long long)h * d;
+    for (int t = 0; t < L; ++t) {
+        const long long off = base + (long long)t * rs;
+        if (ckpt != nullptr && t % CK == 0) {
+            float* cp = ckpt + (((long long)b * H + h) * (nck + 1) + t / CK) * d * d;
+            for (int i = tid; i < d * d; i += kThreads) cp[i] = S[(i / d) * sd + i % d];
+        }
+        for (int i = tid; i < d; i += kThreads) {
+            sq[i] = ldv(q + off + i);
+            sk[i] = ldv(k + off + i);
+        }
+        __syncthreads();
+        for (int i = tid; i < d; i += kThreads) {
+            float r = 0.0f;
+            for (int j = 0; j < d; ++j) r = fmaf(S[i * sd + j], sk[j], r);
+            const float be = beta_scalar ? ldv(beta + ((long long)b * L + t) * H + h)
+                                         : ldv(beta + off + i);
+            su[i] = be * (ldv(v + off + i) - r);
+        }
+        __syncthreads();
+        for (int i = tid; i < d; i += kThreads) {
+            const float u = su[i];
+            float acc = 0.0f;
+            for (int j = 0; j < d; ++j) {
+                const float s = fmaf(u, sk[j], S[i * sd + j]);
+                S[i * sd + j] = s;
+                acc = fmaf(s, sq[j], acc);
+            }
+            st_scalar<T>(o + off + i, acc);
+        }
+        __syncthreads();
+    }
+    if (ckpt != nullptr) {
+        float* cp = ckpt + (((long long)b * H + h) * (nck + 1) + nck) * d * d;
+        for (int i = tid; i < d * d; i += kThreads) cp[i] = S[(i / d) * sd + i % d];
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+    delta_bwd_rec_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                         const T* __restrict__ beta, const T* __restrict__ dO,
+                         const float* __restrict__ ckpt, T* __restrict__ gq, T* __restrict__ gk,
+                         T* __restrict__ gv, T* __restrict__ gbeta, int L, int H, int d,
+                         int beta_scalar) {
+    extern __shared__ float sm[];
+    const int sd = d + 1;
+    float* S = sm;                 // [d][sd]
+    float* dS = S + d * sd;        // [d][sd]
+    float* rbuf = dS + d * sd;     // [CK][d] retrievals of the current chunk
+    float* sq = rbuf + CK * d;
+    float* sk = sq + d;
+    float* sdo = sk + d;
+    float* su = sdo + d;           // beta (.) err
+    float* sbd = su + d;           // beta (.) dS k
+    float* red = sbd + d;          // [kThreads] scratch for the scalar-beta sum
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int tid = threadIdx.x;
+    const int nck = (L + CK - 1) / CK;
+    const long long rs = (long long)H * d;
+    const long long base = (long long)b * L * rs + (long long)h * d;
+    for (int i = tid; i < d * sd; i += kThreads) dS[i] = 0.0f;
+
+    for (int c = nck - 1; c >= 0; --c) {
+        const int t0 = c * CK, t1 = min(L, t0 + CK);
+        const float* cp = ckpt + (((long long)b * H + h) * (nck + 1) + c) * d * d;
+        __syncthreads();
+        for (int i = tid; i < d * d; i += kThreads) S[(i / d) * sd + i % d] = cp[i];
+        __syncthreads();
+        // ---- forward over the chunk: retrievals r_t, S ends as S_{t1-1}
+        for (int t = t0; t < t1; ++t) {
+            const long long off = base + (long long)t * rs;
+            for (int i = tid; i < d; i += kThreads) sk[i] = ldv(k + off + i);
+            __syncthreads();
+            for (int i = tid; i < d; i += kThreads) {
+                float r = 0.0f;
+                for (int j = 0; j < d; ++j) r = fmaf(S[i * sd + j], sk[j], r);
+                rbuf[(t - t0) * d + i] = r;
+                const float be = beta_scalar ? ldv(beta + ((long long)b * L + t) * H + h)
+                                             : ldv(beta + off + i);
+                const float u = be * (ldv(v + off + i) - r);
+                for (int j = 0; j < d; ++j) S[i * sd + j] = fmaf(u, sk[j], S[i * sd + j]);
+            }
+            __syncthreads();
+        }
+        // ---- reverse over the chunk
+        for (int t = t1 - 1; t >= t0; --t) {
+            const long long off = base + (long long)t * rs;
+            const long long boff = ((long long)b * L + t) * H + h;
+            for (int i = tid; i < d; i += kThreads) {
+                sq[i] = ldv(q + off + i);
+                sk[i] = ldv(k + off + i);
+                sdo[i] = ldv(dO + off + i);
+            }
+            __syncthreads();
+            // rows: dS += dO q^T ; u = beta (v - r)
+            for (int i = tid; i < d; i += kThreads) {
+                const float doi = sdo[i];
+                for (int j = 0; j < d; ++j) dS[i * sd + j] = fmaf(doi, sq[j], dS[i * sd + j]);
+                const float be = beta_scalar ? ldv(beta + boff) : ldv(beta + off + i);
+                su[i] = be * (ldv(v + off + i) - rbuf[(t - t0) * d + i]);
+            }
+            __syncthreads();
+            // columns: dq = S_t^T dO
+            for (int j = tid; j < d; j += kThreads) {
+                float acc = 0.0f;
+                for (int i = 0; i < d; ++i) acc = fmaf(S[i * sd + j], sdo[i], acc);
+                st_scalar<T>(gq + off + j, acc);
+            }
+            // rows: dsk = dS k; dv = beta dsk; dbeta = err dsk
+            float bsum = 0.0f;
+            for (int i = tid; i < d; i += kThreads) {
+                float dsk = 0.0f;
+                for (int j = 0; j < d; ++j) dsk = fmaf(dS[i * sd + j], sk[j], dsk);
+                const float be = beta_scalar ? ldv(beta + boff) : ldv(beta + off + i);
+                const float err = ldv(v + off + i) - rbuf[(t - t0) * d + i];
+                st_scalar<T>(gv + off + i, be * dsk);
+                if (beta_scalar) bsum = fmaf(err, dsk, bsum);
+                else st_scalar<T>(gbeta + off + i, err * dsk);
+                sbd[i] = be * dsk;
+            }
+            if (beta_scalar) {
+                red[tid] = bsum;
+            }
+            __syncthreads();
+            if (beta_scalar && tid < 32) {
+                float s = 0.0f;
+                for (int i = tid; i < kThreads; i += 32) s += red[i];
+                for (int off2 = 16; off2 >= 1; off2 >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off2);
+                if (tid == 0) st_scalar<T>(gbeta + boff, s);
+            }
+            // rows: S_{t-1} = S_t - u k^T  (undo the update)
+            for (int i = tid; i < d; i += kThreads) {
+                const float u = su[i];
+                for (int j = 0; j < d; ++j) S[i * sd + j] = fmaf(-u, sk[j], S[i * sd + j]);
+            }
+            __syncthreads();
+            // columns: dk = dS^T u - S_{t-1}^T (beta dsk)
+            for (int j = tid; j < d; j += kThreads) {
+                float acc = 0.0f;
+                for (int i = 0; i < d; ++i)
+                    acc += dS[i * sd + j] * su[i] - S[i * sd + j] * sbd[i];
+                st_scalar<T>(gk + off + j, acc);
+            }
+            __syncthreads();
+            // rows: dS_{t-1} = dS - (beta dsk) k^T
+            for (int i = tid; i < d; i += kThreads) {
+                const float bd = sbd[i];
+                for (int j = 0; j < d; ++j) dS[i * sd + j] = fmaf(-bd, sk[j], dS[i * sd + j]);
+            }
+            __syncthreads();
+        }
+    }
+}
+
+size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+size_t ckpt_bytes(int B, int L, int H, int d) {
+    const int nck = (L + CK - 1) / CK;
+    return (size_t)B * H * (nck + 1) * d * d * sizeof(float);
+}
+
+size_t fwd_smem(int d) { return ((size_t)d * (d + 1) + 3 * d) * sizeof(float); }
+size_t bwd_smem(int d) {
+    return ((size_t)2 * d * (d + 1) + (size_t)CK * d + 5 * d + kThreads) * sizeof(float);
+}
+
+template <typename T>
+int launch_fwd(const void* q, const void* k, const void* v, const void* beta, void* o,
+               float* ckpt, int B, int L, int H, int d, int beta_scalar, cudaStream_t st) {
+    const size_t smem = fwd_smem(d);
+    cudaError_t e = cudaFuncSetAttribute(delta_fwd_rec_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    delta_fwd_rec_kernel<T><<<dim3(H, B), kThreads, smem, st>>>(
+        (const T*)q, (const T*)k, (const T*)v, (const T*)beta, (T*)o, ckpt, L, H, d, beta_scalar);
+    return edb::status_from_cuda(cudaGetLastError());
+}
+
+template <typename T>
+int launch_bwd(const void* q, const void* k, const void* v, const void* beta, const void* dO,
+               const float* ckpt, void* gq, void* gk, void* gv, void* gbeta, int B, int L, int H,
+               int d, int beta_scalar, cudaStream_t st) {
+    const size_t smem = bwd_smem(d);
+    cudaError_t e = cudaFuncSetAttribute(delta_bwd_rec_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    delta_bwd_rec_kernel<T><<<dim3(H, B), kThreads, smem, st>>>(
+        (const T*)q, (const T*)k, (const T*)v, (const T*)beta, (const T*)dO, ckpt, (T*)gq, (T*)gk,
+        (T*)gv, (T*)gbeta, L, H, d, beta_scalar);
+    return edb::status_from_cuda(cudaGetLastError());
+}
+
+int check(int dtype, int B, int L, int H, int d) {
+    if (dtype != EDB_F32 && dtype != EDB_BF16) return EDB_ERR_BAD_DTYPE;
+    if (B <= 0 || L <= 0 || H <= 0 || d <= 0) return EDB_ERR_BAD_SHAPE;
+    if (d > 128) return EDB_ERR_UNSUPPORTED;
+    return EDB_OK;
+}
+
+}  // namespace
+
+extern "C" size_t edb_delta_rule_ckpt_bytes(int batch, int seq_len, int heads, int head_dim) {
+    if (batch <= 0 || seq_len <= 0 || heads <= 0 || head_dim <= 0) return 0;
+    return ckpt_bytes(batch, seq_len, heads, head_dim);
+}
+
+extern "C" int edb_delta_rule_fwd(int dtype, const void* q, const void* k, const void* v,
+                                  const void* beta, int beta_per_element, void* o, float* s_ckpt,
+                                  int batch, int seq_len, int heads, int head_dim, void* stream) {
+    if (int s = check(dtype, batch, seq_len, heads, head_dim)) return s;
+    if (!q || !k || !v || !beta || !o) return EDB_ERR_NULL_POINTER;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int bs = beta_per_element ? 0 : 1;
+    return dtype == EDB_BF16
+               ? launch_fwd<__nv_bfloat16>(q, k, v, beta, o, s_ckpt, batch, seq_len, heads,
+                                           head_dim, bs, st)
+               : launch_fwd<float>(q, k, v, beta, o, s_ckpt, batch, seq_len, heads, head_dim, bs,
+                                   st);
+}
+
+extern "C" size_t edb_delta_rule_bwd_workspace(int batch, int seq_len, int heads, int head_dim,
+                                               int have_ckpt) {
+    if (batch <= 0 || seq_len <= 0 || heads <= 0 || head_dim <= 0) return 0;
+    return have_ckpt ? 0 : a256(ckpt_bytes(batch, seq_len, heads, head_dim));
+}
+
+extern "C" int edb_delta_rule_bwd(int dtype, const void* q, const void* k, const void* v,
+                                  const void* beta, int beta_per_element, const void* dO,
+                                  const float* s_ckpt, void* gq, void* gk, void* gv, void* gbeta,
+                                  int batch, int seq_len, int heads, int head_dim,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+    if (int s = check(dtype, batch, seq_len, heads, head_dim)) return s;
+    if (!q || !k || !v || !beta || !dO || !gq || !gk || !gv || !gbeta) return EDB_ERR_NULL_POINTER;
+    const size_t need =
+        edb_delta_rule_bwd_workspace(batch, seq_len, heads, head_dim, s_ckpt != nullptr);
+    if (workspace_bytes < need || (need && !workspace)) return EDB_ERR_WORKSPACE_TOO_SMALL;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int bs = beta_per_element ? 0 : 1;
+    const float* ck = s_ckpt;
+    if (!ck) {
+        float* w = static_cast<float*>(workspace);
+        // states only: the forward writes o into gq, which the backward overwrites
+        int s = dtype == EDB_BF16
+                    ? launch_fwd<__nv_bfloat16>(q, k, v, beta, gq, w, batch, seq_len, heads,
+                                                head_dim, bs, st)
+                    : launch_fwd<float>(q, k, v, beta, gq, w, batch, seq_len, heads, head_dim,
+                                        bs, st);
+        if (s) return s;
+        ck = w;
+    }
+    return dtype == EDB_BF16
+               ? launch_bwd<__nv_bfloat16>(q, k, v, beta, dO, ck, gq, gk, gv, gbeta, batch,
+                                           seq_len, heads, head_dim, bs, st)
+               : launch_bwd<float>(q, k, v, beta, dO, ck, gq, gk, gv, gbeta, batch, seq_len,
+                                   heads, head_dim, bs, st);
+}

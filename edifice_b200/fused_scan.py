@@ -191,6 +191,69 @@ def selective_scan_backward(x, dt, a, b, c, grad_output, h_ckpt=None):
     return gx, gdt, gB, gC
 
 
+def _delta_shapes(q, k, v, beta):
+    if q.dim() != 4 or q.shape != k.shape or q.shape != v.shape:
+        raise _lib.EdbError("delta_net_scan: q, k, v must share one [B, L, H, d] shape")
+    B, L, H, d = q.shape
+    if tuple(beta.shape) == (B, L, H, d):
+        return B, L, H, d, 1
+    if tuple(beta.shape) == (B, L, H):
+        return B, L, H, d, 0
+    raise _lib.EdbError("delta_net_scan: beta must be [B, L, H, d] or [B, L, H], got %s"
+                        % (tuple(beta.shape),))
+
+
+def delta_net_scan(q, k, v, beta, with_ckpt=False):
+    """FusedScan.delta_net_scan/4 (fused_scan.ex:195-209): q, k (L2-normalised),
+    v [B, L, H, d]; beta (post-sigmoid) [B, L, H, d] or [B, L, H] -> o [B, L, H, d].
+    with_ckpt=True also returns the f32 chunk-start states the backward can reuse."""
+    _dev(q, k, v, beta, what="delta_net_scan")
+    B, L, H, d, per_el = _delta_shapes(q, k, v, beta)
+    o = torch.empty_like(q)
+    lib = _lib.load()
+    ck = None
+    if with_ckpt:
+        ck = torch.empty(lib.edb_delta_rule_ckpt_bytes(B, L, H, d) // 4, dtype=torch.float32,
+                         device=q.device)
+    _lib.check(lib.edb_delta_rule_fwd(_dtype_code(q, "delta_net_scan"), _p(q), _p(k), _p(v),
+                                      _p(beta), per_el, _p(o), _p(ck), B, L, H, d, _stream()),
+               "CUDA fused DeltaNet scan")
+    return (o, ck) if with_ckpt else o
+
+
+def delta_rule_backward(q, k, v, beta, grad_output, s_ckpt=None):
+    """Returns (grad_q, grad_k, grad_v, grad_beta).  Mirrors
+    delta_rule_backward_dispatch/6 (fused_scan.ex:1241-1255)."""
+    _dev(q, k, v, beta, grad_output, s_ckpt, what="delta_rule_backward")
+    B, L, H, d, per_el = _delta_shapes(q, k, v, beta)
+    lib = _lib.load()
+    gq, gk, gv, gb = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
+                      torch.empty_like(beta))
+    wsb = lib.edb_delta_rule_bwd_workspace(B, L, H, d, int(s_ckpt is not None))
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=q.device)
+    _lib.check(lib.edb_delta_rule_bwd(_dtype_code(q, "delta_rule_backward"), _p(q), _p(k), _p(v),
+                                      _p(beta), per_el, _p(grad_output), _p(s_ckpt), _p(gq),
+                                      _p(gk), _p(gv), _p(gb), B, L, H, d, _p(ws), wsb, _stream()),
+               "CUDA fused DeltaNet scan backward")
+    return gq, gk, gv, gb
+
+
+class DeltaNetFn(torch.autograd.Function):
+    """custom_grad wiring of delta_net_custom_call/4 (fused_scan.ex:2195-2210):
+    gradients to q, k, v, beta."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, beta):
+        o, ck = delta_net_scan(q, k, v, beta, with_ckpt=True)
+        ctx.save_for_backward(q, k, v, beta, ck)
+        return o
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        q, k, v, beta, ck = ctx.saved_tensors
+        return delta_rule_backward(q, k, v, beta, grad_output.contiguous(), ck)
+
+
 def _attn_shapes(q, k, v):
     if q.dim() != 4 or k.dim() != 4 or k.shape != v.shape:
         raise _lib.EdbError("flash_attention: expected [B, H, L, d] q and equal k/v shapes")

@@ -83,6 +83,31 @@ int fused_selective_scan_backward_launch(cudaStream_t stream, const edb_io_t* x,
     return st;
 }
 
+int fused_delta_net_scan_launch(cudaStream_t stream, const edb_io_t* q, const edb_io_t* k,
+                                const edb_io_t* v, const edb_io_t* beta, edb_io_t* output,
+                                int batch, int seq_len, int num_heads, int head_dim) {
+    return edb_delta_rule_fwd(kDtype, q, k, v, beta, 1, output, nullptr, batch, seq_len,
+                              num_heads, head_dim, stream);
+}
+
+int fused_delta_rule_scan_backward_launch(cudaStream_t stream, const edb_io_t* q,
+                                          const edb_io_t* k, const edb_io_t* v,
+                                          const edb_io_t* beta, const edb_io_t* forward_out,
+                                          const edb_io_t* grad_output, edb_io_t* output_concat,
+                                          int batch, int seq_len, int num_heads, int head_dim) {
+    (void)forward_out;  // the backward recomputes what it needs from q, k, v, beta
+    const long long n = (long long)batch * seq_len * num_heads * head_dim;
+    const size_t wsb = edb_delta_rule_bwd_workspace(batch, seq_len, num_heads, head_dim, 0);
+    void* ws = nullptr;
+    cudaError_t e = cudaMallocAsync(&ws, wsb, stream);
+    if (e != cudaSuccess) return (int)e;
+    int st = edb_delta_rule_bwd(kDtype, q, k, v, beta, 1, grad_output, nullptr, output_concat,
+                                output_concat + n, output_concat + 2 * n, output_concat + 3 * n,
+                                batch, seq_len, num_heads, head_dim, ws, wsb, stream);
+    cudaFreeAsync(ws, stream);
+    return st;
+}
+
 int fused_flash_attention_launch(cudaStream_t stream, const edb_io_t* q, const edb_io_t* k,
                                  const edb_io_t* v, edb_io_t* output, int batch, int num_heads,
                                  int seq_len, int head_dim, int causal) {

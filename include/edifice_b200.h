@@ -170,6 +170,41 @@ int edb_flash_attention_bwd(int dtype, const void* q, const void* k, const void*
                             int causal, float scale, void* workspace, size_t workspace_bytes,
                             void* stream);
 
+/* ------------------------------------------------------------------------
+ * DeltaNet delta rule.  Per (batch, head), S_0 = 0:
+ *   r = S_{t-1} k_t;  S_t = S_{t-1} + (beta_t (.) (v_t - r)) k_t^T;  o_t = S_t q_t
+ * q, k, v, o: [batch, seq_len, heads, head_dim] (k L2-normalised by the
+ * caller); beta: [batch, seq_len, heads, head_dim] when beta_per_element
+ * (Edifice.build(:delta_net)'s form, lib/edifice/recurrent/delta_net.ex:285-297),
+ * else [batch, seq_len, heads] (one gate per token and head).  head_dim <= 128.
+ * s_ckpt (optional f32, edb_delta_rule_ckpt_bytes() bytes): the forward also
+ * writes S at the start of every 64-token chunk for the backward.
+ * Replaces fused_delta_net_scan_launch / fused_delta_rule_scan_launch with
+ * alpha = NULL (native/cuda/fused_delta_rule_scan.cu:213-258); Nx semantics
+ * lib/edifice/cuda/fused_scan.ex:2212-2236.
+ * ---------------------------------------------------------------------- */
+size_t edb_delta_rule_ckpt_bytes(int batch, int seq_len, int heads, int head_dim);
+
+int edb_delta_rule_fwd(int dtype, const void* q, const void* k, const void* v, const void* beta,
+                       int beta_per_element, void* o, float* s_ckpt, int batch, int seq_len,
+                       int heads, int head_dim, void* stream);
+
+/* Workspace bytes edb_delta_rule_bwd needs (0 when the forward's s_ckpt is passed). */
+size_t edb_delta_rule_bwd_workspace(int batch, int seq_len, int heads, int head_dim,
+                                    int have_ckpt);
+
+/* Backward given dO: gq, gk, gv (shape of q) and gbeta (shape of beta), in
+ * `dtype`.  The key gradient is the exact one (S_{t-1}^T (beta (.) dS k) for the
+ * path through the retrieval), as in native/cuda/fused_delta_rule_scan_backward.cu;
+ * lib/edifice/cuda/fused_scan.ex:1318-1319 scales that term by beta over the key
+ * index, which agrees only for a per-token beta.  Replaces
+ * fused_delta_rule_scan_backward_launch
+ * (native/cuda/fused_delta_rule_scan_backward.cu:277-318). */
+int edb_delta_rule_bwd(int dtype, const void* q, const void* k, const void* v, const void* beta,
+                       int beta_per_element, const void* dO, const float* s_ckpt, void* gq,
+                       void* gk, void* gv, void* gbeta, int batch, int seq_len, int heads,
+                       int head_dim, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Capacity of the library's built-in scratch array used by
  * edb_selective_scan_bwd_noalloc (16 MiB; every GPU that loads the library
  * holds it until the process exits). */

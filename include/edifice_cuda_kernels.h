@@ -67,6 +67,21 @@ int fused_selective_scan_backward_launch(cudaStream_t stream, const edb_io_t* x,
                                          const edb_io_t* grad_output, edb_io_t* output_concat,
                                          int batch, int seq_len, int hidden, int state_size);
 
+/* native/cuda/fused_delta_rule_scan.cu:234-245: q, k, v, beta, output
+ * [B, T, H, d] (beta per element). */
+int fused_delta_net_scan_launch(cudaStream_t stream, const edb_io_t* q, const edb_io_t* k,
+                                const edb_io_t* v, const edb_io_t* beta, edb_io_t* output,
+                                int batch, int seq_len, int num_heads, int head_dim);
+
+/* native/cuda/fused_delta_rule_scan_backward.cu:277-318;
+ * output_concat = [gq | gk | gv | gbeta], each B*T*H*d io elements.  The
+ * checkpoint workspace is taken stream-ordered (cudaMallocAsync / cudaFreeAsync). */
+int fused_delta_rule_scan_backward_launch(cudaStream_t stream, const edb_io_t* q,
+                                          const edb_io_t* k, const edb_io_t* v,
+                                          const edb_io_t* beta, const edb_io_t* forward_out,
+                                          const edb_io_t* grad_output, edb_io_t* output_concat,
+                                          int batch, int seq_len, int num_heads, int head_dim);
+
 /* native/cuda/fused_flash_attention.cu:168-191: q, k, v, output [B, H, T, d],
  * equal heads, scale 1/sqrt(d), causal 0/1. */
 int fused_flash_attention_launch(cudaStream_t stream, const edb_io_t* q, const edb_io_t* k,
