@@ -12,9 +12,9 @@ owns units [rU, (r+1)U) of a global problem of N shards (batch rows; (batch,
 kv-group) pairs for attention), inputs seeded per unit, no collective on the
 data path.
 
-The headline line also carries `paths`: the other implemented configs
-(MinGRU form of configs[1], configs[3] causal GQA attention, configs[4] Mamba
-selective scan), each timed the same way over min(K, 20) steps.
+The headline line also carries `paths`: the other configs (MinGRU form of
+configs[1], configs[2] DeltaNet, configs[3] causal GQA attention, configs[4]
+Mamba selective scan), each timed the same way over min(K, 20) steps.
 
 --impl ours       our kernels (libedifice_b200.so): device-timed with CUDA
                   events, max over ranks; e2e through the public API with host
@@ -45,11 +45,22 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["linear", "mingru", "ssm", "attn"], default="linear")
+    ap.add_argument("--config", choices=["linear", "mingru", "ssm", "attn", "delta"],
+                    default="linear")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-paths", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the config's batch per GPU (small cases for ncu captures)")
     return ap.parse_args()
+
+
+def make_workload(args):
+    import dataclasses
+    wl = WORKLOADS[args.config]()
+    if args.batch:
+        wl.cfg = dataclasses.replace(wl.cfg, batch=args.batch)
+    return wl
 
 
 def dist_env():
@@ -385,8 +396,89 @@ class AttnWorkload:
                 "(4 q heads) at L=1024, scaled to the step by FLOP share")
 
 
+class DeltaWorkload:
+    """DeltaNet delta rule fwd (with state checkpoints) + bwd."""
+
+    def __init__(self):
+        from edifice_b200.shard import DeltaConfig
+        self.cfg = DeltaConfig()
+        self.kname = "delta_rule"
+        self.dtype = "bf16"
+
+    def describe(self, world):
+        c = self.cfg
+        return {"workload": "%s fwd+bwd (BASELINE configs[2])" % c.name,
+                "batch_per_gpu": c.batch, "global_batch": c.batch * world, "heads": c.heads,
+                "seq_len": c.seq_len, "head_dim": c.head_dim, "chunk": c.chunk,
+                "beta": "one per (token, head)",
+                "parallelism": "dp%d ((batch, head) shards, no collective)" % world,
+                "l2": "inputs larger than L2 (%.2f GB per step)"
+                      % ((c.bytes_fwd() + c.bytes_bwd()) / 1e9)}
+
+    def setup(self, dev, rank):
+        from edifice_b200 import shard
+        self.units = shard.plan_units(self.cfg.units, rank, self._world)
+        self.q, self.k, self.v, self.beta, self.do = shard.delta_inputs(self.cfg, self.units, dev)
+
+    def kernels(self):
+        return {"fwd": ("hbm", self.cfg.bytes_fwd()), "bwd": ("hbm", self.cfg.bytes_bwd())}
+
+    launches_per_step = 2
+    tokens = property(lambda self: self.cfg.tokens)
+
+    def step(self, ev=None):
+        from edifice_b200 import fused_scan as fs
+        if ev:
+            ev[0].record()
+        _, ck = fs.delta_net_scan(self.q, self.k, self.v, self.beta, with_ckpt=True)
+        if ev:
+            ev[1].record()
+        fs.delta_rule_backward(self.q, self.k, self.v, self.beta, self.do, ck)
+        if ev:
+            ev[2].record()
+
+    def host_inputs(self):
+        return [self.q, self.k, self.v, self.beta, self.do]
+
+    def e2e_step(self, dev_in):
+        from edifice_b200 import fused_scan as fs
+        q, k, v, beta, do = dev_in
+        o, ck = fs.delta_net_scan(q, k, v, beta, with_ckpt=True)
+        return (o,) + tuple(fs.delta_rule_backward(q, k, v, beta, do, ck))
+
+    api = "edifice_b200.fused_scan.delta_net_scan + delta_rule_backward"
+
+    def extra(self, fwd_ms, bwd_ms):
+        peak = measured_peaks()["tensor"][0]
+        tf = (self.cfg.flops_fwd() + self.cfg.flops_bwd()) / ((fwd_ms + bwd_ms) / 1e3) / 1e12
+        return {"chunked_flops_TFLOP/s": round(tf, 2),
+                "tensor_frac_of_peak": round(tf / peak, 4)}
+
+    def cpu_step(self, rows=None, prec="f32"):
+        import numpy as np
+        import oracle as O
+        c = self.cfg
+        Ls = 512
+        if not hasattr(self, "_cpu"):
+            rng = np.random.default_rng(0)
+            q = rng.standard_normal((1, Ls, 1, c.head_dim), dtype=np.float32)
+            k = rng.standard_normal((1, Ls, 1, c.head_dim), dtype=np.float32)
+            k /= np.sqrt((k * k).sum(-1, keepdims=True) + 1e-6)
+            v = rng.standard_normal((1, Ls, 1, c.head_dim), dtype=np.float32)
+            beta = (1 / (1 + np.exp(-rng.standard_normal((1, Ls, 1))))).astype(np.float32)
+            do = rng.standard_normal((1, Ls, 1, c.head_dim), dtype=np.float32)
+            self._cpu = (q, k, v, beta, do)
+        q, k, v, beta, do = self._cpu
+        O.delta_net_fwd(q, k, v, beta, prec=prec)
+        O.delta_net_bwd(q, k, v, beta, do, prec=prec)
+        return Ls / c.heads  # one head of 16 over 512 tokens, in token-equivalents
+
+    cpu_what = ("oracle f32 port (fused_scan.ex:2212-2236, 1257-1326) on one (batch, head) "
+                "pair over 512 tokens, scaled by the head share")
+
+
 WORKLOADS = {"linear": lambda: ScanWorkload(False), "mingru": lambda: ScanWorkload(True),
-             "ssm": SsmWorkload, "attn": AttnWorkload}
+             "ssm": SsmWorkload, "attn": AttnWorkload, "delta": DeltaWorkload}
 
 
 def roofline(wl, kern_ms):
@@ -472,7 +564,7 @@ def run_ours(args):
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
-    wl = WORKLOADS[args.config]()
+    wl = make_workload(args)
     wl._world = world
     wl.setup(dev, rank)
     sampler = ClockSampler(local)
@@ -526,7 +618,7 @@ def run_ours(args):
     if args.config == "linear" and not args.no_paths:
         del wl.a, wl.b, wl.dy
         torch.cuda.empty_cache()
-        for name in ("mingru", "attn", "ssm"):
+        for name in ("mingru", "attn", "delta", "ssm"):
             pw = WORKLOADS[name]()
             pw._world = world
             pw.setup(dev, rank)
@@ -579,7 +671,7 @@ def run_reference(args):
     if rank != 0:
         return
     import oracle as O
-    wl = WORKLOADS[args.config]()
+    wl = make_workload(args)
     wl._world = 1
     n = cpu_threads()
     O.set_threads(n)

@@ -235,14 +235,24 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
 
             const int kv0 = j * BN;
             float x[BN];
-            float mt = -INFINITY;
+            // only the diagonal tiles and a ragged last tile need a mask (CTA-uniform)
+            const bool need_mask = (kv0 + BN > L) || (CAUSAL && kv0 + BN - 1 > q0);
+            if (need_mask) {
 #pragma unroll
-            for (int c = 0; c < BN; ++c) {
-                const int kv = kv0 + c;
-                const bool masked = kv >= L || (CAUSAL && kv > qrow);
-                x[c] = masked ? -INFINITY : __uint_as_float(sr[c >> 5][c & 31]) * scale_log2;
-                mt = fmaxf(mt, x[c]);
+                for (int c = 0; c < BN; ++c) {
+                    const int kv = kv0 + c;
+                    const bool masked = kv >= L || (CAUSAL && kv > qrow);
+                    x[c] = masked ? -INFINITY : __uint_as_float(sr[c >> 5][c & 31]) * scale_log2;
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < BN; ++c) x[c] = __uint_as_float(sr[c >> 5][c & 31]) * scale_log2;
             }
+            // 4 independent max chains
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int c = 0; c < BN; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
+            const float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
             const float m_new = fmaxf(m_used, mt);
             bool rescale = false;
             float alpha = 1.0f;
@@ -273,7 +283,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                 tc::tmem_wait_st();
             }
             const float mu = m_used == -INFINITY ? 0.0f : m_used;
-            float rs = 0.0f;
+            float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             uint8_t* prow = sP;
 #pragma unroll
             for (int ch = 0; ch < BN / 8; ++ch) {
@@ -281,13 +291,13 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
                     p[e] = tc::ex2(x[ch * 8 + e] - mu);
-                    rs += p[e];
+                    rs4[e & 3] += p[e];
                 }
                 const uint4 v = make_uint4(tc::pack_bf16x2(p[0], p[1]), tc::pack_bf16x2(p[2], p[3]),
                                            tc::pack_bf16x2(p[4], p[5]), tc::pack_bf16x2(p[6], p[7]));
                 *reinterpret_cast<uint4*>(prow + tc::sw128_off(row, ch)) = v;
             }
-            l += rs;
+            l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
             fence_proxy_async();
             tc::fence_before_sync();
             __syncwarp();

@@ -36,7 +36,7 @@ constexpr int kBwdThreads = 320;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct BwdMaps {
-    CUtensorMap q, k, v, dO;
+    CUtensorMap q, k, v, dO, dq;  // dq: the f32 accumulator, 32-column SW128 boxes
 };
 
 template <int HD>
@@ -51,7 +51,9 @@ struct BwdSmem {
     static constexpr int OFF_DO = OFF_Q + QD_STAGES * QD_BYTES;
     static constexpr int OFF_PT = OFF_DO + QD_STAGES * QD_BYTES;
     static constexpr int OFF_DS = OFF_PT + T_BYTES;
-    static constexpr int OFF_LSE = OFF_DS + T_BYTES;
+    static constexpr int OFF_DQ = OFF_DS + T_BYTES;           // f32 dQ staging [HD/32][BQ][32]
+    static constexpr int DQ_BYTES = BQ * HD * 4;
+    static constexpr int OFF_LSE = OFF_DQ + DQ_BYTES;
     static constexpr int OFF_D = OFF_LSE + QD_STAGES * BQ * 4;
     static constexpr int OFF_BAR = OFF_D + QD_STAGES * BQ * 4;
     // kv_full, qd_full[2], qd_empty[2], sdp_full, sdp_free, pds_full, mm2_done,
@@ -62,12 +64,6 @@ struct BwdSmem {
                          TM_DQ = 2 * HD + 128;
     static constexpr int TMEM_COLS = 512;
 };
-
-static __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
-    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
-                 "f"(d)
-                 : "memory");
-}
 
 template <int HD, bool CAUSAL>
 __global__ void __launch_bounds__(kBwdThreads, 1)
@@ -84,6 +80,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     uint8_t* sdO = smem + S::OFF_DO;
     uint8_t* sPt = smem + S::OFF_PT;
     uint8_t* sDs = smem + S::OFF_DS;
+    uint8_t* sDq = smem + S::OFF_DQ;
     float* sLse = reinterpret_cast<float*>(smem + S::OFF_LSE);
     float* sD = reinterpret_cast<float*>(smem + S::OFF_D);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
@@ -288,6 +285,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
             const float* l2 = sLse + s * BQ;
             const float* dd = sD + s * BQ;
+            // masks are only needed on the diagonal and for a ragged last kv tile;
+            // query rows past L carry lse = +inf and give P = 0 by themselves
+            const bool need_mask = (kt * BKV + BKV > L) || (CAUSAL && i * BQ < kt * BKV + BKV);
 #pragma unroll
             for (int ch = 0; ch < BQ / 8; ++ch) {
                 float p[8], ds[8];
@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 for (int e = 0; e < 8; ++e) {
                     const int c = ch * 8 + e;
                     const int q_idx = i * BQ + c;
-                    const bool valid = kv_idx < L && (!CAUSAL || q_idx >= kv_idx);
+                    const bool valid = !need_mask || (kv_idx < L && (!CAUSAL || q_idx >= kv_idx));
                     const float sv = __uint_as_float(sr[c >> 5][c & 31]);
                     const float dpv = __uint_as_float(dr[c >> 5][c & 31]);
                     p[e] = valid ? tc::ex2(fmaf(sv, scale_log2, -l2[c])) : 0.0f;
@@ -333,19 +333,31 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(dq_free);
-            // M = 64 accumulator: lanes 32w + t (t < 16) hold query row 16w + t
-            const int q_row = i * BQ + 16 * w + lane;
-            if (lane < 16 && q_row < L) {
-                float* dst = dq_acc + ((long long)bh * L + q_row) * HD;
+            // the previous tile's bulk reduce must be done reading the staging tile
+            if (w == 0 && lane == 0) tc::tma_store_wait_read_all();
+            tc::named_bar(2, 128);
+            // M = 64 accumulator: lanes 32w + t (t < 16) hold query row 16w + t of the tile
+            if (lane < 16) {
+                const int r = 16 * w + lane;
 #pragma unroll
                 for (int cc = 0; cc < HD / 32; ++cc)
 #pragma unroll
-                    for (int e = 0; e < 32; e += 4)
-                        red_add_v4(dst + cc * 32 + e, __uint_as_float(qv[cc][e]),
-                                   __uint_as_float(qv[cc][e + 1]), __uint_as_float(qv[cc][e + 2]),
-                                   __uint_as_float(qv[cc][e + 3]));
+                    for (int j = 0; j < 8; ++j)
+                        *reinterpret_cast<uint4*>(sDq + cc * (BQ * 128) + tc::sw128_off(r, j)) =
+                            make_uint4(qv[cc][4 * j], qv[cc][4 * j + 1], qv[cc][4 * j + 2],
+                                       qv[cc][4 * j + 3]);
+            }
+            fence_proxy_async();
+            tc::named_bar(2, 128);
+            // dq_acc[bh, i*BQ .., :] += staging tile (rows past L are clipped)
+            if (w == 0 && lane == 0) {
+#pragma unroll
+                for (int cc = 0; cc < HD / 32; ++cc)
+                    tc::tma_reduce_add_3d(&maps.dq, sDq + cc * (BQ * 128), cc * 32, i * BQ, bh);
+                tc::tma_store_commit();
             }
         }
+        if (w == 0 && lane == 0) tc::tma_store_wait_all();
         if (ok && mbar_wait_bounded(all_done, 0, err, EDB_DEVERR_ATTN_PIPE)) {
             tc::fence_after_sync();
             const int r = w * 32 + lane;
@@ -525,6 +537,7 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dO, c
     if ((s = tc::make_attn_map(&maps.dO, dO, HD, L, B * Hq, BQ))) return s;
     if ((s = tc::make_attn_map(&maps.k, k, HD, L, B * Hkv, BKV))) return s;
     if ((s = tc::make_attn_map(&maps.v, v, HD, L, B * Hkv, BKV))) return s;
+    if ((s = tc::make_attn_map_f32(&maps.dq, dq_acc, HD, L, B * Hq, BQ))) return s;
     auto kern = attn_bwd_tc_kernel<HD, CAUSAL>;
     const int smem = BwdSmem<HD>::TOTAL;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

@@ -134,6 +134,19 @@ static __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, cons
         "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
         : "memory");
 }
+// global[tile at {x,y,z}] += smem tile (f32 add), bulk-group completion
+static __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src,
+                                                         int x, int y, int z) {
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group"
+        " [%0, {%2, %3, %4}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+// wait until every committed bulk group has finished READING its smem source
+static __device__ __forceinline__ void tma_store_wait_read_all() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
 static __device__ __forceinline__ void tma_store_commit() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
@@ -171,6 +184,16 @@ inline int make_attn_map(CUtensorMap* m, const void* p, int d, int L, int nbh, i
     const cuuint64_t strides[2] = {(cuuint64_t)d * 2, (cuuint64_t)L * d * 2};
     const cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
     CUresult r = edb::encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(p),
+                                   dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    return r == CUDA_SUCCESS ? EDB_OK : EDB_ERR_UNSUPPORTED;
+}
+
+// 3D f32 tensor map [nbh][L][d] with SWIZZLE_128B boxes of 32 columns x box_rows.
+inline int make_attn_map_f32(CUtensorMap* m, const void* p, int d, int L, int nbh, int box_rows) {
+    const cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)L, (cuuint64_t)nbh};
+    const cuuint64_t strides[2] = {(cuuint64_t)d * 4, (cuuint64_t)L * d * 4};
+    const cuuint32_t box[3] = {32, (cuuint32_t)box_rows, 1};
+    CUresult r = edb::encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(p),
                                    dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     return r == CUDA_SUCCESS ? EDB_OK : EDB_ERR_UNSUPPORTED;
 }

@@ -105,6 +105,44 @@ class AttnConfig:
         return 2.5 * self.flops_fwd()
 
 
+@dataclasses.dataclass(frozen=True)
+class DeltaConfig:
+    """DeltaNet fwd+bwd, bf16 io, f32 state, chunk 64,
+    one beta per (token, head)."""
+    name: str = "delta_net_cfg2"
+    batch: int = 4
+    heads: int = 16
+    seq_len: int = 4096
+    head_dim: int = 128
+    chunk: int = 64
+    dtype: torch.dtype = torch.bfloat16
+
+    @property
+    def units(self):
+        return self.batch * self.heads  # (batch, head) pairs
+
+    @property
+    def tokens(self):
+        return self.batch * self.seq_len
+
+    def flops_fwd(self):
+        # chunked WY form, dense-tile count: 10 C^2 d + 6 C d^2 per chunk
+        C, d = self.chunk, self.head_dim
+        n_chunks = self.batch * self.heads * self.seq_len // C
+        return (10 * C * C * d + 6 * C * d * d) * n_chunks
+
+    def flops_bwd(self):
+        return 2 * self.flops_fwd()
+
+    def bytes_fwd(self):
+        e = self.batch * self.seq_len * self.heads * self.head_dim
+        return 4 * e * 2 + self.batch * self.seq_len * self.heads * 2  # q k v o + beta
+
+    def bytes_bwd(self):
+        e = self.batch * self.seq_len * self.heads * self.head_dim
+        return 8 * e * 2 + 2 * self.batch * self.seq_len * self.heads * 2
+
+
 def unit_seed(base_seed, unit):
     return (int(base_seed) * 1_000_003 + int(unit)) & 0x7FFFFFFFFFFF
 
@@ -185,6 +223,27 @@ def attn_inputs(cfg, units, device, base_seed=0):
         v[b, hk].copy_(torch.randn((L, d), generator=g, device=device))
         do[b, hk * G:(hk + 1) * G].copy_(torch.randn((G, L, d), generator=g, device=device))
     return q, k, v, do
+
+
+def delta_inputs(cfg, units, device, base_seed=0):
+    """configs[2] per (batch, head) unit: q, k ~ N(0,1), k L2-normalised over d;
+    v ~ N(0,1); beta = sigmoid(N(0,1)) per token; dO ~ N(0,1).  The rank's units
+    are laid out as a [len(units)/heads, L, heads, d] batch."""
+    L, H, d = cfg.seq_len, cfg.heads, cfg.head_dim
+    nb = len(units) // H
+    q = torch.empty((nb, L, H, d), dtype=cfg.dtype, device=device)
+    k, v, do = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
+    beta = torch.empty((nb, L, H), dtype=cfg.dtype, device=device)
+    for i, u in enumerate(units):
+        b, h = divmod(i, H)
+        g = torch.Generator(device=device).manual_seed(unit_seed(base_seed, u))
+        q[b, :, h].copy_(torch.randn((L, d), generator=g, device=device))
+        kk = torch.randn((L, d), generator=g, device=device)
+        k[b, :, h].copy_(kk / torch.sqrt((kk * kk).sum(-1, keepdim=True) + 1e-6))
+        v[b, :, h].copy_(torch.randn((L, d), generator=g, device=device))
+        beta[b, :, h].copy_(torch.sigmoid(torch.randn((L,), generator=g, device=device)))
+        do[b, :, h].copy_(torch.randn((L, d), generator=g, device=device))
+    return q, k, v, beta, do
 
 
 def ceil_div(a, b):
