@@ -10,7 +10,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/edifice_b200.h"
+#include "edifice_b200.h"
 
 // ---------------------------------------------------------------- errors
 // Device-side error word, one per device (defined in runtime.cu; kernels get
