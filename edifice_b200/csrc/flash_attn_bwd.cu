@@ -17,9 +17,10 @@
 //   dK  += dS^T Q   (128xD)                             TMEM cols [D, 2D)
 //   dQ_i = dS K     (64xD, dS^T read as an MN-major A)  TMEM cols [2D+128, 3D+128)
 // Warps 0-3 turn S^T, dP^T (TMEM lane = kv row) into P^T and dS^T (bf16,
-// 128-byte swizzled smem); warps 4-7 add each dQ_i into an f32 accumulator with
-// red.global.add.v4.f32 and at the end write dK, dV; warp 8 streams Q_i / dO_i
-// / lse / D through a 2-stage TMA ring; warp 9 issues the MMAs.  S^T/dP^T of
+// 128-byte swizzled smem); warps 4-7 stage each dQ_i in swizzled smem and add
+// it into an f32 accumulator with one TMA bulk reduce-add per 32 columns, and at
+// the end write dK, dV; warp 8 streams Q_i / dO_i / lse / D through a 3-stage
+// TMA ring; warp 9 issues the MMAs.  S^T/dP^T of
 // the next tile is issued as soon as the compute warps have read the current
 // one, so it overlaps their exponentials.  A last kernel converts dQ to the io
 // dtype.  Other shapes run SIMT kernels with the same math.
@@ -31,7 +32,9 @@ namespace {
 
 constexpr int BKV = 128;
 constexpr int BQ = 64;
-constexpr int QD_STAGES = 2;
+// A Q/dO stage is released only after its second use (the dV/dK MMAs), so
+// three stages are needed to keep the next tiles' TMA loads off the critical path.
+constexpr int QD_STAGES = 3;
 constexpr int kBwdThreads = 320;
 constexpr float kLog2e = 1.4426950408889634f;
 
