@@ -35,8 +35,10 @@ SIGNATURES = {
     "edb_flash_attention_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f,
                                      _vp]),
     "edb_delta_rule_ckpt_bytes": (_sz, [_i, _i, _i, _i]),
-    "edb_delta_rule_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _vp]),
-    "edb_delta_rule_bwd_workspace": (_sz, [_i, _i, _i, _i, _i]),
+    "edb_delta_rule_fwd_workspace": (_sz, [_i, _i, _i, _i, _i, _i]),
+    "edb_delta_rule_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _vp, _sz,
+                                _vp]),
+    "edb_delta_rule_bwd_workspace": (_sz, [_i, _i, _i, _i, _i, _i, _i]),
     "edb_delta_rule_bwd": (_i, [_i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i,
                                 _i, _i, _vp, _sz, _vp]),
     "edb_flash_attention_bwd_workspace": (_sz, [_i, _i, _i, _i, _i, _i, _i]),

@@ -1,0 +1,477 @@
+// delta_chunked.cu -- DeltaNet delta rule in chunked WY form on tcgen05 (forward).
+//
+// Same semantics as delta_rule.cu (lib/edifice/cuda/fused_scan.ex:2212-2236,
+// lib/edifice/recurrent/delta_net.ex:231-273; the reference's CUDA kernel,
+// native/cuda/fused_delta_rule_scan.cu, walks tokens one by one).  This path
+// serves bf16 io, one beta per (token, head), head_dim 128.
+//
+// Per chunk of C = 64 tokens (K, Q, V: C x d rows; S_0 the state before the
+// chunk, [d_v][d_k]):
+//   A   = tril(diag(beta) K K^T, -1),   T = (I + A)^-1,   T_b = T diag(beta)
+//   W   = T_b K,   U0 = T_b V,   M = tril(Q K^T) (diagonal included)
+//   U~  = U0 - W S_0^T            (the chunk's beta-scaled errors)
+//   O   = Q S_0^T + M U~
+//   S_C = S_0 + U~^T K
+// which is the token recurrence S_t = S_{t-1} + beta_t (v_t - S_{t-1} k_t) k_t^T,
+// o_t = S_t q_t, regrouped (T solves the within-chunk dependence of the errors).
+//
+// Kernels:
+//   delta_prep_kernel       one CTA per chunk (all chunks at once), SIMT f32:
+//                           K K^T, Q K^T, the unit-triangular solve for T, W and
+//                           U0; writes -W, Q, K^T, U0^T and M (f32) to scratch.
+//   delta_state_fwd_kernel  one CTA per (b, h), chunks in order, tcgen05
+//                           kind::tf32 with every operand K-major.  S lives in
+//                           TMEM (lanes = value dim, columns = key dim) as the f32
+//                           accumulator and is fed back as the A operand:
+//                             D_U  = U0^T + S (-W)^T        M=128, N=64,  K=128
+//                             D_O  = S Q^T + D_U M^T        M=128, N=64,  K=128/64
+//                             S   += D_U (K^T)^T            M=128, N=128, K=64
+//                           -W, Q, K^T, M arrive by TMA (SWIZZLE_128B f32 boxes)
+//                           in a 2-stage ring; U0^T rows are stored into TMEM
+//                           by the threads.  TF32 operands (10-bit mantissa),
+//                           f32 accumulation: ~1e-3 relative per product.
+#include <math.h>
+
+#include "tc_common.cuh"
+
+namespace {
+
+constexpr int C = 64;    // chunk length
+constexpr int D = 128;   // head dim (d_k = d_v)
+constexpr int kPrepThreads = 256;
+constexpr int kStateThreads = 128;
+
+size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// ------------------------------------------------------------------ scratch
+struct FwdScratch {
+    float* Wn;   // [nch][C][D]  -W
+    float* Q;    // [nch][C][D]
+    float* KT;   // [nch][D][C]
+    float* U0T;  // [nch][D][C]
+    float* M;    // [nch][C][C]  tril(Q K^T), diagonal included
+};
+
+size_t fwd_scratch_bytes(long long nch) {
+    return 4 * a256((size_t)nch * C * D * 4) + a256((size_t)nch * C * C * 4);
+}
+
+FwdScratch carve_fwd(void* ws, long long nch) {
+    char* p = static_cast<char*>(ws);
+    const size_t cd = a256((size_t)nch * C * D * 4);
+    FwdScratch s;
+    s.Wn = reinterpret_cast<float*>(p);
+    s.Q = reinterpret_cast<float*>(p + cd);
+    s.KT = reinterpret_cast<float*>(p + 2 * cd);
+    s.U0T = reinterpret_cast<float*>(p + 3 * cd);
+    s.M = reinterpret_cast<float*>(p + 4 * cd);
+    return s;
+}
+
+// ------------------------------------------------------------------ prep
+// grid (NC, H, B), 256 threads.  Rows past L load as zero with beta 0, which
+// makes their W / U0 rows zero, so the padded tail leaves S untouched.
+constexpr int PP = D + 1;      // padded [C][D] row (odd: conflict-free columns)
+constexpr int PC = C + 1;      // padded [C][C] row
+constexpr size_t kPrepSmem = (size_t)(3 * C * PP + 2 * C * PC + C) * sizeof(float);
+
+__global__ void __launch_bounds__(kPrepThreads, 1)
+    delta_prep_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                      const __nv_bfloat16* __restrict__ v, const __nv_bfloat16* __restrict__ beta,
+                      FwdScratch ws, int L, int H, int NC) {
+    extern __shared__ float sm[];
+    float* Ks = sm;              // [C][PP]
+    float* Qs = Ks + C * PP;     // [C][PP]  (then -W)
+    float* Vs = Qs + C * PP;     // [C][PP]  (then U0)
+    float* G = Vs + C * PP;      // [C][PC]  A = tril(diag(beta) K K^T, -1)
+    float* Tm = G + C * PC;      // [C][PC]  T
+    float* bs = Tm + C * PC;     // [C]
+    const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x;
+    const long long ch = ((long long)b * H + h) * NC + c;
+    const int t0 = c * C;
+
+    for (int idx = tid; idx < C * (D / 8); idx += kPrepThreads) {
+        const int t = idx / (D / 8), j8 = (idx % (D / 8)) * 8;
+        float kf[8], qf[8], vf[8];
+        if (t0 + t < L) {
+            const long long off = (((long long)b * L + t0 + t) * H + h) * D + j8;
+            Vec16<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(k + off), kf);
+            Vec16<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(q + off), qf);
+            Vec16<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(v + off), vf);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) kf[e] = qf[e] = vf[e] = 0.0f;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            Ks[t * PP + j8 + e] = kf[e];
+            Qs[t * PP + j8 + e] = qf[e];
+            Vs[t * PP + j8 + e] = vf[e];
+        }
+        float* qg = ws.Q + (ch * C + t) * D + j8;
+        *reinterpret_cast<float4*>(qg) = make_float4(qf[0], qf[1], qf[2], qf[3]);
+        *reinterpret_cast<float4*>(qg + 4) = make_float4(qf[4], qf[5], qf[6], qf[7]);
+    }
+    if (tid < C)
+        bs[tid] = t0 + tid < L ? __bfloat162float(beta[((long long)b * L + t0 + tid) * H + h])
+                               : 0.0f;
+    __syncthreads();
+
+    // K^T: [D][C], coalesced over t
+    for (int idx = tid; idx < D * C; idx += kPrepThreads)
+        ws.KT[ch * D * C + idx] = Ks[(idx % C) * PP + idx / C];
+
+    // A and M: thread -> row t = tid / 4, columns s = (tid % 4) + 4 e
+    {
+        const int t = tid >> 2, sl = tid & 3;
+        float g[16], m[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) g[e] = m[e] = 0.0f;
+        for (int j = 0; j < D; ++j) {
+            const float kt = Ks[t * PP + j], qt = Qs[t * PP + j];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const float ks = Ks[(sl + 4 * e) * PP + j];
+                g[e] = fmaf(kt, ks, g[e]);
+                m[e] = fmaf(qt, ks, m[e]);
+            }
+        }
+        float* mg = ws.M + (ch * C + t) * C;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            const int s = sl + 4 * e;
+            G[t * PC + s] = s < t ? bs[t] * g[e] : 0.0f;
+            mg[s] = s <= t ? m[e] : 0.0f;
+        }
+    }
+    __syncthreads();
+
+    // T = (I + A)^-1, forward substitution, one column per thread
+    if (tid < C) {
+        const int j = tid;
+        for (int t = 0; t < C; ++t) {
+            float acc = (t == j) ? 1.0f : 0.0f;
+            for (int s = j; s < t; ++s) acc = fmaf(-G[t * PC + s], Tm[s * PC + j], acc);
+            Tm[t * PC + j] = t >= j ? acc : 0.0f;
+        }
+    }
+    __syncthreads();
+
+    // W = T_b K, U0 = T_b V: thread -> row t, columns (tid % 4) + 4 e
+    {
+        const int t = tid >> 2, jl = tid & 3;
+        float w[32], u[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) w[e] = u[e] = 0.0f;
+        for (int s = 0; s <= t; ++s) {
+            const float tb = Tm[t * PC + s] * bs[s];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                w[e] = fmaf(tb, Ks[s * PP + jl + 4 * e], w[e]);
+                u[e] = fmaf(tb, Vs[s * PP + jl + 4 * e], u[e]);
+            }
+        }
+        __syncthreads();  // every read of Q and V is done: reuse their rows
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+            Qs[t * PP + jl + 4 * e] = -w[e];
+            Vs[t * PP + jl + 4 * e] = u[e];
+        }
+    }
+    __syncthreads();
+    for (int idx = tid; idx < C * D; idx += kPrepThreads)
+        ws.Wn[ch * C * D + idx] = Qs[(idx / D) * PP + idx % D];
+    for (int idx = tid; idx < D * C; idx += kPrepThreads)
+        ws.U0T[ch * D * C + idx] = Vs[(idx % C) * PP + idx / C];
+}
+
+// ------------------------------------------------------------------ state fwd
+struct StateMaps {
+    CUtensorMap Wn, Q, KT, M;
+};
+
+constexpr int BOX_CD = C * 128;   // 8 KB: [C rows][32 f32] box
+constexpr int BOX_DC = D * 128;   // 16 KB: [D rows][32 f32] box
+constexpr int OFF_W = 0;
+constexpr int OFF_Q = OFF_W + 4 * BOX_CD;
+constexpr int OFF_KT = OFF_Q + 4 * BOX_CD;
+constexpr int OFF_M = OFF_KT + 2 * BOX_DC;
+constexpr int STAGE_BYTES = OFF_M + 2 * BOX_CD;  // 112 KB
+constexpr int OFF_BARS = 2 * STAGE_BYTES;
+constexpr int STATE_SMEM = OFF_BARS + 64;
+constexpr int TM_S = 0, TM_U = 128, TM_O = 192, TM_COLS = 256;
+
+static __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
+    return (1u << 4)                      // D format f32
+           | (2u << 7) | (2u << 10)       // A, B tf32 (both K-major)
+           | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::tf32, A K-major in TMEM.
+static __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem,
+                                                   uint64_t b_desc, uint32_t idesc,
+                                                   uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// K-major SW128 f32 operand: 8-element K step kk inside boxes of 32 columns.
+static __device__ __forceinline__ uint64_t kdesc(const uint8_t* base, int box_bytes, int kk) {
+    return tc::sdesc_sw128(base + (kk >> 2) * box_bytes + (kk & 3) * 32, 16, 1024);
+}
+
+// Thread i: row i of the [D][D] TMEM state -> global row (512 B).
+static __device__ __forceinline__ void store_state_row(float* dst, uint32_t taddr) {
+#pragma unroll
+    for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t x[32];
+        tc::tmem_ld32(taddr + cc * 32, x);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4*>(dst + cc * 32 + e) =
+                make_float4(__uint_as_float(x[e]), __uint_as_float(x[e + 1]),
+                            __uint_as_float(x[e + 2]), __uint_as_float(x[e + 3]));
+    }
+}
+
+__global__ void __launch_bounds__(kStateThreads, 1)
+    delta_state_fwd_kernel(const __grid_constant__ StateMaps maps, const float* __restrict__ U0T,
+                           float* __restrict__ ckpt, __nv_bfloat16* __restrict__ o, int L, int H,
+                           int NC, unsigned* err) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BARS);  // [2]
+    uint64_t* mbar = full + 2;
+    uint32_t* s_misc = reinterpret_cast<uint32_t*>(mbar + 1);  // [0] tmem base, [1] abort
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const long long bh = (long long)b * H + h;
+    const long long ch0 = bh * NC;
+
+    if ((smem_u32(smem) & 1023u) != 0) {  // SW128 boxes need 1 KB alignment
+        if (tid == 0) edb_flag_error(err, EDB_DEVERR_DELTA_PIPE);
+        return;
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(s_misc, TM_COLS);
+        tc::tmem_relinquish();
+    }
+    if (tid == 0) {
+        s_misc[1] = 0;
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        mbar_init(mbar, 1);
+        fence_mbar_init();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = s_misc[0];
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const int i = tid;  // TMEM lane = value-dim row of S
+
+    auto issue = [&](int c) {
+        uint8_t* st = smem + (c & 1) * STAGE_BYTES;
+        uint64_t* bar = &full[c & 1];
+        const int rc = (int)((ch0 + c) * C), rd = (int)((ch0 + c) * D);
+        mbar_arrive_expect_tx(bar, STAGE_BYTES);
+        for (int bx = 0; bx < 4; ++bx) {
+            tma_load_2d(st + OFF_W + bx * BOX_CD, &maps.Wn, bar, bx * 32, rc);
+            tma_load_2d(st + OFF_Q + bx * BOX_CD, &maps.Q, bar, bx * 32, rc);
+        }
+        for (int bx = 0; bx < 2; ++bx) {
+            tma_load_2d(st + OFF_KT + bx * BOX_DC, &maps.KT, bar, bx * 32, rd);
+            tma_load_2d(st + OFF_M + bx * BOX_CD, &maps.M, bar, bx * 32, rc);
+        }
+    };
+    int issued = 0, landed = 0;
+    if (tid == 0) {
+        prefetch_tmap(&maps.Wn);
+        prefetch_tmap(&maps.Q);
+        prefetch_tmap(&maps.KT);
+        prefetch_tmap(&maps.M);
+        issue(0);
+        issued = 1;
+        if (NC > 1) {
+            issue(1);
+            issued = 2;
+        }
+    }
+    {  // S = 0
+        uint32_t z[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) z[e] = 0u;
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) tc::tmem_st32(tmem + TM_S + lane_base + cc * 32, z);
+        tc::tmem_wait_st();
+    }
+    constexpr uint32_t idN64 = idesc_tf32(128, C);
+    constexpr uint32_t idN128 = idesc_tf32(128, D);
+    uint32_t mph = 0;
+    bool mma_pending = false;
+
+    for (int c = 0; c < NC; ++c) {
+        // U0^T row i -> D_U; S row i -> checkpoint c
+        {
+            const float* u = U0T + ((ch0 + c) * D + i) * C;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                uint32_t r[32];
+#pragma unroll
+                for (int e = 0; e < 32; e += 4) {
+                    const float4 f = *reinterpret_cast<const float4*>(u + half * 32 + e);
+                    r[e] = __float_as_uint(f.x);
+                    r[e + 1] = __float_as_uint(f.y);
+                    r[e + 2] = __float_as_uint(f.z);
+                    r[e + 3] = __float_as_uint(f.w);
+                }
+                tc::tmem_st32(tmem + TM_U + lane_base + half * 32, r);
+            }
+            if (ckpt != nullptr)
+                store_state_row(ckpt + ((bh * (NC + 1) + c) * D + i) * D,
+                                tmem + TM_S + lane_base);
+            tc::tmem_wait_st();
+        }
+        tc::fence_before_sync();
+        __syncthreads();
+        tc::fence_after_sync();
+        if (tid == 0) {
+            const uint8_t* st = smem + (c & 1) * STAGE_BYTES;
+            bool ok = mbar_wait_bounded(&full[c & 1], (c >> 1) & 1, err, EDB_DEVERR_DELTA_PIPE);
+            if (ok) {
+                landed = c + 1;
+                tc::fence_after_sync();
+#pragma unroll
+                for (int kk = 0; kk < D / 8; ++kk) {
+                    mma_tf32_ts(tmem + TM_U, tmem + TM_S + kk * 8, kdesc(st + OFF_W, BOX_CD, kk),
+                                idN64, 1);
+                    mma_tf32_ts(tmem + TM_O, tmem + TM_S + kk * 8, kdesc(st + OFF_Q, BOX_CD, kk),
+                                idN64, kk > 0);
+                }
+                tc::commit(mbar);
+                mma_pending = true;
+                ok = mbar_wait_bounded(mbar, mph, err, EDB_DEVERR_DELTA_PIPE);
+                if (ok) {
+                    mph ^= 1u;
+                    mma_pending = false;
+                }
+            }
+            if (ok) {
+                tc::fence_after_sync();
+#pragma unroll
+                for (int kk = 0; kk < C / 8; ++kk) {
+                    mma_tf32_ts(tmem + TM_O, tmem + TM_U + kk * 8, kdesc(st + OFF_M, BOX_CD, kk),
+                                idN64, 1);
+                    mma_tf32_ts(tmem + TM_S, tmem + TM_U + kk * 8,
+                                kdesc(st + OFF_KT, BOX_DC, kk), idN128, 1);
+                }
+                tc::commit(mbar);
+                mma_pending = true;
+                ok = mbar_wait_bounded(mbar, mph, err, EDB_DEVERR_DELTA_PIPE);
+                if (ok) {
+                    mph ^= 1u;
+                    mma_pending = false;
+                }
+            }
+            if (ok && c + 2 < NC) {
+                issue(c + 2);
+                issued = c + 3;
+            }
+            if (!ok) s_misc[1] = 1;
+        }
+        tc::fence_before_sync();
+        __syncthreads();
+        tc::fence_after_sync();
+        if (s_misc[1]) break;
+        // O^T row i (value dim i, tokens t) -> o[b, c C + t, h, i]
+        {
+            uint32_t x0[32], x1[32];
+            tc::tmem_ld32(tmem + TM_O + lane_base, x0);
+            tc::tmem_ld32(tmem + TM_O + lane_base + 32, x1);
+            tc::tmem_wait_ld();
+            __nv_bfloat16* op = o + (((long long)b * L + c * C) * H + h) * D + i;
+            const long long ts = (long long)H * D;
+            const int nt = min(C, L - c * C);
+#pragma unroll
+            for (int t = 0; t < 32; ++t)
+                if (t < nt) op[t * ts] = __float2bfloat16(__uint_as_float(x0[t]));
+#pragma unroll
+            for (int t = 0; t < 32; ++t)
+                if (t + 32 < nt) op[(t + 32) * ts] = __float2bfloat16(__uint_as_float(x1[t]));
+        }
+        tc::fence_before_sync();
+        __syncthreads();
+        tc::fence_after_sync();
+    }
+    if (s_misc[1]) {
+        // Abort: wait (bounded) for the copies and MMAs still in flight before
+        // the shared memory and TMEM they target are released.
+        if (tid == 0) {
+            for (int cc = landed; cc < issued; ++cc)
+                mbar_wait_bounded(&full[cc & 1], (cc >> 1) & 1, err, EDB_DEVERR_DELTA_PIPE);
+            if (mma_pending) mbar_wait_bounded(mbar, mph, err, EDB_DEVERR_DELTA_PIPE);
+        }
+    } else if (ckpt != nullptr) {
+        store_state_row(ckpt + ((bh * (NC + 1) + NC) * D + i) * D, tmem + TM_S + lane_base);
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, TM_COLS);
+    }
+}
+
+// 2D f32 map over a [rows][cols] array, boxes of 32 columns x box_rows rows.
+int make_box_map(CUtensorMap* m, const float* p, long long rows, int cols, int box_rows) {
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
+    const cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
+    CUresult r = edb::encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p),
+                                   dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    return r == CUDA_SUCCESS ? EDB_OK : EDB_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- library-internal
+// Whether the chunked path serves a call.
+bool edb_delta_chunked_ok(int dtype, int beta_per_element, int head_dim) {
+    return dtype == EDB_BF16 && !beta_per_element && head_dim == D;
+}
+
+size_t edb_delta_chunked_fwd_ws(int B, int L, int H) {
+    return fwd_scratch_bytes((long long)B * H * ((L + C - 1) / C));
+}
+
+int edb_delta_chunked_fwd(const void* q, const void* k, const void* v, const void* beta, void* o,
+                          float* s_ckpt, int B, int L, int H, void* ws, cudaStream_t st) {
+    const int NC = (L + C - 1) / C;
+    const long long nch = (long long)B * H * NC;
+    if (nch * D > 0x7fffffffLL) return EDB_ERR_UNSUPPORTED;  // TMA row coordinate is int32
+    FwdScratch w = carve_fwd(ws, nch);
+    cudaError_t e = cudaFuncSetAttribute(delta_prep_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPrepSmem);
+    if (e != cudaSuccess) return (int)e;
+    delta_prep_kernel<<<dim3(NC, H, B), kPrepThreads, kPrepSmem, st>>>(
+        (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
+        (const __nv_bfloat16*)beta, w, L, H, NC);
+    if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
+    StateMaps maps;
+    int s;
+    if ((s = make_box_map(&maps.Wn, w.Wn, nch * C, D, C))) return s;
+    if ((s = make_box_map(&maps.Q, w.Q, nch * C, D, C))) return s;
+    if ((s = make_box_map(&maps.KT, w.KT, nch * D, C, D))) return s;
+    if ((s = make_box_map(&maps.M, w.M, nch * C, C, C))) return s;
+    e = cudaFuncSetAttribute(delta_state_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             STATE_SMEM);
+    if (e != cudaSuccess) return (int)e;
+    delta_state_fwd_kernel<<<dim3(H, B), kStateThreads, STATE_SMEM, st>>>(
+        maps, w.U0T, s_ckpt, (__nv_bfloat16*)o, L, H, NC, edb::device_error_word());
+    return edb::status_from_cuda(cudaGetLastError());
+}

@@ -253,17 +253,42 @@ int check(int dtype, int B, int L, int H, int d) {
 
 }  // namespace
 
+// Chunked tensor-core forward (delta_chunked.cu).
+bool edb_delta_chunked_ok(int dtype, int beta_per_element, int head_dim);
+size_t edb_delta_chunked_fwd_ws(int B, int L, int H);
+int edb_delta_chunked_fwd(const void* q, const void* k, const void* v, const void* beta, void* o,
+                          float* s_ckpt, int B, int L, int H, void* ws, cudaStream_t st);
+
 extern "C" size_t edb_delta_rule_ckpt_bytes(int batch, int seq_len, int heads, int head_dim) {
     if (batch <= 0 || seq_len <= 0 || heads <= 0 || head_dim <= 0) return 0;
     return ckpt_bytes(batch, seq_len, heads, head_dim);
 }
 
+extern "C" size_t edb_delta_rule_fwd_workspace(int dtype, int beta_per_element, int batch,
+                                               int seq_len, int heads, int head_dim) {
+    if (check(dtype, batch, seq_len, heads, head_dim)) return 0;
+    return edb_delta_chunked_ok(dtype, beta_per_element, head_dim)
+               ? edb_delta_chunked_fwd_ws(batch, seq_len, heads)
+               : 0;
+}
+
 extern "C" int edb_delta_rule_fwd(int dtype, const void* q, const void* k, const void* v,
                                   const void* beta, int beta_per_element, void* o, float* s_ckpt,
-                                  int batch, int seq_len, int heads, int head_dim, void* stream) {
+                                  int batch, int seq_len, int heads, int head_dim,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
     if (int s = check(dtype, batch, seq_len, heads, head_dim)) return s;
     if (!q || !k || !v || !beta || !o) return EDB_ERR_NULL_POINTER;
     cudaStream_t st = (cudaStream_t)stream;
+    if (edb_delta_chunked_ok(dtype, beta_per_element, head_dim)) {
+        const size_t need = edb_delta_chunked_fwd_ws(batch, seq_len, heads);
+        if (workspace_bytes < need || !workspace) return EDB_ERR_WORKSPACE_TOO_SMALL;
+        if (!edb::aligned16(q) || !edb::aligned16(k) || !edb::aligned16(v) ||
+            !edb::aligned16(workspace) ||
+            (reinterpret_cast<uintptr_t>(s_ckpt) & 15u))
+            return EDB_ERR_MISALIGNED;
+        return edb_delta_chunked_fwd(q, k, v, beta, o, s_ckpt, batch, seq_len, heads, workspace,
+                                     st);
+    }
     const int bs = beta_per_element ? 0 : 1;
     return dtype == EDB_BF16
                ? launch_fwd<__nv_bfloat16>(q, k, v, beta, o, s_ckpt, batch, seq_len, heads,
@@ -272,10 +297,14 @@ extern "C" int edb_delta_rule_fwd(int dtype, const void* q, const void* k, const
                                    st);
 }
 
-extern "C" size_t edb_delta_rule_bwd_workspace(int batch, int seq_len, int heads, int head_dim,
+extern "C" size_t edb_delta_rule_bwd_workspace(int dtype, int beta_per_element, int batch,
+                                               int seq_len, int heads, int head_dim,
                                                int have_ckpt) {
-    if (batch <= 0 || seq_len <= 0 || heads <= 0 || head_dim <= 0) return 0;
-    return have_ckpt ? 0 : a256(ckpt_bytes(batch, seq_len, heads, head_dim));
+    if (check(dtype, batch, seq_len, heads, head_dim)) return 0;
+    if (have_ckpt) return 0;
+    // checkpoints, then the forward's own scratch
+    return a256(ckpt_bytes(batch, seq_len, heads, head_dim)) +
+           edb_delta_rule_fwd_workspace(dtype, beta_per_element, batch, seq_len, heads, head_dim);
 }
 
 extern "C" int edb_delta_rule_bwd(int dtype, const void* q, const void* k, const void* v,
@@ -285,8 +314,8 @@ extern "C" int edb_delta_rule_bwd(int dtype, const void* q, const void* k, const
                                   void* workspace, size_t workspace_bytes, void* stream) {
     if (int s = check(dtype, batch, seq_len, heads, head_dim)) return s;
     if (!q || !k || !v || !beta || !dO || !gq || !gk || !gv || !gbeta) return EDB_ERR_NULL_POINTER;
-    const size_t need =
-        edb_delta_rule_bwd_workspace(batch, seq_len, heads, head_dim, s_ckpt != nullptr);
+    const size_t need = edb_delta_rule_bwd_workspace(dtype, beta_per_element, batch, seq_len,
+                                                     heads, head_dim, s_ckpt != nullptr);
     if (workspace_bytes < need || (need && !workspace)) return EDB_ERR_WORKSPACE_TOO_SMALL;
     cudaStream_t st = (cudaStream_t)stream;
     const int bs = beta_per_element ? 0 : 1;
@@ -294,11 +323,10 @@ extern "C" int edb_delta_rule_bwd(int dtype, const void* q, const void* k, const
     if (!ck) {
         float* w = static_cast<float*>(workspace);
         // states only: the forward writes o into gq, which the backward overwrites
-        int s = dtype == EDB_BF16
-                    ? launch_fwd<__nv_bfloat16>(q, k, v, beta, gq, w, batch, seq_len, heads,
-                                                head_dim, bs, st)
-                    : launch_fwd<float>(q, k, v, beta, gq, w, batch, seq_len, heads, head_dim,
-                                        bs, st);
+        const size_t ckb = a256(ckpt_bytes(batch, seq_len, heads, head_dim));
+        int s = edb_delta_rule_fwd(dtype, q, k, v, beta, beta_per_element, gq, w, batch, seq_len,
+                                   heads, head_dim, static_cast<char*>(workspace) + ckb,
+                                   workspace_bytes - ckb, stream);
         if (s) return s;
         ck = w;
     }

@@ -211,12 +211,15 @@ def delta_net_scan(q, k, v, beta, with_ckpt=False):
     B, L, H, d, per_el = _delta_shapes(q, k, v, beta)
     o = torch.empty_like(q)
     lib = _lib.load()
+    dt = _dtype_code(q, "delta_net_scan")
     ck = None
     if with_ckpt:
         ck = torch.empty(lib.edb_delta_rule_ckpt_bytes(B, L, H, d) // 4, dtype=torch.float32,
                          device=q.device)
-    _lib.check(lib.edb_delta_rule_fwd(_dtype_code(q, "delta_net_scan"), _p(q), _p(k), _p(v),
-                                      _p(beta), per_el, _p(o), _p(ck), B, L, H, d, _stream()),
+    wsb = lib.edb_delta_rule_fwd_workspace(dt, per_el, B, L, H, d)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=q.device) if wsb else None
+    _lib.check(lib.edb_delta_rule_fwd(dt, _p(q), _p(k), _p(v), _p(beta), per_el, _p(o), _p(ck),
+                                      B, L, H, d, _p(ws), wsb, _stream()),
                "CUDA fused DeltaNet scan")
     return (o, ck) if with_ckpt else o
 
@@ -229,9 +232,10 @@ def delta_rule_backward(q, k, v, beta, grad_output, s_ckpt=None):
     lib = _lib.load()
     gq, gk, gv, gb = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
                       torch.empty_like(beta))
-    wsb = lib.edb_delta_rule_bwd_workspace(B, L, H, d, int(s_ckpt is not None))
+    dt = _dtype_code(q, "delta_rule_backward")
+    wsb = lib.edb_delta_rule_bwd_workspace(dt, per_el, B, L, H, d, int(s_ckpt is not None))
     ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=q.device)
-    _lib.check(lib.edb_delta_rule_bwd(_dtype_code(q, "delta_rule_backward"), _p(q), _p(k), _p(v),
+    _lib.check(lib.edb_delta_rule_bwd(dt, _p(q), _p(k), _p(v),
                                       _p(beta), per_el, _p(grad_output), _p(s_ckpt), _p(gq),
                                       _p(gk), _p(gv), _p(gb), B, L, H, d, _p(ws), wsb, _stream()),
                "CUDA fused DeltaNet scan backward")

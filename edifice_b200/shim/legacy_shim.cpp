@@ -87,7 +87,7 @@ int fused_delta_net_scan_launch(cudaStream_t stream, const edb_io_t* q, const ed
                                 const edb_io_t* v, const edb_io_t* beta, edb_io_t* output,
                                 int batch, int seq_len, int num_heads, int head_dim) {
     return edb_delta_rule_fwd(kDtype, q, k, v, beta, 1, output, nullptr, batch, seq_len,
-                              num_heads, head_dim, stream);
+                              num_heads, head_dim, nullptr, 0, stream);
 }
 
 int fused_delta_rule_scan_backward_launch(cudaStream_t stream, const edb_io_t* q,
@@ -97,7 +97,8 @@ int fused_delta_rule_scan_backward_launch(cudaStream_t stream, const edb_io_t* q
                                           int batch, int seq_len, int num_heads, int head_dim) {
     (void)forward_out;  // the backward recomputes what it needs from q, k, v, beta
     const long long n = (long long)batch * seq_len * num_heads * head_dim;
-    const size_t wsb = edb_delta_rule_bwd_workspace(batch, seq_len, num_heads, head_dim, 0);
+    const size_t wsb =
+        edb_delta_rule_bwd_workspace(kDtype, 1, batch, seq_len, num_heads, head_dim, 0);
     void* ws = nullptr;
     cudaError_t e = cudaMallocAsync(&ws, wsb, stream);
     if (e != cudaSuccess) return (int)e;

@@ -177,21 +177,32 @@ int edb_flash_attention_bwd(int dtype, const void* q, const void* k, const void*
  * caller); beta: [batch, seq_len, heads, head_dim] when beta_per_element
  * (Edifice.build(:delta_net)'s form, lib/edifice/recurrent/delta_net.ex:285-297),
  * else [batch, seq_len, heads] (one gate per token and head).  head_dim <= 128.
- * s_ckpt (optional f32, edb_delta_rule_ckpt_bytes() bytes): the forward also
- * writes S at the start of every 64-token chunk for the backward.
+ * s_ckpt (optional f32, edb_delta_rule_ckpt_bytes() bytes,
+ * [batch][heads][nchunks + 1][head_dim][head_dim]): the forward also writes S
+ * at the start of every 64-token chunk, and the final S, for the backward.
+ * bf16 io with one beta per token and head_dim 128 runs the chunked
+ * tensor-core form (WY representation, tcgen05 TF32 products, f32 state);
+ * every other case runs the token recurrence.
  * Replaces fused_delta_net_scan_launch / fused_delta_rule_scan_launch with
  * alpha = NULL (native/cuda/fused_delta_rule_scan.cu:213-258); Nx semantics
  * lib/edifice/cuda/fused_scan.ex:2212-2236.
  * ---------------------------------------------------------------------- */
 size_t edb_delta_rule_ckpt_bytes(int batch, int seq_len, int heads, int head_dim);
 
+/* Workspace bytes edb_delta_rule_fwd needs (0 when the token recurrence serves
+ * the call). */
+size_t edb_delta_rule_fwd_workspace(int dtype, int beta_per_element, int batch, int seq_len,
+                                    int heads, int head_dim);
+
 int edb_delta_rule_fwd(int dtype, const void* q, const void* k, const void* v, const void* beta,
                        int beta_per_element, void* o, float* s_ckpt, int batch, int seq_len,
-                       int heads, int head_dim, void* stream);
+                       int heads, int head_dim, void* workspace, size_t workspace_bytes,
+                       void* stream);
 
-/* Workspace bytes edb_delta_rule_bwd needs (0 when the forward's s_ckpt is passed). */
-size_t edb_delta_rule_bwd_workspace(int batch, int seq_len, int heads, int head_dim,
-                                    int have_ckpt);
+/* Workspace bytes edb_delta_rule_bwd needs; have_ckpt: the forward's s_ckpt
+ * will be passed. */
+size_t edb_delta_rule_bwd_workspace(int dtype, int beta_per_element, int batch, int seq_len,
+                                    int heads, int head_dim, int have_ckpt);
 
 /* Backward given dO: gq, gk, gv (shape of q) and gbeta (shape of beta), in
  * `dtype`.  The key gradient is the exact one (S_{t-1}^T (beta (.) dS k) for the

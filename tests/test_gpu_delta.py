@@ -65,6 +65,38 @@ def test_delta_rule_parity(cuda, dtype, case, scalar_beta, use_ckpt):
     assert device_errors() == 0
 
 
+CHUNKED_CASES = [
+    (1, 1, 1, 128),     # one token
+    (1, 64, 1, 128),    # exactly one chunk
+    (2, 200, 3, 128),   # ragged last chunk
+    (1, 1000, 2, 128),  # many chunks
+]
+
+
+@pytest.mark.parametrize("case", CHUNKED_CASES)
+def test_delta_chunked_forward(cuda, case):
+    """bf16 io, one beta per token, head_dim 128: the chunked tensor-core
+    forward.  Output against the oracle; the chunk-start states against the
+    token recurrence's (the f32 path run on the same bf16-rounded inputs),
+    which share one layout [B][H][nchunks + 1][d][d]."""
+    q, k, v, beta, do = delta_inputs(*case, torch.bfloat16, seed=54, scalar_beta=True)
+    o, ck = fs.delta_net_scan(q, k, v, beta, with_ckpt=True)
+    of, ckf = fs.delta_net_scan(q.float(), k.float(), v.float(), beta.float(), with_ckpt=True)
+    torch.cuda.synchronize()
+    assert device_errors() == 0
+    args = [_np(t) for t in (q, k, v, beta)]
+    ref = O.delta_net_fwd(*args)
+    assert O.norm_rel(_np(o), ref) <= 2e-2
+    assert O.norm_rel(_np(of), ref) <= 1e-4
+    assert ck.shape == ckf.shape
+    assert O.norm_rel(_np(ck), _np(ckf)) <= 5e-3
+    # the backward consumes the chunked checkpoints
+    grads = fs.delta_rule_backward(q, k, v, beta, do, ck)
+    torch.cuda.synchronize()
+    for got, r in zip(grads, O.delta_net_bwd(*args, _np(do))):
+        assert O.norm_rel(_np(got), r) <= 2e-2
+
+
 @pytest.mark.parametrize("layer", [0, 1])
 def test_delta_golden(cuda, layer):
     g = np.load(os.path.join(GOLD, "delta_net_fixture.npz"))
