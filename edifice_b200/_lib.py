@@ -34,7 +34,7 @@ SIGNATURES = {
                                             _vp, _vp, _i, _i, _i, _i, _f, _f, _vp]),
     "edb_flash_attention_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f,
                                      _vp]),
-    "edb_delta_rule_ckpt_bytes": (_sz, [_i, _i, _i, _i]),
+    "edb_delta_rule_ckpt_bytes": (_sz, [_i, _i, _i, _i, _i, _i]),
     "edb_delta_rule_fwd_workspace": (_sz, [_i, _i, _i, _i, _i, _i]),
     "edb_delta_rule_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _vp, _sz,
                                 _vp]),

@@ -16,7 +16,7 @@
 // o_t = S_t q_t, regrouped (T solves the within-chunk dependence of the errors).
 //
 // Kernels:
-//   delta_prep_kernel       one CTA per chunk (all chunks at once), SIMT f32:
+//   delta_prep_fwd_kernel   one CTA per chunk (all chunks at once), SIMT f32:
 //                           K K^T, Q K^T, the unit-triangular solve for T, W and
 //                           U0; writes -W, Q, K^T, U0^T and M (f32) to scratch.
 //   delta_state_fwd_kernel  one CTA per (b, h), chunks in order, tcgen05
@@ -28,20 +28,19 @@
 //                             S   += D_U (K^T)^T            M=128, N=128, K=64
 //                           -W, Q, K^T, M arrive by TMA (SWIZZLE_128B f32 boxes)
 //                           in a 2-stage ring; U0^T rows are stored into TMEM
-//                           by the threads.  TF32 operands (10-bit mantissa),
-//                           f32 accumulation: ~1e-3 relative per product.
+//                           by the threads.  With a residual buffer it also
+//                           stores S^T at every chunk start (and the final S^T)
+//                           and each chunk's U~ for the backward.  TF32
+//                           operands (10-bit mantissa), f32 accumulation.
 #include <math.h>
 
-#include "tc_common.cuh"
+#include "delta_chunked.cuh"
+
+using namespace dchunk;
 
 namespace {
 
-constexpr int C = 64;    // chunk length
-constexpr int D = 128;   // head dim (d_k = d_v)
-constexpr int kPrepThreads = 256;
 constexpr int kStateThreads = 128;
-
-size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 // ------------------------------------------------------------------ scratch
 struct FwdScratch {
@@ -71,107 +70,47 @@ FwdScratch carve_fwd(void* ws, long long nch) {
 // ------------------------------------------------------------------ prep
 // grid (NC, H, B), 256 threads.  Rows past L load as zero with beta 0, which
 // makes their W / U0 rows zero, so the padded tail leaves S untouched.
-constexpr int PP = D + 1;      // padded [C][D] row (odd: conflict-free columns)
-constexpr int PC = C + 1;      // padded [C][C] row
-constexpr size_t kPrepSmem = (size_t)(3 * C * PP + 2 * C * PC + C) * sizeof(float);
+constexpr size_t kPrepSmem = (size_t)(3 * C * PP + 3 * C * PC + C) * sizeof(float);
 
 __global__ void __launch_bounds__(kPrepThreads, 1)
-    delta_prep_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
-                      const __nv_bfloat16* __restrict__ v, const __nv_bfloat16* __restrict__ beta,
-                      FwdScratch ws, int L, int H, int NC) {
+    delta_prep_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                          const __nv_bfloat16* __restrict__ v,
+                          const __nv_bfloat16* __restrict__ beta, FwdScratch ws, int L, int H,
+                          int NC) {
     extern __shared__ float sm[];
     float* Ks = sm;              // [C][PP]
     float* Qs = Ks + C * PP;     // [C][PP]  (then -W)
     float* Vs = Qs + C * PP;     // [C][PP]  (then U0)
-    float* G = Vs + C * PP;      // [C][PC]  A = tril(diag(beta) K K^T, -1)
-    float* Tm = G + C * PC;      // [C][PC]  T
+    float* Gs = Vs + C * PP;     // [C][PC]  K K^T
+    float* Ms = Gs + C * PC;     // [C][PC]  tril(Q K^T)
+    float* Tm = Ms + C * PC;     // [C][PC]  T
     float* bs = Tm + C * PC;     // [C]
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x;
     const long long ch = ((long long)b * H + h) * NC + c;
-    const int t0 = c * C;
+    const int t0 = c * C, nvalid = min(C, L - t0);
+    const long long row0 = (((long long)b * L + t0) * H + h) * D, ts = (long long)H * D;
 
-    for (int idx = tid; idx < C * (D / 8); idx += kPrepThreads) {
-        const int t = idx / (D / 8), j8 = (idx % (D / 8)) * 8;
-        float kf[8], qf[8], vf[8];
-        if (t0 + t < L) {
-            const long long off = (((long long)b * L + t0 + t) * H + h) * D + j8;
-            Vec16<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(k + off), kf);
-            Vec16<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(q + off), qf);
-            Vec16<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(v + off), vf);
-        } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) kf[e] = qf[e] = vf[e] = 0.0f;
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            Ks[t * PP + j8 + e] = kf[e];
-            Qs[t * PP + j8 + e] = qf[e];
-            Vs[t * PP + j8 + e] = vf[e];
-        }
-        float* qg = ws.Q + (ch * C + t) * D + j8;
-        *reinterpret_cast<float4*>(qg) = make_float4(qf[0], qf[1], qf[2], qf[3]);
-        *reinterpret_cast<float4*>(qg + 4) = make_float4(qf[4], qf[5], qf[6], qf[7]);
-    }
+    load_chunk_rows(Ks, k, row0, ts, nvalid, nullptr);
+    load_chunk_rows(Qs, q, row0, ts, nvalid, ws.Q + ch * C * D);
+    load_chunk_rows(Vs, v, row0, ts, nvalid, nullptr);
     if (tid < C)
-        bs[tid] = t0 + tid < L ? __bfloat162float(beta[((long long)b * L + t0 + tid) * H + h])
+        bs[tid] = tid < nvalid ? __bfloat162float(beta[((long long)b * L + t0 + tid) * H + h])
                                : 0.0f;
     __syncthreads();
-
-    // K^T: [D][C], coalesced over t
-    for (int idx = tid; idx < D * C; idx += kPrepThreads)
+    for (int idx = tid; idx < D * C; idx += kPrepThreads)  // K^T, coalesced over t
         ws.KT[ch * D * C + idx] = Ks[(idx % C) * PP + idx / C];
-
-    // A and M: thread -> row t = tid / 4, columns s = (tid % 4) + 4 e
-    {
-        const int t = tid >> 2, sl = tid & 3;
-        float g[16], m[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) g[e] = m[e] = 0.0f;
-        for (int j = 0; j < D; ++j) {
-            const float kt = Ks[t * PP + j], qt = Qs[t * PP + j];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                const float ks = Ks[(sl + 4 * e) * PP + j];
-                g[e] = fmaf(kt, ks, g[e]);
-                m[e] = fmaf(qt, ks, m[e]);
-            }
-        }
-        float* mg = ws.M + (ch * C + t) * C;
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-            const int s = sl + 4 * e;
-            G[t * PC + s] = s < t ? bs[t] * g[e] : 0.0f;
-            mg[s] = s <= t ? m[e] : 0.0f;
-        }
-    }
+    prep_products(Ks, Qs, Gs, Ms);
     __syncthreads();
-
-    // T = (I + A)^-1, forward substitution, one column per thread
-    if (tid < C) {
-        const int j = tid;
-        for (int t = 0; t < C; ++t) {
-            float acc = (t == j) ? 1.0f : 0.0f;
-            for (int s = j; s < t; ++s) acc = fmaf(-G[t * PC + s], Tm[s * PC + j], acc);
-            Tm[t * PC + j] = t >= j ? acc : 0.0f;
-        }
-    }
+    for (int idx = tid; idx < C * C; idx += kPrepThreads)
+        ws.M[ch * C * C + idx] = Ms[(idx / C) * PC + idx % C];
+    prep_solve(Gs, bs, Tm);
     __syncthreads();
-
-    // W = T_b K, U0 = T_b V: thread -> row t, columns (tid % 4) + 4 e
     {
         const int t = tid >> 2, jl = tid & 3;
         float w[32], u[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) w[e] = u[e] = 0.0f;
-        for (int s = 0; s <= t; ++s) {
-            const float tb = Tm[t * PC + s] * bs[s];
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                w[e] = fmaf(tb, Ks[s * PP + jl + 4 * e], w[e]);
-                u[e] = fmaf(tb, Vs[s * PP + jl + 4 * e], u[e]);
-            }
-        }
+        prep_apply_tb(Tm, bs, Ks, w);
+        prep_apply_tb(Tm, bs, Vs, u);
         __syncthreads();  // every read of Q and V is done: reuse their rows
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
@@ -191,58 +130,18 @@ struct StateMaps {
     CUtensorMap Wn, Q, KT, M;
 };
 
-constexpr int BOX_CD = C * 128;   // 8 KB: [C rows][32 f32] box
-constexpr int BOX_DC = D * 128;   // 16 KB: [D rows][32 f32] box
 constexpr int OFF_W = 0;
-constexpr int OFF_Q = OFF_W + 4 * BOX_CD;
-constexpr int OFF_KT = OFF_Q + 4 * BOX_CD;
-constexpr int OFF_M = OFF_KT + 2 * BOX_DC;
-constexpr int STAGE_BYTES = OFF_M + 2 * BOX_CD;  // 112 KB
+constexpr int OFF_Q = OFF_W + 4 * BOX_C;
+constexpr int OFF_KT = OFF_Q + 4 * BOX_C;
+constexpr int OFF_M = OFF_KT + 2 * BOX_D;
+constexpr int STAGE_BYTES = OFF_M + 2 * BOX_C;  // 112 KB
 constexpr int OFF_BARS = 2 * STAGE_BYTES;
 constexpr int STATE_SMEM = OFF_BARS + 64;
 constexpr int TM_S = 0, TM_U = 128, TM_O = 192, TM_COLS = 256;
 
-static __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
-    return (1u << 4)                      // D format f32
-           | (2u << 7) | (2u << 10)       // A, B tf32 (both K-major)
-           | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-// D[tmem] (+)= A[tmem] * B[smem desc], kind::tf32, A K-major in TMEM.
-static __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem,
-                                                   uint64_t b_desc, uint32_t idesc,
-                                                   uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-// K-major SW128 f32 operand: 8-element K step kk inside boxes of 32 columns.
-static __device__ __forceinline__ uint64_t kdesc(const uint8_t* base, int box_bytes, int kk) {
-    return tc::sdesc_sw128(base + (kk >> 2) * box_bytes + (kk & 3) * 32, 16, 1024);
-}
-
-// Thread i: row i of the [D][D] TMEM state -> global row (512 B).
-static __device__ __forceinline__ void store_state_row(float* dst, uint32_t taddr) {
-#pragma unroll
-    for (int cc = 0; cc < D / 32; ++cc) {
-        uint32_t x[32];
-        tc::tmem_ld32(taddr + cc * 32, x);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; e += 4)
-            *reinterpret_cast<float4*>(dst + cc * 32 + e) =
-                make_float4(__uint_as_float(x[e]), __uint_as_float(x[e + 1]),
-                            __uint_as_float(x[e + 2]), __uint_as_float(x[e + 3]));
-    }
-}
-
 __global__ void __launch_bounds__(kStateThreads, 1)
     delta_state_fwd_kernel(const __grid_constant__ StateMaps maps, const float* __restrict__ U0T,
-                           float* __restrict__ ckpt, __nv_bfloat16* __restrict__ o, int L, int H,
+                           float* __restrict__ resid, __nv_bfloat16* __restrict__ o, int L, int H,
                            int NC, unsigned* err) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BARS);  // [2]
@@ -252,6 +151,12 @@ __global__ void __launch_bounds__(kStateThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5;
     const long long bh = (long long)b * H + h;
     const long long ch0 = bh * NC;
+    // residuals: S^T per chunk start [units][NC+1][D][D], then U~ [units][NC][C][D]
+    float* st_T = resid != nullptr ? resid + bh * (NC + 1) * D * D : nullptr;
+    float* ures = resid != nullptr
+                      ? resid + ckpt_state_floats(gridDim.x * (long long)gridDim.y, NC) +
+                            ch0 * C * D
+                      : nullptr;
 
     if ((smem_u32(smem) & 1023u) != 0) {  // SW128 boxes need 1 KB alignment
         if (tid == 0) edb_flag_error(err, EDB_DEVERR_DELTA_PIPE);
@@ -281,12 +186,12 @@ __global__ void __launch_bounds__(kStateThreads, 1)
         const int rc = (int)((ch0 + c) * C), rd = (int)((ch0 + c) * D);
         mbar_arrive_expect_tx(bar, STAGE_BYTES);
         for (int bx = 0; bx < 4; ++bx) {
-            tma_load_2d(st + OFF_W + bx * BOX_CD, &maps.Wn, bar, bx * 32, rc);
-            tma_load_2d(st + OFF_Q + bx * BOX_CD, &maps.Q, bar, bx * 32, rc);
+            tma_load_2d(st + OFF_W + bx * BOX_C, &maps.Wn, bar, bx * 32, rc);
+            tma_load_2d(st + OFF_Q + bx * BOX_C, &maps.Q, bar, bx * 32, rc);
         }
         for (int bx = 0; bx < 2; ++bx) {
-            tma_load_2d(st + OFF_KT + bx * BOX_DC, &maps.KT, bar, bx * 32, rd);
-            tma_load_2d(st + OFF_M + bx * BOX_CD, &maps.M, bar, bx * 32, rc);
+            tma_load_2d(st + OFF_KT + bx * BOX_D, &maps.KT, bar, bx * 32, rd);
+            tma_load_2d(st + OFF_M + bx * BOX_C, &maps.M, bar, bx * 32, rc);
         }
     };
     int issued = 0, landed = 0;
@@ -316,7 +221,7 @@ __global__ void __launch_bounds__(kStateThreads, 1)
     bool mma_pending = false;
 
     for (int c = 0; c < NC; ++c) {
-        // U0^T row i -> D_U; S row i -> checkpoint c
+        // U0^T row i -> D_U; S row i -> S^T column i of residual c
         {
             const float* u = U0T + ((ch0 + c) * D + i) * C;
 #pragma unroll
@@ -332,9 +237,8 @@ __global__ void __launch_bounds__(kStateThreads, 1)
                 }
                 tc::tmem_st32(tmem + TM_U + lane_base + half * 32, r);
             }
-            if (ckpt != nullptr)
-                store_state_row(ckpt + ((bh * (NC + 1) + c) * D + i) * D,
-                                tmem + TM_S + lane_base);
+            if (st_T != nullptr)
+                store_rows_transposed<D>(st_T + (long long)c * D * D + i, tmem + TM_S + lane_base);
             tc::tmem_wait_st();
         }
         tc::fence_before_sync();
@@ -348,9 +252,9 @@ __global__ void __launch_bounds__(kStateThreads, 1)
                 tc::fence_after_sync();
 #pragma unroll
                 for (int kk = 0; kk < D / 8; ++kk) {
-                    mma_tf32_ts(tmem + TM_U, tmem + TM_S + kk * 8, kdesc(st + OFF_W, BOX_CD, kk),
+                    mma_tf32_ts(tmem + TM_U, tmem + TM_S + kk * 8, kdesc(st + OFF_W, BOX_C, kk),
                                 idN64, 1);
-                    mma_tf32_ts(tmem + TM_O, tmem + TM_S + kk * 8, kdesc(st + OFF_Q, BOX_CD, kk),
+                    mma_tf32_ts(tmem + TM_O, tmem + TM_S + kk * 8, kdesc(st + OFF_Q, BOX_C, kk),
                                 idN64, kk > 0);
                 }
                 tc::commit(mbar);
@@ -365,10 +269,10 @@ __global__ void __launch_bounds__(kStateThreads, 1)
                 tc::fence_after_sync();
 #pragma unroll
                 for (int kk = 0; kk < C / 8; ++kk) {
-                    mma_tf32_ts(tmem + TM_O, tmem + TM_U + kk * 8, kdesc(st + OFF_M, BOX_CD, kk),
+                    mma_tf32_ts(tmem + TM_O, tmem + TM_U + kk * 8, kdesc(st + OFF_M, BOX_C, kk),
                                 idN64, 1);
-                    mma_tf32_ts(tmem + TM_S, tmem + TM_U + kk * 8,
-                                kdesc(st + OFF_KT, BOX_DC, kk), idN128, 1);
+                    mma_tf32_ts(tmem + TM_S, tmem + TM_U + kk * 8, kdesc(st + OFF_KT, BOX_D, kk),
+                                idN128, 1);
                 }
                 tc::commit(mbar);
                 mma_pending = true;
@@ -404,6 +308,9 @@ __global__ void __launch_bounds__(kStateThreads, 1)
             for (int t = 0; t < 32; ++t)
                 if (t + 32 < nt) op[(t + 32) * ts] = __float2bfloat16(__uint_as_float(x1[t]));
         }
+        // U~^T row i -> U~[c][t][i]
+        if (ures != nullptr) store_rows_transposed<C>(ures + (long long)c * C * D + i,
+                                                      tmem + TM_U + lane_base);
         tc::fence_before_sync();
         __syncthreads();
         tc::fence_after_sync();
@@ -416,8 +323,8 @@ __global__ void __launch_bounds__(kStateThreads, 1)
                 mbar_wait_bounded(&full[cc & 1], (cc >> 1) & 1, err, EDB_DEVERR_DELTA_PIPE);
             if (mma_pending) mbar_wait_bounded(mbar, mph, err, EDB_DEVERR_DELTA_PIPE);
         }
-    } else if (ckpt != nullptr) {
-        store_state_row(ckpt + ((bh * (NC + 1) + NC) * D + i) * D, tmem + TM_S + lane_base);
+    } else if (st_T != nullptr) {
+        store_rows_transposed<D>(st_T + (long long)NC * D * D + i, tmem + TM_S + lane_base);
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -425,16 +332,6 @@ __global__ void __launch_bounds__(kStateThreads, 1)
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, TM_COLS);
     }
-}
-
-// 2D f32 map over a [rows][cols] array, boxes of 32 columns x box_rows rows.
-int make_box_map(CUtensorMap* m, const float* p, long long rows, int cols, int box_rows) {
-    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
-    const cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
-    CUresult r = edb::encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p),
-                                   dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-    return r == CUDA_SUCCESS ? EDB_OK : EDB_ERR_UNSUPPORTED;
 }
 
 }  // namespace
@@ -445,20 +342,24 @@ bool edb_delta_chunked_ok(int dtype, int beta_per_element, int head_dim) {
     return dtype == EDB_BF16 && !beta_per_element && head_dim == D;
 }
 
+size_t edb_delta_chunked_ckpt_bytes(int B, int L, int H) {
+    return ckpt_bytes((long long)B * H, (L + C - 1) / C);
+}
+
 size_t edb_delta_chunked_fwd_ws(int B, int L, int H) {
     return fwd_scratch_bytes((long long)B * H * ((L + C - 1) / C));
 }
 
 int edb_delta_chunked_fwd(const void* q, const void* k, const void* v, const void* beta, void* o,
-                          float* s_ckpt, int B, int L, int H, void* ws, cudaStream_t st) {
+                          float* resid, int B, int L, int H, void* ws, cudaStream_t st) {
     const int NC = (L + C - 1) / C;
     const long long nch = (long long)B * H * NC;
     if (nch * D > 0x7fffffffLL) return EDB_ERR_UNSUPPORTED;  // TMA row coordinate is int32
     FwdScratch w = carve_fwd(ws, nch);
-    cudaError_t e = cudaFuncSetAttribute(delta_prep_kernel,
+    cudaError_t e = cudaFuncSetAttribute(delta_prep_fwd_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPrepSmem);
     if (e != cudaSuccess) return (int)e;
-    delta_prep_kernel<<<dim3(NC, H, B), kPrepThreads, kPrepSmem, st>>>(
+    delta_prep_fwd_kernel<<<dim3(NC, H, B), kPrepThreads, kPrepSmem, st>>>(
         (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
         (const __nv_bfloat16*)beta, w, L, H, NC);
     if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
@@ -472,6 +373,6 @@ int edb_delta_chunked_fwd(const void* q, const void* k, const void* v, const voi
                              STATE_SMEM);
     if (e != cudaSuccess) return (int)e;
     delta_state_fwd_kernel<<<dim3(H, B), kStateThreads, STATE_SMEM, st>>>(
-        maps, w.U0T, s_ckpt, (__nv_bfloat16*)o, L, H, NC, edb::device_error_word());
+        maps, w.U0T, resid, (__nv_bfloat16*)o, L, H, NC, edb::device_error_word());
     return edb::status_from_cuda(cudaGetLastError());
 }

@@ -1,0 +1,789 @@
+// delta_chunked_bwd.cu -- DeltaNet delta rule in chunked WY form on tcgen05 (backward).
+//
+// Gradient of the forward in delta_chunked.cu (same notation: per chunk
+// A, T, T_b, W, U0, M, U~, S_0 -> S_C), given dO and the forward's residuals
+// (S^T at every chunk start, U~ per chunk).  Reverse-mode through
+//   O = Q S_0^T + M U~,  S_C = S_0 + U~^T K,  U~ = U0 - W S_0^T,
+//   W = T_b K,  U0 = T_b V,  T_b = T diag(beta),  T = (I + A)^-1,
+//   A = tril(diag(beta) K K^T, -1),  M = tril(Q K^T):
+//   dU~  = M^T dO + K dS_C^T
+//   dS_0 = dS_C + dO^T Q - dU~^T W                       (carried backwards)
+//   dW   = -dU~ S_0,     dM = tril(dO U~^T),     dV = T_b^T dU~
+//   dT_b = dW K^T + dU~ V^T,   dT = dT_b diag(beta),   dA = -T^T dT T^T (strictly lower)
+//   dQ   = dO S_0 + dM K
+//   dK   = U~ dS_C + dM^T Q + T_b^T dW + (dG + dG^T) K,   dG = diag(beta) dA
+//   dbeta_s = sum_t dT_b[t][s] T[t][s] + sum_{r<s} dA[s][r] (K K^T)[s][r]
+// The key gradient is the exact one, as in delta_rule.cu.
+//
+// Kernels (one stream, in order):
+//   delta_prep_bwd_kernel   per chunk, SIMT: K K^T, M, T, W; writes the
+//                           K-major f32 operands of the state kernel and T, K K^T.
+//   delta_state_bwd_kernel  per (b, h), chunks in reverse, tcgen05 kind::tf32,
+//                           dS in TMEM (lanes = value dim):
+//                             D_U = dS K^T + dO^T M        (= dU~^T)   N=64
+//                             dS += dO^T Q + D_U (-W)                  N=128
+//                           stores dS_C^T and dU~ per chunk.
+//   delta_post1_kernel      per chunk, tcgen05: the products with S_0 / dS_C,
+//                           (dO S_0)^T, (dU~ S_0)^T, (U~ dS_C)^T (M=128, N=64,
+//                           K=128) and dO U~^T (M=64); operands by TMA.
+//   delta_post2_kernel      per chunk, SIMT f32: the C x C chain (dT_b, dA,
+//                           dbeta) and the final dQ, dK, dV (bf16).
+#include <math.h>
+
+#include "delta_chunked.cuh"
+
+using namespace dchunk;
+
+namespace {
+
+// ------------------------------------------------------------------ scratch
+struct BwdScratch {
+    float* Kf;    // [nch][C][D]  K (f32)          post1 output: dQa = dO S_0
+    float* dOT;   // [nch][D][C]  dO^T             post1 output: dW = -dU~ S_0
+    float* QT;    // [nch][D][C]  Q^T              post1 output: dK1 = U~ dS_C
+    float* WnT;   // [nch][D][C]  -W^T
+    float* MT;    // [nch][C][C]  M^T              post1 output: dM = tril(dO U~^T)
+    float* T;     // [nch][C][C]  T (unscaled)
+    float* G;     // [nch][C][C]  K K^T
+    float* dSCT;  // [nch][D][D]  dS_C^T
+    float* dU;    // [nch][C][D]  dU~
+};
+
+size_t bwd_scratch_bytes(long long nch) {
+    return 5 * a256((size_t)nch * C * D * 4) + 3 * a256((size_t)nch * C * C * 4) +
+           a256((size_t)nch * D * D * 4);
+}
+
+BwdScratch carve_bwd(void* ws, long long nch) {
+    char* p = static_cast<char*>(ws);
+    const size_t cd = a256((size_t)nch * C * D * 4), cc = a256((size_t)nch * C * C * 4);
+    BwdScratch s;
+    s.Kf = reinterpret_cast<float*>(p); p += cd;
+    s.dOT = reinterpret_cast<float*>(p); p += cd;
+    s.QT = reinterpret_cast<float*>(p); p += cd;
+    s.WnT = reinterpret_cast<float*>(p); p += cd;
+    s.dU = reinterpret_cast<float*>(p); p += cd;
+    s.MT = reinterpret_cast<float*>(p); p += cc;
+    s.T = reinterpret_cast<float*>(p); p += cc;
+    s.G = reinterpret_cast<float*>(p); p += cc;
+    s.dSCT = reinterpret_cast<float*>(p);
+    return s;
+}
+
+// ------------------------------------------------------------------ prep
+constexpr size_t kPrepSmem = (size_t)(3 * C * PP + 3 * C * PC + C) * sizeof(float);
+
+__global__ void __launch_bounds__(kPrepThreads, 1)
+    delta_prep_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                          const __nv_bfloat16* __restrict__ beta,
+                          const __nv_bfloat16* __restrict__ dO, BwdScratch ws, int L, int H,
+                          int NC) {
+    extern __shared__ float sm[];
+    float* Ks = sm;              // [C][PP]
+    float* Qs = Ks + C * PP;     // [C][PP]  (then -W)
+    float* dOs = Qs + C * PP;    // [C][PP]
+    float* Gs = dOs + C * PP;    // [C][PC]  K K^T
+    float* Ms = Gs + C * PC;     // [C][PC]  tril(Q K^T)
+    float* Tm = Ms + C * PC;     // [C][PC]  T
+    float* bs = Tm + C * PC;     // [C]
+    const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x;
+    const long long ch = ((long long)b * H + h) * NC + c;
+    const int t0 = c * C, nvalid = min(C, L - t0);
+    const long long row0 = (((long long)b * L + t0) * H + h) * D, ts = (long long)H * D;
+
+    load_chunk_rows(Ks, k, row0, ts, nvalid, ws.Kf + ch * C * D);
+    load_chunk_rows(Qs, q, row0, ts, nvalid, nullptr);
+    load_chunk_rows(dOs, dO, row0, ts, nvalid, nullptr);
+    if (tid < C)
+        bs[tid] = tid < nvalid ? __bfloat162float(beta[((long long)b * L + t0 + tid) * H + h])
+                               : 0.0f;
+    __syncthreads();
+    for (int idx = tid; idx < D * C; idx += kPrepThreads) {  // transposes, coalesced over t
+        const int j = idx / C, t = idx % C;
+        ws.dOT[ch * D * C + idx] = dOs[t * PP + j];
+        ws.QT[ch * D * C + idx] = Qs[t * PP + j];
+    }
+    prep_products(Ks, Qs, Gs, Ms);
+    __syncthreads();
+    for (int idx = tid; idx < C * C; idx += kPrepThreads) {
+        ws.G[ch * C * C + idx] = Gs[idx / C * PC + idx % C];
+        ws.MT[ch * C * C + idx] = Ms[(idx % C) * PC + idx / C];  // MT[s][t] = M[t][s]
+    }
+    prep_solve(Gs, bs, Tm);
+    __syncthreads();
+    for (int idx = tid; idx < C * C; idx += kPrepThreads)
+        ws.T[ch * C * C + idx] = Tm[idx / C * PC + idx % C];
+    {
+        const int t = tid >> 2, jl = tid & 3;
+        float w[32];
+        prep_apply_tb(Tm, bs, Ks, w);
+        // Q rows were last read by the transposes and products (both before a barrier)
+#pragma unroll
+        for (int e = 0; e < 32; ++e) Qs[t * PP + jl + 4 * e] = -w[e];
+    }
+    __syncthreads();
+    for (int idx = tid; idx < D * C; idx += kPrepThreads)  // -W^T: [j][t]
+        ws.WnT[ch * D * C + idx] = Qs[(idx % C) * PP + idx / C];
+}
+
+// ------------------------------------------------------------------ state bwd
+struct StateBwdMaps {
+    CUtensorMap Kf, dOT, MT, QT, WnT;
+};
+
+constexpr int kStateThreads = 128;
+// X stage (double-buffered): K [C][D] | dO^T [D][C] | M^T [C][C]
+constexpr int XO_K = 0, XO_O = 4 * BOX_C, XO_M = XO_O + 2 * BOX_D;
+constexpr int X_BYTES = XO_M + 2 * BOX_C;  // 80 KB
+// Y stage (single): Q^T [D][C] | -W^T [D][C]
+constexpr int YO_Q = 0, YO_W = 2 * BOX_D;
+constexpr int Y_BYTES = YO_W + 2 * BOX_D;  // 64 KB
+constexpr int SB_OFF_Y = 2 * X_BYTES;
+constexpr int SB_OFF_BARS = SB_OFF_Y + Y_BYTES;
+constexpr int SB_SMEM = SB_OFF_BARS + 64;
+constexpr int SB_TM_S = 0, SB_TM_U = 128, SB_TM_COLS = 256;
+
+__global__ void __launch_bounds__(kStateThreads, 1)
+    delta_state_bwd_kernel(const __grid_constant__ StateBwdMaps maps, float* __restrict__ dSCT,
+                           float* __restrict__ dU, int H, int NC, unsigned* err) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t* fullX = reinterpret_cast<uint64_t*>(smem + SB_OFF_BARS);  // [2]
+    uint64_t* fullY = fullX + 2;
+    uint64_t* mbar = fullY + 1;
+    uint32_t* s_misc = reinterpret_cast<uint32_t*>(mbar + 1);  // [0] tmem base, [1] abort
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const long long ch0 = ((long long)b * H + h) * NC;
+
+    if ((smem_u32(smem) & 1023u) != 0) {
+        if (tid == 0) edb_flag_error(err, EDB_DEVERR_DELTA_PIPE);
+        return;
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(s_misc, SB_TM_COLS);
+        tc::tmem_relinquish();
+    }
+    if (tid == 0) {
+        s_misc[1] = 0;
+        mbar_init(&fullX[0], 1);
+        mbar_init(&fullX[1], 1);
+        mbar_init(fullY, 1);
+        mbar_init(mbar, 1);
+        fence_mbar_init();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = s_misc[0];
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const int i = tid;
+
+    // copies issued / waited per barrier (thread 0 only)
+    int x_issued[2] = {0, 0}, x_landed[2] = {0, 0}, y_issued = 0, y_landed = 0;
+    auto issue_x = [&](int c, int n) {
+        uint8_t* st = smem + (n & 1) * X_BYTES;
+        uint64_t* bar = &fullX[n & 1];
+        const int rc = (int)((ch0 + c) * C), rd = (int)((ch0 + c) * D);
+        mbar_arrive_expect_tx(bar, X_BYTES);
+        for (int bx = 0; bx < 4; ++bx) tma_load_2d(st + XO_K + bx * BOX_C, &maps.Kf, bar, bx * 32, rc);
+        for (int bx = 0; bx < 2; ++bx) {
+            tma_load_2d(st + XO_O + bx * BOX_D, &maps.dOT, bar, bx * 32, rd);
+            tma_load_2d(st + XO_M + bx * BOX_C, &maps.MT, bar, bx * 32, rc);
+        }
+        ++x_issued[n & 1];
+    };
+    auto issue_y = [&](int c) {
+        uint8_t* st = smem + SB_OFF_Y;
+        const int rd = (int)((ch0 + c) * D);
+        mbar_arrive_expect_tx(fullY, Y_BYTES);
+        for (int bx = 0; bx < 2; ++bx) {
+            tma_load_2d(st + YO_Q + bx * BOX_D, &maps.QT, fullY, bx * 32, rd);
+            tma_load_2d(st + YO_W + bx * BOX_D, &maps.WnT, fullY, bx * 32, rd);
+        }
+        ++y_issued;
+    };
+    if (tid == 0) {
+        prefetch_tmap(&maps.Kf);
+        prefetch_tmap(&maps.dOT);
+        prefetch_tmap(&maps.MT);
+        prefetch_tmap(&maps.QT);
+        prefetch_tmap(&maps.WnT);
+        issue_x(NC - 1, 0);
+        issue_y(NC - 1);
+        if (NC > 1) issue_x(NC - 2, 1);
+    }
+    {  // dS = 0: no gradient reaches the final state
+        uint32_t z[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) z[e] = 0u;
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) tc::tmem_st32(tmem + SB_TM_S + lane_base + cc * 32, z);
+        tc::tmem_wait_st();
+    }
+    constexpr uint32_t idN64 = idesc_tf32(128, C);
+    constexpr uint32_t idN128 = idesc_tf32(128, D);
+    uint32_t mph = 0;
+    bool mma_pending = false;
+
+    for (int n = 0; n < NC; ++n) {
+        const int c = NC - 1 - n;
+        // dS (= dS_C of chunk c) row i -> dS_C^T column i
+        store_rows_transposed<D>(dSCT + (ch0 + c) * D * D + i, tmem + SB_TM_S + lane_base);
+        tc::fence_before_sync();
+        __syncthreads();
+        tc::fence_after_sync();
+        if (tid == 0) {
+            const uint8_t* xs = smem + (n & 1) * X_BYTES;
+            const uint8_t* ys = smem + SB_OFF_Y;
+            bool ok = mbar_wait_bounded(&fullX[n & 1], x_landed[n & 1] & 1, err,
+                                        EDB_DEVERR_DELTA_PIPE);
+            if (ok) {
+                ++x_landed[n & 1];
+                tc::fence_after_sync();
+#pragma unroll
+                for (int kk = 0; kk < D / 8; ++kk)
+                    mma_tf32_ts(tmem + SB_TM_U, tmem + SB_TM_S + kk * 8,
+                                kdesc(xs + XO_K, BOX_C, kk), idN64, kk > 0);
+#pragma unroll
+                for (int kk = 0; kk < C / 8; ++kk)
+                    mma_tf32_ss(tmem + SB_TM_U, kdesc(xs + XO_O, BOX_D, kk),
+                                kdesc(xs + XO_M, BOX_C, kk), idN64, 1);
+                tc::commit(mbar);
+                mma_pending = true;
+                ok = mbar_wait_bounded(mbar, mph, err, EDB_DEVERR_DELTA_PIPE);
+                if (ok) {
+                    mph ^= 1u;
+                    mma_pending = false;
+                }
+            }
+            if (ok) {
+                ok = mbar_wait_bounded(fullY, y_landed & 1, err, EDB_DEVERR_DELTA_PIPE);
+                if (ok) ++y_landed;
+            }
+            if (ok) {
+                tc::fence_after_sync();
+#pragma unroll
+                for (int kk = 0; kk < C / 8; ++kk) {
+                    mma_tf32_ss(tmem + SB_TM_S, kdesc(xs + XO_O, BOX_D, kk),
+                                kdesc(ys + YO_Q, BOX_D, kk), idN128, 1);
+                    mma_tf32_ts(tmem + SB_TM_S, tmem + SB_TM_U + kk * 8,
+                                kdesc(ys + YO_W, BOX_D, kk), idN128, 1);
+                }
+                tc::commit(mbar);
+                mma_pending = true;
+                ok = mbar_wait_bounded(mbar, mph, err, EDB_DEVERR_DELTA_PIPE);
+                if (ok) {
+                    mph ^= 1u;
+                    mma_pending = false;
+                }
+            }
+            if (ok) {
+                if (c >= 1) issue_y(c - 1);
+                if (c >= 2) issue_x(c - 2, n + 2);
+            } else {
+                s_misc[1] = 1;
+            }
+        }
+        tc::fence_before_sync();
+        __syncthreads();
+        tc::fence_after_sync();
+        if (s_misc[1]) break;
+        // D_U = dU~^T: row i -> dU~[c][t][i]
+        store_rows_transposed<C>(dU + (ch0 + c) * C * D + i, tmem + SB_TM_U + lane_base);
+    }
+    if (s_misc[1] && tid == 0) {
+        // Abort: bounded waits for the copies and MMAs still in flight.
+        for (int bb = 0; bb < 2; ++bb)
+            for (; x_landed[bb] < x_issued[bb]; ++x_landed[bb])
+                mbar_wait_bounded(&fullX[bb], x_landed[bb] & 1, err, EDB_DEVERR_DELTA_PIPE);
+        for (; y_landed < y_issued; ++y_landed)
+            mbar_wait_bounded(fullY, y_landed & 1, err, EDB_DEVERR_DELTA_PIPE);
+        if (mma_pending) mbar_wait_bounded(mbar, mph, err, EDB_DEVERR_DELTA_PIPE);
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, SB_TM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ post1
+struct Post1Maps {
+    CUtensorMap S0T, dSCT, Ut, dU;
+};
+
+constexpr int P1_S0 = 0, P1_DS = 4 * BOX_D, P1_U = 8 * BOX_D, P1_DU = P1_U + 4 * BOX_C,
+              P1_DO = P1_DU + 4 * BOX_C;
+constexpr int P1_TX = 8 * BOX_D + 8 * BOX_C;  // bytes arriving by TMA (192 KB)
+constexpr int P1_OFF_BARS = P1_DO + 4 * BOX_C;
+constexpr int P1_SMEM = P1_OFF_BARS + 64;
+constexpr int P1_TM_Q = 0, P1_TM_W = 64, P1_TM_K = 128, P1_TM_M = 192, P1_TM_COLS = 256;
+
+__global__ void __launch_bounds__(128, 1)
+    delta_post1_kernel(const __grid_constant__ Post1Maps maps, const __nv_bfloat16* __restrict__ dO,
+                       float* __restrict__ dQa, float* __restrict__ dW, float* __restrict__ dK1,
+                       float* __restrict__ dM, int L, int H, int NC, unsigned* err) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + P1_OFF_BARS);
+    uint64_t* mbar = full + 1;
+    uint32_t* s_misc = reinterpret_cast<uint32_t*>(mbar + 1);
+    const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const long long bh = (long long)b * H + h;
+    const long long ch = bh * NC + c;
+    const int t0 = c * C, nvalid = min(C, L - t0);
+
+    if ((smem_u32(smem) & 1023u) != 0) {
+        if (tid == 0) edb_flag_error(err, EDB_DEVERR_DELTA_PIPE);
+        return;
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(s_misc, P1_TM_COLS);
+        tc::tmem_relinquish();
+    }
+    if (tid == 0) {
+        s_misc[1] = 0;
+        mbar_init(full, 1);
+        mbar_init(mbar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(full, P1_TX);
+        const int rs = (int)((bh * (NC + 1) + c) * D), rd = (int)(ch * D), rc = (int)(ch * C);
+        for (int bx = 0; bx < 4; ++bx) {
+            tma_load_2d(smem + P1_S0 + bx * BOX_D, &maps.S0T, full, bx * 32, rs);
+            tma_load_2d(smem + P1_DS + bx * BOX_D, &maps.dSCT, full, bx * 32, rd);
+            tma_load_2d(smem + P1_U + bx * BOX_C, &maps.Ut, full, bx * 32, rc);
+            tma_load_2d(smem + P1_DU + bx * BOX_C, &maps.dU, full, bx * 32, rc);
+        }
+    }
+    // dO rows (bf16) -> f32 K-major SW128 tile [C][D]
+    for (int idx = tid; idx < C * (D / 4); idx += 128) {
+        const int t = idx / (D / 4), k4 = (idx % (D / 4)) * 4;
+        float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t < nvalid) {
+            const uint2 raw = *reinterpret_cast<const uint2*>(
+                dO + (((long long)b * L + t0 + t) * H + h) * D + k4);
+            f = make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u),
+                            __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xffff0000u));
+        }
+        *reinterpret_cast<float4*>(smem + P1_DO + kmaj_off4(t, k4, C)) = f;
+    }
+    fence_proxy_async();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = s_misc[0];
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    if (tid == 0) {
+        bool ok = mbar_wait_bounded(full, 0, err, EDB_DEVERR_DELTA_PIPE);
+        if (ok) {
+            tc::fence_after_sync();
+            constexpr uint32_t id128 = idesc_tf32(128, C), id64 = idesc_tf32(64, C);
+#pragma unroll
+            for (int kk = 0; kk < D / 8; ++kk) {
+                const uint64_t s0 = kdesc(smem + P1_S0, BOX_D, kk);
+                const uint64_t dof = kdesc(smem + P1_DO, BOX_C, kk);
+                const uint64_t u = kdesc(smem + P1_U, BOX_C, kk);
+                mma_tf32_ss(tmem + P1_TM_Q, s0, dof, id128, kk > 0);
+                mma_tf32_ss(tmem + P1_TM_W, s0, kdesc(smem + P1_DU, BOX_C, kk), id128, kk > 0);
+                mma_tf32_ss(tmem + P1_TM_K, kdesc(smem + P1_DS, BOX_D, kk), u, id128, kk > 0);
+                mma_tf32_ss(tmem + P1_TM_M, dof, u, id64, kk > 0);
+            }
+            tc::commit(mbar);
+            ok = mbar_wait_bounded(mbar, 0, err, EDB_DEVERR_DELTA_PIPE);
+            if (!ok) mbar_wait_bounded(mbar, 0, err, EDB_DEVERR_DELTA_PIPE);
+        } else {
+            mbar_wait_bounded(full, 0, err, EDB_DEVERR_DELTA_PIPE);  // drain the copies
+        }
+        if (!ok) s_misc[1] = 1;
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (!s_misc[1]) {
+        const int j = tid;
+        store_rows_transposed<C>(dQa + ch * C * D + j, tmem + P1_TM_Q + lane_base);
+        store_rows_transposed<C>(dW + ch * C * D + j, tmem + P1_TM_W + lane_base, -1.0f);
+        store_rows_transposed<C>(dK1 + ch * C * D + j, tmem + P1_TM_K + lane_base);
+        // M = 64 accumulator: lanes 32w + r (r < 16) hold row 16w + r
+        uint32_t x0[32], x1[32];
+        tc::tmem_ld32(tmem + P1_TM_M + lane_base, x0);
+        tc::tmem_ld32(tmem + P1_TM_M + lane_base + 32, x1);
+        tc::tmem_wait_ld();
+        if (lane < 16) {
+            const int t = 16 * warp + lane;
+            float* dst = dM + (ch * C + t) * C;
+#pragma unroll
+            for (int s = 0; s < 32; ++s) dst[s] = s <= t ? __uint_as_float(x0[s]) : 0.0f;
+#pragma unroll
+            for (int s = 0; s < 32; ++s)
+                dst[32 + s] = s + 32 <= t ? __uint_as_float(x1[s]) : 0.0f;
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, P1_TM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ post2
+// 256 threads; output tiles of 4 rows (ty + 16 r) x NC2 columns (tx + 16 c).
+constexpr int kPost2Threads = 256;
+constexpr size_t kPost2Smem = (size_t)(4 * C * PP + 4 * C * PC + 2 * C) * sizeof(float);
+
+template <int R, int CN, class F>
+static __device__ __forceinline__ void mm_acc(float (&acc)[R][CN], int k0, int k1, F f) {
+    const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+    for (int kq = k0; kq < k1; ++kq) f(acc, ty, tx, kq);
+}
+
+static __device__ __forceinline__ void load_rows_f32(float* dst, const float* src, int ld_dst) {
+    for (int idx = threadIdx.x; idx < C * (D / 4); idx += kPost2Threads) {
+        const int t = idx / (D / 4), j4 = (idx % (D / 4)) * 4;
+        const float4 f = *reinterpret_cast<const float4*>(src + t * D + j4);
+        dst[t * ld_dst + j4] = f.x;
+        dst[t * ld_dst + j4 + 1] = f.y;
+        dst[t * ld_dst + j4 + 2] = f.z;
+        dst[t * ld_dst + j4 + 3] = f.w;
+    }
+}
+
+static __device__ __forceinline__ void load_cc(float* dst, const float* src) {
+    for (int idx = threadIdx.x; idx < C * C; idx += kPost2Threads)
+        dst[(idx / C) * PC + idx % C] = src[idx];
+}
+
+__global__ void __launch_bounds__(kPost2Threads, 1)
+    delta_post2_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                       const __nv_bfloat16* __restrict__ v, const __nv_bfloat16* __restrict__ beta,
+                       const float* __restrict__ dQa, const float* __restrict__ dWg,
+                       const float* __restrict__ dK1, const float* __restrict__ dMg,
+                       const float* __restrict__ Tg, const float* __restrict__ Gg,
+                       const float* __restrict__ dUg, __nv_bfloat16* __restrict__ gq,
+                       __nv_bfloat16* __restrict__ gk, __nv_bfloat16* __restrict__ gv,
+                       __nv_bfloat16* __restrict__ gbeta, int L, int H, int NC) {
+    extern __shared__ float sm[];
+    float* Ks = sm;                // [C][PP]  K
+    float* Ws = Ks + C * PP;       // [C][PP]  dW
+    float* Us = Ws + C * PP;       // [C][PP]  dU~, then Q
+    float* Vs = Us + C * PP;       // [C][PP]  V
+    float* dMs = Vs + C * PP;      // [C][PC]  dM
+    float* Ts = dMs + C * PC;      // [C][PC]  T
+    float* Xa = Ts + C * PC;       // [C][PC]  dT_b -> dT -> dA
+    float* Xb = Xa + C * PC;       // [C][PC]  X = T^T dT -> E = dG + dG^T
+    float* bs = Xb + C * PC;       // [C]
+    float* dbs = bs + C;           // [C]
+    const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x;
+    const long long ch = ((long long)b * H + h) * NC + c;
+    const int t0 = c * C, nvalid = min(C, L - t0);
+    const long long ts = (long long)H * D;
+    const long long row0 = (((long long)b * L + t0) * H + h) * D;
+    const int ty = tid >> 4, tx = tid & 15;
+
+    // K, V (bf16 -> f32), dW, dU~, dM, T, beta
+    for (int idx = tid; idx < C * (D / 8); idx += kPost2Threads) {
+        const int t = idx / (D / 8), j8 = (idx % (D / 8)) * 8;
+        float kf[8], vf[8];
+        if (t < nvalid) {
+            Vec16<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(k + row0 + t * ts + j8), kf);
+            Vec16<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(v + row0 + t * ts + j8), vf);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) kf[e] = vf[e] = 0.0f;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            Ks[t * PP + j8 + e] = kf[e];
+            Vs[t * PP + j8 + e] = vf[e];
+        }
+    }
+    load_rows_f32(Ws, dWg + ch * C * D, PP);
+    load_rows_f32(Us, dUg + ch * C * D, PP);
+    load_cc(dMs, dMg + ch * C * C);
+    load_cc(Ts, Tg + ch * C * C);
+    if (tid < C)
+        bs[tid] = tid < nvalid ? __bfloat162float(beta[((long long)b * L + t0 + tid) * H + h])
+                               : 0.0f;
+    __syncthreads();
+
+    // dQ = dO S_0 + dM K ;  dV = T_b^T dU~   (64 x 128 each)
+    {
+        float aq[4][8], av[4][8];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) aq[r][cc] = av[r][cc] = 0.0f;
+        for (int s = 0; s < C; ++s) {
+            float am[4], at[4], bk[8], bu[8];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const int row = ty + 16 * r;
+                am[r] = dMs[row * PC + s];                 // dM[row][s]
+                at[r] = Ts[s * PC + row] * bs[row];        // T_b[s][row]
+            }
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+                bk[cc] = Ks[s * PP + tx + 16 * cc];
+                bu[cc] = Us[s * PP + tx + 16 * cc];
+            }
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc) {
+                    aq[r][cc] = fmaf(am[r], bk[cc], aq[r][cc]);
+                    av[r][cc] = fmaf(at[r], bu[cc], av[r][cc]);
+                }
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int row = ty + 16 * r;
+            if (row < nvalid) {
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc) {
+                    const int col = tx + 16 * cc;
+                    gq[row0 + row * ts + col] =
+                        __float2bfloat16(aq[r][cc] + dQa[(ch * C + row) * D + col]);
+                    gv[row0 + row * ts + col] = __float2bfloat16(av[r][cc]);
+                }
+            }
+        }
+    }
+    // dT_b = dW K^T + dU~ V^T   (64 x 64)
+    {
+        float a[4][4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) a[r][cc] = 0.0f;
+        for (int j = 0; j < D; ++j) {
+            float aw[4], au[4], bk[4], bv[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                aw[r] = Ws[(ty + 16 * r) * PP + j];
+                au[r] = Us[(ty + 16 * r) * PP + j];
+            }
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                bk[cc] = Ks[(tx + 16 * cc) * PP + j];
+                bv[cc] = Vs[(tx + 16 * cc) * PP + j];
+            }
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc)
+                    a[r][cc] = fmaf(aw[r], bk[cc], fmaf(au[r], bv[cc], a[r][cc]));
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) Xa[(ty + 16 * r) * PC + tx + 16 * cc] = a[r][cc];
+    }
+    __syncthreads();
+    // dbeta (from T_b) and dT = dT_b diag(beta)
+    if (tid < C) {
+        const int s = tid;
+        float acc = 0.0f;
+        for (int t = s; t < C; ++t) acc = fmaf(Xa[t * PC + s], Ts[t * PC + s], acc);
+        dbs[s] = acc;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < C * C; idx += kPost2Threads) {
+        const int t = idx / C, s = idx % C;
+        Xa[t * PC + s] *= bs[s];
+    }
+    __syncthreads();
+    // X = T^T dT
+    {
+        float a[4][4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) a[r][cc] = 0.0f;
+        for (int t = 0; t < C; ++t) {
+            float at[4], bd[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) at[r] = Ts[t * PC + ty + 16 * r];
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) bd[cc] = Xa[t * PC + tx + 16 * cc];
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) a[r][cc] = fmaf(at[r], bd[cc], a[r][cc]);
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) Xb[(ty + 16 * r) * PC + tx + 16 * cc] = a[r][cc];
+    }
+    __syncthreads();
+    // dA = -X T^T, strictly lower
+    {
+        float a[4][4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) a[r][cc] = 0.0f;
+        for (int s = 0; s < C; ++s) {
+            float ax[4], bt[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) ax[r] = Xb[(ty + 16 * r) * PC + s];
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) bt[cc] = Ts[(tx + 16 * cc) * PC + s];
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) a[r][cc] = fmaf(ax[r], bt[cc], a[r][cc]);
+        }
+        __syncthreads();  // all reads of Xa (dT) and Xb (X) are done
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                const int row = ty + 16 * r, col = tx + 16 * cc;
+                Xa[row * PC + col] = col < row ? -a[r][cc] : 0.0f;
+            }
+    }
+    __syncthreads();
+    // dbeta (from A) ; E = dG + dG^T with dG = diag(beta) dA
+    if (tid < C) {
+        const int t = tid;
+        const float* g = Gg + (ch * C + t) * C;
+        float acc = 0.0f;
+        for (int s = 0; s < t; ++s) acc = fmaf(Xa[t * PC + s], g[s], acc);
+        dbs[t] += acc;
+        if (t < nvalid) gbeta[((long long)b * L + t0 + t) * H + h] = __float2bfloat16(dbs[t]);
+    }
+    for (int idx = tid; idx < C * C; idx += kPost2Threads) {
+        const int t = idx / C, s = idx % C;
+        Xb[t * PC + s] = bs[t] * Xa[t * PC + s] + bs[s] * Xa[s * PC + t];
+    }
+    __syncthreads();
+    // Q replaces dU~
+    for (int idx = tid; idx < C * (D / 8); idx += kPost2Threads) {
+        const int t = idx / (D / 8), j8 = (idx % (D / 8)) * 8;
+        float qf[8];
+        if (t < nvalid) {
+            Vec16<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(q + row0 + t * ts + j8), qf);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) qf[e] = 0.0f;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) Us[t * PP + j8 + e] = qf[e];
+    }
+    __syncthreads();
+    // dK = U~ dS_C + dM^T Q + T_b^T dW + E K
+    {
+        float a[4][8];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) a[r][cc] = 0.0f;
+        for (int t = 0; t < C; ++t) {
+            float am[4], at[4], ae[4], bq[8], bw[8], bk[8];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const int s = ty + 16 * r;
+                am[r] = dMs[t * PC + s];
+                at[r] = Ts[t * PC + s] * bs[s];
+                ae[r] = Xb[t * PC + s];
+            }
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+                const int col = tx + 16 * cc;
+                bq[cc] = Us[t * PP + col];
+                bw[cc] = Ws[t * PP + col];
+                bk[cc] = Ks[t * PP + col];
+            }
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc)
+                    a[r][cc] = fmaf(am[r], bq[cc],
+                                    fmaf(at[r], bw[cc], fmaf(ae[r], bk[cc], a[r][cc])));
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int row = ty + 16 * r;
+            if (row < nvalid) {
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc) {
+                    const int col = tx + 16 * cc;
+                    gk[row0 + row * ts + col] =
+                        __float2bfloat16(a[r][cc] + dK1[(ch * C + row) * D + col]);
+                }
+            }
+        }
+    }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- library-internal
+size_t edb_delta_chunked_bwd_ws(int B, int L, int H) {
+    return bwd_scratch_bytes((long long)B * H * ((L + C - 1) / C));
+}
+
+int edb_delta_chunked_bwd(const void* q, const void* k, const void* v, const void* beta,
+                          const void* dO, const float* resid, void* gq, void* gk, void* gv,
+                          void* gbeta, int B, int L, int H, void* ws, cudaStream_t st) {
+    const int NC = (L + C - 1) / C;
+    const long long units = (long long)B * H, nch = units * NC;
+    if ((units * (NC + 1)) * D > 0x7fffffffLL) return EDB_ERR_UNSUPPORTED;
+    BwdScratch w = carve_bwd(ws, nch);
+    unsigned* err = edb::device_error_word();
+    const __nv_bfloat16 *qb = (const __nv_bfloat16*)q, *kb = (const __nv_bfloat16*)k,
+                        *vb = (const __nv_bfloat16*)v, *bb = (const __nv_bfloat16*)beta,
+                        *dob = (const __nv_bfloat16*)dO;
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(delta_prep_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)kPrepSmem)) != cudaSuccess)
+        return (int)e;
+    delta_prep_bwd_kernel<<<dim3(NC, H, B), kPrepThreads, kPrepSmem, st>>>(qb, kb, bb, dob, w, L,
+                                                                           H, NC);
+    if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
+
+    StateBwdMaps sm;
+    int s;
+    if ((s = make_box_map(&sm.Kf, w.Kf, nch * C, D, C))) return s;
+    if ((s = make_box_map(&sm.dOT, w.dOT, nch * D, C, D))) return s;
+    if ((s = make_box_map(&sm.MT, w.MT, nch * C, C, C))) return s;
+    if ((s = make_box_map(&sm.QT, w.QT, nch * D, C, D))) return s;
+    if ((s = make_box_map(&sm.WnT, w.WnT, nch * D, C, D))) return s;
+    if ((e = cudaFuncSetAttribute(delta_state_bwd_kernel,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, SB_SMEM)) !=
+        cudaSuccess)
+        return (int)e;
+    delta_state_bwd_kernel<<<dim3(H, B), kStateThreads, SB_SMEM, st>>>(sm, w.dSCT, w.dU, H, NC,
+                                                                       err);
+    if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
+
+    // post1 writes into the state kernel's operand buffers, which are dead now
+    float* dQa = w.Kf;
+    float* dW = w.dOT;
+    float* dK1 = w.QT;
+    float* dM = w.MT;
+    Post1Maps pm;
+    if ((s = make_box_map(&pm.S0T, resid, units * (NC + 1) * D, D, D))) return s;
+    if ((s = make_box_map(&pm.dSCT, w.dSCT, nch * D, D, D))) return s;
+    if ((s = make_box_map(&pm.Ut, resid + ckpt_state_floats(units, NC), nch * C, D, C))) return s;
+    if ((s = make_box_map(&pm.dU, w.dU, nch * C, D, C))) return s;
+    if ((e = cudaFuncSetAttribute(delta_post1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  P1_SMEM)) != cudaSuccess)
+        return (int)e;
+    delta_post1_kernel<<<dim3(NC, H, B), 128, P1_SMEM, st>>>(pm, dob, dQa, dW, dK1, dM, L, H, NC,
+                                                             err);
+    if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
+
+    if ((e = cudaFuncSetAttribute(delta_post2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)kPost2Smem)) != cudaSuccess)
+        return (int)e;
+    delta_post2_kernel<<<dim3(NC, H, B), kPost2Threads, kPost2Smem, st>>>(
+        qb, kb, vb, bb, dQa, dW, dK1, dM, w.T, w.G, w.dU, (__nv_bfloat16*)gq, (__nv_bfloat16*)gk,
+        (__nv_bfloat16*)gv, (__nv_bfloat16*)gbeta, L, H, NC);
+    return edb::status_from_cuda(cudaGetLastError());
+}

@@ -253,15 +253,23 @@ int check(int dtype, int B, int L, int H, int d) {
 
 }  // namespace
 
-// Chunked tensor-core forward (delta_chunked.cu).
+// Chunked tensor-core path (delta_chunked.cu, delta_chunked_bwd.cu).
 bool edb_delta_chunked_ok(int dtype, int beta_per_element, int head_dim);
+size_t edb_delta_chunked_ckpt_bytes(int B, int L, int H);
 size_t edb_delta_chunked_fwd_ws(int B, int L, int H);
+size_t edb_delta_chunked_bwd_ws(int B, int L, int H);
 int edb_delta_chunked_fwd(const void* q, const void* k, const void* v, const void* beta, void* o,
-                          float* s_ckpt, int B, int L, int H, void* ws, cudaStream_t st);
+                          float* resid, int B, int L, int H, void* ws, cudaStream_t st);
+int edb_delta_chunked_bwd(const void* q, const void* k, const void* v, const void* beta,
+                          const void* dO, const float* resid, void* gq, void* gk, void* gv,
+                          void* gbeta, int B, int L, int H, void* ws, cudaStream_t st);
 
-extern "C" size_t edb_delta_rule_ckpt_bytes(int batch, int seq_len, int heads, int head_dim) {
-    if (batch <= 0 || seq_len <= 0 || heads <= 0 || head_dim <= 0) return 0;
-    return ckpt_bytes(batch, seq_len, heads, head_dim);
+extern "C" size_t edb_delta_rule_ckpt_bytes(int dtype, int beta_per_element, int batch,
+                                            int seq_len, int heads, int head_dim) {
+    if (check(dtype, batch, seq_len, heads, head_dim)) return 0;
+    return edb_delta_chunked_ok(dtype, beta_per_element, head_dim)
+               ? edb_delta_chunked_ckpt_bytes(batch, seq_len, heads)
+               : ckpt_bytes(batch, seq_len, heads, head_dim);
 }
 
 extern "C" size_t edb_delta_rule_fwd_workspace(int dtype, int beta_per_element, int batch,
@@ -301,10 +309,16 @@ extern "C" size_t edb_delta_rule_bwd_workspace(int dtype, int beta_per_element, 
                                                int seq_len, int heads, int head_dim,
                                                int have_ckpt) {
     if (check(dtype, batch, seq_len, heads, head_dim)) return 0;
-    if (have_ckpt) return 0;
-    // checkpoints, then the forward's own scratch
-    return a256(ckpt_bytes(batch, seq_len, heads, head_dim)) +
-           edb_delta_rule_fwd_workspace(dtype, beta_per_element, batch, seq_len, heads, head_dim);
+    const size_t ck = have_ckpt ? 0
+                                : a256(edb_delta_rule_ckpt_bytes(dtype, beta_per_element, batch,
+                                                                 seq_len, heads, head_dim));
+    if (edb_delta_chunked_ok(dtype, beta_per_element, head_dim)) {
+        // residuals (when not passed), then the forward's or the backward's scratch
+        const size_t f = edb_delta_chunked_fwd_ws(batch, seq_len, heads);
+        const size_t b = edb_delta_chunked_bwd_ws(batch, seq_len, heads);
+        return ck + (have_ckpt ? b : (f > b ? f : b));
+    }
+    return ck;
 }
 
 extern "C" int edb_delta_rule_bwd(int dtype, const void* q, const void* k, const void* v,
@@ -318,15 +332,35 @@ extern "C" int edb_delta_rule_bwd(int dtype, const void* q, const void* k, const
                                                      heads, head_dim, s_ckpt != nullptr);
     if (workspace_bytes < need || (need && !workspace)) return EDB_ERR_WORKSPACE_TOO_SMALL;
     cudaStream_t st = (cudaStream_t)stream;
+    const size_t ckb =
+        s_ckpt ? 0
+               : a256(edb_delta_rule_ckpt_bytes(dtype, beta_per_element, batch, seq_len, heads,
+                                                head_dim));
+    if (edb_delta_chunked_ok(dtype, beta_per_element, head_dim)) {
+        if (!edb::aligned16(q) || !edb::aligned16(k) || !edb::aligned16(v) ||
+            !edb::aligned16(dO) || !edb::aligned16(workspace) ||
+            (reinterpret_cast<uintptr_t>(s_ckpt) & 15u))
+            return EDB_ERR_MISALIGNED;
+        const float* resid = s_ckpt;
+        char* scratch = static_cast<char*>(workspace) + ckb;
+        if (!resid) {
+            // residuals into the workspace; o goes to gq, which the backward overwrites
+            float* r = static_cast<float*>(workspace);
+            int s = edb_delta_chunked_fwd(q, k, v, beta, gq, r, batch, seq_len, heads, scratch,
+                                          st);
+            if (s) return s;
+            resid = r;
+        }
+        return edb_delta_chunked_bwd(q, k, v, beta, dO, resid, gq, gk, gv, gbeta, batch, seq_len,
+                                     heads, scratch, st);
+    }
     const int bs = beta_per_element ? 0 : 1;
     const float* ck = s_ckpt;
     if (!ck) {
-        float* w = static_cast<float*>(workspace);
         // states only: the forward writes o into gq, which the backward overwrites
-        const size_t ckb = a256(ckpt_bytes(batch, seq_len, heads, head_dim));
+        float* w = static_cast<float*>(workspace);
         int s = edb_delta_rule_fwd(dtype, q, k, v, beta, beta_per_element, gq, w, batch, seq_len,
-                                   heads, head_dim, static_cast<char*>(workspace) + ckb,
-                                   workspace_bytes - ckb, stream);
+                                   heads, head_dim, nullptr, 0, stream);
         if (s) return s;
         ck = w;
     }

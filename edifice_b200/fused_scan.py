@@ -214,8 +214,8 @@ def delta_net_scan(q, k, v, beta, with_ckpt=False):
     dt = _dtype_code(q, "delta_net_scan")
     ck = None
     if with_ckpt:
-        ck = torch.empty(lib.edb_delta_rule_ckpt_bytes(B, L, H, d) // 4, dtype=torch.float32,
-                         device=q.device)
+        ck = torch.empty(lib.edb_delta_rule_ckpt_bytes(dt, per_el, B, L, H, d) // 4,
+                         dtype=torch.float32, device=q.device)
     wsb = lib.edb_delta_rule_fwd_workspace(dt, per_el, B, L, H, d)
     ws = torch.empty(wsb, dtype=torch.uint8, device=q.device) if wsb else None
     _lib.check(lib.edb_delta_rule_fwd(dt, _p(q), _p(k), _p(v), _p(beta), per_el, _p(o), _p(ck),

@@ -177,17 +177,21 @@ int edb_flash_attention_bwd(int dtype, const void* q, const void* k, const void*
  * caller); beta: [batch, seq_len, heads, head_dim] when beta_per_element
  * (Edifice.build(:delta_net)'s form, lib/edifice/recurrent/delta_net.ex:285-297),
  * else [batch, seq_len, heads] (one gate per token and head).  head_dim <= 128.
- * s_ckpt (optional f32, edb_delta_rule_ckpt_bytes() bytes,
- * [batch][heads][nchunks + 1][head_dim][head_dim]): the forward also writes S
- * at the start of every 64-token chunk, and the final S, for the backward.
  * bf16 io with one beta per token and head_dim 128 runs the chunked
- * tensor-core form (WY representation, tcgen05 TF32 products, f32 state);
- * every other case runs the token recurrence.
+ * tensor-core form (WY representation over 64-token chunks, tcgen05 TF32
+ * products, f32 state); every other case runs the token recurrence.
+ * s_ckpt (optional, f32, edb_delta_rule_ckpt_bytes() bytes): residuals the
+ * forward leaves for edb_delta_rule_bwd of the same dtype, beta form and shape.
+ * Token recurrence: S ([head_dim][head_dim], value index first) at the start
+ * of every 64-token chunk and the final S, [batch][heads][nchunks + 1][d][d].
+ * Chunked form: the same states transposed (key index first), followed by the
+ * per-chunk errors U~ = U0 - W S_0^T, [batch * heads][nchunks][64][d].
  * Replaces fused_delta_net_scan_launch / fused_delta_rule_scan_launch with
  * alpha = NULL (native/cuda/fused_delta_rule_scan.cu:213-258); Nx semantics
  * lib/edifice/cuda/fused_scan.ex:2212-2236.
  * ---------------------------------------------------------------------- */
-size_t edb_delta_rule_ckpt_bytes(int batch, int seq_len, int heads, int head_dim);
+size_t edb_delta_rule_ckpt_bytes(int dtype, int beta_per_element, int batch, int seq_len,
+                                 int heads, int head_dim);
 
 /* Workspace bytes edb_delta_rule_fwd needs (0 when the token recurrence serves
  * the call). */

@@ -76,9 +76,11 @@ CHUNKED_CASES = [
 @pytest.mark.parametrize("case", CHUNKED_CASES)
 def test_delta_chunked_forward(cuda, case):
     """bf16 io, one beta per token, head_dim 128: the chunked tensor-core
-    forward.  Output against the oracle; the chunk-start states against the
-    token recurrence's (the f32 path run on the same bf16-rounded inputs),
-    which share one layout [B][H][nchunks + 1][d][d]."""
+    forward and backward.  Outputs and gradients against the oracle; the
+    chunk-start states (stored transposed by this path) against the token
+    recurrence's, [B][H][nchunks + 1][d][d], from the f32 path run on the same
+    bf16-rounded inputs."""
+    B, L, H, d = case
     q, k, v, beta, do = delta_inputs(*case, torch.bfloat16, seed=54, scalar_beta=True)
     o, ck = fs.delta_net_scan(q, k, v, beta, with_ckpt=True)
     of, ckf = fs.delta_net_scan(q.float(), k.float(), v.float(), beta.float(), with_ckpt=True)
@@ -88,13 +90,18 @@ def test_delta_chunked_forward(cuda, case):
     ref = O.delta_net_fwd(*args)
     assert O.norm_rel(_np(o), ref) <= 2e-2
     assert O.norm_rel(_np(of), ref) <= 1e-4
-    assert ck.shape == ckf.shape
-    assert O.norm_rel(_np(ck), _np(ckf)) <= 5e-3
-    # the backward consumes the chunked checkpoints
-    grads = fs.delta_rule_backward(q, k, v, beta, do, ck)
-    torch.cuda.synchronize()
-    for got, r in zip(grads, O.delta_net_bwd(*args, _np(do))):
-        assert O.norm_rel(_np(got), r) <= 2e-2
+    nc = (L + 63) // 64
+    states = ck[:B * H * (nc + 1) * d * d].view(B, H, nc + 1, d, d).transpose(-1, -2)
+    assert ck.numel() == B * H * (nc + 1) * d * d + B * H * nc * 64 * d
+    assert O.norm_rel(_np(states), _np(ckf.view(B, H, nc + 1, d, d))) <= 5e-3
+    rg = O.delta_net_bwd(*args, _np(do))
+    for ckpt in (ck, None):  # residuals from the forward, or recomputed inside
+        grads = fs.delta_rule_backward(q, k, v, beta, do, ckpt)
+        torch.cuda.synchronize()
+        assert device_errors() == 0
+        for got, r in zip(grads, rg):
+            assert got.shape == torch.Size(r.shape)
+            assert O.norm_rel(_np(got), r) <= 2e-2, O.norm_rel(_np(got), r)
 
 
 @pytest.mark.parametrize("layer", [0, 1])
