@@ -70,7 +70,7 @@ FwdScratch carve_fwd(void* ws, long long nch) {
 // ------------------------------------------------------------------ prep
 // grid (NC, H, B), 256 threads.  Rows past L load as zero with beta 0, which
 // makes their W / U0 rows zero, so the padded tail leaves S untouched.
-constexpr size_t kPrepSmem = (size_t)(3 * C * PP + 3 * C * PC + C) * sizeof(float);
+constexpr size_t kPrepSmem = (size_t)(3 * C * PP + 3 * C * PC + C * C + C) * sizeof(float);
 
 __global__ void __launch_bounds__(kPrepThreads, 1)
     delta_prep_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
@@ -79,14 +79,15 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
                           int NC) {
     extern __shared__ float sm[];
     float* Ks = sm;              // [C][PP]
-    float* Qs = Ks + C * PP;     // [C][PP]  (then -W)
+    float* Qs = Ks + C * PP;     // [C][PP]
     float* Vs = Qs + C * PP;     // [C][PP]  (then U0)
     float* Gs = Vs + C * PP;     // [C][PC]  K K^T
     float* Ms = Gs + C * PC;     // [C][PC]  tril(Q K^T)
     float* Tm = Ms + C * PC;     // [C][PC]  T
-    float* bs = Tm + C * PC;     // [C]
+    float* ATn = Tm + C * PC;    // [C][C]   solve scratch
+    float* bs = ATn + C * C;     // [C]
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
     const long long ch = ((long long)b * H + h) * NC + c;
     const int t0 = c * C, nvalid = min(C, L - t0);
     const long long row0 = (((long long)b * L + t0) * H + h) * D, ts = (long long)H * D;
@@ -98,31 +99,27 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
         bs[tid] = tid < nvalid ? __bfloat162float(beta[((long long)b * L + t0 + tid) * H + h])
                                : 0.0f;
     __syncthreads();
-    for (int idx = tid; idx < D * C; idx += kPrepThreads)  // K^T, coalesced over t
-        ws.KT[ch * D * C + idx] = Ks[(idx % C) * PP + idx / C];
+    store_transposed(ws.KT + ch * D * C, Ks, 1.0f);
     prep_products(Ks, Qs, Gs, Ms);
     __syncthreads();
     for (int idx = tid; idx < C * C; idx += kPrepThreads)
         ws.M[ch * C * C + idx] = Ms[(idx / C) * PC + idx % C];
-    prep_solve(Gs, bs, Tm);
-    __syncthreads();
-    {
-        const int t = tid >> 2, jl = tid & 3;
-        float w[32], u[32];
-        prep_apply_tb(Tm, bs, Ks, w);
-        prep_apply_tb(Tm, bs, Vs, u);
-        __syncthreads();  // every read of Q and V is done: reuse their rows
+    prep_solve(Gs, bs, ATn, Tm);
+    float w[4][8], u[4][8];
+    prep_apply_tb(Tm, bs, Ks, w);
+    prep_apply_tb(Tm, bs, Vs, u);
+    // -W rows straight to HBM (two float4 per row and thread)
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-            Qs[t * PP + jl + 4 * e] = -w[e];
-            Vs[t * PP + jl + 4 * e] = u[e];
-        }
-    }
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc)
+            st4(ws.Wn + (ch * C + ty + 16 * r) * D + 64 * cc + 4 * tx,
+                make_float4(-w[r][4 * cc], -w[r][4 * cc + 1], -w[r][4 * cc + 2],
+                            -w[r][4 * cc + 3]));
+    __syncthreads();  // every read of V is done: U0 takes its place
+    put_tile(Vs, u, 1.0f);
     __syncthreads();
-    for (int idx = tid; idx < C * D; idx += kPrepThreads)
-        ws.Wn[ch * C * D + idx] = Qs[(idx / D) * PP + idx % D];
-    for (int idx = tid; idx < D * C; idx += kPrepThreads)
-        ws.U0T[ch * D * C + idx] = Vs[(idx % C) * PP + idx / C];
+    store_transposed(ws.U0T + ch * D * C, Vs, 1.0f);
 }
 
 // ------------------------------------------------------------------ state fwd

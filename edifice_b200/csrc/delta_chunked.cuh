@@ -94,89 +94,179 @@ static __device__ __forceinline__ void store_rows_transposed(float* dst, uint32_
     }
 }
 
-// ---------------------------------------------------------------- chunk prep (SIMT)
-// Shared by the forward and backward prep kernels (256 threads, one chunk).
-// Shared-memory operands are f32 with padded rows: [C][PP] for C x D tiles,
-// [C][PC] for C x C (odd strides: column walks are bank-conflict free).
+// ---------------------------------------------------------------- chunk-local SIMT
+// Shared by the prep kernels and the backward's C x C kernel (256 threads,
+// one chunk).  Shared-memory tiles are f32: C x D tiles with rows of PP = 132
+// floats (16-byte aligned; float4 index 33 t + j/4 puts 8 consecutive rows
+// on 8 different bank groups), C x C tiles with rows of PC = 65 floats (odd:
+// scalar column walks are bank-conflict free).  Thread (ty, tx) = (tid / 16,
+// tid % 16) owns output rows ty + 16 r and, for C x D outputs, columns
+// 4 tx + 64 c + e (two float4s per row), for C x C outputs columns tx + 16 c.
 constexpr int kPrepThreads = 256;
-constexpr int PP = D + 1;
+constexpr int PP = D + 4;
 constexpr int PC = C + 1;
 
-// Load rows t0.. of a bf16 [.., heads, D] tensor (token stride H*D) into
-// dst[C][PP] as f32; rows past L are zero.  If gcopy != nullptr, also stores
-// the f32 rows to gcopy[C][D].
+static __device__ __forceinline__ float4 ld4(const float* p) {
+    return *reinterpret_cast<const float4*>(p);
+}
+static __device__ __forceinline__ void st4(float* p, float4 v) {
+    *reinterpret_cast<float4*>(p) = v;
+}
+static __device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
+    return fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, fmaf(a.w, b.w, acc))));
+}
+
+// Load rows of a bf16 [.., heads, D] tensor (token stride tok_stride, first
+// row at row0) into dst[C][PP] as f32; rows >= nvalid are zero.  If gcopy is
+// not null, also stores the f32 rows to gcopy[C][D].
+// All of a thread's global loads are issued before the first use, so the
+// latencies overlap (one loop iteration per load would serialise them).
 static __device__ __forceinline__ void load_chunk_rows(float* dst, const __nv_bfloat16* src,
                                                        long long row0, long long tok_stride,
                                                        int nvalid, float* gcopy) {
-    for (int idx = threadIdx.x; idx < C * (D / 8); idx += kPrepThreads) {
+    constexpr int N = C * (D / 8) / kPrepThreads;
+    uint4 raw[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+        const int idx = threadIdx.x + n * kPrepThreads;
+        const int t = idx / (D / 8), j8 = (idx % (D / 8)) * 8;
+        raw[n] = t < nvalid ? *reinterpret_cast<const uint4*>(src + row0 + t * tok_stride + j8)
+                            : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+        const int idx = threadIdx.x + n * kPrepThreads;
         const int t = idx / (D / 8), j8 = (idx % (D / 8)) * 8;
         float f[8];
-        if (t < nvalid) {
-            Vec16<__nv_bfloat16>::unpack(
-                *reinterpret_cast<const uint4*>(src + row0 + t * tok_stride + j8), f);
-        } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = 0.0f;
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) dst[t * PP + j8 + e] = f[e];
+        Vec16<__nv_bfloat16>::unpack(raw[n], f);
+        const float4 lo = make_float4(f[0], f[1], f[2], f[3]), hi = make_float4(f[4], f[5], f[6], f[7]);
+        st4(dst + t * PP + j8, lo);
+        st4(dst + t * PP + j8 + 4, hi);
         if (gcopy != nullptr) {
-            *reinterpret_cast<float4*>(gcopy + t * D + j8) = make_float4(f[0], f[1], f[2], f[3]);
-            *reinterpret_cast<float4*>(gcopy + t * D + j8 + 4) =
-                make_float4(f[4], f[5], f[6], f[7]);
+            st4(gcopy + t * D + j8, lo);
+            st4(gcopy + t * D + j8 + 4, hi);
         }
     }
 }
 
-// Gs = K K^T (all entries), Ms = tril(Q K^T) with the diagonal.
+// out[j][t] = scale * src[t][j] for a [C][PP] tile (out is [D][C]); each
+// store instruction is coalesced over t.
+static __device__ __forceinline__ void store_transposed(float* out, const float* src,
+                                                        float scale) {
+    for (int idx = threadIdx.x; idx < C * (D / 4); idx += blockDim.x) {
+        const int t = idx % C, j4 = (idx / C) * 4;
+        const float4 f = ld4(src + t * PP + j4);
+        out[(j4 + 0) * C + t] = scale * f.x;
+        out[(j4 + 1) * C + t] = scale * f.y;
+        out[(j4 + 2) * C + t] = scale * f.z;
+        out[(j4 + 3) * C + t] = scale * f.w;
+    }
+}
+
+// Gs = K K^T (every entry), Ms = tril(Q K^T) with the diagonal.
 static __device__ __forceinline__ void prep_products(const float* Ks, const float* Qs, float* Gs,
                                                      float* Ms) {
-    const int t = threadIdx.x >> 2, sl = threadIdx.x & 3;
-    float g[16], m[16];
+    const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+    float g[4][4], m[4][4];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) g[e] = m[e] = 0.0f;
-    for (int j = 0; j < D; ++j) {
-        const float kt = Ks[t * PP + j], qt = Qs[t * PP + j];
+    for (int r = 0; r < 4; ++r)
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-            const float ks = Ks[(sl + 4 * e) * PP + j];
-            g[e] = fmaf(kt, ks, g[e]);
-            m[e] = fmaf(qt, ks, m[e]);
+        for (int c = 0; c < 4; ++c) g[r][c] = m[r][c] = 0.0f;
+    for (int j = 0; j < D; j += 4) {
+        float4 kt[4], qt[4], ks[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            kt[r] = ld4(Ks + (ty + 16 * r) * PP + j);
+            qt[r] = ld4(Qs + (ty + 16 * r) * PP + j);
         }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) ks[c] = ld4(Ks + (tx + 16 * c) * PP + j);
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                g[r][c] = dot4(kt[r], ks[c], g[r][c]);
+                m[r][c] = dot4(qt[r], ks[c], m[r][c]);
+            }
     }
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-        const int s = sl + 4 * e;
-        Gs[t * PC + s] = g[e];
-        Ms[t * PC + s] = s <= t ? m[e] : 0.0f;
-    }
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int t = ty + 16 * r, s = tx + 16 * c;
+            Gs[t * PC + s] = g[r][c];
+            Ms[t * PC + s] = s <= t ? m[r][c] : 0.0f;
+        }
 }
 
-// Tm = (I + A)^-1 with A = tril(diag(beta) Gs, -1): forward substitution, one
-// column per thread (threads 0..C-1).  Caller syncs before and after.
-static __device__ __forceinline__ void prep_solve(const float* Gs, const float* bs, float* Tm) {
+// Tm = (I + A)^-1 with A = tril(diag(beta) Gs, -1).  ATn ([C][C], stride C)
+// is scratch.  Right-looking substitution: thread j < C holds column j in
+// registers; once row s is final it is folded into every later row, so the
+// critical path is one FMA per row.  Caller syncs before; syncs inside.
+static __device__ __forceinline__ void prep_solve(const float* Gs, const float* bs, float* ATn,
+                                                  float* Tm) {
+    for (int idx = threadIdx.x; idx < C * C; idx += blockDim.x) {
+        const int s = idx / C, r = idx % C;  // ATn[s][r] = -A[r][s]
+        ATn[idx] = s < r ? -bs[r] * Gs[r * PC + s] : 0.0f;
+    }
+    __syncthreads();
     if (threadIdx.x < C) {
         const int j = threadIdx.x;
-        for (int t = 0; t < C; ++t) {
-            float acc = (t == j) ? 1.0f : 0.0f;
-            const float bt = bs[t];
-            for (int s = j; s < t; ++s) acc = fmaf(-bt * Gs[t * PC + s], Tm[s * PC + j], acc);
-            Tm[t * PC + j] = t >= j ? acc : 0.0f;
+        float acc[C];
+#pragma unroll
+        for (int r = 0; r < C; ++r) acc[r] = (r == j) ? 1.0f : 0.0f;
+#pragma unroll
+        for (int s = 0; s < C - 1; ++s) {
+            const float xs = acc[s];
+#pragma unroll
+            for (int r = (s + 1) & ~3; r < C; r += 4) {  // lanes r <= s add 0
+                const float4 a = ld4(ATn + s * C + r);
+                acc[r] = fmaf(a.x, xs, acc[r]);
+                acc[r + 1] = fmaf(a.y, xs, acc[r + 1]);
+                acc[r + 2] = fmaf(a.z, xs, acc[r + 2]);
+                acc[r + 3] = fmaf(a.w, xs, acc[r + 3]);
+            }
         }
+#pragma unroll
+        for (int r = 0; r < C; ++r) Tm[r * PC + j] = acc[r];
+    }
+    __syncthreads();
+}
+
+// out = (T diag(beta) X) for this thread's rows ty + 16 r and columns
+// 4 tx + 64 c + e: out[r][4 c + e].  T is lower triangular, so row t only
+// needs s <= t.
+static __device__ __forceinline__ void prep_apply_tb(const float* Tm, const float* bs,
+                                                     const float* Xs, float (&out)[4][8]) {
+    const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) out[r][e] = 0.0f;
+    for (int s = 0; s <= ty + 48; ++s) {
+        float tb[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) tb[r] = Tm[(ty + 16 * r) * PC + s] * bs[s];
+        const float4 x0 = ld4(Xs + s * PP + 4 * tx), x1 = ld4(Xs + s * PP + 64 + 4 * tx);
+        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) out[r][e] = fmaf(tb[r], xv[e], out[r][e]);
     }
 }
 
-// out[e] = (T diag(beta) X)[t][jl + 4 e] for thread (t = tid / 4, jl = tid % 4).
-static __device__ __forceinline__ void prep_apply_tb(const float* Tm, const float* bs,
-                                                     const float* Xs, float (&out)[32]) {
-    const int t = threadIdx.x >> 2, jl = threadIdx.x & 3;
+// Writes a thread's [4][8] C x D tile (rows ty + 16 r, columns 4 tx + 64 c + e)
+// into a [C][PP] shared tile, times scale.
+static __device__ __forceinline__ void put_tile(float* dst, const float (&v)[4][8], float scale) {
+    const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
 #pragma unroll
-    for (int e = 0; e < 32; ++e) out[e] = 0.0f;
-    for (int s = 0; s <= t; ++s) {
-        const float tb = Tm[t * PC + s] * bs[s];
+    for (int r = 0; r < 4; ++r)
 #pragma unroll
-        for (int e = 0; e < 32; ++e) out[e] = fmaf(tb, Xs[s * PP + jl + 4 * e], out[e]);
-    }
+        for (int c = 0; c < 2; ++c)
+            st4(dst + (ty + 16 * r) * PP + 64 * c + 4 * tx,
+                make_float4(scale * v[r][4 * c], scale * v[r][4 * c + 1],
+                            scale * v[r][4 * c + 2], scale * v[r][4 * c + 3]));
 }
 
 }  // namespace dchunk

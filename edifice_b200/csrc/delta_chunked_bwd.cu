@@ -26,8 +26,9 @@
 //   delta_post1_kernel      per chunk, tcgen05: the products with S_0 / dS_C,
 //                           (dO S_0)^T, (dU~ S_0)^T, (U~ dS_C)^T (M=128, N=64,
 //                           K=128) and dO U~^T (M=64); operands by TMA.
-//   delta_post2_kernel      per chunk, SIMT f32: the C x C chain (dT_b, dA,
-//                           dbeta) and the final dQ, dK, dV (bf16).
+//   delta_post2_kernel      (delta_chunked_post.cu) per chunk, SIMT f32: the
+//                           C x C chain (dT_b, dA, dbeta) and the final dQ, dK,
+//                           dV (bf16).
 #include <math.h>
 
 #include "delta_chunked.cuh"
@@ -71,7 +72,7 @@ BwdScratch carve_bwd(void* ws, long long nch) {
 }
 
 // ------------------------------------------------------------------ prep
-constexpr size_t kPrepSmem = (size_t)(3 * C * PP + 3 * C * PC + C) * sizeof(float);
+constexpr size_t kPrepSmem = (size_t)(3 * C * PP + 3 * C * PC + C * C + C) * sizeof(float);
 
 __global__ void __launch_bounds__(kPrepThreads, 1)
     delta_prep_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
@@ -85,7 +86,8 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
     float* Gs = dOs + C * PP;    // [C][PC]  K K^T
     float* Ms = Gs + C * PC;     // [C][PC]  tril(Q K^T)
     float* Tm = Ms + C * PC;     // [C][PC]  T
-    float* bs = Tm + C * PC;     // [C]
+    float* ATn = Tm + C * PC;    // [C][C]   solve scratch
+    float* bs = ATn + C * C;     // [C]
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x;
     const long long ch = ((long long)b * H + h) * NC + c;
@@ -99,32 +101,23 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
         bs[tid] = tid < nvalid ? __bfloat162float(beta[((long long)b * L + t0 + tid) * H + h])
                                : 0.0f;
     __syncthreads();
-    for (int idx = tid; idx < D * C; idx += kPrepThreads) {  // transposes, coalesced over t
-        const int j = idx / C, t = idx % C;
-        ws.dOT[ch * D * C + idx] = dOs[t * PP + j];
-        ws.QT[ch * D * C + idx] = Qs[t * PP + j];
-    }
+    store_transposed(ws.dOT + ch * D * C, dOs, 1.0f);
+    store_transposed(ws.QT + ch * D * C, Qs, 1.0f);
     prep_products(Ks, Qs, Gs, Ms);
     __syncthreads();
     for (int idx = tid; idx < C * C; idx += kPrepThreads) {
         ws.G[ch * C * C + idx] = Gs[idx / C * PC + idx % C];
         ws.MT[ch * C * C + idx] = Ms[(idx % C) * PC + idx / C];  // MT[s][t] = M[t][s]
     }
-    prep_solve(Gs, bs, Tm);
-    __syncthreads();
+    prep_solve(Gs, bs, ATn, Tm);
     for (int idx = tid; idx < C * C; idx += kPrepThreads)
         ws.T[ch * C * C + idx] = Tm[idx / C * PC + idx % C];
-    {
-        const int t = tid >> 2, jl = tid & 3;
-        float w[32];
-        prep_apply_tb(Tm, bs, Ks, w);
-        // Q rows were last read by the transposes and products (both before a barrier)
-#pragma unroll
-        for (int e = 0; e < 32; ++e) Qs[t * PP + jl + 4 * e] = -w[e];
-    }
+    float w[4][8];
+    prep_apply_tb(Tm, bs, Ks, w);
+    // Q rows were last read before the barriers inside prep_solve
+    put_tile(Qs, w, 1.0f);
     __syncthreads();
-    for (int idx = tid; idx < D * C; idx += kPrepThreads)  // -W^T: [j][t]
-        ws.WnT[ch * D * C + idx] = Qs[(idx % C) * PP + idx / C];
+    store_transposed(ws.WnT + ch * D * C, Qs, -1.0f);  // -W^T: [j][t]
 }
 
 // ------------------------------------------------------------------ state bwd
@@ -358,16 +351,25 @@ __global__ void __launch_bounds__(128, 1)
         }
     }
     // dO rows (bf16) -> f32 K-major SW128 tile [C][D]
-    for (int idx = tid; idx < C * (D / 4); idx += 128) {
-        const int t = idx / (D / 4), k4 = (idx % (D / 4)) * 4;
-        float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t < nvalid) {
-            const uint2 raw = *reinterpret_cast<const uint2*>(
-                dO + (((long long)b * L + t0 + t) * H + h) * D + k4);
-            f = make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u),
-                            __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xffff0000u));
+    {
+        constexpr int N = C * (D / 4) / 128;  // every load issued before the first store
+        uint2 raw[N];
+#pragma unroll
+        for (int n = 0; n < N; ++n) {
+            const int idx = tid + n * 128, t = idx / (D / 4), k4 = (idx % (D / 4)) * 4;
+            raw[n] = t < nvalid ? *reinterpret_cast<const uint2*>(
+                                      dO + (((long long)b * L + t0 + t) * H + h) * D + k4)
+                                : make_uint2(0u, 0u);
         }
-        *reinterpret_cast<float4*>(smem + P1_DO + kmaj_off4(t, k4, C)) = f;
+#pragma unroll
+        for (int n = 0; n < N; ++n) {
+            const int idx = tid + n * 128, t = idx / (D / 4), k4 = (idx % (D / 4)) * 4;
+            *reinterpret_cast<float4*>(smem + P1_DO + kmaj_off4(t, k4, C)) =
+                make_float4(__uint_as_float(raw[n].x << 16),
+                            __uint_as_float(raw[n].x & 0xffff0000u),
+                            __uint_as_float(raw[n].y << 16),
+                            __uint_as_float(raw[n].y & 0xffff0000u));
+        }
     }
     fence_proxy_async();
     tc::fence_before_sync();
@@ -429,301 +431,14 @@ __global__ void __launch_bounds__(128, 1)
     }
 }
 
-// ------------------------------------------------------------------ post2
-// 256 threads; output tiles of 4 rows (ty + 16 r) x NC2 columns (tx + 16 c).
-constexpr int kPost2Threads = 256;
-constexpr size_t kPost2Smem = (size_t)(4 * C * PP + 4 * C * PC + 2 * C) * sizeof(float);
-
-template <int R, int CN, class F>
-static __device__ __forceinline__ void mm_acc(float (&acc)[R][CN], int k0, int k1, F f) {
-    const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
-    for (int kq = k0; kq < k1; ++kq) f(acc, ty, tx, kq);
-}
-
-static __device__ __forceinline__ void load_rows_f32(float* dst, const float* src, int ld_dst) {
-    for (int idx = threadIdx.x; idx < C * (D / 4); idx += kPost2Threads) {
-        const int t = idx / (D / 4), j4 = (idx % (D / 4)) * 4;
-        const float4 f = *reinterpret_cast<const float4*>(src + t * D + j4);
-        dst[t * ld_dst + j4] = f.x;
-        dst[t * ld_dst + j4 + 1] = f.y;
-        dst[t * ld_dst + j4 + 2] = f.z;
-        dst[t * ld_dst + j4 + 3] = f.w;
-    }
-}
-
-static __device__ __forceinline__ void load_cc(float* dst, const float* src) {
-    for (int idx = threadIdx.x; idx < C * C; idx += kPost2Threads)
-        dst[(idx / C) * PC + idx % C] = src[idx];
-}
-
-__global__ void __launch_bounds__(kPost2Threads, 1)
-    delta_post2_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
-                       const __nv_bfloat16* __restrict__ v, const __nv_bfloat16* __restrict__ beta,
-                       const float* __restrict__ dQa, const float* __restrict__ dWg,
-                       const float* __restrict__ dK1, const float* __restrict__ dMg,
-                       const float* __restrict__ Tg, const float* __restrict__ Gg,
-                       const float* __restrict__ dUg, __nv_bfloat16* __restrict__ gq,
-                       __nv_bfloat16* __restrict__ gk, __nv_bfloat16* __restrict__ gv,
-                       __nv_bfloat16* __restrict__ gbeta, int L, int H, int NC) {
-    extern __shared__ float sm[];
-    float* Ks = sm;                // [C][PP]  K
-    float* Ws = Ks + C * PP;       // [C][PP]  dW
-    float* Us = Ws + C * PP;       // [C][PP]  dU~, then Q
-    float* Vs = Us + C * PP;       // [C][PP]  V
-    float* dMs = Vs + C * PP;      // [C][PC]  dM
-    float* Ts = dMs + C * PC;      // [C][PC]  T
-    float* Xa = Ts + C * PC;       // [C][PC]  dT_b -> dT -> dA
-    float* Xb = Xa + C * PC;       // [C][PC]  X = T^T dT -> E = dG + dG^T
-    float* bs = Xb + C * PC;       // [C]
-    float* dbs = bs + C;           // [C]
-    const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-    const int tid = threadIdx.x;
-    const long long ch = ((long long)b * H + h) * NC + c;
-    const int t0 = c * C, nvalid = min(C, L - t0);
-    const long long ts = (long long)H * D;
-    const long long row0 = (((long long)b * L + t0) * H + h) * D;
-    const int ty = tid >> 4, tx = tid & 15;
-
-    // K, V (bf16 -> f32), dW, dU~, dM, T, beta
-    for (int idx = tid; idx < C * (D / 8); idx += kPost2Threads) {
-        const int t = idx / (D / 8), j8 = (idx % (D / 8)) * 8;
-        float kf[8], vf[8];
-        if (t < nvalid) {
-            Vec16<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(k + row0 + t * ts + j8), kf);
-            Vec16<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(v + row0 + t * ts + j8), vf);
-        } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) kf[e] = vf[e] = 0.0f;
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            Ks[t * PP + j8 + e] = kf[e];
-            Vs[t * PP + j8 + e] = vf[e];
-        }
-    }
-    load_rows_f32(Ws, dWg + ch * C * D, PP);
-    load_rows_f32(Us, dUg + ch * C * D, PP);
-    load_cc(dMs, dMg + ch * C * C);
-    load_cc(Ts, Tg + ch * C * C);
-    if (tid < C)
-        bs[tid] = tid < nvalid ? __bfloat162float(beta[((long long)b * L + t0 + tid) * H + h])
-                               : 0.0f;
-    __syncthreads();
-
-    // dQ = dO S_0 + dM K ;  dV = T_b^T dU~   (64 x 128 each)
-    {
-        float aq[4][8], av[4][8];
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc) aq[r][cc] = av[r][cc] = 0.0f;
-        for (int s = 0; s < C; ++s) {
-            float am[4], at[4], bk[8], bu[8];
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const int row = ty + 16 * r;
-                am[r] = dMs[row * PC + s];                 // dM[row][s]
-                at[r] = Ts[s * PC + row] * bs[row];        // T_b[s][row]
-            }
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc) {
-                bk[cc] = Ks[s * PP + tx + 16 * cc];
-                bu[cc] = Us[s * PP + tx + 16 * cc];
-            }
-#pragma unroll
-            for (int r = 0; r < 4; ++r)
-#pragma unroll
-                for (int cc = 0; cc < 8; ++cc) {
-                    aq[r][cc] = fmaf(am[r], bk[cc], aq[r][cc]);
-                    av[r][cc] = fmaf(at[r], bu[cc], av[r][cc]);
-                }
-        }
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int row = ty + 16 * r;
-            if (row < nvalid) {
-#pragma unroll
-                for (int cc = 0; cc < 8; ++cc) {
-                    const int col = tx + 16 * cc;
-                    gq[row0 + row * ts + col] =
-                        __float2bfloat16(aq[r][cc] + dQa[(ch * C + row) * D + col]);
-                    gv[row0 + row * ts + col] = __float2bfloat16(av[r][cc]);
-                }
-            }
-        }
-    }
-    // dT_b = dW K^T + dU~ V^T   (64 x 64)
-    {
-        float a[4][4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) a[r][cc] = 0.0f;
-        for (int j = 0; j < D; ++j) {
-            float aw[4], au[4], bk[4], bv[4];
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                aw[r] = Ws[(ty + 16 * r) * PP + j];
-                au[r] = Us[(ty + 16 * r) * PP + j];
-            }
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                bk[cc] = Ks[(tx + 16 * cc) * PP + j];
-                bv[cc] = Vs[(tx + 16 * cc) * PP + j];
-            }
-#pragma unroll
-            for (int r = 0; r < 4; ++r)
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc)
-                    a[r][cc] = fmaf(aw[r], bk[cc], fmaf(au[r], bv[cc], a[r][cc]));
-        }
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) Xa[(ty + 16 * r) * PC + tx + 16 * cc] = a[r][cc];
-    }
-    __syncthreads();
-    // dbeta (from T_b) and dT = dT_b diag(beta)
-    if (tid < C) {
-        const int s = tid;
-        float acc = 0.0f;
-        for (int t = s; t < C; ++t) acc = fmaf(Xa[t * PC + s], Ts[t * PC + s], acc);
-        dbs[s] = acc;
-    }
-    __syncthreads();
-    for (int idx = tid; idx < C * C; idx += kPost2Threads) {
-        const int t = idx / C, s = idx % C;
-        Xa[t * PC + s] *= bs[s];
-    }
-    __syncthreads();
-    // X = T^T dT
-    {
-        float a[4][4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) a[r][cc] = 0.0f;
-        for (int t = 0; t < C; ++t) {
-            float at[4], bd[4];
-#pragma unroll
-            for (int r = 0; r < 4; ++r) at[r] = Ts[t * PC + ty + 16 * r];
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) bd[cc] = Xa[t * PC + tx + 16 * cc];
-#pragma unroll
-            for (int r = 0; r < 4; ++r)
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc) a[r][cc] = fmaf(at[r], bd[cc], a[r][cc]);
-        }
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) Xb[(ty + 16 * r) * PC + tx + 16 * cc] = a[r][cc];
-    }
-    __syncthreads();
-    // dA = -X T^T, strictly lower
-    {
-        float a[4][4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) a[r][cc] = 0.0f;
-        for (int s = 0; s < C; ++s) {
-            float ax[4], bt[4];
-#pragma unroll
-            for (int r = 0; r < 4; ++r) ax[r] = Xb[(ty + 16 * r) * PC + s];
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) bt[cc] = Ts[(tx + 16 * cc) * PC + s];
-#pragma unroll
-            for (int r = 0; r < 4; ++r)
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc) a[r][cc] = fmaf(ax[r], bt[cc], a[r][cc]);
-        }
-        __syncthreads();  // all reads of Xa (dT) and Xb (X) are done
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                const int row = ty + 16 * r, col = tx + 16 * cc;
-                Xa[row * PC + col] = col < row ? -a[r][cc] : 0.0f;
-            }
-    }
-    __syncthreads();
-    // dbeta (from A) ; E = dG + dG^T with dG = diag(beta) dA
-    if (tid < C) {
-        const int t = tid;
-        const float* g = Gg + (ch * C + t) * C;
-        float acc = 0.0f;
-        for (int s = 0; s < t; ++s) acc = fmaf(Xa[t * PC + s], g[s], acc);
-        dbs[t] += acc;
-        if (t < nvalid) gbeta[((long long)b * L + t0 + t) * H + h] = __float2bfloat16(dbs[t]);
-    }
-    for (int idx = tid; idx < C * C; idx += kPost2Threads) {
-        const int t = idx / C, s = idx % C;
-        Xb[t * PC + s] = bs[t] * Xa[t * PC + s] + bs[s] * Xa[s * PC + t];
-    }
-    __syncthreads();
-    // Q replaces dU~
-    for (int idx = tid; idx < C * (D / 8); idx += kPost2Threads) {
-        const int t = idx / (D / 8), j8 = (idx % (D / 8)) * 8;
-        float qf[8];
-        if (t < nvalid) {
-            Vec16<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(q + row0 + t * ts + j8), qf);
-        } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) qf[e] = 0.0f;
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) Us[t * PP + j8 + e] = qf[e];
-    }
-    __syncthreads();
-    // dK = U~ dS_C + dM^T Q + T_b^T dW + E K
-    {
-        float a[4][8];
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc) a[r][cc] = 0.0f;
-        for (int t = 0; t < C; ++t) {
-            float am[4], at[4], ae[4], bq[8], bw[8], bk[8];
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const int s = ty + 16 * r;
-                am[r] = dMs[t * PC + s];
-                at[r] = Ts[t * PC + s] * bs[s];
-                ae[r] = Xb[t * PC + s];
-            }
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc) {
-                const int col = tx + 16 * cc;
-                bq[cc] = Us[t * PP + col];
-                bw[cc] = Ws[t * PP + col];
-                bk[cc] = Ks[t * PP + col];
-            }
-#pragma unroll
-            for (int r = 0; r < 4; ++r)
-#pragma unroll
-                for (int cc = 0; cc < 8; ++cc)
-                    a[r][cc] = fmaf(am[r], bq[cc],
-                                    fmaf(at[r], bw[cc], fmaf(ae[r], bk[cc], a[r][cc])));
-        }
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int row = ty + 16 * r;
-            if (row < nvalid) {
-#pragma unroll
-                for (int cc = 0; cc < 8; ++cc) {
-                    const int col = tx + 16 * cc;
-                    gk[row0 + row * ts + col] =
-                        __float2bfloat16(a[r][cc] + dK1[(ch * C + row) * D + col]);
-                }
-            }
-        }
-    }
-}
-
 }  // namespace
 
 // ---------------------------------------------------------------- library-internal
+int edb_delta_chunked_post2(const void* q, const void* k, const void* v, const void* beta,
+                            const float* dQa, const float* dW, const float* dK1, const float* dM,
+                            const float* T, const float* G, const float* dU, void* gq, void* gk,
+                            void* gv, void* gbeta, int B, int L, int H, cudaStream_t st);
+
 size_t edb_delta_chunked_bwd_ws(int B, int L, int H) {
     return bwd_scratch_bytes((long long)B * H * ((L + C - 1) / C));
 }
@@ -779,11 +494,6 @@ int edb_delta_chunked_bwd(const void* q, const void* k, const void* v, const voi
                                                              err);
     if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
 
-    if ((e = cudaFuncSetAttribute(delta_post2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)kPost2Smem)) != cudaSuccess)
-        return (int)e;
-    delta_post2_kernel<<<dim3(NC, H, B), kPost2Threads, kPost2Smem, st>>>(
-        qb, kb, vb, bb, dQa, dW, dK1, dM, w.T, w.G, w.dU, (__nv_bfloat16*)gq, (__nv_bfloat16*)gk,
-        (__nv_bfloat16*)gv, (__nv_bfloat16*)gbeta, L, H, NC);
-    return edb::status_from_cuda(cudaGetLastError());
+    return edb_delta_chunked_post2(q, k, v, beta, dQa, dW, dK1, dM, w.T, w.G, w.dU, gq, gk, gv,
+                                   gbeta, B, L, H, st);
 }
