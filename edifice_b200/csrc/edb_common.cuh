@@ -105,6 +105,22 @@ static __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap*
         : "memory");
 }
 
+// 16-byte asynchronous copy global -> shared (cp.async.cg); src_bytes < 16
+// zero-fills the rest (0: nothing is read, the whole 16 bytes become zero).
+static __device__ __forceinline__ void cp_async16(void* dst, const void* src, unsigned src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(src_bytes)
+                 : "memory");
+}
+static __device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// Wait until at most `PENDING` of this thread's committed groups are in flight.
+template <int PENDING>
+static __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(PENDING) : "memory");
+}
+
 static __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

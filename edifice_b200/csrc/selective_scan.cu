@@ -314,6 +314,348 @@ __global__ void ssm_reduce_kernel(const float* __restrict__ gpart, float* __rest
     gC[i] = sc;
 }
 
+// ------------------------------------------------------------------ staged kernels
+// The same recurrences with every per-step read of x / dt (/ dy) served from
+// shared memory: [steps][128 channels] tiles arrive by 16-byte cp.async
+// (zero-filled past L and D), so a step never waits on HBM latency.  Used when
+// D is a multiple of 16 / sizeof(T) and x, dt (, dy) are 16-byte aligned.
+template <typename T>
+struct StageGeom {
+    static constexpr int ROWB = kThreads * (int)sizeof(T);  // bytes of one tile row
+    static constexpr int CPR = ROWB / 16;                    // 16-byte copies per row
+    static constexpr int EPC = 16 / (int)sizeof(T);          // elements per copy
+};
+
+// Copies rows t0 .. t0 + rows - 1, channels d0 .. d0 + 127 of a [B*L][D]
+// array (row0 = b * L) into dst[rows][128].
+template <typename T, int ROWS>
+static __device__ __forceinline__ void stage_rows(unsigned char* dst, const T* src, long long row0,
+                                                  int t0, int L, int d0, int D) {
+    using G = StageGeom<T>;
+    constexpr int CPT = ROWS * G::CPR / kThreads;
+#pragma unroll
+    for (int i = 0; i < CPT; ++i) {
+        const int idx = threadIdx.x + i * kThreads;
+        const int r = idx / G::CPR, c16 = idx % G::CPR;
+        const int t = t0 + r, dd = d0 + c16 * G::EPC;
+        const bool ok = t < L && dd < D;
+        cp_async16(dst + r * G::ROWB + c16 * 16, src + (ok ? (row0 + t) * D + dd : 0),
+                   ok ? 16u : 0u);
+    }
+}
+
+// grid (ceil(D/128), B), block 128; two x/dt tiles of TB steps in flight.
+template <typename T, int NS, bool STATES_ONLY>
+__global__ void __launch_bounds__(kThreads)
+    ssm_fwd_staged_kernel(const T* __restrict__ x, const T* __restrict__ dt,
+                          const T* __restrict__ A, const T* __restrict__ Bm,
+                          const T* __restrict__ Cm, T* __restrict__ y, float* __restrict__ ckpt,
+                          int L, int D, int N, float dt_min, float dt_max) {
+    constexpr int TB = 32;
+    constexpr int CK = SsmTiling<NS>::CK;
+    static_assert(CK % TB == 0, "checkpoints fall on tile starts");
+    constexpr int TILEB = TB * StageGeom<T>::ROWB;
+    constexpr int BCV = TB * NS / kThreads;  // B (and C) values per thread and tile
+    extern __shared__ __align__(16) unsigned char smem[];
+    unsigned char* sX = smem;                                 // [2][TB][128] T
+    unsigned char* sDt = smem + 2 * TILEB;                    // [2][TB][128] T
+    float* sB = reinterpret_cast<float*>(smem + 4 * TILEB);  // [2][TB][NS]
+    float* sC = sB + 2 * TB * NS;                             // [2][TB][NS]
+    const int tid = threadIdx.x;
+    const int d0 = blockIdx.x * kThreads, d = d0 + tid;
+    const int b = blockIdx.y;
+    const bool live = d < D;
+    const int nck = (L + CK - 1) / CK;
+    const int ntiles = (L + TB - 1) / TB;
+    const long long row0 = (long long)b * L;
+
+    float A2[NS], h[NS];
+#pragma unroll
+    for (int n = 0; n < NS; ++n) {
+        A2[n] = (live && n < N) ? ldf(A + (long long)d * N + n) * kLog2e : 0.0f;
+        h[n] = 0.0f;
+    }
+    float rb[BCV], rc[BCV];
+    auto load_bc = [&](int k) {
+#pragma unroll
+        for (int v = 0; v < BCV; ++v) {
+            const int idx = tid + v * kThreads, tt = idx / NS, n = idx % NS;
+            const int t = k * TB + tt;
+            const bool ok = t < L && n < N;
+            const long long o = (row0 + (ok ? t : 0)) * N + (ok ? n : 0);
+            rb[v] = ok ? ldf(Bm + o) : 0.0f;
+            rc[v] = (ok && !STATES_ONLY) ? ldf(Cm + o) : 0.0f;
+        }
+    };
+    auto store_bc = [&](int k) {
+#pragma unroll
+        for (int v = 0; v < BCV; ++v) {
+            sB[(k & 1) * TB * NS + tid + v * kThreads] = rb[v];
+            sC[(k & 1) * TB * NS + tid + v * kThreads] = rc[v];
+        }
+    };
+    auto issue = [&](int k) {
+        stage_rows<T, TB>(sX + (k & 1) * TILEB, x, row0, k * TB, L, d0, D);
+        stage_rows<T, TB>(sDt + (k & 1) * TILEB, dt, row0, k * TB, L, d0, D);
+        cp_async_commit();
+    };
+    issue(0);
+    load_bc(0);
+    store_bc(0);
+    for (int k = 0; k < ntiles; ++k) {
+        if (k + 1 < ntiles) {
+            issue(k + 1);
+            load_bc(k + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        if (live) {
+            const T* xs = reinterpret_cast<const T*>(sX + (k & 1) * TILEB) + tid;
+            const T* dts = reinterpret_cast<const T*>(sDt + (k & 1) * TILEB) + tid;
+            const float* bk = sB + (k & 1) * TB * NS;
+            const float* ckc = sC + (k & 1) * TB * NS;
+            const int t0 = k * TB, tn = min(TB, L - t0);
+            if (ckpt != nullptr && t0 % CK == 0) {
+                float* cp = ckpt + (((long long)b * nck + t0 / CK) * D + d) * NS;
+#pragma unroll
+                for (int n = 0; n < NS; n += 4)
+                    *reinterpret_cast<float4*>(cp + n) = make_float4(h[n], h[n + 1], h[n + 2], h[n + 3]);
+            }
+            for (int tt = 0; tt < tn; ++tt) {
+                const float dtc = fminf(fmaxf(ldf(dts + tt * kThreads), dt_min), dt_max);
+                const float dtx = dtc * ldf(xs + tt * kThreads);
+                float acc = 0.0f;
+#pragma unroll
+                for (int n = 0; n < NS; n += 4) {
+                    const float4 b4 = *reinterpret_cast<const float4*>(bk + tt * NS + n);
+                    const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+                    float cv[4] = {0.f, 0.f, 0.f, 0.f};
+                    if (!STATES_ONLY) {
+                        const float4 c4 = *reinterpret_cast<const float4*>(ckc + tt * NS + n);
+                        cv[0] = c4.x;
+                        cv[1] = c4.y;
+                        cv[2] = c4.z;
+                        cv[3] = c4.w;
+                    }
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        h[n + e] = fmaf(ex2(dtc * A2[n + e]), h[n + e], dtx * bv[e]);
+                        if (!STATES_ONLY) acc = fmaf(cv[e], h[n + e], acc);
+                    }
+                }
+                if (!STATES_ONLY) st_scalar<T>(y + (row0 + t0 + tt) * D + d, acc);
+            }
+        }
+        if (k + 1 < ntiles) store_bc(k + 1);
+        __syncthreads();
+    }
+}
+
+template <typename T, int NS>
+constexpr size_t fwd_staged_smem() {
+    return (size_t)4 * 32 * StageGeom<T>::ROWB + (size_t)4 * 32 * NS * sizeof(float);
+}
+
+// grid (ceil(D/128), B), block 128: ssm_bwd_kernel with the chunk's x, dt, dy
+// rows staged in shared memory (one chunk at a time; two CTAs share an SM).
+template <typename T, int NS>
+__global__ void __launch_bounds__(kThreads)
+    ssm_bwd_staged_kernel(const T* __restrict__ x, const T* __restrict__ dt,
+                          const T* __restrict__ A, const T* __restrict__ Bm,
+                          const T* __restrict__ Cm, const T* __restrict__ dy,
+                          const float* __restrict__ ckpt, T* __restrict__ gx, T* __restrict__ gdt,
+                          float* __restrict__ gpart, int Bsz, int L, int D, int N, float dt_min,
+                          float dt_max) {
+    constexpr int TS = SsmTiling<NS>::TS;
+    constexpr int CK = SsmTiling<NS>::CK;
+    constexpr int SUBS = CK / TS;
+    constexpr int V = 2 * NS;
+    static_assert(V <= 32, "NS <= 16 in this kernel");
+    constexpr int TILEB = CK * StageGeom<T>::ROWB;
+    constexpr int BCV = CK * NS / kThreads;
+    extern __shared__ __align__(16) unsigned char smem[];
+    auto sSub = reinterpret_cast<float(*)[NS][kThreads]>(smem);  // [SUBS][NS][128]
+    unsigned char* tiles = smem + SUBS * NS * kThreads * sizeof(float);  // x | dt | dy
+    float* sB = reinterpret_cast<float*>(tiles + 3 * TILEB);             // [CK][NS]
+    float* sC = sB + CK * NS;                                             // [CK][NS]
+    auto sRed = reinterpret_cast<float(*)[TS][32]>(sC + CK * NS);        // [4][TS][32]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int d0 = blockIdx.x * kThreads, d = d0 + tid;
+    const int b = blockIdx.y;
+    const bool live = d < D;
+    const int nck = (L + CK - 1) / CK;
+    const int nblk = gridDim.x;
+    const long long row0 = (long long)b * L;
+    const T* sx = reinterpret_cast<const T*>(tiles) + tid;
+    const T* sdt = reinterpret_cast<const T*>(tiles + TILEB) + tid;
+    const T* sdy = reinterpret_cast<const T*>(tiles + 2 * TILEB) + tid;
+
+    float A2[NS], A2ln[NS], dh[NS];
+#pragma unroll
+    for (int n = 0; n < NS; ++n) {
+        A2[n] = (live && n < N) ? ldf(A + (long long)d * N + n) * kLog2e : 0.0f;
+        A2ln[n] = A2[n] * kLn2;
+        dh[n] = 0.0f;
+    }
+    const int ridx = reduced_index<V>(lane);
+
+    for (int c = nck - 1; c >= 0; --c) {
+        const int t0 = c * CK;
+        const int tn = min(CK, L - t0);
+        __syncthreads();  // the previous chunk is done with the tiles
+        stage_rows<T, CK>(tiles, x, row0, t0, L, d0, D);
+        stage_rows<T, CK>(tiles + TILEB, dt, row0, t0, L, d0, D);
+        stage_rows<T, CK>(tiles + 2 * TILEB, dy, row0, t0, L, d0, D);
+        cp_async_commit();
+        {
+            float rb[BCV], rc[BCV];
+#pragma unroll
+            for (int v = 0; v < BCV; ++v) {
+                const int idx = tid + v * kThreads, tt = idx / NS, n = idx % NS;
+                const bool ok = tt < tn && n < N;
+                const long long o = (row0 + t0 + (ok ? tt : 0)) * N + (ok ? n : 0);
+                rb[v] = ok ? ldf(Bm + o) : 0.0f;
+                rc[v] = ok ? ldf(Cm + o) : 0.0f;
+            }
+#pragma unroll
+            for (int v = 0; v < BCV; ++v) {
+                sB[tid + v * kThreads] = rb[v];
+                sC[tid + v * kThreads] = rc[v];
+            }
+        }
+        float h[NS];
+        if (live) {
+            const float* cp = ckpt + (((long long)b * nck + c) * D + d) * NS;
+#pragma unroll
+            for (int n = 0; n < NS; n += 4) {
+                const float4 v4 = *reinterpret_cast<const float4*>(cp + n);
+                h[n] = v4.x;
+                h[n + 1] = v4.y;
+                h[n + 2] = v4.z;
+                h[n + 3] = v4.w;
+            }
+        } else {
+#pragma unroll
+            for (int n = 0; n < NS; ++n) h[n] = 0.0f;
+        }
+        cp_async_wait<0>();
+        __syncthreads();
+        // ---- sub-chunk start states
+        for (int tt = 0; tt < tn; ++tt) {
+            if (tt % TS == 0) {
+#pragma unroll
+                for (int n = 0; n < NS; ++n) sSub[tt / TS][n][tid] = h[n];
+            }
+            const float dtc = fminf(fmaxf(ldf(sdt + tt * kThreads), dt_min), dt_max);
+            const float dtx = dtc * ldf(sx + tt * kThreads);
+#pragma unroll
+            for (int n = 0; n < NS; n += 4) {
+                const float4 b4 = *reinterpret_cast<const float4*>(sB + tt * NS + n);
+                h[n] = fmaf(ex2(dtc * A2[n]), h[n], dtx * b4.x);
+                h[n + 1] = fmaf(ex2(dtc * A2[n + 1]), h[n + 1], dtx * b4.y);
+                h[n + 2] = fmaf(ex2(dtc * A2[n + 2]), h[n + 2], dtx * b4.z);
+                h[n + 3] = fmaf(ex2(dtc * A2[n + 3]), h[n + 3], dtx * b4.w);
+            }
+        }
+        // ---- sub-chunks in reverse: recompute h and exp(dt A) into registers,
+        // then walk back
+        const int nsub = (tn + TS - 1) / TS;
+        for (int s = nsub - 1; s >= 0; --s) {
+            const int u0 = s * TS;
+            const int un = min(TS, tn - u0);
+            float hs[TS][NS], as[TS][NS];
+#pragma unroll
+            for (int n = 0; n < NS; ++n) h[n] = sSub[s][n][tid];
+#pragma unroll
+            for (int j = 0; j < TS; ++j) {
+                const int tt = min(u0 + j, tn - 1);  // steps past tn are never read back
+                const float dtc = fminf(fmaxf(ldf(sdt + tt * kThreads), dt_min), dt_max);
+                const float dtx = dtc * ldf(sx + tt * kThreads);
+#pragma unroll
+                for (int n = 0; n < NS; n += 4) {
+                    const float4 b4 = *reinterpret_cast<const float4*>(sB + tt * NS + n);
+                    const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        as[j][n + e] = ex2(dtc * A2[n + e]);
+                        h[n + e] = fmaf(as[j][n + e], h[n + e], dtx * bv[e]);
+                        hs[j][n + e] = h[n + e];
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = TS - 1; j >= 0; --j) {
+                float red[V];
+                if (j < un && live) {
+                    const int tt = u0 + j;
+                    const float draw = ldf(sdt + tt * kThreads);
+                    const float dtc = fminf(fmaxf(draw, dt_min), dt_max);
+                    const float xv = ldf(sx + tt * kThreads);
+                    const float dyv = ldf(sdy + tt * kThreads);
+                    const float dtx = dtc * xv;
+                    float gxa = 0.0f, gda = 0.0f;
+#pragma unroll
+                    for (int n = 0; n < NS; n += 4) {
+                        const float4 b4 = *reinterpret_cast<const float4*>(sB + tt * NS + n);
+                        const float4 c4 = *reinterpret_cast<const float4*>(sC + tt * NS + n);
+                        const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+                        const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int m = n + e;
+                            const float hc = hs[j][m];
+                            const float dht = fmaf(dyv, cv[e], dh[m]);
+                            red[NS + m] = dyv * hc;
+                            red[m] = dht * dtx;
+                            gxa = fmaf(dht, bv[e], gxa);
+                            // d h_t / d dtc = A (a h_{t-1}) + B x, a h_{t-1} = h_t - dtc x B;
+                            // the B x part is summed once below (x gxa)
+                            gda = fmaf(dht * A2ln[m], fmaf(-dtx, bv[e], hc), gda);
+                            dh[m] = dht * as[j][m];
+                        }
+                    }
+                    gda = fmaf(xv, gxa, gda);
+                    const long long o = (row0 + t0 + tt) * D + d;
+                    st_scalar<T>(gx + o, gxa * dtc);
+                    const bool inr = draw >= dt_min && draw <= dt_max;
+                    st_scalar<T>(gdt + o, inr ? gda : 0.0f);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < V; ++i) red[i] = 0.0f;
+                }
+                const float r = warp_transpose_reduce<V>(red, lane);
+                if (lane < V) sRed[warp][j][ridx] = r;
+            }
+            __syncthreads();
+            for (int i = tid; i < TS * V; i += kThreads) {
+                const int j = i / V, vi = i % V;
+                if (j < un) {
+                    float sum = 0.0f;
+#pragma unroll
+                    for (int w = 0; w < kThreads / 32; ++w) sum += sRed[w][j][vi];
+                    const int which = vi >= NS;
+                    const int n = vi - which * NS;
+                    const long long o =
+                        ((((long long)which * nblk + blockIdx.x) * Bsz + b) * L + t0 + u0 + j) *
+                            NS + n;
+                    gpart[o] = sum;
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+template <typename T, int NS>
+constexpr size_t bwd_staged_smem() {
+    constexpr int TS = SsmTiling<NS>::TS, CK = SsmTiling<NS>::CK;
+    return (size_t)(CK / TS) * NS * kThreads * sizeof(float) +
+           (size_t)3 * CK * StageGeom<T>::ROWB + (size_t)2 * CK * NS * sizeof(float) +
+           (size_t)(kThreads / 32) * TS * 32 * sizeof(float);
+}
+
 int pad_states(int N) {
     if (N <= 8) return 8;
     if (N <= 16) return 16;
@@ -339,6 +681,17 @@ int launch_fwd(const void* x, const void* dt, const void* A, const void* Bm, con
                void* y, float* ckpt, int B, int L, int D, int N, float lo, float hi,
                bool states_only, cudaStream_t st) {
     dim3 grid((D + kThreads - 1) / kThreads, B);
+    if (D % StageGeom<T>::EPC == 0 && edb::aligned16(x) && edb::aligned16(dt)) {
+        constexpr size_t sm = fwd_staged_smem<T, NS>();
+        auto kern = states_only ? ssm_fwd_staged_kernel<T, NS, true>
+                                : ssm_fwd_staged_kernel<T, NS, false>;
+        cudaError_t ea =
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        if (ea != cudaSuccess) return (int)ea;
+        kern<<<grid, kThreads, sm, st>>>((const T*)x, (const T*)dt, (const T*)A, (const T*)Bm,
+                                         (const T*)Cm, (T*)y, ckpt, L, D, N, lo, hi);
+        return edb::status_from_cuda(cudaGetLastError());
+    }
     if (states_only)
         ssm_fwd_kernel<T, NS, true><<<grid, kThreads, 0, st>>>(
             (const T*)x, (const T*)dt, (const T*)A, (const T*)Bm, (const T*)Cm, (T*)y, ckpt, L, D,
@@ -356,14 +709,26 @@ int launch_bwd(const void* x, const void* dt, const void* A, const void* Bm, con
                float* gpart, int B, int L, int D, int N, float lo, float hi, cudaStream_t st) {
     const int nblk = (D + kThreads - 1) / kThreads;
     dim3 grid(nblk, B);
-    constexpr int SUBS = SsmTiling<NS>::CK / SsmTiling<NS>::TS;
-    const size_t dsmem = (size_t)SUBS * NS * kThreads * sizeof(float);
-    cudaError_t ea = cudaFuncSetAttribute(ssm_bwd_kernel<T, NS>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dsmem);
-    if (ea != cudaSuccess) return (int)ea;
-    ssm_bwd_kernel<T, NS><<<grid, kThreads, dsmem, st>>>(
-        (const T*)x, (const T*)dt, (const T*)A, (const T*)Bm, (const T*)Cm, (const T*)dy, ckpt,
-        (T*)gx, (T*)gdt, gpart, B, L, D, N, lo, hi);
+    if (D % StageGeom<T>::EPC == 0 && edb::aligned16(x) && edb::aligned16(dt) &&
+        edb::aligned16(dy)) {
+        constexpr size_t sm = bwd_staged_smem<T, NS>();
+        cudaError_t ea = cudaFuncSetAttribute(ssm_bwd_staged_kernel<T, NS>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        if (ea != cudaSuccess) return (int)ea;
+        ssm_bwd_staged_kernel<T, NS><<<grid, kThreads, sm, st>>>(
+            (const T*)x, (const T*)dt, (const T*)A, (const T*)Bm, (const T*)Cm, (const T*)dy,
+            ckpt, (T*)gx, (T*)gdt, gpart, B, L, D, N, lo, hi);
+    } else {
+        constexpr int SUBS = SsmTiling<NS>::CK / SsmTiling<NS>::TS;
+        const size_t dsmem = (size_t)SUBS * NS * kThreads * sizeof(float);
+        cudaError_t ea = cudaFuncSetAttribute(ssm_bwd_kernel<T, NS>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)dsmem);
+        if (ea != cudaSuccess) return (int)ea;
+        ssm_bwd_kernel<T, NS><<<grid, kThreads, dsmem, st>>>(
+            (const T*)x, (const T*)dt, (const T*)A, (const T*)Bm, (const T*)Cm, (const T*)dy,
+            ckpt, (T*)gx, (T*)gdt, gpart, B, L, D, N, lo, hi);
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return (int)e;
     const long long total = (long long)B * L * N;
