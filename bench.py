@@ -125,17 +125,28 @@ class ClockSampler:
                 "samples": len(inside), "window": "timed" if inside else "whole run"}
 
 
+# Special-function unit: 16 ex2 results per clock per SM (sm_100), 148 SMs,
+# clocks.max.sm 1965 MHz -> G ex2/s.  No measured figure exists for it.
+SFU_PEAK_GEXP = 16 * 148 * 1.965
+
+
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    sfu = (SFU_PEAK_GEXP, "nominal (16 ex2/clk/SM x 148 SMs x 1965 MHz clocks.max.sm)")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
         return {"hbm": (float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"),
                 "tensor": (float(d["bf16_tflops_sustained"]),
                            "measured (MEASURED_PEAKS.json bf16_tflops_sustained: the kernel runs "
-                           "back to back inside a seconds-long step loop)")}
+                           "back to back inside a seconds-long step loop)"),
+                "sfu": sfu}
     return {"hbm": (6650.0, "fallback (6.65 TB/s pool measurement)"),
-            "tensor": (1400.0, "fallback (1.4 PFLOP/s sustained pool measurement)")}
+            "tensor": (1400.0, "fallback (1.4 PFLOP/s sustained pool measurement)"), "sfu": sfu}
+
+
+# unit scale and name of each bound's rate
+RATE = {"hbm": (1e9, "GB/s"), "tensor": (1e12, "TFLOP/s"), "sfu": (1e9, "Gexp/s")}
 
 
 def ncu_traffic(kernel_key):
@@ -265,7 +276,9 @@ class SsmWorkload:
         self.x, self.dt, self.A, self.B, self.C, self.dy = shard.ssm_inputs(self.cfg, self.units, dev)
 
     def kernels(self):
-        return {"fwd": ("hbm", self.cfg.bytes_fwd()), "bwd": ("hbm", self.cfg.bytes_bwd())}
+        # exp-bound, not HBM-bound: one ex2 per (t, d, n) costs more SFU time
+        # (16/clk/SM) than the element's bytes cost HBM time
+        return {"fwd": ("sfu", self.cfg.exps_fwd()), "bwd": ("sfu", self.cfg.exps_bwd())}
 
     launches_per_step = 3  # fwd, bwd, dB/dC reduce
     tokens = property(lambda self: self.cfg.tokens)
@@ -293,10 +306,13 @@ class SsmWorkload:
     api = "edifice_b200.fused_scan.selective_scan + backward"
 
     def extra(self, fwd_ms, bwd_ms):
-        e = self.cfg.exps_fwd()
-        return {"fwd_exp_per_s": e / (fwd_ms / 1000.0),
-                "note": "exp-bound: one ex2 per (t,d,n) in the forward; the MUFU rate "
-                        "(16/clk/SM) caps the config-4 forward near 7.6 ms at 1.9 GHz"}
+        c = self.cfg
+        hbm_gbs = (c.bytes_fwd() + c.bytes_bwd()) / ((fwd_ms + bwd_ms) / 1e3) / 1e9
+        return {"hbm_GB/s_fwd+bwd": round(hbm_gbs, 1),
+                "hbm_frac_of_peak": round(hbm_gbs / measured_peaks()["hbm"][0], 4),
+                "note": "exp-bound, not HBM-bound: one ex2 per (t,d,n) in the forward and two "
+                        "in the recompute-not-store backward; the SFU rate (16/clk/SM) caps the "
+                        "config-4 forward near 7.4 ms at 1965 MHz"}
 
     def cpu_step(self, rows=None, prec="f32"):
         import numpy as np
@@ -421,9 +437,11 @@ class DeltaWorkload:
         self.q, self.k, self.v, self.beta, self.do = shard.delta_inputs(self.cfg, self.units, dev)
 
     def kernels(self):
-        return {"fwd": ("hbm", self.cfg.bytes_fwd()), "bwd": ("hbm", self.cfg.bytes_bwd())}
+        # dense chunked contractions: measured against the tensor peak
+        return {"fwd": ("tensor", self.cfg.flops_fwd()), "bwd": ("tensor", self.cfg.flops_bwd())}
 
-    launches_per_step = 2
+    # chunked path: prep + state (forward), prep + state + two post kernels (backward)
+    launches_per_step = 6
     tokens = property(lambda self: self.cfg.tokens)
 
     def step(self, ev=None):
@@ -487,21 +505,20 @@ def roofline(wl, kern_ms):
     dom = max(kern_ms, key=kern_ms.get)
     bound, amount = work[dom]
     peak, src = peaks[bound]
-    if bound == "hbm":
-        achieved, unit = amount / (kern_ms[dom] / 1e3) / 1e9, "GB/s"
-    else:
-        achieved, unit = amount / (kern_ms[dom] / 1e3) / 1e12, "TFLOP/s"
+    scale, unit = RATE[bound]
+    achieved = amount / (kern_ms[dom] / 1e3) / scale
     kname = "%s_%s" % (wl.kname, dom)
+    amount_key = {"hbm": "algorithmic_bytes_per_launch", "tensor": "algorithmic_flops_per_launch",
+                  "sfu": "algorithmic_exps_per_launch"}[bound]
     roof = {"bound": bound, "kernel": kname, "achieved": round(achieved, 2), "peak": peak,
             "unit": unit, "frac": round(achieved / peak, 4), "peak_source": src,
-            ("algorithmic_bytes_per_launch" if bound == "hbm" else "algorithmic_flops_per_launch"):
-                amount,
-            "traffic": ncu_traffic(kname)}
+            amount_key: amount, "traffic": ncu_traffic(kname)}
     per = {}
     for k, ms in kern_ms.items():
         b_, a_ = work[k]
-        rate = a_ / (ms / 1e3) / (1e9 if b_ == "hbm" else 1e12)
-        per[k] = {"ms": round(ms, 4), ("GB/s" if b_ == "hbm" else "TFLOP/s"): round(rate, 2),
+        sc, un = RATE[b_]
+        rate = a_ / (ms / 1e3) / sc
+        per[k] = {"ms": round(ms, 4), un: round(rate, 2),
                   "frac_of_peak": round(rate / peaks[b_][0], 4)}
     return roof, per
 

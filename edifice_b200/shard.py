@@ -74,7 +74,14 @@ class SsmConfig:
         return 5 * e * 2 + 2 * bc * 2 + 2 * bc * 4 + self.d_inner * self.d_state * 2
 
     def exps_fwd(self):
+        """exp(dt A) evaluations of the forward: one per (b, t, d, n)."""
         return self.batch * self.seq_len * self.d_inner * self.d_state
+
+    def exps_bwd(self):
+        """Of the recompute-not-store backward: one per element to rebuild the
+        sub-chunk start states from the chunk checkpoint, one to recompute each
+        sub-chunk (its exp(dt A) then serves the reverse walk)."""
+        return 2 * self.exps_fwd()
 
 
 @dataclasses.dataclass(frozen=True)
