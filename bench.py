@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--no-paths", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the config's batch per GPU (small cases for ncu captures)")
+    ap.add_argument("--seq-len", type=int, default=None,
+                    help="override the config's sequence length (small cases for ncu captures)")
     return ap.parse_args()
 
 
@@ -60,6 +62,8 @@ def make_workload(args):
     wl = WORKLOADS[args.config]()
     if args.batch:
         wl.cfg = dataclasses.replace(wl.cfg, batch=args.batch)
+    if args.seq_len:
+        wl.cfg = dataclasses.replace(wl.cfg, seq_len=args.seq_len)
     return wl
 
 

@@ -1,0 +1,94 @@
+"""Host-side logic of the multi-GPU (weak-scaling) path, on CPU.
+
+Every config partitions into independent units (batch rows; (batch, head);
+(batch, kv group)); a rank owns a contiguous range of global units and draws
+each unit's inputs from its own seed, so a unit's data never depends on the
+world size.  The only collectives are the barrier and the max-over-ranks time
+reduction of bench.py, exercised here on a world_size-2 gloo group.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from edifice_b200 import shard
+
+
+def test_plan_units_weak_scaling():
+    for world in (1, 2, 4, 8):
+        seen = []
+        for r in range(world):
+            u = shard.plan_units(3, r, world)
+            assert u == list(range(3 * r, 3 * r + 3))
+            seen += u
+        assert seen == list(range(3 * world))
+    with pytest.raises(ValueError):
+        shard.plan_units(3, 2, 2)
+    with pytest.raises(ValueError):
+        shard.plan_units(3, 0, 0)
+
+
+def test_split_units_strong_scaling():
+    for n, w in ((64, 8), (10, 4), (3, 8)):
+        parts = shard.split_units(n, w)
+        assert sum(c for _, c in parts) == n
+        assert max(c for _, c in parts) - min(c for _, c in parts) <= 1
+        starts = [s for s, _ in parts]
+        assert starts == sorted(starts) and starts[0] == 0
+
+
+def test_unit_inputs_do_not_depend_on_world_size():
+    cfg = shard.ScanConfig(batch=4, seq_len=16, hidden=32, dtype=torch.float32)
+    a_all, b_all, dy_all = shard.scan_inputs(cfg, [0, 1, 2, 3], "cpu")
+    a_r1, b_r1, dy_r1 = shard.scan_inputs(cfg, shard.plan_units(2, 1, 2), "cpu")
+    assert torch.equal(a_all[2:], a_r1) and torch.equal(b_all[2:], b_r1)
+    assert torch.equal(dy_all[2:], dy_r1)
+    dcfg = shard.DeltaConfig(batch=2, heads=2, seq_len=8, head_dim=16, dtype=torch.float32)
+    full = shard.delta_inputs(dcfg, [0, 1, 2, 3], "cpu")
+    upper = shard.delta_inputs(dcfg, [2, 3], "cpu")  # (b=1, h=0..1) of the full problem
+    for f, u in zip(full, upper):
+        assert torch.equal(f[1:], u)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, out_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = shard.ScanConfig(batch=2, seq_len=16, hidden=32, dtype=torch.float32)
+        units = shard.plan_units(cfg.batch, rank, world)
+        a, b, _ = shard.scan_inputs(cfg, units, "cpu")
+        # this rank's "elapsed time": the bench takes the max over ranks
+        t = torch.tensor([1.5 + rank], dtype=torch.float64)
+        dist.barrier()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sums = [torch.zeros(2, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(sums, torch.tensor([a.double().sum(), b.double().sum()]))
+        if rank == 0:
+            torch.save({"tmax": float(t), "sums": torch.stack(sums)}, out_path)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gloo_plan_and_max_time(tmp_path):
+    world = 2
+    out = str(tmp_path / "r0.pt")
+    mp.spawn(_rank_main, args=(world, _free_port(), out), nprocs=world, join=True)
+    res = torch.load(out)
+    assert res["tmax"] == 1.5 + (world - 1)
+    cfg = shard.ScanConfig(batch=2, seq_len=16, hidden=32, dtype=torch.float32)
+    a, b, _ = shard.scan_inputs(cfg, list(range(cfg.batch * world)), "cpu")
+    for r in range(world):
+        sl = slice(r * cfg.batch, (r + 1) * cfg.batch)
+        assert torch.allclose(res["sums"][r],
+                              torch.tensor([a[sl].double().sum(), b[sl].double().sum()]))
