@@ -369,11 +369,14 @@ __global__ void __launch_bounds__(kThreads)
     const int ntiles = (L + TB - 1) / TB;
     const long long row0 = (long long)b * L;
 
-    float A2[NS], h[NS];
+    constexpr int NP = NS / 2;  // state pairs for the packed f32x2 instructions
+    float2 A2[NP], h[NP];
 #pragma unroll
-    for (int n = 0; n < NS; ++n) {
-        A2[n] = (live && n < N) ? ldf(A + (long long)d * N + n) * kLog2e : 0.0f;
-        h[n] = 0.0f;
+    for (int p = 0; p < NP; ++p) {
+        const int n = 2 * p;
+        A2[p].x = (live && n < N) ? ldf(A + (long long)d * N + n) * kLog2e : 0.0f;
+        A2[p].y = (live && n + 1 < N) ? ldf(A + (long long)d * N + n + 1) * kLog2e : 0.0f;
+        h[p] = dup2(0.0f);
     }
     float rb[BCV], rc[BCV];
     auto load_bc = [&](int k) {
@@ -420,32 +423,32 @@ __global__ void __launch_bounds__(kThreads)
             if (ckpt != nullptr && t0 % CK == 0) {
                 float* cp = ckpt + (((long long)b * nck + t0 / CK) * D + d) * NS;
 #pragma unroll
-                for (int n = 0; n < NS; n += 4)
-                    *reinterpret_cast<float4*>(cp + n) = make_float4(h[n], h[n + 1], h[n + 2], h[n + 3]);
+                for (int p = 0; p < NP; p += 2)
+                    *reinterpret_cast<float4*>(cp + 2 * p) =
+                        make_float4(h[p].x, h[p].y, h[p + 1].x, h[p + 1].y);
             }
             for (int tt = 0; tt < tn; ++tt) {
                 const float dtc = fminf(fmaxf(ldf(dts + tt * kThreads), dt_min), dt_max);
-                const float dtx = dtc * ldf(xs + tt * kThreads);
-                float acc = 0.0f;
+                const float2 dtc2 = dup2(dtc), dtx2 = dup2(dtc * ldf(xs + tt * kThreads));
+                float2 acc = dup2(0.0f);
 #pragma unroll
-                for (int n = 0; n < NS; n += 4) {
-                    const float4 b4 = *reinterpret_cast<const float4*>(bk + tt * NS + n);
-                    const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
-                    float cv[4] = {0.f, 0.f, 0.f, 0.f};
-                    if (!STATES_ONLY) {
-                        const float4 c4 = *reinterpret_cast<const float4*>(ckc + tt * NS + n);
-                        cv[0] = c4.x;
-                        cv[1] = c4.y;
-                        cv[2] = c4.z;
-                        cv[3] = c4.w;
-                    }
+                for (int p = 0; p < NP; p += 2) {
+                    const float4 b4 = *reinterpret_cast<const float4*>(bk + tt * NS + 2 * p);
+                    float4 c4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (!STATES_ONLY) c4 = *reinterpret_cast<const float4*>(ckc + tt * NS + 2 * p);
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        h[n + e] = fmaf(ex2(dtc * A2[n + e]), h[n + e], dtx * bv[e]);
-                        if (!STATES_ONLY) acc = fmaf(cv[e], h[n + e], acc);
+                    for (int q = 0; q < 2; ++q) {
+                        const float2 bq = q ? make_float2(b4.z, b4.w) : make_float2(b4.x, b4.y);
+                        const float2 arg = mul2(dtc2, A2[p + q]);
+                        const float2 a = make_float2(ex2(arg.x), ex2(arg.y));
+                        h[p + q] = fma2(a, h[p + q], mul2(dtx2, bq));
+                        if (!STATES_ONLY) {
+                            const float2 cq = q ? make_float2(c4.z, c4.w) : make_float2(c4.x, c4.y);
+                            acc = fma2(cq, h[p + q], acc);
+                        }
                     }
                 }
-                if (!STATES_ONLY) st_scalar<T>(y + (row0 + t0 + tt) * D + d, acc);
+                if (!STATES_ONLY) st_scalar<T>(y + (row0 + t0 + tt) * D + d, acc.x + acc.y);
             }
         }
         if (k + 1 < ntiles) store_bc(k + 1);
@@ -492,12 +495,16 @@ __global__ void __launch_bounds__(kThreads)
     const T* sdt = reinterpret_cast<const T*>(tiles + TILEB) + tid;
     const T* sdy = reinterpret_cast<const T*>(tiles + 2 * TILEB) + tid;
 
-    float A2[NS], A2ln[NS], dh[NS];
+    // state pairs (n, n+1) go through the packed f32x2 instructions
+    constexpr int NP = NS / 2;
+    float2 A2[NP], A2ln[NP], dh[NP];
 #pragma unroll
-    for (int n = 0; n < NS; ++n) {
-        A2[n] = (live && n < N) ? ldf(A + (long long)d * N + n) * kLog2e : 0.0f;
-        A2ln[n] = A2[n] * kLn2;
-        dh[n] = 0.0f;
+    for (int p = 0; p < NP; ++p) {
+        const int n = 2 * p;
+        A2[p].x = (live && n < N) ? ldf(A + (long long)d * N + n) * kLog2e : 0.0f;
+        A2[p].y = (live && n + 1 < N) ? ldf(A + (long long)d * N + n + 1) * kLog2e : 0.0f;
+        A2ln[p] = mul2(A2[p], dup2(kLn2));
+        dh[p] = dup2(0.0f);
     }
     const int ridx = reduced_index<V>(lane);
 
@@ -525,20 +532,18 @@ __global__ void __launch_bounds__(kThreads)
                 sC[tid + v * kThreads] = rc[v];
             }
         }
-        float h[NS];
+        float2 h[NP];
         if (live) {
             const float* cp = ckpt + (((long long)b * nck + c) * D + d) * NS;
 #pragma unroll
-            for (int n = 0; n < NS; n += 4) {
-                const float4 v4 = *reinterpret_cast<const float4*>(cp + n);
-                h[n] = v4.x;
-                h[n + 1] = v4.y;
-                h[n + 2] = v4.z;
-                h[n + 3] = v4.w;
+            for (int p = 0; p < NP; p += 2) {
+                const float4 v4 = *reinterpret_cast<const float4*>(cp + 2 * p);
+                h[p] = make_float2(v4.x, v4.y);
+                h[p + 1] = make_float2(v4.z, v4.w);
             }
         } else {
 #pragma unroll
-            for (int n = 0; n < NS; ++n) h[n] = 0.0f;
+            for (int p = 0; p < NP; ++p) h[p] = dup2(0.0f);
         }
         cp_async_wait<0>();
         __syncthreads();
@@ -546,17 +551,23 @@ __global__ void __launch_bounds__(kThreads)
         for (int tt = 0; tt < tn; ++tt) {
             if (tt % TS == 0) {
 #pragma unroll
-                for (int n = 0; n < NS; ++n) sSub[tt / TS][n][tid] = h[n];
+                for (int p = 0; p < NP; ++p) {
+                    sSub[tt / TS][2 * p][tid] = h[p].x;
+                    sSub[tt / TS][2 * p + 1][tid] = h[p].y;
+                }
             }
             const float dtc = fminf(fmaxf(ldf(sdt + tt * kThreads), dt_min), dt_max);
-            const float dtx = dtc * ldf(sx + tt * kThreads);
+            const float2 dtc2 = dup2(dtc), dtx2 = dup2(dtc * ldf(sx + tt * kThreads));
 #pragma unroll
-            for (int n = 0; n < NS; n += 4) {
-                const float4 b4 = *reinterpret_cast<const float4*>(sB + tt * NS + n);
-                h[n] = fmaf(ex2(dtc * A2[n]), h[n], dtx * b4.x);
-                h[n + 1] = fmaf(ex2(dtc * A2[n + 1]), h[n + 1], dtx * b4.y);
-                h[n + 2] = fmaf(ex2(dtc * A2[n + 2]), h[n + 2], dtx * b4.z);
-                h[n + 3] = fmaf(ex2(dtc * A2[n + 3]), h[n + 3], dtx * b4.w);
+            for (int p = 0; p < NP; p += 2) {
+                const float4 b4 = *reinterpret_cast<const float4*>(sB + tt * NS + 2 * p);
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const float2 bq = q ? make_float2(b4.z, b4.w) : make_float2(b4.x, b4.y);
+                    const float2 arg = mul2(dtc2, A2[p + q]);
+                    const float2 a = make_float2(ex2(arg.x), ex2(arg.y));
+                    h[p + q] = fma2(a, h[p + q], mul2(dtx2, bq));
+                }
             }
         }
         // ---- sub-chunks in reverse: recompute h and exp(dt A) into registers,
@@ -565,23 +576,24 @@ __global__ void __launch_bounds__(kThreads)
         for (int s = nsub - 1; s >= 0; --s) {
             const int u0 = s * TS;
             const int un = min(TS, tn - u0);
-            float hs[TS][NS], as[TS][NS];
+            float2 hs[TS][NP], as[TS][NP];
 #pragma unroll
-            for (int n = 0; n < NS; ++n) h[n] = sSub[s][n][tid];
+            for (int p = 0; p < NP; ++p) h[p] = make_float2(sSub[s][2 * p][tid], sSub[s][2 * p + 1][tid]);
 #pragma unroll
             for (int j = 0; j < TS; ++j) {
                 const int tt = min(u0 + j, tn - 1);  // steps past tn are never read back
                 const float dtc = fminf(fmaxf(ldf(sdt + tt * kThreads), dt_min), dt_max);
-                const float dtx = dtc * ldf(sx + tt * kThreads);
+                const float2 dtc2 = dup2(dtc), dtx2 = dup2(dtc * ldf(sx + tt * kThreads));
 #pragma unroll
-                for (int n = 0; n < NS; n += 4) {
-                    const float4 b4 = *reinterpret_cast<const float4*>(sB + tt * NS + n);
-                    const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+                for (int p = 0; p < NP; p += 2) {
+                    const float4 b4 = *reinterpret_cast<const float4*>(sB + tt * NS + 2 * p);
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        as[j][n + e] = ex2(dtc * A2[n + e]);
-                        h[n + e] = fmaf(as[j][n + e], h[n + e], dtx * bv[e]);
-                        hs[j][n + e] = h[n + e];
+                    for (int q = 0; q < 2; ++q) {
+                        const float2 bq = q ? make_float2(b4.z, b4.w) : make_float2(b4.x, b4.y);
+                        const float2 arg = mul2(dtc2, A2[p + q]);
+                        as[j][p + q] = make_float2(ex2(arg.x), ex2(arg.y));
+                        h[p + q] = fma2(as[j][p + q], h[p + q], mul2(dtx2, bq));
+                        hs[j][p + q] = h[p + q];
                     }
                 }
             }
@@ -595,32 +607,38 @@ __global__ void __launch_bounds__(kThreads)
                     const float xv = ldf(sx + tt * kThreads);
                     const float dyv = ldf(sdy + tt * kThreads);
                     const float dtx = dtc * xv;
-                    float gxa = 0.0f, gda = 0.0f;
+                    const float2 dy2 = dup2(dyv), dtx2 = dup2(dtx), ndtx2 = dup2(-dtx);
+                    float2 gxa = dup2(0.0f), gda = dup2(0.0f);
 #pragma unroll
-                    for (int n = 0; n < NS; n += 4) {
-                        const float4 b4 = *reinterpret_cast<const float4*>(sB + tt * NS + n);
-                        const float4 c4 = *reinterpret_cast<const float4*>(sC + tt * NS + n);
-                        const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
-                        const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+                    for (int p = 0; p < NP; p += 2) {
+                        const float4 b4 = *reinterpret_cast<const float4*>(sB + tt * NS + 2 * p);
+                        const float4 c4 = *reinterpret_cast<const float4*>(sC + tt * NS + 2 * p);
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int m = n + e;
-                            const float hc = hs[j][m];
-                            const float dht = fmaf(dyv, cv[e], dh[m]);
-                            red[NS + m] = dyv * hc;
-                            red[m] = dht * dtx;
-                            gxa = fmaf(dht, bv[e], gxa);
+                        for (int q = 0; q < 2; ++q) {
+                            const int m = p + q;
+                            const float2 bq = q ? make_float2(b4.z, b4.w) : make_float2(b4.x, b4.y);
+                            const float2 cq = q ? make_float2(c4.z, c4.w) : make_float2(c4.x, c4.y);
+                            const float2 hc = hs[j][m];
+                            const float2 dht = fma2(dy2, cq, dh[m]);
+                            const float2 gc = mul2(dy2, hc);
+                            const float2 gb = mul2(dht, dtx2);
+                            red[NS + 2 * m] = gc.x;
+                            red[NS + 2 * m + 1] = gc.y;
+                            red[2 * m] = gb.x;
+                            red[2 * m + 1] = gb.y;
+                            gxa = fma2(dht, bq, gxa);
                             // d h_t / d dtc = A (a h_{t-1}) + B x, a h_{t-1} = h_t - dtc x B;
                             // the B x part is summed once below (x gxa)
-                            gda = fmaf(dht * A2ln[m], fmaf(-dtx, bv[e], hc), gda);
-                            dh[m] = dht * as[j][m];
+                            gda = fma2(mul2(dht, A2ln[m]), fma2(ndtx2, bq, hc), gda);
+                            dh[m] = mul2(dht, as[j][m]);
                         }
                     }
-                    gda = fmaf(xv, gxa, gda);
+                    const float gxs = gxa.x + gxa.y;
+                    const float gds = fmaf(xv, gxs, gda.x + gda.y);
                     const long long o = (row0 + t0 + tt) * D + d;
-                    st_scalar<T>(gx + o, gxa * dtc);
+                    st_scalar<T>(gx + o, gxs * dtc);
                     const bool inr = draw >= dt_min && draw <= dt_max;
-                    st_scalar<T>(gdt + o, inr ? gda : 0.0f);
+                    st_scalar<T>(gdt + o, inr ? gds : 0.0f);
                 } else {
 #pragma unroll
                     for (int i = 0; i < V; ++i) red[i] = 0.0f;
