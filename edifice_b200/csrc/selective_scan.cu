@@ -483,7 +483,9 @@ __global__ void __launch_bounds__(kThreads)
     unsigned char* tiles = smem + SUBS * NS * kThreads * sizeof(float);  // x | dt | dy
     float* sB = reinterpret_cast<float*>(tiles + 3 * TILEB);             // [CK][NS]
     float* sC = sB + CK * NS;                                             // [CK][NS]
-    auto sRed = reinterpret_cast<float(*)[TS][32]>(sC + CK * NS);        // [4][TS][32]
+    // per-warp gB|gC sums of every step of the chunk; summed across warps once
+    // per chunk, so the warps run out of phase between the chunk barriers
+    auto sRed = reinterpret_cast<float(*)[CK][V]>(sC + CK * NS);         // [4][CK][V]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int d0 = blockIdx.x * kThreads, d = d0 + tid;
     const int b = blockIdx.y;
@@ -644,24 +646,23 @@ __global__ void __launch_bounds__(kThreads)
                     for (int i = 0; i < V; ++i) red[i] = 0.0f;
                 }
                 const float r = warp_transpose_reduce<V>(red, lane);
-                if (lane < V) sRed[warp][j][ridx] = r;
+                if (lane < V) sRed[warp][u0 + j][ridx] = r;
             }
-            __syncthreads();
-            for (int i = tid; i < TS * V; i += kThreads) {
-                const int j = i / V, vi = i % V;
-                if (j < un) {
-                    float sum = 0.0f;
+        }
+        __syncthreads();
+        // this CTA's partial gB|gC of every step of the chunk (fixed warp order)
+        for (int i = tid; i < CK * V; i += kThreads) {
+            const int j = i / V, vi = i % V;
+            if (j < tn) {
+                float sum = 0.0f;
 #pragma unroll
-                    for (int w = 0; w < kThreads / 32; ++w) sum += sRed[w][j][vi];
-                    const int which = vi >= NS;
-                    const int n = vi - which * NS;
-                    const long long o =
-                        ((((long long)which * nblk + blockIdx.x) * Bsz + b) * L + t0 + u0 + j) *
-                            NS + n;
-                    gpart[o] = sum;
-                }
+                for (int w = 0; w < kThreads / 32; ++w) sum += sRed[w][j][vi];
+                const int which = vi >= NS;
+                const int n = vi - which * NS;
+                const long long o =
+                    ((((long long)which * nblk + blockIdx.x) * Bsz + b) * L + t0 + j) * NS + n;
+                gpart[o] = sum;
             }
-            __syncthreads();
         }
     }
 }
@@ -671,7 +672,7 @@ constexpr size_t bwd_staged_smem() {
     constexpr int TS = SsmTiling<NS>::TS, CK = SsmTiling<NS>::CK;
     return (size_t)(CK / TS) * NS * kThreads * sizeof(float) +
            (size_t)3 * CK * StageGeom<T>::ROWB + (size_t)2 * CK * NS * sizeof(float) +
-           (size_t)(kThreads / 32) * TS * 32 * sizeof(float);
+           (size_t)(kThreads / 32) * CK * 2 * NS * sizeof(float);
 }
 
 int pad_states(int N) {
