@@ -35,7 +35,11 @@ constexpr int BQ = 64;
 // A Q/dO stage is released only after its second use (the dV/dK MMAs), so
 // three stages are needed to keep the next tiles' TMA loads off the critical path.
 constexpr int QD_STAGES = 3;
-constexpr int kBwdThreads = 320;
+// warps 0-7 P^T/dS^T (two per TMEM lane quarter, 32 query columns each),
+// 8-11 dQ staging/reduce + dK/dV epilogue, 12 TMA producer, 13 MMA issuer
+constexpr int kBwdThreads = 448;
+constexpr int kComputeWarps = 8;
+constexpr int kDqWarp0 = 8, kProducerWarp = 12, kMmaWarp = 13;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct BwdMaps {
@@ -114,7 +118,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (tid == 0) edb_flag_error(err, EDB_DEVERR_ATTN_PIPE);
         return;
     }
-    if (warp == 9) {
+    if (warp == kMmaWarp) {
         tc::tmem_alloc(s_tmem, S::TMEM_COLS);
         tc::tmem_relinquish();
     }
@@ -125,8 +129,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             mbar_init(&qd_empty[s], 1);
         }
         mbar_init(sdp_full, 1);
-        mbar_init(sdp_free, 4);
-        mbar_init(pds_full, 4);
+        mbar_init(sdp_free, kComputeWarps);
+        mbar_init(pds_full, kComputeWarps);
         mbar_init(mm2_done, 1);
         mbar_init(dq_full, 1);
         mbar_init(dq_free, 4);
@@ -140,7 +144,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t tmem = *s_tmem;
     volatile int* abort_flag = s_abort;
 
-    if (warp == 8) {
+    if (warp == kProducerWarp) {
         // ------------------------------------------------ producer (whole warp)
         if (lane == 0) {
             prefetch_tmap(&maps.q);
@@ -172,8 +176,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             for (int c = lane; c < BQ; c += 32) {
                 const int qr = i * BQ + c;
                 const bool ok = qr < L;
-                sLse[s * BQ + c] = ok ? lse[(long long)bh * L + qr] * kLog2e : INFINITY;
-                sD[s * BQ + c] = ok ? Dv[(long long)bh * L + qr] : 0.0f;
+                // stored as -lse log2(e) and -D scale: P = ex2(S scale log2(e) + .),
+                // dS = P (dP scale + .); rows past L give P = 0
+                sLse[s * BQ + c] = ok ? -lse[(long long)bh * L + qr] * kLog2e : -INFINITY;
+                sD[s * BQ + c] = ok ? -Dv[(long long)bh * L + qr] * scale : 0.0f;
             }
             __syncwarp();
             if (lane == 0) {
@@ -193,7 +199,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                   EDB_DEVERR_ATTN_PIPE);
             mbar_wait_bounded(kv_full, 0, err, EDB_DEVERR_ATTN_PIPE);
         }
-    } else if (warp == 9) {
+    } else if (warp == kMmaWarp) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idSP = tc::idesc_bf16(BKV, BQ, 0, 0);   // S^T, dP^T
@@ -258,11 +264,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             tc::commit(all_done);
             mbar_wait_bounded(all_done, 0, err, EDB_DEVERR_ATTN_PIPE);
         }
-    } else if (warp < 4) {
+    } else if (warp < kComputeWarps) {
         // ------------------------------------------------ P^T / dS^T compute
-        const int r = warp * 32 + lane;
+        // warp (quarter q = warp % 4, half hf = warp / 4): kv row r = 32 q + lane
+        // (TMEM lane), query columns [32 hf, 32 hf + 32) of the tile
+        const int qw = warp & 3, hf = warp >> 2;
+        const int r = qw * 32 + lane;
         const int kv_idx = kt * BKV + r;
-        const uint32_t lb = (uint32_t)(warp * 32) << 16;
+        const uint32_t lb = (uint32_t)(qw * 32) << 16;
+        const int c0 = hf * 32;
+        const float2 sl2 = dup2(scale_log2), sc2 = dup2(scale);
         for (int n = 0; n < N; ++n) {
             const int s = n % QD_STAGES;
             const int i = i0 + n % nqi;
@@ -273,11 +284,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 break;
             }
             tc::fence_after_sync();
-            uint32_t sr[2][32], dr[2][32];
-            tc::tmem_ld32(tmem + S::TM_S + lb, sr[0]);
-            tc::tmem_ld32(tmem + S::TM_S + lb + 32, sr[1]);
-            tc::tmem_ld32(tmem + S::TM_DP + lb, dr[0]);
-            tc::tmem_ld32(tmem + S::TM_DP + lb + 32, dr[1]);
+            uint32_t sr[32], dr[32];
+            tc::tmem_ld32(tmem + S::TM_S + lb + c0, sr);
+            tc::tmem_ld32(tmem + S::TM_DP + lb + c0, dr);
             tc::tmem_wait_ld();
             tc::fence_before_sync();
             __syncwarp();
@@ -286,30 +295,44 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 *abort_flag = 1;
                 break;
             }
-            const float* l2 = sLse + s * BQ;
-            const float* dd = sD + s * BQ;
-            // masks are only needed on the diagonal and for a ragged last kv tile;
-            // query rows past L carry lse = +inf and give P = 0 by themselves
+            const float* nl2 = sLse + s * BQ + c0;   // -lse log2(e)
+            const float* ndd = sD + s * BQ + c0;     // -D scale
+            // masks only on the diagonal and for a ragged last kv tile; query rows
+            // past L carry -lse = -inf and give P = 0 by themselves
             const bool need_mask = (kt * BKV + BKV > L) || (CAUSAL && i * BQ < kt * BKV + BKV);
 #pragma unroll
-            for (int ch = 0; ch < BQ / 8; ++ch) {
-                float p[8], ds[8];
+            for (int ch = 0; ch < 4; ++ch) {
+                const float4 la = *reinterpret_cast<const float4*>(nl2 + ch * 8);
+                const float4 lb4 = *reinterpret_cast<const float4*>(nl2 + ch * 8 + 4);
+                const float4 da = *reinterpret_cast<const float4*>(ndd + ch * 8);
+                const float4 db = *reinterpret_cast<const float4*>(ndd + ch * 8 + 4);
+                const float2 lv[4] = {make_float2(la.x, la.y), make_float2(la.z, la.w),
+                                      make_float2(lb4.x, lb4.y), make_float2(lb4.z, lb4.w)};
+                const float2 dv2[4] = {make_float2(da.x, da.y), make_float2(da.z, da.w),
+                                       make_float2(db.x, db.y), make_float2(db.z, db.w)};
+                uint32_t pk[4], dk2[4];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const int c = ch * 8 + e;
-                    const int q_idx = i * BQ + c;
-                    const bool valid = !need_mask || (kv_idx < L && (!CAUSAL || q_idx >= kv_idx));
-                    const float sv = __uint_as_float(sr[c >> 5][c & 31]);
-                    const float dpv = __uint_as_float(dr[c >> 5][c & 31]);
-                    p[e] = valid ? tc::ex2(fmaf(sv, scale_log2, -l2[c])) : 0.0f;
-                    ds[e] = p[e] * (dpv - dd[c]) * scale;
+                for (int e = 0; e < 4; ++e) {
+                    const int cc = ch * 8 + 2 * e;  // column within this warp's 32
+                    const float2 sv = make_float2(__uint_as_float(sr[cc]), __uint_as_float(sr[cc + 1]));
+                    const float2 dp = make_float2(__uint_as_float(dr[cc]), __uint_as_float(dr[cc + 1]));
+                    const float2 arg = fma2(sv, sl2, lv[e]);
+                    float2 p = make_float2(tc::ex2(arg.x), tc::ex2(arg.y));
+                    if (need_mask) {
+                        const int q_idx = i * BQ + c0 + cc;
+                        const bool ok = kv_idx < L;
+                        if (!ok || (CAUSAL && q_idx < kv_idx)) p.x = 0.0f;
+                        if (!ok || (CAUSAL && q_idx + 1 < kv_idx)) p.y = 0.0f;
+                    }
+                    const float2 ds = mul2(p, fma2(dp, sc2, dv2[e]));
+                    pk[e] = tc::pack_bf16x2(p.x, p.y);
+                    dk2[e] = tc::pack_bf16x2(ds.x, ds.y);
                 }
-                *reinterpret_cast<uint4*>(sPt + tc::sw128_off(r, ch)) =
-                    make_uint4(tc::pack_bf16x2(p[0], p[1]), tc::pack_bf16x2(p[2], p[3]),
-                               tc::pack_bf16x2(p[4], p[5]), tc::pack_bf16x2(p[6], p[7]));
-                *reinterpret_cast<uint4*>(sDs + tc::sw128_off(r, ch)) =
-                    make_uint4(tc::pack_bf16x2(ds[0], ds[1]), tc::pack_bf16x2(ds[2], ds[3]),
-                               tc::pack_bf16x2(ds[4], ds[5]), tc::pack_bf16x2(ds[6], ds[7]));
+                const int chunk = hf * 4 + ch;  // 16-byte chunk of the 128-byte row
+                *reinterpret_cast<uint4*>(sPt + tc::sw128_off(r, chunk)) =
+                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                *reinterpret_cast<uint4*>(sDs + tc::sw128_off(r, chunk)) =
+                    make_uint4(dk2[0], dk2[1], dk2[2], dk2[3]);
             }
             fence_proxy_async();
             __syncwarp();
@@ -317,7 +340,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
     } else {
         // ------------------------------------------------ dQ reduction + dK/dV epilogue (warps 4-7)
-        const int w = warp - 4;
+        const int w = warp - kDqWarp0;
         const uint32_t lb = (uint32_t)(w * 32) << 16;
         bool ok = true;
         for (int n = 0; n < N; ++n) {
@@ -329,27 +352,33 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 break;
             }
             tc::fence_after_sync();
-            uint32_t qv[HD / 32][32];
-#pragma unroll
-            for (int cc = 0; cc < HD / 32; ++cc) tc::tmem_ld32(tmem + S::TM_DQ + lb + cc * 32, qv[cc]);
-            tc::tmem_wait_ld();
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(dq_free);
             // the previous tile's bulk reduce must be done reading the staging tile
             if (w == 0 && lane == 0) tc::tma_store_wait_read_all();
             tc::named_bar(2, 128);
-            // M = 64 accumulator: lanes 32w + t (t < 16) hold query row 16w + t of the tile
-            if (lane < 16) {
-                const int r = 16 * w + lane;
+            // dQ_i in two halves of HD/2 columns (register budget); M = 64
+            // accumulator: lanes 32w + t (t < 16) hold query row 16w + t of the tile
 #pragma unroll
-                for (int cc = 0; cc < HD / 32; ++cc)
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t qv[HD / 64][32];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        *reinterpret_cast<uint4*>(sDq + cc * (BQ * 128) + tc::sw128_off(r, j)) =
-                            make_uint4(qv[cc][4 * j], qv[cc][4 * j + 1], qv[cc][4 * j + 2],
-                                       qv[cc][4 * j + 3]);
+                for (int cc = 0; cc < HD / 64; ++cc)
+                    tc::tmem_ld32(tmem + S::TM_DQ + lb + (hh * (HD / 64) + cc) * 32, qv[cc]);
+                tc::tmem_wait_ld();
+                if (lane < 16) {
+                    const int r = 16 * w + lane;
+#pragma unroll
+                    for (int cc = 0; cc < HD / 64; ++cc)
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            *reinterpret_cast<uint4*>(sDq + (hh * (HD / 64) + cc) * (BQ * 128) +
+                                                      tc::sw128_off(r, j)) =
+                                make_uint4(qv[cc][4 * j], qv[cc][4 * j + 1], qv[cc][4 * j + 2],
+                                           qv[cc][4 * j + 3]);
+                }
             }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(dq_free);
             fence_proxy_async();
             tc::named_bar(2, 128);
             // dq_acc[bh, i*BQ .., :] += staging tile (rows past L are clipped)
@@ -389,7 +418,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     tc::fence_before_sync();
     __syncthreads();
-    if (warp == 9) {
+    if (warp == kMmaWarp) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, S::TMEM_COLS);
     }
