@@ -53,8 +53,10 @@ struct FwdSmem {
     static constexpr int OFF_V = OFF_K + KV_STAGES * KV_BYTES;
     static constexpr int OFF_P = OFF_V + KV_STAGES * KV_BYTES;
     static constexpr int OFF_BAR = OFF_P + P_BYTES;
-    // barriers: q_full, kv_full[2], kv_empty[2], s_full, s_free, p_full, pv_done, mma_done
-    static constexpr int NBAR = 1 + 2 * KV_STAGES + 5;
+    // barriers: q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full, s_free,
+    // p_full, pv_done, mma_done.  K and V rings are separate: K_j is free once
+    // S_j has been computed, V_j only after P_j V_j.
+    static constexpr int NBAR = 1 + 4 * KV_STAGES + 5;
     static constexpr int TOTAL = OFF_BAR + NBAR * 8 + 16;
     static constexpr int TMEM_COLS = HD == 128 ? 256 : 128;
     static constexpr int TMEM_S = 0;
@@ -77,9 +79,11 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     uint8_t* sP = smem + S::OFF_P;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
     uint64_t* q_full = bars + 0;
-    uint64_t* kv_full = bars + 1;
-    uint64_t* kv_empty = bars + 1 + KV_STAGES;
-    uint64_t* s_full = bars + 1 + 2 * KV_STAGES;
+    uint64_t* k_full = bars + 1;
+    uint64_t* k_empty = k_full + KV_STAGES;
+    uint64_t* v_full = k_empty + KV_STAGES;
+    uint64_t* v_empty = v_full + KV_STAGES;
+    uint64_t* s_full = bars + 1 + 4 * KV_STAGES;
     uint64_t* s_free = s_full + 1;
     uint64_t* p_full = s_full + 2;
     uint64_t* pv_done = s_full + 3;
@@ -108,8 +112,10 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     if (tid == 128) {
         mbar_init(q_full, 1);
         for (int s = 0; s < KV_STAGES; ++s) {
-            mbar_init(&kv_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+            mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 1);
+            mbar_init(&v_full[s], 1);
+            mbar_init(&v_empty[s], 1);
         }
         mbar_init(s_full, 1);
         mbar_init(s_free, 4);
@@ -126,38 +132,42 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
 
     if (warp == 4) {
         // ------------------------------------------------ TMA producer
-        if (lane == 0) {
-            prefetch_tmap(&maps.q);
-            prefetch_tmap(&maps.k);
-            prefetch_tmap(&maps.v);
-            mbar_arrive_expect_tx(q_full, S::Q_BYTES);
-            for (int bx = 0; bx < NB; ++bx)
-                tma_load_3d(sQ + bx * (BM * 128), &maps.q, q_full, bx * 64, q0, bh);
+        // lane 0: Q, then the K ring; lane 1: the V ring (independent waits)
+        if (lane < 2) {
+            const bool is_k = lane == 0;
+            const CUtensorMap* map = is_k ? &maps.k : &maps.v;
+            uint8_t* ring = is_k ? sK : sV;
+            uint64_t* full = is_k ? k_full : v_full;
+            uint64_t* empty = is_k ? k_empty : v_empty;
+            prefetch_tmap(map);
+            if (is_k) {
+                prefetch_tmap(&maps.q);
+                mbar_arrive_expect_tx(q_full, S::Q_BYTES);
+                for (int bx = 0; bx < NB; ++bx)
+                    tma_load_3d(sQ + bx * (BM * 128), &maps.q, q_full, bx * 64, q0, bh);
+            }
             int issued = 0;
             for (int j = 0; j < nkv; ++j) {
                 const int s = j % KV_STAGES;
                 if (j >= KV_STAGES) {
                     if (*(volatile int*)s_abort) break;
-                    if (!mbar_wait_bounded(&kv_empty[s], ((j / KV_STAGES) - 1) & 1, err,
+                    if (!mbar_wait_bounded(&empty[s], ((j / KV_STAGES) - 1) & 1, err,
                                            EDB_DEVERR_ATTN_PIPE)) {
                         *(volatile int*)s_abort = 1;
                         break;
                     }
                 }
-                mbar_arrive_expect_tx(&kv_full[s], 2 * S::KV_BYTES);
-                for (int bx = 0; bx < NB; ++bx) {
-                    tma_load_3d(sK + s * S::KV_BYTES + bx * (BN * 128), &maps.k, &kv_full[s],
-                                bx * 64, j * BN, bhk);
-                    tma_load_3d(sV + s * S::KV_BYTES + bx * (BN * 128), &maps.v, &kv_full[s],
-                                bx * 64, j * BN, bhk);
-                }
+                mbar_arrive_expect_tx(&full[s], S::KV_BYTES);
+                for (int bx = 0; bx < NB; ++bx)
+                    tma_load_3d(ring + s * S::KV_BYTES + bx * (BN * 128), map, &full[s], bx * 64,
+                                j * BN, bhk);
                 issued = j + 1;
             }
             // make sure no copy is still landing when the CTA leaves (bounded)
             for (int j = max(0, issued - KV_STAGES); j < issued; ++j)
-                mbar_wait_bounded(&kv_full[j % KV_STAGES], (j / KV_STAGES) & 1, err,
+                mbar_wait_bounded(&full[j % KV_STAGES], (j / KV_STAGES) & 1, err,
                                   EDB_DEVERR_ATTN_PIPE);
-            mbar_wait_bounded(q_full, 0, err, EDB_DEVERR_ATTN_PIPE);
+            if (is_k) mbar_wait_bounded(q_full, 0, err, EDB_DEVERR_ATTN_PIPE);
         }
     } else if (warp == 5) {
         // ------------------------------------------------ MMA issuer
@@ -175,9 +185,10 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                     tc::mma_bf16_ss(tS, ad, bd, idS, kk > 0);
                 }
                 tc::commit(s_full);
+                tc::commit(&k_empty[s]);  // K_j may be reloaded once S_j is done
             };
             bool ok = mbar_wait_bounded(q_full, 0, err, EDB_DEVERR_ATTN_PIPE) &&
-                      mbar_wait_bounded(&kv_full[0], 0, err, EDB_DEVERR_ATTN_PIPE);
+                      mbar_wait_bounded(&k_full[0], 0, err, EDB_DEVERR_ATTN_PIPE);
             if (ok) {
                 tc::fence_after_sync();
                 issue_S(0);
@@ -185,14 +196,16 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
             for (int j = 0; ok && j < nkv; ++j) {
                 if (j + 1 < nkv) {
                     const int s1 = (j + 1) % KV_STAGES;
-                    ok = mbar_wait_bounded(&kv_full[s1], ((j + 1) / KV_STAGES) & 1, err,
+                    ok = mbar_wait_bounded(&k_full[s1], ((j + 1) / KV_STAGES) & 1, err,
                                            EDB_DEVERR_ATTN_PIPE) &&
                          mbar_wait_bounded(s_free, j & 1, err, EDB_DEVERR_ATTN_PIPE);
                     if (!ok) break;
                     tc::fence_after_sync();
                     issue_S(j + 1);
                 }
-                ok = mbar_wait_bounded(p_full, j & 1, err, EDB_DEVERR_ATTN_PIPE);
+                ok = mbar_wait_bounded(p_full, j & 1, err, EDB_DEVERR_ATTN_PIPE) &&
+                     mbar_wait_bounded(&v_full[j % KV_STAGES], (j / KV_STAGES) & 1, err,
+                                       EDB_DEVERR_ATTN_PIPE);
                 if (!ok) break;
                 tc::fence_after_sync();
                 const uint8_t* vb = sV + (j % KV_STAGES) * S::KV_BYTES;
@@ -203,7 +216,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                     tc::mma_bf16_ss(tO, ad, bd, idO, (j > 0 || kk > 0));
                 }
                 tc::commit(pv_done);
-                tc::commit(&kv_empty[j % KV_STAGES]);
+                tc::commit(&v_empty[j % KV_STAGES]);
             }
             if (!ok) *(volatile int*)s_abort = 1;
             // every MMA issued above has completed before TMEM is released
