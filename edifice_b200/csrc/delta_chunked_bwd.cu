@@ -22,13 +22,12 @@
 //                           dS in TMEM (lanes = value dim):
 //                             D_U = dS K^T + dO^T M        (= dU~^T)   N=64
 //                             dS += dO^T Q + D_U (-W)                  N=128
-//                           stores dS_C^T and dU~ per chunk.
+//                           stores dS_C^T, dU~ and dU~^T per chunk.
 //   delta_post1_kernel      per chunk, tcgen05: the products with S_0 / dS_C,
 //                           (dO S_0)^T, (dU~ S_0)^T, (U~ dS_C)^T (M=128, N=64,
 //                           K=128) and dO U~^T (M=64); operands by TMA.
-//   delta_post2_kernel      (delta_chunked_post.cu) per chunk, SIMT f32: the
-//                           C x C chain (dT_b, dA, dbeta) and the final dQ, dK,
-//                           dV (bf16).
+//   delta_post2_kernel      (delta_chunked_post.cu) per chunk: dT_b, dQ, dK, dV
+//                           on tcgen05, the C x C chain (dA, dbeta) SIMT.
 #include <math.h>
 
 #include "delta_chunked.cuh"
@@ -39,35 +38,57 @@ namespace {
 
 // ------------------------------------------------------------------ scratch
 struct BwdScratch {
-    float* Kf;    // [nch][C][D]  K (f32)          post1 output: dQa = dO S_0
-    float* dOT;   // [nch][D][C]  dO^T             post1 output: dW = -dU~ S_0
-    float* QT;    // [nch][D][C]  Q^T              post1 output: dK1 = U~ dS_C
+    // prep outputs
+    float* Kf;    // [nch][C][D]  K (f32)
+    float* KT;    // [nch][D][C]  K^T
+    float* dOT;   // [nch][D][C]  dO^T
+    float* QT;    // [nch][D][C]  Q^T
     float* WnT;   // [nch][D][C]  -W^T
-    float* MT;    // [nch][C][C]  M^T              post1 output: dM = tril(dO U~^T)
+    float* MT;    // [nch][C][C]  M^T
     float* T;     // [nch][C][C]  T (unscaled)
     float* G;     // [nch][C][C]  K K^T
+    // state kernel outputs
     float* dSCT;  // [nch][D][D]  dS_C^T
     float* dU;    // [nch][C][D]  dU~
+    float* dUT;   // [nch][D][C]  dU~^T
+    // post1 outputs
+    float* dQa;   // [nch][C][D]  dO S_0
+    float* dW;    // [nch][C][D]  -dU~ S_0
+    float* dWT;   // [nch][D][C]  its transpose
+    float* dK1;   // [nch][C][D]  U~ dS_C
+    float* dM;    // [nch][C][C]  tril(dO U~^T)
 };
 
 size_t bwd_scratch_bytes(long long nch) {
-    return 5 * a256((size_t)nch * C * D * 4) + 3 * a256((size_t)nch * C * C * 4) +
+    return 11 * a256((size_t)nch * C * D * 4) + 4 * a256((size_t)nch * C * C * 4) +
            a256((size_t)nch * D * D * 4);
 }
 
 BwdScratch carve_bwd(void* ws, long long nch) {
     char* p = static_cast<char*>(ws);
     const size_t cd = a256((size_t)nch * C * D * 4), cc = a256((size_t)nch * C * C * 4);
+    auto take = [&](size_t bytes) {
+        float* r = reinterpret_cast<float*>(p);
+        p += bytes;
+        return r;
+    };
     BwdScratch s;
-    s.Kf = reinterpret_cast<float*>(p); p += cd;
-    s.dOT = reinterpret_cast<float*>(p); p += cd;
-    s.QT = reinterpret_cast<float*>(p); p += cd;
-    s.WnT = reinterpret_cast<float*>(p); p += cd;
-    s.dU = reinterpret_cast<float*>(p); p += cd;
-    s.MT = reinterpret_cast<float*>(p); p += cc;
-    s.T = reinterpret_cast<float*>(p); p += cc;
-    s.G = reinterpret_cast<float*>(p); p += cc;
-    s.dSCT = reinterpret_cast<float*>(p);
+    s.Kf = take(cd);
+    s.KT = take(cd);
+    s.dOT = take(cd);
+    s.QT = take(cd);
+    s.WnT = take(cd);
+    s.dU = take(cd);
+    s.dUT = take(cd);
+    s.dQa = take(cd);
+    s.dW = take(cd);
+    s.dWT = take(cd);
+    s.dK1 = take(cd);
+    s.MT = take(cc);
+    s.T = take(cc);
+    s.G = take(cc);
+    s.dM = take(cc);
+    s.dSCT = take(a256((size_t)nch * D * D * 4));
     return s;
 }
 
@@ -103,6 +124,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
     __syncthreads();
     store_transposed(ws.dOT + ch * D * C, dOs, 1.0f);
     store_transposed(ws.QT + ch * D * C, Qs, 1.0f);
+    store_transposed(ws.KT + ch * D * C, Ks, 1.0f);
     prep_products(Ks, Qs, Gs, Ms);
     __syncthreads();
     for (int idx = tid; idx < C * C; idx += kPrepThreads) {
@@ -139,7 +161,8 @@ constexpr int SB_TM_S = 0, SB_TM_U = 128, SB_TM_COLS = 256;
 
 __global__ void __launch_bounds__(kStateThreads, 1)
     delta_state_bwd_kernel(const __grid_constant__ StateBwdMaps maps, float* __restrict__ dSCT,
-                           float* __restrict__ dU, int H, int NC, unsigned* err) {
+                           float* __restrict__ dU, float* __restrict__ dUT, int H, int NC,
+                           unsigned* err) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* fullX = reinterpret_cast<uint64_t*>(smem + SB_OFF_BARS);  // [2]
     uint64_t* fullY = fullX + 2;
@@ -282,8 +305,24 @@ __global__ void __launch_bounds__(kStateThreads, 1)
         __syncthreads();
         tc::fence_after_sync();
         if (s_misc[1]) break;
-        // D_U = dU~^T: row i -> dU~[c][t][i]
-        store_rows_transposed<C>(dU + (ch0 + c) * C * D + i, tmem + SB_TM_U + lane_base);
+        // D_U = dU~^T: row i -> dU~[c][t][i] (coalesced over i) and dU~^T[c][i][t]
+        {
+            float* ut = dUT + ((ch0 + c) * D + i) * C;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                uint32_t x[32];
+                tc::tmem_ld32(tmem + SB_TM_U + lane_base + half * 32, x);
+                tc::tmem_wait_ld();
+                float* du = dU + (ch0 + c) * C * D + (long long)half * 32 * D + i;
+#pragma unroll
+                for (int e = 0; e < 32; ++e) du[e * D] = __uint_as_float(x[e]);
+#pragma unroll
+                for (int e = 0; e < 32; e += 4)
+                    st4(ut + half * 32 + e,
+                        make_float4(__uint_as_float(x[e]), __uint_as_float(x[e + 1]),
+                                    __uint_as_float(x[e + 2]), __uint_as_float(x[e + 3])));
+            }
+        }
     }
     if (s_misc[1] && tid == 0) {
         // Abort: bounded waits for the copies and MMAs still in flight.
@@ -316,8 +355,9 @@ constexpr int P1_TM_Q = 0, P1_TM_W = 64, P1_TM_K = 128, P1_TM_M = 192, P1_TM_COL
 
 __global__ void __launch_bounds__(128, 1)
     delta_post1_kernel(const __grid_constant__ Post1Maps maps, const __nv_bfloat16* __restrict__ dO,
-                       float* __restrict__ dQa, float* __restrict__ dW, float* __restrict__ dK1,
-                       float* __restrict__ dM, int L, int H, int NC, unsigned* err) {
+                       float* __restrict__ dQa, float* __restrict__ dW, float* __restrict__ dWT,
+                       float* __restrict__ dK1, float* __restrict__ dM, int L, int H, int NC,
+                       unsigned* err) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + P1_OFF_BARS);
     uint64_t* mbar = full + 1;
@@ -406,7 +446,23 @@ __global__ void __launch_bounds__(128, 1)
     if (!s_misc[1]) {
         const int j = tid;
         store_rows_transposed<C>(dQa + ch * C * D + j, tmem + P1_TM_Q + lane_base);
-        store_rows_transposed<C>(dW + ch * C * D + j, tmem + P1_TM_W + lane_base, -1.0f);
+        {  // -(dU~ S_0): [t][j] (coalesced over j) and its transpose [j][t]
+            float* wt = dWT + (ch * D + j) * C;
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                uint32_t x[32];
+                tc::tmem_ld32(tmem + P1_TM_W + lane_base + half * 32, x);
+                tc::tmem_wait_ld();
+                float* dw = dW + ch * C * D + (long long)half * 32 * D + j;
+#pragma unroll
+                for (int e = 0; e < 32; ++e) dw[e * D] = -__uint_as_float(x[e]);
+#pragma unroll
+                for (int e = 0; e < 32; e += 4)
+                    st4(wt + half * 32 + e,
+                        make_float4(-__uint_as_float(x[e]), -__uint_as_float(x[e + 1]),
+                                    -__uint_as_float(x[e + 2]), -__uint_as_float(x[e + 3])));
+            }
+        }
         store_rows_transposed<C>(dK1 + ch * C * D + j, tmem + P1_TM_K + lane_base);
         // M = 64 accumulator: lanes 32w + r (r < 16) hold row 16w + r
         uint32_t x0[32], x1[32];
@@ -434,10 +490,11 @@ __global__ void __launch_bounds__(128, 1)
 }  // namespace
 
 // ---------------------------------------------------------------- library-internal
-int edb_delta_chunked_post2(const void* q, const void* k, const void* v, const void* beta,
-                            const float* dQa, const float* dW, const float* dK1, const float* dM,
-                            const float* T, const float* G, const float* dU, void* gq, void* gk,
-                            void* gv, void* gbeta, int B, int L, int H, cudaStream_t st);
+int edb_delta_chunked_post2(const void* v, const void* beta, const float* dQa, const float* dW,
+                            const float* dWT, const float* dK1, const float* dM, const float* T,
+                            const float* G, const float* dU, const float* dUT, const float* Kf,
+                            const float* KT, const float* QT, void* gq, void* gk, void* gv,
+                            void* gbeta, int B, int L, int H, cudaStream_t st);
 
 size_t edb_delta_chunked_bwd_ws(int B, int L, int H) {
     return bwd_scratch_bytes((long long)B * H * ((L + C - 1) / C));
@@ -452,7 +509,7 @@ int edb_delta_chunked_bwd(const void* q, const void* k, const void* v, const voi
     BwdScratch w = carve_bwd(ws, nch);
     unsigned* err = edb::device_error_word();
     const __nv_bfloat16 *qb = (const __nv_bfloat16*)q, *kb = (const __nv_bfloat16*)k,
-                        *vb = (const __nv_bfloat16*)v, *bb = (const __nv_bfloat16*)beta,
+                        *bb = (const __nv_bfloat16*)beta,
                         *dob = (const __nv_bfloat16*)dO;
     cudaError_t e;
     if ((e = cudaFuncSetAttribute(delta_prep_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -473,15 +530,10 @@ int edb_delta_chunked_bwd(const void* q, const void* k, const void* v, const voi
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, SB_SMEM)) !=
         cudaSuccess)
         return (int)e;
-    delta_state_bwd_kernel<<<dim3(H, B), kStateThreads, SB_SMEM, st>>>(sm, w.dSCT, w.dU, H, NC,
-                                                                       err);
+    delta_state_bwd_kernel<<<dim3(H, B), kStateThreads, SB_SMEM, st>>>(sm, w.dSCT, w.dU, w.dUT, H,
+                                                                       NC, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
 
-    // post1 writes into the state kernel's operand buffers, which are dead now
-    float* dQa = w.Kf;
-    float* dW = w.dOT;
-    float* dK1 = w.QT;
-    float* dM = w.MT;
     Post1Maps pm;
     if ((s = make_box_map(&pm.S0T, resid, units * (NC + 1) * D, D, D))) return s;
     if ((s = make_box_map(&pm.dSCT, w.dSCT, nch * D, D, D))) return s;
@@ -490,10 +542,10 @@ int edb_delta_chunked_bwd(const void* q, const void* k, const void* v, const voi
     if ((e = cudaFuncSetAttribute(delta_post1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   P1_SMEM)) != cudaSuccess)
         return (int)e;
-    delta_post1_kernel<<<dim3(NC, H, B), 128, P1_SMEM, st>>>(pm, dob, dQa, dW, dK1, dM, L, H, NC,
-                                                             err);
+    delta_post1_kernel<<<dim3(NC, H, B), 128, P1_SMEM, st>>>(pm, dob, w.dQa, w.dW, w.dWT, w.dK1,
+                                                             w.dM, L, H, NC, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
 
-    return edb_delta_chunked_post2(q, k, v, beta, dQa, dW, dK1, dM, w.T, w.G, w.dU, gq, gk, gv,
-                                   gbeta, B, L, H, st);
+    return edb_delta_chunked_post2(v, beta, w.dQa, w.dW, w.dWT, w.dK1, w.dM, w.T, w.G, w.dU,
+                                   w.dUT, w.Kf, w.KT, w.QT, gq, gk, gv, gbeta, B, L, H, st);
 }
