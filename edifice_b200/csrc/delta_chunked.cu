@@ -41,8 +41,6 @@ using namespace dchunk;
 
 namespace {
 
-constexpr int kStateThreads = 128;
-
 // ------------------------------------------------------------------ scratch
 struct FwdScratch {
     float* Wn;   // [nch][C][D]  -W
@@ -297,25 +295,47 @@ struct StateMaps {
     CUtensorMap Wn, Q, KT, M;
 };
 
+// grid (H, B), one CTA per (b, h), chunks in order.  Warp roles:
+//   warps 0-3  read S out of TMEM at every chunk start and store S^T (residual);
+//   warps 4-7  store U0^T rows into TMEM ahead of each chunk, and read the
+//              finished O and U~ of the previous chunk out (o, residual U~);
+//   warp 8     lane 0 issues the TMA loads (2-stage ring) and the MMAs.
+// The TMEM accumulators U and O are double-buffered by chunk parity, so the
+// read-out of chunk c - 1 and the S^T store of chunk c run while the tensor
+// core works on chunk c:
+//   P1(c): D_U[b] = U0^T + S (-W)^T,  D_O[b] = S Q^T      (S read as A from TMEM)
+//   P2(c): D_O[b] += D_U[b] M^T,  S += D_U[b] (K^T)^T      (after S^T is read out)
+// mbarriers (per buffer where two chunks could otherwise alias one phase):
+//   full[s]       TMA stage s landed          u0_ready[b]  U0^T rows in D_U[b]
+//   p1[b], p2[b]  tcgen05.commit of P1 / P2   s_read       S^T of this chunk read
+namespace sf {
+constexpr int THREADS = 288;
 constexpr int OFF_W = 0;
 constexpr int OFF_Q = OFF_W + 4 * BOX_C;
 constexpr int OFF_KT = OFF_Q + 4 * BOX_C;
 constexpr int OFF_M = OFF_KT + 2 * BOX_D;
 constexpr int STAGE_BYTES = OFF_M + 2 * BOX_C;  // 112 KB
 constexpr int OFF_BARS = 2 * STAGE_BYTES;
-constexpr int STATE_SMEM = OFF_BARS + 64;
-constexpr int TM_S = 0, TM_U = 128, TM_O = 192, TM_COLS = 256;
+constexpr int SMEM = OFF_BARS + 128;
+constexpr int TM_S = 0, TM_U = 128, TM_O = 256, TM_COLS = 512;  // U, O: 2 x 64 columns
+}  // namespace sf
 
-__global__ void __launch_bounds__(kStateThreads, 1)
+__global__ void __launch_bounds__(sf::THREADS, 1)
     delta_state_fwd_kernel(const __grid_constant__ StateMaps maps, const float* __restrict__ U0T,
                            float* __restrict__ resid, __nv_bfloat16* __restrict__ o, int L, int H,
                            int NC, unsigned* err) {
+    using namespace sf;
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BARS);  // [2]
-    uint64_t* mbar = full + 2;
-    uint32_t* s_misc = reinterpret_cast<uint32_t*>(mbar + 1);  // [0] tmem base, [1] abort
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BARS);
+    uint64_t* full = bars;          // [2]
+    uint64_t* u0_ready = bars + 2;  // [2]
+    uint64_t* p1 = bars + 4;        // [2]
+    uint64_t* p2 = bars + 6;        // [2]
+    uint64_t* s_read = bars + 8;
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 9);
+    volatile uint32_t* s_abort = s_tmem + 1;
     const int h = blockIdx.x, b = blockIdx.y;
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const long long bh = (long long)b * H + h;
     const long long ch0 = bh * NC;
     // residuals: S^T per chunk start [units][NC+1][D][D], then U~ [units][NC][C][D]
@@ -330,51 +350,21 @@ __global__ void __launch_bounds__(kStateThreads, 1)
         return;
     }
     if (warp == 0) {
-        tc::tmem_alloc(s_misc, TM_COLS);
+        tc::tmem_alloc(s_tmem, TM_COLS);
         tc::tmem_relinquish();
     }
     if (tid == 0) {
-        s_misc[1] = 0;
-        mbar_init(&full[0], 1);
-        mbar_init(&full[1], 1);
-        mbar_init(mbar, 1);
+        *s_abort = 0;
+        for (int e = 0; e < 9; ++e) mbar_init(&bars[e], (e >= 2 && e < 4) || e == 8 ? 4 : 1);
         fence_mbar_init();
     }
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
-    const uint32_t tmem = s_misc[0];
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const int i = tid;  // TMEM lane = value-dim row of S
-
-    auto issue = [&](int c) {
-        uint8_t* st = smem + (c & 1) * STAGE_BYTES;
-        uint64_t* bar = &full[c & 1];
-        const int rc = (int)((ch0 + c) * C), rd = (int)((ch0 + c) * D);
-        mbar_arrive_expect_tx(bar, STAGE_BYTES);
-        for (int bx = 0; bx < 4; ++bx) {
-            tma_load_2d(st + OFF_W + bx * BOX_C, &maps.Wn, bar, bx * 32, rc);
-            tma_load_2d(st + OFF_Q + bx * BOX_C, &maps.Q, bar, bx * 32, rc);
-        }
-        for (int bx = 0; bx < 2; ++bx) {
-            tma_load_2d(st + OFF_KT + bx * BOX_D, &maps.KT, bar, bx * 32, rd);
-            tma_load_2d(st + OFF_M + bx * BOX_C, &maps.M, bar, bx * 32, rc);
-        }
-    };
-    int issued = 0, landed = 0;
-    if (tid == 0) {
-        prefetch_tmap(&maps.Wn);
-        prefetch_tmap(&maps.Q);
-        prefetch_tmap(&maps.KT);
-        prefetch_tmap(&maps.M);
-        issue(0);
-        issued = 1;
-        if (NC > 1) {
-            issue(1);
-            issued = 2;
-        }
-    }
-    {  // S = 0
+    const uint32_t tmem = *s_tmem;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const int i = (warp & 3) * 32 + lane;  // TMEM lane = value-dim row of S
+    if (warp < 4) {  // S = 0
         uint32_t z[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) z[e] = 0u;
@@ -382,116 +372,171 @@ __global__ void __launch_bounds__(kStateThreads, 1)
         for (int cc = 0; cc < D / 32; ++cc) tc::tmem_st32(tmem + TM_S + lane_base + cc * 32, z);
         tc::tmem_wait_st();
     }
-    constexpr uint32_t idN64 = idesc_tf32(128, C);
-    constexpr uint32_t idN128 = idesc_tf32(128, D);
-    uint32_t mph = 0;
-    bool mma_pending = false;
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+        if (mbar_wait_bounded(bar, parity, err, EDB_DEVERR_DELTA_PIPE)) return true;
+        *s_abort = 1;
+        return false;
+    };
 
-    for (int c = 0; c < NC; ++c) {
-        // U0^T row i -> D_U; S row i -> S^T column i of residual c
-        {
-            const float* u = U0T + ((ch0 + c) * D + i) * C;
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                uint32_t r[32];
-#pragma unroll
-                for (int e = 0; e < 32; e += 4) {
-                    const float4 f = *reinterpret_cast<const float4*>(u + half * 32 + e);
-                    r[e] = __float_as_uint(f.x);
-                    r[e + 1] = __float_as_uint(f.y);
-                    r[e + 2] = __float_as_uint(f.z);
-                    r[e + 3] = __float_as_uint(f.w);
+    if (warp == 8) {
+        // ---------------------------------------------------------- TMA + MMA
+        if (lane == 0) {
+            auto issue = [&](int c) {
+                uint8_t* st = smem + (c & 1) * STAGE_BYTES;
+                uint64_t* bar = &full[c & 1];
+                const int rc = (int)((ch0 + c) * C), rd = (int)((ch0 + c) * D);
+                mbar_arrive_expect_tx(bar, STAGE_BYTES);
+                for (int bx = 0; bx < 4; ++bx) {
+                    tma_load_2d(st + OFF_W + bx * BOX_C, &maps.Wn, bar, bx * 32, rc);
+                    tma_load_2d(st + OFF_Q + bx * BOX_C, &maps.Q, bar, bx * 32, rc);
                 }
-                tc::tmem_st32(tmem + TM_U + lane_base + half * 32, r);
+                for (int bx = 0; bx < 2; ++bx) {
+                    tma_load_2d(st + OFF_KT + bx * BOX_D, &maps.KT, bar, bx * 32, rd);
+                    tma_load_2d(st + OFF_M + bx * BOX_C, &maps.M, bar, bx * 32, rc);
+                }
+            };
+            prefetch_tmap(&maps.Wn);
+            prefetch_tmap(&maps.Q);
+            prefetch_tmap(&maps.KT);
+            prefetch_tmap(&maps.M);
+            int issued = 0, landed = 0, committed = 0, done = 0;
+            issue(0);
+            issued = 1;
+            if (NC > 1) {
+                issue(1);
+                issued = 2;
             }
-            if (st_T != nullptr)
-                store_rows_transposed<D>(st_T + (long long)c * D * D + i, tmem + TM_S + lane_base);
-            tc::tmem_wait_st();
-        }
-        tc::fence_before_sync();
-        __syncthreads();
-        tc::fence_after_sync();
-        if (tid == 0) {
-            const uint8_t* st = smem + (c & 1) * STAGE_BYTES;
-            bool ok = mbar_wait_bounded(&full[c & 1], (c >> 1) & 1, err, EDB_DEVERR_DELTA_PIPE);
-            if (ok) {
+            constexpr uint32_t idN64 = idesc_tf32(128, C);
+            constexpr uint32_t idN128 = idesc_tf32(128, D);
+            for (int c = 0; c < NC; ++c) {
+                const int bf = c & 1;
+                const uint32_t par = (c >> 1) & 1;
+                const uint8_t* st = smem + bf * STAGE_BYTES;
+                const uint32_t tU = tmem + TM_U + bf * 64, tO = tmem + TM_O + bf * 64;
+                if (!wait(&full[bf], par)) break;
                 landed = c + 1;
+                if (!wait(&u0_ready[bf], par)) break;
                 tc::fence_after_sync();
 #pragma unroll
                 for (int kk = 0; kk < D / 8; ++kk) {
-                    mma_tf32_ts(tmem + TM_U, tmem + TM_S + kk * 8, kdesc(st + OFF_W, BOX_C, kk),
-                                idN64, 1);
-                    mma_tf32_ts(tmem + TM_O, tmem + TM_S + kk * 8, kdesc(st + OFF_Q, BOX_C, kk),
-                                idN64, kk > 0);
+                    mma_tf32_ts(tU, tmem + TM_S + kk * 8, kdesc(st + OFF_W, BOX_C, kk), idN64, 1);
+                    mma_tf32_ts(tO, tmem + TM_S + kk * 8, kdesc(st + OFF_Q, BOX_C, kk), idN64,
+                                kk > 0);
                 }
-                tc::commit(mbar);
-                mma_pending = true;
-                ok = mbar_wait_bounded(mbar, mph, err, EDB_DEVERR_DELTA_PIPE);
-                if (ok) {
-                    mph ^= 1u;
-                    mma_pending = false;
-                }
-            }
-            if (ok) {
+                tc::commit(&p1[bf]);
+                committed = 2 * c + 1;
+                if (!wait(&p1[bf], par)) break;
+                done = 2 * c + 1;
+                if (!wait(s_read, c & 1)) break;
                 tc::fence_after_sync();
 #pragma unroll
                 for (int kk = 0; kk < C / 8; ++kk) {
-                    mma_tf32_ts(tmem + TM_O, tmem + TM_U + kk * 8, kdesc(st + OFF_M, BOX_C, kk),
-                                idN64, 1);
-                    mma_tf32_ts(tmem + TM_S, tmem + TM_U + kk * 8, kdesc(st + OFF_KT, BOX_D, kk),
-                                idN128, 1);
+                    mma_tf32_ts(tO, tU + kk * 8, kdesc(st + OFF_M, BOX_C, kk), idN64, 1);
+                    mma_tf32_ts(tmem + TM_S, tU + kk * 8, kdesc(st + OFF_KT, BOX_D, kk), idN128,
+                                1);
                 }
-                tc::commit(mbar);
-                mma_pending = true;
-                ok = mbar_wait_bounded(mbar, mph, err, EDB_DEVERR_DELTA_PIPE);
-                if (ok) {
-                    mph ^= 1u;
-                    mma_pending = false;
+                tc::commit(&p2[bf]);
+                committed = 2 * c + 2;
+                if (!wait(&p2[bf], par)) break;
+                done = 2 * c + 2;
+                if (c + 2 < NC) {
+                    issue(c + 2);
+                    issued = c + 3;
                 }
             }
-            if (ok && c + 2 < NC) {
-                issue(c + 2);
-                issued = c + 3;
+            if (*s_abort) {
+                // wait (bounded) for the copies and MMAs still in flight before the
+                // shared memory and TMEM they target are released
+                for (int cc = landed; cc < issued; ++cc)
+                    mbar_wait_bounded(&full[cc & 1], (cc >> 1) & 1, err, EDB_DEVERR_DELTA_PIPE);
+                if (committed > done) {
+                    const int cc = (committed - 1) >> 1;
+                    uint64_t* bar = (committed & 1) ? &p1[cc & 1] : &p2[cc & 1];
+                    mbar_wait_bounded(bar, (cc >> 1) & 1, err, EDB_DEVERR_DELTA_PIPE);
+                }
             }
-            if (!ok) s_misc[1] = 1;
         }
-        tc::fence_before_sync();
-        __syncthreads();
-        tc::fence_after_sync();
-        if (s_misc[1]) break;
-        // O^T row i (value dim i, tokens t) -> o[b, c C + t, h, i]
-        {
-            uint32_t x0[32], x1[32];
-            tc::tmem_ld32(tmem + TM_O + lane_base, x0);
-            tc::tmem_ld32(tmem + TM_O + lane_base + 32, x1);
-            tc::tmem_wait_ld();
-            __nv_bfloat16* op = o + (((long long)b * L + c * C) * H + h) * D + i;
-            const long long ts = (long long)H * D;
+    } else if (warp < 4) {
+        // ---------------------------------------------------------- S^T residual
+        for (int c = 0; c <= NC; ++c) {
+            if (c > 0 && !wait(&p2[(c - 1) & 1], ((c - 1) >> 1) & 1)) break;
+            if (*s_abort) break;
+            tc::fence_after_sync();
+            if (st_T != nullptr)
+                store_rows_transposed<D>(st_T + (long long)c * D * D + i, tmem + TM_S + lane_base);
+            if (c == NC) break;
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_read);
+        }
+    } else {
+        // ---------------------------------------------------------- U0^T in, O / U~ out
+        float4 u[16];
+        auto load_u0 = [&](int c) {
+            const float4* src = reinterpret_cast<const float4*>(U0T + ((ch0 + c) * D + i) * C);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) u[e] = src[e];
+        };
+        auto readout = [&](int c) {  // O^T row i -> o[b, cC + t, h, i]; U~^T row i -> U~[c][t][i]
+            const int bf = c & 1;
             const int nt = min(C, L - c * C);
 #pragma unroll
-            for (int t = 0; t < 32; ++t)
-                if (t < nt) op[t * ts] = __float2bfloat16(__uint_as_float(x0[t]));
+            for (int half = 0; half < 2; ++half) {
+                uint32_t x[32];
+                tc::tmem_ld32(tmem + TM_O + bf * 64 + lane_base + half * 32, x);
+                tc::tmem_wait_ld();
+                __nv_bfloat16* op =
+                    o + (((long long)b * L + c * C + half * 32) * H + h) * D + i;
 #pragma unroll
-            for (int t = 0; t < 32; ++t)
-                if (t + 32 < nt) op[(t + 32) * ts] = __float2bfloat16(__uint_as_float(x1[t]));
+                for (int t = 0; t < 32; ++t) {
+                    if (half * 32 + t < nt) *op = __float2bfloat16(__uint_as_float(x[t]));
+                    op += H * D;
+                }
+            }
+            if (ures != nullptr)
+                store_rows_transposed<C>(ures + (long long)c * C * D + i,
+                                         tmem + TM_U + bf * 64 + lane_base);
+        };
+        load_u0(0);
+        for (int c = 0; c < NC; ++c) {
+            const int bf = c & 1;
+            // P1(c - 1) was issued, so u0_ready[bf ^ 1] is consumed and the
+            // buffer pair bf (last used by chunk c - 2, read out already) is free
+            if (c > 0 && !wait(&p1[bf ^ 1], ((c - 1) >> 1) & 1)) break;
+            if (*s_abort) break;
+            {
+                uint32_t r[32];
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        r[4 * e] = __float_as_uint(u[8 * half + e].x);
+                        r[4 * e + 1] = __float_as_uint(u[8 * half + e].y);
+                        r[4 * e + 2] = __float_as_uint(u[8 * half + e].z);
+                        r[4 * e + 3] = __float_as_uint(u[8 * half + e].w);
+                    }
+                    tc::tmem_st32(tmem + TM_U + bf * 64 + lane_base + half * 32, r);
+                }
+                tc::tmem_wait_st();
+            }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&u0_ready[bf]);
+            if (c > 0) {
+                if (!wait(&p2[bf ^ 1], ((c - 1) >> 1) & 1)) break;
+                tc::fence_after_sync();
+                readout(c - 1);
+            }
+            // the next rows land while P1(c) runs
+            if (c + 1 < NC) load_u0(c + 1);
         }
-        // U~^T row i -> U~[c][t][i]
-        if (ures != nullptr) store_rows_transposed<C>(ures + (long long)c * C * D + i,
-                                                      tmem + TM_U + lane_base);
-        tc::fence_before_sync();
-        __syncthreads();
-        tc::fence_after_sync();
-    }
-    if (s_misc[1]) {
-        // Abort: wait (bounded) for the copies and MMAs still in flight before
-        // the shared memory and TMEM they target are released.
-        if (tid == 0) {
-            for (int cc = landed; cc < issued; ++cc)
-                mbar_wait_bounded(&full[cc & 1], (cc >> 1) & 1, err, EDB_DEVERR_DELTA_PIPE);
-            if (mma_pending) mbar_wait_bounded(mbar, mph, err, EDB_DEVERR_DELTA_PIPE);
+        if (!*s_abort && wait(&p2[(NC - 1) & 1], ((NC - 1) >> 1) & 1)) {
+            tc::fence_after_sync();
+            readout(NC - 1);
         }
-    } else if (st_T != nullptr) {
-        store_rows_transposed<D>(st_T + (long long)NC * D * D + i, tmem + TM_S + lane_base);
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -500,7 +545,6 @@ __global__ void __launch_bounds__(kStateThreads, 1)
         tc::tmem_dealloc(tmem, TM_COLS);
     }
 }
-
 }  // namespace
 
 // ---------------------------------------------------------------- library-internal
@@ -537,9 +581,9 @@ int edb_delta_chunked_fwd(const void* q, const void* k, const void* v, const voi
     if ((s = make_box_map(&maps.KT, w.KT, nch * D, C, D))) return s;
     if ((s = make_box_map(&maps.M, w.M, nch * C, C, C))) return s;
     e = cudaFuncSetAttribute(delta_state_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             STATE_SMEM);
+                             sf::SMEM);
     if (e != cudaSuccess) return (int)e;
-    delta_state_fwd_kernel<<<dim3(H, B), kStateThreads, STATE_SMEM, st>>>(
+    delta_state_fwd_kernel<<<dim3(H, B), sf::THREADS, sf::SMEM, st>>>(
         maps, w.U0T, resid, (__nv_bfloat16*)o, L, H, NC, edb::device_error_word());
     return edb::status_from_cuda(cudaGetLastError());
 }
