@@ -83,7 +83,7 @@ constexpr int OFF_Q = OFF_K + 4 * BOX_C;    // [C][D]
 constexpr int OFF_KT = OFF_Q + 4 * BOX_C;   // [D][C]  K-major (K = token)
 constexpr int OFF_VT = OFF_KT + 2 * BOX_D;  // [D][C]
 constexpr int OFF_TB = OFF_VT + 2 * BOX_D;  // [C][C]  T diag(beta)
-constexpr int OFF_F = OFF_TB + 2 * BOX_C;   // f32: V rows [C][D] while staging, then G | T | ATn
+constexpr int OFF_F = OFF_TB + 2 * BOX_C;   // f32: V [C][D] K-major while staging, then G | T | Ys
 constexpr int F_FLOATS = 2 * C * PC + C * C;
 static_assert(F_FLOATS >= C * D, "V rows fit the solve scratch");
 constexpr int OFF_BS = OFF_F + F_FLOATS * 4;
@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(prep::THREADS, 1)
     float* F = reinterpret_cast<float*>(smem + OFF_F);
     float* Gs = F;                   // [C][PC]
     float* Tm = F + C * PC;          // [C][PC]
-    float* ATn = F + 2 * C * PC;     // [C][C]
+    float* Ys = F + 2 * C * PC;      // solve scratch
     float* bs = reinterpret_cast<float*>(smem + OFF_BS);
     uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint32_t* s_misc = reinterpret_cast<uint32_t*>(mbar + 1);  // [0] tmem base, [1] abort
@@ -152,29 +152,30 @@ __global__ void __launch_bounds__(prep::THREADS, 1)
             st4(ws.Q + (ch * C + t) * D + j8, q0);
             st4(ws.Q + (ch * C + t) * D + j8 + 4, q1);
             Vec16<__nv_bfloat16>::unpack(rv[n], f);
-            st4(F + t * D + j8, make_float4(f[0], f[1], f[2], f[3]));
-            st4(F + t * D + j8 + 4, make_float4(f[4], f[5], f[6], f[7]));
+            st4(reinterpret_cast<float*>(smem + OFF_F + kmaj_off4(t, j8, C)), make_float4(f[0], f[1], f[2], f[3]));
+            st4(reinterpret_cast<float*>(smem + OFF_F + kmaj_off4(t, j8 + 4, C)), make_float4(f[4], f[5], f[6], f[7]));
         }
     }
     if (tid < C)
         bs[tid] = tid < nvalid ? __bfloat162float(beta[((long long)b * L + t0 + tid) * H + h])
                                : 0.0f;
     __syncthreads();
-    // ---- K^T, V^T tiles (thread: one row d, 4 tokens); K^T also to HBM [d][t]
-    for (int idx = tid; idx < D * (C / 4); idx += THREADS) {
-        const int t4 = (idx % (C / 4)) * 4, j = idx / (C / 4);
-        float kv[4], vv[4];
+    // ---- K^T, V^T tiles.  A warp takes 32 consecutive tokens t and 4 columns
+    // j: one float4 read per row tile (8 rows cover the 8 swizzled 16-byte
+    // slots), 4 scalar writes into one 128-byte row of each transposed tile
+    // (conflict free), and K^T[j][t] to HBM coalesced over t.
+    for (int idx = tid; idx < C * (D / 4); idx += THREADS) {
+        const int t = idx % C, j4 = (idx / C) * 4;
+        const float4 k4 = ld4(reinterpret_cast<const float*>(smem + OFF_K + kmaj_off4(t, j4, C)));
+        const float4 v4 = ld4(reinterpret_cast<const float*>(smem + OFF_F + kmaj_off4(t, j4, C)));
+        const float kv[4] = {k4.x, k4.y, k4.z, k4.w}, vv[4] = {v4.x, v4.y, v4.z, v4.w};
+        const uint32_t o = (t & 3) * 4;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            kv[e] = *reinterpret_cast<const float*>(smem + OFF_K + kmaj_off4(t4 + e, j & ~3, C) +
-                                                    (j & 3) * 4);
-            vv[e] = F[(t4 + e) * D + j];
+            *reinterpret_cast<float*>(smem + OFF_KT + kmaj_off4(j4 + e, t & ~3, D) + o) = kv[e];
+            *reinterpret_cast<float*>(smem + OFF_VT + kmaj_off4(j4 + e, t & ~3, D) + o) = vv[e];
+            ws.KT[(ch * D + j4 + e) * C + t] = kv[e];
         }
-        const float4 k4 = make_float4(kv[0], kv[1], kv[2], kv[3]);
-        st4(reinterpret_cast<float*>(smem + OFF_KT + kmaj_off4(j, t4, D)), k4);
-        st4(reinterpret_cast<float*>(smem + OFF_VT + kmaj_off4(j, t4, D)),
-            make_float4(vv[0], vv[1], vv[2], vv[3]));
-        st4(ws.KT + (ch * D + j) * C + t4, k4);
     }
     fence_proxy_async();
     tc::fence_before_sync();
@@ -235,7 +236,7 @@ __global__ void __launch_bounds__(prep::THREADS, 1)
     }
     __syncthreads();
     if (!s_misc[1]) {
-        prep_solve(Gs, bs, ATn, Tm);
+        prep_solve<THREADS>(Gs, bs, Ys, Tm);
         // ---- T diag(beta) -> K-major tile [t][s]
         for (int idx = tid; idx < C * (C / 4); idx += THREADS) {
             const int t = idx / (C / 4), s4 = (idx % (C / 4)) * 4;

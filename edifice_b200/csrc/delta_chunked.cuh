@@ -199,38 +199,92 @@ static __device__ __forceinline__ void prep_products(const float* Ks, const floa
         }
 }
 
-// Tm = (I + A)^-1 with A = tril(diag(beta) Gs, -1).  ATn ([C][C], stride C)
-// is scratch.  Right-looking substitution: thread j < C holds column j in
-// registers; once row s is final it is folded into every later row, so the
-// critical path is one FMA per row.  Caller syncs before; syncs inside.
-static __device__ __forceinline__ void prep_solve(const float* Gs, const float* bs, float* ATn,
+// One block diagonal d = i - j of the blocked solve below: every block (i, i - d)
+//   Y_ij = sum_{k=j}^{i-1} N_ik T_kj,   T_ij = T_ii Y_ij,   N = -diag(beta) G
+// with each thread's NE entries accumulated side by side (independent chains
+// over unrolled 16-step block products).
+template <int LEV, int NTH>
+static __device__ __forceinline__ void prep_solve_level(const float* Gs, const float* bs,
+                                                        float* Ys, float* Tm) {
+    constexpr int NE = (4 - LEV) * 256 / NTH;
+    static_assert(NE * NTH == (4 - LEV) * 256, "thread count divides the level");
+    const int tid = threadIdx.x;
+    float acc[NE];
+    int g0[NE], t0[NE];
+#pragma unroll
+    for (int m = 0; m < NE; ++m) {
+        const int e = tid + NTH * m, i = LEV + (e >> 8), j = i - LEV, r = (e >> 4) & 15, c = e & 15;
+        g0[m] = (16 * i + r) * PC + 16 * j;
+        t0[m] = 16 * j * PC + 16 * j + c;
+        acc[m] = 0.0f;
+    }
+#pragma unroll
+    for (int kk = 0; kk < LEV; ++kk)
+#pragma unroll
+        for (int s = 0; s < 16; ++s)
+#pragma unroll
+            for (int m = 0; m < NE; ++m)
+                acc[m] = fmaf(Gs[g0[m] + 16 * kk + s], Tm[t0[m] + (16 * kk + s) * PC], acc[m]);
+#pragma unroll
+    for (int m = 0; m < NE; ++m) {
+        const int e = tid + NTH * m, i = LEV + (e >> 8), r = (e >> 4) & 15;
+        Ys[e] = -bs[16 * i + r] * acc[m];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < NE; ++m) {
+        const int e = tid + NTH * m, i = LEV + (e >> 8), r = (e >> 4) & 15, c = e & 15;
+        g0[m] = (16 * i + r) * PC + 16 * i;  // row r of T_ii (zero above its diagonal)
+        t0[m] = (e & ~255) + c;              // column c of Y_ij
+        acc[m] = 0.0f;
+    }
+#pragma unroll
+    for (int s = 0; s < 16; ++s)
+#pragma unroll
+        for (int m = 0; m < NE; ++m) acc[m] = fmaf(Tm[g0[m] + s], Ys[t0[m] + 16 * s], acc[m]);
+#pragma unroll
+    for (int m = 0; m < NE; ++m) {
+        const int e = tid + NTH * m, i = LEV + (e >> 8), j = i - LEV, r = (e >> 4) & 15, c = e & 15;
+        Tm[(16 * i + r) * PC + 16 * j + c] = acc[m];
+    }
+    __syncthreads();
+}
+
+// Tm = (I + A)^-1 with A = tril(diag(beta) Gs, -1), in 16 x 16 blocks: the
+// four diagonal blocks by substitution (one thread per column, 16 steps), then
+// the blocks below the diagonal one block diagonal at a time (block row i of
+// (I + A) T = I gives T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj).  NTH threads
+// (128 or 256); Ys is scratch of 768 floats.  Caller syncs before; syncs
+// inside.  Tm is written in full (zero above the diagonal).
+template <int NTH>
+static __device__ __forceinline__ void prep_solve(const float* Gs, const float* bs, float* Ys,
                                                   float* Tm) {
-    for (int idx = threadIdx.x; idx < C * C; idx += blockDim.x) {
-        const int s = idx / C, r = idx % C;  // ATn[s][r] = -A[r][s]
-        ATn[idx] = s < r ? -bs[r] * Gs[r * PC + s] : 0.0f;
-    }
-    __syncthreads();
-    if (threadIdx.x < C) {
-        const int j = threadIdx.x;
-        float acc[C];
+    const int tid = threadIdx.x;
+    if (tid < C) {
+        const int o = 16 * (tid >> 4), j = tid & 15;
+        float x[16];
 #pragma unroll
-        for (int r = 0; r < C; ++r) acc[r] = (r == j) ? 1.0f : 0.0f;
+        for (int r = 0; r < 16; ++r) x[r] = r == j ? 1.0f : 0.0f;
 #pragma unroll
-        for (int s = 0; s < C - 1; ++s) {
-            const float xs = acc[s];
+        for (int s = 0; s < 15; ++s)
 #pragma unroll
-            for (int r = (s + 1) & ~3; r < C; r += 4) {  // lanes r <= s add 0
-                const float4 a = ld4(ATn + s * C + r);
-                acc[r] = fmaf(a.x, xs, acc[r]);
-                acc[r + 1] = fmaf(a.y, xs, acc[r + 1]);
-                acc[r + 2] = fmaf(a.z, xs, acc[r + 2]);
-                acc[r + 3] = fmaf(a.w, xs, acc[r + 3]);
-            }
+            for (int r = s + 1; r < 16; ++r)
+                x[r] = fmaf(-bs[o + r] * Gs[(o + r) * PC + o + s], x[s], x[r]);
+#pragma unroll
+        for (int r = 0; r < 16; ++r) Tm[(o + r) * PC + o + j] = x[r];
+    } else {
+        // the six blocks above the diagonal are zero
+        for (int idx = tid - C; idx < 6 * 256; idx += NTH - C) {
+            const int blk = idx >> 8, r = (idx >> 4) & 15, c = idx & 15;
+            const int bi = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
+            const int bj = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
+            Tm[(16 * bi + r) * PC + 16 * bj + c] = 0.0f;
         }
-#pragma unroll
-        for (int r = 0; r < C; ++r) Tm[r * PC + j] = acc[r];
     }
     __syncthreads();
+    prep_solve_level<1, NTH>(Gs, bs, Ys, Tm);
+    prep_solve_level<2, NTH>(Gs, bs, Ys, Tm);
+    prep_solve_level<3, NTH>(Gs, bs, Ys, Tm);
 }
 
 // out = (T diag(beta) X) for this thread's rows ty + 16 r and columns

@@ -107,8 +107,8 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
     float* Gs = dOs + C * PP;    // [C][PC]  K K^T
     float* Ms = Gs + C * PC;     // [C][PC]  tril(Q K^T)
     float* Tm = Ms + C * PC;     // [C][PC]  T
-    float* ATn = Tm + C * PC;    // [C][C]   solve scratch
-    float* bs = ATn + C * C;     // [C]
+    float* Ys = Tm + C * PC;     // [C][C]   solve scratch
+    float* bs = Ys + C * C;      // [C]
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x;
     const long long ch = ((long long)b * H + h) * NC + c;
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
         ws.G[ch * C * C + idx] = Gs[idx / C * PC + idx % C];
         ws.MT[ch * C * C + idx] = Ms[(idx % C) * PC + idx / C];  // MT[s][t] = M[t][s]
     }
-    prep_solve(Gs, bs, ATn, Tm);
+    prep_solve<kPrepThreads>(Gs, bs, Ys, Tm);
     for (int idx = tid; idx < C * C; idx += kPrepThreads)
         ws.T[ch * C * C + idx] = Tm[idx / C * PC + idx % C];
     float w[4][8];
