@@ -16,8 +16,9 @@
 // o_t = S_t q_t, regrouped (T solves the within-chunk dependence of the errors).
 //
 // Kernels:
-//   delta_prep_fwd_kernel   one CTA per chunk (all chunks at once), tcgen05
-//                           kind::tf32 for K K^T, Q K^T, W and U0, SIMT for the
+//   delta_prep_kernel<true> (delta_prep.cuh) one CTA per chunk (all chunks at
+//                           once), tcgen05 kind::f16 for K K^T, Q K^T, W and U0
+//                           (T_b as a bf16 hi/lo pair), SIMT for the blocked
 //                           unit-triangular solve for T; writes -W, Q, K^T, U0^T
 //                           and M (f32) to scratch.
 //   delta_state_fwd_kernel  one CTA per (b, h), chunks in order, tcgen05
@@ -36,6 +37,7 @@
 #include <math.h>
 
 #include "delta_chunked.cuh"
+#include "delta_prep.cuh"
 
 using namespace dchunk;
 
@@ -64,231 +66,6 @@ FwdScratch carve_fwd(void* ws, long long nch) {
     s.U0T = reinterpret_cast<float*>(p + 3 * cd);
     s.M = reinterpret_cast<float*>(p + 4 * cd);
     return s;
-}
-
-// ------------------------------------------------------------------ prep (tcgen05)
-// grid (NC, H, B), 128 threads, one chunk per CTA, all chunks at once.  The
-// threads stage f32 K-major SWIZZLE_128B operand tiles in shared memory (bf16 ->
-// f32 is exact, and so is the tf32 view of a bf16 value), the products run on
-// tcgen05 kind::tf32 with the accumulators in TMEM:
-//   G = K K^T, Mq = Q K^T                M=64,  N=64, K=128   TMEM cols [0,64), [64,128)
-//   W^T = K^T T_b^T, U0^T = V^T T_b^T    M=128, N=64, K=64    TMEM cols [128,192), [192,256)
-// and the unit-triangular solve for T between them is SIMT on G read out of TMEM.
-// Rows past L load as zero with beta 0, which makes their W / U0 rows zero, so
-// the padded tail leaves S untouched.
-namespace prep {
-constexpr int THREADS = 128;
-constexpr int OFF_K = 0;                    // [C][D]  K-major (K = d)
-constexpr int OFF_Q = OFF_K + 4 * BOX_C;    // [C][D]
-constexpr int OFF_KT = OFF_Q + 4 * BOX_C;   // [D][C]  K-major (K = token)
-constexpr int OFF_VT = OFF_KT + 2 * BOX_D;  // [D][C]
-constexpr int OFF_TB = OFF_VT + 2 * BOX_D;  // [C][C]  T diag(beta)
-constexpr int OFF_F = OFF_TB + 2 * BOX_C;   // f32: V [C][D] K-major while staging, then G | T | Ys
-constexpr int F_FLOATS = 2 * C * PC + C * C;
-static_assert(F_FLOATS >= C * D, "V rows fit the solve scratch");
-constexpr int OFF_BS = OFF_F + F_FLOATS * 4;
-constexpr int OFF_BAR = OFF_BS + C * 4;
-constexpr int SMEM = OFF_BAR + 64;
-constexpr int TM_G = 0, TM_M = 64, TM_W = 128, TM_U = 192, TM_COLS = 256;
-}  // namespace prep
-
-__global__ void __launch_bounds__(prep::THREADS, 1)
-    delta_prep_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
-                          const __nv_bfloat16* __restrict__ v,
-                          const __nv_bfloat16* __restrict__ beta, FwdScratch ws, int L, int H,
-                          int NC, unsigned* err) {
-    using namespace prep;
-    extern __shared__ __align__(1024) uint8_t smem[];
-    float* F = reinterpret_cast<float*>(smem + OFF_F);
-    float* Gs = F;                   // [C][PC]
-    float* Tm = F + C * PC;          // [C][PC]
-    float* Ys = F + 2 * C * PC;      // solve scratch
-    float* bs = reinterpret_cast<float*>(smem + OFF_BS);
-    uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-    uint32_t* s_misc = reinterpret_cast<uint32_t*>(mbar + 1);  // [0] tmem base, [1] abort
-    const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const long long ch = ((long long)b * H + h) * NC + c;
-    const int t0 = c * C, nvalid = min(C, L - t0);
-    const long long row0 = (((long long)b * L + t0) * H + h) * D, ts = (long long)H * D;
-
-    if ((smem_u32(smem) & 1023u) != 0) {  // SW128 tiles need 1 KB alignment
-        if (tid == 0) edb_flag_error(err, EDB_DEVERR_DELTA_PIPE);
-        return;
-    }
-    if (warp == 0) {
-        tc::tmem_alloc(s_misc, TM_COLS);
-        tc::tmem_relinquish();
-    }
-    if (tid == 0) {
-        s_misc[1] = 0;
-        mbar_init(mbar, 1);
-        fence_mbar_init();
-    }
-    // ---- K, Q -> swizzled row tiles, V -> plain rows; the f32 Q rows also to HBM
-    {
-        constexpr int N = C * (D / 8) / THREADS;
-        uint4 rk[N], rq[N], rv[N];
-#pragma unroll
-        for (int n = 0; n < N; ++n) {
-            const int idx = tid + n * THREADS, t = idx / (D / 8), j8 = (idx % (D / 8)) * 8;
-            const bool ok = t < nvalid;
-            const long long off = row0 + t * ts + j8;
-            rk[n] = ok ? *reinterpret_cast<const uint4*>(k + off) : make_uint4(0u, 0u, 0u, 0u);
-            rq[n] = ok ? *reinterpret_cast<const uint4*>(q + off) : make_uint4(0u, 0u, 0u, 0u);
-            rv[n] = ok ? *reinterpret_cast<const uint4*>(v + off) : make_uint4(0u, 0u, 0u, 0u);
-        }
-#pragma unroll
-        for (int n = 0; n < N; ++n) {
-            const int idx = tid + n * THREADS, t = idx / (D / 8), j8 = (idx % (D / 8)) * 8;
-            float f[8];
-            Vec16<__nv_bfloat16>::unpack(rk[n], f);
-            st4(reinterpret_cast<float*>(smem + OFF_K + kmaj_off4(t, j8, C)), make_float4(f[0], f[1], f[2], f[3]));
-            st4(reinterpret_cast<float*>(smem + OFF_K + kmaj_off4(t, j8 + 4, C)), make_float4(f[4], f[5], f[6], f[7]));
-            Vec16<__nv_bfloat16>::unpack(rq[n], f);
-            const float4 q0 = make_float4(f[0], f[1], f[2], f[3]), q1 = make_float4(f[4], f[5], f[6], f[7]);
-            st4(reinterpret_cast<float*>(smem + OFF_Q + kmaj_off4(t, j8, C)), q0);
-            st4(reinterpret_cast<float*>(smem + OFF_Q + kmaj_off4(t, j8 + 4, C)), q1);
-            st4(ws.Q + (ch * C + t) * D + j8, q0);
-            st4(ws.Q + (ch * C + t) * D + j8 + 4, q1);
-            Vec16<__nv_bfloat16>::unpack(rv[n], f);
-            st4(reinterpret_cast<float*>(smem + OFF_F + kmaj_off4(t, j8, C)), make_float4(f[0], f[1], f[2], f[3]));
-            st4(reinterpret_cast<float*>(smem + OFF_F + kmaj_off4(t, j8 + 4, C)), make_float4(f[4], f[5], f[6], f[7]));
-        }
-    }
-    if (tid < C)
-        bs[tid] = tid < nvalid ? __bfloat162float(beta[((long long)b * L + t0 + tid) * H + h])
-                               : 0.0f;
-    __syncthreads();
-    // ---- K^T, V^T tiles.  A warp takes 32 consecutive tokens t and 4 columns
-    // j: one float4 read per row tile (8 rows cover the 8 swizzled 16-byte
-    // slots), 4 scalar writes into one 128-byte row of each transposed tile
-    // (conflict free), and K^T[j][t] to HBM coalesced over t.
-    for (int idx = tid; idx < C * (D / 4); idx += THREADS) {
-        const int t = idx % C, j4 = (idx / C) * 4;
-        const float4 k4 = ld4(reinterpret_cast<const float*>(smem + OFF_K + kmaj_off4(t, j4, C)));
-        const float4 v4 = ld4(reinterpret_cast<const float*>(smem + OFF_F + kmaj_off4(t, j4, C)));
-        const float kv[4] = {k4.x, k4.y, k4.z, k4.w}, vv[4] = {v4.x, v4.y, v4.z, v4.w};
-        const uint32_t o = (t & 3) * 4;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            *reinterpret_cast<float*>(smem + OFF_KT + kmaj_off4(j4 + e, t & ~3, D) + o) = kv[e];
-            *reinterpret_cast<float*>(smem + OFF_VT + kmaj_off4(j4 + e, t & ~3, D) + o) = vv[e];
-            ws.KT[(ch * D + j4 + e) * C + t] = kv[e];
-        }
-    }
-    fence_proxy_async();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    const uint32_t tmem = s_misc[0];
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    if (tid == 0) {
-        constexpr uint32_t id64 = idesc_tf32(64, C);
-#pragma unroll
-        for (int kk = 0; kk < D / 8; ++kk) {
-            const uint64_t kd = kdesc(smem + OFF_K, BOX_C, kk);
-            mma_tf32_ss(tmem + TM_G, kd, kd, id64, kk > 0);
-            mma_tf32_ss(tmem + TM_M, kdesc(smem + OFF_Q, BOX_C, kk), kd, id64, kk > 0);
-        }
-        tc::commit(mbar);
-        if (!mbar_wait_bounded(mbar, 0, err, EDB_DEVERR_DELTA_PIPE)) {
-            mbar_wait_bounded(mbar, 0, err, EDB_DEVERR_DELTA_PIPE);
-            s_misc[1] = 1;
-        }
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    if (!s_misc[1]) {
-        // ---- G -> shared (solve input), Mq -> HBM (masked); M=64 accumulators:
-        // lanes 32w + r (r < 16) hold row 16w + r
-        uint32_t g0[32], g1[32];
-        tc::tmem_ld32(tmem + TM_G + lane_base, g0);
-        tc::tmem_ld32(tmem + TM_G + lane_base + 32, g1);
-        tc::tmem_wait_ld();
-        if (lane < 16) {
-            const int t = 16 * warp + lane;
-#pragma unroll
-            for (int s = 0; s < 32; ++s) {
-                Gs[t * PC + s] = __uint_as_float(g0[s]);
-                Gs[t * PC + 32 + s] = __uint_as_float(g1[s]);
-            }
-        }
-        tc::tmem_ld32(tmem + TM_M + lane_base, g0);
-        tc::tmem_ld32(tmem + TM_M + lane_base + 32, g1);
-        tc::tmem_wait_ld();
-        if (lane < 16) {
-            const int t = 16 * warp + lane;
-            float* mg = ws.M + (ch * C + t) * C;
-#pragma unroll
-            for (int s = 0; s < 32; s += 4) {
-                st4(mg + s, make_float4(s <= t ? __uint_as_float(g0[s]) : 0.f,
-                                        s + 1 <= t ? __uint_as_float(g0[s + 1]) : 0.f,
-                                        s + 2 <= t ? __uint_as_float(g0[s + 2]) : 0.f,
-                                        s + 3 <= t ? __uint_as_float(g0[s + 3]) : 0.f));
-                st4(mg + 32 + s, make_float4(s + 32 <= t ? __uint_as_float(g1[s]) : 0.f,
-                                             s + 33 <= t ? __uint_as_float(g1[s + 1]) : 0.f,
-                                             s + 34 <= t ? __uint_as_float(g1[s + 2]) : 0.f,
-                                             s + 35 <= t ? __uint_as_float(g1[s + 3]) : 0.f));
-            }
-        }
-    }
-    __syncthreads();
-    if (!s_misc[1]) {
-        prep_solve<THREADS>(Gs, bs, Ys, Tm);
-        // ---- T diag(beta) -> K-major tile [t][s]
-        for (int idx = tid; idx < C * (C / 4); idx += THREADS) {
-            const int t = idx / (C / 4), s4 = (idx % (C / 4)) * 4;
-            st4(reinterpret_cast<float*>(smem + OFF_TB + kmaj_off4(t, s4, C)),
-                make_float4(Tm[t * PC + s4] * bs[s4], Tm[t * PC + s4 + 1] * bs[s4 + 1],
-                            Tm[t * PC + s4 + 2] * bs[s4 + 2], Tm[t * PC + s4 + 3] * bs[s4 + 3]));
-        }
-        fence_proxy_async();
-        tc::fence_before_sync();
-        __syncthreads();
-        tc::fence_after_sync();
-        if (tid == 0) {
-            constexpr uint32_t id128 = idesc_tf32(128, C);
-#pragma unroll
-            for (int kk = 0; kk < C / 8; ++kk) {
-                const uint64_t tb = kdesc(smem + OFF_TB, BOX_C, kk);
-                mma_tf32_ss(tmem + TM_W, kdesc(smem + OFF_KT, BOX_D, kk), tb, id128, kk > 0);
-                mma_tf32_ss(tmem + TM_U, kdesc(smem + OFF_VT, BOX_D, kk), tb, id128, kk > 0);
-            }
-            tc::commit(mbar);
-            if (!mbar_wait_bounded(mbar, 1, err, EDB_DEVERR_DELTA_PIPE)) {
-                mbar_wait_bounded(mbar, 1, err, EDB_DEVERR_DELTA_PIPE);
-                s_misc[1] = 1;
-            }
-        }
-        tc::fence_before_sync();
-        __syncthreads();
-        tc::fence_after_sync();
-        if (!s_misc[1]) {
-            // W^T row j -> -W[t][j] (coalesced over j); U0^T row i -> U0^T[i][t]
-            const int j = tid;
-            store_rows_transposed<C>(ws.Wn + ch * C * D + j, tmem + TM_W + lane_base, -1.0f);
-            float* ug = ws.U0T + (ch * D + j) * C;
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                uint32_t x[32];
-                tc::tmem_ld32(tmem + TM_U + lane_base + half * 32, x);
-                tc::tmem_wait_ld();
-#pragma unroll
-                for (int e = 0; e < 32; e += 4)
-                    st4(ug + half * 32 + e,
-                        make_float4(__uint_as_float(x[e]), __uint_as_float(x[e + 1]),
-                                    __uint_as_float(x[e + 2]), __uint_as_float(x[e + 3])));
-            }
-        }
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    if (warp == 0) {
-        tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, TM_COLS);
-    }
 }
 
 // ------------------------------------------------------------------ state fwd
@@ -568,21 +345,21 @@ int edb_delta_chunked_fwd(const void* q, const void* k, const void* v, const voi
     const long long nch = (long long)B * H * NC;
     if (nch * D > 0x7fffffffLL) return EDB_ERR_UNSUPPORTED;  // TMA row coordinate is int32
     FwdScratch w = carve_fwd(ws, nch);
-    cudaError_t e = cudaFuncSetAttribute(delta_prep_fwd_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, prep::SMEM);
-    if (e != cudaSuccess) return (int)e;
-    delta_prep_fwd_kernel<<<dim3(NC, H, B), prep::THREADS, prep::SMEM, st>>>(
-        (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
-        (const __nv_bfloat16*)beta, w, L, H, NC, edb::device_error_word());
-    if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
+    PrepOut po{};
+    po.KT = w.KT;
+    po.Q = w.Q;
+    po.M = w.M;
+    po.Wn = w.Wn;
+    po.U0T = w.U0T;
+    int s = launch_delta_prep<true>(q, k, v, beta, po, B, L, H, st);
+    if (s != EDB_OK) return s;
     StateMaps maps;
-    int s;
     if ((s = make_box_map(&maps.Wn, w.Wn, nch * C, D, C))) return s;
     if ((s = make_box_map(&maps.Q, w.Q, nch * C, D, C))) return s;
     if ((s = make_box_map(&maps.KT, w.KT, nch * D, C, D))) return s;
     if ((s = make_box_map(&maps.M, w.M, nch * C, C, C))) return s;
-    e = cudaFuncSetAttribute(delta_state_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             sf::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(delta_state_fwd_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, sf::SMEM);
     if (e != cudaSuccess) return (int)e;
     delta_state_fwd_kernel<<<dim3(H, B), sf::THREADS, sf::SMEM, st>>>(
         maps, w.U0T, resid, (__nv_bfloat16*)o, L, H, NC, edb::device_error_word());

@@ -16,8 +16,9 @@
 // The key gradient is the exact one, as in delta_rule.cu.
 //
 // Kernels (one stream, in order):
-//   delta_prep_bwd_kernel   per chunk, SIMT: K K^T, M, T, W; writes the
-//                           K-major f32 operands of the state kernel and T, K K^T.
+//   delta_prep_kernel<false> (delta_prep.cuh) per chunk, tcgen05 kind::f16:
+//                           K K^T, M, T, W; writes the K-major f32 operands of
+//                           the state kernel and T, K K^T.
 //   delta_state_bwd_kernel  per (b, h), chunks in reverse, tcgen05 kind::tf32,
 //                           dS in TMEM (lanes = value dim):
 //                             D_U = dS K^T + dO^T M        (= dU~^T)   N=64
@@ -31,6 +32,7 @@
 #include <math.h>
 
 #include "delta_chunked.cuh"
+#include "delta_prep.cuh"
 
 using namespace dchunk;
 
@@ -90,56 +92,6 @@ BwdScratch carve_bwd(void* ws, long long nch) {
     s.dM = take(cc);
     s.dSCT = take(a256((size_t)nch * D * D * 4));
     return s;
-}
-
-// ------------------------------------------------------------------ prep
-constexpr size_t kPrepSmem = (size_t)(3 * C * PP + 3 * C * PC + C * C + C) * sizeof(float);
-
-__global__ void __launch_bounds__(kPrepThreads, 1)
-    delta_prep_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
-                          const __nv_bfloat16* __restrict__ beta,
-                          const __nv_bfloat16* __restrict__ dO, BwdScratch ws, int L, int H,
-                          int NC) {
-    extern __shared__ float sm[];
-    float* Ks = sm;              // [C][PP]
-    float* Qs = Ks + C * PP;     // [C][PP]  (then -W)
-    float* dOs = Qs + C * PP;    // [C][PP]
-    float* Gs = dOs + C * PP;    // [C][PC]  K K^T
-    float* Ms = Gs + C * PC;     // [C][PC]  tril(Q K^T)
-    float* Tm = Ms + C * PC;     // [C][PC]  T
-    float* Ys = Tm + C * PC;     // [C][C]   solve scratch
-    float* bs = Ys + C * C;      // [C]
-    const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-    const int tid = threadIdx.x;
-    const long long ch = ((long long)b * H + h) * NC + c;
-    const int t0 = c * C, nvalid = min(C, L - t0);
-    const long long row0 = (((long long)b * L + t0) * H + h) * D, ts = (long long)H * D;
-
-    load_chunk_rows(Ks, k, row0, ts, nvalid, ws.Kf + ch * C * D);
-    load_chunk_rows(Qs, q, row0, ts, nvalid, nullptr);
-    load_chunk_rows(dOs, dO, row0, ts, nvalid, nullptr);
-    if (tid < C)
-        bs[tid] = tid < nvalid ? __bfloat162float(beta[((long long)b * L + t0 + tid) * H + h])
-                               : 0.0f;
-    __syncthreads();
-    store_transposed(ws.dOT + ch * D * C, dOs, 1.0f);
-    store_transposed(ws.QT + ch * D * C, Qs, 1.0f);
-    store_transposed(ws.KT + ch * D * C, Ks, 1.0f);
-    prep_products(Ks, Qs, Gs, Ms);
-    __syncthreads();
-    for (int idx = tid; idx < C * C; idx += kPrepThreads) {
-        ws.G[ch * C * C + idx] = Gs[idx / C * PC + idx % C];
-        ws.MT[ch * C * C + idx] = Ms[(idx % C) * PC + idx / C];  // MT[s][t] = M[t][s]
-    }
-    prep_solve<kPrepThreads>(Gs, bs, Ys, Tm);
-    for (int idx = tid; idx < C * C; idx += kPrepThreads)
-        ws.T[ch * C * C + idx] = Tm[idx / C * PC + idx % C];
-    float w[4][8];
-    prep_apply_tb(Tm, bs, Ks, w);
-    // Q rows were last read before the barriers inside prep_solve
-    put_tile(Qs, w, 1.0f);
-    __syncthreads();
-    store_transposed(ws.WnT + ch * D * C, Qs, -1.0f);  // -W^T: [j][t]
 }
 
 // ------------------------------------------------------------------ state bwd
@@ -508,19 +460,21 @@ int edb_delta_chunked_bwd(const void* q, const void* k, const void* v, const voi
     if ((units * (NC + 1)) * D > 0x7fffffffLL) return EDB_ERR_UNSUPPORTED;
     BwdScratch w = carve_bwd(ws, nch);
     unsigned* err = edb::device_error_word();
-    const __nv_bfloat16 *qb = (const __nv_bfloat16*)q, *kb = (const __nv_bfloat16*)k,
-                        *bb = (const __nv_bfloat16*)beta,
-                        *dob = (const __nv_bfloat16*)dO;
+    const __nv_bfloat16* dob = (const __nv_bfloat16*)dO;
     cudaError_t e;
-    if ((e = cudaFuncSetAttribute(delta_prep_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)kPrepSmem)) != cudaSuccess)
-        return (int)e;
-    delta_prep_bwd_kernel<<<dim3(NC, H, B), kPrepThreads, kPrepSmem, st>>>(qb, kb, bb, dob, w, L,
-                                                                           H, NC);
-    if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
+    PrepOut po{};
+    po.KT = w.KT;
+    po.Kf = w.Kf;
+    po.XT = w.dOT;
+    po.QT = w.QT;
+    po.MT = w.MT;
+    po.WnT = w.WnT;
+    po.T = w.T;
+    po.G = w.G;
+    int s = launch_delta_prep<false>(q, k, dO, beta, po, B, L, H, st);
+    if (s != EDB_OK) return s;
 
     StateBwdMaps sm;
-    int s;
     if ((s = make_box_map(&sm.Kf, w.Kf, nch * C, D, C))) return s;
     if ((s = make_box_map(&sm.dOT, w.dOT, nch * D, C, D))) return s;
     if ((s = make_box_map(&sm.MT, w.MT, nch * C, C, C))) return s;
