@@ -99,29 +99,49 @@ struct StateBwdMaps {
     CUtensorMap Kf, dOT, MT, QT, WnT;
 };
 
-constexpr int kStateThreads = 128;
+// grid (H, B), one CTA per (b, h), chunks in reverse.  Warp roles as in the
+// forward state kernel:
+//   warps 0-3  read dS (= dS_C of the chunk) out of TMEM at every step and
+//              store dS_C^T;
+//   warps 4-7  read the finished D_U = dU~^T of each step out (dU~ and
+//              dU~^T) while P2 of that step runs;
+//   warp 8     lane 0 issues the TMA loads and the MMAs.
+// D_U is double-buffered by step parity:
+//   P1(n): D_U[b] = dS K^T + dO^T M            (dS read as A from TMEM)
+//   P2(n): dS += dO^T Q + D_U[b] (-W)          (after dS_C^T is read out)
+// mbarriers: fullX[2], fullY (TMA), p1[b], p2[b] (tcgen05.commit), s_read
+// (dS read out, 4 warp arrivals), u_free[b] (D_U[b] read out, 4 arrivals).
+namespace sb {
+constexpr int THREADS = 288;
 // X stage (double-buffered): K [C][D] | dO^T [D][C] | M^T [C][C]
 constexpr int XO_K = 0, XO_O = 4 * BOX_C, XO_M = XO_O + 2 * BOX_D;
 constexpr int X_BYTES = XO_M + 2 * BOX_C;  // 80 KB
 // Y stage (single): Q^T [D][C] | -W^T [D][C]
 constexpr int YO_Q = 0, YO_W = 2 * BOX_D;
 constexpr int Y_BYTES = YO_W + 2 * BOX_D;  // 64 KB
-constexpr int SB_OFF_Y = 2 * X_BYTES;
-constexpr int SB_OFF_BARS = SB_OFF_Y + Y_BYTES;
-constexpr int SB_SMEM = SB_OFF_BARS + 64;
-constexpr int SB_TM_S = 0, SB_TM_U = 128, SB_TM_COLS = 256;
+constexpr int OFF_Y = 2 * X_BYTES;
+constexpr int OFF_BARS = OFF_Y + Y_BYTES;
+constexpr int SMEM = OFF_BARS + 128;
+constexpr int TM_S = 0, TM_U = 128, TM_COLS = 256;  // D_U: 2 x 64 columns
+}  // namespace sb
 
-__global__ void __launch_bounds__(kStateThreads, 1)
+__global__ void __launch_bounds__(sb::THREADS, 1)
     delta_state_bwd_kernel(const __grid_constant__ StateBwdMaps maps, float* __restrict__ dSCT,
                            float* __restrict__ dU, float* __restrict__ dUT, int H, int NC,
                            unsigned* err) {
+    using namespace sb;
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint64_t* fullX = reinterpret_cast<uint64_t*>(smem + SB_OFF_BARS);  // [2]
-    uint64_t* fullY = fullX + 2;
-    uint64_t* mbar = fullY + 1;
-    uint32_t* s_misc = reinterpret_cast<uint32_t*>(mbar + 1);  // [0] tmem base, [1] abort
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BARS);
+    uint64_t* fullX = bars;       // [2]
+    uint64_t* fullY = bars + 2;
+    uint64_t* p1 = bars + 3;      // [2]
+    uint64_t* p2 = bars + 5;      // [2]
+    uint64_t* s_read = bars + 7;
+    uint64_t* u_free = bars + 8;  // [2]
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 10);
+    volatile uint32_t* s_abort = s_tmem + 1;
     const int h = blockIdx.x, b = blockIdx.y;
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const long long ch0 = ((long long)b * H + h) * NC;
 
     if ((smem_u32(smem) & 1023u) != 0) {
@@ -129,141 +149,156 @@ __global__ void __launch_bounds__(kStateThreads, 1)
         return;
     }
     if (warp == 0) {
-        tc::tmem_alloc(s_misc, SB_TM_COLS);
+        tc::tmem_alloc(s_tmem, TM_COLS);
         tc::tmem_relinquish();
     }
     if (tid == 0) {
-        s_misc[1] = 0;
-        mbar_init(&fullX[0], 1);
-        mbar_init(&fullX[1], 1);
-        mbar_init(fullY, 1);
-        mbar_init(mbar, 1);
+        *s_abort = 0;
+        for (int e = 0; e < 10; ++e) mbar_init(&bars[e], e >= 7 ? 4 : 1);
         fence_mbar_init();
     }
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
-    const uint32_t tmem = s_misc[0];
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const int i = tid;
-
-    // copies issued / waited per barrier (thread 0 only)
-    int x_issued[2] = {0, 0}, x_landed[2] = {0, 0}, y_issued = 0, y_landed = 0;
-    auto issue_x = [&](int c, int n) {
-        uint8_t* st = smem + (n & 1) * X_BYTES;
-        uint64_t* bar = &fullX[n & 1];
-        const int rc = (int)((ch0 + c) * C), rd = (int)((ch0 + c) * D);
-        mbar_arrive_expect_tx(bar, X_BYTES);
-        for (int bx = 0; bx < 4; ++bx) tma_load_2d(st + XO_K + bx * BOX_C, &maps.Kf, bar, bx * 32, rc);
-        for (int bx = 0; bx < 2; ++bx) {
-            tma_load_2d(st + XO_O + bx * BOX_D, &maps.dOT, bar, bx * 32, rd);
-            tma_load_2d(st + XO_M + bx * BOX_C, &maps.MT, bar, bx * 32, rc);
-        }
-        ++x_issued[n & 1];
-    };
-    auto issue_y = [&](int c) {
-        uint8_t* st = smem + SB_OFF_Y;
-        const int rd = (int)((ch0 + c) * D);
-        mbar_arrive_expect_tx(fullY, Y_BYTES);
-        for (int bx = 0; bx < 2; ++bx) {
-            tma_load_2d(st + YO_Q + bx * BOX_D, &maps.QT, fullY, bx * 32, rd);
-            tma_load_2d(st + YO_W + bx * BOX_D, &maps.WnT, fullY, bx * 32, rd);
-        }
-        ++y_issued;
-    };
-    if (tid == 0) {
-        prefetch_tmap(&maps.Kf);
-        prefetch_tmap(&maps.dOT);
-        prefetch_tmap(&maps.MT);
-        prefetch_tmap(&maps.QT);
-        prefetch_tmap(&maps.WnT);
-        issue_x(NC - 1, 0);
-        issue_y(NC - 1);
-        if (NC > 1) issue_x(NC - 2, 1);
-    }
-    {  // dS = 0: no gradient reaches the final state
+    const uint32_t tmem = *s_tmem;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const int i = (warp & 3) * 32 + lane;  // TMEM lane = value-dim row of dS
+    if (warp < 4) {  // dS = 0: no gradient reaches the final state
         uint32_t z[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) z[e] = 0u;
 #pragma unroll
-        for (int cc = 0; cc < D / 32; ++cc) tc::tmem_st32(tmem + SB_TM_S + lane_base + cc * 32, z);
+        for (int cc = 0; cc < D / 32; ++cc) tc::tmem_st32(tmem + TM_S + lane_base + cc * 32, z);
         tc::tmem_wait_st();
     }
-    constexpr uint32_t idN64 = idesc_tf32(128, C);
-    constexpr uint32_t idN128 = idesc_tf32(128, D);
-    uint32_t mph = 0;
-    bool mma_pending = false;
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+        if (mbar_wait_bounded(bar, parity, err, EDB_DEVERR_DELTA_PIPE)) return true;
+        *s_abort = 1;
+        return false;
+    };
 
-    for (int n = 0; n < NC; ++n) {
-        const int c = NC - 1 - n;
-        // dS (= dS_C of chunk c) row i -> dS_C^T column i
-        store_rows_transposed<D>(dSCT + (ch0 + c) * D * D + i, tmem + SB_TM_S + lane_base);
-        tc::fence_before_sync();
-        __syncthreads();
-        tc::fence_after_sync();
-        if (tid == 0) {
-            const uint8_t* xs = smem + (n & 1) * X_BYTES;
-            const uint8_t* ys = smem + SB_OFF_Y;
-            bool ok = mbar_wait_bounded(&fullX[n & 1], x_landed[n & 1] & 1, err,
-                                        EDB_DEVERR_DELTA_PIPE);
-            if (ok) {
-                ++x_landed[n & 1];
+    if (warp == 8) {
+        // ---------------------------------------------------------- TMA + MMA
+        if (lane == 0) {
+            // copies issued / waited per barrier
+            int x_issued[2] = {0, 0}, x_landed[2] = {0, 0}, y_issued = 0, y_landed = 0;
+            int committed = 0, done = 0;
+            auto issue_x = [&](int c, int n) {
+                uint8_t* st = smem + (n & 1) * X_BYTES;
+                uint64_t* bar = &fullX[n & 1];
+                const int rc = (int)((ch0 + c) * C), rd = (int)((ch0 + c) * D);
+                mbar_arrive_expect_tx(bar, X_BYTES);
+                for (int bx = 0; bx < 4; ++bx)
+                    tma_load_2d(st + XO_K + bx * BOX_C, &maps.Kf, bar, bx * 32, rc);
+                for (int bx = 0; bx < 2; ++bx) {
+                    tma_load_2d(st + XO_O + bx * BOX_D, &maps.dOT, bar, bx * 32, rd);
+                    tma_load_2d(st + XO_M + bx * BOX_C, &maps.MT, bar, bx * 32, rc);
+                }
+                ++x_issued[n & 1];
+            };
+            auto issue_y = [&](int c) {
+                uint8_t* st = smem + OFF_Y;
+                const int rd = (int)((ch0 + c) * D);
+                mbar_arrive_expect_tx(fullY, Y_BYTES);
+                for (int bx = 0; bx < 2; ++bx) {
+                    tma_load_2d(st + YO_Q + bx * BOX_D, &maps.QT, fullY, bx * 32, rd);
+                    tma_load_2d(st + YO_W + bx * BOX_D, &maps.WnT, fullY, bx * 32, rd);
+                }
+                ++y_issued;
+            };
+            prefetch_tmap(&maps.Kf);
+            prefetch_tmap(&maps.dOT);
+            prefetch_tmap(&maps.MT);
+            prefetch_tmap(&maps.QT);
+            prefetch_tmap(&maps.WnT);
+            issue_x(NC - 1, 0);
+            issue_y(NC - 1);
+            if (NC > 1) issue_x(NC - 2, 1);
+            constexpr uint32_t idN64 = idesc_tf32(128, C);
+            constexpr uint32_t idN128 = idesc_tf32(128, D);
+            for (int n = 0; n < NC; ++n) {
+                const int c = NC - 1 - n, bf = n & 1;
+                const uint32_t par = (n >> 1) & 1;
+                const uint8_t* xs = smem + bf * X_BYTES;
+                const uint8_t* ys = smem + OFF_Y;
+                const uint32_t tU = tmem + TM_U + bf * 64;
+                if (!wait(&fullX[bf], x_landed[bf] & 1)) break;
+                ++x_landed[bf];
+                // D_U[bf] was read out at step n - 2
+                if (n >= 2 && !wait(&u_free[bf], ((n - 2) >> 1) & 1)) break;
                 tc::fence_after_sync();
 #pragma unroll
                 for (int kk = 0; kk < D / 8; ++kk)
-                    mma_tf32_ts(tmem + SB_TM_U, tmem + SB_TM_S + kk * 8,
-                                kdesc(xs + XO_K, BOX_C, kk), idN64, kk > 0);
+                    mma_tf32_ts(tU, tmem + TM_S + kk * 8, kdesc(xs + XO_K, BOX_C, kk), idN64,
+                                kk > 0);
 #pragma unroll
                 for (int kk = 0; kk < C / 8; ++kk)
-                    mma_tf32_ss(tmem + SB_TM_U, kdesc(xs + XO_O, BOX_D, kk),
-                                kdesc(xs + XO_M, BOX_C, kk), idN64, 1);
-                tc::commit(mbar);
-                mma_pending = true;
-                ok = mbar_wait_bounded(mbar, mph, err, EDB_DEVERR_DELTA_PIPE);
-                if (ok) {
-                    mph ^= 1u;
-                    mma_pending = false;
-                }
-            }
-            if (ok) {
-                ok = mbar_wait_bounded(fullY, y_landed & 1, err, EDB_DEVERR_DELTA_PIPE);
-                if (ok) ++y_landed;
-            }
-            if (ok) {
+                    mma_tf32_ss(tU, kdesc(xs + XO_O, BOX_D, kk), kdesc(xs + XO_M, BOX_C, kk),
+                                idN64, 1);
+                tc::commit(&p1[bf]);
+                committed = 2 * n + 1;
+                if (!wait(&p1[bf], par)) break;
+                done = 2 * n + 1;
+                if (!wait(fullY, y_landed & 1)) break;
+                ++y_landed;
+                if (!wait(s_read, n & 1)) break;
                 tc::fence_after_sync();
 #pragma unroll
                 for (int kk = 0; kk < C / 8; ++kk) {
-                    mma_tf32_ss(tmem + SB_TM_S, kdesc(xs + XO_O, BOX_D, kk),
+                    mma_tf32_ss(tmem + TM_S, kdesc(xs + XO_O, BOX_D, kk),
                                 kdesc(ys + YO_Q, BOX_D, kk), idN128, 1);
-                    mma_tf32_ts(tmem + SB_TM_S, tmem + SB_TM_U + kk * 8,
-                                kdesc(ys + YO_W, BOX_D, kk), idN128, 1);
+                    mma_tf32_ts(tmem + TM_S, tU + kk * 8, kdesc(ys + YO_W, BOX_D, kk), idN128, 1);
                 }
-                tc::commit(mbar);
-                mma_pending = true;
-                ok = mbar_wait_bounded(mbar, mph, err, EDB_DEVERR_DELTA_PIPE);
-                if (ok) {
-                    mph ^= 1u;
-                    mma_pending = false;
-                }
-            }
-            if (ok) {
+                tc::commit(&p2[bf]);
+                committed = 2 * n + 2;
+                if (!wait(&p2[bf], par)) break;
+                done = 2 * n + 2;
                 if (c >= 1) issue_y(c - 1);
                 if (c >= 2) issue_x(c - 2, n + 2);
-            } else {
-                s_misc[1] = 1;
+            }
+            if (*s_abort) {
+                // bounded waits for the copies and MMAs still in flight
+                for (int bb = 0; bb < 2; ++bb)
+                    for (; x_landed[bb] < x_issued[bb]; ++x_landed[bb])
+                        mbar_wait_bounded(&fullX[bb], x_landed[bb] & 1, err,
+                                          EDB_DEVERR_DELTA_PIPE);
+                for (; y_landed < y_issued; ++y_landed)
+                    mbar_wait_bounded(fullY, y_landed & 1, err, EDB_DEVERR_DELTA_PIPE);
+                if (committed > done) {
+                    const int nn = (committed - 1) >> 1;
+                    uint64_t* bar = (committed & 1) ? &p1[nn & 1] : &p2[nn & 1];
+                    mbar_wait_bounded(bar, (nn >> 1) & 1, err, EDB_DEVERR_DELTA_PIPE);
+                }
             }
         }
-        tc::fence_before_sync();
-        __syncthreads();
-        tc::fence_after_sync();
-        if (s_misc[1]) break;
-        // D_U = dU~^T: row i -> dU~[c][t][i] (coalesced over i) and dU~^T[c][i][t]
-        {
+    } else if (warp < 4) {
+        // ---------------------------------------------------------- dS_C^T
+        for (int n = 0; n < NC; ++n) {
+            if (n > 0 && !wait(&p2[(n - 1) & 1], ((n - 1) >> 1) & 1)) break;
+            if (*s_abort) break;
+            tc::fence_after_sync();
+            store_rows_transposed<D>(dSCT + (ch0 + NC - 1 - n) * D * D + i, tmem + TM_S + lane_base);
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_read);
+        }
+    } else {
+        // ---------------------------------------------------------- dU~, dU~^T
+        for (int n = 0; n < NC; ++n) {
+            // D_U[n & 1] is final once P1(n) is done (P2(n) only reads it)
+            if (!wait(&p1[n & 1], (n >> 1) & 1)) break;
+            if (*s_abort) break;
+            tc::fence_after_sync();
+            // D_U row i -> dU~[c][t][i] (coalesced over i) and dU~^T[c][i][t]
+            const int c = NC - 1 - n;
             float* ut = dUT + ((ch0 + c) * D + i) * C;
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 uint32_t x[32];
-                tc::tmem_ld32(tmem + SB_TM_U + lane_base + half * 32, x);
+                tc::tmem_ld32(tmem + TM_U + (n & 1) * 64 + lane_base + half * 32, x);
                 tc::tmem_wait_ld();
                 float* du = dU + (ch0 + c) * C * D + (long long)half * 32 * D + i;
 #pragma unroll
@@ -274,22 +309,16 @@ __global__ void __launch_bounds__(kStateThreads, 1)
                         make_float4(__uint_as_float(x[e]), __uint_as_float(x[e + 1]),
                                     __uint_as_float(x[e + 2]), __uint_as_float(x[e + 3])));
             }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&u_free[n & 1]);
         }
-    }
-    if (s_misc[1] && tid == 0) {
-        // Abort: bounded waits for the copies and MMAs still in flight.
-        for (int bb = 0; bb < 2; ++bb)
-            for (; x_landed[bb] < x_issued[bb]; ++x_landed[bb])
-                mbar_wait_bounded(&fullX[bb], x_landed[bb] & 1, err, EDB_DEVERR_DELTA_PIPE);
-        for (; y_landed < y_issued; ++y_landed)
-            mbar_wait_bounded(fullY, y_landed & 1, err, EDB_DEVERR_DELTA_PIPE);
-        if (mma_pending) mbar_wait_bounded(mbar, mph, err, EDB_DEVERR_DELTA_PIPE);
     }
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 0) {
         tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, SB_TM_COLS);
+        tc::tmem_dealloc(tmem, TM_COLS);
     }
 }
 
@@ -481,10 +510,10 @@ int edb_delta_chunked_bwd(const void* q, const void* k, const void* v, const voi
     if ((s = make_box_map(&sm.QT, w.QT, nch * D, C, D))) return s;
     if ((s = make_box_map(&sm.WnT, w.WnT, nch * D, C, D))) return s;
     if ((e = cudaFuncSetAttribute(delta_state_bwd_kernel,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, SB_SMEM)) !=
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, sb::SMEM)) !=
         cudaSuccess)
         return (int)e;
-    delta_state_bwd_kernel<<<dim3(H, B), kStateThreads, SB_SMEM, st>>>(sm, w.dSCT, w.dU, w.dUT, H,
+    delta_state_bwd_kernel<<<dim3(H, B), sb::THREADS, sb::SMEM, st>>>(sm, w.dSCT, w.dU, w.dUT, H,
                                                                        NC, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
 
