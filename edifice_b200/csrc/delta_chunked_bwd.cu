@@ -24,11 +24,9 @@
 //                             D_U = dS K^T + dO^T M        (= dU~^T)   N=64
 //                             dS += dO^T Q + D_U (-W)                  N=128
 //                           stores dS_C^T, dU~ and dU~^T per chunk.
-//   delta_post1_kernel      per chunk, tcgen05: the products with S_0 / dS_C,
-//                           (dO S_0)^T, (dU~ S_0)^T, (U~ dS_C)^T (M=128, N=64,
-//                           K=128) and dO U~^T (M=64); operands by TMA.
-//   delta_post2_kernel      (delta_chunked_post.cu) per chunk: dT_b, dQ, dK, dV
-//                           on tcgen05, the C x C chain (dA, dbeta) SIMT.
+//   delta_post_kernel       (delta_chunked_post.cu) per chunk: the products
+//                           with S_0 / dS_C, dT_b, dQ, dK, dV on tcgen05, the
+//                           C x C chain (dA, dbeta) SIMT.
 #include <math.h>
 
 #include "delta_chunked.cuh"
@@ -53,16 +51,10 @@ struct BwdScratch {
     float* dSCT;  // [nch][D][D]  dS_C^T
     float* dU;    // [nch][C][D]  dU~
     float* dUT;   // [nch][D][C]  dU~^T
-    // post1 outputs
-    float* dQa;   // [nch][C][D]  dO S_0
-    float* dW;    // [nch][C][D]  -dU~ S_0
-    float* dWT;   // [nch][D][C]  its transpose
-    float* dK1;   // [nch][C][D]  U~ dS_C
-    float* dM;    // [nch][C][C]  tril(dO U~^T)
 };
 
 size_t bwd_scratch_bytes(long long nch) {
-    return 11 * a256((size_t)nch * C * D * 4) + 4 * a256((size_t)nch * C * C * 4) +
+    return 7 * a256((size_t)nch * C * D * 4) + 3 * a256((size_t)nch * C * C * 4) +
            a256((size_t)nch * D * D * 4);
 }
 
@@ -82,14 +74,9 @@ BwdScratch carve_bwd(void* ws, long long nch) {
     s.WnT = take(cd);
     s.dU = take(cd);
     s.dUT = take(cd);
-    s.dQa = take(cd);
-    s.dW = take(cd);
-    s.dWT = take(cd);
-    s.dK1 = take(cd);
     s.MT = take(cc);
     s.T = take(cc);
     s.G = take(cc);
-    s.dM = take(cc);
     s.dSCT = take(a256((size_t)nch * D * D * 4));
     return s;
 }
@@ -322,160 +309,14 @@ __global__ void __launch_bounds__(sb::THREADS, 1)
     }
 }
 
-// ------------------------------------------------------------------ post1
-struct Post1Maps {
-    CUtensorMap S0T, dSCT, Ut, dU;
-};
-
-constexpr int P1_S0 = 0, P1_DS = 4 * BOX_D, P1_U = 8 * BOX_D, P1_DU = P1_U + 4 * BOX_C,
-              P1_DO = P1_DU + 4 * BOX_C;
-constexpr int P1_TX = 8 * BOX_D + 8 * BOX_C;  // bytes arriving by TMA (192 KB)
-constexpr int P1_OFF_BARS = P1_DO + 4 * BOX_C;
-constexpr int P1_SMEM = P1_OFF_BARS + 64;
-constexpr int P1_TM_Q = 0, P1_TM_W = 64, P1_TM_K = 128, P1_TM_M = 192, P1_TM_COLS = 256;
-
-__global__ void __launch_bounds__(128, 1)
-    delta_post1_kernel(const __grid_constant__ Post1Maps maps, const __nv_bfloat16* __restrict__ dO,
-                       float* __restrict__ dQa, float* __restrict__ dW, float* __restrict__ dWT,
-                       float* __restrict__ dK1, float* __restrict__ dM, int L, int H, int NC,
-                       unsigned* err) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + P1_OFF_BARS);
-    uint64_t* mbar = full + 1;
-    uint32_t* s_misc = reinterpret_cast<uint32_t*>(mbar + 1);
-    const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const long long bh = (long long)b * H + h;
-    const long long ch = bh * NC + c;
-    const int t0 = c * C, nvalid = min(C, L - t0);
-
-    if ((smem_u32(smem) & 1023u) != 0) {
-        if (tid == 0) edb_flag_error(err, EDB_DEVERR_DELTA_PIPE);
-        return;
-    }
-    if (warp == 0) {
-        tc::tmem_alloc(s_misc, P1_TM_COLS);
-        tc::tmem_relinquish();
-    }
-    if (tid == 0) {
-        s_misc[1] = 0;
-        mbar_init(full, 1);
-        mbar_init(mbar, 1);
-        fence_mbar_init();
-        mbar_arrive_expect_tx(full, P1_TX);
-        const int rs = (int)((bh * (NC + 1) + c) * D), rd = (int)(ch * D), rc = (int)(ch * C);
-        for (int bx = 0; bx < 4; ++bx) {
-            tma_load_2d(smem + P1_S0 + bx * BOX_D, &maps.S0T, full, bx * 32, rs);
-            tma_load_2d(smem + P1_DS + bx * BOX_D, &maps.dSCT, full, bx * 32, rd);
-            tma_load_2d(smem + P1_U + bx * BOX_C, &maps.Ut, full, bx * 32, rc);
-            tma_load_2d(smem + P1_DU + bx * BOX_C, &maps.dU, full, bx * 32, rc);
-        }
-    }
-    // dO rows (bf16) -> f32 K-major SW128 tile [C][D]
-    {
-        constexpr int N = C * (D / 4) / 128;  // every load issued before the first store
-        uint2 raw[N];
-#pragma unroll
-        for (int n = 0; n < N; ++n) {
-            const int idx = tid + n * 128, t = idx / (D / 4), k4 = (idx % (D / 4)) * 4;
-            raw[n] = t < nvalid ? *reinterpret_cast<const uint2*>(
-                                      dO + (((long long)b * L + t0 + t) * H + h) * D + k4)
-                                : make_uint2(0u, 0u);
-        }
-#pragma unroll
-        for (int n = 0; n < N; ++n) {
-            const int idx = tid + n * 128, t = idx / (D / 4), k4 = (idx % (D / 4)) * 4;
-            *reinterpret_cast<float4*>(smem + P1_DO + kmaj_off4(t, k4, C)) =
-                make_float4(__uint_as_float(raw[n].x << 16),
-                            __uint_as_float(raw[n].x & 0xffff0000u),
-                            __uint_as_float(raw[n].y << 16),
-                            __uint_as_float(raw[n].y & 0xffff0000u));
-        }
-    }
-    fence_proxy_async();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    const uint32_t tmem = s_misc[0];
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    if (tid == 0) {
-        bool ok = mbar_wait_bounded(full, 0, err, EDB_DEVERR_DELTA_PIPE);
-        if (ok) {
-            tc::fence_after_sync();
-            constexpr uint32_t id128 = idesc_tf32(128, C), id64 = idesc_tf32(64, C);
-#pragma unroll
-            for (int kk = 0; kk < D / 8; ++kk) {
-                const uint64_t s0 = kdesc(smem + P1_S0, BOX_D, kk);
-                const uint64_t dof = kdesc(smem + P1_DO, BOX_C, kk);
-                const uint64_t u = kdesc(smem + P1_U, BOX_C, kk);
-                mma_tf32_ss(tmem + P1_TM_Q, s0, dof, id128, kk > 0);
-                mma_tf32_ss(tmem + P1_TM_W, s0, kdesc(smem + P1_DU, BOX_C, kk), id128, kk > 0);
-                mma_tf32_ss(tmem + P1_TM_K, kdesc(smem + P1_DS, BOX_D, kk), u, id128, kk > 0);
-                mma_tf32_ss(tmem + P1_TM_M, dof, u, id64, kk > 0);
-            }
-            tc::commit(mbar);
-            ok = mbar_wait_bounded(mbar, 0, err, EDB_DEVERR_DELTA_PIPE);
-            if (!ok) mbar_wait_bounded(mbar, 0, err, EDB_DEVERR_DELTA_PIPE);
-        } else {
-            mbar_wait_bounded(full, 0, err, EDB_DEVERR_DELTA_PIPE);  // drain the copies
-        }
-        if (!ok) s_misc[1] = 1;
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    if (!s_misc[1]) {
-        const int j = tid;
-        store_rows_transposed<C>(dQa + ch * C * D + j, tmem + P1_TM_Q + lane_base);
-        {  // -(dU~ S_0): [t][j] (coalesced over j) and its transpose [j][t]
-            float* wt = dWT + (ch * D + j) * C;
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                uint32_t x[32];
-                tc::tmem_ld32(tmem + P1_TM_W + lane_base + half * 32, x);
-                tc::tmem_wait_ld();
-                float* dw = dW + ch * C * D + (long long)half * 32 * D + j;
-#pragma unroll
-                for (int e = 0; e < 32; ++e) dw[e * D] = -__uint_as_float(x[e]);
-#pragma unroll
-                for (int e = 0; e < 32; e += 4)
-                    st4(wt + half * 32 + e,
-                        make_float4(-__uint_as_float(x[e]), -__uint_as_float(x[e + 1]),
-                                    -__uint_as_float(x[e + 2]), -__uint_as_float(x[e + 3])));
-            }
-        }
-        store_rows_transposed<C>(dK1 + ch * C * D + j, tmem + P1_TM_K + lane_base);
-        // M = 64 accumulator: lanes 32w + r (r < 16) hold row 16w + r
-        uint32_t x0[32], x1[32];
-        tc::tmem_ld32(tmem + P1_TM_M + lane_base, x0);
-        tc::tmem_ld32(tmem + P1_TM_M + lane_base + 32, x1);
-        tc::tmem_wait_ld();
-        if (lane < 16) {
-            const int t = 16 * warp + lane;
-            float* dst = dM + (ch * C + t) * C;
-#pragma unroll
-            for (int s = 0; s < 32; ++s) dst[s] = s <= t ? __uint_as_float(x0[s]) : 0.0f;
-#pragma unroll
-            for (int s = 0; s < 32; ++s)
-                dst[32 + s] = s + 32 <= t ? __uint_as_float(x1[s]) : 0.0f;
-        }
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    if (warp == 0) {
-        tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, P1_TM_COLS);
-    }
-}
-
 }  // namespace
 
 // ---------------------------------------------------------------- library-internal
-int edb_delta_chunked_post2(const void* v, const void* beta, const float* dQa, const float* dW,
-                            const float* dWT, const float* dK1, const float* dM, const float* T,
-                            const float* G, const float* dU, const float* dUT, const float* Kf,
-                            const float* KT, const float* QT, void* gq, void* gk, void* gv,
-                            void* gbeta, int B, int L, int H, cudaStream_t st);
+int edb_delta_chunked_post(const float* resid, const void* dO, const void* v, const void* beta,
+                           const float* dSCT, const float* dU, const float* dUT, const float* Kf,
+                           const float* KT, const float* QT, const float* T, const float* G,
+                           void* gq, void* gk, void* gv, void* gbeta, int B, int L, int H,
+                           cudaStream_t st);
 
 size_t edb_delta_chunked_bwd_ws(int B, int L, int H) {
     return bwd_scratch_bytes((long long)B * H * ((L + C - 1) / C));
@@ -489,7 +330,6 @@ int edb_delta_chunked_bwd(const void* q, const void* k, const void* v, const voi
     if ((units * (NC + 1)) * D > 0x7fffffffLL) return EDB_ERR_UNSUPPORTED;
     BwdScratch w = carve_bwd(ws, nch);
     unsigned* err = edb::device_error_word();
-    const __nv_bfloat16* dob = (const __nv_bfloat16*)dO;
     cudaError_t e;
     PrepOut po{};
     po.KT = w.KT;
@@ -517,18 +357,6 @@ int edb_delta_chunked_bwd(const void* q, const void* k, const void* v, const voi
                                                                        NC, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
 
-    Post1Maps pm;
-    if ((s = make_box_map(&pm.S0T, resid, units * (NC + 1) * D, D, D))) return s;
-    if ((s = make_box_map(&pm.dSCT, w.dSCT, nch * D, D, D))) return s;
-    if ((s = make_box_map(&pm.Ut, resid + ckpt_state_floats(units, NC), nch * C, D, C))) return s;
-    if ((s = make_box_map(&pm.dU, w.dU, nch * C, D, C))) return s;
-    if ((e = cudaFuncSetAttribute(delta_post1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  P1_SMEM)) != cudaSuccess)
-        return (int)e;
-    delta_post1_kernel<<<dim3(NC, H, B), 128, P1_SMEM, st>>>(pm, dob, w.dQa, w.dW, w.dWT, w.dK1,
-                                                             w.dM, L, H, NC, err);
-    if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
-
-    return edb_delta_chunked_post2(v, beta, w.dQa, w.dW, w.dWT, w.dK1, w.dM, w.T, w.G, w.dU,
-                                   w.dUT, w.Kf, w.KT, w.QT, gq, gk, gv, gbeta, B, L, H, st);
+    return edb_delta_chunked_post(resid, dO, v, beta, w.dSCT, w.dU, w.dUT, w.Kf, w.KT, w.QT, w.T,
+                                  w.G, gq, gk, gv, gbeta, B, L, H, st);
 }
