@@ -8,8 +8,9 @@
 //   dQa^T = (dO S_0)^T, dW^T = -(dU~ S_0)^T, dK1^T = (U~ dS_C)^T   M=128, N=64, K=128
 //   dM    = tril(dO U~^T)                                         M=64,  N=64, K=128
 //   dT_b  = dW K^T + dU~ V^T                                      M=64,  N=64, K=2x128
-//   dbeta_s = sum_t dT_b[t][s] T[t][s],  dT = dT_b diag(beta)
-//   dA = -(T^T dT) T^T (strictly lower),  dbeta_t += sum_{s<t} dA[t][s] (K K^T)[t][s]
+//   X' = T^T dT_b,  dbeta_s = X'[s][s] (= sum_t dT_b[t][s] T[t][s])
+//   dA = -X' T_b^T (strictly lower; = -(T^T dT) T^T with dT = dT_b diag(beta)),
+//   dbeta_t += sum_{s<t} dA[t][s] (K K^T)[t][s]
 //   E = dG + dG^T,  dG = diag(beta) dA                             SIMT (64 x 64 x 64)
 //   dQ^T = dQa^T + K^T dM^T                                       M=128, N=64, K=64
 //   dV^T = dU~^T T_b                                              M=128, N=64, K=64
@@ -48,9 +49,10 @@ constexpr int SMEM = OFF_BAR + 64;
 constexpr int PHASE_A_TX = 8 * BOX_D + 8 * BOX_C;  // S_0^T, dS_C^T, U~, dU~
 constexpr int TM_Q = 0, TM_W = 64, TM_K = 128, TM_M = 192, TM_DTB = 256, TM_V = 320,
               TM_COLS = 512;
-// SIMT scratch of the C x C chain (floats, in R2..R3)
-constexpr int SC_T = 0, SC_DT = C * PC, SC_X = 2 * C * PC;
-static_assert((3 * C * PC) * 4 <= 8 * BOX_C, "chain scratch fits R2-R3");
+// SIMT scratch of the C x C chain (floats, in R2..R3): three [C][PS] arrays
+// and one [C]
+constexpr int PS = C + 4;
+static_assert((3 * C * PS + C) * 4 <= 8 * BOX_C, "chain scratch fits R2-R3");
 
 struct PostMaps {
     CUtensorMap S0T, dSCT, Ut, dU;  // phase A
@@ -80,7 +82,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t* s_misc = reinterpret_cast<uint32_t*>(bar_mma + 1);  // [0] tmem, [1] abort
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int ty = tid >> 4, tx = tid & 15;
     const long long bh = (long long)b * H + h;
     const long long ch = bh * NC + c;
     const int t0 = c * C, nvalid = min(C, L - t0);
@@ -247,128 +248,38 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     tc::fence_after_sync();
     const bool aborted2 = s_misc[1] != 0;
-    float* Ts = sc + SC_T;
-    float* Ds = sc + SC_DT;
-    float* Xs = sc + SC_X;
     if (!aborted2) {
-        // dT_b out of TMEM (M = 64: lanes 32w + r, r < 16, hold row 16w + r); T in
+        // ---- the C x C chain.  Thread (a, b) = (tid / 16, tid % 16) owns rows
+        // 4a..4a+3 and columns 4b..4b+3 of each 64 x 64 product; row-major f32
+        // scratch with rows of PS floats (float4 aligned), products by float4
+        // loads and packed f32x2 FMAs over the triangular ranges only.
+        float* Ts = sc;               // T [t][s]; then X'^T [t'][s]
+        float* Ds = sc + C * PS;      // dT_b [t][t']; then dA [t][s]
+        float* Tb = sc + 2 * C * PS;  // T_b^T [s][t] = T[t][s] beta_s
+        float* dbT = sc + 3 * C * PS; // [C]: sum_t dT_b[t][s] T[t][s]
+        const int a = tid >> 4, bq = tid & 15;
         if (warp < 4) {
+            // dT_b and dM out of TMEM (M = 64: lanes 32w + r, r < 16, hold row 16w + r);
+            // dM into the B tiles dM [t][s] and dM^T [s][t]
             uint32_t x0[32], x1[32];
             tc::tmem_ld32(tmem + TM_DTB + lane_base, x0);
             tc::tmem_ld32(tmem + TM_DTB + lane_base + 32, x1);
             tc::tmem_wait_ld();
+            const int t = 16 * warp + lane;
             if (lane < 16) {
-                const int t = 16 * warp + lane;
 #pragma unroll
-                for (int s = 0; s < 32; ++s) {
-                    Ds[t * PC + s] = __uint_as_float(x0[s]);
-                    Ds[t * PC + 32 + s] = __uint_as_float(x1[s]);
+                for (int s4 = 0; s4 < 32; s4 += 4) {
+                    st4(Ds + t * PS + s4, make_float4(__uint_as_float(x0[s4]), __uint_as_float(x0[s4 + 1]),
+                                                      __uint_as_float(x0[s4 + 2]), __uint_as_float(x0[s4 + 3])));
+                    st4(Ds + t * PS + 32 + s4,
+                        make_float4(__uint_as_float(x1[s4]), __uint_as_float(x1[s4 + 1]),
+                                    __uint_as_float(x1[s4 + 2]), __uint_as_float(x1[s4 + 3])));
                 }
             }
-        }
-#pragma unroll
-        for (int n = 0; n < NT; ++n) {
-            const int e0 = 4 * (tid + n * THREADS);
-            float* d = Ts + (e0 / C) * PC + e0 % C;
-            d[0] = tv[n].x;
-            d[1] = tv[n].y;
-            d[2] = tv[n].z;
-            d[3] = tv[n].w;
-        }
-        __syncthreads();
-        // dbeta through T_b: column s = tid / 4, four threads per column
-        float dbeta_part;
-        {
-            const int s = tid >> 2, qd = tid & 3;
-            float acc = 0.0f;
-            for (int t = qd; t < C; t += 4) acc = fmaf(Ds[t * PC + s], Ts[t * PC + s], acc);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            dbeta_part = acc + __shfl_xor_sync(0xffffffffu, acc, 2);
-        }
-        __syncthreads();
-        for (int idx = tid; idx < C * C; idx += THREADS) Ds[(idx / C) * PC + idx % C] *= bs[idx % C];
-        __syncthreads();
-        {  // X = T^T dT
-            float a[4][4];
-#pragma unroll
-            for (int r = 0; r < 4; ++r)
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc) a[r][cc] = 0.0f;
-            for (int t = 0; t < C; ++t) {
-                float at[4], bd[4];
-#pragma unroll
-                for (int r = 0; r < 4; ++r) at[r] = Ts[t * PC + ty + 16 * r];
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc) bd[cc] = Ds[t * PC + tx + 16 * cc];
-#pragma unroll
-                for (int r = 0; r < 4; ++r)
-#pragma unroll
-                    for (int cc = 0; cc < 4; ++cc) a[r][cc] = fmaf(at[r], bd[cc], a[r][cc]);
-            }
-#pragma unroll
-            for (int r = 0; r < 4; ++r)
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc) Xs[(ty + 16 * r) * PC + tx + 16 * cc] = a[r][cc];
-        }
-        __syncthreads();
-        {  // dA = -X T^T, strictly lower (into Ds: dT is no longer needed)
-            float a[4][4];
-#pragma unroll
-            for (int r = 0; r < 4; ++r)
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc) a[r][cc] = 0.0f;
-            for (int s = 0; s < C; ++s) {
-                float ax[4], bt[4];
-#pragma unroll
-                for (int r = 0; r < 4; ++r) ax[r] = Xs[(ty + 16 * r) * PC + s];
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc) bt[cc] = Ts[(tx + 16 * cc) * PC + s];
-#pragma unroll
-                for (int r = 0; r < 4; ++r)
-#pragma unroll
-                    for (int cc = 0; cc < 4; ++cc) a[r][cc] = fmaf(ax[r], bt[cc], a[r][cc]);
-            }
-            __syncthreads();  // every read of Ds (dT) and Xs (X) is done
-#pragma unroll
-            for (int r = 0; r < 4; ++r)
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {
-                    const int row = ty + 16 * r, col = tx + 16 * cc;
-                    Ds[row * PC + col] = col < row ? -a[r][cc] : 0.0f;
-                }
-        }
-        __syncthreads();
-        // dbeta through A: row t = tid / 4 (same threads as the column sums above)
-        {
-            const int t = tid >> 2, qd = tid & 3;
-            const float* g = Gg + (ch * C + t) * C + 16 * qd;
-            float acc = 0.0f;
-#pragma unroll
-            for (int s4 = 0; s4 < 16; s4 += 4) {
-                const float4 gv4 = f4(g + s4);
-                const float* da = Ds + t * PC + 16 * qd + s4;
-                acc = fmaf(da[0], gv4.x, fmaf(da[1], gv4.y, fmaf(da[2], gv4.z, fmaf(da[3], gv4.w, acc))));
-            }
-            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-            if (qd == 0 && t < nvalid)
-                gbeta[((long long)b * L + t0 + t) * H + h] = __float2bfloat16(acc + dbeta_part);
-        }
-        for (int idx = tid; idx < C * C; idx += THREADS) {
-            const int t = idx / C, s = idx % C;
-            Xs[t * PC + s] = bs[t] * Ds[t * PC + s] + bs[s] * Ds[s * PC + t];
-        }
-        __syncthreads();
-        // ---- B tiles of the last products (K-major [n][k]): dM [t][s], dM^T [s][t]
-        // (warps 0-3, from TMEM), T_b^T [s][t] = T[t][s] beta_s and E [s][t]
-        // (symmetric) (warps 4-7)
-        if (warp < 4) {
-            uint32_t x0[32], x1[32];
             tc::tmem_ld32(tmem + TM_M + lane_base, x0);
             tc::tmem_ld32(tmem + TM_M + lane_base + 32, x1);
             tc::tmem_wait_ld();
             if (lane < 16) {
-                const int t = 16 * warp + lane;
 #pragma unroll
                 for (int s4 = 0; s4 < C; s4 += 4) {
                     float m[4];
@@ -382,18 +293,107 @@ __global__ void __launch_bounds__(THREADS, 1)
                         make_float4(m[0], m[1], m[2], m[3]));
                 }
             }
-        } else {
-            for (int idx = tid - 128; idx < C * C / 4; idx += 128) {
-                const int s = idx / (C / 4), t4 = (idx % (C / 4)) * 4;
-                const float bsv = bs[s];
-                st4(reinterpret_cast<float*>(smem + OFF_TBT + kmaj_off4(s, t4, C)),
-                    make_float4(Ts[t4 * PC + s] * bsv, Ts[(t4 + 1) * PC + s] * bsv,
-                                Ts[(t4 + 2) * PC + s] * bsv, Ts[(t4 + 3) * PC + s] * bsv));
-                st4(reinterpret_cast<float*>(smem + OFF_E + kmaj_off4(s, t4, C)),
-                    make_float4(Xs[s * PC + t4], Xs[s * PC + t4 + 1], Xs[s * PC + t4 + 2],
-                                Xs[s * PC + t4 + 3]));
+        }
+        // T rows; T_b^T (scratch and the K-major B tile [s][t])
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            const int e0 = 4 * (tid + n * THREADS), t = e0 / C, s0 = e0 % C;
+            st4(Ts + t * PS + s0, tv[n]);
+            const float tvv[4] = {tv[n].x, tv[n].y, tv[n].z, tv[n].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float tb = tvv[e] * bs[s0 + e];
+                Tb[(s0 + e) * PS + t] = tb;
+                st_f32(smem + OFF_TBT, kmaj_off4(s0 + e, t & ~3, C) + (t & 3) * 4, tb);
             }
         }
+        __syncthreads();
+        float2 acc[4][2];
+        // X' = T^T dT_b (T[t][s] = 0 for t < s); its diagonal is the dbeta term of T_b
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[r][0] = acc[r][1] = make_float2(0.0f, 0.0f);
+        for (int t = 4 * a; t < C; ++t) {
+            const float4 tt = ld4(Ts + t * PS + 4 * a), dd = ld4(Ds + t * PS + 4 * bq);
+            const float2 d01 = make_float2(dd.x, dd.y), d23 = make_float2(dd.z, dd.w);
+            const float tr[4] = {tt.x, tt.y, tt.z, tt.w};
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                acc[r][0] = fma2(dup2(tr[r]), d01, acc[r][0]);
+                acc[r][1] = fma2(dup2(tr[r]), d23, acc[r][1]);
+            }
+        }
+        if (a == bq) {
+            dbT[4 * a] = acc[0][0].x;
+            dbT[4 * a + 1] = acc[1][0].y;
+            dbT[4 * a + 2] = acc[2][1].x;
+            dbT[4 * a + 3] = acc[3][1].y;
+        }
+        __syncthreads();  // T is no longer read: X'^T goes in its place
+        st4(Ts + (4 * bq) * PS + 4 * a, make_float4(acc[0][0].x, acc[1][0].x, acc[2][0].x, acc[3][0].x));
+        st4(Ts + (4 * bq + 1) * PS + 4 * a, make_float4(acc[0][0].y, acc[1][0].y, acc[2][0].y, acc[3][0].y));
+        st4(Ts + (4 * bq + 2) * PS + 4 * a, make_float4(acc[0][1].x, acc[1][1].x, acc[2][1].x, acc[3][1].x));
+        st4(Ts + (4 * bq + 3) * PS + 4 * a, make_float4(acc[0][1].y, acc[1][1].y, acc[2][1].y, acc[3][1].y));
+        __syncthreads();
+        // dA = -X' T_b^T, strictly lower (T_b[col][s] = 0 for s > col): only
+        // blocks with b <= a are nonzero
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[r][0] = acc[r][1] = make_float2(0.0f, 0.0f);
+        if (bq <= a) {
+            for (int s = 0; s <= 4 * bq + 3; ++s) {
+                const float4 xv = ld4(Ts + s * PS + 4 * a), tb = ld4(Tb + s * PS + 4 * bq);
+                const float2 t01 = make_float2(tb.x, tb.y), t23 = make_float2(tb.z, tb.w);
+                const float xr[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    acc[r][0] = fma2(dup2(xr[r]), t01, acc[r][0]);
+                    acc[r][1] = fma2(dup2(xr[r]), t23, acc[r][1]);
+                }
+            }
+        }
+        float dA[4][4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const float v4[4] = {acc[r][0].x, acc[r][0].y, acc[r][1].x, acc[r][1].y};
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) dA[r][cc] = 4 * bq + cc < 4 * a + r ? -v4[cc] : 0.0f;
+        }
+        // dT_b is no longer read (its last reader was X'): dA goes in its place
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+            st4(Ds + (4 * a + r) * PS + 4 * bq, make_float4(dA[r][0], dA[r][1], dA[r][2], dA[r][3]));
+        // dbeta_t = sum_s dT_b[t][s]-term (diagonal of X') + sum_{s<t} dA[t][s] (K K^T)[t][s]
+        {
+            float p[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const float4 g = f4(Gg + (ch * C + 4 * a + r) * C + 4 * bq);
+                p[r] = dA[r][0] * g.x + dA[r][1] * g.y + dA[r][2] * g.z + dA[r][3] * g.w;
+#pragma unroll
+                for (int o = 1; o < 16; o <<= 1) p[r] += __shfl_xor_sync(0xffffffffu, p[r], o);
+            }
+            __syncthreads();  // dA and dbT complete
+            if (bq == 0) {
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const int t = 4 * a + r;
+                    if (t < nvalid)
+                        gbeta[((long long)b * L + t0 + t) * H + h] = __float2bfloat16(p[r] + dbT[t]);
+                }
+            }
+        }
+        // E = dG + dG^T, dG = diag(beta) dA, into its B tile (symmetric)
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+            const float4 tr = ld4(Ds + (4 * bq + cc) * PS + 4 * a);  // dA[4b+cc][4a..4a+3]
+            const float trv[4] = {tr.x, tr.y, tr.z, tr.w};
+            const float bc = bs[4 * bq + cc];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) dA[r][cc] = bs[4 * a + r] * dA[r][cc] + bc * trv[r];
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+            st4(reinterpret_cast<float*>(smem + OFF_E + kmaj_off4(4 * a + r, 4 * bq, C)),
+                make_float4(dA[r][0], dA[r][1], dA[r][2], dA[r][3]));
     }
     fence_proxy_async();
     tc::fence_before_sync();
