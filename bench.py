@@ -444,8 +444,8 @@ class DeltaWorkload:
         # dense chunked contractions: measured against the tensor peak
         return {"fwd": ("tensor", self.cfg.flops_fwd()), "bwd": ("tensor", self.cfg.flops_bwd())}
 
-    # chunked path: prep + state (forward), prep + state + two post kernels (backward)
-    launches_per_step = 6
+    # chunked path: prep + state (forward), prep + state + post (backward)
+    launches_per_step = 5
     tokens = property(lambda self: self.cfg.tokens)
 
     def step(self, ev=None):
