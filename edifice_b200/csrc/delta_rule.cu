@@ -13,12 +13,21 @@
 // q, k, v, o: [B, L, H, d]; beta: [B, L, H, d] (per element, the model's form,
 // delta_net.ex:285-297) or [B, L, H] (one gate per token and head).
 //
+// GatedDeltaNet (fused_scan.ex:2256-2284, 1347-1431; gated_delta_net.ex:300-350)
+// adds a decay alpha [B, L, H] per token and head: S_d = alpha_t S_{t-1},
+// r = S_d k_t, S_t = S_d + (beta_t (.) (v_t - r)) k_t^T; its gradients add
+// dalpha_t = <dS_d, S_{t-1}> and dS_{t-1} = alpha_t dS_d.
+//
 // This file is the general path (any d <= 128, either beta form, f32 or bf16
 // io): one CTA per (b, h) holding S (and dS) in shared memory as f32, token
 // order.  The forward can write S at the start of every CK-token chunk (plus
-// the final state); the backward walks chunks in reverse, recomputes each
-// chunk's retrievals r_t from its checkpoint, and undoes the updates
+// the final state); the delta-rule backward walks chunks in reverse, recomputes
+// each chunk's retrievals r_t from its checkpoint, and undoes the updates
 // (S_{t-1} = S_t - u_t k_t^T with the stored r_t) instead of storing every state.
+// The gated backward cannot undo an update (that divides by alpha_t, which
+// amplifies rounding by 1/alpha per token): it recomputes each chunk's states
+// S_{t-1} forward from the checkpoint into a global buffer and reads them back
+// in reverse.
 #include <math.h>
 
 #include "edb_common.cuh"
@@ -37,8 +46,9 @@ static __device__ __forceinline__ float ldv(const T* p) {
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
     delta_fwd_rec_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-                         const T* __restrict__ beta, T* __restrict__ o, float* __restrict__ ckpt,
-                         int L, int H, int d, int beta_scalar) {
+                         const T* __restrict__ beta, const T* __restrict__ alpha,
+                         T* __restrict__ o, float* __restrict__ ckpt, int L, int H, int d,
+                         int beta_scalar) {
     extern __shared__ float sm[];
     const int sd = d + 1;
     float* S = sm;
@@ -63,19 +73,21 @@ __global__ void __launch_bounds__(kThreads)
             sk[i] = ldv(k + off + i);
         }
         __syncthreads();
+        // gated form: S_d = alpha S, so r = alpha (S k) and S_t = alpha S + u k^T
+        const float al = alpha != nullptr ? ldv(alpha + ((long long)b * L + t) * H + h) : 1.0f;
         for (int i = tid; i < d; i += kThreads) {
             float r = 0.0f;
             for (int j = 0; j < d; ++j) r = fmaf(S[i * sd + j], sk[j], r);
             const float be = beta_scalar ? ldv(beta + ((long long)b * L + t) * H + h)
                                          : ldv(beta + off + i);
-            su[i] = be * (ldv(v + off + i) - r);
+            su[i] = be * (ldv(v + off + i) - al * r);
         }
         __syncthreads();
         for (int i = tid; i < d; i += kThreads) {
             const float u = su[i];
             float acc = 0.0f;
             for (int j = 0; j < d; ++j) {
-                const float s = fmaf(u, sk[j], S[i * sd + j]);
+                const float s = fmaf(u, sk[j], al * S[i * sd + j]);
                 S[i * sd + j] = s;
                 acc = fmaf(s, sq[j], acc);
             }
@@ -206,6 +218,151 @@ __global__ void __launch_bounds__(kThreads)
     }
 }
 
+// Gated backward.  sbuf: [B*H][CK][d][d] f32 scratch for one chunk's states
+// S_{t-1} (written by the chunk's forward recompute, read back in reverse).
+// shared: Sa, Sb, dS [d][d+1] | q k dO u beta-dsk err [6][d] | red [kThreads]
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+    gated_bwd_rec_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                         const T* __restrict__ beta, const T* __restrict__ alpha,
+                         const T* __restrict__ dO, const float* __restrict__ ckpt,
+                         float* __restrict__ sbuf, T* __restrict__ gq, T* __restrict__ gk,
+                         T* __restrict__ gv, T* __restrict__ gbeta, T* __restrict__ galpha,
+                         int L, int H, int d, int beta_scalar) {
+    extern __shared__ float sm[];
+    const int sd = d + 1;
+    float* Sa = sm;                // S_t (after the token's update)
+    float* Sb = Sa + d * sd;       // S_{t-1}
+    float* dS = Sb + d * sd;       // gradient w.r.t. S_t
+    float* sq = dS + d * sd;
+    float* sk = sq + d;
+    float* sdo = sk + d;
+    float* su = sdo + d;           // beta (.) err
+    float* sbd = su + d;           // beta (.) dS k
+    float* ser = sbd + d;          // err = v - alpha S_{t-1} k
+    float* red = ser + d;          // [kThreads]
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nck = (L + CK - 1) / CK;
+    const long long rs = (long long)H * d;
+    const long long base = (long long)b * L * rs + (long long)h * d;
+    float* buf = sbuf + ((long long)b * H + h) * CK * d * d;
+    for (int i = tid; i < d * sd; i += kThreads) dS[i] = 0.0f;
+
+    // block sum of one value per thread; every thread gets the total
+    auto block_sum = [&](float x) {
+        for (int o = 16; o >= 1; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+        __syncthreads();  // red is free
+        if (lane == 0) red[warp] = x;
+        __syncthreads();
+        float s = 0.0f;
+        for (int w = 0; w < kThreads / 32; ++w) s += red[w];
+        return s;
+    };
+
+    for (int c = nck - 1; c >= 0; --c) {
+        const int t0 = c * CK, t1 = min(L, t0 + CK);
+        const float* cp = ckpt + (((long long)b * H + h) * (nck + 1) + c) * d * d;
+        __syncthreads();
+        for (int i = tid; i < d * d; i += kThreads) Sa[(i / d) * sd + i % d] = cp[i];
+        __syncthreads();
+        // ---- forward over the chunk: S_{t-1} -> buf[t - t0]; Sa ends as S_{t1-1}
+        for (int t = t0; t < t1; ++t) {
+            const long long off = base + (long long)t * rs;
+            float* dst = buf + (long long)(t - t0) * d * d;
+            for (int i = tid; i < d * d; i += kThreads) dst[i] = Sa[(i / d) * sd + i % d];
+            for (int i = tid; i < d; i += kThreads) sk[i] = ldv(k + off + i);
+            __syncthreads();
+            const float al = ldv(alpha + ((long long)b * L + t) * H + h);
+            for (int i = tid; i < d; i += kThreads) {
+                float r = 0.0f;
+                for (int j = 0; j < d; ++j) r = fmaf(Sa[i * sd + j], sk[j], r);
+                const float be = beta_scalar ? ldv(beta + ((long long)b * L + t) * H + h)
+                                             : ldv(beta + off + i);
+                const float u = be * (ldv(v + off + i) - al * r);
+                for (int j = 0; j < d; ++j) Sa[i * sd + j] = fmaf(u, sk[j], al * Sa[i * sd + j]);
+            }
+            __syncthreads();
+        }
+        // ---- reverse over the chunk (Sa = S_t, Sb = S_{t-1})
+        for (int t = t1 - 1; t >= t0; --t) {
+            const long long off = base + (long long)t * rs;
+            const long long boff = ((long long)b * L + t) * H + h;
+            const float al = ldv(alpha + boff);
+            const float* srcb = buf + (long long)(t - t0) * d * d;
+            for (int i = tid; i < d * d; i += kThreads) Sb[(i / d) * sd + i % d] = srcb[i];
+            for (int i = tid; i < d; i += kThreads) {
+                sq[i] = ldv(q + off + i);
+                sk[i] = ldv(k + off + i);
+                sdo[i] = ldv(dO + off + i);
+            }
+            __syncthreads();
+            // rows: dS += dO q^T ; u = beta (v - alpha S_{t-1} k)
+            for (int i = tid; i < d; i += kThreads) {
+                const float doi = sdo[i];
+                float r = 0.0f;
+                for (int j = 0; j < d; ++j) {
+                    dS[i * sd + j] = fmaf(doi, sq[j], dS[i * sd + j]);
+                    r = fmaf(Sb[i * sd + j], sk[j], r);
+                }
+                const float be = beta_scalar ? ldv(beta + boff) : ldv(beta + off + i);
+                const float err = ldv(v + off + i) - al * r;
+                ser[i] = err;
+                su[i] = be * err;
+            }
+            __syncthreads();
+            // columns: dq = S_t^T dO
+            for (int j = tid; j < d; j += kThreads) {
+                float acc = 0.0f;
+                for (int i = 0; i < d; ++i) acc = fmaf(Sa[i * sd + j], sdo[i], acc);
+                st_scalar<T>(gq + off + j, acc);
+            }
+            // rows: dsk = dS k; dv = beta dsk; dbeta = err dsk
+            float bsum = 0.0f;
+            for (int i = tid; i < d; i += kThreads) {
+                float dsk = 0.0f;
+                for (int j = 0; j < d; ++j) dsk = fmaf(dS[i * sd + j], sk[j], dsk);
+                const float be = beta_scalar ? ldv(beta + boff) : ldv(beta + off + i);
+                const float err = ser[i];
+                st_scalar<T>(gv + off + i, be * dsk);
+                if (beta_scalar) bsum = fmaf(err, dsk, bsum);
+                else st_scalar<T>(gbeta + off + i, err * dsk);
+                sbd[i] = be * dsk;
+            }
+            if (beta_scalar) {
+                const float s = block_sum(bsum);
+                if (tid == 0) st_scalar<T>(gbeta + boff, s);
+            }
+            __syncthreads();
+            // columns: dk = dS^T u - alpha S_{t-1}^T (beta dsk)
+            for (int j = tid; j < d; j += kThreads) {
+                float acc = 0.0f;
+                for (int i = 0; i < d; ++i)
+                    acc += dS[i * sd + j] * su[i] - al * Sb[i * sd + j] * sbd[i];
+                st_scalar<T>(gk + off + j, acc);
+            }
+            __syncthreads();
+            // rows: dS_d = dS - (beta dsk) k^T; dalpha = <dS_d, S_{t-1}>; dS_{t-1} = alpha dS_d
+            float ga = 0.0f;
+            for (int i = tid; i < d; i += kThreads) {
+                const float bd = sbd[i];
+                for (int j = 0; j < d; ++j) {
+                    const float x = fmaf(-bd, sk[j], dS[i * sd + j]);
+                    ga = fmaf(x, Sb[i * sd + j], ga);
+                    dS[i * sd + j] = al * x;
+                }
+            }
+            const float gas = block_sum(ga);
+            if (tid == 0) st_scalar<T>(galpha + boff, gas);
+            // S_{t-1} becomes the next step's S_t
+            float* tmp = Sa;
+            Sa = Sb;
+            Sb = tmp;
+            __syncthreads();
+        }
+    }
+}
+
 size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 size_t ckpt_bytes(int B, int L, int H, int d) {
@@ -214,19 +371,42 @@ size_t ckpt_bytes(int B, int L, int H, int d) {
 }
 
 size_t fwd_smem(int d) { return ((size_t)d * (d + 1) + 3 * d) * sizeof(float); }
+size_t gated_bwd_smem(int d) {
+    return ((size_t)3 * d * (d + 1) + 6 * d + kThreads) * sizeof(float);
+}
+size_t gated_state_buf_bytes(int B, int H, int d) {
+    return (size_t)B * H * CK * d * d * sizeof(float);
+}
 size_t bwd_smem(int d) {
     return ((size_t)2 * d * (d + 1) + (size_t)CK * d + 5 * d + kThreads) * sizeof(float);
 }
 
 template <typename T>
-int launch_fwd(const void* q, const void* k, const void* v, const void* beta, void* o,
-               float* ckpt, int B, int L, int H, int d, int beta_scalar, cudaStream_t st) {
+int launch_fwd(const void* q, const void* k, const void* v, const void* beta, const void* alpha,
+               void* o, float* ckpt, int B, int L, int H, int d, int beta_scalar,
+               cudaStream_t st) {
     const size_t smem = fwd_smem(d);
     cudaError_t e = cudaFuncSetAttribute(delta_fwd_rec_kernel<T>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return (int)e;
     delta_fwd_rec_kernel<T><<<dim3(H, B), kThreads, smem, st>>>(
-        (const T*)q, (const T*)k, (const T*)v, (const T*)beta, (T*)o, ckpt, L, H, d, beta_scalar);
+        (const T*)q, (const T*)k, (const T*)v, (const T*)beta, (const T*)alpha, (T*)o, ckpt, L,
+        H, d, beta_scalar);
+    return edb::status_from_cuda(cudaGetLastError());
+}
+
+template <typename T>
+int launch_gated_bwd(const void* q, const void* k, const void* v, const void* beta,
+                     const void* alpha, const void* dO, const float* ckpt, float* sbuf, void* gq,
+                     void* gk, void* gv, void* gbeta, void* galpha, int B, int L, int H, int d,
+                     int beta_scalar, cudaStream_t st) {
+    const size_t smem = gated_bwd_smem(d);
+    cudaError_t e = cudaFuncSetAttribute(gated_bwd_rec_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    gated_bwd_rec_kernel<T><<<dim3(H, B), kThreads, smem, st>>>(
+        (const T*)q, (const T*)k, (const T*)v, (const T*)beta, (const T*)alpha, (const T*)dO,
+        ckpt, sbuf, (T*)gq, (T*)gk, (T*)gv, (T*)gbeta, (T*)galpha, L, H, d, beta_scalar);
     return edb::status_from_cuda(cudaGetLastError());
 }
 
@@ -299,10 +479,10 @@ extern "C" int edb_delta_rule_fwd(int dtype, const void* q, const void* k, const
     }
     const int bs = beta_per_element ? 0 : 1;
     return dtype == EDB_BF16
-               ? launch_fwd<__nv_bfloat16>(q, k, v, beta, o, s_ckpt, batch, seq_len, heads,
-                                           head_dim, bs, st)
-               : launch_fwd<float>(q, k, v, beta, o, s_ckpt, batch, seq_len, heads, head_dim, bs,
-                                   st);
+               ? launch_fwd<__nv_bfloat16>(q, k, v, beta, nullptr, o, s_ckpt, batch, seq_len,
+                                           heads, head_dim, bs, st)
+               : launch_fwd<float>(q, k, v, beta, nullptr, o, s_ckpt, batch, seq_len, heads,
+                                   head_dim, bs, st);
 }
 
 extern "C" size_t edb_delta_rule_bwd_workspace(int dtype, int beta_per_element, int batch,
@@ -369,4 +549,76 @@ extern "C" int edb_delta_rule_bwd(int dtype, const void* q, const void* k, const
                                            seq_len, heads, head_dim, bs, st)
                : launch_bwd<float>(q, k, v, beta, dO, ck, gq, gk, gv, gbeta, batch, seq_len,
                                    heads, head_dim, bs, st);
+}
+
+// ------------------------------------------------------------------ GatedDeltaNet
+// Token recurrence only (the chunked tensor-core form serves the ungated rule).
+extern "C" size_t edb_gated_delta_net_ckpt_bytes(int dtype, int beta_per_element, int batch,
+                                                 int seq_len, int heads, int head_dim) {
+    (void)beta_per_element;
+    if (check(dtype, batch, seq_len, heads, head_dim)) return 0;
+    return ckpt_bytes(batch, seq_len, heads, head_dim);
+}
+
+extern "C" int edb_gated_delta_net_fwd(int dtype, const void* q, const void* k, const void* v,
+                                       const void* beta, int beta_per_element, const void* alpha,
+                                       void* o, float* s_ckpt, int batch, int seq_len, int heads,
+                                       int head_dim, void* stream) {
+    if (int s = check(dtype, batch, seq_len, heads, head_dim)) return s;
+    if (!q || !k || !v || !beta || !alpha || !o) return EDB_ERR_NULL_POINTER;
+    const int bs = beta_per_element ? 0 : 1;
+    cudaStream_t st = (cudaStream_t)stream;
+    return dtype == EDB_BF16
+               ? launch_fwd<__nv_bfloat16>(q, k, v, beta, alpha, o, s_ckpt, batch, seq_len,
+                                           heads, head_dim, bs, st)
+               : launch_fwd<float>(q, k, v, beta, alpha, o, s_ckpt, batch, seq_len, heads,
+                                   head_dim, bs, st);
+}
+
+extern "C" size_t edb_gated_delta_net_bwd_workspace(int dtype, int beta_per_element, int batch,
+                                                    int seq_len, int heads, int head_dim,
+                                                    int have_ckpt) {
+    if (check(dtype, batch, seq_len, heads, head_dim)) return 0;
+    const size_t ck = have_ckpt ? 0
+                                : a256(edb_gated_delta_net_ckpt_bytes(dtype, beta_per_element,
+                                                                      batch, seq_len, heads,
+                                                                      head_dim));
+    return ck + gated_state_buf_bytes(batch, heads, head_dim);
+}
+
+extern "C" int edb_gated_delta_net_bwd(int dtype, const void* q, const void* k, const void* v,
+                                       const void* beta, int beta_per_element, const void* alpha,
+                                       const void* dO, const float* s_ckpt, void* gq, void* gk,
+                                       void* gv, void* gbeta, void* galpha, int batch,
+                                       int seq_len, int heads, int head_dim, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+    if (int s = check(dtype, batch, seq_len, heads, head_dim)) return s;
+    if (!q || !k || !v || !beta || !alpha || !dO || !gq || !gk || !gv || !gbeta || !galpha)
+        return EDB_ERR_NULL_POINTER;
+    const size_t need = edb_gated_delta_net_bwd_workspace(dtype, beta_per_element, batch,
+                                                          seq_len, heads, head_dim,
+                                                          s_ckpt != nullptr);
+    if (workspace_bytes < need || !workspace) return EDB_ERR_WORKSPACE_TOO_SMALL;
+    if (reinterpret_cast<uintptr_t>(workspace) & 15u) return EDB_ERR_MISALIGNED;
+    cudaStream_t st = (cudaStream_t)stream;
+    char* p = static_cast<char*>(workspace);
+    const float* ck = s_ckpt;
+    if (!ck) {
+        // states only: the forward writes o into gq, which the backward overwrites
+        float* w = reinterpret_cast<float*>(p);
+        p += a256(edb_gated_delta_net_ckpt_bytes(dtype, beta_per_element, batch, seq_len, heads,
+                                                 head_dim));
+        int s = edb_gated_delta_net_fwd(dtype, q, k, v, beta, beta_per_element, alpha, gq, w,
+                                        batch, seq_len, heads, head_dim, stream);
+        if (s) return s;
+        ck = w;
+    }
+    const int bs = beta_per_element ? 0 : 1;
+    float* sbuf = reinterpret_cast<float*>(p);
+    return dtype == EDB_BF16
+               ? launch_gated_bwd<__nv_bfloat16>(q, k, v, beta, alpha, dO, ck, sbuf, gq, gk, gv,
+                                                 gbeta, galpha, batch, seq_len, heads, head_dim,
+                                                 bs, st)
+               : launch_gated_bwd<float>(q, k, v, beta, alpha, dO, ck, sbuf, gq, gk, gv, gbeta,
+                                         galpha, batch, seq_len, heads, head_dim, bs, st);
 }

@@ -258,6 +258,68 @@ class DeltaNetFn(torch.autograd.Function):
         return delta_rule_backward(q, k, v, beta, grad_output.contiguous(), ck)
 
 
+def _gated_shapes(q, k, v, beta, alpha):
+    B, L, H, d, per_el = _delta_shapes(q, k, v, beta)
+    if tuple(alpha.shape) != (B, L, H) or alpha.dtype != q.dtype:
+        raise _lib.EdbError("gated_delta_net: alpha must be [B, L, H] of the q dtype, got %s %s"
+                            % (tuple(alpha.shape), alpha.dtype))
+    return B, L, H, d, per_el
+
+
+def gated_delta_net_scan(q, k, v, beta, alpha, with_ckpt=False):
+    """FusedScan.gated_delta_net_scan/5 (fused_scan.ex:219-233): q, k (L2-normalised),
+    v [B, L, H, d]; beta (post-sigmoid) [B, L, H, d] or [B, L, H]; alpha (decay)
+    [B, L, H] -> o [B, L, H, d].  with_ckpt=True also returns the f32 chunk-start
+    states the backward can reuse."""
+    _dev(q, k, v, beta, alpha, what="gated_delta_net_scan")
+    B, L, H, d, per_el = _gated_shapes(q, k, v, beta, alpha)
+    o = torch.empty_like(q)
+    lib = _lib.load()
+    dt = _dtype_code(q, "gated_delta_net_scan")
+    ck = None
+    if with_ckpt:
+        ck = torch.empty(lib.edb_gated_delta_net_ckpt_bytes(dt, per_el, B, L, H, d) // 4,
+                         dtype=torch.float32, device=q.device)
+    _lib.check(lib.edb_gated_delta_net_fwd(dt, _p(q), _p(k), _p(v), _p(beta), per_el, _p(alpha),
+                                           _p(o), _p(ck), B, L, H, d, _stream()),
+               "CUDA fused GatedDeltaNet scan")
+    return (o, ck) if with_ckpt else o
+
+
+def gated_delta_net_backward(q, k, v, beta, alpha, grad_output, s_ckpt=None):
+    """Returns (grad_q, grad_k, grad_v, grad_beta, grad_alpha).  Mirrors
+    gated_delta_net_backward_dispatch/7 (fused_scan.ex:1330-1345)."""
+    _dev(q, k, v, beta, alpha, grad_output, s_ckpt, what="gated_delta_net_backward")
+    B, L, H, d, per_el = _gated_shapes(q, k, v, beta, alpha)
+    lib = _lib.load()
+    gq, gk, gv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    gb, ga = torch.empty_like(beta), torch.empty_like(alpha)
+    dt = _dtype_code(q, "gated_delta_net_backward")
+    wsb = lib.edb_gated_delta_net_bwd_workspace(dt, per_el, B, L, H, d, int(s_ckpt is not None))
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=q.device)
+    _lib.check(lib.edb_gated_delta_net_bwd(dt, _p(q), _p(k), _p(v), _p(beta), per_el, _p(alpha),
+                                           _p(grad_output), _p(s_ckpt), _p(gq), _p(gk), _p(gv),
+                                           _p(gb), _p(ga), B, L, H, d, _p(ws), wsb, _stream()),
+               "CUDA fused GatedDeltaNet scan backward")
+    return gq, gk, gv, gb, ga
+
+
+class GatedDeltaNetFn(torch.autograd.Function):
+    """custom_grad wiring of gated_delta_net_custom_call/5 (fused_scan.ex:2239-2254):
+    gradients to q, k, v, beta, alpha."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, beta, alpha):
+        o, ck = gated_delta_net_scan(q, k, v, beta, alpha, with_ckpt=True)
+        ctx.save_for_backward(q, k, v, beta, alpha, ck)
+        return o
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        q, k, v, beta, alpha, ck = ctx.saved_tensors
+        return gated_delta_net_backward(q, k, v, beta, alpha, grad_output.contiguous(), ck)
+
+
 def _attn_shapes(q, k, v):
     if q.dim() != 4 or k.dim() != 4 or k.shape != v.shape:
         raise _lib.EdbError("flash_attention: expected [B, H, L, d] q and equal k/v shapes")

@@ -109,6 +109,47 @@ int fused_delta_rule_scan_backward_launch(cudaStream_t stream, const edb_io_t* q
     return st;
 }
 
+int fused_gated_delta_net_scan_launch(cudaStream_t stream, const edb_io_t* q,
+                                      const edb_io_t* k, const edb_io_t* v, const edb_io_t* beta,
+                                      const edb_io_t* alpha, edb_io_t* output, int batch,
+                                      int seq_len, int num_heads, int head_dim) {
+    return edb_gated_delta_net_fwd(kDtype, q, k, v, beta, 1, alpha, output, nullptr, batch,
+                                   seq_len, num_heads, head_dim, stream);
+}
+
+int fused_delta_rule_scan_launch(cudaStream_t stream, const edb_io_t* q, const edb_io_t* k,
+                                 const edb_io_t* v, const edb_io_t* beta, const edb_io_t* alpha,
+                                 edb_io_t* output, int batch, int seq_len, int num_heads,
+                                 int head_dim) {
+    if (alpha != nullptr)
+        return fused_gated_delta_net_scan_launch(stream, q, k, v, beta, alpha, output, batch,
+                                                 seq_len, num_heads, head_dim);
+    return fused_delta_net_scan_launch(stream, q, k, v, beta, output, batch, seq_len, num_heads,
+                                       head_dim);
+}
+
+int fused_gated_delta_net_scan_backward_launch(cudaStream_t stream, const edb_io_t* q,
+                                               const edb_io_t* k, const edb_io_t* v,
+                                               const edb_io_t* beta, const edb_io_t* alpha,
+                                               const edb_io_t* forward_out,
+                                               const edb_io_t* grad_output,
+                                               edb_io_t* output_concat, int batch, int seq_len,
+                                               int num_heads, int head_dim) {
+    (void)forward_out;  // the backward recomputes what it needs from q, k, v, beta, alpha
+    const long long n = (long long)batch * seq_len * num_heads * head_dim;
+    const size_t wsb =
+        edb_gated_delta_net_bwd_workspace(kDtype, 1, batch, seq_len, num_heads, head_dim, 0);
+    void* ws = nullptr;
+    cudaError_t e = cudaMallocAsync(&ws, wsb, stream);
+    if (e != cudaSuccess) return (int)e;
+    int st = edb_gated_delta_net_bwd(kDtype, q, k, v, beta, 1, alpha, grad_output, nullptr,
+                                     output_concat, output_concat + n, output_concat + 2 * n,
+                                     output_concat + 3 * n, output_concat + 4 * n, batch, seq_len,
+                                     num_heads, head_dim, ws, wsb, stream);
+    cudaFreeAsync(ws, stream);
+    return st;
+}
+
 int fused_flash_attention_launch(cudaStream_t stream, const edb_io_t* q, const edb_io_t* k,
                                  const edb_io_t* v, edb_io_t* output, int batch, int num_heads,
                                  int seq_len, int head_dim, int causal) {

@@ -220,6 +220,46 @@ int edb_delta_rule_bwd(int dtype, const void* q, const void* k, const void* v, c
                        void* gk, void* gv, void* gbeta, int batch, int seq_len, int heads,
                        int head_dim, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ----------------------------------------------------------------------
+ * GatedDeltaNet: per token, S_d = alpha_t S_{t-1}; r = S_d k_t;
+ * S_t = S_d + (beta_t (.) (v_t - r)) k_t^T; o_t = S_t q_t (S_0 = 0).
+ * q, k, v, o, beta as edb_delta_rule_fwd; alpha: [batch, seq_len, heads]
+ * (one decay per token and head, Edifice.build(:gated_delta_net)'s form,
+ * lib/edifice/recurrent/gated_delta_net.ex:389-394).  head_dim <= 128; token
+ * recurrence for every dtype and beta form.  s_ckpt (optional, f32,
+ * edb_gated_delta_net_ckpt_bytes() bytes): S at the start of every 64-token
+ * chunk and the final S, [batch][heads][nchunks + 1][d][d].
+ * Replaces fused_gated_delta_net_scan_launch / fused_delta_rule_scan_launch
+ * with alpha (native/cuda/fused_delta_rule_scan.cu:213-258); Nx semantics
+ * lib/edifice/cuda/fused_scan.ex:2256-2284.
+ * ---------------------------------------------------------------------- */
+size_t edb_gated_delta_net_ckpt_bytes(int dtype, int beta_per_element, int batch, int seq_len,
+                                      int heads, int head_dim);
+
+int edb_gated_delta_net_fwd(int dtype, const void* q, const void* k, const void* v,
+                            const void* beta, int beta_per_element, const void* alpha, void* o,
+                            float* s_ckpt, int batch, int seq_len, int heads, int head_dim,
+                            void* stream);
+
+/* Workspace bytes edb_gated_delta_net_bwd needs (a buffer of one chunk's 64
+ * states per (batch, head), plus the checkpoints when have_ckpt == 0). */
+size_t edb_gated_delta_net_bwd_workspace(int dtype, int beta_per_element, int batch,
+                                         int seq_len, int heads, int head_dim, int have_ckpt);
+
+/* Backward given dO: gq, gk, gv (shape of q), gbeta (shape of beta), galpha
+ * (shape of alpha), in `dtype`.  The key gradient is the exact one
+ * (-S_d^T (beta (.) dS k) through the retrieval); lib/edifice/cuda/
+ * fused_scan.ex:1405-1407 scales S_d^T dS k by beta over the key index, which
+ * agrees only for a per-token beta.  dalpha_t = <dS_t - (beta (.) dS_t k_t) k_t^T,
+ * S_{t-1}>.  Replaces fused_gated_delta_net_scan_backward_launch
+ * (native/cuda/fused_gated_delta_net_scan_backward.cu:348-394); Nx semantics
+ * lib/edifice/cuda/fused_scan.ex:1347-1431. */
+int edb_gated_delta_net_bwd(int dtype, const void* q, const void* k, const void* v,
+                            const void* beta, int beta_per_element, const void* alpha,
+                            const void* dO, const float* s_ckpt, void* gq, void* gk, void* gv,
+                            void* gbeta, void* galpha, int batch, int seq_len, int heads,
+                            int head_dim, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Capacity of the library's built-in scratch array used by
  * edb_selective_scan_bwd_noalloc (16 MiB; every GPU that loads the library
  * holds it until the process exits). */

@@ -82,6 +82,32 @@ int fused_delta_rule_scan_backward_launch(cudaStream_t stream, const edb_io_t* q
                                           const edb_io_t* grad_output, edb_io_t* output_concat,
                                           int batch, int seq_len, int num_heads, int head_dim);
 
+/* native/cuda/fused_delta_rule_scan.cu:247-258: GatedDeltaNet, q, k, v, beta,
+ * output [B, T, H, d] (beta per element), alpha [B, T, H]. */
+int fused_gated_delta_net_scan_launch(cudaStream_t stream, const edb_io_t* q,
+                                      const edb_io_t* k, const edb_io_t* v, const edb_io_t* beta,
+                                      const edb_io_t* alpha, edb_io_t* output, int batch,
+                                      int seq_len, int num_heads, int head_dim);
+
+/* native/cuda/fused_delta_rule_scan.cu:213-232: the delta rule, gated when
+ * alpha is not NULL. */
+int fused_delta_rule_scan_launch(cudaStream_t stream, const edb_io_t* q, const edb_io_t* k,
+                                 const edb_io_t* v, const edb_io_t* beta, const edb_io_t* alpha,
+                                 edb_io_t* output, int batch, int seq_len, int num_heads,
+                                 int head_dim);
+
+/* native/cuda/fused_gated_delta_net_scan_backward.cu:348-394;
+ * output_concat = [gq | gk | gv | gbeta | galpha]: four B*T*H*d blocks, then
+ * B*T*H io elements.  Scratch is taken stream-ordered (cudaMallocAsync /
+ * cudaFreeAsync). */
+int fused_gated_delta_net_scan_backward_launch(cudaStream_t stream, const edb_io_t* q,
+                                               const edb_io_t* k, const edb_io_t* v,
+                                               const edb_io_t* beta, const edb_io_t* alpha,
+                                               const edb_io_t* forward_out,
+                                               const edb_io_t* grad_output,
+                                               edb_io_t* output_concat, int batch, int seq_len,
+                                               int num_heads, int head_dim);
+
 /* native/cuda/fused_flash_attention.cu:168-191: q, k, v, output [B, H, T, d],
  * equal heads, scale 1/sqrt(d), causal 0/1. */
 int fused_flash_attention_launch(cudaStream_t stream, const edb_io_t* q, const edb_io_t* k,

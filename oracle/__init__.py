@@ -166,6 +166,29 @@ def delta_net_bwd(q, k, v, beta, dO, prec="f64"):
     return gq, gk, gv, gbeta
 
 
+# ------------------------------------------------------ gated delta rule
+def gated_delta_net_fwd(q, k, v, beta, alpha, prec="f64"):
+    q, k, v, beta, alpha = map(_f32, (q, k, v, beta, alpha))
+    B, L, H, d = q.shape
+    scalar = int(beta.ndim == 3)
+    o = np.empty_like(q)
+    _fn("gated_delta_net_fwd", prec)(_p(q), _p(k), _p(v), _p(beta), _p(alpha), _p(o), _I(B),
+                                     _I(L), _I(H), _I(d), _I(scalar))
+    return o
+
+
+def gated_delta_net_bwd(q, k, v, beta, alpha, dO, prec="f64"):
+    q, k, v, beta, alpha, dO = map(_f32, (q, k, v, beta, alpha, dO))
+    B, L, H, d = q.shape
+    scalar = int(beta.ndim == 3)
+    gq, gk, gv = np.empty_like(q), np.empty_like(q), np.empty_like(q)
+    gbeta, galpha = np.empty_like(beta), np.empty_like(alpha)
+    _fn("gated_delta_net_bwd", prec)(_p(q), _p(k), _p(v), _p(beta), _p(alpha), _p(dO), _p(gq),
+                                     _p(gk), _p(gv), _p(gbeta), _p(galpha), _I(B), _I(L), _I(H),
+                                     _I(d), _I(scalar))
+    return gq, gk, gv, gbeta, galpha
+
+
 # ------------------------------------------------------------- attention
 def attention_fwd(q, k, v, causal=True, prec="f64", want_lse=False):
     q, k, v = map(_f32, (q, k, v))

@@ -12,6 +12,7 @@
  *   scans            [B, L, H] row-major, channel fastest
  *   selective scan   x, dt [B, L, D]; A [D, N]; B, C [B, L, N]
  *   delta rule       q, k, v [B, L, H, d]; beta [B, L, H, d] or [B, L, H]
+ *   gated delta rule as the delta rule, plus alpha [B, L, H]
  *   attention        q [B, Hq, L, d]; k, v [B, Hkv, L, d]
  *
  * Each function cites the reference file:line it restates (paths relative to
@@ -422,6 +423,158 @@ void FN(delta_net_bwd)(const float* q, const float* k, const float* v, const flo
                 }
             }
         }
+        free(ck); free(Sc); free(dS); free(r); free(dsk);
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* GatedDeltaNet.  S_0 = 0; per token: S_d = alpha_t S; r = S_d k;            */
+/* S = S_d + (beta (.) (v - r)) k^T; o = S q.  fused_scan.ex:2256-2284        */
+/* (gated_delta_net_scan_fallback) == lib/edifice/recurrent/                  */
+/* gated_delta_net.ex:300-350.  alpha [B, L, H] (one decay per token and      */
+/* head); beta [B, L, H, d], or [B, L, H] when beta_scalar != 0.              */
+/* ------------------------------------------------------------------------ */
+void FN(gated_delta_net_fwd)(const float* q, const float* k, const float* v, const float* beta,
+                             const float* alpha, float* o, int B, int L, int H, int d,
+                             int beta_scalar) {
+    #pragma omp parallel for schedule(dynamic)
+    for (long bh = 0; bh < (long)B * H; bh++) {
+        int b = (int)(bh / H), hh = (int)(bh % H);
+        REAL* S = (REAL*)calloc((size_t)d * d, sizeof(REAL));
+        for (int t = 0; t < L; t++) {
+            size_t off = (((size_t)b * L + t) * H + hh) * d;
+            size_t boff = ((size_t)b * L + t) * H + hh;
+            REAL al = (REAL)alpha[boff];
+            for (int i = 0; i < d; i++) {
+                REAL r = 0;
+                for (int j = 0; j < d; j++) {
+                    S[(size_t)i * d + j] *= al;
+                    r += S[(size_t)i * d + j] * (REAL)k[off + j];
+                }
+                REAL be = (REAL)beta[beta_scalar ? boff : off + i];
+                REAL se = be * ((REAL)v[off + i] - r);
+                for (int j = 0; j < d; j++) S[(size_t)i * d + j] += se * (REAL)k[off + j];
+            }
+            for (int i = 0; i < d; i++) {
+                REAL acc = 0;
+                for (int j = 0; j < d; j++) acc += S[(size_t)i * d + j] * (REAL)q[off + j];
+                o[off + i] = (float)acc;
+            }
+        }
+        free(S);
+    }
+}
+
+/* Backward: fused_scan.ex:1347-1431 (gated_delta_net_backward_fallback):
+ *   dS += dO q^T; dq = S_t^T dO; dsk = dS k; dv = beta (.) dsk;
+ *   dbeta = err (.) dsk; dk = dS^T (beta (.) err) - S_d^T (beta (.) dsk);
+ *   dS_d = dS - (beta (.) dsk) k^T; dalpha = sum(dS_d (.) S_{t-1}); dS_prev = alpha dS_d,
+ * with S_d = alpha S_{t-1}.  The through-retrieval key gradient is the exact
+ * one, S_d^T (beta (.) dsk) (the fallback scales S_d^T dsk by beta over the key
+ * index, equal only when beta is the same for every row).  For scalar beta the
+ * per-row dbeta is summed over rows.  S_{t-1} is recomputed per chunk from
+ * stored chunk-boundary states. */
+void FN(gated_delta_net_bwd)(const float* q, const float* k, const float* v, const float* beta,
+                             const float* alpha, const float* dO, float* gq, float* gk,
+                             float* gv, float* gbeta, float* galpha, int B, int L, int H, int d,
+                             int beta_scalar) {
+    const int CH = 16;
+    int nck = (L + CH - 1) / CH;
+    #pragma omp parallel for schedule(dynamic)
+    for (long bh = 0; bh < (long)B * H; bh++) {
+        int b = (int)(bh / H), hh = (int)(bh % H);
+        size_t dd = (size_t)d * d;
+        REAL* ck = (REAL*)calloc((size_t)nck * dd, sizeof(REAL));
+        REAL* Sc = (REAL*)calloc((size_t)(CH + 1) * dd, sizeof(REAL));
+        REAL* dS = (REAL*)calloc(dd, sizeof(REAL));
+        REAL* r = (REAL*)malloc((size_t)d * sizeof(REAL));
+        REAL* dsk = (REAL*)malloc((size_t)d * sizeof(REAL));
+        /* one step S_prev -> S_next (S_next may alias nothing) */
+#define ORC_GATED_STEP(Sp, Sn, t)                                                       \
+        do {                                                                             \
+            size_t off_ = (((size_t)b * L + (t)) * H + hh) * d;                          \
+            size_t boff_ = ((size_t)b * L + (t)) * H + hh;                               \
+            REAL al_ = (REAL)alpha[boff_];                                               \
+            for (int i = 0; i < d; i++) {                                                \
+                REAL rr = 0;                                                             \
+                for (int j = 0; j < d; j++) rr += al_ * (Sp)[(size_t)i * d + j] * (REAL)k[off_ + j]; \
+                REAL be = (REAL)beta[beta_scalar ? boff_ : off_ + i];                    \
+                REAL se = be * ((REAL)v[off_ + i] - rr);                                 \
+                for (int j = 0; j < d; j++)                                              \
+                    (Sn)[(size_t)i * d + j] = al_ * (Sp)[(size_t)i * d + j] + se * (REAL)k[off_ + j]; \
+            }                                                                            \
+        } while (0)
+        REAL* S = Sc;
+        for (size_t i = 0; i < dd; i++) S[i] = 0;
+        for (int t = 0; t < L; t++) {
+            if (t % CH == 0) memcpy(ck + (size_t)(t / CH) * dd, S, dd * sizeof(REAL));
+            ORC_GATED_STEP(Sc, Sc + dd, t);
+            memcpy(Sc, Sc + dd, dd * sizeof(REAL));
+        }
+        for (int c = nck - 1; c >= 0; c--) {
+            int t0 = c * CH, t1 = t0 + CH < L ? t0 + CH : L;
+            memcpy(Sc, ck + (size_t)c * dd, dd * sizeof(REAL));
+            for (int t = t0; t < t1; t++) {
+                REAL* Sp = Sc + (size_t)(t - t0) * dd;
+                ORC_GATED_STEP(Sp, Sp + dd, t);
+            }
+            for (int t = t1 - 1; t >= t0; t--) {
+                REAL* Sp = Sc + (size_t)(t - t0) * dd;
+                REAL* Sn = Sp + dd;
+                size_t off = (((size_t)b * L + t) * H + hh) * d;
+                size_t boff = ((size_t)b * L + t) * H + hh;
+                REAL al = (REAL)alpha[boff];
+                for (int i = 0; i < d; i++) {
+                    REAL rr = 0;
+                    for (int j = 0; j < d; j++) rr += al * Sp[(size_t)i * d + j] * (REAL)k[off + j];
+                    r[i] = rr;
+                }
+                for (int i = 0; i < d; i++)
+                    for (int j = 0; j < d; j++)
+                        dS[(size_t)i * d + j] += (REAL)dO[off + i] * (REAL)q[off + j];
+                for (int j = 0; j < d; j++) {
+                    REAL acc = 0;
+                    for (int i = 0; i < d; i++) acc += Sn[(size_t)i * d + j] * (REAL)dO[off + i];
+                    gq[off + j] = (float)acc;
+                }
+                for (int i = 0; i < d; i++) {
+                    REAL acc = 0;
+                    for (int j = 0; j < d; j++) acc += dS[(size_t)i * d + j] * (REAL)k[off + j];
+                    dsk[i] = acc;
+                }
+                REAL gbs = 0;
+                for (int i = 0; i < d; i++) {
+                    REAL be = (REAL)beta[beta_scalar ? boff : off + i];
+                    REAL err = (REAL)v[off + i] - r[i];
+                    gv[off + i] = (float)(be * dsk[i]);
+                    if (beta_scalar) gbs += err * dsk[i];
+                    else gbeta[off + i] = (float)(err * dsk[i]);
+                }
+                if (beta_scalar) gbeta[boff] = (float)gbs;
+                for (int j = 0; j < d; j++) {
+                    REAL a1 = 0, a2 = 0;
+                    for (int i = 0; i < d; i++) {
+                        REAL be = (REAL)beta[beta_scalar ? boff : off + i];
+                        REAL err = (REAL)v[off + i] - r[i];
+                        a1 += dS[(size_t)i * d + j] * be * err;
+                        a2 += al * Sp[(size_t)i * d + j] * be * dsk[i];
+                    }
+                    gk[off + j] = (float)(a1 - a2);
+                }
+                /* dS_d = dS - (beta dsk) k^T; dalpha = <dS_d, S_{t-1}>; dS_prev = alpha dS_d */
+                REAL ga = 0;
+                for (int i = 0; i < d; i++) {
+                    REAL be = (REAL)beta[beta_scalar ? boff : off + i];
+                    for (int j = 0; j < d; j++) {
+                        REAL x = dS[(size_t)i * d + j] - be * dsk[i] * (REAL)k[off + j];
+                        ga += x * Sp[(size_t)i * d + j];
+                        dS[(size_t)i * d + j] = al * x;
+                    }
+                }
+                galpha[boff] = (float)ga;
+            }
+        }
+#undef ORC_GATED_STEP
         free(ck); free(Sc); free(dS); free(r); free(dsk);
     }
 }

@@ -71,3 +71,13 @@ def test_host_validation_rejects_bad_arguments():
     assert lib.edb_mingru_bwd(0, dummy, dummy, None, dummy, None, dummy, dummy, None, 1, 4, 4,
                               None) == 1000
     assert lib.edb_mingru_fwd(0, dummy, dummy, None, dummy, 2, -1, 4, None) == 1001
+    # GatedDeltaNet: alpha is required; a too-small workspace is refused
+    assert lib.edb_gated_delta_net_fwd(0, dummy, dummy, dummy, dummy, 1, None, dummy, None, 1,
+                                       4, 2, 8, None) == 1000
+    assert lib.edb_gated_delta_net_fwd(0, dummy, dummy, dummy, dummy, 1, dummy, dummy, None, 1,
+                                       4, 2, 256, None) != 0
+    need = lib.edb_gated_delta_net_bwd_workspace(0, 1, 1, 4, 2, 8, 0)
+    assert need > 0
+    assert lib.edb_gated_delta_net_bwd(0, dummy, dummy, dummy, dummy, 1, dummy, dummy, None,
+                                       dummy, dummy, dummy, dummy, dummy, 1, 4, 2, 8, dummy,
+                                       need - 1, None) == 1004

@@ -181,6 +181,48 @@ def test_delta_net_bwd_autograd(scalar_beta):
         np.testing.assert_allclose(x, t_.grad.numpy(), rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("scalar_beta", [False, True])
+def test_gated_delta_net_bwd_autograd(scalar_beta):
+    """GatedDeltaNet: the forward restates gated_delta_net_scan_fallback
+    (fused_scan.ex:2256-2284); the backward is checked against autograd of that
+    forward, the reference's own test strategy for it
+    (test/edifice/cuda/backward_kernels_test.exs:1003-1060), at alpha in [0.8, 0.99]
+    as there and at alpha in [0.05, 1) (decays a division-based backward could
+    not undo)."""
+    rng = np.random.default_rng(7)
+    Bsz, L, H, d = 2, 37, 2, 8
+    for lo in (0.8, 0.05):
+        q, k, v = (rng.standard_normal((Bsz, L, H, d)).astype(np.float32) for _ in range(3))
+        k /= np.sqrt((k * k).sum(-1, keepdims=True) + 1e-6)
+        beta = rng.uniform(0.1, 0.9, (Bsz, L, H) if scalar_beta else (Bsz, L, H, d)).astype(
+            np.float32)
+        alpha = rng.uniform(lo, 0.99, (Bsz, L, H)).astype(np.float32)
+        do = rng.standard_normal((Bsz, L, H, d)).astype(np.float32)
+        tq, tk, tv, tb, ta = _t(q), _t(k), _t(v), _t(beta), _t(alpha)
+        bb = tb[..., None] if scalar_beta else tb
+        S = torch.zeros(Bsz, H, d, d, dtype=torch.float64)
+        outs = []
+        for t in range(L):
+            Sd = ta[:, t, :, None, None] * S
+            r = torch.einsum("bhij,bhj->bhi", Sd, tk[:, t])
+            S = Sd + torch.einsum("bhi,bhj->bhij", bb[:, t] * (tv[:, t] - r), tk[:, t])
+            outs.append(torch.einsum("bhij,bhj->bhi", S, tq[:, t]))
+        o = torch.stack(outs, 1)
+        np.testing.assert_allclose(O.gated_delta_net_fwd(q, k, v, beta, alpha),
+                                   o.detach().numpy(), rtol=1e-5, atol=1e-6)
+        o.backward(torch.tensor(do, dtype=torch.float64))
+        got = O.gated_delta_net_bwd(q, k, v, beta, alpha, do)
+        for x, t_ in zip(got, (tq, tk, tv, tb, ta)):
+            np.testing.assert_allclose(x, t_.grad.numpy(), rtol=1e-5, atol=1e-5)
+        # alpha == 1 is the plain delta rule
+        one = np.ones_like(alpha)
+        np.testing.assert_allclose(O.gated_delta_net_fwd(q, k, v, beta, one),
+                                   O.delta_net_fwd(q, k, v, beta), rtol=1e-6, atol=1e-6)
+        g1 = O.gated_delta_net_bwd(q, k, v, beta, one, do)
+        for x, y in zip(g1[:4], O.delta_net_bwd(q, k, v, beta, do)):
+            np.testing.assert_allclose(x, y, rtol=1e-6, atol=1e-6)
+
+
 @pytest.mark.parametrize("causal,hq,hkv", [(True, 4, 2), (False, 4, 4), (True, 8, 2)])
 def test_attention_bwd_autograd(causal, hq, hkv):
     rng = np.random.default_rng(6)
