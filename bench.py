@@ -2,7 +2,7 @@
 """Benchmark of the fused sequence-mixing hot path on B200 (one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config linear|mingru|ssm|attn] [--no-paths]
+                    [--config linear|mingru|ssm|attn|delta|gated] [--no-paths]
 
 Headline (default --config linear): BASELINE configs[1] -- the diagonal
 linear-RNN scan h_t = a_t h_{t-1} + b_t, forward + backward, bf16 io / f32
@@ -45,7 +45,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["linear", "mingru", "ssm", "attn", "delta"],
+    ap.add_argument("--config", choices=["linear", "mingru", "ssm", "attn", "delta", "gated"],
                     default="linear")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -499,8 +499,91 @@ class DeltaWorkload:
                 "pair over 512 tokens, scaled by the head share")
 
 
+class GatedDeltaWorkload(DeltaWorkload):
+    """GatedDeltaNet (delta rule with a per-token decay alpha) fwd + bwd at the
+    configs[2] shapes and distributions, alpha = mean of sigmoid(N(0,1)) gates over
+    head_dim (the model's form).  Token recurrence (SIMT, one CTA per (b, h))."""
+
+    def __init__(self):
+        import dataclasses
+        super().__init__()
+        self.cfg = dataclasses.replace(self.cfg, name="gated_delta_net_cfg2")
+        self.kname = "gated_delta_net"
+
+    def describe(self, world):
+        d = super().describe(world)
+        d["workload"] = "%s fwd+bwd (configs[2] shapes, alpha = mean of sigmoid gates)" % (
+            self.cfg.name)
+        d["alpha"] = "one per (token, head)"
+        return d
+
+    def setup(self, dev, rank):
+        from edifice_b200 import shard
+        super().setup(dev, rank)
+        self.alpha = shard.gated_alpha(self.cfg, self.units, dev)
+
+    def kernels(self):
+        # serial token recurrence: against HBM with the algorithmic io bytes
+        a = self.alpha.numel() * self.alpha.element_size()
+        return {"fwd": ("hbm", self.cfg.bytes_fwd() + a),
+                "bwd": ("hbm", self.cfg.bytes_bwd() + 2 * a)}
+
+    launches_per_step = 2  # forward (writes the checkpoints), backward
+
+    def step(self, ev=None):
+        from edifice_b200 import fused_scan as fs
+        if ev:
+            ev[0].record()
+        _, ck = fs.gated_delta_net_scan(self.q, self.k, self.v, self.beta, self.alpha,
+                                        with_ckpt=True)
+        if ev:
+            ev[1].record()
+        fs.gated_delta_net_backward(self.q, self.k, self.v, self.beta, self.alpha, self.do, ck)
+        if ev:
+            ev[2].record()
+
+    def host_inputs(self):
+        return [self.q, self.k, self.v, self.beta, self.alpha, self.do]
+
+    def e2e_step(self, dev_in):
+        from edifice_b200 import fused_scan as fs
+        q, k, v, beta, alpha, do = dev_in
+        o, ck = fs.gated_delta_net_scan(q, k, v, beta, alpha, with_ckpt=True)
+        return (o,) + tuple(fs.gated_delta_net_backward(q, k, v, beta, alpha, do, ck))
+
+    api = "edifice_b200.fused_scan.gated_delta_net_scan + gated_delta_net_backward"
+
+    def extra(self, fwd_ms, bwd_ms):
+        return {}
+
+    def cpu_step(self, rows=None, prec="f32"):
+        import numpy as np
+        import oracle as O
+        c = self.cfg
+        Ls = 256
+        if not hasattr(self, "_cpu"):
+            rng = np.random.default_rng(0)
+            q = rng.standard_normal((1, Ls, 1, c.head_dim), dtype=np.float32)
+            k = rng.standard_normal((1, Ls, 1, c.head_dim), dtype=np.float32)
+            k /= np.sqrt((k * k).sum(-1, keepdims=True) + 1e-6)
+            v = rng.standard_normal((1, Ls, 1, c.head_dim), dtype=np.float32)
+            beta = (1 / (1 + np.exp(-rng.standard_normal((1, Ls, 1))))).astype(np.float32)
+            alpha = (1 / (1 + np.exp(-rng.standard_normal((1, Ls, 1, c.head_dim))))).mean(
+                -1).astype(np.float32)
+            do = rng.standard_normal((1, Ls, 1, c.head_dim), dtype=np.float32)
+            self._cpu = (q, k, v, beta, alpha, do)
+        q, k, v, beta, alpha, do = self._cpu
+        O.gated_delta_net_fwd(q, k, v, beta, alpha, prec=prec)
+        O.gated_delta_net_bwd(q, k, v, beta, alpha, do, prec=prec)
+        return Ls / c.heads
+
+    cpu_what = ("oracle f32 port (fused_scan.ex:2256-2284, 1347-1431) on one (batch, head) "
+                "pair over 256 tokens, scaled by the head share")
+
+
 WORKLOADS = {"linear": lambda: ScanWorkload(False), "mingru": lambda: ScanWorkload(True),
-             "ssm": SsmWorkload, "attn": AttnWorkload, "delta": DeltaWorkload}
+             "ssm": SsmWorkload, "attn": AttnWorkload, "delta": DeltaWorkload,
+             "gated": GatedDeltaWorkload}
 
 
 def roofline(wl, kern_ms):
@@ -639,7 +722,7 @@ def run_ours(args):
     if args.config == "linear" and not args.no_paths:
         del wl.a, wl.b, wl.dy
         torch.cuda.empty_cache()
-        for name in ("mingru", "attn", "delta", "ssm"):
+        for name in ("mingru", "attn", "delta", "gated", "ssm"):
             pw = WORKLOADS[name]()
             pw._world = world
             pw.setup(dev, rank)

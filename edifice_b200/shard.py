@@ -253,6 +253,23 @@ def delta_inputs(cfg, units, device, base_seed=0):
     return q, k, v, beta, do
 
 
+def gated_alpha(cfg, units, device, base_seed=0):
+    """The decay of GatedDeltaNet per (batch, head) unit, alpha [len(units)/heads, L,
+    heads]: the mean over head_dim of sigmoid(N(0,1)) gates, the model's form
+    (lib/edifice/recurrent/gated_delta_net.ex:382-389), drawn after that unit's
+    delta_inputs stream (a separate generator offset, so the q/k/v/beta/dO draws
+    are the configs[2] ones)."""
+    L, H, d = cfg.seq_len, cfg.heads, cfg.head_dim
+    nb = len(units) // H
+    alpha = torch.empty((nb, L, H), dtype=cfg.dtype, device=device)
+    for i, u in enumerate(units):
+        b, h = divmod(i, H)
+        g = torch.Generator(device=device).manual_seed(unit_seed(base_seed + 1, u))
+        gates = torch.sigmoid(torch.randn((L, d), generator=g, device=device))
+        alpha[b, :, h].copy_(gates.mean(-1))
+    return alpha
+
+
 def ceil_div(a, b):
     return -(-a // b)
 

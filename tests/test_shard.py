@@ -92,3 +92,13 @@ def test_two_rank_gloo_plan_and_max_time(tmp_path):
         sl = slice(r * cfg.batch, (r + 1) * cfg.batch)
         assert torch.allclose(res["sums"][r],
                               torch.tensor([a[sl].double().sum(), b[sl].double().sum()]))
+
+
+def test_gated_alpha_per_unit():
+    """GatedDeltaNet decays: in (0, 1), identical for a unit wherever it lands."""
+    cfg = shard.DeltaConfig(batch=2, heads=2, seq_len=16, head_dim=8, dtype=torch.float32)
+    a_all = shard.gated_alpha(cfg, [0, 1, 2, 3], torch.device("cpu"))
+    a_hi = shard.gated_alpha(cfg, [2, 3], torch.device("cpu"))
+    assert a_all.shape == (2, 16, 2)
+    assert torch.equal(a_all[1], a_hi[0])
+    assert float(a_all.min()) > 0.0 and float(a_all.max()) < 1.0
