@@ -42,63 +42,138 @@ static __device__ __forceinline__ float ldv(const T* p) {
     return ld_scalar<T>(p);
 }
 
-// shared layout: S [d][d+1] | q k v beta o-scratch [5][DMAX] (| dS [d][d+1] | r [CK][d] | vec [4][DMAX])
-template <typename T>
-__global__ void __launch_bounds__(kThreads)
-    delta_fwd_rec_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-                         const T* __restrict__ beta, const T* __restrict__ alpha,
-                         T* __restrict__ o, float* __restrict__ ckpt, int L, int H, int d,
-                         int beta_scalar) {
-    extern __shared__ float sm[];
-    const int sd = d + 1;
-    float* S = sm;
-    float* sq = S + d * sd;
-    float* sk = sq + d;
-    float* su = sk + d;  // beta (.) (v - r)
-    const int h = blockIdx.x, b = blockIdx.y;
-    const int tid = threadIdx.x;
-    const int nck = (L + CK - 1) / CK;
-    for (int i = tid; i < d * sd; i += kThreads) S[i] = 0.0f;
-    __syncthreads();
+// Forward, row-parallel.  Each row i of S (value index) evolves on its own in
+// the forward: S[i] <- alpha S[i] + beta_i (v_i - alpha S[i].k) k^T,
+// o_i = S[i].q, so a row lives in the registers of 4 lanes (CPL columns each)
+// and no block barrier is needed per token; k, q and the CTA's rows of v,
+// beta (and alpha) are staged in shared memory one CK-token chunk at a time.
+// grid (H, B, ceil(d / 32)), 128 threads = 32 rows x 4 lanes.  Shared memory
+// (dynamic): k, q [CK][4][CPL + 4] (a pad of 4 floats per lane's slice puts
+// the 4 slices of one token on different banks) | v, beta, o [CK][32] | alpha [CK].
+constexpr int kRowThreads = 128, kRowsPerCta = 32;
+
+template <int CPL>
+constexpr size_t fwd_rows_smem() {
+    return ((size_t)2 * CK * 4 * (CPL + 4) + 3 * CK * kRowsPerCta + CK) * sizeof(float);
+}
+
+template <typename T, int CPL, bool GATED>
+__global__ void __launch_bounds__(kRowThreads)
+    delta_fwd_rows_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                          const T* __restrict__ v, const T* __restrict__ beta,
+                          const T* __restrict__ alpha, T* __restrict__ o,
+                          float* __restrict__ ckpt, int L, int H, int d, int beta_scalar) {
+    constexpr int SP = CPL + 4;  // floats per lane slice (padded)
+    constexpr int RP = 4 * SP;   // floats per staged token row
+    extern __shared__ __align__(16) float smf[];
+    float* sk = smf;                        // [CK][RP]
+    float* sq = sk + CK * RP;               // [CK][RP]
+    float* sv = sq + CK * RP;               // [CK][32]
+    float* sb = sv + CK * kRowsPerCta;      // [CK][32]
+    float* so = sb + CK * kRowsPerCta;      // [CK][32]
+    float* sa = so + CK * kRowsPerCta;      // [CK]
+    const int h = blockIdx.x, b = blockIdx.y, rb = blockIdx.z * kRowsPerCta;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int rl = warp * 8 + (lane >> 2);  // local row
+    const int i = rb + rl;                  // value-dim row of S
+    const int part = lane & 3;              // column slice [part CPL, part CPL + CPL)
+    const int c0 = part * CPL;
+    const bool row_ok = i < d;
     const long long rs = (long long)H * d;  // token stride
     const long long base = (long long)b * L * rs + (long long)h * d;
-    for (int t = 0; t < L; ++t) {
-        const long long off = base + (long long)t * rs;
-        if (ckpt != nullptr && t % CK == 0) {
-            float* cp = ckpt + (((long long)b * H + h) * (nck + 1) + t / CK) * d * d;
-            for (int i = tid; i < d * d; i += kThreads) cp[i] = S[(i / d) * sd + i % d];
-        }
-        for (int i = tid; i < d; i += kThreads) {
-            sq[i] = ldv(q + off + i);
-            sk[i] = ldv(k + off + i);
-        }
-        __syncthreads();
-        // gated form: S_d = alpha S, so r = alpha (S k) and S_t = alpha S + u k^T
-        const float al = alpha != nullptr ? ldv(alpha + ((long long)b * L + t) * H + h) : 1.0f;
-        for (int i = tid; i < d; i += kThreads) {
-            float r = 0.0f;
-            for (int j = 0; j < d; ++j) r = fmaf(S[i * sd + j], sk[j], r);
-            const float be = beta_scalar ? ldv(beta + ((long long)b * L + t) * H + h)
-                                         : ldv(beta + off + i);
-            su[i] = be * (ldv(v + off + i) - al * r);
-        }
-        __syncthreads();
-        for (int i = tid; i < d; i += kThreads) {
-            const float u = su[i];
-            float acc = 0.0f;
-            for (int j = 0; j < d; ++j) {
-                const float s = fmaf(u, sk[j], al * S[i * sd + j]);
-                S[i * sd + j] = s;
-                acc = fmaf(s, sq[j], acc);
+    const int nck = (L + CK - 1) / CK;
+    float* ck_row = ckpt != nullptr && row_ok
+                        ? ckpt + ((long long)b * H + h) * (nck + 1) * d * d + (long long)i * d
+                        : nullptr;
+    float S[CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) S[c] = 0.0f;
+    auto save_state = [&](int slot) {
+        if (ck_row == nullptr) return;
+        float* dst = ck_row + (long long)slot * d * d;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c)
+            if (c0 + c < d) dst[c0 + c] = S[c];
+    };
+
+    for (int t0 = 0; t0 < L; t0 += CK) {
+        const int tn = min(CK, L - t0);
+        save_state(t0 / CK);
+        __syncthreads();  // the previous chunk's stage is consumed
+        // ---- stage this chunk (loads batched per thread before the stores)
+        for (int base_idx = 0; base_idx < CK * 4 * CPL; base_idx += kRowThreads * 8) {
+            float fk[8], fq[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int idx = base_idx + tid + u * kRowThreads;
+                const int tt = idx / (4 * CPL), c = idx % (4 * CPL);
+                const bool ok = tt < tn && c < d;
+                const long long off = base + (long long)(t0 + tt) * rs + c;
+                fk[u] = ok ? ldv(k + off) : 0.0f;
+                fq[u] = ok ? ldv(q + off) : 0.0f;
             }
-            st_scalar<T>(o + off + i, acc);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int idx = base_idx + tid + u * kRowThreads;
+                const int tt = idx / (4 * CPL), c = idx % (4 * CPL);
+                if (tt < CK) {
+                    const int so_ = tt * RP + (c / CPL) * SP + c % CPL;
+                    sk[so_] = fk[u];
+                    sq[so_] = fq[u];
+                }
+            }
+        }
+        for (int idx = tid; idx < CK * kRowsPerCta; idx += kRowThreads) {
+            const int tt = idx / kRowsPerCta, r = idx % kRowsPerCta;
+            const bool ok = tt < tn && rb + r < d;
+            const long long off = base + (long long)(t0 + tt) * rs + rb + r;
+            sv[idx] = ok ? ldv(v + off) : 0.0f;
+            sb[idx] = !ok ? 0.0f
+                          : beta_scalar ? ldv(beta + ((long long)b * L + t0 + tt) * H + h)
+                                        : ldv(beta + off);
+        }
+        if (GATED)
+            for (int tt = tid; tt < CK; tt += kRowThreads)
+                sa[tt] = tt < tn ? ldv(alpha + ((long long)b * L + t0 + tt) * H + h) : 1.0f;
+        __syncthreads();
+        // ---- the chunk's tokens, row by row in registers
+        for (int tt = 0; tt < tn; ++tt) {
+            const float* kr = sk + tt * RP + part * SP;
+            const float* qr = sq + tt * RP + part * SP;
+            float r = 0.0f;
+#pragma unroll
+            for (int c = 0; c < CPL; c += 4) {
+                const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
+                r = fmaf(S[c], k4.x, fmaf(S[c + 1], k4.y, fmaf(S[c + 2], k4.z, fmaf(S[c + 3], k4.w, r))));
+            }
+            r += __shfl_xor_sync(0xffffffffu, r, 1);
+            r += __shfl_xor_sync(0xffffffffu, r, 2);
+            const float al = GATED ? sa[tt] : 1.0f;
+            const float u = sb[tt * kRowsPerCta + rl] * (sv[tt * kRowsPerCta + rl] - al * r);
+            float ov = 0.0f;
+#pragma unroll
+            for (int c = 0; c < CPL; c += 4) {
+                const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
+                const float4 q4 = *reinterpret_cast<const float4*>(qr + c);
+                const float kv[4] = {k4.x, k4.y, k4.z, k4.w}, qv[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float sn = fmaf(u, kv[e], GATED ? al * S[c + e] : S[c + e]);
+                    S[c + e] = sn;
+                    ov = fmaf(sn, qv[e], ov);
+                }
+            }
+            ov += __shfl_xor_sync(0xffffffffu, ov, 1);
+            ov += __shfl_xor_sync(0xffffffffu, ov, 2);
+            if (part == 0) so[tt * kRowsPerCta + rl] = ov;
         }
         __syncthreads();
+        for (int idx = tid; idx < tn * kRowsPerCta; idx += kRowThreads) {
+            const int tt = idx / kRowsPerCta, r = idx % kRowsPerCta;
+            if (rb + r < d) st_scalar<T>(o + base + (long long)(t0 + tt) * rs + rb + r, so[idx]);
+        }
     }
-    if (ckpt != nullptr) {
-        float* cp = ckpt + (((long long)b * H + h) * (nck + 1) + nck) * d * d;
-        for (int i = tid; i < d * d; i += kThreads) cp[i] = S[(i / d) * sd + i % d];
-    }
+    save_state(nck);
 }
 
 template <typename T>
@@ -370,7 +445,6 @@ size_t ckpt_bytes(int B, int L, int H, int d) {
     return (size_t)B * H * (nck + 1) * d * d * sizeof(float);
 }
 
-size_t fwd_smem(int d) { return ((size_t)d * (d + 1) + 3 * d) * sizeof(float); }
 size_t gated_bwd_smem(int d) {
     return ((size_t)3 * d * (d + 1) + 6 * d + kThreads) * sizeof(float);
 }
@@ -381,18 +455,36 @@ size_t bwd_smem(int d) {
     return ((size_t)2 * d * (d + 1) + (size_t)CK * d + 5 * d + kThreads) * sizeof(float);
 }
 
+template <typename T, int CPL, bool GATED>
+int launch_fwd_rows(const void* q, const void* k, const void* v, const void* beta,
+                    const void* alpha, void* o, float* ckpt, int B, int L, int H, int d,
+                    int beta_scalar, cudaStream_t st) {
+    constexpr size_t smem = fwd_rows_smem<CPL>();
+    cudaError_t e = cudaFuncSetAttribute(delta_fwd_rows_kernel<T, CPL, GATED>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    delta_fwd_rows_kernel<T, CPL, GATED>
+        <<<dim3(H, B, (d + kRowsPerCta - 1) / kRowsPerCta), kRowThreads, smem, st>>>(
+            (const T*)q, (const T*)k, (const T*)v, (const T*)beta, (const T*)alpha, (T*)o, ckpt,
+            L, H, d, beta_scalar);
+    return edb::status_from_cuda(cudaGetLastError());
+}
+
 template <typename T>
 int launch_fwd(const void* q, const void* k, const void* v, const void* beta, const void* alpha,
                void* o, float* ckpt, int B, int L, int H, int d, int beta_scalar,
                cudaStream_t st) {
-    const size_t smem = fwd_smem(d);
-    cudaError_t e = cudaFuncSetAttribute(delta_fwd_rec_kernel<T>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return (int)e;
-    delta_fwd_rec_kernel<T><<<dim3(H, B), kThreads, smem, st>>>(
-        (const T*)q, (const T*)k, (const T*)v, (const T*)beta, (const T*)alpha, (T*)o, ckpt, L,
-        H, d, beta_scalar);
-    return edb::status_from_cuda(cudaGetLastError());
+    if (d <= 32)
+        return alpha != nullptr
+                   ? launch_fwd_rows<T, 8, true>(q, k, v, beta, alpha, o, ckpt, B, L, H, d,
+                                                 beta_scalar, st)
+                   : launch_fwd_rows<T, 8, false>(q, k, v, beta, alpha, o, ckpt, B, L, H, d,
+                                                  beta_scalar, st);
+    return alpha != nullptr
+               ? launch_fwd_rows<T, 32, true>(q, k, v, beta, alpha, o, ckpt, B, L, H, d,
+                                              beta_scalar, st)
+               : launch_fwd_rows<T, 32, false>(q, k, v, beta, alpha, o, ckpt, B, L, H, d,
+                                               beta_scalar, st);
 }
 
 template <typename T>
