@@ -1,0 +1,186 @@
+// host_pipeline.cu -- forward + backward of the diagonal scans (linear scan,
+// MinGRU) over HOST-resident tensors: batch rows are streamed through a small
+// ring of device slots so that the host->device copies of chunk i+1, the scan
+// kernels of chunk i and the device->host copies of chunk i-1 run at the same
+// time (the two copy directions use separate copy engines; PCIe is full duplex).
+//
+// The scans are independent per batch row, so a chunk of rows is a complete
+// sub-problem and the results equal those of one whole-batch call.  Ordering:
+// the helper streams first wait for everything already queued on the caller's
+// stream, and the caller's stream finally waits for the last copy, so the call
+// behaves like any other stream-ordered entry point.
+#include <cstdint>
+
+#include "edb_common.cuh"
+
+namespace {
+
+constexpr int kSlots = 3;  // device slots in the ring
+constexpr size_t kChunkTarget = 16u << 20;  // aim for ~16 MiB per tensor per chunk
+
+enum { HOST_LINEAR = 0, HOST_MINGRU = 1 };
+
+size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+int chunk_rows(int B, int L, int H, int esize) {
+    const size_t row = (size_t)L * H * esize;
+    size_t r = row >= kChunkTarget ? 1 : kChunkTarget / row;
+    // keep at least ~4 chunks in flight when the batch allows it
+    const size_t quarter = ((size_t)B + 3) / 4;
+    if (r > quarter) r = quarter;
+    if (r < 1) r = 1;
+    return (int)r;
+}
+
+// One slot: x0, x1, dy, h, g0, g1 ([rows, L, H]) then h0, gh0 ([rows, H]).
+size_t slot_bytes(int rows, int L, int H, int esize) {
+    const size_t t = a256((size_t)rows * L * H * esize);
+    const size_t s = a256((size_t)rows * H * esize);
+    return 6 * t + 2 * s;
+}
+
+int check_shape(int dtype, int B, int L, int H) {
+    if (dtype != EDB_F32 && dtype != EDB_BF16) return EDB_ERR_BAD_DTYPE;
+    if (B <= 0 || L <= 0 || H <= 0) return EDB_ERR_BAD_SHAPE;
+    if ((long long)B * L > 0x7fffffffLL) return EDB_ERR_BAD_SHAPE;
+    return EDB_OK;
+}
+
+struct Res {
+    cudaStream_t sin = nullptr, sout = nullptr;
+    cudaEvent_t start = nullptr, done = nullptr;
+    cudaEvent_t in[kSlots] = {}, comp[kSlots] = {}, free_[kSlots] = {};
+    ~Res() {
+        // destruction is deferred by the runtime until queued work completes
+        if (sin) cudaStreamDestroy(sin);
+        if (sout) cudaStreamDestroy(sout);
+        for (cudaEvent_t e : {start, done})
+            if (e) cudaEventDestroy(e);
+        for (int i = 0; i < kSlots; ++i)
+            for (cudaEvent_t e : {in[i], comp[i], free_[i]})
+                if (e) cudaEventDestroy(e);
+    }
+    cudaError_t init() {
+        cudaError_t e;
+        if ((e = cudaStreamCreateWithFlags(&sin, cudaStreamNonBlocking))) return e;
+        if ((e = cudaStreamCreateWithFlags(&sout, cudaStreamNonBlocking))) return e;
+        if ((e = cudaEventCreateWithFlags(&start, cudaEventDisableTiming))) return e;
+        if ((e = cudaEventCreateWithFlags(&done, cudaEventDisableTiming))) return e;
+        for (int i = 0; i < kSlots; ++i) {
+            if ((e = cudaEventCreateWithFlags(&in[i], cudaEventDisableTiming))) return e;
+            if ((e = cudaEventCreateWithFlags(&comp[i], cudaEventDisableTiming))) return e;
+            if ((e = cudaEventCreateWithFlags(&free_[i], cudaEventDisableTiming))) return e;
+        }
+        return cudaSuccess;
+    }
+};
+
+#define EDB_TRY(expr)                                   \
+    do {                                                \
+        cudaError_t e_ = (expr);                        \
+        if (e_ != cudaSuccess) return edb::status_from_cuda(e_); \
+    } while (0)
+#define EDB_TRY_ST(expr)            \
+    do {                            \
+        int st_ = (expr);           \
+        if (st_ != EDB_OK) return st_; \
+    } while (0)
+
+// x0/x1: (a, b) for the linear scan, (z, c) for MinGRU.  g0/g1 likewise.
+int run(int op, int dtype, const void* x0, const void* x1, const void* h0, const void* dy,
+        void* h, void* g0, void* g1, void* gh0, int B, int L, int H, void* ws, size_t ws_bytes,
+        void* stream) {
+    if (int st = check_shape(dtype, B, L, H)) return st;
+    if (!x0 || !x1 || !dy || !h || !g0 || !g1 || !ws) return EDB_ERR_NULL_POINTER;
+    const int es = dtype == EDB_BF16 ? 2 : 4;
+    const int rows = chunk_rows(B, L, H, es);
+    const size_t sb = slot_bytes(rows, L, H, es);
+    if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0) return EDB_ERR_MISALIGNED;
+    if (ws_bytes < kSlots * sb) return EDB_ERR_WORKSPACE_TOO_SMALL;
+    const size_t tb = a256((size_t)rows * L * H * es);
+    const size_t hb = a256((size_t)rows * H * es);
+
+    cudaStream_t s = (cudaStream_t)stream;
+    Res r;
+    EDB_TRY(r.init());
+    EDB_TRY(cudaEventRecord(r.start, s));
+    EDB_TRY(cudaStreamWaitEvent(r.sin, r.start, 0));
+    EDB_TRY(cudaStreamWaitEvent(r.sout, r.start, 0));
+
+    const int nchunks = (B + rows - 1) / rows;
+    for (int i = 0; i < nchunks; ++i) {
+        const int slot = i % kSlots;
+        const int r0 = i * rows, nr = B - r0 < rows ? B - r0 : rows;
+        char* base = static_cast<char*>(ws) + slot * sb;
+        void* dx0 = base;
+        void* dx1 = base + tb;
+        void* ddy = base + 2 * tb;
+        void* dh = base + 3 * tb;
+        void* dg0 = base + 4 * tb;
+        void* dg1 = base + 5 * tb;
+        void* dh0 = base + 6 * tb;
+        void* dgh0 = base + 6 * tb + hb;
+        const size_t off = (size_t)r0 * L * H * es, n = (size_t)nr * L * H * es;
+        const size_t off0 = (size_t)r0 * H * es, n0 = (size_t)nr * H * es;
+        auto hp = [](const void* p, size_t o) { return static_cast<const char*>(p) + o; };
+        auto hq = [](void* p, size_t o) { return static_cast<char*>(p) + o; };
+
+        // host -> device, once the slot's previous chunk has been copied out
+        if (i >= kSlots) EDB_TRY(cudaStreamWaitEvent(r.sin, r.free_[slot], 0));
+        EDB_TRY(cudaMemcpyAsync(dx0, hp(x0, off), n, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaMemcpyAsync(dx1, hp(x1, off), n, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaMemcpyAsync(ddy, hp(dy, off), n, cudaMemcpyHostToDevice, r.sin));
+        if (h0) EDB_TRY(cudaMemcpyAsync(dh0, hp(h0, off0), n0, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaEventRecord(r.in[slot], r.sin));
+
+        // forward + backward of the chunk on the caller's stream
+        EDB_TRY(cudaStreamWaitEvent(s, r.in[slot], 0));
+        const void* ph0 = h0 ? dh0 : nullptr;
+        void* pgh0 = gh0 ? dgh0 : nullptr;
+        if (op == HOST_LINEAR) {
+            EDB_TRY_ST(edb_linear_scan_fwd(dtype, dx0, dx1, ph0, dh, nr, L, H, s));
+            EDB_TRY_ST(edb_linear_scan_bwd(dtype, dx0, ph0, dh, ddy, dg0, dg1, pgh0, nr, L, H, s));
+        } else {
+            EDB_TRY_ST(edb_mingru_fwd(dtype, dx0, dx1, ph0, dh, nr, L, H, s));
+            EDB_TRY_ST(edb_mingru_bwd(dtype, dx0, dx1, ph0, dh, ddy, dg0, dg1, pgh0, nr, L, H, s));
+        }
+        EDB_TRY(cudaEventRecord(r.comp[slot], s));
+
+        // device -> host
+        EDB_TRY(cudaStreamWaitEvent(r.sout, r.comp[slot], 0));
+        EDB_TRY(cudaMemcpyAsync(hq(h, off), dh, n, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaMemcpyAsync(hq(g0, off), dg0, n, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaMemcpyAsync(hq(g1, off), dg1, n, cudaMemcpyDeviceToHost, r.sout));
+        if (gh0) EDB_TRY(cudaMemcpyAsync(hq(gh0, off0), dgh0, n0, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaEventRecord(r.free_[slot], r.sout));
+    }
+    // the caller's stream completes only after every result has reached the host
+    EDB_TRY(cudaEventRecord(r.done, r.sout));
+    EDB_TRY(cudaStreamWaitEvent(s, r.done, 0));
+    return EDB_OK;
+}
+
+}  // namespace
+
+extern "C" size_t edb_scan_train_host_workspace(int dtype, int batch, int seq_len, int hidden) {
+    if (check_shape(dtype, batch, seq_len, hidden) != EDB_OK) return 0;
+    const int es = dtype == EDB_BF16 ? 2 : 4;
+    return kSlots * slot_bytes(chunk_rows(batch, seq_len, hidden, es), seq_len, hidden, es);
+}
+
+extern "C" int edb_linear_scan_train_host(int dtype, const void* a, const void* b,
+                                          const void* h0, const void* dy, void* h, void* ga,
+                                          void* gb, void* gh0, int batch, int seq_len,
+                                          int hidden, void* workspace, size_t workspace_bytes,
+                                          void* stream) {
+    return run(HOST_LINEAR, dtype, a, b, h0, dy, h, ga, gb, gh0, batch, seq_len, hidden,
+               workspace, workspace_bytes, stream);
+}
+
+extern "C" int edb_mingru_train_host(int dtype, const void* z, const void* c, const void* h0,
+                                     const void* dy, void* h, void* gz, void* gc, void* gh0,
+                                     int batch, int seq_len, int hidden, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+    return run(HOST_MINGRU, dtype, z, c, h0, dy, h, gz, gc, gh0, batch, seq_len, hidden,
+               workspace, workspace_bytes, stream);
+}

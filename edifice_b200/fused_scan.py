@@ -142,6 +142,67 @@ class MinGRUFn(torch.autograd.Function):
         return gz * z * (1 - z), gc
 
 
+# --------------------------------------------- scans over host-resident tensors
+_HOST_WS = {}
+
+
+def _host_ws(device, nbytes):
+    """Device workspace for the host entry points, kept per device and grown on
+    demand (the caching allocator would hand back the same block anyway)."""
+    ws = _HOST_WS.get(device)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        _HOST_WS[device] = ws
+    return ws
+
+
+def _host_train(op, x0, x1, dy, h0, out, device, what):
+    for t in (x0, x1, dy, h0):
+        if t is not None and (t.is_cuda or not t.is_contiguous()):
+            raise _lib.EdbError("%s: inputs must be contiguous host tensors" % what)
+    _same(x0.shape, x1.shape, what)
+    _same(x0.shape, dy.shape, what)
+    B, L, H = x0.shape
+    if h0 is not None:
+        _same(h0.shape, (B, H), what)
+    if out is None:
+        out = tuple(torch.empty(x0.shape, dtype=x0.dtype, pin_memory=True) for _ in range(3)) + (
+            torch.empty((B, H), dtype=x0.dtype, pin_memory=True),)
+    for o in out:
+        if o is not None and (o.is_cuda or not o.is_contiguous() or o.dtype != x0.dtype):
+            raise _lib.EdbError("%s: outputs must be contiguous host tensors of the input dtype"
+                                % what)
+    device = torch.device(device if device is not None else "cuda")
+    dt_code = _dtype_code(x0, what)
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        nbytes = lib.edb_scan_train_host_workspace(dt_code, B, L, H)
+        ws = _host_ws(device, nbytes)
+        fn = lib.edb_linear_scan_train_host if op == "linear" else lib.edb_mingru_train_host
+        _lib.check(fn(dt_code, _p(x0), _p(x1), _p(h0), _p(dy), _p(out[0]), _p(out[1]),
+                      _p(out[2]), _p(out[3]), B, L, H, _p(ws), nbytes, _stream()),
+                   "CUDA %s over host tensors" % what)
+    return out
+
+
+def linear_scan_train_host(a_vals, b_vals, grad_output, h0=None, out=None, device=None):
+    """Forward and backward of the linear scan for host-resident tensors, copies
+    overlapped with the kernels batch-row chunk by chunk.  Returns host tensors
+    (h, grad_a, grad_b, grad_h0), written into ``out`` when given (four
+    contiguous host tensors; the last may be None).  Asynchronous on the current
+    stream of ``device``: synchronise it before reading the results.  Inputs and
+    outputs should be pinned for the copies to overlap."""
+    return _host_train("linear", a_vals, b_vals, grad_output, h0, out, device,
+                       "linear_scan_train_host")
+
+
+def mingru_train_host(z, candidates, grad_output, h0=None, out=None, device=None):
+    """As linear_scan_train_host for MinGRU on post-sigmoid z: returns
+    (h, grad_z, grad_cand, grad_h0) on the host."""
+    return _host_train("mingru", z, candidates, grad_output, h0, out, device,
+                       "mingru_train_host")
+
+
 # ---------------------------------------------------------------- selective scan
 DT_MIN, DT_MAX = 0.001, 0.1  # lib/edifice/ssm/common.ex:58-63
 

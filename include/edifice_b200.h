@@ -99,6 +99,34 @@ int edb_mingru_bwd(int dtype, const void* z, const void* c, const void* h0, cons
                    int hidden, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Forward + backward of the linear scan / MinGRU over HOST tensors.
+ * a, b (z, c), dy, and the outputs h, ga, gb (gz, gc): [batch, seq_len, hidden]
+ * in host memory; h0 / gh0: [batch, hidden] host or NULL (h0 = NULL: zeros;
+ * gh0 = NULL: not returned).  Batch rows stream through a ring of device slots
+ * in `workspace` (edb_scan_train_host_workspace() bytes, 256-byte aligned) so
+ * that host->device copies, the kernels above and device->host copies of
+ * successive row chunks overlap.  Host buffers should be page-locked
+ * (cudaHostAlloc / cudaHostRegister) for the copies to overlap.  Stream-ordered:
+ * the results are on the host once `stream` has reached this point.
+ * Results are those of edb_<op>_fwd followed by edb_<op>_bwd on the whole batch.
+ * Replaces the host-side round trip a caller with host-resident Nx tensors makes
+ * around fused_linear_scan_launch / fused_mingru_scan_launch (and their
+ * backward launches, native/cuda/fused_linear_scan{,_backward}.cu,
+ * fused_mingru_scan{,_backward}.cu); the reference has no single entry point
+ * for it.
+ * ---------------------------------------------------------------------- */
+size_t edb_scan_train_host_workspace(int dtype, int batch, int seq_len, int hidden);
+
+int edb_linear_scan_train_host(int dtype, const void* a, const void* b, const void* h0,
+                               const void* dy, void* h, void* ga, void* gb, void* gh0, int batch,
+                               int seq_len, int hidden, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
+int edb_mingru_train_host(int dtype, const void* z, const void* c, const void* h0, const void* dy,
+                          void* h, void* gz, void* gc, void* gh0, int batch, int seq_len,
+                          int hidden, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * Mamba selective scan, kernel semantics (given A, per-channel clamped dt):
  *   dtc = clip(dt, dt_min, dt_max);  h_n = exp(dtc A[d,n]) h_n + dtc B[b,t,n] x;
  *   y = sum_n C[b,t,n] h_n   (h_{-1} = 0).

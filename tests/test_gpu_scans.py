@@ -161,3 +161,51 @@ def test_rejects_cpu_tensors(cuda):
     a = torch.rand(1, 4, 8)
     with pytest.raises(RuntimeError):
         fs.linear_scan(a, a)
+
+
+HOST_SHAPES = [
+    (8, 300, 128),   # 4 chunks of 2 rows through 3 slots (slot reuse)
+    (9, 50, 45),     # odd hidden -> generic kernel; ragged last chunk
+    (1, 1000, 256),  # one row, one chunk
+    (2, 4096, 2048), # 16 MiB rows: one row per chunk
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape", HOST_SHAPES)
+@pytest.mark.parametrize("op", ["linear", "mingru"])
+def test_train_host_matches_device_path(cuda, dtype, shape, op):
+    """Forward + backward over pinned host tensors (copies overlapped with the
+    kernels chunk by chunk) equals the device entry points on the whole batch,
+    bit for bit (every kernel is independent per batch row), for two calls in a
+    row through the same workspace, and agrees with the oracle."""
+    a, b, dy, h0 = _inputs(shape, dtype, 21)
+    for use_h0 in (False, True):
+        hh0 = h0 if use_h0 else None
+        if op == "linear":
+            ref_h = fs.linear_scan(a, b, hh0)
+            ref = (ref_h,) + tuple(fs.linear_scan_backward(a, hh0, ref_h, dy))
+            fn = fs.linear_scan_train_host
+        else:
+            ref_h = fs.mingru_scan(a, b, hh0)
+            ref = (ref_h,) + tuple(fs.mingru_backward(a, b, hh0, ref_h, dy))
+            fn = fs.mingru_train_host
+        pin = [x.cpu().pin_memory() for x in (a, b, dy)]
+        ph0 = hh0.cpu().pin_memory() if use_h0 else None
+        for _ in range(2):
+            out = fn(pin[0], pin[1], pin[2], h0=ph0)
+            torch.cuda.synchronize()
+            for o, r in zip(out, ref):
+                assert torch.equal(o, r.cpu())
+    if op == "linear":
+        ref_o = O.linear_scan_fwd(_np(a), _np(b), _np(h0))
+    else:
+        ref_o = O.mingru_fwd(_np(a), _np(b), _np(h0))
+    assert O.norm_rel(out[0].float().numpy(), ref_o) <= TOL[dtype]
+    assert device_errors() == 0
+
+
+def test_train_host_rejects_device_tensors(cuda):
+    a = torch.rand(1, 4, 8, device="cuda")
+    with pytest.raises(RuntimeError):
+        fs.linear_scan_train_host(a, a, a)
