@@ -45,7 +45,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["linear", "mingru", "ssm", "attn", "delta", "gated"],
+    ap.add_argument("--config", choices=["linear", "mingru", "ssm", "ssm_model", "attn", "delta",
+                                         "gated"],
                     default="linear")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -353,6 +354,69 @@ class SsmWorkload:
                 "fused_scan.ex:1453-1531) on 1 batch row x 128 of 4096 channels, scaled")
 
 
+class SsmModelWorkload(SsmWorkload):
+    """configs[4] shapes and distributions through the model semantics of
+    Edifice.build(:mamba) (common.ex:402-470: B_bar from the channel-mean of the
+    clamped dt, fixed A = -(1..N)): fwd (dt mean + scan with checkpoints) + bwd."""
+
+    def __init__(self):
+        import dataclasses
+        super().__init__()
+        self.cfg = dataclasses.replace(self.cfg, name="selective_scan_model_cfg4")
+        self.kname = "selective_scan_model"
+
+    def describe(self, world):
+        d = super().describe(world)
+        d["workload"] = ("%s fwd+bwd (configs[4] shapes, Edifice.build(:mamba) semantics: "
+                         "B_bar = mean_d(dt) B, A = -(1..N))" % self.cfg.name)
+        return d
+
+    launches_per_step = 5  # dt mean, fwd, bwd, dB/dC reduce, gdt mean term
+
+    def step(self, ev=None):
+        from edifice_b200 import fused_scan as fs
+        if ev:
+            ev[0].record()
+        _, dtm, ck = fs.selective_scan_model(self.x, self.dt, self.B, self.C, with_ckpt=True)
+        if ev:
+            ev[1].record()
+        fs.selective_scan_model_backward(self.x, self.dt, self.B, self.C, self.dy, dtm, h_ckpt=ck)
+        if ev:
+            ev[2].record()
+
+    def host_inputs(self):
+        return [self.x, self.dt, self.B, self.C, self.dy]
+
+    def e2e_step(self, dev_in):
+        from edifice_b200 import fused_scan as fs
+        x, dt, B, C, dy = dev_in
+        y, dtm, ck = fs.selective_scan_model(x, dt, B, C, with_ckpt=True)
+        return (y,) + tuple(fs.selective_scan_model_backward(x, dt, B, C, dy, dtm, h_ckpt=ck))
+
+    api = "edifice_b200.fused_scan.selective_scan_model + backward"
+
+    def cpu_step(self, rows=None, prec="f32"):
+        import numpy as np
+        import oracle as O
+        c = self.cfg
+        ch, L, rows = 128, 1024, cpu_threads()  # the oracle runs one batch row per thread
+        if not hasattr(self, "_cpu_m"):
+            rng = np.random.default_rng(0)
+            x = rng.standard_normal((rows, L, ch), dtype=np.float32)
+            dt = np.log1p(np.exp(rng.standard_normal((rows, L, ch)) * 0.5 - 2)).astype(np.float32)
+            B = rng.standard_normal((rows, L, c.d_state), dtype=np.float32)
+            C = rng.standard_normal((rows, L, c.d_state), dtype=np.float32)
+            dy = rng.standard_normal((rows, L, ch), dtype=np.float32)
+            self._cpu_m = (x, dt, B, C, dy)
+        x, dt, B, C, dy = self._cpu_m
+        O.selective_scan_model_fwd(x, dt, B, C, prec=prec)
+        O.selective_scan_model_bwd(x, dt, B, C, dy, prec=prec)
+        return rows * L * ch / c.d_inner  # token-equivalents (128 of 4096 channels)
+
+    cpu_what = ("oracle f32 port (model semantics, common.ex:402-515 and its gradient) on "
+                "one batch row per thread x 1024 steps x 128 of 4096 channels, scaled")
+
+
 class AttnWorkload:
     """causal GQA attention fwd (with lse) + bwd."""
 
@@ -594,7 +658,8 @@ class GatedDeltaWorkload(DeltaWorkload):
 
 
 WORKLOADS = {"linear": lambda: ScanWorkload(False), "mingru": lambda: ScanWorkload(True),
-             "ssm": SsmWorkload, "attn": AttnWorkload, "delta": DeltaWorkload,
+             "ssm": SsmWorkload, "ssm_model": SsmModelWorkload, "attn": AttnWorkload,
+             "delta": DeltaWorkload,
              "gated": GatedDeltaWorkload}
 
 
@@ -740,7 +805,7 @@ def run_ours(args):
     if args.config == "linear" and not args.no_paths:
         del wl.a, wl.b, wl.dy
         torch.cuda.empty_cache()
-        for name in ("mingru", "attn", "delta", "gated", "ssm"):
+        for name in ("mingru", "attn", "delta", "gated", "ssm", "ssm_model"):
             pw = WORKLOADS[name]()
             pw._world = world
             pw.setup(dev, rank)

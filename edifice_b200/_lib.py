@@ -35,6 +35,10 @@ SIGNATURES = {
     "edb_selective_scan_bwd_workspace": (_sz, [_i, _i, _i, _i, _i]),
     "edb_selective_scan_bwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                     _i, _i, _i, _i, _f, _f, _vp, _sz, _vp]),
+    "edb_selective_scan_model_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i,
+                                          _i, _f, _f, _vp]),
+    "edb_selective_scan_model_bwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                          _vp, _vp, _i, _i, _i, _i, _f, _f, _vp, _sz, _vp]),
     "edb_selective_scan_bwd_noalloc": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                             _vp, _vp, _i, _i, _i, _i, _f, _f, _vp]),
     "edb_flash_attention_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f,

@@ -54,17 +54,27 @@ static __device__ __forceinline__ float ldf(const T* p) {
     return ld_scalar<T>(p);
 }
 
+// A[d, n]; in model mode a NULL A is the fixed diagonal -(n + 1) of
+// lib/edifice/ssm/common.ex:409 (discretize_ssm).
+template <bool MODEL, typename T>
+static __device__ __forceinline__ float a_at(const T* A, int d, int n, int N) {
+    if (MODEL && A == nullptr) return -(float)(n + 1);
+    return ldf(A + (long long)d * N + n);
+}
+
 // ------------------------------------------------------------------ forward
 // grid (ceil(D/128), B), block 128.  TB time steps of B/C per smem tile.
-template <typename T, int NS, bool STATES_ONLY>
+template <typename T, int NS, bool STATES_ONLY, bool MODEL>
 __global__ void __launch_bounds__(kThreads)
     ssm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ dt, const T* __restrict__ A,
                    const T* __restrict__ Bm, const T* __restrict__ Cm, T* __restrict__ y,
-                   float* __restrict__ ckpt, int L, int D, int N, float dt_min, float dt_max) {
+                   float* __restrict__ ckpt, const float* __restrict__ dtm, int L, int D, int N,
+                   float dt_min, float dt_max) {
     constexpr int TB = 32;
     constexpr int CK = SsmTiling<NS>::CK;
     __shared__ float sB[TB][NS];
     __shared__ float sC[TB][NS];
+    __shared__ float sDm[TB];  // model mode: channel-mean of the clamped dt per step
     const int tid = threadIdx.x;
     const int d = blockIdx.x * kThreads + tid;
     const int b = blockIdx.y;
@@ -74,7 +84,7 @@ __global__ void __launch_bounds__(kThreads)
     float A2[NS], h[NS];
 #pragma unroll
     for (int n = 0; n < NS; ++n) {
-        A2[n] = (live && n < N) ? ldf(A + (long long)d * N + n) * kLog2e : 0.0f;
+        A2[n] = (live && n < N) ? a_at<MODEL>(A, d, n, N) * kLog2e : 0.0f;
         h[n] = 0.0f;
     }
     const long long row0 = (long long)b * L;
@@ -88,6 +98,8 @@ __global__ void __launch_bounds__(kThreads)
             sB[tt][n] = ok ? ldf(Bm + o) : 0.0f;
             if (!STATES_ONLY) sC[tt][n] = ok ? ldf(Cm + o) : 0.0f;
         }
+        if (MODEL)
+            for (int i = tid; i < TB; i += kThreads) sDm[i] = i < tn ? dtm[row0 + t0 + i] : 0.0f;
         __syncthreads();
         if (!live) continue;
         for (int tt = 0; tt < tn; ++tt) {
@@ -100,7 +112,7 @@ __global__ void __launch_bounds__(kThreads)
             }
             const long long o = (row0 + t) * D + d;
             const float dtc = fminf(fmaxf(ldf(dt + o), dt_min), dt_max);
-            const float dtx = dtc * ldf(x + o);
+            const float dtx = (MODEL ? sDm[tt] : dtc) * ldf(x + o);
             float acc = 0.0f;
 #pragma unroll
             for (int n = 0; n < NS; ++n) {
@@ -148,20 +160,20 @@ static __device__ __forceinline__ int reduced_index(int lane) {
 
 // grid (ceil(D/128), B), block 128.
 // gpart: [2][nblk][B][L][NS] f32 partial sums over this CTA's 128 channels
-template <typename T, int NS>
+template <typename T, int NS, bool MODEL>
 __global__ void __launch_bounds__(kThreads)
     ssm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ dt, const T* __restrict__ A,
                    const T* __restrict__ Bm, const T* __restrict__ Cm, const T* __restrict__ dy,
-                   const float* __restrict__ ckpt, T* __restrict__ gx, T* __restrict__ gdt,
-                   float* __restrict__ gpart, int Bsz, int L, int D, int N, float dt_min,
-                   float dt_max) {
+                   const float* __restrict__ ckpt, const float* __restrict__ dtm,
+                   T* __restrict__ gx, T* __restrict__ gdt, float* __restrict__ gpart, int Bsz,
+                   int L, int D, int N, float dt_min, float dt_max) {
     constexpr int TS = SsmTiling<NS>::TS;
     constexpr int CK = SsmTiling<NS>::CK;
-    constexpr int SUBS = CK / TS;
     constexpr int V = 2 * NS;  // gB and gC values per step
     static_assert(V <= 32, "NS <= 16 in this kernel");
     __shared__ float sB[CK][NS];
     __shared__ float sC[CK][NS];
+    __shared__ float sDm[CK];                        // model mode: mean clamped dt per step
     __shared__ float sRed[kThreads / 32][TS][32];    // per-warp reduced gB|gC
     extern __shared__ float sSubFlat[];              // [SUBS][NS][kThreads] sub-chunk states
     auto sSub = reinterpret_cast<float(*)[NS][kThreads]>(sSubFlat);
@@ -177,7 +189,7 @@ __global__ void __launch_bounds__(kThreads)
     float A2[NS], dh[NS];
 #pragma unroll
     for (int n = 0; n < NS; ++n) {
-        A2[n] = (live && n < N) ? ldf(A + (long long)d * N + n) * kLog2e : 0.0f;
+        A2[n] = (live && n < N) ? a_at<MODEL>(A, d, n, N) * kLog2e : 0.0f;
         dh[n] = 0.0f;
     }
     const int ridx = reduced_index<V>(lane);
@@ -193,6 +205,8 @@ __global__ void __launch_bounds__(kThreads)
             sB[tt][n] = ok ? ldf(Bm + o) : 0.0f;
             sC[tt][n] = ok ? ldf(Cm + o) : 0.0f;
         }
+        if (MODEL)
+            for (int i = tid; i < CK; i += kThreads) sDm[i] = i < tn ? dtm[row0 + t0 + i] : 0.0f;
         __syncthreads();
         // ---- sub-chunk start states
         float h[NS];
@@ -212,7 +226,7 @@ __global__ void __launch_bounds__(kThreads)
             if (live) {
                 const long long o = (row0 + t0 + tt) * D + d;
                 const float dtc = fminf(fmaxf(ldf(dt + o), dt_min), dt_max);
-                const float dtx = dtc * ldf(x + o);
+                const float dtx = (MODEL ? sDm[tt] : dtc) * ldf(x + o);
 #pragma unroll
                 for (int n = 0; n < NS; ++n)
                     h[n] = fmaf(ex2(dtc * A2[n]), h[n], dtx * sB[tt][n]);
@@ -231,7 +245,7 @@ __global__ void __launch_bounds__(kThreads)
                 if (j < un && live) {
                     const long long o = (row0 + t0 + u0 + j) * D + d;
                     const float dtc = fminf(fmaxf(ldf(dt + o), dt_min), dt_max);
-                    const float dtx = dtc * ldf(x + o);
+                    const float dtx = (MODEL ? sDm[u0 + j] : dtc) * ldf(x + o);
 #pragma unroll
                     for (int n = 0; n < NS; ++n)
                         h[n] = fmaf(ex2(dtc * A2[n]), h[n], dtx * sB[u0 + j][n]);
@@ -252,7 +266,8 @@ __global__ void __launch_bounds__(kThreads)
                     const float dtc = fminf(fmaxf(draw, dt_min), dt_max);
                     const float xv = ldf(x + o);
                     const float dyv = ldf(dy + o);
-                    const float dtx = dtc * xv;
+                    const float dti = MODEL ? sDm[tt] : dtc;  // dt of the input term
+                    const float dtx = dti * xv;
                     float gxa = 0.0f, gda = 0.0f;
 #pragma unroll
                     for (int n = 0; n < NS; ++n) {
@@ -265,10 +280,10 @@ __global__ void __launch_bounds__(kThreads)
                         gxa = fmaf(dht, Bn, gxa);                   // gx = dt * sum dh B
                         // ddt = dh * (A_bar h_prev A + B x), A_bar h_prev = hc - dtx B
                         const float abhp = fmaf(-dtx, Bn, hc);
-                        gda = fmaf(dht, fmaf(abhp, A2[n] * kLn2, Bn * xv), gda);
+                        gda = fmaf(dht, fmaf(abhp, A2[n] * kLn2, MODEL ? 0.0f : Bn * xv), gda);
                         dh[n] = dht * ab;
                     }
-                    st_scalar<T>(gx + o, gxa * dtc);
+                    st_scalar<T>(gx + o, gxa * dti);
                     const bool inr = draw >= dt_min && draw <= dt_max;
                     st_scalar<T>(gdt + o, inr ? gda : 0.0f);
                 }
@@ -345,12 +360,13 @@ static __device__ __forceinline__ void stage_rows(unsigned char* dst, const T* s
 }
 
 // grid (ceil(D/128), B), block 128; two x/dt tiles of TB steps in flight.
-template <typename T, int NS, bool STATES_ONLY>
+template <typename T, int NS, bool STATES_ONLY, bool MODEL>
 __global__ void __launch_bounds__(kThreads)
     ssm_fwd_staged_kernel(const T* __restrict__ x, const T* __restrict__ dt,
                           const T* __restrict__ A, const T* __restrict__ Bm,
                           const T* __restrict__ Cm, T* __restrict__ y, float* __restrict__ ckpt,
-                          int L, int D, int N, float dt_min, float dt_max) {
+                          const float* __restrict__ dtm, int L, int D, int N, float dt_min,
+                          float dt_max) {
     constexpr int TB = 32;
     constexpr int CK = SsmTiling<NS>::CK;
     static_assert(CK % TB == 0, "checkpoints fall on tile starts");
@@ -361,6 +377,7 @@ __global__ void __launch_bounds__(kThreads)
     unsigned char* sDt = smem + 2 * TILEB;                    // [2][TB][128] T
     float* sB = reinterpret_cast<float*>(smem + 4 * TILEB);  // [2][TB][NS]
     float* sC = sB + 2 * TB * NS;                             // [2][TB][NS]
+    float* sDm = sC + 2 * TB * NS;                            // [2][TB] (model mode)
     const int tid = threadIdx.x;
     const int d0 = blockIdx.x * kThreads, d = d0 + tid;
     const int b = blockIdx.y;
@@ -374,12 +391,16 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
     for (int p = 0; p < NP; ++p) {
         const int n = 2 * p;
-        A2[p].x = (live && n < N) ? ldf(A + (long long)d * N + n) * kLog2e : 0.0f;
-        A2[p].y = (live && n + 1 < N) ? ldf(A + (long long)d * N + n + 1) * kLog2e : 0.0f;
+        A2[p].x = (live && n < N) ? a_at<MODEL>(A, d, n, N) * kLog2e : 0.0f;
+        A2[p].y = (live && n + 1 < N) ? a_at<MODEL>(A, d, n + 1, N) * kLog2e : 0.0f;
         h[p] = dup2(0.0f);
     }
-    float rb[BCV], rc[BCV];
+    float rb[BCV], rc[BCV], rdm = 0.0f;
     auto load_bc = [&](int k) {
+        if (MODEL) {
+            const int t = k * TB + tid;
+            rdm = (tid < TB && t < L) ? dtm[row0 + t] : 0.0f;
+        }
 #pragma unroll
         for (int v = 0; v < BCV; ++v) {
             const int idx = tid + v * kThreads, tt = idx / NS, n = idx % NS;
@@ -396,6 +417,7 @@ __global__ void __launch_bounds__(kThreads)
             sB[(k & 1) * TB * NS + tid + v * kThreads] = rb[v];
             sC[(k & 1) * TB * NS + tid + v * kThreads] = rc[v];
         }
+        if (MODEL && tid < TB) sDm[(k & 1) * TB + tid] = rdm;
     };
     auto issue = [&](int k) {
         stage_rows<T, TB>(sX + (k & 1) * TILEB, x, row0, k * TB, L, d0, D);
@@ -429,7 +451,8 @@ __global__ void __launch_bounds__(kThreads)
             }
             for (int tt = 0; tt < tn; ++tt) {
                 const float dtc = fminf(fmaxf(ldf(dts + tt * kThreads), dt_min), dt_max);
-                const float2 dtc2 = dup2(dtc), dtx2 = dup2(dtc * ldf(xs + tt * kThreads));
+                const float dti = MODEL ? sDm[(k & 1) * TB + tt] : dtc;
+                const float2 dtc2 = dup2(dtc), dtx2 = dup2(dti * ldf(xs + tt * kThreads));
                 float2 acc = dup2(0.0f);
 #pragma unroll
                 for (int p = 0; p < NP; p += 2) {
@@ -458,19 +481,20 @@ __global__ void __launch_bounds__(kThreads)
 
 template <typename T, int NS>
 constexpr size_t fwd_staged_smem() {
-    return (size_t)4 * 32 * StageGeom<T>::ROWB + (size_t)4 * 32 * NS * sizeof(float);
+    return (size_t)4 * 32 * StageGeom<T>::ROWB + (size_t)4 * 32 * NS * sizeof(float) +
+           (size_t)2 * 32 * sizeof(float);
 }
 
 // grid (ceil(D/128), B), block 128: ssm_bwd_kernel with the chunk's x, dt, dy
 // rows staged in shared memory (one chunk at a time; two CTAs share an SM).
-template <typename T, int NS>
+template <typename T, int NS, bool MODEL>
 __global__ void __launch_bounds__(kThreads)
     ssm_bwd_staged_kernel(const T* __restrict__ x, const T* __restrict__ dt,
                           const T* __restrict__ A, const T* __restrict__ Bm,
                           const T* __restrict__ Cm, const T* __restrict__ dy,
-                          const float* __restrict__ ckpt, T* __restrict__ gx, T* __restrict__ gdt,
-                          float* __restrict__ gpart, int Bsz, int L, int D, int N, float dt_min,
-                          float dt_max) {
+                          const float* __restrict__ ckpt, const float* __restrict__ dtm,
+                          T* __restrict__ gx, T* __restrict__ gdt, float* __restrict__ gpart,
+                          int Bsz, int L, int D, int N, float dt_min, float dt_max) {
     constexpr int TS = SsmTiling<NS>::TS;
     constexpr int CK = SsmTiling<NS>::CK;
     constexpr int SUBS = CK / TS;
@@ -486,6 +510,7 @@ __global__ void __launch_bounds__(kThreads)
     // per-warp gB|gC sums of every step of the chunk; summed across warps once
     // per chunk, so the warps run out of phase between the chunk barriers
     auto sRed = reinterpret_cast<float(*)[CK][V]>(sC + CK * NS);         // [4][CK][V]
+    float* sDm = &sRed[kThreads / 32][0][0];  // [CK] model mode: mean clamped dt per step
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int d0 = blockIdx.x * kThreads, d = d0 + tid;
     const int b = blockIdx.y;
@@ -503,8 +528,8 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
     for (int p = 0; p < NP; ++p) {
         const int n = 2 * p;
-        A2[p].x = (live && n < N) ? ldf(A + (long long)d * N + n) * kLog2e : 0.0f;
-        A2[p].y = (live && n + 1 < N) ? ldf(A + (long long)d * N + n + 1) * kLog2e : 0.0f;
+        A2[p].x = (live && n < N) ? a_at<MODEL>(A, d, n, N) * kLog2e : 0.0f;
+        A2[p].y = (live && n + 1 < N) ? a_at<MODEL>(A, d, n + 1, N) * kLog2e : 0.0f;
         A2ln[p] = mul2(A2[p], dup2(kLn2));
         dh[p] = dup2(0.0f);
     }
@@ -533,6 +558,9 @@ __global__ void __launch_bounds__(kThreads)
                 sB[tid + v * kThreads] = rb[v];
                 sC[tid + v * kThreads] = rc[v];
             }
+            if (MODEL)
+                for (int i = tid; i < CK; i += kThreads)
+                    sDm[i] = i < tn ? dtm[row0 + t0 + i] : 0.0f;
         }
         float2 h[NP];
         if (live) {
@@ -559,7 +587,8 @@ __global__ void __launch_bounds__(kThreads)
                 }
             }
             const float dtc = fminf(fmaxf(ldf(sdt + tt * kThreads), dt_min), dt_max);
-            const float2 dtc2 = dup2(dtc), dtx2 = dup2(dtc * ldf(sx + tt * kThreads));
+            const float2 dtc2 = dup2(dtc),
+                         dtx2 = dup2((MODEL ? sDm[tt] : dtc) * ldf(sx + tt * kThreads));
 #pragma unroll
             for (int p = 0; p < NP; p += 2) {
                 const float4 b4 = *reinterpret_cast<const float4*>(sB + tt * NS + 2 * p);
@@ -585,7 +614,8 @@ __global__ void __launch_bounds__(kThreads)
             for (int j = 0; j < TS; ++j) {
                 const int tt = min(u0 + j, tn - 1);  // steps past tn are never read back
                 const float dtc = fminf(fmaxf(ldf(sdt + tt * kThreads), dt_min), dt_max);
-                const float2 dtc2 = dup2(dtc), dtx2 = dup2(dtc * ldf(sx + tt * kThreads));
+                const float2 dtc2 = dup2(dtc),
+                             dtx2 = dup2((MODEL ? sDm[tt] : dtc) * ldf(sx + tt * kThreads));
 #pragma unroll
                 for (int p = 0; p < NP; p += 2) {
                     const float4 b4 = *reinterpret_cast<const float4*>(sB + tt * NS + 2 * p);
@@ -608,7 +638,8 @@ __global__ void __launch_bounds__(kThreads)
                     const float dtc = fminf(fmaxf(draw, dt_min), dt_max);
                     const float xv = ldf(sx + tt * kThreads);
                     const float dyv = ldf(sdy + tt * kThreads);
-                    const float dtx = dtc * xv;
+                    const float dti = MODEL ? sDm[tt] : dtc;  // dt of the input term
+                    const float dtx = dti * xv;
                     const float2 dy2 = dup2(dyv), dtx2 = dup2(dtx), ndtx2 = dup2(-dtx);
                     float2 gxa = dup2(0.0f), gda = dup2(0.0f);
 #pragma unroll
@@ -636,9 +667,11 @@ __global__ void __launch_bounds__(kThreads)
                         }
                     }
                     const float gxs = gxa.x + gxa.y;
-                    const float gds = fmaf(xv, gxs, gda.x + gda.y);
+                    // model mode: the input term's dt is the channel mean, whose
+                    // gradient ssm_model_gdt_kernel adds afterwards
+                    const float gds = MODEL ? gda.x + gda.y : fmaf(xv, gxs, gda.x + gda.y);
                     const long long o = (row0 + t0 + tt) * D + d;
-                    st_scalar<T>(gx + o, gxs * dtc);
+                    st_scalar<T>(gx + o, gxs * dti);
                     const bool inr = draw >= dt_min && draw <= dt_max;
                     st_scalar<T>(gdt + o, inr ? gds : 0.0f);
                 } else {
@@ -672,7 +705,59 @@ constexpr size_t bwd_staged_smem() {
     constexpr int TS = SsmTiling<NS>::TS, CK = SsmTiling<NS>::CK;
     return (size_t)(CK / TS) * NS * kThreads * sizeof(float) +
            (size_t)3 * CK * StageGeom<T>::ROWB + (size_t)2 * CK * NS * sizeof(float) +
-           (size_t)(kThreads / 32) * CK * 2 * NS * sizeof(float);
+           (size_t)(kThreads / 32) * CK * 2 * NS * sizeof(float) + (size_t)CK * sizeof(float);
+}
+
+// ------------------------------------------------------------ model semantics
+// lib/edifice/ssm/common.ex:402-444 (discretize_ssm): B_bar = mean_d(clip(dt)) B.
+// dtm[row] = mean over d_inner of the clamped dt, one warp per (b, t) row, summed
+// in a fixed order (deterministic).
+template <typename T>
+__global__ void __launch_bounds__(256)
+    ssm_dt_mean_kernel(const T* __restrict__ dt, float* __restrict__ dtm, long long rows, int D,
+                       float dt_min, float dt_max) {
+    const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const T* p = dt + row * D;
+    float acc = 0.0f;
+    constexpr int EPV = 16 / (int)sizeof(T);
+    if (D % EPV == 0 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+        for (int i = lane * EPV; i < D; i += 32 * EPV) {
+            float f[EPV];
+            Vec16<T>::unpack(*reinterpret_cast<const uint4*>(p + i), f);
+#pragma unroll
+            for (int j = 0; j < EPV; ++j) acc += fminf(fmaxf(f[j], dt_min), dt_max);
+        }
+    } else {
+        for (int i = lane; i < D; i += 32) acc += fminf(fmaxf(ldf(p + i), dt_min), dt_max);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) dtm[row] = acc / (float)D;
+}
+
+// gdt[b,t,d] += [dt in range] * g_m / D with g_m = sum_{d,n} dh B x
+// = sum_n B[b,t,n] gB[b,t,n] / dtm[b,t] (gB = dtm sum_d dh x).  One warp per row.
+template <typename T>
+__global__ void __launch_bounds__(256)
+    ssm_model_gdt_kernel(const T* __restrict__ dt, const T* __restrict__ Bm,
+                         const float* __restrict__ gB, const float* __restrict__ dtm,
+                         T* __restrict__ gdt, long long rows, int D, int N, float dt_min,
+                         float dt_max) {
+    const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    float gm = lane < N ? ldf(Bm + row * N + lane) * gB[row * N + lane] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) gm += __shfl_xor_sync(0xffffffffu, gm, o);
+    const float add = gm / dtm[row] / (float)D;
+    const T* p = dt + row * D;
+    T* g = gdt + row * D;
+    for (int i = lane; i < D; i += 32) {
+        const float draw = ldf(p + i);
+        if (draw >= dt_min && draw <= dt_max) st_scalar<T>(g + i, ldf(g + i) + add);
+    }
 }
 
 int pad_states(int N) {
@@ -695,58 +780,54 @@ size_t part_bytes(int B, int L, int D, int NS) {
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-template <typename T, int NS>
+template <typename T, int NS, bool MODEL>
 int launch_fwd(const void* x, const void* dt, const void* A, const void* Bm, const void* Cm,
-               void* y, float* ckpt, int B, int L, int D, int N, float lo, float hi,
-               bool states_only, cudaStream_t st) {
+               void* y, float* ckpt, const float* dtm, int B, int L, int D, int N, float lo,
+               float hi, bool states_only, cudaStream_t st) {
     dim3 grid((D + kThreads - 1) / kThreads, B);
     if (D % StageGeom<T>::EPC == 0 && edb::aligned16(x) && edb::aligned16(dt)) {
         constexpr size_t sm = fwd_staged_smem<T, NS>();
-        auto kern = states_only ? ssm_fwd_staged_kernel<T, NS, true>
-                                : ssm_fwd_staged_kernel<T, NS, false>;
+        auto kern = states_only ? ssm_fwd_staged_kernel<T, NS, true, MODEL>
+                                : ssm_fwd_staged_kernel<T, NS, false, MODEL>;
         cudaError_t ea =
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
         if (ea != cudaSuccess) return (int)ea;
         kern<<<grid, kThreads, sm, st>>>((const T*)x, (const T*)dt, (const T*)A, (const T*)Bm,
-                                         (const T*)Cm, (T*)y, ckpt, L, D, N, lo, hi);
+                                         (const T*)Cm, (T*)y, ckpt, dtm, L, D, N, lo, hi);
         return edb::status_from_cuda(cudaGetLastError());
     }
-    if (states_only)
-        ssm_fwd_kernel<T, NS, true><<<grid, kThreads, 0, st>>>(
-            (const T*)x, (const T*)dt, (const T*)A, (const T*)Bm, (const T*)Cm, (T*)y, ckpt, L, D,
-            N, lo, hi);
-    else
-        ssm_fwd_kernel<T, NS, false><<<grid, kThreads, 0, st>>>(
-            (const T*)x, (const T*)dt, (const T*)A, (const T*)Bm, (const T*)Cm, (T*)y, ckpt, L, D,
-            N, lo, hi);
+    auto kern = states_only ? ssm_fwd_kernel<T, NS, true, MODEL> : ssm_fwd_kernel<T, NS, false, MODEL>;
+    kern<<<grid, kThreads, 0, st>>>((const T*)x, (const T*)dt, (const T*)A, (const T*)Bm,
+                                    (const T*)Cm, (T*)y, ckpt, dtm, L, D, N, lo, hi);
     return edb::status_from_cuda(cudaGetLastError());
 }
 
-template <typename T, int NS>
+template <typename T, int NS, bool MODEL>
 int launch_bwd(const void* x, const void* dt, const void* A, const void* Bm, const void* Cm,
-               const void* dy, const float* ckpt, void* gx, void* gdt, float* gB, float* gC,
-               float* gpart, int B, int L, int D, int N, float lo, float hi, cudaStream_t st) {
+               const void* dy, const float* ckpt, const float* dtm, void* gx, void* gdt,
+               float* gB, float* gC, float* gpart, int B, int L, int D, int N, float lo, float hi,
+               cudaStream_t st) {
     const int nblk = (D + kThreads - 1) / kThreads;
     dim3 grid(nblk, B);
     if (D % StageGeom<T>::EPC == 0 && edb::aligned16(x) && edb::aligned16(dt) &&
         edb::aligned16(dy)) {
         constexpr size_t sm = bwd_staged_smem<T, NS>();
-        cudaError_t ea = cudaFuncSetAttribute(ssm_bwd_staged_kernel<T, NS>,
+        cudaError_t ea = cudaFuncSetAttribute(ssm_bwd_staged_kernel<T, NS, MODEL>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
         if (ea != cudaSuccess) return (int)ea;
-        ssm_bwd_staged_kernel<T, NS><<<grid, kThreads, sm, st>>>(
+        ssm_bwd_staged_kernel<T, NS, MODEL><<<grid, kThreads, sm, st>>>(
             (const T*)x, (const T*)dt, (const T*)A, (const T*)Bm, (const T*)Cm, (const T*)dy,
-            ckpt, (T*)gx, (T*)gdt, gpart, B, L, D, N, lo, hi);
+            ckpt, dtm, (T*)gx, (T*)gdt, gpart, B, L, D, N, lo, hi);
     } else {
         constexpr int SUBS = SsmTiling<NS>::CK / SsmTiling<NS>::TS;
         const size_t dsmem = (size_t)SUBS * NS * kThreads * sizeof(float);
-        cudaError_t ea = cudaFuncSetAttribute(ssm_bwd_kernel<T, NS>,
+        cudaError_t ea = cudaFuncSetAttribute(ssm_bwd_kernel<T, NS, MODEL>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               (int)dsmem);
         if (ea != cudaSuccess) return (int)ea;
-        ssm_bwd_kernel<T, NS><<<grid, kThreads, dsmem, st>>>(
+        ssm_bwd_kernel<T, NS, MODEL><<<grid, kThreads, dsmem, st>>>(
             (const T*)x, (const T*)dt, (const T*)A, (const T*)Bm, (const T*)Cm, (const T*)dy,
-            ckpt, (T*)gx, (T*)gdt, gpart, B, L, D, N, lo, hi);
+            ckpt, dtm, (T*)gx, (T*)gdt, gpart, B, L, D, N, lo, hi);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return (int)e;
@@ -754,8 +835,43 @@ int launch_bwd(const void* x, const void* dt, const void* A, const void* Bm, con
     const int thr = 256;
     ssm_reduce_kernel<NS><<<(unsigned)((total + thr - 1) / thr), thr, 0, st>>>(
         gpart, gB, gC, nblk, (long long)B * L, N);
+    e = cudaGetLastError();
+    if (e != cudaSuccess || !MODEL) return edb::status_from_cuda(e);
+    // model mode: the gradient through the channel mean of dt
+    const long long rows = (long long)B * L;
+    ssm_model_gdt_kernel<T><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+        (const T*)dt, (const T*)Bm, gB, dtm, (T*)gdt, rows, D, N, lo, hi);
     return edb::status_from_cuda(cudaGetLastError());
 }
+
+// Runs F<T, NS>::run(args...) for the dtype / padded state count.
+template <template <typename, int> class F, typename... Args>
+int dispatch(int dtype, int NS, Args... args) {
+    if (dtype == EDB_BF16)
+        return NS == 8 ? F<__nv_bfloat16, 8>::run(args...) : F<__nv_bfloat16, 16>::run(args...);
+    return NS == 8 ? F<float, 8>::run(args...) : F<float, 16>::run(args...);
+}
+
+template <typename T, int NS>
+struct FwdKernelMode {
+    template <typename... A>
+    static int run(A... a) { return launch_fwd<T, NS, false>(a...); }
+};
+template <typename T, int NS>
+struct FwdModelMode {
+    template <typename... A>
+    static int run(A... a) { return launch_fwd<T, NS, true>(a...); }
+};
+template <typename T, int NS>
+struct BwdKernelMode {
+    template <typename... A>
+    static int run(A... a) { return launch_bwd<T, NS, false>(a...); }
+};
+template <typename T, int NS>
+struct BwdModelMode {
+    template <typename... A>
+    static int run(A... a) { return launch_bwd<T, NS, true>(a...); }
+};
 
 int check_args(int dtype, int B, int L, int D, int N, float lo, float hi) {
     if (dtype != EDB_F32 && dtype != EDB_BF16) return EDB_ERR_BAD_DTYPE;
@@ -781,17 +897,9 @@ extern "C" int edb_selective_scan_fwd(int dtype, const void* x, const void* dt, 
     if (int s = check_args(dtype, batch, seq_len, d_inner, d_state, dt_min, dt_max)) return s;
     if (!x || !dt || !A || !B || !C || !y) return EDB_ERR_NULL_POINTER;
     if (h_ckpt && !edb::aligned16(h_ckpt)) return EDB_ERR_MISALIGNED;
-    const int NS = pad_states(d_state);
-    cudaStream_t st = (cudaStream_t)stream;
-    if (dtype == EDB_BF16)
-        return NS == 8 ? launch_fwd<__nv_bfloat16, 8>(x, dt, A, B, C, y, h_ckpt, batch, seq_len,
-                                                      d_inner, d_state, dt_min, dt_max, false, st)
-                       : launch_fwd<__nv_bfloat16, 16>(x, dt, A, B, C, y, h_ckpt, batch, seq_len,
-                                                       d_inner, d_state, dt_min, dt_max, false, st);
-    return NS == 8 ? launch_fwd<float, 8>(x, dt, A, B, C, y, h_ckpt, batch, seq_len, d_inner,
-                                          d_state, dt_min, dt_max, false, st)
-                   : launch_fwd<float, 16>(x, dt, A, B, C, y, h_ckpt, batch, seq_len, d_inner,
-                                           d_state, dt_min, dt_max, false, st);
+    return dispatch<FwdKernelMode>(dtype, pad_states(d_state), x, dt, A, B, C, y, h_ckpt,
+                                   (const float*)nullptr, batch, seq_len, d_inner, d_state,
+                                   dt_min, dt_max, false, (cudaStream_t)stream);
 }
 
 extern "C" size_t edb_selective_scan_bwd_workspace(int batch, int seq_len, int d_inner,
@@ -803,15 +911,14 @@ extern "C" size_t edb_selective_scan_bwd_workspace(int batch, int seq_len, int d
     return ws;
 }
 
-extern "C" int edb_selective_scan_bwd(int dtype, const void* x, const void* dt, const void* A,
-                                      const void* B, const void* C, const void* dy,
-                                      const float* h_ckpt, void* gx, void* gdt, float* gB,
-                                      float* gC, int batch, int seq_len, int d_inner,
-                                      int d_state, float dt_min, float dt_max, void* workspace,
-                                      size_t workspace_bytes, void* stream) {
-    if (int s = check_args(dtype, batch, seq_len, d_inner, d_state, dt_min, dt_max)) return s;
-    if (!x || !dt || !A || !B || !C || !dy || !gx || !gdt || !gB || !gC)
-        return EDB_ERR_NULL_POINTER;
+namespace {
+
+// Shared body of the kernel-mode and model-mode backward (dtm != nullptr: model).
+int ssm_bwd(int dtype, const void* x, const void* dt, const void* A, const void* B,
+            const void* C, const void* dy, const float* dtm, const float* h_ckpt, void* gx,
+            void* gdt, float* gB, float* gC, int batch, int seq_len, int d_inner, int d_state,
+            float dt_min, float dt_max, void* workspace, size_t workspace_bytes, void* stream) {
+    const bool model = dtm != nullptr;
     const size_t need =
         edb_selective_scan_bwd_workspace(batch, seq_len, d_inner, d_state, h_ckpt != nullptr);
     if (workspace_bytes < need || (need && !workspace)) return EDB_ERR_WORKSPACE_TOO_SMALL;
@@ -824,33 +931,75 @@ extern "C" int edb_selective_scan_bwd(int dtype, const void* x, const void* dt, 
     if (!ck) {
         float* ckw = reinterpret_cast<float*>(static_cast<char*>(workspace) +
                                               align256(part_bytes(batch, seq_len, d_inner, NS)));
-        int s;
-        if (dtype == EDB_BF16)
-            s = NS == 8 ? launch_fwd<__nv_bfloat16, 8>(x, dt, A, B, C, nullptr, ckw, batch,
-                                                       seq_len, d_inner, d_state, dt_min, dt_max,
-                                                       true, st)
-                        : launch_fwd<__nv_bfloat16, 16>(x, dt, A, B, C, nullptr, ckw, batch,
-                                                        seq_len, d_inner, d_state, dt_min, dt_max,
-                                                        true, st);
-        else
-            s = NS == 8 ? launch_fwd<float, 8>(x, dt, A, B, C, nullptr, ckw, batch, seq_len,
-                                               d_inner, d_state, dt_min, dt_max, true, st)
-                        : launch_fwd<float, 16>(x, dt, A, B, C, nullptr, ckw, batch, seq_len,
-                                                d_inner, d_state, dt_min, dt_max, true, st);
+        const int s =
+            model ? dispatch<FwdModelMode>(dtype, NS, x, dt, A, B, C, (void*)nullptr, ckw, dtm,
+                                           batch, seq_len, d_inner, d_state, dt_min, dt_max, true,
+                                           st)
+                  : dispatch<FwdKernelMode>(dtype, NS, x, dt, A, B, C, (void*)nullptr, ckw, dtm,
+                                            batch, seq_len, d_inner, d_state, dt_min, dt_max, true,
+                                            st);
         if (s) return s;
         ck = ckw;
     }
+    return model ? dispatch<BwdModelMode>(dtype, NS, x, dt, A, B, C, dy, ck, dtm, gx, gdt, gB, gC,
+                                          gpart, batch, seq_len, d_inner, d_state, dt_min, dt_max,
+                                          st)
+                 : dispatch<BwdKernelMode>(dtype, NS, x, dt, A, B, C, dy, ck, dtm, gx, gdt, gB, gC,
+                                           gpart, batch, seq_len, d_inner, d_state, dt_min, dt_max,
+                                           st);
+}
+
+}  // namespace
+
+extern "C" int edb_selective_scan_bwd(int dtype, const void* x, const void* dt, const void* A,
+                                      const void* B, const void* C, const void* dy,
+                                      const float* h_ckpt, void* gx, void* gdt, float* gB,
+                                      float* gC, int batch, int seq_len, int d_inner,
+                                      int d_state, float dt_min, float dt_max, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+    if (int s = check_args(dtype, batch, seq_len, d_inner, d_state, dt_min, dt_max)) return s;
+    if (!x || !dt || !A || !B || !C || !dy || !gx || !gdt || !gB || !gC)
+        return EDB_ERR_NULL_POINTER;
+    return ssm_bwd(dtype, x, dt, A, B, C, dy, nullptr, h_ckpt, gx, gdt, gB, gC, batch, seq_len,
+                   d_inner, d_state, dt_min, dt_max, workspace, workspace_bytes, stream);
+}
+
+// ------------------------------------------------------------- model semantics
+extern "C" int edb_selective_scan_model_fwd(int dtype, const void* x, const void* dt,
+                                            const void* A, const void* B, const void* C, void* y,
+                                            float* dt_mean, float* h_ckpt, int batch,
+                                            int seq_len, int d_inner, int d_state, float dt_min,
+                                            float dt_max, void* stream) {
+    if (int s = check_args(dtype, batch, seq_len, d_inner, d_state, dt_min, dt_max)) return s;
+    if (!x || !dt || !B || !C || !y || !dt_mean) return EDB_ERR_NULL_POINTER;
+    if (h_ckpt && !edb::aligned16(h_ckpt)) return EDB_ERR_MISALIGNED;
+    cudaStream_t st = (cudaStream_t)stream;
+    const long long rows = (long long)batch * seq_len;
     if (dtype == EDB_BF16)
-        return NS == 8 ? launch_bwd<__nv_bfloat16, 8>(x, dt, A, B, C, dy, ck, gx, gdt, gB, gC,
-                                                      gpart, batch, seq_len, d_inner, d_state,
-                                                      dt_min, dt_max, st)
-                       : launch_bwd<__nv_bfloat16, 16>(x, dt, A, B, C, dy, ck, gx, gdt, gB, gC,
-                                                       gpart, batch, seq_len, d_inner, d_state,
-                                                       dt_min, dt_max, st);
-    return NS == 8 ? launch_bwd<float, 8>(x, dt, A, B, C, dy, ck, gx, gdt, gB, gC, gpart, batch,
-                                          seq_len, d_inner, d_state, dt_min, dt_max, st)
-                   : launch_bwd<float, 16>(x, dt, A, B, C, dy, ck, gx, gdt, gB, gC, gpart, batch,
-                                           seq_len, d_inner, d_state, dt_min, dt_max, st);
+        ssm_dt_mean_kernel<__nv_bfloat16><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+            (const __nv_bfloat16*)dt, dt_mean, rows, d_inner, dt_min, dt_max);
+    else
+        ssm_dt_mean_kernel<float><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+            (const float*)dt, dt_mean, rows, d_inner, dt_min, dt_max);
+    if (cudaError_t e = cudaGetLastError()) return (int)e;
+    return dispatch<FwdModelMode>(dtype, pad_states(d_state), x, dt, A, B, C, y, h_ckpt,
+                                  (const float*)dt_mean, batch, seq_len, d_inner, d_state, dt_min,
+                                  dt_max, false, st);
+}
+
+extern "C" int edb_selective_scan_model_bwd(int dtype, const void* x, const void* dt,
+                                            const void* A, const void* B, const void* C,
+                                            const void* dy, const float* dt_mean,
+                                            const float* h_ckpt, void* gx, void* gdt, float* gB,
+                                            float* gC, int batch, int seq_len, int d_inner,
+                                            int d_state, float dt_min, float dt_max,
+                                            void* workspace, size_t workspace_bytes,
+                                            void* stream) {
+    if (int s = check_args(dtype, batch, seq_len, d_inner, d_state, dt_min, dt_max)) return s;
+    if (!x || !dt || !B || !C || !dy || !dt_mean || !gx || !gdt || !gB || !gC)
+        return EDB_ERR_NULL_POINTER;
+    return ssm_bwd(dtype, x, dt, A, B, C, dy, dt_mean, h_ckpt, gx, gdt, gB, gC, batch, seq_len,
+                   d_inner, d_state, dt_min, dt_max, workspace, workspace_bytes, stream);
 }
 
 // ---------------------------------------------------------------- no-alloc variant

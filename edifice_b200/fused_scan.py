@@ -252,6 +252,75 @@ def selective_scan_backward(x, dt, a, b, c, grad_output, h_ckpt=None):
     return gx, gdt, gB, gC
 
 
+def _model_shapes(x, a, b):
+    Bsz, L, D = x.shape
+    N = b.shape[2]
+    if tuple(b.shape[:2]) != (Bsz, L) or (a is not None and tuple(a.shape) != (D, N)):
+        raise _lib.EdbError("selective_scan_model: shape mismatch x%s B%s A%s"
+                            % (tuple(x.shape), tuple(b.shape),
+                               None if a is None else tuple(a.shape)))
+    return Bsz, L, D, N
+
+
+def selective_scan_model(x, dt, b, c, a=None, with_ckpt=False):
+    """Model semantics of Edifice.build(:mamba): Common.selective_scan_fallback/5
+    (lib/edifice/ssm/common.ex:661-670 -> discretize_ssm :402-444): B_bar is the
+    channel mean of the clamped dt times B, A the fixed -(1..N) diagonal when
+    ``a`` is None (common.ex:409; Mamba.parallel_scan_ssm_impl builds the same
+    matrix, mamba.ex:187-193).  Returns (y, dt_mean) or (y, dt_mean, h_ckpt);
+    dt_mean [B, L] f32 is what the backward needs."""
+    _dev(x, dt, a, b, c, what="selective_scan_model")
+    Bsz, L, D, N = _model_shapes(x, a, b)
+    y = torch.empty_like(x)
+    dtm = torch.empty((Bsz, L), dtype=torch.float32, device=x.device)
+    lib = _lib.load()
+    ck = None
+    if with_ckpt:
+        nbytes = lib.edb_selective_scan_ckpt_bytes(Bsz, L, D, N)
+        ck = torch.empty(nbytes // 4, dtype=torch.float32, device=x.device)
+    _lib.check(lib.edb_selective_scan_model_fwd(_dtype_code(x, "selective_scan_model"), _p(x),
+                                                _p(dt), _p(a), _p(b), _p(c), _p(y), _p(dtm),
+                                                _p(ck), Bsz, L, D, N, DT_MIN, DT_MAX, _stream()),
+               "CUDA fused selective scan (model semantics)")
+    return (y, dtm, ck) if with_ckpt else (y, dtm)
+
+
+def selective_scan_model_backward(x, dt, b, c, grad_output, dt_mean, a=None, h_ckpt=None):
+    """Returns (grad_x, grad_dt, grad_B, grad_C) of selective_scan_model;
+    grad_B/grad_C f32, A gets none."""
+    _dev(x, dt, a, b, c, grad_output, dt_mean, h_ckpt, what="selective_scan_model_backward")
+    Bsz, L, D, N = _model_shapes(x, a, b)
+    lib = _lib.load()
+    gx, gdt = torch.empty_like(x), torch.empty_like(x)
+    gB = torch.empty((Bsz, L, N), dtype=torch.float32, device=x.device)
+    gC = torch.empty_like(gB)
+    wsb = lib.edb_selective_scan_bwd_workspace(Bsz, L, D, N, int(h_ckpt is not None))
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=x.device)
+    _lib.check(lib.edb_selective_scan_model_bwd(
+        _dtype_code(x, "selective_scan_model_backward"), _p(x), _p(dt), _p(a), _p(b), _p(c),
+        _p(grad_output), _p(dt_mean), _p(h_ckpt), _p(gx), _p(gdt), _p(gB), _p(gC), Bsz, L, D, N,
+        DT_MIN, DT_MAX, _p(ws), wsb, _stream()),
+        "CUDA fused selective scan backward (model semantics)")
+    return gx, gdt, gB, gC
+
+
+class SelectiveScanModelFn(torch.autograd.Function):
+    """The Mamba layer's SSM core with gradients to x, dt, B and C (A is the
+    fixed diagonal, as Edifice.build(:mamba) uses it)."""
+
+    @staticmethod
+    def forward(ctx, x, dt, b, c):
+        y, dtm, ck = selective_scan_model(x, dt, b, c, with_ckpt=True)
+        ctx.save_for_backward(x, dt, b, c, dtm, ck)
+        return y
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        x, dt, b, c, dtm, ck = ctx.saved_tensors
+        return selective_scan_model_backward(x, dt, b, c, grad_output.contiguous(), dtm,
+                                             h_ckpt=ck)
+
+
 def _delta_shapes(q, k, v, beta):
     if q.dim() != 4 or q.shape != k.shape or q.shape != v.shape:
         raise _lib.EdbError("delta_net_scan: q, k, v must share one [B, L, H, d] shape")

@@ -165,6 +165,34 @@ int edb_selective_scan_bwd(int dtype, const void* x, const void* dt, const void*
                            void* stream);
 
 /* ------------------------------------------------------------------------
+ * Mamba selective scan, MODEL semantics (what Edifice.build(:mamba) computes:
+ * lib/edifice/ssm/common.ex:402-470 discretize_ssm + scan + output, reached
+ * through selective_scan_fallback :661-670 and mamba.ex:183-213):
+ *   dtc = clip(dt, dt_min, dt_max);  m_t = mean over d_inner of dtc;
+ *   h_n = exp(dtc A[d,n]) h_n + m_t B[b,t,n] x;  y = sum_n C[b,t,n] h_n.
+ * A = NULL is the model's fixed diagonal A[d,n] = -(n+1) (common.ex:409); a
+ * non-NULL A [d_inner, d_state] is used as given.  dt_mean ([batch, seq_len]
+ * f32) receives m; the backward reads it back.  h_ckpt as in
+ * edb_selective_scan_fwd.
+ * ---------------------------------------------------------------------- */
+int edb_selective_scan_model_fwd(int dtype, const void* x, const void* dt, const void* A,
+                                 const void* B, const void* C, void* y, float* dt_mean,
+                                 float* h_ckpt, int batch, int seq_len, int d_inner, int d_state,
+                                 float dt_min, float dt_max, void* stream);
+
+/* Backward of the model semantics (the gradient Nx's autodiff takes through
+ * common.ex:402-515): gx, gdt in `dtype`, gB, gC f32; A gets no gradient; gdt
+ * is 0 where dt lies outside [dt_min, dt_max] and includes the term through the
+ * channel mean m.  dt_mean: the forward's.  Workspace:
+ * edb_selective_scan_bwd_workspace() bytes, 16-byte aligned. */
+int edb_selective_scan_model_bwd(int dtype, const void* x, const void* dt, const void* A,
+                                 const void* B, const void* C, const void* dy,
+                                 const float* dt_mean, const float* h_ckpt, void* gx, void* gdt,
+                                 float* gB, float* gC, int batch, int seq_len, int d_inner,
+                                 int d_state, float dt_min, float dt_max, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * Scaled-dot-product attention, causal or full, with grouped KV heads (GQA).
  *   O = softmax(Q K^T * scale [+ -inf above the diagonal if causal]) V
  * q, o: [batch, q_heads, seq_len, head_dim]; k, v: [batch, kv_heads, seq_len,

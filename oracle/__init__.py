@@ -133,15 +133,32 @@ def selective_scan_bwd(x, dt, A, Bm, Cm, dy, prec="f64", dt_min=DT_MIN, dt_max=D
     return gx, gdt, gB, gC
 
 
-def selective_scan_model_fwd(x, dt, Bm, Cm, prec="f64", dt_min=DT_MIN, dt_max=DT_MAX):
+def selective_scan_model_fwd(x, dt, Bm, Cm, prec="f64", dt_min=DT_MIN, dt_max=DT_MAX, A=None):
+    """Model semantics (common.ex:661-670); A=None is the fixed -(1..N) diagonal."""
     x, dt, Bm, Cm = map(_f32, (x, dt, Bm, Cm))
+    A = None if A is None else _f32(A)
     B, L, D = x.shape
     N = Bm.shape[2]
     y = np.empty_like(x)
-    _fn("selective_scan_model_fwd", prec)(_p(x), _p(dt), _p(Bm), _p(Cm), _p(y), _I(B), _I(L),
-                                          _I(D), _I(N), ctypes.c_float(dt_min),
+    _fn("selective_scan_model_fwd", prec)(_p(x), _p(dt), _p(A), _p(Bm), _p(Cm), _p(y), _I(B),
+                                          _I(L), _I(D), _I(N), ctypes.c_float(dt_min),
                                           ctypes.c_float(dt_max))
     return y
+
+
+def selective_scan_model_bwd(x, dt, Bm, Cm, dy, prec="f64", dt_min=DT_MIN, dt_max=DT_MAX,
+                             A=None):
+    """Gradients (gx, gdt, gB, gC) of the model semantics; A gets none."""
+    x, dt, Bm, Cm, dy = map(_f32, (x, dt, Bm, Cm, dy))
+    A = None if A is None else _f32(A)
+    B, L, D = x.shape
+    N = Bm.shape[2]
+    gx, gdt = np.empty_like(x), np.empty_like(x)
+    gB, gC = np.empty((B, L, N), np.float32), np.empty((B, L, N), np.float32)
+    _fn("selective_scan_model_bwd", prec)(_p(x), _p(dt), _p(A), _p(Bm), _p(Cm), _p(dy), _p(gx),
+                                          _p(gdt), _p(gB), _p(gC), _I(B), _I(L), _I(D), _I(N),
+                                          ctypes.c_float(dt_min), ctypes.c_float(dt_max))
+    return gx, gdt, gB, gC
 
 
 # ------------------------------------------------------------ delta rule

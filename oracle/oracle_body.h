@@ -258,10 +258,18 @@ void FN(selective_scan_bwd)(const float* x, const float* dt, const float* A, con
 /* Mamba selective scan, MODEL semantics (Edifice.build(:mamba) fallback):
  * lib/edifice/ssm/common.ex:661-670 -> discretize_ssm :402-444 (fixed
  * A = -(1..N), B_bar from the channel-mean of the clamped dt), sequential_scan
- * :492-515, compute_ssm_output :462-470.  A is not read. */
-void FN(selective_scan_model_fwd)(const float* x, const float* dt, const float* Bm,
-                                  const float* Cm, float* y, int B, int L, int D, int N,
-                                  float dt_min, float dt_max) {
+ * :492-515, compute_ssm_output :462-470.  The fallback does not read its A
+ * argument; its caller lib/edifice/ssm/mamba.ex:187-193 hands the fused path the
+ * same fixed matrix.  A == NULL here means that fixed diagonal; a non-NULL A
+ * [D, N] is used instead (the fused path's contract). */
+static REAL ORC_CAT(model_a, SFX)(const float* A, int d, int n, int N) {
+    return A ? (REAL)A[(size_t)d * N + n] : -(REAL)(n + 1);
+}
+
+void FN(selective_scan_model_fwd)(const float* x, const float* dt, const float* A,
+                                  const float* Bm, const float* Cm, float* y, int B, int L, int D,
+                                  int N, float dt_min, float dt_max) {
+    #pragma omp parallel for schedule(dynamic)
     for (int b = 0; b < B; b++) {
         REAL* h = (REAL*)calloc((size_t)D * N, sizeof(REAL));
         for (int t = 0; t < L; t++) {
@@ -274,7 +282,7 @@ void FN(selective_scan_model_fwd)(const float* x, const float* dt, const float* 
                 REAL dtc = ORC_CAT(clampr, SFX)((REAL)dt[row + d], (REAL)dt_min, (REAL)dt_max);
                 REAL acc = 0;
                 for (int n = 0; n < N; n++) {
-                    REAL abar = exp(dtc * -(REAL)(n + 1));
+                    REAL abar = exp(dtc * ORC_CAT(model_a, SFX)(A, d, n, N));
                     REAL bx = mean * (REAL)Bm[bc + n] * (REAL)x[row + d];
                     h[(size_t)d * N + n] = abar * h[(size_t)d * N + n] + bx;
                     acc += (REAL)Cm[bc + n] * h[(size_t)d * N + n];
@@ -283,6 +291,82 @@ void FN(selective_scan_model_fwd)(const float* x, const float* dt, const float* 
             }
         }
         free(h);
+    }
+}
+
+/* Backward of the model semantics: the gradient Nx's autodiff takes through
+ * discretize_ssm -> sequential_scan -> compute_ssm_output (common.ex:402-515).
+ * With m = mean_d(clip(dt)):
+ *   dh_tot = dh + dy C;  gC += dy h;  gx = m sum_n dh_tot B;
+ *   gB = m sum_d dh_tot x;  g_m = sum_{d,n} dh_tot B x;
+ *   gdt = [dt in range] (sum_n dh_tot h_prev abar A + g_m / D);  dh = dh_tot abar.
+ * A receives no gradient.  Keeps every state of a batch row (small cases). */
+void FN(selective_scan_model_bwd)(const float* x, const float* dt, const float* A,
+                                  const float* Bm, const float* Cm, const float* dy, float* gx,
+                                  float* gdt, float* gB, float* gC, int B, int L, int D, int N,
+                                  float dt_min, float dt_max) {
+    #pragma omp parallel for schedule(dynamic)
+    for (int b = 0; b < B; b++) {
+        REAL* hs = (REAL*)malloc((size_t)(L + 1) * D * N * sizeof(REAL));
+        REAL* mean = (REAL*)malloc((size_t)L * sizeof(REAL));
+        REAL* dh = (REAL*)malloc((size_t)D * N * sizeof(REAL));
+        REAL* gdir = (REAL*)malloc((size_t)D * sizeof(REAL));
+        for (size_t i = 0; i < (size_t)D * N; i++) hs[i] = 0;
+        for (int t = 0; t < L; t++) {
+            size_t row = ((size_t)b * L + t) * D, bc = ((size_t)b * L + t) * N;
+            REAL m = 0;
+            for (int d = 0; d < D; d++)
+                m += ORC_CAT(clampr, SFX)((REAL)dt[row + d], (REAL)dt_min, (REAL)dt_max);
+            m /= (REAL)D;
+            mean[t] = m;
+            REAL* hp = hs + (size_t)t * D * N;
+            REAL* hn = hp + (size_t)D * N;
+            for (int d = 0; d < D; d++) {
+                REAL dtc = ORC_CAT(clampr, SFX)((REAL)dt[row + d], (REAL)dt_min, (REAL)dt_max);
+                for (int n = 0; n < N; n++)
+                    hn[(size_t)d * N + n] =
+                        exp(dtc * ORC_CAT(model_a, SFX)(A, d, n, N)) * hp[(size_t)d * N + n] +
+                        m * (REAL)Bm[bc + n] * (REAL)x[row + d];
+            }
+        }
+        for (size_t i = 0; i < (size_t)D * N; i++) dh[i] = 0;
+        for (int t = L - 1; t >= 0; t--) {
+            size_t row = ((size_t)b * L + t) * D, bc = ((size_t)b * L + t) * N;
+            const REAL* hp = hs + (size_t)t * D * N;
+            const REAL* hc = hp + (size_t)D * N;
+            REAL m = mean[t], gm = 0;
+            for (int n = 0; n < N; n++) {
+                REAL pb = 0, pc = 0;
+                for (int d = 0; d < D; d++) {
+                    REAL dtot = dh[(size_t)d * N + n] + (REAL)dy[row + d] * (REAL)Cm[bc + n];
+                    pc += (REAL)dy[row + d] * hc[(size_t)d * N + n];
+                    pb += dtot * (REAL)x[row + d];
+                }
+                gB[bc + n] = (float)(m * pb);
+                gC[bc + n] = (float)pc;
+                gm += pb * (REAL)Bm[bc + n];
+            }
+            for (int d = 0; d < D; d++) {
+                REAL dtc = ORC_CAT(clampr, SFX)((REAL)dt[row + d], (REAL)dt_min, (REAL)dt_max);
+                REAL gxv = 0, gdv = 0;
+                for (int n = 0; n < N; n++) {
+                    REAL a = ORC_CAT(model_a, SFX)(A, d, n, N);
+                    REAL abar = exp(dtc * a);
+                    REAL dtot = dh[(size_t)d * N + n] + (REAL)dy[row + d] * (REAL)Cm[bc + n];
+                    gxv += dtot * m * (REAL)Bm[bc + n];
+                    gdv += dtot * hp[(size_t)d * N + n] * abar * a;
+                    dh[(size_t)d * N + n] = dtot * abar;
+                }
+                gdir[d] = gdv;
+                gx[row + d] = (float)gxv;
+            }
+            for (int d = 0; d < D; d++) {
+                REAL draw = (REAL)dt[row + d];
+                int inr = draw >= (REAL)dt_min && draw <= (REAL)dt_max;
+                gdt[row + d] = inr ? (float)(gdir[d] + gm / (REAL)D) : 0.0f;
+            }
+        }
+        free(hs); free(mean); free(dh); free(gdir);
     }
 }
 

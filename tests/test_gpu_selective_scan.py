@@ -163,3 +163,72 @@ def test_autograd_fn(cuda):
     ref = O.selective_scan_bwd(*[_np(t) for t in (x, dt, A, Bm, Cm)], _np(dy))
     for leaf, r in zip(leaves, ref):
         assert O.norm_rel(_np(leaf.grad), r) <= 1e-4
+
+
+# ------------------------------------------------------------ model semantics
+@pytest.mark.parametrize("layer", [0, 1])
+def test_model_semantics_golden(cuda, layer):
+    """Edifice.build(:mamba)'s SSM core against the reference's own fixture
+    (test/fixtures/numerical/mamba_random.safetensors replayed through the
+    reference generator's model; tests/golden/make_golden.py), atol 1e-4 as
+    architecture_numerical_test.exs:363-423 checks it."""
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "mamba_fixture.npz"))
+    x, dt, Bm, Cm = (torch.tensor(g["%s%d" % (n, layer)]).cuda() for n in ("x", "dt", "B", "C"))
+    y, _ = fs.selective_scan_model(x, dt, Bm, Cm)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(_np(y), g["y%d" % layer], atol=1e-4)
+    assert O.norm_rel(_np(y), g["y%d" % layer]) <= 1e-4
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("case", CASES)
+@pytest.mark.parametrize("use_ckpt", [False, True])
+@pytest.mark.parametrize("given_a", [False, True])
+def test_model_semantics_parity(cuda, dtype, case, use_ckpt, given_a):
+    x, dt, A, Bm, Cm, dy = ssm_inputs(*case, dtype, seed=31)
+    a = A if given_a else None
+    if use_ckpt:
+        y, dtm, ck = fs.selective_scan_model(x, dt, Bm, Cm, a=a, with_ckpt=True)
+    else:
+        (y, dtm), ck = fs.selective_scan_model(x, dt, Bm, Cm, a=a), None
+    gx, gdt, gB, gC = fs.selective_scan_model_backward(x, dt, Bm, Cm, dy, dtm, a=a, h_ckpt=ck)
+    torch.cuda.synchronize()
+    an = _np(A) if given_a else None
+    args = [_np(t) for t in (x, dt, Bm, Cm)]
+    dtc = np.clip(args[1], O.DT_MIN, O.DT_MAX).astype(np.float64)
+    assert O.norm_rel(_np(dtm), dtc.mean(2)) <= 1e-6
+    assert O.norm_rel(_np(y), O.selective_scan_model_fwd(*args, A=an)) <= TOL[dtype]
+    ref = O.selective_scan_model_bwd(*args, _np(dy), A=an)
+    for name, got, r in zip(("gx", "gdt", "gB", "gC"), (gx, gdt, gB, gC), ref):
+        assert O.norm_rel(_np(got), r) <= TOL[dtype], (name, O.norm_rel(_np(got), r))
+    dtn = _np(dt)
+    mask = (dtn < 0.001) | (dtn > 0.1)
+    assert np.all(_np(gdt)[mask] == 0)
+    assert device_errors() == 0
+
+
+def test_model_semantics_fixed_a_is_the_default(cuda):
+    """A = None and the explicit fixed -(1..N) matrix (what mamba.ex:187-193
+    passes to the fused path) give identical results."""
+    x, dt, A, Bm, Cm, dy = ssm_inputs(2, 300, 256, 16, torch.bfloat16, seed=5)
+    D, N = A.shape
+    fixed = (-(torch.arange(N, dtype=torch.float32) + 1)).expand(D, N).contiguous()
+    fixed = fixed.to(torch.bfloat16).cuda()
+    y0, m0 = fs.selective_scan_model(x, dt, Bm, Cm)
+    y1, m1 = fs.selective_scan_model(x, dt, Bm, Cm, a=fixed)
+    torch.cuda.synchronize()
+    assert torch.equal(y0, y1) and torch.equal(m0, m1)
+    g0 = fs.selective_scan_model_backward(x, dt, Bm, Cm, dy, m0)
+    g1 = fs.selective_scan_model_backward(x, dt, Bm, Cm, dy, m1, a=fixed)
+    for u, v in zip(g0, g1):
+        assert torch.equal(u, v)
+
+
+def test_model_semantics_autograd_fn(cuda):
+    x, dt, A, Bm, Cm, dy = ssm_inputs(2, 130, 192, 16, torch.float32, seed=8)
+    leaves = [t.clone().requires_grad_(True) for t in (x, dt, Bm, Cm)]
+    y = fs.SelectiveScanModelFn.apply(*leaves)
+    y.backward(dy)
+    ref = O.selective_scan_model_bwd(*[_np(t) for t in (x, dt, Bm, Cm)], _np(dy))
+    for leaf, r in zip(leaves, ref):
+        assert O.norm_rel(_np(leaf.grad), r) <= 1e-4

@@ -156,6 +156,59 @@ def test_selective_scan_kernel_semantics_autograd():
     np.testing.assert_allclose(gC, tC.grad.numpy(), rtol=1e-5, atol=1e-6)
 
 
+def _ssm_model_torch(x, dt, A, Bm, Cm, lo=O.DT_MIN, hi=O.DT_MAX):
+    """discretize_ssm + sequential_scan + compute_ssm_output (common.ex:402-515)
+    written in torch f64; A None is the fixed -(1..N) diagonal."""
+    D, N = x.shape[2], Bm.shape[2]
+    if A is None:
+        A = -(torch.arange(N, dtype=torch.float64) + 1).expand(D, N)
+    dtc = dt.clamp(lo, hi)
+    mean = dtc.mean(2, keepdim=True)
+    abar = torch.exp(dtc[..., None] * A)
+    bx = (mean * x)[..., None] * Bm[:, :, None, :]
+    h = torch.zeros(x.shape[0], D, N, dtype=torch.float64)
+    ys = []
+    for t in range(x.shape[1]):
+        h = abar[:, t] * h + bx[:, t]
+        ys.append((h * Cm[:, t, None, :]).sum(-1))
+    return torch.stack(ys, 1)
+
+
+@pytest.mark.parametrize("given_a", [False, True])
+def test_selective_scan_model_semantics_autograd(given_a):
+    """Model semantics (Edifice.build(:mamba) fallback): forward against a torch
+    restatement and the golden-pinned oracle forward, backward against its
+    autograd (A gets no gradient; gdt masked outside the clamp, and it carries
+    the channel-mean term of B_bar)."""
+    rng = np.random.default_rng(5)
+    Bsz, L, D, N = 2, 11, 7, 5
+    x = rng.standard_normal((Bsz, L, D)).astype(np.float32)
+    dt = np.log1p(np.exp(rng.standard_normal((Bsz, L, D)) * 0.5 - 2)).astype(np.float32)
+    dt[0, 3, 2] = 0.5
+    dt[1, 5, 1] = 0.0005
+    A = (-np.exp(rng.uniform(0, np.log(16), (D, N)))).astype(np.float32) if given_a else None
+    Bm = rng.standard_normal((Bsz, L, N)).astype(np.float32)
+    Cm = rng.standard_normal((Bsz, L, N)).astype(np.float32)
+    dy = rng.standard_normal((Bsz, L, D)).astype(np.float32)
+    tx, tdt, tB, tC = _t(x), _t(dt), _t(Bm), _t(Cm)
+    tA = None if A is None else torch.tensor(A, dtype=torch.float64)
+    y = _ssm_model_torch(tx, tdt, tA, tB, tC)
+    np.testing.assert_allclose(O.selective_scan_model_fwd(x, dt, Bm, Cm, A=A),
+                               y.detach().numpy(), rtol=1e-5, atol=1e-6)
+    y.backward(torch.tensor(dy, dtype=torch.float64))
+    gx, gdt, gB, gC = O.selective_scan_model_bwd(x, dt, Bm, Cm, dy, A=A)
+    np.testing.assert_allclose(gx, tx.grad.numpy(), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(gdt, tdt.grad.numpy(), rtol=1e-5, atol=1e-6)
+    assert gdt[0, 3, 2] == 0 and gdt[1, 5, 1] == 0
+    np.testing.assert_allclose(gB, tB.grad.numpy(), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(gC, tC.grad.numpy(), rtol=1e-5, atol=1e-6)
+    if not given_a:
+        # the fixed diagonal passed explicitly gives the same numbers
+        fixed = np.broadcast_to(-(np.arange(N, dtype=np.float32) + 1), (D, N))
+        np.testing.assert_array_equal(O.selective_scan_model_fwd(x, dt, Bm, Cm, A=fixed),
+                                      O.selective_scan_model_fwd(x, dt, Bm, Cm))
+
+
 @pytest.mark.parametrize("scalar_beta", [False, True])
 def test_delta_net_bwd_autograd(scalar_beta):
     rng = np.random.default_rng(5)
