@@ -24,6 +24,7 @@ SIGNATURES = {
     "edb_linear_scan_bwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "edb_mingru_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "edb_mingru_bwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "edb_native_rec_fwd": (_i, [_i, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "edb_scan_train_host_workspace": (_sz, [_i, _i, _i, _i]),
     "edb_linear_scan_train_host": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i,
                                         _vp, _sz, _vp]),
@@ -62,6 +63,7 @@ SIGNATURES = {
 }
 
 EDB_F32, EDB_BF16 = 0, 1
+EDB_NATIVE_ELU_GRU, EDB_NATIVE_REAL_GRU, EDB_NATIVE_DIAG_LINEAR = 0, 1, 2
 
 _lib = None
 

@@ -34,7 +34,24 @@ namespace {
 
 constexpr int kThreads = 256;
 
-enum { OP_LINEAR = 0, OP_MINGRU = 1 };
+// OP_ELUGRU / OP_REALGRU / OP_DIAGLIN: the native-recurrence scans
+// (lib/edifice/recurrent/native_recurrence.ex:125-230), forward only, with the
+// activation applied to the raw inputs on load as native/cuda/fused_native_rec_scan.cu
+// does; their backwards are the MinGRU / linear ones on the activated values.
+enum { OP_LINEAR = 0, OP_MINGRU = 1, OP_ELUGRU = 2, OP_REALGRU = 3, OP_DIAGLIN = 4 };
+
+// logistic sigmoid from one ex2 and one reciprocal
+static __device__ __forceinline__ float sigmoid_fast(float x) {
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-1.4426950408889634f * x));
+    return __frcp_rn(1.0f + e);
+}
+// 1 + elu(x): x + 1 for x >= 0, exp(x) for x < 0
+static __device__ __forceinline__ float one_plus_elu(float x) {
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(1.4426950408889634f * fminf(x, 0.0f)));
+    return x >= 0.0f ? x + 1.0f : e;
+}
 
 template <int OP, bool BWD>
 struct StepMap;
@@ -52,6 +69,32 @@ struct StepMap<OP_MINGRU, false> {
     static __device__ __forceinline__ void map(float x0, float x1, float& A, float& B) {
         A = 1.0f - x0;
         B = x0 * x1;
+    }
+};
+// x0 = raw gate, x1 = raw candidate: z = sigmoid(x0), c = 1 + elu(x1)
+template <>
+struct StepMap<OP_ELUGRU, false> {
+    static __device__ __forceinline__ void map(float x0, float x1, float& A, float& B) {
+        const float z = sigmoid_fast(x0);
+        A = 1.0f - z;
+        B = z * one_plus_elu(x1);
+    }
+};
+// x0 = raw gate, x1 = candidate: z = sigmoid(x0)
+template <>
+struct StepMap<OP_REALGRU, false> {
+    static __device__ __forceinline__ void map(float x0, float x1, float& A, float& B) {
+        const float z = sigmoid_fast(x0);
+        A = 1.0f - z;
+        B = z * x1;
+    }
+};
+// x0 = raw a, x1 = b: h = sigmoid(a) h + b
+template <>
+struct StepMap<OP_DIAGLIN, false> {
+    static __device__ __forceinline__ void map(float x0, float x1, float& A, float& B) {
+        A = sigmoid_fast(x0);
+        B = x1;
     }
 };
 // backward: x0 = a | z, x1 = dY
@@ -486,6 +529,28 @@ extern "C" int edb_mingru_fwd(int dtype, const void* z, const void* c, const voi
     return dtype == EDB_BF16
                ? scan_fwd<__nv_bfloat16, OP_MINGRU>(z, c, h0, h, batch, seq_len, hidden, s)
                : scan_fwd<float, OP_MINGRU>(z, c, h0, h, batch, seq_len, hidden, s);
+}
+
+extern "C" int edb_native_rec_fwd(int kind, int dtype, const void* x0, const void* x1,
+                                  const void* h0, void* h, int batch, int seq_len, int hidden,
+                                  void* stream) {
+    if (int st = check_common(dtype, batch, seq_len, hidden)) return st;
+    if (!x0 || !x1 || !h) return EDB_ERR_NULL_POINTER;
+    cudaStream_t s = (cudaStream_t)stream;
+    const bool bf = dtype == EDB_BF16;
+    switch (kind) {
+        case EDB_NATIVE_ELU_GRU:
+            return bf ? scan_fwd<__nv_bfloat16, OP_ELUGRU>(x0, x1, h0, h, batch, seq_len, hidden, s)
+                      : scan_fwd<float, OP_ELUGRU>(x0, x1, h0, h, batch, seq_len, hidden, s);
+        case EDB_NATIVE_REAL_GRU:
+            return bf ? scan_fwd<__nv_bfloat16, OP_REALGRU>(x0, x1, h0, h, batch, seq_len, hidden, s)
+                      : scan_fwd<float, OP_REALGRU>(x0, x1, h0, h, batch, seq_len, hidden, s);
+        case EDB_NATIVE_DIAG_LINEAR:
+            return bf ? scan_fwd<__nv_bfloat16, OP_DIAGLIN>(x0, x1, h0, h, batch, seq_len, hidden, s)
+                      : scan_fwd<float, OP_DIAGLIN>(x0, x1, h0, h, batch, seq_len, hidden, s);
+        default:
+            return EDB_ERR_UNSUPPORTED;
+    }
 }
 
 extern "C" int edb_mingru_bwd(int dtype, const void* z, const void* c, const void* h0,

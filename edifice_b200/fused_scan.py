@@ -142,6 +142,94 @@ class MinGRUFn(torch.autograd.Function):
         return gz * z * (1 - z), gc
 
 
+# ------------------------------------------------- native-recurrence scans
+def _native_rec(kind, x0, x1, h0, what):
+    _dev(x0, x1, h0, what=what)
+    _same(x0.shape, x1.shape, what)
+    B, L, H = x0.shape
+    out = torch.empty_like(x0)
+    lib = _lib.load()
+    _lib.check(lib.edb_native_rec_fwd(kind, _dtype_code(x0, what), _p(x0), _p(x1), _p(h0),
+                                      _p(out), B, L, H, _stream()), "CUDA fused %s" % what)
+    return out
+
+
+def elu_gru(gates, candidates, h0=None):
+    """FusedScan.elu_gru/2 (fused_scan.ex:94-108; NativeRecurrence.elu_gru_scan,
+    native_recurrence.ex:146-172): z = sigmoid(gates), c = 1 + elu(candidates),
+    h = (1 - z) h + z c, activations inside the kernel."""
+    return _native_rec(_lib.EDB_NATIVE_ELU_GRU, gates, candidates, h0, "elu_gru")
+
+
+def real_gru(gates, candidates, h0=None):
+    """FusedScan.real_gru/2 (fused_scan.ex:111-125; native_recurrence.ex:193-213):
+    z = sigmoid(gates), h = (1 - z) h + z candidates."""
+    return _native_rec(_lib.EDB_NATIVE_REAL_GRU, gates, candidates, h0, "real_gru")
+
+
+def diag_linear(a_vals, b_vals, h0=None):
+    """FusedScan.diag_linear/2 (fused_scan.ex:128-142; native_recurrence.ex:232-250):
+    h = sigmoid(a_vals) h + b_vals."""
+    return _native_rec(_lib.EDB_NATIVE_DIAG_LINEAR, a_vals, b_vals, h0, "diag_linear")
+
+
+class EluGRUFn(torch.autograd.Function):
+    """custom_grad wiring of elu_gru_custom_call (fused_scan.ex:679-706): the
+    MinGRU backward on z = sigmoid(gates), c = 1 + elu(candidates), then the
+    sigmoid and elu chain rules (elu'(x) = 1 for x > 0, exp(x) otherwise)."""
+
+    @staticmethod
+    def forward(ctx, gates, candidates):
+        out = elu_gru(gates, candidates)
+        ctx.save_for_backward(gates, candidates, out)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        gates, cand, out = ctx.saved_tensors
+        z = torch.sigmoid(gates)
+        c_act = 1.0 + torch.where(cand > 0, cand, torch.expm1(cand))
+        gz, gc, _ = mingru_backward(z, c_act, None, out, grad_output.contiguous())
+        elu_d = torch.where(cand > 0, torch.ones_like(cand), torch.exp(cand))
+        return gz * z * (1 - z), gc * elu_d
+
+
+class RealGRUFn(torch.autograd.Function):
+    """custom_grad wiring of real_gru (the MinGRU backward, fused_scan.ex:995-998,
+    and the sigmoid chain rule)."""
+
+    @staticmethod
+    def forward(ctx, gates, candidates):
+        out = real_gru(gates, candidates)
+        ctx.save_for_backward(gates, candidates, out)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        gates, cand, out = ctx.saved_tensors
+        z = torch.sigmoid(gates)
+        gz, gc, _ = mingru_backward(z, cand, None, out, grad_output.contiguous())
+        return gz * z * (1 - z), gc
+
+
+class DiagLinearFn(torch.autograd.Function):
+    """custom_grad wiring of diag_linear (the linear-scan backward on
+    a = sigmoid(a_vals), fused_scan.ex:1019-1023, and the sigmoid chain rule)."""
+
+    @staticmethod
+    def forward(ctx, a_vals, b_vals):
+        out = diag_linear(a_vals, b_vals)
+        ctx.save_for_backward(a_vals, out)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        a_vals, out = ctx.saved_tensors
+        a = torch.sigmoid(a_vals)
+        ga, gb, _ = linear_scan_backward(a, None, out, grad_output.contiguous())
+        return ga * a * (1 - a), gb
+
+
 # --------------------------------------------- scans over host-resident tensors
 _HOST_WS = {}
 

@@ -52,6 +52,53 @@ int fused_mingru_scan_backward_launch(cudaStream_t stream, const edb_io_t* z,
                           stream);
 }
 
+int fused_elu_gru_scan_launch(cudaStream_t stream, const edb_io_t* gates,
+                              const edb_io_t* candidates, const edb_io_t* h0, edb_io_t* output,
+                              int batch, int seq_len, int hidden) {
+    return edb_native_rec_fwd(EDB_NATIVE_ELU_GRU, kDtype, gates, candidates, h0, output, batch,
+                              seq_len, hidden, stream);
+}
+
+int fused_real_gru_scan_launch(cudaStream_t stream, const edb_io_t* gates,
+                               const edb_io_t* candidates, const edb_io_t* h0, edb_io_t* output,
+                               int batch, int seq_len, int hidden) {
+    return edb_native_rec_fwd(EDB_NATIVE_REAL_GRU, kDtype, gates, candidates, h0, output, batch,
+                              seq_len, hidden, stream);
+}
+
+int fused_diag_linear_scan_launch(cudaStream_t stream, const edb_io_t* a_vals,
+                                  const edb_io_t* b_vals, const edb_io_t* h0, edb_io_t* output,
+                                  int batch, int seq_len, int hidden) {
+    return edb_native_rec_fwd(EDB_NATIVE_DIAG_LINEAR, kDtype, a_vals, b_vals, h0, output, batch,
+                              seq_len, hidden, stream);
+}
+
+// the three backwards are the MinGRU / linear-scan backwards on activated values
+int fused_elu_gru_scan_backward_launch(cudaStream_t stream, const edb_io_t* z, const edb_io_t* c,
+                                       const edb_io_t* h0, const edb_io_t* forward_out,
+                                       const edb_io_t* grad_output, edb_io_t* output_concat,
+                                       int batch, int seq_len, int hidden) {
+    return fused_mingru_scan_backward_launch(stream, z, c, h0, forward_out, grad_output,
+                                             output_concat, batch, seq_len, hidden);
+}
+
+int fused_real_gru_scan_backward_launch(cudaStream_t stream, const edb_io_t* z,
+                                        const edb_io_t* candidates, const edb_io_t* h0,
+                                        const edb_io_t* forward_out, const edb_io_t* grad_output,
+                                        edb_io_t* output_concat, int batch, int seq_len,
+                                        int hidden) {
+    return fused_mingru_scan_backward_launch(stream, z, candidates, h0, forward_out, grad_output,
+                                             output_concat, batch, seq_len, hidden);
+}
+
+int fused_diag_linear_scan_backward_launch(cudaStream_t stream, const edb_io_t* a,
+                                           const edb_io_t* h0, const edb_io_t* forward_out,
+                                           const edb_io_t* grad_output, edb_io_t* output_concat,
+                                           int batch, int seq_len, int hidden) {
+    return fused_linear_scan_backward_launch(stream, a, h0, forward_out, grad_output,
+                                             output_concat, batch, seq_len, hidden);
+}
+
 int fused_selective_scan_launch(cudaStream_t stream, const edb_io_t* x, const edb_io_t* dt,
                                 const edb_io_t* A, const edb_io_t* B, const edb_io_t* C,
                                 edb_io_t* out, int batch, int seq_len, int hidden, int state) {

@@ -99,6 +99,24 @@ int edb_mingru_bwd(int dtype, const void* z, const void* c, const void* h0, cons
                    int hidden, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Native-recurrence scans (lib/edifice/recurrent/native_recurrence.ex:125-230),
+ * forward, activations applied to the raw inputs inside the kernel:
+ *   EDB_NATIVE_ELU_GRU:    z = sigmoid(x0), c = 1 + elu(x1), h = (1 - z) h + z c
+ *   EDB_NATIVE_REAL_GRU:   z = sigmoid(x0), h = (1 - z) h + z x1
+ *   EDB_NATIVE_DIAG_LINEAR: h = sigmoid(x0) h + x1
+ * x0, x1, h: [batch, seq_len, hidden]; h0: [batch, hidden] or NULL (zeros).
+ * Replaces fused_{elu_gru,real_gru,diag_linear}_scan_launch
+ * (native/cuda/fused_native_rec_scan.cu:142-198).  Their backwards
+ * (fused_{elu_gru,real_gru}_scan_backward.cu, fused_diag_linear_scan_backward.cu;
+ * fused_scan.ex:941-1023) take the activated values and are edb_mingru_bwd
+ * (z, c) and edb_linear_scan_bwd (a = sigmoid(x0)).
+ * ---------------------------------------------------------------------- */
+enum { EDB_NATIVE_ELU_GRU = 0, EDB_NATIVE_REAL_GRU = 1, EDB_NATIVE_DIAG_LINEAR = 2 };
+
+int edb_native_rec_fwd(int kind, int dtype, const void* x0, const void* x1, const void* h0,
+                       void* h, int batch, int seq_len, int hidden, void* stream);
+
+/* ------------------------------------------------------------------------
  * Forward + backward of the linear scan / MinGRU over HOST tensors.
  * a, b (z, c), dy, and the outputs h, ga, gb (gz, gc): [batch, seq_len, hidden]
  * in host memory; h0 / gh0: [batch, hidden] host or NULL (h0 = NULL: zeros;

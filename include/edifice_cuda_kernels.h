@@ -50,6 +50,37 @@ int fused_mingru_scan_backward_launch(cudaStream_t stream, const edb_io_t* z,
                                       edb_io_t* output_concat, int batch, int seq_len,
                                       int hidden);
 
+/* native/cuda/fused_native_rec_scan.cu:142-198: raw gates / candidates / a,
+ * activations applied in the kernel */
+int fused_elu_gru_scan_launch(cudaStream_t stream, const edb_io_t* gates,
+                              const edb_io_t* candidates, const edb_io_t* h0, edb_io_t* output,
+                              int batch, int seq_len, int hidden);
+int fused_real_gru_scan_launch(cudaStream_t stream, const edb_io_t* gates,
+                               const edb_io_t* candidates, const edb_io_t* h0, edb_io_t* output,
+                               int batch, int seq_len, int hidden);
+int fused_diag_linear_scan_launch(cudaStream_t stream, const edb_io_t* a_vals,
+                                  const edb_io_t* b_vals, const edb_io_t* h0, edb_io_t* output,
+                                  int batch, int seq_len, int hidden);
+
+/* native/cuda/fused_elu_gru_scan_backward.cu:97-127, fused_real_gru_scan_backward.cu:94-124
+ * (post-activation z, c); output_concat = [gz | gc | gh0] */
+int fused_elu_gru_scan_backward_launch(cudaStream_t stream, const edb_io_t* z, const edb_io_t* c,
+                                       const edb_io_t* h0, const edb_io_t* forward_out,
+                                       const edb_io_t* grad_output, edb_io_t* output_concat,
+                                       int batch, int seq_len, int hidden);
+int fused_real_gru_scan_backward_launch(cudaStream_t stream, const edb_io_t* z,
+                                        const edb_io_t* candidates, const edb_io_t* h0,
+                                        const edb_io_t* forward_out, const edb_io_t* grad_output,
+                                        edb_io_t* output_concat, int batch, int seq_len,
+                                        int hidden);
+
+/* native/cuda/fused_diag_linear_scan_backward.cu:90-120 (post-sigmoid a);
+ * output_concat = [ga | gb | gh0] */
+int fused_diag_linear_scan_backward_launch(cudaStream_t stream, const edb_io_t* a,
+                                           const edb_io_t* h0, const edb_io_t* forward_out,
+                                           const edb_io_t* grad_output, edb_io_t* output_concat,
+                                           int batch, int seq_len, int hidden);
+
 /* native/cuda/fused_selective_scan.cu:105-124 (dt clamp [0.001, 0.1]) */
 int fused_selective_scan_launch(cudaStream_t stream, const edb_io_t* x, const edb_io_t* dt,
                                 const edb_io_t* A, const edb_io_t* B, const edb_io_t* C,

@@ -105,6 +105,34 @@ def mingru_bwd(z, c, h0, fwd, dy, prec="f64"):
     return gz, gc, gh0
 
 
+# ------------------------------------------ native-recurrence scans
+# lib/edifice/recurrent/native_recurrence.ex: elu_gru_scan :146-172 (z = sigmoid(g),
+# c = 1 + elu(x)), real_gru_scan :193-213 (z = sigmoid(g)), diag_linear_scan
+# :232-250 (a = sigmoid(a_pre)).  The activations are taken in f64 and the
+# recurrences run through the MinGRU / linear-scan restatements above (the
+# activated values are rounded to f32 on the way, ~6e-8 relative).
+def sigmoid64(x):
+    x = np.asarray(x, np.float64)
+    return 1.0 / (1.0 + np.exp(-x))
+
+
+def one_plus_elu64(x):
+    x = np.asarray(x, np.float64)
+    return 1.0 + np.where(x > 0, x, np.expm1(np.minimum(x, 0.0)))
+
+
+def elu_gru_fwd(gates, cand, h0=None, prec="f64"):
+    return mingru_fwd(sigmoid64(gates), one_plus_elu64(cand), h0, prec)
+
+
+def real_gru_fwd(gates, cand, h0=None, prec="f64"):
+    return mingru_fwd(sigmoid64(gates), cand, h0, prec)
+
+
+def diag_linear_fwd(a_pre, b, h0=None, prec="f64"):
+    return linear_scan_fwd(sigmoid64(a_pre), b, h0, prec)
+
+
 # ------------------------------------------------------- selective scan
 DT_MIN, DT_MAX = 0.001, 0.1
 

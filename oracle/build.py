@@ -53,6 +53,8 @@ _REF_HOT = [
     "fused_selective_scan.cu", "fused_selective_scan_backward.cu",
     "fused_delta_rule_scan.cu", "fused_delta_rule_scan_backward.cu",
     "fused_flash_attention.cu", "fused_flash_attention_backward.cu",
+    "fused_native_rec_scan.cu", "fused_elu_gru_scan_backward.cu",
+    "fused_real_gru_scan_backward.cu", "fused_diag_linear_scan_backward.cu",
 ]
 
 NVCC = os.environ.get("NVCC", "nvcc")
@@ -101,7 +103,8 @@ def build_ref(force=False):
     built.append(REF_CPU_SO)
     hot = [os.path.join(REF_CUDA, f) for f in _REF_HOT]
     for prec, out in REF_KERNELS_SO.items():
-        if force or not _newer(out, hot):
+        # this file lists the sources, so a change here rebuilds too
+        if force or not _newer(out, hot + [os.path.abspath(__file__)]):
             extra = ["-DUSE_BF16"] if prec == "bf16" else []
             _run([NVCC, *ARCH, "-O3", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
                   "-I", REF_CUDA, *extra, *hot, "-o", out])
