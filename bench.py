@@ -49,6 +49,9 @@ def parse():
                                          "gated"],
                     default="linear")
     ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--replicate", action="store_true",
+                    help="N>1: also time the optional all-gather of the forward output "
+                         "(a replicated output; never part of the kernel path)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-paths", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
@@ -224,6 +227,9 @@ class ScanWorkload:
 
     def host_inputs(self):
         return [self.a, self.b, self.dy]
+
+    def forward_output(self):
+        return self._fwd(self.a, self.b)
 
     def e2e_host_shapes(self):
         B, L, H = self.a.shape
@@ -800,6 +806,31 @@ def run_ours(args):
                "ms_per_step": el2 / args.e2e_steps, "steps": args.e2e_steps, "api": wl.api}
         del pin, dev_in, outs_host
 
+    # ---- optional replicated output (N > 1): all-gather of the forward output,
+    # timed on its own; every rank takes the same collective steps
+    replicate = None
+    if args.replicate and world > 1 and hasattr(wl, "forward_output"):
+        from edifice_b200 import shard
+        h = wl.forward_output()
+        shard.all_gather_units(h)
+        torch.cuda.synchronize()
+        dist.barrier()
+        reps = 10
+        s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s3.record()
+        for _ in range(reps):
+            shard.all_gather_units(h)
+        e3.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([s3.elapsed_time(e3) / reps], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+        total = world * h.numel() * h.element_size()
+        replicate = {"what": "all-gather of the forward output along the batch (NCCL)",
+                     "bytes_gathered_per_rank": total, "ms": ms,
+                     "bus_GB/s": (world - 1) / world * total / (ms / 1e3) / 1e9}
+        del h
+
     # ---- other paths (same process, smaller step count)
     paths = {}
     if args.config == "linear" and not args.no_paths:
@@ -847,6 +878,8 @@ def run_ours(args):
     }
     if hasattr(wl, "extra"):
         line.update(wl.extra(kern_ms["fwd"], kern_ms["bwd"]))
+    if replicate:
+        line["replicate"] = replicate
     if paths:
         line["paths"] = paths
     print(json.dumps(line), flush=True)

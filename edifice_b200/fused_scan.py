@@ -602,6 +602,60 @@ class FlashAttentionFn(torch.autograd.Function):
         return dq, dk, dv, None
 
 
+# ------------------------------------------- attention callers routed to flash
+def _attend(q, k, v, causal):
+    """[B, H, L, d] attention through the flash kernel, with gradients when any
+    input requires them."""
+    if torch.is_grad_enabled() and any(t.requires_grad for t in (q, k, v)):
+        return FlashAttentionFn.apply(q, k, v, causal)
+    return flash_attention(q, k, v, causal=causal)
+
+
+def sdpa_compute(q, k, v, num_heads, head_dim, causal=False, num_kv_heads=None):
+    """Blocks.SDPA.compute/6 (lib/edifice/blocks/sdpa.ex:74-118) on the flash
+    kernel: q [B, L, num_heads * head_dim], k / v [B, L, num_kv_heads * head_dim]
+    (num_kv_heads defaults to num_heads) -> [B, L, num_heads * head_dim].  The
+    reference takes this branch for self-attention (equal lengths) and passes
+    causal = (mask != nil); K/V heads are grouped natively, never repeated."""
+    B, L, _ = q.shape
+    hkv = num_kv_heads or num_heads
+    if k.shape[1] != L or v.shape[1] != L:
+        raise _lib.EdbError("sdpa_compute: the flash path takes self-attention "
+                            "(equal query and key lengths)")
+    qh = q.reshape(B, L, num_heads, head_dim).transpose(1, 2).contiguous()
+    kh = k.reshape(B, L, hkv, head_dim).transpose(1, 2).contiguous()
+    vh = v.reshape(B, L, hkv, head_dim).transpose(1, 2).contiguous()
+    o = _attend(qh, kh, vh, causal)
+    return o.transpose(1, 2).reshape(B, L, num_heads * head_dim)
+
+
+def gqa_attention(q, k, v, num_heads, num_kv_heads, head_dim):
+    """GQA.gqa_attention_impl (lib/edifice/attention/gqa.ex:192-306, rope / yarn
+    off): causal grouped-query attention.  The reference repeats K/V to
+    num_heads and masks with -1e9; the kernel reads each K/V head once per group
+    and masks with -inf, which is identical here because every causal row keeps
+    its diagonal."""
+    if num_heads % num_kv_heads:
+        raise _lib.EdbError("gqa_attention: num_heads must be a multiple of num_kv_heads")
+    return sdpa_compute(q, k, v, num_heads, head_dim, causal=True, num_kv_heads=num_kv_heads)
+
+
+def multi_head_sdpa(query, key, value, mask=None):
+    """Primitives.multi_head_sdpa/4 (lib/edifice/attention/primitives.ex:307-341):
+    [B, H, L, d] in and out.  mask None is full attention; a [L, L] (or
+    broadcastable [B, H, L, L]) boolean mask equal to the causal lower triangle
+    runs the causal kernel (the reference's -1e9 fill equals -inf there).  Any
+    other mask has no kernel on this path and raises."""
+    causal = False
+    if mask is not None:
+        L = query.shape[2]
+        tri = torch.ones(L, L, dtype=torch.bool, device=mask.device).tril()
+        if not bool((mask.bool() == tri).all()):
+            raise _lib.EdbError("multi_head_sdpa: only a causal mask runs on the flash path")
+        causal = True
+    return _attend(query.contiguous(), key.contiguous(), value.contiguous(), causal)
+
+
 class SelectiveScanFn(torch.autograd.Function):
     """custom_grad wiring of selective_scan_custom_call/5 (fused_scan.ex:2595-2611):
     gradients to x, dt, B, C; A gets none."""

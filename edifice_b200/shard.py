@@ -270,6 +270,24 @@ def gated_alpha(cfg, units, device, base_seed=0):
     return alpha
 
 
+def all_gather_units(local, group=None):
+    """A replicated output, when the caller asks for one: every rank's shard
+    (dim 0 unit-major over its contiguous units, e.g. batch rows) gathered in rank
+    order along dim 0, so each rank holds the whole problem's tensor.  NCCL over
+    NVLink on GPUs, gloo on CPU.  The kernel path never calls it; it is the one
+    collective the sharded configs have, and it moves only outputs."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    local = local.contiguous()
+    out = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
+                      device=local.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, local, group=group)
+    else:
+        dist.all_gather(list(out.chunk(world)), local, group=group)
+    return out
+
+
 def ceil_div(a, b):
     return -(-a // b)
 

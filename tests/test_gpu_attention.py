@@ -230,3 +230,64 @@ def test_autograd_fn(cuda):
     ref = O.attention_bwd(_np(q), _np(k), _np(v), _np(do), causal=True)
     for leaf, r in zip(leaves, ref):
         assert O.norm_rel(_np(leaf.grad), r) <= 2e-2
+
+
+# ----------------------------------------- the reference's attention callers
+def _dense_reference(q, k, v, heads, kv_heads, d, causal):
+    """SDPA.compute / GQA.gqa_attention_impl as the reference writes them
+    (sdpa.ex:74-118, gqa.ex:192-306): reshape [B, L, H*d] -> [B, H, L, d], repeat
+    K/V over the group, scores / sqrt(d), -1e9 causal fill, softmax, P V; in f64."""
+    B, L, _ = q.shape
+    qh = q.double().reshape(B, L, heads, d).transpose(1, 2)
+    kh = k.double().reshape(B, L, kv_heads, d).transpose(1, 2)
+    vh = v.double().reshape(B, L, kv_heads, d).transpose(1, 2)
+    g = heads // kv_heads
+    kh = kh[:, :, None].expand(B, kv_heads, g, L, d).reshape(B, heads, L, d)
+    vh = vh[:, :, None].expand(B, kv_heads, g, L, d).reshape(B, heads, L, d)
+    s = qh @ kh.transpose(-1, -2) / d ** 0.5
+    if causal:
+        tri = torch.ones(L, L, dtype=torch.bool, device=q.device).tril()
+        s = torch.where(tri, s, torch.full_like(s, -1.0e9))
+    o = torch.softmax(s, -1) @ vh
+    return o.transpose(1, 2).reshape(B, L, heads * d)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("heads,kv_heads,d,L", [(8, 2, 128, 300), (4, 4, 64, 129), (4, 1, 96, 77)])
+def test_gqa_attention_routes_to_flash(cuda, dtype, heads, kv_heads, d, L):
+    """GQA.gqa_attention_impl's numbers (K/V repeated, -1e9 causal fill) from the
+    flash kernel with native grouped heads, forward and gradients."""
+    B = 2
+    g = torch.Generator(device="cpu").manual_seed(61)
+    q = torch.randn(B, L, heads * d, generator=g).to(dtype).cuda().requires_grad_(True)
+    k = torch.randn(B, L, kv_heads * d, generator=g).to(dtype).cuda().requires_grad_(True)
+    v = torch.randn(B, L, kv_heads * d, generator=g).to(dtype).cuda().requires_grad_(True)
+    do = torch.randn(B, L, heads * d, generator=g).to(dtype).cuda()
+    o = fs.gqa_attention(q, k, v, heads, kv_heads, d)
+    o.backward(do)
+    rq, rk, rv = (t.detach().double().requires_grad_(True) for t in (q, k, v))
+    ro = _dense_reference(rq, rk, rv, heads, kv_heads, d, causal=True)
+    ro.backward(do.double())
+    assert O.norm_rel(_np(o), _np(ro)) <= TOL[dtype]
+    for got, ref in ((q.grad, rq.grad), (k.grad, rk.grad), (v.grad, rv.grad)):
+        assert O.norm_rel(_np(got), _np(ref)) <= TOL[dtype]
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_sdpa_compute_and_multi_head_sdpa(cuda, causal):
+    """SDPA.compute/6 (causal = mask given) and Primitives.multi_head_sdpa/4
+    (mask None, or the causal lower triangle) against the dense formulation;
+    a non-causal mask is refused rather than silently ignored."""
+    B, L, H, d = 2, 200, 4, 128
+    g = torch.Generator(device="cpu").manual_seed(62)
+    q, k, v = (torch.randn(B, L, H * d, generator=g).to(torch.bfloat16).cuda() for _ in range(3))
+    o = fs.sdpa_compute(q, k, v, H, d, causal=causal)
+    ref = _dense_reference(q, k, v, H, H, d, causal)
+    assert O.norm_rel(_np(o), _np(ref)) <= 2e-2
+    qh, kh, vh = (t.reshape(B, L, H, d).transpose(1, 2) for t in (q, k, v))
+    mask = torch.ones(L, L, dtype=torch.bool, device="cuda").tril() if causal else None
+    oh = fs.multi_head_sdpa(qh, kh, vh, mask=mask)
+    assert O.norm_rel(_np(oh.transpose(1, 2).reshape(B, L, H * d)), _np(ref)) <= 2e-2
+    band = torch.ones(L, L, dtype=torch.bool, device="cuda").triu(-4).tril()
+    with pytest.raises(RuntimeError):
+        fs.multi_head_sdpa(qh, kh, vh, mask=band)

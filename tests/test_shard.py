@@ -94,6 +94,40 @@ def test_two_rank_gloo_plan_and_max_time(tmp_path):
                               torch.tensor([a[sl].double().sum(), b[sl].double().sum()]))
 
 
+def _gather_main(rank, world, port, out_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = shard.ScanConfig(batch=2, seq_len=16, hidden=32, dtype=torch.float32)
+        a, _, _ = shard.scan_inputs(cfg, shard.plan_units(cfg.batch, rank, world), "cpu")
+        dcfg = shard.DeltaConfig(batch=1, heads=2, seq_len=8, head_dim=16, dtype=torch.float32)
+        q = shard.delta_inputs(dcfg, shard.plan_units(dcfg.batch * dcfg.heads, rank, world),
+                               "cpu")[0]
+        ga = shard.all_gather_units(a)
+        gq = shard.all_gather_units(q)
+        if rank == 0:
+            torch.save({"a": ga, "q": gq}, out_path)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gloo_replicated_output(tmp_path):
+    """all_gather_units rebuilds the whole problem's tensor on every rank from the
+    ranks' unit shards (batch rows; (batch, head) units of whole batch rows)."""
+    world = 2
+    out = str(tmp_path / "g0.pt")
+    mp.spawn(_gather_main, args=(world, _free_port(), out), nprocs=world, join=True)
+    res = torch.load(out)
+    cfg = shard.ScanConfig(batch=2, seq_len=16, hidden=32, dtype=torch.float32)
+    a, _, _ = shard.scan_inputs(cfg, list(range(cfg.batch * world)), "cpu")
+    assert torch.equal(res["a"], a)
+    dcfg = shard.DeltaConfig(batch=1, heads=2, seq_len=8, head_dim=16, dtype=torch.float32)
+    q = shard.delta_inputs(dcfg, list(range(dcfg.batch * dcfg.heads * world)), "cpu")[0]
+    assert torch.equal(res["q"], q)
+
+
 def test_gated_alpha_per_unit():
     """GatedDeltaNet decays: in (0, 1), identical for a unit wherever it lands."""
     cfg = shard.DeltaConfig(batch=2, heads=2, seq_len=16, head_dim=8, dtype=torch.float32)
