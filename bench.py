@@ -46,7 +46,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["linear", "mingru", "ssm", "ssm_model", "attn", "delta",
-                                         "gated"],
+                                         "delta_model", "gated"],
                     default="linear")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--replicate", action="store_true",
@@ -136,11 +136,13 @@ class ClockSampler:
 # Special-function unit: 16 ex2 results per clock per SM (sm_100), 148 SMs,
 # clocks.max.sm 1965 MHz -> G ex2/s.  No measured figure exists for it.
 SFU_PEAK_GEXP = 16 * 148 * 1.965
+FP32_PEAK_TFLOPS = 128 * 2 * 148 * 1.965 / 1000.0
 
 
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     sfu = (SFU_PEAK_GEXP, "nominal (16 ex2/clk/SM x 148 SMs x 1965 MHz clocks.max.sm)")
+    fp32 = (FP32_PEAK_TFLOPS, "nominal (128 f32 FMA lanes/SM x 2 x 148 SMs x 1965 MHz)")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
@@ -148,13 +150,15 @@ def measured_peaks():
                 "tensor": (float(d["bf16_tflops_sustained"]),
                            "measured (MEASURED_PEAKS.json bf16_tflops_sustained: the kernel runs "
                            "back to back inside a seconds-long step loop)"),
-                "sfu": sfu}
+                "sfu": sfu, "fp32": fp32}
     return {"hbm": (6650.0, "fallback (6.65 TB/s pool measurement)"),
-            "tensor": (1400.0, "fallback (1.4 PFLOP/s sustained pool measurement)"), "sfu": sfu}
+            "tensor": (1400.0, "fallback (1.4 PFLOP/s sustained pool measurement)"), "sfu": sfu,
+            "fp32": fp32}
 
 
 # unit scale and name of each bound's rate
-RATE = {"hbm": (1e9, "GB/s"), "tensor": (1e12, "TFLOP/s"), "sfu": (1e9, "Gexp/s")}
+RATE = {"hbm": (1e9, "GB/s"), "tensor": (1e12, "TFLOP/s"), "sfu": (1e9, "Gexp/s"),
+        "fp32": (1e12, "TFLOP/s")}
 
 
 def ncu_traffic(kernel_key):
@@ -581,6 +585,75 @@ class DeltaWorkload:
                 "pair over 512 tokens, scaled by the head share")
 
 
+def recurrence_flops(cfg, gated, bwd):
+    """Algorithmic FLOPs of the token recurrence per step, per token and (b, h) in
+    units of d^2: forward r = S k (2), S <- alpha S + u k^T (2, +1 gated), o = S q (2);
+    backward dS += dO q^T (2), gq = S^T dO (2), r (2), dS k (2), gk (4),
+    dS <- alpha (dS - bd k^T) (2, +1 gated), galpha = <., S> (2, gated).  The
+    backward's forward recompute is not counted."""
+    per = (12 + (3 if gated else 0)) if bwd else (6 + (1 if gated else 0))
+    return per * cfg.head_dim ** 2 * cfg.batch * cfg.heads * cfg.seq_len
+
+
+class DeltaModelWorkload(DeltaWorkload):
+    """configs[2] shapes with the Edifice.build(:delta_net) form of beta: one gate
+    per (token, head, value row) (delta_net.ex:285-297), which runs the
+    row-parallel token recurrence (the chunked tensor-core form needs one beta per
+    token)."""
+
+    def __init__(self):
+        import dataclasses
+        super().__init__()
+        self.cfg = dataclasses.replace(self.cfg, name="delta_net_model_cfg2")
+        self.kname = "delta_rule_rows"
+
+    def describe(self, world):
+        d = super().describe(world)
+        d["workload"] = ("%s fwd+bwd (configs[2] shapes, per-element beta as "
+                         "Edifice.build(:delta_net))" % self.cfg.name)
+        d["beta"] = "one per (token, head, row) = sigmoid(N(0,1))"
+        return d
+
+    def setup(self, dev, rank):
+        import torch
+        super().setup(dev, rank)
+        g = torch.Generator(device=dev).manual_seed(1234 + rank)
+        self.beta = torch.sigmoid(torch.randn(self.q.shape, generator=g, device=dev)).to(
+            self.q.dtype)
+
+    def kernels(self):
+        return {"fwd": ("fp32", recurrence_flops(self.cfg, False, False)),
+                "bwd": ("fp32", recurrence_flops(self.cfg, False, True))}
+
+    launches_per_step = 3  # forward (writes the checkpoints), backward, row-sum reduce
+
+    def extra(self, fwd_ms, bwd_ms):
+        return {}
+
+    def cpu_step(self, rows=None, prec="f32"):
+        import numpy as np
+        import oracle as O
+        c = self.cfg
+        Ls = 512
+        if not hasattr(self, "_cpu_m"):
+            rng = np.random.default_rng(0)
+            q = rng.standard_normal((1, Ls, 1, c.head_dim), dtype=np.float32)
+            k = rng.standard_normal((1, Ls, 1, c.head_dim), dtype=np.float32)
+            k /= np.sqrt((k * k).sum(-1, keepdims=True) + 1e-6)
+            v = rng.standard_normal((1, Ls, 1, c.head_dim), dtype=np.float32)
+            beta = (1 / (1 + np.exp(-rng.standard_normal((1, Ls, 1, c.head_dim))))).astype(
+                np.float32)
+            do = rng.standard_normal((1, Ls, 1, c.head_dim), dtype=np.float32)
+            self._cpu_m = (q, k, v, beta, do)
+        q, k, v, beta, do = self._cpu_m
+        O.delta_net_fwd(q, k, v, beta, prec=prec)
+        O.delta_net_bwd(q, k, v, beta, do, prec=prec)
+        return Ls / c.heads
+
+    cpu_what = ("oracle f32 port (fused_scan.ex:2212-2236, 1257-1326; per-element beta) on "
+                "one (batch, head) pair over 512 tokens, scaled by the head share")
+
+
 class GatedDeltaWorkload(DeltaWorkload):
     """GatedDeltaNet (delta rule with a per-token decay alpha) fwd + bwd at the
     configs[2] shapes and distributions, alpha = mean of sigmoid(N(0,1)) gates over
@@ -605,12 +678,11 @@ class GatedDeltaWorkload(DeltaWorkload):
         self.alpha = shard.gated_alpha(self.cfg, self.units, dev)
 
     def kernels(self):
-        # serial token recurrence: against HBM with the algorithmic io bytes
-        a = self.alpha.numel() * self.alpha.element_size()
-        return {"fwd": ("hbm", self.cfg.bytes_fwd() + a),
-                "bwd": ("hbm", self.cfg.bytes_bwd() + 2 * a)}
+        # token recurrence on the f32 pipes: algorithmic FLOPs of the recurrence
+        return {"fwd": ("fp32", recurrence_flops(self.cfg, True, False)),
+                "bwd": ("fp32", recurrence_flops(self.cfg, True, True))}
 
-    launches_per_step = 2  # forward (writes the checkpoints), backward
+    launches_per_step = 3  # forward (writes the checkpoints), backward, row-sum reduce
 
     def step(self, ev=None):
         from edifice_b200 import fused_scan as fs
@@ -665,7 +737,7 @@ class GatedDeltaWorkload(DeltaWorkload):
 
 WORKLOADS = {"linear": lambda: ScanWorkload(False), "mingru": lambda: ScanWorkload(True),
              "ssm": SsmWorkload, "ssm_model": SsmModelWorkload, "attn": AttnWorkload,
-             "delta": DeltaWorkload,
+             "delta": DeltaWorkload, "delta_model": DeltaModelWorkload,
              "gated": GatedDeltaWorkload}
 
 
@@ -679,7 +751,8 @@ def roofline(wl, kern_ms):
     achieved = amount / (kern_ms[dom] / 1e3) / scale
     kname = "%s_%s" % (wl.kname, dom)
     amount_key = {"hbm": "algorithmic_bytes_per_launch", "tensor": "algorithmic_flops_per_launch",
-                  "sfu": "algorithmic_exps_per_launch"}[bound]
+                  "sfu": "algorithmic_exps_per_launch",
+                  "fp32": "algorithmic_flops_per_launch"}[bound]
     roof = {"bound": bound, "kernel": kname, "achieved": round(achieved, 2), "peak": peak,
             "unit": unit, "frac": round(achieved / peak, 4), "peak_source": src,
             amount_key: amount, "traffic": ncu_traffic(kname)}
@@ -836,7 +909,7 @@ def run_ours(args):
     if args.config == "linear" and not args.no_paths:
         del wl.a, wl.b, wl.dy
         torch.cuda.empty_cache()
-        for name in ("mingru", "attn", "delta", "gated", "ssm", "ssm_model"):
+        for name in ("mingru", "attn", "delta", "delta_model", "gated", "ssm", "ssm_model"):
             pw = WORKLOADS[name]()
             pw._world = world
             pw.setup(dev, rank)

@@ -19,22 +19,21 @@
 // dalpha_t = <dS_d, S_{t-1}> and dS_{t-1} = alpha_t dS_d.
 //
 // This file is the general path (any d <= 128, either beta form, f32 or bf16
-// io): one CTA per (b, h) holding S (and dS) in shared memory as f32, token
-// order.  The forward can write S at the start of every CK-token chunk (plus
-// the final state); the delta-rule backward walks chunks in reverse, recomputes
-// each chunk's retrievals r_t from its checkpoint, and undoes the updates
-// (S_{t-1} = S_t - u_t k_t^T with the stored r_t) instead of storing every state.
-// The gated backward cannot undo an update (that divides by alpha_t, which
-// amplifies rounding by 1/alpha per token): it recomputes each chunk's states
-// S_{t-1} forward from the checkpoint into a global buffer and reads them back
-// in reverse.
+// io; the chunked tensor-core form in delta_chunked*.cu takes bf16, d = 128 and
+// one beta per token of the ungated rule).  Forward and backward are
+// row-parallel: each row of S (and of dS) evolves on its own, so a row lives in
+// the registers of 4 lanes, and only the gradients that sum over rows (gq, gk,
+// galpha, a per-token gbeta) couple them.  The forward can write S at the start
+// of every CK-token chunk (plus the final state); the backward rebuilds the
+// states it needs from those checkpoints by recomputing forward, never by
+// undoing an update (that divides by alpha_t in the gated rule, which amplifies
+// rounding by 1/alpha per token).
 #include <math.h>
 
 #include "edb_common.cuh"
 
 namespace {
 
-constexpr int kThreads = 256;
 constexpr int CK = 64;  // tokens per checkpoint chunk
 
 template <typename T>
@@ -176,268 +175,6 @@ __global__ void __launch_bounds__(kRowThreads)
     save_state(nck);
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kThreads)
-    delta_bwd_rec_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-                         const T* __restrict__ beta, const T* __restrict__ dO,
-                         const float* __restrict__ ckpt, T* __restrict__ gq, T* __restrict__ gk,
-                         T* __restrict__ gv, T* __restrict__ gbeta, int L, int H, int d,
-                         int beta_scalar) {
-    extern __shared__ float sm[];
-    const int sd = d + 1;
-    float* S = sm;                 // [d][sd]
-    float* dS = S + d * sd;        // [d][sd]
-    float* rbuf = dS + d * sd;     // [CK][d] retrievals of the current chunk
-    float* sq = rbuf + CK * d;
-    float* sk = sq + d;
-    float* sdo = sk + d;
-    float* su = sdo + d;           // beta (.) err
-    float* sbd = su + d;           // beta (.) dS k
-    float* red = sbd + d;          // [kThreads] scratch for the scalar-beta sum
-    const int h = blockIdx.x, b = blockIdx.y;
-    const int tid = threadIdx.x;
-    const int nck = (L + CK - 1) / CK;
-    const long long rs = (long long)H * d;
-    const long long base = (long long)b * L * rs + (long long)h * d;
-    for (int i = tid; i < d * sd; i += kThreads) dS[i] = 0.0f;
-
-    for (int c = nck - 1; c >= 0; --c) {
-        const int t0 = c * CK, t1 = min(L, t0 + CK);
-        const float* cp = ckpt + (((long long)b * H + h) * (nck + 1) + c) * d * d;
-        __syncthreads();
-        for (int i = tid; i < d * d; i += kThreads) S[(i / d) * sd + i % d] = cp[i];
-        __syncthreads();
-        // ---- forward over the chunk: retrievals r_t, S ends as S_{t1-1}
-        for (int t = t0; t < t1; ++t) {
-            const long long off = base + (long long)t * rs;
-            for (int i = tid; i < d; i += kThreads) sk[i] = ldv(k + off + i);
-            __syncthreads();
-            for (int i = tid; i < d; i += kThreads) {
-                float r = 0.0f;
-                for (int j = 0; j < d; ++j) r = fmaf(S[i * sd + j], sk[j], r);
-                rbuf[(t - t0) * d + i] = r;
-                const float be = beta_scalar ? ldv(beta + ((long long)b * L + t) * H + h)
-                                             : ldv(beta + off + i);
-                const float u = be * (ldv(v + off + i) - r);
-                for (int j = 0; j < d; ++j) S[i * sd + j] = fmaf(u, sk[j], S[i * sd + j]);
-            }
-            __syncthreads();
-        }
-        // ---- reverse over the chunk
-        for (int t = t1 - 1; t >= t0; --t) {
-            const long long off = base + (long long)t * rs;
-            const long long boff = ((long long)b * L + t) * H + h;
-            for (int i = tid; i < d; i += kThreads) {
-                sq[i] = ldv(q + off + i);
-                sk[i] = ldv(k + off + i);
-                sdo[i] = ldv(dO + off + i);
-            }
-            __syncthreads();
-            // rows: dS += dO q^T ; u = beta (v - r)
-            for (int i = tid; i < d; i += kThreads) {
-                const float doi = sdo[i];
-                for (int j = 0; j < d; ++j) dS[i * sd + j] = fmaf(doi, sq[j], dS[i * sd + j]);
-                const float be = beta_scalar ? ldv(beta + boff) : ldv(beta + off + i);
-                su[i] = be * (ldv(v + off + i) - rbuf[(t - t0) * d + i]);
-            }
-            __syncthreads();
-            // columns: dq = S_t^T dO
-            for (int j = tid; j < d; j += kThreads) {
-                float acc = 0.0f;
-                for (int i = 0; i < d; ++i) acc = fmaf(S[i * sd + j], sdo[i], acc);
-                st_scalar<T>(gq + off + j, acc);
-            }
-            // rows: dsk = dS k; dv = beta dsk; dbeta = err dsk
-            float bsum = 0.0f;
-            for (int i = tid; i < d; i += kThreads) {
-                float dsk = 0.0f;
-                for (int j = 0; j < d; ++j) dsk = fmaf(dS[i * sd + j], sk[j], dsk);
-                const float be = beta_scalar ? ldv(beta + boff) : ldv(beta + off + i);
-                const float err = ldv(v + off + i) - rbuf[(t - t0) * d + i];
-                st_scalar<T>(gv + off + i, be * dsk);
-                if (beta_scalar) bsum = fmaf(err, dsk, bsum);
-                else st_scalar<T>(gbeta + off + i, err * dsk);
-                sbd[i] = be * dsk;
-            }
-            if (beta_scalar) {
-                red[tid] = bsum;
-            }
-            __syncthreads();
-            if (beta_scalar && tid < 32) {
-                float s = 0.0f;
-                for (int i = tid; i < kThreads; i += 32) s += red[i];
-                for (int off2 = 16; off2 >= 1; off2 >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off2);
-                if (tid == 0) st_scalar<T>(gbeta + boff, s);
-            }
-            // rows: S_{t-1} = S_t - u k^T  (undo the update)
-            for (int i = tid; i < d; i += kThreads) {
-                const float u = su[i];
-                for (int j = 0; j < d; ++j) S[i * sd + j] = fmaf(-u, sk[j], S[i * sd + j]);
-            }
-            __syncthreads();
-            // columns: dk = dS^T u - S_{t-1}^T (beta dsk)
-            for (int j = tid; j < d; j += kThreads) {
-                float acc = 0.0f;
-                for (int i = 0; i < d; ++i)
-                    acc += dS[i * sd + j] * su[i] - S[i * sd + j] * sbd[i];
-                st_scalar<T>(gk + off + j, acc);
-            }
-            __syncthreads();
-            // rows: dS_{t-1} = dS - (beta dsk) k^T
-            for (int i = tid; i < d; i += kThreads) {
-                const float bd = sbd[i];
-                for (int j = 0; j < d; ++j) dS[i * sd + j] = fmaf(-bd, sk[j], dS[i * sd + j]);
-            }
-            __syncthreads();
-        }
-    }
-}
-
-// Gated backward.  sbuf: [B*H][CK][d][d] f32 scratch for one chunk's states
-// S_{t-1} (written by the chunk's forward recompute, read back in reverse).
-// shared: Sa, Sb, dS [d][d+1] | q k dO u beta-dsk err [6][d] | red [kThreads]
-template <typename T>
-__global__ void __launch_bounds__(kThreads)
-    gated_bwd_rec_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-                         const T* __restrict__ beta, const T* __restrict__ alpha,
-                         const T* __restrict__ dO, const float* __restrict__ ckpt,
-                         float* __restrict__ sbuf, T* __restrict__ gq, T* __restrict__ gk,
-                         T* __restrict__ gv, T* __restrict__ gbeta, T* __restrict__ galpha,
-                         int L, int H, int d, int beta_scalar) {
-    extern __shared__ float sm[];
-    const int sd = d + 1;
-    float* Sa = sm;                // S_t (after the token's update)
-    float* Sb = Sa + d * sd;       // S_{t-1}
-    float* dS = Sb + d * sd;       // gradient w.r.t. S_t
-    float* sq = dS + d * sd;
-    float* sk = sq + d;
-    float* sdo = sk + d;
-    float* su = sdo + d;           // beta (.) err
-    float* sbd = su + d;           // beta (.) dS k
-    float* ser = sbd + d;          // err = v - alpha S_{t-1} k
-    float* red = ser + d;          // [kThreads]
-    const int h = blockIdx.x, b = blockIdx.y;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nck = (L + CK - 1) / CK;
-    const long long rs = (long long)H * d;
-    const long long base = (long long)b * L * rs + (long long)h * d;
-    float* buf = sbuf + ((long long)b * H + h) * CK * d * d;
-    for (int i = tid; i < d * sd; i += kThreads) dS[i] = 0.0f;
-
-    // block sum of one value per thread; every thread gets the total
-    auto block_sum = [&](float x) {
-        for (int o = 16; o >= 1; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-        __syncthreads();  // red is free
-        if (lane == 0) red[warp] = x;
-        __syncthreads();
-        float s = 0.0f;
-        for (int w = 0; w < kThreads / 32; ++w) s += red[w];
-        return s;
-    };
-
-    for (int c = nck - 1; c >= 0; --c) {
-        const int t0 = c * CK, t1 = min(L, t0 + CK);
-        const float* cp = ckpt + (((long long)b * H + h) * (nck + 1) + c) * d * d;
-        __syncthreads();
-        for (int i = tid; i < d * d; i += kThreads) Sa[(i / d) * sd + i % d] = cp[i];
-        __syncthreads();
-        // ---- forward over the chunk: S_{t-1} -> buf[t - t0]; Sa ends as S_{t1-1}
-        for (int t = t0; t < t1; ++t) {
-            const long long off = base + (long long)t * rs;
-            float* dst = buf + (long long)(t - t0) * d * d;
-            for (int i = tid; i < d * d; i += kThreads) dst[i] = Sa[(i / d) * sd + i % d];
-            for (int i = tid; i < d; i += kThreads) sk[i] = ldv(k + off + i);
-            __syncthreads();
-            const float al = ldv(alpha + ((long long)b * L + t) * H + h);
-            for (int i = tid; i < d; i += kThreads) {
-                float r = 0.0f;
-                for (int j = 0; j < d; ++j) r = fmaf(Sa[i * sd + j], sk[j], r);
-                const float be = beta_scalar ? ldv(beta + ((long long)b * L + t) * H + h)
-                                             : ldv(beta + off + i);
-                const float u = be * (ldv(v + off + i) - al * r);
-                for (int j = 0; j < d; ++j) Sa[i * sd + j] = fmaf(u, sk[j], al * Sa[i * sd + j]);
-            }
-            __syncthreads();
-        }
-        // ---- reverse over the chunk (Sa = S_t, Sb = S_{t-1})
-        for (int t = t1 - 1; t >= t0; --t) {
-            const long long off = base + (long long)t * rs;
-            const long long boff = ((long long)b * L + t) * H + h;
-            const float al = ldv(alpha + boff);
-            const float* srcb = buf + (long long)(t - t0) * d * d;
-            for (int i = tid; i < d * d; i += kThreads) Sb[(i / d) * sd + i % d] = srcb[i];
-            for (int i = tid; i < d; i += kThreads) {
-                sq[i] = ldv(q + off + i);
-                sk[i] = ldv(k + off + i);
-                sdo[i] = ldv(dO + off + i);
-            }
-            __syncthreads();
-            // rows: dS += dO q^T ; u = beta (v - alpha S_{t-1} k)
-            for (int i = tid; i < d; i += kThreads) {
-                const float doi = sdo[i];
-                float r = 0.0f;
-                for (int j = 0; j < d; ++j) {
-                    dS[i * sd + j] = fmaf(doi, sq[j], dS[i * sd + j]);
-                    r = fmaf(Sb[i * sd + j], sk[j], r);
-                }
-                const float be = beta_scalar ? ldv(beta + boff) : ldv(beta + off + i);
-                const float err = ldv(v + off + i) - al * r;
-                ser[i] = err;
-                su[i] = be * err;
-            }
-            __syncthreads();
-            // columns: dq = S_t^T dO
-            for (int j = tid; j < d; j += kThreads) {
-                float acc = 0.0f;
-                for (int i = 0; i < d; ++i) acc = fmaf(Sa[i * sd + j], sdo[i], acc);
-                st_scalar<T>(gq + off + j, acc);
-            }
-            // rows: dsk = dS k; dv = beta dsk; dbeta = err dsk
-            float bsum = 0.0f;
-            for (int i = tid; i < d; i += kThreads) {
-                float dsk = 0.0f;
-                for (int j = 0; j < d; ++j) dsk = fmaf(dS[i * sd + j], sk[j], dsk);
-                const float be = beta_scalar ? ldv(beta + boff) : ldv(beta + off + i);
-                const float err = ser[i];
-                st_scalar<T>(gv + off + i, be * dsk);
-                if (beta_scalar) bsum = fmaf(err, dsk, bsum);
-                else st_scalar<T>(gbeta + off + i, err * dsk);
-                sbd[i] = be * dsk;
-            }
-            if (beta_scalar) {
-                const float s = block_sum(bsum);
-                if (tid == 0) st_scalar<T>(gbeta + boff, s);
-            }
-            __syncthreads();
-            // columns: dk = dS^T u - alpha S_{t-1}^T (beta dsk)
-            for (int j = tid; j < d; j += kThreads) {
-                float acc = 0.0f;
-                for (int i = 0; i < d; ++i)
-                    acc += dS[i * sd + j] * su[i] - al * Sb[i * sd + j] * sbd[i];
-                st_scalar<T>(gk + off + j, acc);
-            }
-            __syncthreads();
-            // rows: dS_d = dS - (beta dsk) k^T; dalpha = <dS_d, S_{t-1}>; dS_{t-1} = alpha dS_d
-            float ga = 0.0f;
-            for (int i = tid; i < d; i += kThreads) {
-                const float bd = sbd[i];
-                for (int j = 0; j < d; ++j) {
-                    const float x = fmaf(-bd, sk[j], dS[i * sd + j]);
-                    ga = fmaf(x, Sb[i * sd + j], ga);
-                    dS[i * sd + j] = al * x;
-                }
-            }
-            const float gas = block_sum(ga);
-            if (tid == 0) st_scalar<T>(galpha + boff, gas);
-            // S_{t-1} becomes the next step's S_t
-            float* tmp = Sa;
-            Sa = Sb;
-            Sb = tmp;
-            __syncthreads();
-        }
-    }
-}
-
 size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 size_t ckpt_bytes(int B, int L, int H, int d) {
@@ -445,15 +182,418 @@ size_t ckpt_bytes(int B, int L, int H, int d) {
     return (size_t)B * H * (nck + 1) * d * d * sizeof(float);
 }
 
-size_t gated_bwd_smem(int d) {
-    return ((size_t)3 * d * (d + 1) + 6 * d + kThreads) * sizeof(float);
+// ---------------------------------------------------------------- backward, row-parallel
+// The rows of S and of dS evolve independently in the backward as well.  For
+// row i (value index) and token t, with P = S_{t-1}[i], S = S_t[i]:
+//   dS[i] += dO_t[i] q_t;  r_i = P.k_t;  err_i = v_i - alpha_t r_i;  u_i = beta_i err_i
+//   dsk_i = dS[i].k_t;  gv_i = beta_i dsk_i;  gbeta_i = err_i dsk_i   (per-element beta)
+//   x = dS[i] - beta_i dsk_i k_t;  dS[i] <- alpha_t x  (the gradient w.r.t. S_{t-1}[i])
+// Only gq = S_t^T dO_t, gk = dS_t^T u - alpha_t S_{t-1}^T (beta (.) dsk), galpha = <x, P>
+// summed over rows, and a per-token beta's gradient, couple the rows.
+// grid (H, B, ceil(d / 32)), 128 threads = 32 rows x 4 lanes of CPL columns (the forward's
+// layout).  A checkpoint chunk (CK tokens) is walked in reverse in pieces of SB tokens:
+//   pass 1: from the chunk's checkpoint, forward over the chunk, keeping the state at every
+//           piece start (pstart);
+//   pass 2: per piece, last first: forward over the piece from its start writing every S_{t-1}
+//           row slice (sbuf), then backward over the piece reading them back.
+// pstart and sbuf are per-CTA scratch (320 KB per CTA at d = 128, L2-resident); each
+// thread reads back only what it wrote.  Row sums: per token, a lane's CPL partials are
+// summed over the 8 rows of its warp by recursive halving (the lane keeps CPL / 8 sums),
+// the 4 warps' sums meet in shared memory every RB tokens, and one partial per (row
+// block, token, head) goes to global memory, where delta_rows_reduce_kernel adds the row
+// blocks in a fixed order.
+constexpr int SB = 16;  // tokens per backward piece
+constexpr int NPIECE = CK / SB;
+constexpr int RB = 8;   // tokens per cross-warp reduction
+
+// Sums v over the lanes that differ in bits 2..4 (the 8 rows of a warp that share a
+// column slice).  On return v[0 .. NV/8) holds the totals of values
+// [base, base + NV/8), base = (lane >> 2 & 7) * NV / 8 (bit 4 -> NV/2, bit 3 -> NV/4,
+// bit 2 -> NV/8).
+template <int NV>
+static __device__ __forceinline__ void rows_halving_sum(float (&v)[NV], int lane) {
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+        const int m = 16 >> r;          // lane mask of this round
+        const int hn = NV >> (r + 1);   // values kept after this round
+        const bool up = (lane & m) != 0;
+#pragma unroll
+        for (int j = 0; j < hn; ++j) {
+            const float send = up ? v[j] : v[j + hn];
+            const float keep = up ? v[j + hn] : v[j];
+            v[j] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+        }
+    }
 }
-size_t gated_state_buf_bytes(int B, int H, int d) {
-    return (size_t)B * H * CK * d * d * sizeof(float);
+static __device__ __forceinline__ int halving_base(int lane, int nv) {
+    return ((lane >> 4) & 1) * (nv / 2) + ((lane >> 3) & 1) * (nv / 4) + ((lane >> 2) & 1) * (nv / 8);
 }
-size_t bwd_smem(int d) {
-    return ((size_t)2 * d * (d + 1) + (size_t)CK * d + 5 * d + kThreads) * sizeof(float);
+
+template <int CPL>
+struct RowsBwdSmem {
+    static constexpr int SP = CPL + 4, RP = 4 * SP, W = 4 * CPL;  // W: columns per CTA
+    static constexpr int RED = 2 * W + 2;                         // per warp and token
+    static constexpr size_t floats = (size_t)2 * SB * RP + 5 * SB * kRowsPerCta + SB +
+                                     (size_t)RB * 4 * RED;
+    static constexpr size_t bytes = floats * sizeof(float);
+};
+
+// per-CTA scratch floats: NPIECE piece starts + SB token states, 128 threads x CPL
+template <int CPL>
+constexpr size_t rows_scratch_floats() {
+    return (size_t)(NPIECE + SB) * kRowThreads * CPL;
 }
+
+template <typename T, int CPL, bool GATED>
+__global__ void __launch_bounds__(kRowThreads, 2)
+    delta_bwd_rows_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                          const T* __restrict__ v, const T* __restrict__ beta,
+                          const T* __restrict__ alpha, const T* __restrict__ dO,
+                          const float* __restrict__ ckpt, float* scratch,
+                          float* __restrict__ part, float* __restrict__ part_s,
+                          T* __restrict__ gv, T* __restrict__ gbeta, int B, int L, int H, int d,
+                          int beta_scalar) {
+    using G = RowsBwdSmem<CPL>;
+    constexpr int SP = G::SP, RP = G::RP, W = G::W, RED = G::RED;
+    constexpr int NV = 2 * CPL;  // gq | gk partials of one lane
+    extern __shared__ __align__(16) float smf[];
+    float* sk = smf;                       // [SB][RP]
+    float* sq = sk + SB * RP;              // [SB][RP]
+    float* sv = sq + SB * RP;              // [SB][32]
+    float* sb = sv + SB * kRowsPerCta;     // [SB][32]
+    float* sdo = sb + SB * kRowsPerCta;    // [SB][32]
+    float* sgv = sdo + SB * kRowsPerCta;   // [SB][32] staged gv
+    float* sgb = sgv + SB * kRowsPerCta;   // [SB][32] staged per-element gbeta
+    float* sa = sgb + SB * kRowsPerCta;    // [SB]
+    float* red = sa + SB;                  // [RB][4 warps][RED]
+    const int h = blockIdx.x, b = blockIdx.y, z = blockIdx.z, rb = z * kRowsPerCta;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int rl = warp * 8 + (lane >> 2);
+    const int i = rb + rl;
+    const int part_ix = lane & 3;
+    const int c0 = part_ix * CPL;
+    const bool row_ok = i < d;
+    const long long rs = (long long)H * d;
+    const long long base = (long long)b * L * rs + (long long)h * d;
+    const int nck = (L + CK - 1) / CK;
+    const long long cta = ((long long)b * H + h) * gridDim.z + z;
+    float* pstart = scratch + cta * rows_scratch_floats<CPL>();
+    float* sbuf = pstart + (size_t)NPIECE * kRowThreads * CPL;
+    const float* ck_unit = ckpt + ((long long)b * H + h) * (nck + 1) * d * d;
+    const int hb = halving_base(lane, NV);
+
+    auto st_slice = [&](float* dst, const float (&x)[CPL]) {
+        float4* p = reinterpret_cast<float4*>(dst + (size_t)tid * CPL);
+#pragma unroll
+        for (int c = 0; c < CPL; c += 4) p[c / 4] = make_float4(x[c], x[c + 1], x[c + 2], x[c + 3]);
+    };
+    auto ld_slice = [&](const float* src, float (&x)[CPL]) {
+        const float4* p = reinterpret_cast<const float4*>(src + (size_t)tid * CPL);
+#pragma unroll
+        for (int c = 0; c < CPL; c += 4) {
+            const float4 w = p[c / 4];
+            x[c] = w.x; x[c + 1] = w.y; x[c + 2] = w.z; x[c + 3] = w.w;
+        }
+    };
+    // stage tokens [t0, t0 + n) of the piece; with_q: also q and dO (the backward's)
+    auto stage = [&](int t0, int n, bool with_q) {
+        __syncthreads();  // the previous piece's stage is consumed
+        for (int base_idx = 0; base_idx < SB * 4 * CPL; base_idx += kRowThreads * 4) {
+            float fk[4], fq[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int idx = base_idx + tid + u * kRowThreads;
+                const int tt = idx / (4 * CPL), c = idx % (4 * CPL);
+                const bool ok = tt < n && c < d;
+                const long long off = base + (long long)(t0 + tt) * rs + c;
+                fk[u] = ok ? ldv(k + off) : 0.0f;
+                fq[u] = (ok && with_q) ? ldv(q + off) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int idx = base_idx + tid + u * kRowThreads;
+                const int tt = idx / (4 * CPL), c = idx % (4 * CPL);
+                if (tt < SB) {
+                    const int so = tt * RP + (c / CPL) * SP + c % CPL;
+                    sk[so] = fk[u];
+                    sq[so] = fq[u];
+                }
+            }
+        }
+        for (int idx = tid; idx < SB * kRowsPerCta; idx += kRowThreads) {
+            const int tt = idx / kRowsPerCta, r = idx % kRowsPerCta;
+            const bool ok = tt < n && rb + r < d;
+            const long long off = base + (long long)(t0 + tt) * rs + rb + r;
+            sv[idx] = ok ? ldv(v + off) : 0.0f;
+            sb[idx] = !ok ? 0.0f
+                          : beta_scalar ? ldv(beta + ((long long)b * L + t0 + tt) * H + h)
+                                        : ldv(beta + off);
+            sdo[idx] = (ok && with_q) ? ldv(dO + off) : 0.0f;
+        }
+        if (GATED)
+            for (int tt = tid; tt < SB; tt += kRowThreads)
+                sa[tt] = tt < n ? ldv(alpha + ((long long)b * L + t0 + tt) * H + h) : 1.0f;
+        __syncthreads();
+    };
+    // one forward step of this thread's row slice (token tt of the staged piece)
+    auto fwd_step = [&](float (&S)[CPL], int tt) {
+        const float* kr = sk + tt * RP + part_ix * SP;
+        float r0 = 0.0f, r1 = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CPL; c += 4) {
+            const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
+            r0 = fmaf(S[c], k4.x, fmaf(S[c + 1], k4.y, r0));
+            r1 = fmaf(S[c + 2], k4.z, fmaf(S[c + 3], k4.w, r1));
+        }
+        float r = r0 + r1;
+        r += __shfl_xor_sync(0xffffffffu, r, 1);
+        r += __shfl_xor_sync(0xffffffffu, r, 2);
+        const float al = GATED ? sa[tt] : 1.0f;
+        const float u = sb[tt * kRowsPerCta + rl] * (sv[tt * kRowsPerCta + rl] - al * r);
+#pragma unroll
+        for (int c = 0; c < CPL; c += 4) {
+            const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
+            S[c] = fmaf(u, k4.x, GATED ? al * S[c] : S[c]);
+            S[c + 1] = fmaf(u, k4.y, GATED ? al * S[c + 1] : S[c + 1]);
+            S[c + 2] = fmaf(u, k4.z, GATED ? al * S[c + 2] : S[c + 2]);
+            S[c + 3] = fmaf(u, k4.w, GATED ? al * S[c + 3] : S[c + 3]);
+        }
+    };
+    // the 4 warps' row sums of tokens [tb, tb + n) of the piece -> global partials
+    auto flush = [&](int t_abs0, int n) {
+        __syncthreads();
+        for (int idx = tid; idx < n * RED; idx += kRowThreads) {
+            const int tt = idx / RED, e = idx % RED;
+            const float* rr = red + tt * 4 * RED + e;
+            const float s = (rr[0] + rr[RED]) + (rr[2 * RED] + rr[3 * RED]);
+            const long long row = ((long long)z * B + b) * L + t_abs0 + tt;
+            if (e < 2 * W) {
+                const int which = e / W, col = e % W;
+                if (col < d) part[(row * H + h) * 2 * d + which * d + col] = s;
+            } else {
+                part_s[(row * H + h) * 2 + (e - 2 * W)] = s;
+            }
+        }
+        __syncthreads();
+    };
+
+    float dS[CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) dS[c] = 0.0f;
+
+    for (int ch = nck - 1; ch >= 0; --ch) {
+        const int t0 = ch * CK, tn = min(CK, L - t0);
+        const int np = (tn + SB - 1) / SB;
+        // ---- pass 1: piece-start states from the checkpoint
+        {
+            float S[CPL];
+            const float* src = ck_unit + (long long)ch * d * d + (long long)i * d + c0;
+#pragma unroll
+            for (int c = 0; c < CPL; ++c) S[c] = (row_ok && c0 + c < d) ? src[c] : 0.0f;
+            for (int p = 0; p < np; ++p) {
+                st_slice(pstart + (size_t)p * kRowThreads * CPL, S);
+                if (p == np - 1) break;
+                stage(t0 + p * SB, SB, false);
+                for (int tt = 0; tt < SB; ++tt) fwd_step(S, tt);
+            }
+        }
+        // ---- pass 2: pieces in reverse
+        for (int p = np - 1; p >= 0; --p) {
+            const int pt0 = t0 + p * SB, pn = min(SB, tn - p * SB);
+            stage(pt0, pn, true);
+            float S[CPL];
+            ld_slice(pstart + (size_t)p * kRowThreads * CPL, S);
+            for (int tt = 0; tt < pn; ++tt) {
+                st_slice(sbuf + (size_t)tt * kRowThreads * CPL, S);
+                fwd_step(S, tt);
+            }
+            // S = S_t of the piece's last token; walk back
+            float P[CPL];
+            ld_slice(sbuf + (size_t)(pn - 1) * kRowThreads * CPL, P);
+            for (int tt = pn - 1; tt >= 0; --tt) {
+                float Pn[CPL];
+                if (tt > 0) ld_slice(sbuf + (size_t)(tt - 1) * kRowThreads * CPL, Pn);
+                const float* kr = sk + tt * RP + part_ix * SP;
+                const float* qr = sq + tt * RP + part_ix * SP;
+                const float doi = sdo[tt * kRowsPerCta + rl];
+                const float al = GATED ? sa[tt] : 1.0f;
+                const float be = sb[tt * kRowsPerCta + rl];
+                float* rw = red + ((tt % RB) * 4 + warp) * RED;
+                // gq partial (S_t dO_i) and dS += dO_i q
+                {
+                    float w[NV];
+#pragma unroll
+                    for (int c = 0; c < CPL; c += 4) {
+                        const float4 q4 = *reinterpret_cast<const float4*>(qr + c);
+                        dS[c] = fmaf(doi, q4.x, dS[c]);
+                        dS[c + 1] = fmaf(doi, q4.y, dS[c + 1]);
+                        dS[c + 2] = fmaf(doi, q4.z, dS[c + 2]);
+                        dS[c + 3] = fmaf(doi, q4.w, dS[c + 3]);
+                    }
+#pragma unroll
+                    for (int c = 0; c < CPL; ++c) w[c] = S[c] * doi;
+                    // r = P.k and dsk = dS.k
+                    float r0 = 0.0f, r1 = 0.0f, s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+                    for (int c = 0; c < CPL; c += 4) {
+                        const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
+                        r0 = fmaf(P[c], k4.x, fmaf(P[c + 1], k4.y, r0));
+                        r1 = fmaf(P[c + 2], k4.z, fmaf(P[c + 3], k4.w, r1));
+                        s0 = fmaf(dS[c], k4.x, fmaf(dS[c + 1], k4.y, s0));
+                        s1 = fmaf(dS[c + 2], k4.z, fmaf(dS[c + 3], k4.w, s1));
+                    }
+                    float r = r0 + r1, dsk = s0 + s1;
+                    r += __shfl_xor_sync(0xffffffffu, r, 1);
+                    dsk += __shfl_xor_sync(0xffffffffu, dsk, 1);
+                    r += __shfl_xor_sync(0xffffffffu, r, 2);
+                    dsk += __shfl_xor_sync(0xffffffffu, dsk, 2);
+                    const float err = sv[tt * kRowsPerCta + rl] - al * r;
+                    const float u = be * err;
+                    const float bd = be * dsk;
+                    if (part_ix == 0) {
+                        sgv[tt * kRowsPerCta + rl] = bd;
+                        sgb[tt * kRowsPerCta + rl] = err * dsk;
+                    }
+                    // gk partial: dS u - alpha P (beta dsk); then dS <- alpha (dS - bd k)
+                    float ga = 0.0f;
+#pragma unroll
+                    for (int c = 0; c < CPL; c += 4) {
+                        const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
+                        const float kv[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            w[CPL + c + e] = fmaf(dS[c + e], u, -al * bd * P[c + e]);
+                            const float x = fmaf(-bd, kv[e], dS[c + e]);
+                            ga = fmaf(x, P[c + e], ga);
+                            dS[c + e] = GATED ? al * x : x;
+                        }
+                    }
+                    rows_halving_sum<NV>(w, lane);
+#pragma unroll
+                    for (int j = 0; j < NV / 8; ++j) {
+                        const int e = hb + j;  // index into [gq CPL | gk CPL] of slice part_ix
+                        const int which = e >= CPL, col = c0 + e - which * CPL;
+                        rw[which * W + col] = w[j];
+                    }
+                    // scalars: galpha, and a per-token beta's gradient (one lane per row)
+                    float bsum = (part_ix == 0 && row_ok) ? err * dsk : 0.0f;
+#pragma unroll
+                    for (int o = 16; o >= 1; o >>= 1) {
+                        ga += __shfl_xor_sync(0xffffffffu, ga, o);
+                        bsum += __shfl_xor_sync(0xffffffffu, bsum, o);
+                    }
+                    if (lane == 0) {
+                        rw[2 * W] = ga;
+                        rw[2 * W + 1] = bsum;
+                    }
+                }
+#pragma unroll
+                for (int c = 0; c < CPL; ++c) S[c] = P[c];
+                if (tt > 0) {
+#pragma unroll
+                    for (int c = 0; c < CPL; ++c) P[c] = Pn[c];
+                }
+                if (tt % RB == 0) flush(pt0 + tt, min(RB, pn - tt));
+            }
+            // this piece's gv and per-element gbeta rows
+            for (int idx = tid; idx < pn * kRowsPerCta; idx += kRowThreads) {
+                const int tt = idx / kRowsPerCta, r = idx % kRowsPerCta;
+                if (rb + r < d) {
+                    const long long off = base + (long long)(pt0 + tt) * rs + rb + r;
+                    st_scalar<T>(gv + off, sgv[idx]);
+                    if (!beta_scalar) st_scalar<T>(gbeta + off, sgb[idx]);
+                }
+            }
+        }
+    }
+}
+
+// gq, gk [B, L, H, d] and galpha, a per-token gbeta [B, L, H]: the row blocks' partials
+// added in order.  One block of 128 threads per (b, t, h) row group of 4.
+template <typename T, bool GATED>
+__global__ void __launch_bounds__(256)
+    delta_rows_reduce_kernel(const float* __restrict__ part, const float* __restrict__ part_s,
+                             T* __restrict__ gq, T* __restrict__ gk, T* __restrict__ galpha,
+                             T* __restrict__ gbeta, long long rows, int d, int nz,
+                             int beta_scalar) {
+    const long long row = (long long)blockIdx.x * 2 + (threadIdx.x >> 7);
+    const int tx = threadIdx.x & 127;
+    if (row >= rows) return;
+    for (int e = tx; e < 2 * d; e += 128) {
+        float s = 0.0f;
+        for (int zz = 0; zz < nz; ++zz) s += part[((long long)zz * rows + row) * 2 * d + e];
+        if (e < d) st_scalar<T>(gq + row * d + e, s);
+        else st_scalar<T>(gk + row * d + e - d, s);
+    }
+    if (tx < 2) {
+        float s = 0.0f;
+        for (int zz = 0; zz < nz; ++zz) s += part_s[((long long)zz * rows + row) * 2 + tx];
+        if (tx == 0 && GATED) st_scalar<T>(galpha + row, s);
+        if (tx == 1 && beta_scalar) st_scalar<T>(gbeta + row, s);
+    }
+}
+
+template <int CPL>
+size_t rows_bwd_scratch_bytes(int B, int H, int d) {
+    const int nz = (d + kRowsPerCta - 1) / kRowsPerCta;
+    return (size_t)B * H * nz * rows_scratch_floats<CPL>() * sizeof(float);
+}
+size_t rows_bwd_ws_bytes(int B, int L, int H, int d) {
+    const int nz = (d + kRowsPerCta - 1) / kRowsPerCta;
+    const size_t rows = (size_t)B * L * H;
+    const size_t sc = d <= 32 ? rows_bwd_scratch_bytes<8>(B, H, d)
+                              : rows_bwd_scratch_bytes<32>(B, H, d);
+    return a256(sc) + a256((size_t)nz * rows * 2 * d * sizeof(float)) +
+           a256((size_t)nz * rows * 2 * sizeof(float));
+}
+
+template <typename T, int CPL, bool GATED>
+int launch_bwd_rows_t(const void* q, const void* k, const void* v, const void* beta,
+                      const void* alpha, const void* dO, const float* ckpt, void* ws, void* gq,
+                      void* gk, void* gv, void* gbeta, void* galpha, int B, int L, int H, int d,
+                      int beta_scalar, cudaStream_t st) {
+    const int nz = (d + kRowsPerCta - 1) / kRowsPerCta;
+    const size_t rows = (size_t)B * L * H;
+    char* p = static_cast<char*>(ws);
+    float* scratch = reinterpret_cast<float*>(p);
+    p += a256(rows_bwd_scratch_bytes<CPL>(B, H, d));
+    float* part = reinterpret_cast<float*>(p);
+    p += a256((size_t)nz * rows * 2 * d * sizeof(float));
+    float* part_s = reinterpret_cast<float*>(p);
+    constexpr size_t smem = RowsBwdSmem<CPL>::bytes;
+    cudaError_t e = cudaFuncSetAttribute(delta_bwd_rows_kernel<T, CPL, GATED>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    delta_bwd_rows_kernel<T, CPL, GATED><<<dim3(H, B, nz), kRowThreads, smem, st>>>(
+        (const T*)q, (const T*)k, (const T*)v, (const T*)beta, (const T*)alpha, (const T*)dO,
+        ckpt, scratch, part, part_s, (T*)gv, (T*)gbeta, B, L, H, d, beta_scalar);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return (int)e;
+    delta_rows_reduce_kernel<T, GATED><<<(unsigned)((rows + 1) / 2), 256, 0, st>>>(
+        part, part_s, (T*)gq, (T*)gk, (T*)galpha, (T*)gbeta, (long long)rows, d, nz,
+        beta_scalar);
+    return edb::status_from_cuda(cudaGetLastError());
+}
+
+template <typename T>
+int launch_bwd_rows(const void* q, const void* k, const void* v, const void* beta,
+                    const void* alpha, const void* dO, const float* ckpt, void* ws, void* gq,
+                    void* gk, void* gv, void* gbeta, void* galpha, int B, int L, int H, int d,
+                    int beta_scalar, cudaStream_t st) {
+    if (d <= 32)
+        return alpha ? launch_bwd_rows_t<T, 8, true>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk,
+                                                     gv, gbeta, galpha, B, L, H, d, beta_scalar,
+                                                     st)
+                     : launch_bwd_rows_t<T, 8, false>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk,
+                                                      gv, gbeta, galpha, B, L, H, d, beta_scalar,
+                                                      st);
+    return alpha ? launch_bwd_rows_t<T, 32, true>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk, gv,
+                                                  gbeta, galpha, B, L, H, d, beta_scalar, st)
+                 : launch_bwd_rows_t<T, 32, false>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk,
+                                                   gv, gbeta, galpha, B, L, H, d, beta_scalar,
+                                                   st);
+}
+
 
 template <typename T, int CPL, bool GATED>
 int launch_fwd_rows(const void* q, const void* k, const void* v, const void* beta,
@@ -485,35 +625,6 @@ int launch_fwd(const void* q, const void* k, const void* v, const void* beta, co
                                               beta_scalar, st)
                : launch_fwd_rows<T, 32, false>(q, k, v, beta, alpha, o, ckpt, B, L, H, d,
                                                beta_scalar, st);
-}
-
-template <typename T>
-int launch_gated_bwd(const void* q, const void* k, const void* v, const void* beta,
-                     const void* alpha, const void* dO, const float* ckpt, float* sbuf, void* gq,
-                     void* gk, void* gv, void* gbeta, void* galpha, int B, int L, int H, int d,
-                     int beta_scalar, cudaStream_t st) {
-    const size_t smem = gated_bwd_smem(d);
-    cudaError_t e = cudaFuncSetAttribute(gated_bwd_rec_kernel<T>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return (int)e;
-    gated_bwd_rec_kernel<T><<<dim3(H, B), kThreads, smem, st>>>(
-        (const T*)q, (const T*)k, (const T*)v, (const T*)beta, (const T*)alpha, (const T*)dO,
-        ckpt, sbuf, (T*)gq, (T*)gk, (T*)gv, (T*)gbeta, (T*)galpha, L, H, d, beta_scalar);
-    return edb::status_from_cuda(cudaGetLastError());
-}
-
-template <typename T>
-int launch_bwd(const void* q, const void* k, const void* v, const void* beta, const void* dO,
-               const float* ckpt, void* gq, void* gk, void* gv, void* gbeta, int B, int L, int H,
-               int d, int beta_scalar, cudaStream_t st) {
-    const size_t smem = bwd_smem(d);
-    cudaError_t e = cudaFuncSetAttribute(delta_bwd_rec_kernel<T>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return (int)e;
-    delta_bwd_rec_kernel<T><<<dim3(H, B), kThreads, smem, st>>>(
-        (const T*)q, (const T*)k, (const T*)v, (const T*)beta, (const T*)dO, ckpt, (T*)gq, (T*)gk,
-        (T*)gv, (T*)gbeta, L, H, d, beta_scalar);
-    return edb::status_from_cuda(cudaGetLastError());
 }
 
 int check(int dtype, int B, int L, int H, int d) {
@@ -590,7 +701,8 @@ extern "C" size_t edb_delta_rule_bwd_workspace(int dtype, int beta_per_element, 
         const size_t b = edb_delta_chunked_bwd_ws(batch, seq_len, heads);
         return ck + (have_ckpt ? b : (f > b ? f : b));
     }
-    return ck;
+    // checkpoints (when not passed), then the row-parallel backward's scratch
+    return ck + rows_bwd_ws_bytes(batch, seq_len, heads, head_dim);
 }
 
 extern "C" int edb_delta_rule_bwd(int dtype, const void* q, const void* k, const void* v,
@@ -626,6 +738,7 @@ extern "C" int edb_delta_rule_bwd(int dtype, const void* q, const void* k, const
         return edb_delta_chunked_bwd(q, k, v, beta, dO, resid, gq, gk, gv, gbeta, batch, seq_len,
                                      heads, scratch, st);
     }
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return EDB_ERR_MISALIGNED;
     const int bs = beta_per_element ? 0 : 1;
     const float* ck = s_ckpt;
     if (!ck) {
@@ -636,11 +749,13 @@ extern "C" int edb_delta_rule_bwd(int dtype, const void* q, const void* k, const
         if (s) return s;
         ck = w;
     }
+    void* rows_ws = static_cast<char*>(workspace) + ckb;
     return dtype == EDB_BF16
-               ? launch_bwd<__nv_bfloat16>(q, k, v, beta, dO, ck, gq, gk, gv, gbeta, batch,
-                                           seq_len, heads, head_dim, bs, st)
-               : launch_bwd<float>(q, k, v, beta, dO, ck, gq, gk, gv, gbeta, batch, seq_len,
-                                   heads, head_dim, bs, st);
+               ? launch_bwd_rows<__nv_bfloat16>(q, k, v, beta, nullptr, dO, ck, rows_ws, gq, gk,
+                                                gv, gbeta, nullptr, batch, seq_len, heads,
+                                                head_dim, bs, st)
+               : launch_bwd_rows<float>(q, k, v, beta, nullptr, dO, ck, rows_ws, gq, gk, gv,
+                                        gbeta, nullptr, batch, seq_len, heads, head_dim, bs, st);
 }
 
 // ------------------------------------------------------------------ GatedDeltaNet
@@ -675,7 +790,7 @@ extern "C" size_t edb_gated_delta_net_bwd_workspace(int dtype, int beta_per_elem
                                 : a256(edb_gated_delta_net_ckpt_bytes(dtype, beta_per_element,
                                                                       batch, seq_len, heads,
                                                                       head_dim));
-    return ck + gated_state_buf_bytes(batch, heads, head_dim);
+    return ck + rows_bwd_ws_bytes(batch, seq_len, heads, head_dim);
 }
 
 extern "C" int edb_gated_delta_net_bwd(int dtype, const void* q, const void* k, const void* v,
@@ -691,7 +806,7 @@ extern "C" int edb_gated_delta_net_bwd(int dtype, const void* q, const void* k, 
                                                           seq_len, heads, head_dim,
                                                           s_ckpt != nullptr);
     if (workspace_bytes < need || !workspace) return EDB_ERR_WORKSPACE_TOO_SMALL;
-    if (reinterpret_cast<uintptr_t>(workspace) & 15u) return EDB_ERR_MISALIGNED;
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return EDB_ERR_MISALIGNED;
     cudaStream_t st = (cudaStream_t)stream;
     char* p = static_cast<char*>(workspace);
     const float* ck = s_ckpt;
@@ -706,11 +821,10 @@ extern "C" int edb_gated_delta_net_bwd(int dtype, const void* q, const void* k, 
         ck = w;
     }
     const int bs = beta_per_element ? 0 : 1;
-    float* sbuf = reinterpret_cast<float*>(p);
     return dtype == EDB_BF16
-               ? launch_gated_bwd<__nv_bfloat16>(q, k, v, beta, alpha, dO, ck, sbuf, gq, gk, gv,
-                                                 gbeta, galpha, batch, seq_len, heads, head_dim,
-                                                 bs, st)
-               : launch_gated_bwd<float>(q, k, v, beta, alpha, dO, ck, sbuf, gq, gk, gv, gbeta,
-                                         galpha, batch, seq_len, heads, head_dim, bs, st);
+               ? launch_bwd_rows<__nv_bfloat16>(q, k, v, beta, alpha, dO, ck, p, gq, gk, gv,
+                                                gbeta, galpha, batch, seq_len, heads, head_dim,
+                                                bs, st)
+               : launch_bwd_rows<float>(q, k, v, beta, alpha, dO, ck, p, gq, gk, gv, gbeta,
+                                        galpha, batch, seq_len, heads, head_dim, bs, st);
 }
