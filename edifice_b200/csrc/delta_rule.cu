@@ -205,6 +205,7 @@ size_t ckpt_bytes(int B, int L, int H, int d) {
 constexpr int SB = 16;  // tokens per backward piece
 constexpr int NPIECE = CK / SB;
 constexpr int RB = 8;   // tokens per cross-warp reduction
+constexpr int NSLOT = 2 * RB;  // row-sum slots: a token's gq arrives one step after its gk
 
 // Sums v over the lanes that differ in bits 2..4 (the 8 rows of a warp that share a
 // column slice).  On return v[0 .. NV/8) holds the totals of values
@@ -232,9 +233,14 @@ static __device__ __forceinline__ int halving_base(int lane, int nv) {
 template <int CPL>
 struct RowsBwdSmem {
     static constexpr int SP = CPL + 4, RP = 4 * SP, W = 4 * CPL;  // W: columns per CTA
-    static constexpr int RED = 2 * W + 2;                         // per warp and token
+    // per warp and token: [gq | gk][4 slices][CPL + 2], the halves 4 (CPL + 2) + 1 apart,
+    // then galpha and a per-token gbeta: the skews put the 32 lanes' stores of one
+    // halving result on 32 different banks
+    static constexpr int SLICE = CPL + 2, HALF = 4 * SLICE + 1;
+    static constexpr int RED = 2 * HALF + 2;
+    // red holds 2 RB token slots: a token's gq arrives one step after its gk
     static constexpr size_t floats = (size_t)2 * SB * RP + 5 * SB * kRowsPerCta + SB +
-                                     (size_t)RB * 4 * RED;
+                                     (size_t)NSLOT * 4 * RED;
     static constexpr size_t bytes = floats * sizeof(float);
 };
 
@@ -253,9 +259,12 @@ __global__ void __launch_bounds__(kRowThreads, 2)
                           float* __restrict__ part, float* __restrict__ part_s,
                           T* __restrict__ gv, T* __restrict__ gbeta, int B, int L, int H, int d,
                           int beta_scalar) {
+    static_assert(SB % NSLOT == 0, "red slots are indexed by the token's place in its piece");
     using G = RowsBwdSmem<CPL>;
     constexpr int SP = G::SP, RP = G::RP, W = G::W, RED = G::RED;
+    constexpr int SLICE = G::SLICE, HALF = G::HALF;
     constexpr int NV = 2 * CPL;  // gq | gk partials of one lane
+    constexpr int NP = CPL / 2;  // packed f32 pairs per row slice
     extern __shared__ __align__(16) float smf[];
     float* sk = smf;                       // [SB][RP]
     float* sq = sk + SB * RP;              // [SB][RP]
@@ -265,7 +274,7 @@ __global__ void __launch_bounds__(kRowThreads, 2)
     float* sgv = sdo + SB * kRowsPerCta;   // [SB][32] staged gv
     float* sgb = sgv + SB * kRowsPerCta;   // [SB][32] staged per-element gbeta
     float* sa = sgb + SB * kRowsPerCta;    // [SB]
-    float* red = sa + SB;                  // [RB][4 warps][RED]
+    float* red = sa + SB;                  // [NSLOT][4 warps][RED]
     const int h = blockIdx.x, b = blockIdx.y, z = blockIdx.z, rb = z * kRowsPerCta;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int rl = warp * 8 + (lane >> 2);
@@ -282,17 +291,18 @@ __global__ void __launch_bounds__(kRowThreads, 2)
     const float* ck_unit = ckpt + ((long long)b * H + h) * (nck + 1) * d * d;
     const int hb = halving_base(lane, NV);
 
-    auto st_slice = [&](float* dst, const float (&x)[CPL]) {
+    auto st_slice = [&](float* dst, const float2 (&x)[NP]) {
         float4* p = reinterpret_cast<float4*>(dst + (size_t)tid * CPL);
 #pragma unroll
-        for (int c = 0; c < CPL; c += 4) p[c / 4] = make_float4(x[c], x[c + 1], x[c + 2], x[c + 3]);
+        for (int c = 0; c < NP; c += 2) p[c / 2] = make_float4(x[c].x, x[c].y, x[c + 1].x, x[c + 1].y);
     };
-    auto ld_slice = [&](const float* src, float (&x)[CPL]) {
+    auto ld_slice = [&](const float* src, float2 (&x)[NP]) {
         const float4* p = reinterpret_cast<const float4*>(src + (size_t)tid * CPL);
 #pragma unroll
-        for (int c = 0; c < CPL; c += 4) {
-            const float4 w = p[c / 4];
-            x[c] = w.x; x[c + 1] = w.y; x[c + 2] = w.z; x[c + 3] = w.w;
+        for (int c = 0; c < NP; c += 2) {
+            const float4 w = p[c / 2];
+            x[c] = make_float2(w.x, w.y);
+            x[c + 1] = make_float2(w.z, w.w);
         }
     };
     // stage tokens [t0, t0 + n) of the piece; with_q: also q and dO (the backward's)
@@ -335,61 +345,145 @@ __global__ void __launch_bounds__(kRowThreads, 2)
                 sa[tt] = tt < n ? ldv(alpha + ((long long)b * L + t0 + tt) * H + h) : 1.0f;
         __syncthreads();
     };
+    auto krow = [&](int tt, int p) {  // k pair p of token tt (this lane's slice)
+        return *reinterpret_cast<const float2*>(sk + tt * RP + part_ix * SP + 2 * p);
+    };
+    auto qrow = [&](int tt, int p) {
+        return *reinterpret_cast<const float2*>(sq + tt * RP + part_ix * SP + 2 * p);
+    };
     // one forward step of this thread's row slice (token tt of the staged piece)
-    auto fwd_step = [&](float (&S)[CPL], int tt) {
-        const float* kr = sk + tt * RP + part_ix * SP;
-        float r0 = 0.0f, r1 = 0.0f;
+    auto fwd_step = [&](float2 (&S)[NP], int tt) {
+        float2 ra = dup2(0.0f), rc = dup2(0.0f);
 #pragma unroll
-        for (int c = 0; c < CPL; c += 4) {
-            const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
-            r0 = fmaf(S[c], k4.x, fmaf(S[c + 1], k4.y, r0));
-            r1 = fmaf(S[c + 2], k4.z, fmaf(S[c + 3], k4.w, r1));
+        for (int p = 0; p < NP; p += 2) {
+            ra = fma2(S[p], krow(tt, p), ra);
+            rc = fma2(S[p + 1], krow(tt, p + 1), rc);
         }
-        float r = r0 + r1;
+        float r = (ra.x + ra.y) + (rc.x + rc.y);
         r += __shfl_xor_sync(0xffffffffu, r, 1);
         r += __shfl_xor_sync(0xffffffffu, r, 2);
         const float al = GATED ? sa[tt] : 1.0f;
-        const float u = sb[tt * kRowsPerCta + rl] * (sv[tt * kRowsPerCta + rl] - al * r);
+        const float2 u2 = dup2(sb[tt * kRowsPerCta + rl] * (sv[tt * kRowsPerCta + rl] - al * r));
 #pragma unroll
-        for (int c = 0; c < CPL; c += 4) {
-            const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
-            S[c] = fmaf(u, k4.x, GATED ? al * S[c] : S[c]);
-            S[c + 1] = fmaf(u, k4.y, GATED ? al * S[c + 1] : S[c + 1]);
-            S[c + 2] = fmaf(u, k4.z, GATED ? al * S[c + 2] : S[c + 2]);
-            S[c + 3] = fmaf(u, k4.w, GATED ? al * S[c + 3] : S[c + 3]);
-        }
+        for (int p = 0; p < NP; ++p)
+            S[p] = fma2(u2, krow(tt, p), GATED ? mul2(dup2(al), S[p]) : S[p]);
     };
-    // the 4 warps' row sums of tokens [tb, tb + n) of the piece -> global partials
-    auto flush = [&](int t_abs0, int n) {
+    // the 4 warps' row sums of tokens [tt0, tt0 + n) of the piece -> global partials
+    auto flush = [&](int pt0, int tt0, int n) {
         __syncthreads();
-        for (int idx = tid; idx < n * RED; idx += kRowThreads) {
-            const int tt = idx / RED, e = idx % RED;
-            const float* rr = red + tt * 4 * RED + e;
-            const float s = (rr[0] + rr[RED]) + (rr[2 * RED] + rr[3 * RED]);
-            const long long row = ((long long)z * B + b) * L + t_abs0 + tt;
+        for (int idx = tid; idx < n * (2 * W + 2); idx += kRowThreads) {
+            const int tt = tt0 + idx / (2 * W + 2), e = idx % (2 * W + 2);
+            const long long row = ((long long)z * B + b) * L + pt0 + tt;
             if (e < 2 * W) {
                 const int which = e / W, col = e % W;
+                const float* rr =
+                    red + (tt % NSLOT) * 4 * RED + which * HALF + (col / CPL) * SLICE + col % CPL;
+                const float s = (rr[0] + rr[RED]) + (rr[2 * RED] + rr[3 * RED]);
                 if (col < d) part[(row * H + h) * 2 * d + which * d + col] = s;
             } else {
+                const float* rr = red + (tt % NSLOT) * 4 * RED + 2 * HALF + (e - 2 * W);
+                const float s = (rr[0] + rr[RED]) + (rr[2 * RED] + rr[3 * RED]);
                 part_s[(row * H + h) * 2 + (e - 2 * W)] = s;
             }
         }
         __syncthreads();
     };
-
-    float dS[CPL];
+    // w = [gq partial of token tq | gk partial of token tk] (tq < 0 or tk < 0: skip that half)
+    auto reduce_rows = [&](float (&w)[NV], int tq, int tk) {
+        rows_halving_sum<NV>(w, lane);
 #pragma unroll
-    for (int c = 0; c < CPL; ++c) dS[c] = 0.0f;
+        for (int j = 0; j < NV / 8; ++j) {
+            const int e = hb + j;  // index into [gq CPL | gk CPL] of slice part_ix
+            const int which = e >= CPL;
+            const int tt = which ? tk : tq;
+            if (tt >= 0)
+                red[((tt % NSLOT) * 4 + warp) * RED + which * HALF + part_ix * SLICE + e -
+                    which * CPL] =
+                    w[j];
+        }
+    };
+
+    float2 dS[NP];
+#pragma unroll
+    for (int p = 0; p < NP; ++p) dS[p] = dup2(0.0f);
+
+    // backward step of token tt; P = S_{t-1} (slot tt), Pn <- slot tt - 1.  Also the gq
+    // of token tt - 1, whose state after the update is P.
+    auto bstep = [&](const float2 (&P)[NP], float2 (&Pn)[NP], int pt0, int pn, int tt) {
+        if (tt > 0) ld_slice(sbuf + (size_t)(tt - 1) * kRowThreads * CPL, Pn);
+        const float doj = sdo[tt * kRowsPerCta + rl];
+        const float dop = tt > 0 ? sdo[(tt - 1) * kRowsPerCta + rl] : 0.0f;
+        const float al = GATED ? sa[tt] : 1.0f;
+        const float be = sb[tt * kRowsPerCta + rl];
+        float w[NV];
+        float2 ra = dup2(0.0f), rc = dup2(0.0f), sa2 = dup2(0.0f), sc2 = dup2(0.0f);
+        const float2 do2 = dup2(doj), dp2 = dup2(dop);
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
+            const float2 kp = krow(tt, p);
+            dS[p] = fma2(do2, qrow(tt, p), dS[p]);
+            const float2 g = mul2(P[p], dp2);
+            w[2 * p] = g.x;
+            w[2 * p + 1] = g.y;
+            if (p & 1) {
+                rc = fma2(P[p], kp, rc);
+                sc2 = fma2(dS[p], kp, sc2);
+            } else {
+                ra = fma2(P[p], kp, ra);
+                sa2 = fma2(dS[p], kp, sa2);
+            }
+        }
+        float r = (ra.x + ra.y) + (rc.x + rc.y), dsk = (sa2.x + sa2.y) + (sc2.x + sc2.y);
+        r += __shfl_xor_sync(0xffffffffu, r, 1);
+        dsk += __shfl_xor_sync(0xffffffffu, dsk, 1);
+        r += __shfl_xor_sync(0xffffffffu, r, 2);
+        dsk += __shfl_xor_sync(0xffffffffu, dsk, 2);
+        const float err = sv[tt * kRowsPerCta + rl] - al * r;
+        const float u = be * err;
+        const float bd = be * dsk;
+        if (part_ix == 0) {
+            sgv[tt * kRowsPerCta + rl] = bd;
+            sgb[tt * kRowsPerCta + rl] = err * dsk;
+        }
+        // gk partial: dS u - alpha P (beta dsk); then dS <- alpha (dS - bd k)
+        const float2 u2 = dup2(u), nabd = dup2(-al * bd), nbd = dup2(-bd), al2 = dup2(al);
+        float2 ga2 = dup2(0.0f);
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
+            const float2 g = fma2(dS[p], u2, mul2(nabd, P[p]));
+            w[CPL + 2 * p] = g.x;
+            w[CPL + 2 * p + 1] = g.y;
+            const float2 x = fma2(nbd, krow(tt, p), dS[p]);
+            ga2 = fma2(x, P[p], ga2);
+            dS[p] = GATED ? mul2(al2, x) : x;
+        }
+        reduce_rows(w, tt - 1, tt);
+        // scalars: galpha, and a per-token beta's gradient (one lane per row)
+        float ga = ga2.x + ga2.y;
+        float bsum = (part_ix == 0 && row_ok) ? err * dsk : 0.0f;
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+            ga += __shfl_xor_sync(0xffffffffu, ga, o);
+            bsum += __shfl_xor_sync(0xffffffffu, bsum, o);
+        }
+        if (lane == 0) {
+            red[((tt % NSLOT) * 4 + warp) * RED + 2 * HALF] = ga;
+            red[((tt % NSLOT) * 4 + warp) * RED + 2 * HALF + 1] = bsum;
+        }
+        if (tt % RB == 0) flush(pt0, tt, min(RB, pn - tt));
+    };
 
     for (int ch = nck - 1; ch >= 0; --ch) {
         const int t0 = ch * CK, tn = min(CK, L - t0);
         const int np = (tn + SB - 1) / SB;
         // ---- pass 1: piece-start states from the checkpoint
         {
-            float S[CPL];
+            float2 S[NP];
             const float* src = ck_unit + (long long)ch * d * d + (long long)i * d + c0;
 #pragma unroll
-            for (int c = 0; c < CPL; ++c) S[c] = (row_ok && c0 + c < d) ? src[c] : 0.0f;
+            for (int p = 0; p < NP; ++p)
+                S[p] = make_float2((row_ok && c0 + 2 * p < d) ? src[2 * p] : 0.0f,
+                                   (row_ok && c0 + 2 * p + 1 < d) ? src[2 * p + 1] : 0.0f);
             for (int p = 0; p < np; ++p) {
                 st_slice(pstart + (size_t)p * kRowThreads * CPL, S);
                 if (p == np - 1) break;
@@ -401,99 +495,33 @@ __global__ void __launch_bounds__(kRowThreads, 2)
         for (int p = np - 1; p >= 0; --p) {
             const int pt0 = t0 + p * SB, pn = min(SB, tn - p * SB);
             stage(pt0, pn, true);
-            float S[CPL];
-            ld_slice(pstart + (size_t)p * kRowThreads * CPL, S);
-            for (int tt = 0; tt < pn; ++tt) {
-                st_slice(sbuf + (size_t)tt * kRowThreads * CPL, S);
-                fwd_step(S, tt);
+            {
+                float2 S[NP];
+                ld_slice(pstart + (size_t)p * kRowThreads * CPL, S);
+                for (int tt = 0; tt < pn; ++tt) {
+                    st_slice(sbuf + (size_t)tt * kRowThreads * CPL, S);
+                    fwd_step(S, tt);
+                }
+                // gq of the piece's last token from its state after the update
+                float w[NV];
+                const float2 dl = dup2(sdo[(pn - 1) * kRowsPerCta + rl]);
+#pragma unroll
+                for (int p2 = 0; p2 < NP; ++p2) {
+                    const float2 g = mul2(S[p2], dl);
+                    w[2 * p2] = g.x;
+                    w[2 * p2 + 1] = g.y;
+                    w[CPL + 2 * p2] = 0.0f;
+                    w[CPL + 2 * p2 + 1] = 0.0f;
+                }
+                reduce_rows(w, pn - 1, -1);
             }
-            // S = S_t of the piece's last token; walk back
-            float P[CPL];
-            ld_slice(sbuf + (size_t)(pn - 1) * kRowThreads * CPL, P);
-            for (int tt = pn - 1; tt >= 0; --tt) {
-                float Pn[CPL];
-                if (tt > 0) ld_slice(sbuf + (size_t)(tt - 1) * kRowThreads * CPL, Pn);
-                const float* kr = sk + tt * RP + part_ix * SP;
-                const float* qr = sq + tt * RP + part_ix * SP;
-                const float doi = sdo[tt * kRowsPerCta + rl];
-                const float al = GATED ? sa[tt] : 1.0f;
-                const float be = sb[tt * kRowsPerCta + rl];
-                float* rw = red + ((tt % RB) * 4 + warp) * RED;
-                // gq partial (S_t dO_i) and dS += dO_i q
-                {
-                    float w[NV];
-#pragma unroll
-                    for (int c = 0; c < CPL; c += 4) {
-                        const float4 q4 = *reinterpret_cast<const float4*>(qr + c);
-                        dS[c] = fmaf(doi, q4.x, dS[c]);
-                        dS[c + 1] = fmaf(doi, q4.y, dS[c + 1]);
-                        dS[c + 2] = fmaf(doi, q4.z, dS[c + 2]);
-                        dS[c + 3] = fmaf(doi, q4.w, dS[c + 3]);
-                    }
-#pragma unroll
-                    for (int c = 0; c < CPL; ++c) w[c] = S[c] * doi;
-                    // r = P.k and dsk = dS.k
-                    float r0 = 0.0f, r1 = 0.0f, s0 = 0.0f, s1 = 0.0f;
-#pragma unroll
-                    for (int c = 0; c < CPL; c += 4) {
-                        const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
-                        r0 = fmaf(P[c], k4.x, fmaf(P[c + 1], k4.y, r0));
-                        r1 = fmaf(P[c + 2], k4.z, fmaf(P[c + 3], k4.w, r1));
-                        s0 = fmaf(dS[c], k4.x, fmaf(dS[c + 1], k4.y, s0));
-                        s1 = fmaf(dS[c + 2], k4.z, fmaf(dS[c + 3], k4.w, s1));
-                    }
-                    float r = r0 + r1, dsk = s0 + s1;
-                    r += __shfl_xor_sync(0xffffffffu, r, 1);
-                    dsk += __shfl_xor_sync(0xffffffffu, dsk, 1);
-                    r += __shfl_xor_sync(0xffffffffu, r, 2);
-                    dsk += __shfl_xor_sync(0xffffffffu, dsk, 2);
-                    const float err = sv[tt * kRowsPerCta + rl] - al * r;
-                    const float u = be * err;
-                    const float bd = be * dsk;
-                    if (part_ix == 0) {
-                        sgv[tt * kRowsPerCta + rl] = bd;
-                        sgb[tt * kRowsPerCta + rl] = err * dsk;
-                    }
-                    // gk partial: dS u - alpha P (beta dsk); then dS <- alpha (dS - bd k)
-                    float ga = 0.0f;
-#pragma unroll
-                    for (int c = 0; c < CPL; c += 4) {
-                        const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
-                        const float kv[4] = {k4.x, k4.y, k4.z, k4.w};
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            w[CPL + c + e] = fmaf(dS[c + e], u, -al * bd * P[c + e]);
-                            const float x = fmaf(-bd, kv[e], dS[c + e]);
-                            ga = fmaf(x, P[c + e], ga);
-                            dS[c + e] = GATED ? al * x : x;
-                        }
-                    }
-                    rows_halving_sum<NV>(w, lane);
-#pragma unroll
-                    for (int j = 0; j < NV / 8; ++j) {
-                        const int e = hb + j;  // index into [gq CPL | gk CPL] of slice part_ix
-                        const int which = e >= CPL, col = c0 + e - which * CPL;
-                        rw[which * W + col] = w[j];
-                    }
-                    // scalars: galpha, and a per-token beta's gradient (one lane per row)
-                    float bsum = (part_ix == 0 && row_ok) ? err * dsk : 0.0f;
-#pragma unroll
-                    for (int o = 16; o >= 1; o >>= 1) {
-                        ga += __shfl_xor_sync(0xffffffffu, ga, o);
-                        bsum += __shfl_xor_sync(0xffffffffu, bsum, o);
-                    }
-                    if (lane == 0) {
-                        rw[2 * W] = ga;
-                        rw[2 * W + 1] = bsum;
-                    }
-                }
-#pragma unroll
-                for (int c = 0; c < CPL; ++c) S[c] = P[c];
-                if (tt > 0) {
-#pragma unroll
-                    for (int c = 0; c < CPL; ++c) P[c] = Pn[c];
-                }
-                if (tt % RB == 0) flush(pt0 + tt, min(RB, pn - tt));
+            // walk back; the two state buffers trade roles every token
+            float2 A[NP], Bv[NP];
+            ld_slice(sbuf + (size_t)(pn - 1) * kRowThreads * CPL, A);
+            for (int tt = pn - 1; tt >= 0; tt -= 2) {
+                bstep(A, Bv, pt0, pn, tt);
+                if (tt == 0) break;
+                bstep(Bv, A, pt0, pn, tt - 1);
             }
             // this piece's gv and per-element gbeta rows
             for (int idx = tid; idx < pn * kRowsPerCta; idx += kRowThreads) {
