@@ -45,8 +45,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["linear", "mingru", "ssm", "ssm_model", "attn", "delta",
-                                         "delta_model", "gated"],
+    ap.add_argument("--config", choices=["linear", "mingru", "ssm", "ssm_model", "attn", "laser",
+                                         "delta", "delta_model", "gated"],
                     default="linear")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--replicate", action="store_true",
@@ -502,6 +502,65 @@ class AttnWorkload:
                 "(4 q heads) at L=1024, scaled to the step by FLOP share")
 
 
+class LaserWorkload(AttnWorkload):
+    """LASER attention (fused_scan.ex:3593-3611, 3667-3766) fwd + bwd at the configs[3]
+    shapes (causal, grouped heads): the flash kernels on exp(V - v_max) plus the
+    element-wise passes (v_max, exp, log, dO / A, dV' exp(V - v_max))."""
+
+    def __init__(self):
+        import dataclasses
+        super().__init__()
+        self.cfg = dataclasses.replace(self.cfg, name="laser_attention_cfg3")
+        self.kname = "laser_attention"
+
+    def describe(self, world):
+        d = super().describe(world)
+        d["workload"] = "%s fwd+bwd (configs[3] shapes)" % self.cfg.name
+        return d
+
+    launches_per_step = 9  # vmax, exp, flash fwd, log; dR, rowdot, flash bwd, dq convert, dV
+
+    def step(self, ev=None):
+        from edifice_b200 import fused_scan as fs
+        if ev:
+            ev[0].record()
+        _, resid = fs.laser_attention(self.q, self.k, self.v, causal=True, return_resid=True)
+        if ev:
+            ev[1].record()
+        fs.laser_attention_backward(self.q, self.k, self.v, self.do, resid, causal=True)
+        if ev:
+            ev[2].record()
+
+    def e2e_step(self, dev_in):
+        from edifice_b200 import fused_scan as fs
+        q, k, v, do = dev_in
+        o, resid = fs.laser_attention(q, k, v, causal=True, return_resid=True)
+        return (o,) + tuple(fs.laser_attention_backward(q, k, v, do, resid, causal=True))
+
+    api = "edifice_b200.fused_scan.laser_attention + laser_attention_backward"
+
+    def cpu_step(self, rows=None, prec="f32"):
+        import numpy as np
+        import oracle as O
+        c = self.cfg
+        Ls = 1024
+        if not hasattr(self, "_cpu_l"):
+            rng = np.random.default_rng(0)
+            q = rng.standard_normal((1, 4, Ls, c.head_dim), dtype=np.float32)
+            k = rng.standard_normal((1, 1, Ls, c.head_dim), dtype=np.float32)
+            v = rng.standard_normal((1, 1, Ls, c.head_dim), dtype=np.float32)
+            do = rng.standard_normal((1, 4, Ls, c.head_dim), dtype=np.float32)
+            self._cpu_l = (q, k, v, do)
+        q, k, v, do = self._cpu_l
+        O.laser_fwd(q, k, v, causal=True, prec=prec)
+        O.laser_bwd(q, k, v, do, causal=True, prec=prec)
+        f_sample = 4.0 * 4 * Ls * Ls * c.head_dim / 2 * 3.5
+        return c.tokens * f_sample / (c.flops_fwd() + c.flops_bwd())
+
+    cpu_what = ("oracle f32 port (fused_scan.ex:3667-3766) on one kv group (4 q heads) at "
+                "L=1024, scaled to the step by FLOP share")
+
+
 class DeltaWorkload:
     """DeltaNet delta rule fwd (with state checkpoints) + bwd."""
 
@@ -737,6 +796,7 @@ class GatedDeltaWorkload(DeltaWorkload):
 
 WORKLOADS = {"linear": lambda: ScanWorkload(False), "mingru": lambda: ScanWorkload(True),
              "ssm": SsmWorkload, "ssm_model": SsmModelWorkload, "attn": AttnWorkload,
+             "laser": LaserWorkload,
              "delta": DeltaWorkload, "delta_model": DeltaModelWorkload,
              "gated": GatedDeltaWorkload}
 
@@ -909,7 +969,8 @@ def run_ours(args):
     if args.config == "linear" and not args.no_paths:
         del wl.a, wl.b, wl.dy
         torch.cuda.empty_cache()
-        for name in ("mingru", "attn", "delta", "delta_model", "gated", "ssm", "ssm_model"):
+        for name in ("mingru", "attn", "laser", "delta", "delta_model", "gated", "ssm",
+                     "ssm_model"):
             pw = WORKLOADS[name]()
             pw._world = world
             pw.setup(dev, rank)

@@ -602,6 +602,64 @@ class FlashAttentionFn(torch.autograd.Function):
         return dq, dk, dv, None
 
 
+# --------------------------------------------------------------- LASER attention
+def laser_attention(q, k, v, causal=True, v_max=None, scale=None, return_resid=False):
+    """FusedScan.laser_attention/4 (fused_scan.ex:3593-3611): attention over
+    exp(V - v_max), O = log(max(A, 1e-7)) + v_max, with v_max the max over the
+    sequence of v (computed when None, else [B, Hkv, d] as the reference passes it).
+    q [B, Hq, L, d], k / v [B, Hkv, L, d].  return_resid adds the buffer
+    laser_attention_backward reads."""
+    _dev(q, k, v, v_max, what="laser_attention")
+    B, Hq, Hkv, L, d = _attn_shapes(q, k, v)
+    code = _dtype_code(q, "laser_attention")
+    lib = _lib.load()
+    o = torch.empty_like(q)
+    resid = torch.empty(lib.edb_laser_attention_resid_bytes(code, B, Hq, Hkv, L, d),
+                        dtype=torch.uint8, device=q.device)
+    _lib.check(lib.edb_laser_attention_fwd(code, _p(q), _p(k), _p(v), _p(v_max), _p(o),
+                                           _p(resid), B, Hq, Hkv, L, d, int(bool(causal)),
+                                           float(scale or 0.0), _stream()),
+               "CUDA LASER attention")
+    return (o, resid) if return_resid else o
+
+
+def laser_attention_backward(q, k, v, grad_output, resid, causal=True, scale=None):
+    """Returns (grad_q, grad_k, grad_v) of laser_attention from its resid; mirrors
+    laser_attention_backward_dispatch (fused_scan.ex:3705-3721, 3723-3766)."""
+    _dev(q, k, v, grad_output, resid, what="laser_attention_backward")
+    B, Hq, Hkv, L, d = _attn_shapes(q, k, v)
+    code = _dtype_code(q, "laser_attention_backward")
+    lib = _lib.load()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    wsb = lib.edb_laser_attention_bwd_workspace(code, B, Hq, Hkv, L, d)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=q.device)
+    _lib.check(lib.edb_laser_attention_bwd(code, _p(q), _p(k), _p(grad_output), _p(resid),
+                                           _p(dq), _p(dk), _p(dv), B, Hq, Hkv, L, d,
+                                           int(bool(causal)), float(scale or 0.0), _p(ws), wsb,
+                                           _stream()),
+               "CUDA LASER attention backward")
+    return dq, dk, dv
+
+
+class LaserAttentionFn(torch.autograd.Function):
+    """custom_grad wiring of laser_attention_custom_call (fused_scan.ex:3615-3633):
+    gradients to q, k, v (v_max held constant)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, causal=True):
+        o, resid = laser_attention(q, k, v, causal=causal, return_resid=True)
+        ctx.causal = causal
+        ctx.save_for_backward(q, k, v, resid)
+        return o
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        q, k, v, resid = ctx.saved_tensors
+        dq, dk, dv = laser_attention_backward(q, k, v, grad_output.contiguous(), resid,
+                                              causal=ctx.causal)
+        return dq, dk, dv, None
+
+
 # ------------------------------------------- attention callers routed to flash
 def _attend(q, k, v, causal):
     """[B, H, L, d] attention through the flash kernel, with gradients when any

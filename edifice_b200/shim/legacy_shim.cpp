@@ -99,6 +99,48 @@ int fused_diag_linear_scan_backward_launch(cudaStream_t stream, const edb_io_t* 
                                              output_concat, batch, seq_len, hidden);
 }
 
+int fused_laser_attention_launch(cudaStream_t stream, const edb_io_t* q, const edb_io_t* k,
+                                 const edb_io_t* v, const edb_io_t* v_max, edb_io_t* output,
+                                 int batch, int num_heads, int seq_len, int head_dim,
+                                 int causal) {
+    const size_t rb = edb_laser_attention_resid_bytes(kDtype, batch, num_heads, num_heads,
+                                                      seq_len, head_dim);
+    void* resid = nullptr;
+    cudaError_t e = cudaMallocAsync(&resid, rb ? rb : 256, stream);
+    if (e != cudaSuccess) return (int)e;
+    int st = edb_laser_attention_fwd(kDtype, q, k, v, v_max, output, resid, batch, num_heads,
+                                     num_heads, seq_len, head_dim, causal, 0.0f, stream);
+    cudaFreeAsync(resid, stream);
+    return st;
+}
+
+int fused_laser_attention_backward_launch(cudaStream_t stream, const edb_io_t* q,
+                                          const edb_io_t* k, const edb_io_t* v,
+                                          const edb_io_t* v_max, const edb_io_t* o,
+                                          const edb_io_t* grad_o, edb_io_t* output_concat,
+                                          int batch, int num_heads, int seq_len, int head_dim,
+                                          int causal) {
+    (void)o;  // the residual is rebuilt by a forward pass; its output lands in dq first
+    const long long n = (long long)batch * num_heads * seq_len * head_dim;
+    const size_t rb = edb_laser_attention_resid_bytes(kDtype, batch, num_heads, num_heads,
+                                                      seq_len, head_dim);
+    const size_t wb = edb_laser_attention_bwd_workspace(kDtype, batch, num_heads, num_heads,
+                                                        seq_len, head_dim);
+    void* buf = nullptr;
+    cudaError_t e = cudaMallocAsync(&buf, rb + wb, stream);
+    if (e != cudaSuccess) return (int)e;
+    int st = edb_laser_attention_fwd(kDtype, q, k, v, v_max, output_concat, buf, batch,
+                                     num_heads, num_heads, seq_len, head_dim, causal, 0.0f,
+                                     stream);
+    if (st == 0)
+        st = edb_laser_attention_bwd(kDtype, q, k, grad_o, buf, output_concat, output_concat + n,
+                                     output_concat + 2 * n, batch, num_heads, num_heads, seq_len,
+                                     head_dim, causal, 0.0f, static_cast<char*>(buf) + rb, wb,
+                                     stream);
+    cudaFreeAsync(buf, stream);
+    return st;
+}
+
 int fused_selective_scan_launch(cudaStream_t stream, const edb_io_t* x, const edb_io_t* dt,
                                 const edb_io_t* A, const edb_io_t* B, const edb_io_t* C,
                                 edb_io_t* out, int batch, int seq_len, int hidden, int state) {

@@ -245,6 +245,37 @@ int edb_flash_attention_bwd(int dtype, const void* q, const void* k, const void*
                             void* stream);
 
 /* ------------------------------------------------------------------------
+ * LASER attention (attention over exp(V)):
+ *   A = softmax(Q K^T scale (+ causal mask)) exp(V - v_max);  O = log(max(A, 1e-7)) + v_max
+ * q, o [B, Hq, L, d]; k, v [B, Hkv, L, d] (Hq a multiple of Hkv, grouped heads);
+ * v_max [B, Hkv, d] in `dtype` (the reference's argument: the max over the sequence
+ * of v), or NULL to have it computed.  scale <= 0 means 1/sqrt(d).  resid
+ * (edb_laser_attention_resid_bytes(), 256-byte aligned) receives what the backward
+ * reads.  The contractions run the flash-attention kernels above on exp(V - v_max).
+ * Replaces fused_laser_attention_launch (native/cuda/fused_laser_attention.cu:156-178);
+ * Nx semantics lib/edifice/cuda/fused_scan.ex:3593-3611, 3667-3703.
+ * ---------------------------------------------------------------------- */
+size_t edb_laser_attention_resid_bytes(int dtype, int batch, int q_heads, int kv_heads,
+                                       int seq_len, int head_dim);
+
+int edb_laser_attention_fwd(int dtype, const void* q, const void* k, const void* v,
+                            const void* v_max, void* o, void* resid, int batch, int q_heads,
+                            int kv_heads, int seq_len, int head_dim, int causal, float scale,
+                            void* stream);
+
+size_t edb_laser_attention_bwd_workspace(int dtype, int batch, int q_heads, int kv_heads,
+                                         int seq_len, int head_dim);
+
+/* Backward from the forward's resid and dO: dq [B,Hq,L,d], dk/dv [B,Hkv,L,d]; v_max
+ * gets no gradient (the reference holds it constant).  Workspace 256-byte aligned.
+ * Replaces fused_laser_attention_backward_launch
+ * (native/cuda/fused_laser_attention_backward.cu:372-420); fused_scan.ex:3723-3766. */
+int edb_laser_attention_bwd(int dtype, const void* q, const void* k, const void* dO,
+                            const void* resid, void* dq, void* dk, void* dv, int batch,
+                            int q_heads, int kv_heads, int seq_len, int head_dim, int causal,
+                            float scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * DeltaNet delta rule.  Per (batch, head), S_0 = 0:
  *   r = S_{t-1} k_t;  S_t = S_{t-1} + (beta_t (.) (v_t - r)) k_t^T;  o_t = S_t q_t
  * q, k, v, o: [batch, seq_len, heads, head_dim] (k L2-normalised by the

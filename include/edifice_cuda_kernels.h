@@ -81,6 +81,19 @@ int fused_diag_linear_scan_backward_launch(cudaStream_t stream, const edb_io_t* 
                                            const edb_io_t* grad_output, edb_io_t* output_concat,
                                            int batch, int seq_len, int hidden);
 
+/* native/cuda/fused_laser_attention.cu:156-178 (equal heads; v_max [B, H, d]) */
+int fused_laser_attention_launch(cudaStream_t stream, const edb_io_t* q, const edb_io_t* k,
+                                 const edb_io_t* v, const edb_io_t* v_max, edb_io_t* output,
+                                 int batch, int num_heads, int seq_len, int head_dim, int causal);
+
+/* native/cuda/fused_laser_attention_backward.cu:372-420; output_concat = [dq | dk | dv] */
+int fused_laser_attention_backward_launch(cudaStream_t stream, const edb_io_t* q,
+                                          const edb_io_t* k, const edb_io_t* v,
+                                          const edb_io_t* v_max, const edb_io_t* o,
+                                          const edb_io_t* grad_o, edb_io_t* output_concat,
+                                          int batch, int num_heads, int seq_len, int head_dim,
+                                          int causal);
+
 /* native/cuda/fused_selective_scan.cu:105-124 (dt clamp [0.001, 0.1]) */
 int fused_selective_scan_launch(cudaStream_t stream, const edb_io_t* x, const edb_io_t* dt,
                                 const edb_io_t* A, const edb_io_t* B, const edb_io_t* C,

@@ -256,6 +256,41 @@ def attention_bwd(q, k, v, dO, causal=True, prec="f64"):
     return dq, dk, dv
 
 
+# ------------------------------------------------------------- LASER attention
+# lib/edifice/cuda/fused_scan.ex:3593-3611 (v_max = max over the sequence of v),
+# laser_attention_fallback :3667-3703 and laser_attention_backward_fallback
+# :3723-3766, composed from the attention restatement above: the values are
+# exp(V - v_max) (taken in f64, rounded to f32 on the way in), the log and the
+# gradient pre/post-scaling in f64.  v_max is a constant for the gradient, as in
+# the reference.
+def _laser_parts(v, v_max):
+    v64 = np.asarray(v, np.float64)
+    vm = v64.max(axis=2, keepdims=True) if v_max is None else \
+        np.asarray(v_max, np.float64)[:, :, None, :]
+    return vm, np.exp(v64 - vm)
+
+
+def _expand_heads(x, hq):
+    """[B, Hkv, ...] -> [B, Hq, ...] (each kv head repeated over its query group)."""
+    return np.repeat(x, hq // x.shape[1], axis=1)
+
+
+def laser_fwd(q, k, v, causal=True, v_max=None, prec="f64"):
+    """Returns (O, A): the output and the attention output before the log."""
+    vm, ev = _laser_parts(v, v_max)
+    A = attention_fwd(q, k, ev, causal=causal, prec=prec).astype(np.float64)
+    O = np.log(np.maximum(A, 1e-7)) + _expand_heads(vm, A.shape[1])
+    return O.astype(np.float32), A
+
+
+def laser_bwd(q, k, v, dO, causal=True, v_max=None, prec="f64"):
+    vm, ev = _laser_parts(v, v_max)
+    A = attention_fwd(q, k, ev, causal=causal, prec=prec).astype(np.float64)
+    dR = np.asarray(dO, np.float64) / np.maximum(A, 1e-7)
+    dq, dk, dev = attention_bwd(q, k, ev, dR, causal=causal, prec=prec)
+    return dq, dk, (dev.astype(np.float64) * ev).astype(np.float32)
+
+
 # ---------------------------------------------- the reference's own C refs
 def ref_linear_scan_cpu(a, b, h0):
     r = ref_cpu_lib()

@@ -291,3 +291,73 @@ def test_sdpa_compute_and_multi_head_sdpa(cuda, causal):
     band = torch.ones(L, L, dtype=torch.bool, device="cuda").triu(-4).tril()
     with pytest.raises(RuntimeError):
         fs.multi_head_sdpa(qh, kh, vh, mask=band)
+
+
+# ---------------------------------------------------------------- LASER attention
+LASER_CASES = [
+    # (B, Hq, Hkv, L, d)
+    (2, 4, 4, 200, 128),   # equal heads (the reference's form), tcgen05 path in bf16
+    (1, 8, 2, 300, 128),   # grouped heads, partial last tile
+    (2, 2, 2, 129, 64),    # head_dim 64
+    (1, 4, 1, 77, 96),     # SIMT path
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("case", LASER_CASES)
+@pytest.mark.parametrize("causal", [True, False])
+def test_laser_attention(cuda, dtype, case, causal):
+    """LASER (fused_scan.ex:3593-3611, 3667-3766) forward and backward against the
+    oracle on the same rounded inputs."""
+    q, k, v, do = attn_inputs(*case, dtype, seed=71)
+    o, resid = fs.laser_attention(q, k, v, causal=causal, return_resid=True)
+    dq, dk, dv = fs.laser_attention_backward(q, k, v, do, resid, causal=causal)
+    torch.cuda.synchronize()
+    ro, _ = O.laser_fwd(_np(q), _np(k), _np(v), causal=causal)
+    assert O.norm_rel(_np(o), ro) <= TOL[dtype]
+    for got, ref in zip((dq, dk, dv), O.laser_bwd(_np(q), _np(k), _np(v), _np(do),
+                                                  causal=causal)):
+        assert O.norm_rel(_np(got), ref) <= TOL[dtype], O.norm_rel(_np(got), ref)
+    assert device_errors() == 0
+
+
+def test_laser_given_v_max_and_autograd(cuda):
+    """A caller-given v_max (the reference's argument) equal to the computed one
+    gives the same bits; the autograd wiring matches the explicit backward."""
+    q, k, v, do = attn_inputs(2, 4, 2, 150, 128, torch.bfloat16, seed=72)
+    vmax = v.amax(dim=2)
+    o1 = fs.laser_attention(q, k, v)
+    o2 = fs.laser_attention(q, k, v, v_max=vmax.contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2)
+    leaves = [t.clone().requires_grad_(True) for t in (q, k, v)]
+    fs.LaserAttentionFn.apply(*leaves, True).backward(do)
+    _, resid = fs.laser_attention(q, k, v, return_resid=True)
+    want = fs.laser_attention_backward(q, k, v, do, resid)
+    for leaf, w in zip(leaves, want):
+        assert torch.equal(leaf.grad, w)
+
+
+@pytest.mark.parametrize("prec,dtype", [("f32", torch.float32), ("bf16", torch.bfloat16)])
+def test_laser_shim_symbols(cuda, prec, dtype):
+    """fused_laser_attention_launch / _backward_launch (equal heads, NULL stream,
+    [dq | dk | dv] concatenated) match the edb_* path."""
+    lib = ctypes.CDLL(build.SHIMS[prec])
+    B, H, L, d = 2, 2, 96, 64
+    q, k, v, do = attn_inputs(B, H, H, L, d, dtype, seed=73)
+    vmax = v.amax(dim=2).contiguous()
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    out = torch.empty_like(q)
+    assert lib.fused_laser_attention_launch(None, P(q), P(k), P(v), P(vmax), P(out), B, H, L, d,
+                                            1) == 0
+    cat = torch.empty(3 * q.numel(), dtype=dtype, device="cuda")
+    assert lib.fused_laser_attention_backward_launch(None, P(q), P(k), P(v), P(vmax), P(out),
+                                                     P(do), P(cat), B, H, L, d, 1) == 0
+    torch.cuda.synchronize()
+    o, resid = fs.laser_attention(q, k, v, return_resid=True)
+    want = fs.laser_attention_backward(q, k, v, do, resid)
+    torch.cuda.synchronize()
+    assert torch.equal(out, o)
+    n = q.numel()
+    for i, w in enumerate(want):
+        assert torch.equal(cat[i * n:(i + 1) * n].view_as(w), w)

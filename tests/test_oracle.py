@@ -209,6 +209,29 @@ def test_selective_scan_model_semantics_autograd(given_a):
                                       O.selective_scan_model_fwd(x, dt, Bm, Cm))
 
 
+@pytest.mark.parametrize("causal", [True, False])
+def test_laser_attention_autograd(causal):
+    """LASER (fused_scan.ex:3667-3703 forward, :3723-3766 backward) in torch f64:
+    the oracle's composition matches the restated fallback and its autograd (v_max
+    held constant, as the reference captures it)."""
+    rng = np.random.default_rng(9)
+    B, H, L, d = 2, 3, 21, 8
+    q, k, v, do = (rng.standard_normal((B, H, L, d)).astype(np.float32) for _ in range(4))
+    tq, tk, tv = _t(q), _t(k), _t(v)
+    vm = tv.detach().amax(2, keepdim=True)
+    s = tq @ tk.transpose(-1, -2) / np.sqrt(d)
+    if causal:
+        s = s.masked_fill(~torch.ones(L, L, dtype=torch.bool).tril(), float("-inf"))
+    A = torch.softmax(s, -1) @ torch.exp(tv - vm)
+    o = torch.log(A.clamp_min(1e-7)) + vm
+    o.backward(torch.tensor(do, dtype=torch.float64))
+    got_o, got_a = O.laser_fwd(q, k, v, causal=causal)
+    np.testing.assert_allclose(got_o, o.detach().numpy(), rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(got_a, A.detach().numpy(), rtol=1e-5, atol=1e-6)
+    for got, ref in zip(O.laser_bwd(q, k, v, do, causal=causal), (tq, tk, tv)):
+        np.testing.assert_allclose(got, ref.grad.numpy(), rtol=1e-4, atol=1e-5)
+
+
 @pytest.mark.parametrize("scalar_beta", [False, True])
 def test_delta_net_bwd_autograd(scalar_beta):
     rng = np.random.default_rng(5)
