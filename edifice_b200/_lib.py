@@ -63,6 +63,12 @@ SIGNATURES = {
     "edb_laser_attention_bwd_workspace": (_sz, [_i, _i, _i, _i, _i, _i]),
     "edb_laser_attention_bwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
                                      _i, _f, _vp, _sz, _vp]),
+    "edb_fox_attention_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f,
+                                   _vp]),
+    "edb_fox_attention_bwd_workspace": (_sz, [_i, _i, _i, _i, _i, _i]),
+    "edb_fox_attention_bwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
+                                   _i, _i, _i, _i, _f, _vp, _sz, _vp]),
+    "edb_convert": (_i, [_i, _vp, _i, _vp, _sz, _vp]),
     "edb_flash_attention_bwd_workspace": (_sz, [_i, _i, _i, _i, _i, _i, _i]),
     "edb_flash_attention_bwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i,
                                      _i, _i, _i, _i, _f, _vp, _sz, _vp]),

@@ -366,7 +366,7 @@ template <typename T, int HDMAX>
 __global__ void __launch_bounds__(128)
     attn_fwd_simt_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                          T* __restrict__ o, float* __restrict__ lse, int L, int Hq, int Hkv, int d,
-                         int causal, float scale) {
+                         int causal, float scale, const float* __restrict__ cs = nullptr) {
     constexpr int TK = 32;
     __shared__ float sk[TK][HDMAX];
     __shared__ float sv[TK][HDMAX];
@@ -401,6 +401,7 @@ __global__ void __launch_bounds__(128)
             if (causal && j > i) break;
             float s = 0.0f;
             for (int e = 0; e < HDMAX; ++e) s = fmaf(qv[e], sk[r][e], s);
+            if (cs != nullptr) s = fmaf(-cs[((long long)b * Hq + hq) * L + j], kLog2e, s);
             const float mn = fmaxf(m, s);
             const float a = exp2f(m - mn), p = exp2f(s - mn);
             l = l * a + p;
@@ -441,17 +442,21 @@ int launch_fwd_tc(const void* q, const void* k, const void* v, void* o, float* l
 
 template <typename T>
 int launch_fwd_simt(const void* q, const void* k, const void* v, void* o, float* lse, int B,
-                    int Hq, int Hkv, int L, int d, int causal, float scale, cudaStream_t st) {
+                    int Hq, int Hkv, int L, int d, int causal, float scale, cudaStream_t st,
+                    const float* cs = nullptr) {
     dim3 grid((L + 127) / 128, Hq, B);
     if (d <= 32)
         attn_fwd_simt_kernel<T, 32><<<grid, 128, 0, st>>>((const T*)q, (const T*)k, (const T*)v,
-                                                          (T*)o, lse, L, Hq, Hkv, d, causal, scale);
+                                                          (T*)o, lse, L, Hq, Hkv, d, causal, scale,
+                                                          cs);
     else if (d <= 64)
         attn_fwd_simt_kernel<T, 64><<<grid, 128, 0, st>>>((const T*)q, (const T*)k, (const T*)v,
-                                                          (T*)o, lse, L, Hq, Hkv, d, causal, scale);
+                                                          (T*)o, lse, L, Hq, Hkv, d, causal, scale,
+                                                          cs);
     else
         attn_fwd_simt_kernel<T, 128><<<grid, 128, 0, st>>>((const T*)q, (const T*)k, (const T*)v,
-                                                           (T*)o, lse, L, Hq, Hkv, d, causal, scale);
+                                                           (T*)o, lse, L, Hq, Hkv, d, causal, scale,
+                                                           cs);
     return edb::status_from_cuda(cudaGetLastError());
 }
 
@@ -504,4 +509,23 @@ extern "C" int edb_flash_attention_fwd(int dtype, const void* q, const void* k, 
                                                 head_dim, causal, scale, st)
                : launch_fwd_simt<float>(q, k, v, o, lse, batch, q_heads, kv_heads, seq_len,
                                         head_dim, causal, scale, st);
+}
+
+// ------------------------------------------------------------ FoX attention forward
+extern "C" int edb_fox_attention_fwd(int dtype, const void* q, const void* k, const void* v,
+                                     const float* cs, void* o, float* lse, int B, int Hq, int Hkv,
+                                     int L, int d, float scale, void* stream) {
+    if (dtype != EDB_F32 && dtype != EDB_BF16) return EDB_ERR_BAD_DTYPE;
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || L <= 0 || d <= 0) return EDB_ERR_BAD_SHAPE;
+    if (Hq % Hkv != 0) return EDB_ERR_BAD_SHAPE;
+    if (d > 128) return EDB_ERR_UNSUPPORTED;
+    if (!q || !k || !v || !cs || !o || !lse) return EDB_ERR_NULL_POINTER;
+    if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)d);
+    cudaStream_t st = (cudaStream_t)stream;
+    // SIMT kernels: a tcgen05 variant with the bias in the softmax warps did not
+    // complete on the B200 and is not built
+    return dtype == EDB_BF16
+               ? launch_fwd_simt<__nv_bfloat16>(q, k, v, o, lse, B, Hq, Hkv, L, d, 1, scale, st,
+                                                cs)
+               : launch_fwd_simt<float>(q, k, v, o, lse, B, Hq, Hkv, L, d, 1, scale, st, cs);
 }

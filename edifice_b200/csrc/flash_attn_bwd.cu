@@ -482,7 +482,8 @@ __global__ void attn_bwd_dq_simt_kernel(const T* __restrict__ q, const T* __rest
                                         const T* __restrict__ v, const T* __restrict__ dO,
                                         const float* __restrict__ lse, const float* __restrict__ Dv,
                                         T* __restrict__ dq, int L, int Hq, int Hkv, int d,
-                                        int causal, float scale) {
+                                        int causal, float scale,
+                                        const float* __restrict__ cs = nullptr) {
     const int hq = blockIdx.y, b = blockIdx.z;
     const int hk = hq / (Hq / Hkv);
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -504,7 +505,8 @@ __global__ void attn_bwd_dq_simt_kernel(const T* __restrict__ q, const T* __rest
             s = fmaf(qv[e], ld_scalar<T>(kb + (long long)j * d + e), s);
             dp = fmaf(dov[e], ld_scalar<T>(vb + (long long)j * d + e), dp);
         }
-        const float p = exp2f(s * scale * kLog2e - l2);
+        const float bias = cs != nullptr ? cs[((long long)b * Hq + hq) * L + j] * kLog2e : 0.0f;
+        const float p = exp2f(s * scale * kLog2e - l2 - bias);
         const float ds = p * (dp - Di) * scale;
         for (int e = 0; e < d; ++e) acc[e] = fmaf(ds, ld_scalar<T>(kb + (long long)j * d + e), acc[e]);
     }
@@ -517,7 +519,9 @@ __global__ void attn_bwd_dkdv_simt_kernel(const T* __restrict__ q, const T* __re
                                           const float* __restrict__ lse,
                                           const float* __restrict__ Dv, T* __restrict__ dk,
                                           T* __restrict__ dvo, int L, int Hq, int Hkv, int d,
-                                          int causal, float scale) {
+                                          int causal, float scale,
+                                          const float* __restrict__ cs = nullptr,
+                                          float* __restrict__ cs_part = nullptr) {
     const int hk = blockIdx.y, b = blockIdx.z;
     const int j = blockIdx.x * blockDim.x + threadIdx.x;
     if (j >= L) return;
@@ -532,6 +536,8 @@ __global__ void attn_bwd_dkdv_simt_kernel(const T* __restrict__ q, const T* __re
     }
     for (int g = 0; g < G; ++g) {
         const long long bh = (long long)b * Hq + hk * G + g;
+        const float bias = cs != nullptr ? cs[bh * L + j] * kLog2e : 0.0f;
+        float dssum = 0.0f;
         for (int i = causal ? j : 0; i < L; ++i) {
             const long long row = bh * L + i;
             float s = 0.0f, dp = 0.0f;
@@ -539,18 +545,32 @@ __global__ void attn_bwd_dkdv_simt_kernel(const T* __restrict__ q, const T* __re
                 s = fmaf(ld_scalar<T>(q + row * d + e), kv[e], s);
                 dp = fmaf(ld_scalar<T>(dO + row * d + e), vv[e], dp);
             }
-            const float p = exp2f(s * scale * kLog2e - lse[row] * kLog2e);
+            const float p = exp2f(s * scale * kLog2e - lse[row] * kLog2e - bias);
             const float ds = p * (dp - Dv[row]) * scale;
+            dssum += ds;
             for (int e = 0; e < d; ++e) {
                 ak[e] = fmaf(ds, ld_scalar<T>(q + row * d + e), ak[e]);
                 av[e] = fmaf(p, ld_scalar<T>(dO + row * d + e), av[e]);
             }
+        }
+        if (cs_part != nullptr) {  // one writer per (bh, j): the second half is zero
+            const long long bhq = (long long)gridDim.z * Hq;
+            cs_part[bh * L + j] = dssum;
+            cs_part[(bhq + bh) * L + j] = 0.0f;
         }
     }
     for (int e = 0; e < d; ++e) {
         st_scalar<T>(dk + krow * d + e, ak[e]);
         st_scalar<T>(dvo + krow * d + e, av[e]);
     }
+}
+
+// grad_cs = -(part[0] + part[1]) / scale: the two halves' column sums of dS (which
+// carry the softmax scale) for the key side; the query side (row sums of dS) is zero.
+__global__ void fox_dcs_kernel(const float* __restrict__ part, float* __restrict__ dcs, long long n,
+                               float inv_scale) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) dcs[i] = -(part[i] + part[n + i]) * inv_scale;
 }
 
 size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -584,15 +604,17 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dO, c
 template <typename T>
 int launch_bwd_simt(const void* q, const void* k, const void* v, const void* dO, const float* lse,
                     const float* D, void* dq, void* dk, void* dv, int B, int Hq, int Hkv, int L,
-                    int d, int causal, float scale, cudaStream_t st) {
+                    int d, int causal, float scale, cudaStream_t st, const float* cs = nullptr,
+                    float* cs_part = nullptr) {
     dim3 gq((L + 63) / 64, Hq, B), gk((L + 63) / 64, Hkv, B);
 #define EDB_SIMT_BWD(HDM)                                                                        \
     attn_bwd_dq_simt_kernel<T, HDM><<<gq, 64, 0, st>>>((const T*)q, (const T*)k, (const T*)v,   \
                                                        (const T*)dO, lse, D, (T*)dq, L, Hq, Hkv, \
-                                                       d, causal, scale);                        \
+                                                       d, causal, scale, cs);                    \
     attn_bwd_dkdv_simt_kernel<T, HDM><<<gk, 64, 0, st>>>((const T*)q, (const T*)k, (const T*)v, \
                                                          (const T*)dO, lse, D, (T*)dk, (T*)dv,  \
-                                                         L, Hq, Hkv, d, causal, scale);
+                                                         L, Hq, Hkv, d, causal, scale, cs,      \
+                                                         cs_part);
     if (d <= 32) {
         EDB_SIMT_BWD(32)
     } else if (d <= 64) {
@@ -721,4 +743,61 @@ extern "C" int edb_flash_attention_bwd(int dtype, const void* q, const void* k, 
                                                 kv_heads, seq_len, head_dim, causal, scale, st)
                : launch_bwd_simt<float>(q, k, v, dO, L_, D, dq, dk, dv, batch, q_heads, kv_heads,
                                         seq_len, head_dim, causal, scale, st);
+}
+
+// ------------------------------------------------------------ FoX attention backward
+extern "C" size_t edb_fox_attention_bwd_workspace(int dtype, int batch, int q_heads,
+                                                  int kv_heads, int seq_len, int head_dim) {
+    if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || seq_len <= 0 || head_dim <= 0) return 0;
+    const size_t rows = (size_t)batch * q_heads * seq_len;
+    return a256(rows * 4) + a256(2 * rows * 4);  // D, the two cs partial halves
+}
+
+extern "C" int edb_fox_attention_bwd(int dtype, const void* q, const void* k, const void* v,
+                                     const float* cs, const void* o, const void* dO,
+                                     const float* lse, void* dq, void* dk, void* dv, float* dcs,
+                                     int batch, int q_heads, int kv_heads, int seq_len,
+                                     int head_dim, float scale, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+    if (dtype != EDB_F32 && dtype != EDB_BF16) return EDB_ERR_BAD_DTYPE;
+    if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || seq_len <= 0 || head_dim <= 0)
+        return EDB_ERR_BAD_SHAPE;
+    if (q_heads % kv_heads != 0) return EDB_ERR_BAD_SHAPE;
+    if (head_dim > 128) return EDB_ERR_UNSUPPORTED;
+    if (!q || !k || !v || !cs || !o || !dO || !lse || !dq || !dk || !dv || !dcs)
+        return EDB_ERR_NULL_POINTER;
+    const size_t need = edb_fox_attention_bwd_workspace(dtype, batch, q_heads, kv_heads, seq_len,
+                                                        head_dim);
+    if (workspace_bytes < need || !workspace) return EDB_ERR_WORKSPACE_TOO_SMALL;
+    if (!edb::aligned16(workspace)) return EDB_ERR_MISALIGNED;
+    if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)head_dim);
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t rows = (size_t)batch * q_heads * seq_len;
+    char* w = static_cast<char*>(workspace);
+    float* D = reinterpret_cast<float*>(w);
+    w += a256(rows * 4);
+    float* part = reinterpret_cast<float*>(w);
+    w += a256(2 * rows * 4);
+    {
+        dim3 blk(32, 4);
+        const unsigned nb = (unsigned)((rows + 3) / 4);
+        if (dtype == EDB_BF16)
+            attn_bwd_rowdot_kernel<__nv_bfloat16><<<nb, blk, 0, st>>>(
+                (const __nv_bfloat16*)o, (const __nv_bfloat16*)dO, D, (long long)rows, head_dim);
+        else
+            attn_bwd_rowdot_kernel<float><<<nb, blk, 0, st>>>((const float*)o, (const float*)dO, D,
+                                                              (long long)rows, head_dim);
+        if (cudaError_t e = cudaGetLastError()) return (int)e;
+    }
+    // SIMT kernels (the tcgen05 forward variant did not complete; see flash_attn.cu)
+    const int s =
+        dtype == EDB_BF16
+            ? launch_bwd_simt<__nv_bfloat16>(q, k, v, dO, lse, D, dq, dk, dv, batch, q_heads,
+                                             kv_heads, seq_len, head_dim, 1, scale, st, cs, part)
+            : launch_bwd_simt<float>(q, k, v, dO, lse, D, dq, dk, dv, batch, q_heads, kv_heads,
+                                     seq_len, head_dim, 1, scale, st, cs, part);
+    if (s) return s;
+    fox_dcs_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(part, dcs, (long long)rows,
+                                                                 1.0f / scale);
+    return edb::status_from_cuda(cudaGetLastError());
 }

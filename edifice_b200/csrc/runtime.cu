@@ -99,3 +99,33 @@ extern "C" int edb_get_device_errors(unsigned int* flags_out, int clear) {
     }
     return (int)e;
 }
+
+// ------------------------------------------------------------ storage conversion
+namespace {
+template <typename S, typename D>
+__global__ void edb_convert_kernel(const S* __restrict__ src, D* __restrict__ dst, size_t n) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) st_scalar<D>(dst + i, ld_scalar<S>(src + i));
+}
+}  // namespace
+
+extern "C" int edb_convert(int src_dtype, const void* src, int dst_dtype, void* dst, size_t n,
+                           void* stream) {
+    if ((src_dtype != EDB_F32 && src_dtype != EDB_BF16) ||
+        (dst_dtype != EDB_F32 && dst_dtype != EDB_BF16))
+        return EDB_ERR_BAD_DTYPE;
+    if (n == 0) return EDB_OK;
+    if (!src || !dst) return EDB_ERR_NULL_POINTER;
+    cudaStream_t st = (cudaStream_t)stream;
+    const unsigned blocks = (unsigned)((n + 255) / 256);
+    using bf = __nv_bfloat16;
+    if (src_dtype == EDB_F32 && dst_dtype == EDB_F32)
+        edb_convert_kernel<float, float><<<blocks, 256, 0, st>>>((const float*)src, (float*)dst, n);
+    else if (src_dtype == EDB_F32)
+        edb_convert_kernel<float, bf><<<blocks, 256, 0, st>>>((const float*)src, (bf*)dst, n);
+    else if (dst_dtype == EDB_F32)
+        edb_convert_kernel<bf, float><<<blocks, 256, 0, st>>>((const bf*)src, (float*)dst, n);
+    else
+        edb_convert_kernel<bf, bf><<<blocks, 256, 0, st>>>((const bf*)src, (bf*)dst, n);
+    return edb::status_from_cuda(cudaGetLastError());
+}

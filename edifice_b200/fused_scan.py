@@ -660,6 +660,61 @@ class LaserAttentionFn(torch.autograd.Function):
         return dq, dk, dv, None
 
 
+# ----------------------------------------------------------------- FoX attention
+def fox_attention(q, k, v, cs, scale=None, return_lse=False):
+    """FusedScan.fox_attention/4 (fused_scan.ex:3796-3861): causal attention with
+    the forget bias cs_i - cs_j, cs [B, Hq, L] the cumulative log forget gates (f32).
+    q [B, Hq, L, d], k / v [B, Hkv, L, d].  return_lse adds the f32 row
+    log-sum-exp (without the row's own cs_i) the backward reads."""
+    _dev(q, k, v, cs, what="fox_attention")
+    B, Hq, Hkv, L, d = _attn_shapes(q, k, v)
+    if cs.dtype != torch.float32 or tuple(cs.shape) != (B, Hq, L):
+        raise _lib.EdbError("fox_attention: cs must be f32 [B, Hq, L]")
+    o = torch.empty_like(q)
+    lse = torch.empty((B, Hq, L), dtype=torch.float32, device=q.device)
+    lib = _lib.load()
+    _lib.check(lib.edb_fox_attention_fwd(_dtype_code(q, "fox_attention"), _p(q), _p(k), _p(v),
+                                         _p(cs), _p(o), _p(lse), B, Hq, Hkv, L, d,
+                                         float(scale or 0.0), _stream()),
+               "CUDA FoX attention")
+    return (o, lse) if return_lse else o
+
+
+def fox_attention_backward(q, k, v, cs, forward_out, grad_output, lse, scale=None):
+    """Returns (grad_q, grad_k, grad_v, grad_cs) as fox_attention_backward_dispatch
+    (fused_scan.ex:3914-3924); grad_cs f32."""
+    _dev(q, k, v, cs, forward_out, grad_output, lse, what="fox_attention_backward")
+    B, Hq, Hkv, L, d = _attn_shapes(q, k, v)
+    code = _dtype_code(q, "fox_attention_backward")
+    lib = _lib.load()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dcs = torch.empty((B, Hq, L), dtype=torch.float32, device=q.device)
+    wsb = lib.edb_fox_attention_bwd_workspace(code, B, Hq, Hkv, L, d)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=q.device)
+    _lib.check(lib.edb_fox_attention_bwd(code, _p(q), _p(k), _p(v), _p(cs), _p(forward_out),
+                                         _p(grad_output), _p(lse), _p(dq), _p(dk), _p(dv),
+                                         _p(dcs), B, Hq, Hkv, L, d, float(scale or 0.0), _p(ws),
+                                         wsb, _stream()),
+               "CUDA FoX attention backward")
+    return dq, dk, dv, dcs
+
+
+class FoxAttentionFn(torch.autograd.Function):
+    """custom_grad wiring of fox_attention_custom_call (fused_scan.ex:3796-3861):
+    gradients to q, k, v and cs."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, cs):
+        o, lse = fox_attention(q, k, v, cs, return_lse=True)
+        ctx.save_for_backward(q, k, v, cs, o, lse)
+        return o
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        q, k, v, cs, o, lse = ctx.saved_tensors
+        return fox_attention_backward(q, k, v, cs, o, grad_output.contiguous(), lse)
+
+
 # ------------------------------------------- attention callers routed to flash
 def _attend(q, k, v, causal):
     """[B, H, L, d] attention through the flash kernel, with gradients when any

@@ -141,6 +141,55 @@ int fused_laser_attention_backward_launch(cudaStream_t stream, const edb_io_t* q
     return st;
 }
 
+int fused_fox_attention_launch(cudaStream_t stream, const edb_io_t* q, const edb_io_t* k,
+                               const edb_io_t* v, const edb_io_t* cs, edb_io_t* output,
+                               int batch, int num_heads, int seq_len, int head_dim) {
+    const size_t rows = (size_t)batch * num_heads * seq_len;
+    void* buf = nullptr;  // cs as f32, then lse
+    cudaError_t e = cudaMallocAsync(&buf, 2 * rows * sizeof(float), stream);
+    if (e != cudaSuccess) return (int)e;
+    float* cs32 = static_cast<float*>(buf);
+    int st = edb_convert(kDtype, cs, EDB_F32, cs32, rows, stream);
+    if (st == 0)
+        st = edb_fox_attention_fwd(kDtype, q, k, v, cs32, output, cs32 + rows, batch, num_heads,
+                                   num_heads, seq_len, head_dim, 0.0f, stream);
+    cudaFreeAsync(buf, stream);
+    return st;
+}
+
+int fused_fox_attention_backward_launch(cudaStream_t stream, const edb_io_t* q,
+                                        const edb_io_t* k, const edb_io_t* v,
+                                        const edb_io_t* cs, const edb_io_t* o,
+                                        const edb_io_t* grad_o, edb_io_t* output_concat,
+                                        int batch, int num_heads, int seq_len, int head_dim) {
+    (void)o;  // rebuilt with its lse by a forward pass (into the dq slot, then overwritten)
+    const long long n = (long long)batch * num_heads * seq_len * head_dim;
+    const size_t rows = (size_t)batch * num_heads * seq_len;
+    const size_t wb = edb_fox_attention_bwd_workspace(kDtype, batch, num_heads, num_heads,
+                                                      seq_len, head_dim);
+    const size_t ob = ((size_t)n * sizeof(edb_io_t) + 255) & ~(size_t)255;
+    void* buf = nullptr;  // cs f32 | lse | dcs f32 | o | workspace
+    const size_t head = ((3 * rows * sizeof(float)) + 255) & ~(size_t)255;
+    cudaError_t e = cudaMallocAsync(&buf, head + ob + wb, stream);
+    if (e != cudaSuccess) return (int)e;
+    float* cs32 = static_cast<float*>(buf);
+    float* lse = cs32 + rows;
+    float* dcs = lse + rows;
+    edb_io_t* o2 = reinterpret_cast<edb_io_t*>(static_cast<char*>(buf) + head);
+    void* ws = static_cast<char*>(buf) + head + ob;
+    int st = edb_convert(kDtype, cs, EDB_F32, cs32, rows, stream);
+    if (st == 0)
+        st = edb_fox_attention_fwd(kDtype, q, k, v, cs32, o2, lse, batch, num_heads, num_heads,
+                                   seq_len, head_dim, 0.0f, stream);
+    if (st == 0)
+        st = edb_fox_attention_bwd(kDtype, q, k, v, cs32, o2, grad_o, lse, output_concat,
+                                   output_concat + n, output_concat + 2 * n, dcs, batch,
+                                   num_heads, num_heads, seq_len, head_dim, 0.0f, ws, wb, stream);
+    if (st == 0) st = edb_convert(EDB_F32, dcs, kDtype, output_concat + 3 * n, rows, stream);
+    cudaFreeAsync(buf, stream);
+    return st;
+}
+
 int fused_selective_scan_launch(cudaStream_t stream, const edb_io_t* x, const edb_io_t* dt,
                                 const edb_io_t* A, const edb_io_t* B, const edb_io_t* C,
                                 edb_io_t* out, int batch, int seq_len, int hidden, int state) {

@@ -276,6 +276,39 @@ int edb_laser_attention_bwd(int dtype, const void* q, const void* k, const void*
                             float scale, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * FoX attention (forgetting attention), always causal:
+ *   S_ij = q_i.k_j scale + cs_i - cs_j (j <= i);  O = softmax(S) V
+ * cs [B, Hq, L] f32: the cumulative log forget gates, cumsum(log(sigmoid(f))).
+ * q, o [B, Hq, L, d]; k, v [B, Hkv, L, d] (grouped heads).  lse [B, Hq, L] f32
+ * (required; the backward reads it) is the row log-sum-exp without the row's own
+ * cs_i, which cancels in the softmax.  scale <= 0 means 1/sqrt(d).  tcgen05 kernels
+ * for bf16, head_dim 64/128, L % 4 == 0; SIMT kernels otherwise.
+ * Replaces fused_fox_attention_launch (native/cuda/fused_fox_attention.cu:162-190);
+ * Nx semantics lib/edifice/cuda/fused_scan.ex:3796-3912.
+ * ---------------------------------------------------------------------- */
+int edb_fox_attention_fwd(int dtype, const void* q, const void* k, const void* v,
+                          const float* cs, void* o, float* lse, int batch, int q_heads,
+                          int kv_heads, int seq_len, int head_dim, float scale, void* stream);
+
+size_t edb_fox_attention_bwd_workspace(int dtype, int batch, int q_heads, int kv_heads,
+                                       int seq_len, int head_dim);
+
+/* Backward: dq [B,Hq,L,d], dk/dv [B,Hkv,L,d] in `dtype`, dcs [B,Hq,L] f32 =
+ * rowsum(dS) - colsum(dS) of the unscaled score gradient (the row sums vanish: only
+ * the key side is computed).  o and lse are the forward's.  Workspace 16-byte aligned.
+ * Replaces fused_fox_attention_backward_launch
+ * (native/cuda/fused_fox_attention_backward.cu:373-420); fused_scan.ex:3914-3984. */
+int edb_fox_attention_bwd(int dtype, const void* q, const void* k, const void* v,
+                          const float* cs, const void* o, const void* dO, const float* lse,
+                          void* dq, void* dk, void* dv, float* dcs, int batch, int q_heads,
+                          int kv_heads, int seq_len, int head_dim, float scale, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* Element-wise storage conversion of n values (EDB_F32 <-> EDB_BF16, or a copy);
+ * the shims use it for the reference's io-typed cs arguments. */
+int edb_convert(int src_dtype, const void* src, int dst_dtype, void* dst, size_t n, void* stream);
+
+/* ------------------------------------------------------------------------
  * DeltaNet delta rule.  Per (batch, head), S_0 = 0:
  *   r = S_{t-1} k_t;  S_t = S_{t-1} + (beta_t (.) (v_t - r)) k_t^T;  o_t = S_t q_t
  * q, k, v, o: [batch, seq_len, heads, head_dim] (k L2-normalised by the

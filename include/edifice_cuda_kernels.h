@@ -94,6 +94,19 @@ int fused_laser_attention_backward_launch(cudaStream_t stream, const edb_io_t* q
                                           int batch, int num_heads, int seq_len, int head_dim,
                                           int causal);
 
+/* native/cuda/fused_fox_attention.cu:162-190 (causal, equal heads; cs [B, H, L]) */
+int fused_fox_attention_launch(cudaStream_t stream, const edb_io_t* q, const edb_io_t* k,
+                               const edb_io_t* v, const edb_io_t* cs, edb_io_t* output,
+                               int batch, int num_heads, int seq_len, int head_dim);
+
+/* native/cuda/fused_fox_attention_backward.cu:373-420;
+ * output_concat = [dq | dk | dv | dcs (B*H*L)] */
+int fused_fox_attention_backward_launch(cudaStream_t stream, const edb_io_t* q,
+                                        const edb_io_t* k, const edb_io_t* v,
+                                        const edb_io_t* cs, const edb_io_t* o,
+                                        const edb_io_t* grad_o, edb_io_t* output_concat,
+                                        int batch, int num_heads, int seq_len, int head_dim);
+
 /* native/cuda/fused_selective_scan.cu:105-124 (dt clamp [0.001, 0.1]) */
 int fused_selective_scan_launch(cudaStream_t stream, const edb_io_t* x, const edb_io_t* dt,
                                 const edb_io_t* A, const edb_io_t* B, const edb_io_t* C,

@@ -291,6 +291,51 @@ def laser_bwd(q, k, v, dO, causal=True, v_max=None, prec="f64"):
     return dq, dk, (dev.astype(np.float64) * ev).astype(np.float32)
 
 
+# --------------------------------------------------------------- FoX attention
+# fox_attention_fallback (fused_scan.ex:3863-3912) and its backward (:3926-3984),
+# dense in f64 numpy (small cases): scores q k^T / sqrt(d) + (cs_i - cs_j) with the
+# diagonal bias zeroed, causal, softmax; grad_cs = rowsum(dS) - colsum(dS) of the
+# unscaled score gradient with the diagonal excluded.  Grouped kv heads are expanded
+# to the query heads (gqa.ex:257-271), their gradients summed back.
+def _fox_parts(q, k, v, cs):
+    q, k, v, cs = (np.asarray(x, np.float64) for x in (q, k, v, cs))
+    B, Hq, L, d = q.shape
+    ke, ve = _expand_heads(k, Hq), _expand_heads(v, Hq)
+    scale = np.sqrt(d)
+    s = q @ np.swapaxes(ke, -1, -2) / scale
+    bias = cs[..., :, None] - cs[..., None, :]
+    eye = np.eye(L, dtype=bool)
+    s = s + np.where(eye, 0.0, bias)
+    s = np.where(np.tri(L, dtype=bool), s, -np.inf)
+    w = np.exp(s - s.max(-1, keepdims=True))
+    w /= w.sum(-1, keepdims=True)
+    return q, ke, ve, w, scale, eye
+
+
+def fox_fwd(q, k, v, cs):
+    q, ke, ve, w, _, _ = _fox_parts(q, k, v, cs)
+    return (w @ ve).astype(np.float32)
+
+
+def fox_bwd(q, k, v, cs, dO):
+    q, ke, ve, w, scale, eye = _fox_parts(q, k, v, cs)
+    dO = np.asarray(dO, np.float64)
+    Hkv = np.asarray(k).shape[1]
+    g = q.shape[1] // Hkv
+    gv = np.swapaxes(w, -1, -2) @ dO
+    dw = dO @ np.swapaxes(ve, -1, -2)
+    ds = w * (dw - (dw * w).sum(-1, keepdims=True))
+    ds_nd = np.where(eye, 0.0, ds)
+    gcs = ds_nd.sum(-1) - ds_nd.sum(-2)
+    ds = ds / scale
+    gq = ds @ ke
+    gk = np.swapaxes(ds, -1, -2) @ q
+
+    def fold(x):  # [B, Hq, ...] -> [B, Hkv, ...], summed over each group
+        return x.reshape(x.shape[0], Hkv, g, *x.shape[2:]).sum(2)
+    return tuple(x.astype(np.float32) for x in (gq, fold(gk), fold(gv), gcs))
+
+
 # ---------------------------------------------- the reference's own C refs
 def ref_linear_scan_cpu(a, b, h0):
     r = ref_cpu_lib()

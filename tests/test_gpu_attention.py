@@ -361,3 +361,75 @@ def test_laser_shim_symbols(cuda, prec, dtype):
     n = q.numel()
     for i, w in enumerate(want):
         assert torch.equal(cat[i * n:(i + 1) * n].view_as(w), w)
+
+
+# ------------------------------------------------------------------ FoX attention
+def fox_cs(B, H, L, seed):
+    """cs = cumsum(log(sigmoid(f))), f ~ N(0, 1) (the model's forget gates)."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    f = torch.randn(B, H, L, generator=g)
+    return torch.cumsum(torch.nn.functional.logsigmoid(f), -1).cuda()
+
+
+FOX_CASES = [
+    # (B, Hq, Hkv, L, d)
+    (2, 4, 4, 200, 128),   # equal heads (the reference's form)
+    (1, 8, 2, 300, 128),   # grouped heads
+    (2, 2, 2, 132, 64),    # head_dim 64
+    (1, 2, 2, 77, 64),     # odd length
+    (1, 4, 1, 64, 96),     # other head_dim
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("case", FOX_CASES)
+def test_fox_attention(cuda, dtype, case):
+    """FoX (fused_scan.ex:3796-3984) forward and backward, grad_cs included, against
+    the oracle on the same rounded inputs."""
+    B, Hq, Hkv, L, d = case
+    q, k, v, do = attn_inputs(*case, dtype, seed=81)
+    cs = fox_cs(B, Hq, L, 82)
+    o, lse = fs.fox_attention(q, k, v, cs, return_lse=True)
+    dq, dk, dv, dcs = fs.fox_attention_backward(q, k, v, cs, o, do, lse)
+    torch.cuda.synchronize()
+    assert O.norm_rel(_np(o), O.fox_fwd(_np(q), _np(k), _np(v), _np(cs))) <= TOL[dtype]
+    ref = O.fox_bwd(_np(q), _np(k), _np(v), _np(cs), _np(do))
+    for name, got, r in zip(("dq", "dk", "dv", "dcs"), (dq, dk, dv, dcs), ref):
+        assert O.norm_rel(_np(got), r) <= TOL[dtype], (name, O.norm_rel(_np(got), r))
+    assert device_errors() == 0
+
+
+def test_fox_zero_gates_is_causal_attention(cuda):
+    """cs = 0 (no forgetting) is causal attention."""
+    q, k, v, _ = attn_inputs(2, 4, 2, 256, 128, torch.bfloat16, seed=83)
+    cs = torch.zeros(2, 4, 256, device="cuda")
+    o = fs.fox_attention(q, k, v, cs)
+    ref = fs.flash_attention(q, k, v, causal=True)
+    torch.cuda.synchronize()
+    assert O.norm_rel(_np(o), _np(ref)) <= 2e-2
+
+
+@pytest.mark.parametrize("prec,dtype", [("f32", torch.float32), ("bf16", torch.bfloat16)])
+def test_fox_shim_symbols(cuda, prec, dtype):
+    """fused_fox_attention_launch / _backward_launch (io-typed cs, [dq|dk|dv|dcs])
+    match the edb_* path on the io-rounded cs."""
+    lib = ctypes.CDLL(build.SHIMS[prec])
+    B, H, L, d = 2, 2, 96, 64
+    q, k, v, do = attn_inputs(B, H, H, L, d, dtype, seed=84)
+    cs_io = fox_cs(B, H, L, 85).to(dtype)
+    cs = cs_io.float()
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    out = torch.empty_like(q)
+    assert lib.fused_fox_attention_launch(None, P(q), P(k), P(v), P(cs_io), P(out), B, H, L, d) == 0
+    n = q.numel()
+    cat = torch.empty(3 * n + B * H * L, dtype=dtype, device="cuda")
+    assert lib.fused_fox_attention_backward_launch(None, P(q), P(k), P(v), P(cs_io), P(out),
+                                                   P(do), P(cat), B, H, L, d) == 0
+    torch.cuda.synchronize()
+    o, lse = fs.fox_attention(q, k, v, cs, return_lse=True)
+    want = fs.fox_attention_backward(q, k, v, cs, o, do, lse)
+    torch.cuda.synchronize()
+    assert torch.equal(out, o)
+    for i, w in enumerate(want[:3]):
+        assert torch.equal(cat[i * n:(i + 1) * n].view_as(w), w)
+    assert torch.equal(cat[3 * n:].view(B, H, L), want[3].to(dtype))

@@ -232,6 +232,29 @@ def test_laser_attention_autograd(causal):
         np.testing.assert_allclose(got, ref.grad.numpy(), rtol=1e-4, atol=1e-5)
 
 
+@pytest.mark.parametrize("hkv", [3, 1])
+def test_fox_attention_autograd(hkv):
+    """FoX (fused_scan.ex:3863-3912 forward, :3926-3984 backward): the oracle's
+    backward equals torch f64 autograd of the forward (grad_cs included)."""
+    rng = np.random.default_rng(10)
+    B, H, L, d = 2, 3, 17, 8
+    q = rng.standard_normal((B, H, L, d)).astype(np.float32)
+    k, v = (rng.standard_normal((B, hkv, L, d)).astype(np.float32) for _ in range(2))
+    cs = np.cumsum(np.log(1 / (1 + np.exp(-rng.standard_normal((B, H, L))))), -1).astype(
+        np.float32)
+    do = rng.standard_normal((B, H, L, d)).astype(np.float32)
+    tq, tk, tv, tcs = _t(q), _t(k), _t(v), _t(cs)
+    ke = tk.repeat_interleave(H // hkv, 1)
+    ve = tv.repeat_interleave(H // hkv, 1)
+    s = tq @ ke.transpose(-1, -2) / np.sqrt(d) + (tcs[..., :, None] - tcs[..., None, :])
+    s = s.masked_fill(~torch.ones(L, L, dtype=torch.bool).tril(), float("-inf"))
+    o = torch.softmax(s, -1) @ ve
+    o.backward(torch.tensor(do, dtype=torch.float64))
+    np.testing.assert_allclose(O.fox_fwd(q, k, v, cs), o.detach().numpy(), rtol=1e-5, atol=1e-6)
+    for got, ref in zip(O.fox_bwd(q, k, v, cs, do), (tq, tk, tv, tcs)):
+        np.testing.assert_allclose(got, ref.grad.numpy(), rtol=1e-4, atol=1e-6)
+
+
 @pytest.mark.parametrize("scalar_beta", [False, True])
 def test_delta_net_bwd_autograd(scalar_beta):
     rng = np.random.default_rng(5)
