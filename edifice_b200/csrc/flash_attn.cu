@@ -340,16 +340,19 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
             if (lse != nullptr && qrow < L)
                 lse[(long long)bh * L + qrow] = (m_used + log2f(l)) * kLn2;
             fence_proxy_async();
-            tc::named_bar(1, 128);
-            if (STORE_O && tid == 0) {
-                prefetch_tmap(&maps.o);
-                for (int bx = 0; bx < NB; ++bx)
-                    tc::tma_store_3d(&maps.o, sQ + bx * (BM * 128), bx * 64, q0, bh);
-                tc::tma_store_commit();
-                tc::tma_store_wait_all();
-            }
         } else {
             *(volatile int*)s_abort = 1;
+        }
+        // every softmax warp reaches this barrier, whether or not its waits succeeded
+        // (a warp that gave up must not leave the others waiting); the tile is stored
+        // only when none gave up
+        tc::named_bar(1, 128);
+        if (STORE_O && tid == 0 && *(volatile int*)s_abort == 0) {
+            prefetch_tmap(&maps.o);
+            for (int bx = 0; bx < NB; ++bx)
+                tc::tma_store_3d(&maps.o, sQ + bx * (BM * 128), bx * 64, q0, bh);
+            tc::tma_store_commit();
+            tc::tma_store_wait_all();
         }
     }
     tc::fence_before_sync();

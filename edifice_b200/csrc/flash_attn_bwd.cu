@@ -342,47 +342,52 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         // ------------------------------------------------ dQ reduction + dK/dV epilogue (warps 4-7)
         const int w = warp - kDqWarp0;
         const uint32_t lb = (uint32_t)(w * 32) << 16;
+        // A warp whose wait gives up keeps taking the two named barriers of every
+        // remaining tile (doing nothing else), so no other dQ warp is left waiting.
         bool ok = true;
         for (int n = 0; n < N; ++n) {
             const int g = n / nqi, i = i0 + n % nqi;
             const int bh = b * Hq + hk * G + g;
-            if (*abort_flag || !mbar_wait_bounded(dq_full, n & 1, err, EDB_DEVERR_ATTN_PIPE)) {
+            if (ok && (*abort_flag || !mbar_wait_bounded(dq_full, n & 1, err, EDB_DEVERR_ATTN_PIPE))) {
                 *abort_flag = 1;
                 ok = false;
-                break;
             }
-            tc::fence_after_sync();
-            // the previous tile's bulk reduce must be done reading the staging tile
-            if (w == 0 && lane == 0) tc::tma_store_wait_read_all();
+            if (ok) {
+                tc::fence_after_sync();
+                // the previous tile's bulk reduce must be done reading the staging tile
+                if (w == 0 && lane == 0) tc::tma_store_wait_read_all();
+            }
             tc::named_bar(2, 128);
-            // dQ_i in two halves of HD/2 columns (register budget); M = 64
-            // accumulator: lanes 32w + t (t < 16) hold query row 16w + t of the tile
+            if (ok) {
+                // dQ_i in two halves of HD/2 columns (register budget); M = 64
+                // accumulator: lanes 32w + t (t < 16) hold query row 16w + t of the tile
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                uint32_t qv[HD / 64][32];
-#pragma unroll
-                for (int cc = 0; cc < HD / 64; ++cc)
-                    tc::tmem_ld32(tmem + S::TM_DQ + lb + (hh * (HD / 64) + cc) * 32, qv[cc]);
-                tc::tmem_wait_ld();
-                if (lane < 16) {
-                    const int r = 16 * w + lane;
+                for (int hh = 0; hh < 2; ++hh) {
+                    uint32_t qv[HD / 64][32];
 #pragma unroll
                     for (int cc = 0; cc < HD / 64; ++cc)
+                        tc::tmem_ld32(tmem + S::TM_DQ + lb + (hh * (HD / 64) + cc) * 32, qv[cc]);
+                    tc::tmem_wait_ld();
+                    if (lane < 16) {
+                        const int r = 16 * w + lane;
 #pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            *reinterpret_cast<uint4*>(sDq + (hh * (HD / 64) + cc) * (BQ * 128) +
-                                                      tc::sw128_off(r, j)) =
-                                make_uint4(qv[cc][4 * j], qv[cc][4 * j + 1], qv[cc][4 * j + 2],
-                                           qv[cc][4 * j + 3]);
+                        for (int cc = 0; cc < HD / 64; ++cc)
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                *reinterpret_cast<uint4*>(sDq + (hh * (HD / 64) + cc) * (BQ * 128) +
+                                                          tc::sw128_off(r, j)) =
+                                    make_uint4(qv[cc][4 * j], qv[cc][4 * j + 1], qv[cc][4 * j + 2],
+                                               qv[cc][4 * j + 3]);
+                    }
                 }
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(dq_free);
+                fence_proxy_async();
             }
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(dq_free);
-            fence_proxy_async();
             tc::named_bar(2, 128);
             // dq_acc[bh, i*BQ .., :] += staging tile (rows past L are clipped)
-            if (w == 0 && lane == 0) {
+            if (ok && w == 0 && lane == 0 && *abort_flag == 0) {
 #pragma unroll
                 for (int cc = 0; cc < HD / 32; ++cc)
                     tc::tma_reduce_add_3d(&maps.dq, sDq + cc * (BQ * 128), cc * 32, i * BQ, bh);
