@@ -190,31 +190,31 @@ size_t ckpt_bytes(int B, int L, int H, int d) {
 //   x = dS[i] - beta_i dsk_i k_t;  dS[i] <- alpha_t x  (the gradient w.r.t. S_{t-1}[i])
 // Only gq = S_t^T dO_t, gk = dS_t^T u - alpha_t S_{t-1}^T (beta (.) dsk), galpha = <x, P>
 // summed over rows, and a per-token beta's gradient, couple the rows.
-// grid (H, B, ceil(d / 32)), 128 threads = 32 rows x 4 lanes of CPL columns (the forward's
-// layout).  A checkpoint chunk (CK tokens) is walked in reverse in pieces of SB tokens:
+// grid (H, B, ceil(d / 32)), 32 rows per CTA, LPR lanes of CPL columns per row: 8 lanes
+// of 16 columns for d > 32 (256 threads: twice the forward's warps, for latency hiding),
+// 4 lanes of 8 columns for d <= 32.  A checkpoint chunk (CK tokens) is walked in reverse
+// in pieces of SB tokens:
 //   pass 1: from the chunk's checkpoint, forward over the chunk, keeping the state at every
 //           piece start (pstart);
 //   pass 2: per piece, last first: forward over the piece from its start writing every S_{t-1}
 //           row slice (sbuf), then backward over the piece reading them back.
 // pstart and sbuf are per-CTA scratch (320 KB per CTA at d = 128, L2-resident); each
-// thread reads back only what it wrote.  Row sums: per token, a lane's CPL partials are
-// summed over the 8 rows of its warp by recursive halving (the lane keeps CPL / 8 sums),
-// the 4 warps' sums meet in shared memory every RB tokens, and one partial per (row
-// block, token, head) goes to global memory, where delta_rows_reduce_kernel adds the row
-// blocks in a fixed order.
+// thread reads back only what it wrote.  Row sums: per token, a lane's 2 CPL partials
+// are summed over the rows of its warp that share its column slice by recursive
+// halving, the warps' sums meet in shared memory every RB tokens, and one partial per
+// (row block, token, head) goes to global memory, where delta_rows_reduce_kernel adds
+// the row blocks in a fixed order.
 constexpr int SB = 16;  // tokens per backward piece
 constexpr int NPIECE = CK / SB;
-constexpr int RB = 8;   // tokens per cross-warp reduction
-constexpr int NSLOT = 2 * RB;  // row-sum slots: a token's gq arrives one step after its gk
 
-// Sums v over the lanes that differ in bits 2..4 (the 8 rows of a warp that share a
-// column slice).  On return v[0 .. NV/8) holds the totals of values
-// [base, base + NV/8), base = (lane >> 2 & 7) * NV / 8 (bit 4 -> NV/2, bit 3 -> NV/4,
-// bit 2 -> NV/8).
-template <int NV>
+// Sums v over the lanes that differ in bits 5 - ROUNDS .. 4 (the rows of a warp that
+// share a column slice: 8 rows at 4 lanes per row, 4 rows at 8).  Recursive halving:
+// on return v[0 .. NV >> ROUNDS) holds the totals of the values starting at
+// halving_base(lane) (bit 4 -> NV/2, bit 3 -> NV/4, bit 2 -> NV/8).
+template <int NV, int ROUNDS>
 static __device__ __forceinline__ void rows_halving_sum(float (&v)[NV], int lane) {
 #pragma unroll
-    for (int r = 0; r < 3; ++r) {
+    for (int r = 0; r < ROUNDS; ++r) {
         const int m = 16 >> r;          // lane mask of this round
         const int hn = NV >> (r + 1);   // values kept after this round
         const bool up = (lane & m) != 0;
@@ -226,32 +226,42 @@ static __device__ __forceinline__ void rows_halving_sum(float (&v)[NV], int lane
         }
     }
 }
+template <int ROUNDS>
 static __device__ __forceinline__ int halving_base(int lane, int nv) {
-    return ((lane >> 4) & 1) * (nv / 2) + ((lane >> 3) & 1) * (nv / 4) + ((lane >> 2) & 1) * (nv / 8);
+    int base = 0;
+#pragma unroll
+    for (int r = 0; r < ROUNDS; ++r)
+        if (lane & (16 >> r)) base += nv >> (r + 1);
+    return base;
 }
 
-template <int CPL>
+// LPR lanes per row of S, CPL columns each; 32 rows per CTA, so LPR warps.
+template <int CPL, int LPR>
 struct RowsBwdSmem {
-    static constexpr int SP = CPL + 4, RP = 4 * SP, W = 4 * CPL;  // W: columns per CTA
-    // per warp and token: [gq | gk][4 slices][CPL + 2], the halves 4 (CPL + 2) + 1 apart,
-    // then galpha and a per-token gbeta: the skews put the 32 lanes' stores of one
+    static constexpr int NT = 32 * LPR, NW = LPR;
+    static constexpr int ROUNDS = LPR == 4 ? 3 : 2;       // halving rounds (rows per warp)
+    static constexpr int SP = CPL + 4, RP = LPR * SP, W = LPR * CPL;  // W: columns per CTA
+    // per warp and token: [gq | gk][LPR slices][CPL + 1], the halves LPR (CPL + 1) + 8
+    // apart, then galpha and a per-token gbeta: the skews put the 32 lanes' stores of one
     // halving result on 32 different banks
-    static constexpr int SLICE = CPL + 2, HALF = 4 * SLICE + 1;
+    static constexpr int SLICE = CPL + 1, HALF = LPR * SLICE + 8;
     static constexpr int RED = 2 * HALF + 2;
-    // red holds 2 RB token slots: a token's gq arrives one step after its gk
+    // tokens per cross-warp reduction, and 2 RB slots: a token's gq arrives one step
+    // after its gk
+    static constexpr int RB = LPR == 4 ? 8 : 4, NSLOT = 2 * RB;
     static constexpr size_t floats = (size_t)2 * SB * RP + 5 * SB * kRowsPerCta + SB +
-                                     (size_t)NSLOT * 4 * RED;
+                                     (size_t)NSLOT * NW * RED;
     static constexpr size_t bytes = floats * sizeof(float);
 };
 
-// per-CTA scratch floats: NPIECE piece starts + SB token states, 128 threads x CPL
-template <int CPL>
+// per-CTA scratch floats: NPIECE piece starts + SB token states of 32 rows x W columns
+template <int CPL, int LPR>
 constexpr size_t rows_scratch_floats() {
-    return (size_t)(NPIECE + SB) * kRowThreads * CPL;
+    return (size_t)(NPIECE + SB) * 32 * LPR * CPL;
 }
 
-template <typename T, int CPL, bool GATED>
-__global__ void __launch_bounds__(kRowThreads, 2)
+template <typename T, int CPL, int LPR, bool GATED>
+__global__ void __launch_bounds__(32 * LPR, 2)
     delta_bwd_rows_kernel(const T* __restrict__ q, const T* __restrict__ k,
                           const T* __restrict__ v, const T* __restrict__ beta,
                           const T* __restrict__ alpha, const T* __restrict__ dO,
@@ -259,10 +269,11 @@ __global__ void __launch_bounds__(kRowThreads, 2)
                           float* __restrict__ part, float* __restrict__ part_s,
                           T* __restrict__ gv, T* __restrict__ gbeta, int B, int L, int H, int d,
                           int beta_scalar) {
-    static_assert(SB % NSLOT == 0, "red slots are indexed by the token's place in its piece");
-    using G = RowsBwdSmem<CPL>;
+    using G = RowsBwdSmem<CPL, LPR>;
+    constexpr int NT = G::NT, NW = G::NW, ROUNDS = G::ROUNDS;
     constexpr int SP = G::SP, RP = G::RP, W = G::W, RED = G::RED;
-    constexpr int SLICE = G::SLICE, HALF = G::HALF;
+    constexpr int SLICE = G::SLICE, HALF = G::HALF, RB = G::RB, NSLOT = G::NSLOT;
+    static_assert(SB % NSLOT == 0, "red slots are indexed by the token's place in its piece");
     constexpr int NV = 2 * CPL;  // gq | gk partials of one lane
     constexpr int NP = CPL / 2;  // packed f32 pairs per row slice
     extern __shared__ __align__(16) float smf[];
@@ -274,22 +285,22 @@ __global__ void __launch_bounds__(kRowThreads, 2)
     float* sgv = sdo + SB * kRowsPerCta;   // [SB][32] staged gv
     float* sgb = sgv + SB * kRowsPerCta;   // [SB][32] staged per-element gbeta
     float* sa = sgb + SB * kRowsPerCta;    // [SB]
-    float* red = sa + SB;                  // [NSLOT][4 warps][RED]
+    float* red = sa + SB;                  // [NSLOT][NW warps][RED]
     const int h = blockIdx.x, b = blockIdx.y, z = blockIdx.z, rb = z * kRowsPerCta;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int rl = warp * 8 + (lane >> 2);
+    const int rl = warp * (32 / LPR) + lane / LPR;
     const int i = rb + rl;
-    const int part_ix = lane & 3;
+    const int part_ix = lane % LPR;
     const int c0 = part_ix * CPL;
     const bool row_ok = i < d;
     const long long rs = (long long)H * d;
     const long long base = (long long)b * L * rs + (long long)h * d;
     const int nck = (L + CK - 1) / CK;
     const long long cta = ((long long)b * H + h) * gridDim.z + z;
-    float* pstart = scratch + cta * rows_scratch_floats<CPL>();
-    float* sbuf = pstart + (size_t)NPIECE * kRowThreads * CPL;
+    float* pstart = scratch + cta * rows_scratch_floats<CPL, LPR>();
+    float* sbuf = pstart + (size_t)NPIECE * NT * CPL;
     const float* ck_unit = ckpt + ((long long)b * H + h) * (nck + 1) * d * d;
-    const int hb = halving_base(lane, NV);
+    const int hb = halving_base<ROUNDS>(lane, NV);
 
     auto st_slice = [&](float* dst, const float2 (&x)[NP]) {
         float4* p = reinterpret_cast<float4*>(dst + (size_t)tid * CPL);
@@ -308,12 +319,12 @@ __global__ void __launch_bounds__(kRowThreads, 2)
     // stage tokens [t0, t0 + n) of the piece; with_q: also q and dO (the backward's)
     auto stage = [&](int t0, int n, bool with_q) {
         __syncthreads();  // the previous piece's stage is consumed
-        for (int base_idx = 0; base_idx < SB * 4 * CPL; base_idx += kRowThreads * 4) {
+        for (int base_idx = 0; base_idx < SB * W; base_idx += NT * 4) {
             float fk[4], fq[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                const int idx = base_idx + tid + u * kRowThreads;
-                const int tt = idx / (4 * CPL), c = idx % (4 * CPL);
+                const int idx = base_idx + tid + u * NT;
+                const int tt = idx / W, c = idx % W;
                 const bool ok = tt < n && c < d;
                 const long long off = base + (long long)(t0 + tt) * rs + c;
                 fk[u] = ok ? ldv(k + off) : 0.0f;
@@ -321,8 +332,8 @@ __global__ void __launch_bounds__(kRowThreads, 2)
             }
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                const int idx = base_idx + tid + u * kRowThreads;
-                const int tt = idx / (4 * CPL), c = idx % (4 * CPL);
+                const int idx = base_idx + tid + u * NT;
+                const int tt = idx / W, c = idx % W;
                 if (tt < SB) {
                     const int so = tt * RP + (c / CPL) * SP + c % CPL;
                     sk[so] = fk[u];
@@ -330,7 +341,7 @@ __global__ void __launch_bounds__(kRowThreads, 2)
                 }
             }
         }
-        for (int idx = tid; idx < SB * kRowsPerCta; idx += kRowThreads) {
+        for (int idx = tid; idx < SB * kRowsPerCta; idx += NT) {
             const int tt = idx / kRowsPerCta, r = idx % kRowsPerCta;
             const bool ok = tt < n && rb + r < d;
             const long long off = base + (long long)(t0 + tt) * rs + rb + r;
@@ -341,7 +352,7 @@ __global__ void __launch_bounds__(kRowThreads, 2)
             sdo[idx] = (ok && with_q) ? ldv(dO + off) : 0.0f;
         }
         if (GATED)
-            for (int tt = tid; tt < SB; tt += kRowThreads)
+            for (int tt = tid; tt < SB; tt += NT)
                 sa[tt] = tt < n ? ldv(alpha + ((long long)b * L + t0 + tt) * H + h) : 1.0f;
         __syncthreads();
     };
@@ -360,8 +371,8 @@ __global__ void __launch_bounds__(kRowThreads, 2)
             rc = fma2(S[p + 1], krow(tt, p + 1), rc);
         }
         float r = (ra.x + ra.y) + (rc.x + rc.y);
-        r += __shfl_xor_sync(0xffffffffu, r, 1);
-        r += __shfl_xor_sync(0xffffffffu, r, 2);
+#pragma unroll
+        for (int o = 1; o < LPR; o <<= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
         const float al = GATED ? sa[tt] : 1.0f;
         const float2 u2 = dup2(sb[tt * kRowsPerCta + rl] * (sv[tt * kRowsPerCta + rl] - al * r));
 #pragma unroll
@@ -371,18 +382,22 @@ __global__ void __launch_bounds__(kRowThreads, 2)
     // the 4 warps' row sums of tokens [tt0, tt0 + n) of the piece -> global partials
     auto flush = [&](int pt0, int tt0, int n) {
         __syncthreads();
-        for (int idx = tid; idx < n * (2 * W + 2); idx += kRowThreads) {
+        for (int idx = tid; idx < n * (2 * W + 2); idx += NT) {
             const int tt = tt0 + idx / (2 * W + 2), e = idx % (2 * W + 2);
             const long long row = ((long long)z * B + b) * L + pt0 + tt;
             if (e < 2 * W) {
                 const int which = e / W, col = e % W;
                 const float* rr =
-                    red + (tt % NSLOT) * 4 * RED + which * HALF + (col / CPL) * SLICE + col % CPL;
-                const float s = (rr[0] + rr[RED]) + (rr[2 * RED] + rr[3 * RED]);
+                    red + (tt % NSLOT) * NW * RED + which * HALF + (col / CPL) * SLICE + col % CPL;
+                float s = 0.0f;
+#pragma unroll
+                for (int w = 0; w < NW; ++w) s += rr[w * RED];
                 if (col < d) part[(row * H + h) * 2 * d + which * d + col] = s;
             } else {
-                const float* rr = red + (tt % NSLOT) * 4 * RED + 2 * HALF + (e - 2 * W);
-                const float s = (rr[0] + rr[RED]) + (rr[2 * RED] + rr[3 * RED]);
+                const float* rr = red + (tt % NSLOT) * NW * RED + 2 * HALF + (e - 2 * W);
+                float s = 0.0f;
+#pragma unroll
+                for (int w = 0; w < NW; ++w) s += rr[w * RED];
                 part_s[(row * H + h) * 2 + (e - 2 * W)] = s;
             }
         }
@@ -390,14 +405,14 @@ __global__ void __launch_bounds__(kRowThreads, 2)
     };
     // w = [gq partial of token tq | gk partial of token tk] (tq < 0 or tk < 0: skip that half)
     auto reduce_rows = [&](float (&w)[NV], int tq, int tk) {
-        rows_halving_sum<NV>(w, lane);
+        rows_halving_sum<NV, ROUNDS>(w, lane);
 #pragma unroll
-        for (int j = 0; j < NV / 8; ++j) {
+        for (int j = 0; j < (NV >> ROUNDS); ++j) {
             const int e = hb + j;  // index into [gq CPL | gk CPL] of slice part_ix
             const int which = e >= CPL;
             const int tt = which ? tk : tq;
             if (tt >= 0)
-                red[((tt % NSLOT) * 4 + warp) * RED + which * HALF + part_ix * SLICE + e -
+                red[((tt % NSLOT) * NW + warp) * RED + which * HALF + part_ix * SLICE + e -
                     which * CPL] =
                     w[j];
         }
@@ -410,7 +425,7 @@ __global__ void __launch_bounds__(kRowThreads, 2)
     // backward step of token tt; P = S_{t-1} (slot tt), Pn <- slot tt - 1.  Also the gq
     // of token tt - 1, whose state after the update is P.
     auto bstep = [&](const float2 (&P)[NP], float2 (&Pn)[NP], int pt0, int pn, int tt) {
-        if (tt > 0) ld_slice(sbuf + (size_t)(tt - 1) * kRowThreads * CPL, Pn);
+        if (tt > 0) ld_slice(sbuf + (size_t)(tt - 1) * NT * CPL, Pn);
         const float doj = sdo[tt * kRowsPerCta + rl];
         const float dop = tt > 0 ? sdo[(tt - 1) * kRowsPerCta + rl] : 0.0f;
         const float al = GATED ? sa[tt] : 1.0f;
@@ -434,10 +449,11 @@ __global__ void __launch_bounds__(kRowThreads, 2)
             }
         }
         float r = (ra.x + ra.y) + (rc.x + rc.y), dsk = (sa2.x + sa2.y) + (sc2.x + sc2.y);
-        r += __shfl_xor_sync(0xffffffffu, r, 1);
-        dsk += __shfl_xor_sync(0xffffffffu, dsk, 1);
-        r += __shfl_xor_sync(0xffffffffu, r, 2);
-        dsk += __shfl_xor_sync(0xffffffffu, dsk, 2);
+#pragma unroll
+        for (int o = 1; o < LPR; o <<= 1) {
+            r += __shfl_xor_sync(0xffffffffu, r, o);
+            dsk += __shfl_xor_sync(0xffffffffu, dsk, o);
+        }
         const float err = sv[tt * kRowsPerCta + rl] - al * r;
         const float u = be * err;
         const float bd = be * dsk;
@@ -467,8 +483,8 @@ __global__ void __launch_bounds__(kRowThreads, 2)
             bsum += __shfl_xor_sync(0xffffffffu, bsum, o);
         }
         if (lane == 0) {
-            red[((tt % NSLOT) * 4 + warp) * RED + 2 * HALF] = ga;
-            red[((tt % NSLOT) * 4 + warp) * RED + 2 * HALF + 1] = bsum;
+            red[((tt % NSLOT) * NW + warp) * RED + 2 * HALF] = ga;
+            red[((tt % NSLOT) * NW + warp) * RED + 2 * HALF + 1] = bsum;
         }
         if (tt % RB == 0) flush(pt0, tt, min(RB, pn - tt));
     };
@@ -485,7 +501,7 @@ __global__ void __launch_bounds__(kRowThreads, 2)
                 S[p] = make_float2((row_ok && c0 + 2 * p < d) ? src[2 * p] : 0.0f,
                                    (row_ok && c0 + 2 * p + 1 < d) ? src[2 * p + 1] : 0.0f);
             for (int p = 0; p < np; ++p) {
-                st_slice(pstart + (size_t)p * kRowThreads * CPL, S);
+                st_slice(pstart + (size_t)p * NT * CPL, S);
                 if (p == np - 1) break;
                 stage(t0 + p * SB, SB, false);
                 for (int tt = 0; tt < SB; ++tt) fwd_step(S, tt);
@@ -497,9 +513,9 @@ __global__ void __launch_bounds__(kRowThreads, 2)
             stage(pt0, pn, true);
             {
                 float2 S[NP];
-                ld_slice(pstart + (size_t)p * kRowThreads * CPL, S);
+                ld_slice(pstart + (size_t)p * NT * CPL, S);
                 for (int tt = 0; tt < pn; ++tt) {
-                    st_slice(sbuf + (size_t)tt * kRowThreads * CPL, S);
+                    st_slice(sbuf + (size_t)tt * NT * CPL, S);
                     fwd_step(S, tt);
                 }
                 // gq of the piece's last token from its state after the update
@@ -517,14 +533,14 @@ __global__ void __launch_bounds__(kRowThreads, 2)
             }
             // walk back; the two state buffers trade roles every token
             float2 A[NP], Bv[NP];
-            ld_slice(sbuf + (size_t)(pn - 1) * kRowThreads * CPL, A);
+            ld_slice(sbuf + (size_t)(pn - 1) * NT * CPL, A);
             for (int tt = pn - 1; tt >= 0; tt -= 2) {
                 bstep(A, Bv, pt0, pn, tt);
                 if (tt == 0) break;
                 bstep(Bv, A, pt0, pn, tt - 1);
             }
             // this piece's gv and per-element gbeta rows
-            for (int idx = tid; idx < pn * kRowsPerCta; idx += kRowThreads) {
+            for (int idx = tid; idx < pn * kRowsPerCta; idx += NT) {
                 const int tt = idx / kRowsPerCta, r = idx % kRowsPerCta;
                 if (rb + r < d) {
                     const long long off = base + (long long)(pt0 + tt) * rs + rb + r;
@@ -561,21 +577,21 @@ __global__ void __launch_bounds__(256)
     }
 }
 
-template <int CPL>
+template <int CPL, int LPR>
 size_t rows_bwd_scratch_bytes(int B, int H, int d) {
     const int nz = (d + kRowsPerCta - 1) / kRowsPerCta;
-    return (size_t)B * H * nz * rows_scratch_floats<CPL>() * sizeof(float);
+    return (size_t)B * H * nz * rows_scratch_floats<CPL, LPR>() * sizeof(float);
 }
 size_t rows_bwd_ws_bytes(int B, int L, int H, int d) {
     const int nz = (d + kRowsPerCta - 1) / kRowsPerCta;
     const size_t rows = (size_t)B * L * H;
-    const size_t sc = d <= 32 ? rows_bwd_scratch_bytes<8>(B, H, d)
-                              : rows_bwd_scratch_bytes<32>(B, H, d);
+    const size_t sc = d <= 32 ? rows_bwd_scratch_bytes<8, 4>(B, H, d)
+                              : rows_bwd_scratch_bytes<16, 8>(B, H, d);
     return a256(sc) + a256((size_t)nz * rows * 2 * d * sizeof(float)) +
            a256((size_t)nz * rows * 2 * sizeof(float));
 }
 
-template <typename T, int CPL, bool GATED>
+template <typename T, int CPL, int LPR, bool GATED>
 int launch_bwd_rows_t(const void* q, const void* k, const void* v, const void* beta,
                       const void* alpha, const void* dO, const float* ckpt, void* ws, void* gq,
                       void* gk, void* gv, void* gbeta, void* galpha, int B, int L, int H, int d,
@@ -584,15 +600,15 @@ int launch_bwd_rows_t(const void* q, const void* k, const void* v, const void* b
     const size_t rows = (size_t)B * L * H;
     char* p = static_cast<char*>(ws);
     float* scratch = reinterpret_cast<float*>(p);
-    p += a256(rows_bwd_scratch_bytes<CPL>(B, H, d));
+    p += a256(rows_bwd_scratch_bytes<CPL, LPR>(B, H, d));
     float* part = reinterpret_cast<float*>(p);
     p += a256((size_t)nz * rows * 2 * d * sizeof(float));
     float* part_s = reinterpret_cast<float*>(p);
-    constexpr size_t smem = RowsBwdSmem<CPL>::bytes;
-    cudaError_t e = cudaFuncSetAttribute(delta_bwd_rows_kernel<T, CPL, GATED>,
+    constexpr size_t smem = RowsBwdSmem<CPL, LPR>::bytes;
+    cudaError_t e = cudaFuncSetAttribute(delta_bwd_rows_kernel<T, CPL, LPR, GATED>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return (int)e;
-    delta_bwd_rows_kernel<T, CPL, GATED><<<dim3(H, B, nz), kRowThreads, smem, st>>>(
+    delta_bwd_rows_kernel<T, CPL, LPR, GATED><<<dim3(H, B, nz), 32 * LPR, smem, st>>>(
         (const T*)q, (const T*)k, (const T*)v, (const T*)beta, (const T*)alpha, (const T*)dO,
         ckpt, scratch, part, part_s, (T*)gv, (T*)gbeta, B, L, H, d, beta_scalar);
     e = cudaGetLastError();
@@ -609,15 +625,15 @@ int launch_bwd_rows(const void* q, const void* k, const void* v, const void* bet
                     void* gk, void* gv, void* gbeta, void* galpha, int B, int L, int H, int d,
                     int beta_scalar, cudaStream_t st) {
     if (d <= 32)
-        return alpha ? launch_bwd_rows_t<T, 8, true>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk,
+        return alpha ? launch_bwd_rows_t<T, 8, 4, true>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk,
                                                      gv, gbeta, galpha, B, L, H, d, beta_scalar,
                                                      st)
-                     : launch_bwd_rows_t<T, 8, false>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk,
+                     : launch_bwd_rows_t<T, 8, 4, false>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk,
                                                       gv, gbeta, galpha, B, L, H, d, beta_scalar,
                                                       st);
-    return alpha ? launch_bwd_rows_t<T, 32, true>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk, gv,
+    return alpha ? launch_bwd_rows_t<T, 16, 8, true>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk, gv,
                                                   gbeta, galpha, B, L, H, d, beta_scalar, st)
-                 : launch_bwd_rows_t<T, 32, false>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk,
+                 : launch_bwd_rows_t<T, 16, 8, false>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk,
                                                    gv, gbeta, galpha, B, L, H, d, beta_scalar,
                                                    st);
 }
