@@ -34,7 +34,8 @@
 
 namespace {
 
-constexpr int CK = 64;  // tokens per checkpoint chunk
+constexpr int CK = 64;   // tokens per forward staging chunk
+constexpr int CKP = 16;  // tokens between the state checkpoints the forward writes
 
 template <typename T>
 static __device__ __forceinline__ float ldv(const T* p) {
@@ -80,24 +81,32 @@ __global__ void __launch_bounds__(kRowThreads)
     const bool row_ok = i < d;
     const long long rs = (long long)H * d;  // token stride
     const long long base = (long long)b * L * rs + (long long)h * d;
-    const int nck = (L + CK - 1) / CK;
+    const int ncp = (L + CKP - 1) / CKP;
     float* ck_row = ckpt != nullptr && row_ok
-                        ? ckpt + ((long long)b * H + h) * (nck + 1) * d * d + (long long)i * d
+                        ? ckpt + ((long long)b * H + h) * (ncp + 1) * d * d + (long long)i * d
                         : nullptr;
     float S[CPL];
 #pragma unroll
     for (int c = 0; c < CPL; ++c) S[c] = 0.0f;
+    // 16-byte stores when the row slice lies inside d and d % 4 == 0 (so the slice starts
+    // on a 16-byte boundary), scalar stores otherwise
+    const bool vec_ok = d % 4 == 0 && c0 + CPL <= d;
     auto save_state = [&](int slot) {
         if (ck_row == nullptr) return;
-        float* dst = ck_row + (long long)slot * d * d;
+        float* dst = ck_row + (long long)slot * d * d + c0;
+        if (vec_ok) {
 #pragma unroll
-        for (int c = 0; c < CPL; ++c)
-            if (c0 + c < d) dst[c0 + c] = S[c];
+            for (int c = 0; c < CPL; c += 4)
+                *reinterpret_cast<float4*>(dst + c) = make_float4(S[c], S[c + 1], S[c + 2], S[c + 3]);
+        } else {
+#pragma unroll
+            for (int c = 0; c < CPL; ++c)
+                if (c0 + c < d) dst[c] = S[c];
+        }
     };
 
     for (int t0 = 0; t0 < L; t0 += CK) {
         const int tn = min(CK, L - t0);
-        save_state(t0 / CK);
         __syncthreads();  // the previous chunk's stage is consumed
         // ---- stage this chunk (loads batched per thread before the stores)
         for (int base_idx = 0; base_idx < CK * 4 * CPL; base_idx += kRowThreads * 8) {
@@ -137,6 +146,7 @@ __global__ void __launch_bounds__(kRowThreads)
         __syncthreads();
         // ---- the chunk's tokens, row by row in registers
         for (int tt = 0; tt < tn; ++tt) {
+            if (tt % CKP == 0) save_state((t0 + tt) / CKP);
             const float* kr = sk + tt * RP + part * SP;
             const float* qr = sq + tt * RP + part * SP;
             float r = 0.0f;
@@ -172,14 +182,14 @@ __global__ void __launch_bounds__(kRowThreads)
             if (rb + r < d) st_scalar<T>(o + base + (long long)(t0 + tt) * rs + rb + r, so[idx]);
         }
     }
-    save_state(nck);
+    save_state(ncp);
 }
 
 size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 size_t ckpt_bytes(int B, int L, int H, int d) {
-    const int nck = (L + CK - 1) / CK;
-    return (size_t)B * H * (nck + 1) * d * d * sizeof(float);
+    const int ncp = (L + CKP - 1) / CKP;
+    return (size_t)B * H * (ncp + 1) * d * d * sizeof(float);
 }
 
 // ---------------------------------------------------------------- backward, row-parallel
@@ -192,20 +202,16 @@ size_t ckpt_bytes(int B, int L, int H, int d) {
 // summed over rows, and a per-token beta's gradient, couple the rows.
 // grid (H, B, ceil(d / 32)), 32 rows per CTA, LPR lanes of CPL columns per row: 8 lanes
 // of 16 columns for d > 32 (256 threads: twice the forward's warps, for latency hiding),
-// 4 lanes of 8 columns for d <= 32.  A checkpoint chunk (CK tokens) is walked in reverse
-// in pieces of SB tokens:
-//   pass 1: from the chunk's checkpoint, forward over the chunk, keeping the state at every
-//           piece start (pstart);
-//   pass 2: per piece, last first: forward over the piece from its start writing every S_{t-1}
-//           row slice (sbuf), then backward over the piece reading them back.
-// pstart and sbuf are per-CTA scratch (320 KB per CTA at d = 128, L2-resident); each
-// thread reads back only what it wrote.  Row sums: per token, a lane's 2 CPL partials
+// 4 lanes of 8 columns for d <= 32.  The forward's checkpoints are SB = CKP tokens
+// apart; per checkpoint piece, last first: forward over the piece from its checkpoint
+// writing every S_{t-1} row slice to a per-CTA scratch (sbuf: 256 KB per CTA at d = 128,
+// L2-resident; each thread reads back only what it wrote), then backward over the piece
+// reading them back.  Row sums: per token, a lane's 2 CPL partials
 // are summed over the rows of its warp that share its column slice by recursive
 // halving, the warps' sums meet in shared memory every RB tokens, and one partial per
 // (row block, token, head) goes to global memory, where delta_rows_reduce_kernel adds
 // the row blocks in a fixed order.
-constexpr int SB = 16;  // tokens per backward piece
-constexpr int NPIECE = CK / SB;
+constexpr int SB = CKP;  // tokens per backward piece: one checkpoint interval
 
 // Sums v over the lanes that differ in bits 5 - ROUNDS .. 4 (the rows of a warp that
 // share a column slice: 8 rows at 4 lanes per row, 4 rows at 8).  Recursive halving:
@@ -254,10 +260,10 @@ struct RowsBwdSmem {
     static constexpr size_t bytes = floats * sizeof(float);
 };
 
-// per-CTA scratch floats: NPIECE piece starts + SB token states of 32 rows x W columns
+// per-CTA scratch floats: SB token states of 32 rows x W columns
 template <int CPL, int LPR>
 constexpr size_t rows_scratch_floats() {
-    return (size_t)(NPIECE + SB) * 32 * LPR * CPL;
+    return (size_t)SB * 32 * LPR * CPL;
 }
 
 template <typename T, int CPL, int LPR, bool GATED>
@@ -295,11 +301,10 @@ __global__ void __launch_bounds__(32 * LPR, 2)
     const bool row_ok = i < d;
     const long long rs = (long long)H * d;
     const long long base = (long long)b * L * rs + (long long)h * d;
-    const int nck = (L + CK - 1) / CK;
+    const int ncp = (L + CKP - 1) / CKP;
     const long long cta = ((long long)b * H + h) * gridDim.z + z;
-    float* pstart = scratch + cta * rows_scratch_floats<CPL, LPR>();
-    float* sbuf = pstart + (size_t)NPIECE * NT * CPL;
-    const float* ck_unit = ckpt + ((long long)b * H + h) * (nck + 1) * d * d;
+    float* sbuf = scratch + cta * rows_scratch_floats<CPL, LPR>();
+    const float* ck_unit = ckpt + ((long long)b * H + h) * (ncp + 1) * d * d;
     const int hb = halving_base<ROUNDS>(lane, NV);
 
     auto st_slice = [&](float* dst, const float2 (&x)[NP]) {
@@ -489,31 +494,17 @@ __global__ void __launch_bounds__(32 * LPR, 2)
         if (tt % RB == 0) flush(pt0, tt, min(RB, pn - tt));
     };
 
-    for (int ch = nck - 1; ch >= 0; --ch) {
-        const int t0 = ch * CK, tn = min(CK, L - t0);
-        const int np = (tn + SB - 1) / SB;
-        // ---- pass 1: piece-start states from the checkpoint
+    for (int p = ncp - 1; p >= 0; --p) {
         {
-            float2 S[NP];
-            const float* src = ck_unit + (long long)ch * d * d + (long long)i * d + c0;
-#pragma unroll
-            for (int p = 0; p < NP; ++p)
-                S[p] = make_float2((row_ok && c0 + 2 * p < d) ? src[2 * p] : 0.0f,
-                                   (row_ok && c0 + 2 * p + 1 < d) ? src[2 * p + 1] : 0.0f);
-            for (int p = 0; p < np; ++p) {
-                st_slice(pstart + (size_t)p * NT * CPL, S);
-                if (p == np - 1) break;
-                stage(t0 + p * SB, SB, false);
-                for (int tt = 0; tt < SB; ++tt) fwd_step(S, tt);
-            }
-        }
-        // ---- pass 2: pieces in reverse
-        for (int p = np - 1; p >= 0; --p) {
-            const int pt0 = t0 + p * SB, pn = min(SB, tn - p * SB);
+            const int pt0 = p * SB, pn = min(SB, L - pt0);
             stage(pt0, pn, true);
             {
                 float2 S[NP];
-                ld_slice(pstart + (size_t)p * NT * CPL, S);
+                const float* src = ck_unit + (long long)p * d * d + (long long)i * d + c0;
+#pragma unroll
+                for (int q2 = 0; q2 < NP; ++q2)
+                    S[q2] = make_float2((row_ok && c0 + 2 * q2 < d) ? src[2 * q2] : 0.0f,
+                                        (row_ok && c0 + 2 * q2 + 1 < d) ? src[2 * q2 + 1] : 0.0f);
                 for (int tt = 0; tt < pn; ++tt) {
                     st_slice(sbuf + (size_t)tt * NT * CPL, S);
                     fwd_step(S, tt);
