@@ -44,27 +44,30 @@ static __device__ __forceinline__ float ldv(const T* p) {
 
 // Forward, row-parallel.  Each row i of S (value index) evolves on its own in
 // the forward: S[i] <- alpha S[i] + beta_i (v_i - alpha S[i].k) k^T,
-// o_i = S[i].q, so a row lives in the registers of 4 lanes (CPL columns each)
-// and no block barrier is needed per token; k, q and the CTA's rows of v,
-// beta (and alpha) are staged in shared memory one CK-token chunk at a time.
-// grid (H, B, ceil(d / 32)), 128 threads = 32 rows x 4 lanes.  Shared memory
-// (dynamic): k, q [CK][4][CPL + 4] (a pad of 4 floats per lane's slice puts
-// the 4 slices of one token on different banks) | v, beta, o [CK][32] | alpha [CK].
-constexpr int kRowThreads = 128, kRowsPerCta = 32;
+// o_i = S[i].q, so a row lives in the registers of LPR lanes (CPL columns each:
+// 8 x 16 for d > 32, 4 x 8 for d <= 32) and no block barrier is needed per token;
+// k, q and the CTA's rows of v, beta (and alpha) are staged in shared memory one
+// CK-token chunk at a time.  grid (H, B, ceil(d / 32)), 32 rows x LPR lanes per CTA.
+// Shared memory (dynamic): k, q [CK][LPR][CPL + 4] (a pad of 4 floats per lane's
+// slice puts the slices of one token on different banks) | v, beta, o [CK][32] |
+// alpha [CK].
+constexpr int kRowsPerCta = 32;
 
-template <int CPL>
+template <int CPL, int LPR>
 constexpr size_t fwd_rows_smem() {
-    return ((size_t)2 * CK * 4 * (CPL + 4) + 3 * CK * kRowsPerCta + CK) * sizeof(float);
+    return ((size_t)2 * CK * LPR * (CPL + 4) + 3 * CK * kRowsPerCta + CK) * sizeof(float);
 }
 
-template <typename T, int CPL, bool GATED>
-__global__ void __launch_bounds__(kRowThreads)
+template <typename T, int CPL, int LPR, bool GATED>
+__global__ void __launch_bounds__(32 * LPR)
     delta_fwd_rows_kernel(const T* __restrict__ q, const T* __restrict__ k,
                           const T* __restrict__ v, const T* __restrict__ beta,
                           const T* __restrict__ alpha, T* __restrict__ o,
                           float* __restrict__ ckpt, int L, int H, int d, int beta_scalar) {
-    constexpr int SP = CPL + 4;  // floats per lane slice (padded)
-    constexpr int RP = 4 * SP;   // floats per staged token row
+    constexpr int NT = 32 * LPR;      // threads
+    constexpr int W = LPR * CPL;      // columns per CTA
+    constexpr int SP = CPL + 4;       // floats per lane slice (padded)
+    constexpr int RP = LPR * SP;      // floats per staged token row
     extern __shared__ __align__(16) float smf[];
     float* sk = smf;                        // [CK][RP]
     float* sq = sk + CK * RP;               // [CK][RP]
@@ -74,9 +77,9 @@ __global__ void __launch_bounds__(kRowThreads)
     float* sa = so + CK * kRowsPerCta;      // [CK]
     const int h = blockIdx.x, b = blockIdx.y, rb = blockIdx.z * kRowsPerCta;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int rl = warp * 8 + (lane >> 2);  // local row
+    const int rl = warp * (32 / LPR) + lane / LPR;  // local row
     const int i = rb + rl;                  // value-dim row of S
-    const int part = lane & 3;              // column slice [part CPL, part CPL + CPL)
+    const int part = lane % LPR;            // column slice [part CPL, part CPL + CPL)
     const int c0 = part * CPL;
     const bool row_ok = i < d;
     const long long rs = (long long)H * d;  // token stride
@@ -109,12 +112,12 @@ __global__ void __launch_bounds__(kRowThreads)
         const int tn = min(CK, L - t0);
         __syncthreads();  // the previous chunk's stage is consumed
         // ---- stage this chunk (loads batched per thread before the stores)
-        for (int base_idx = 0; base_idx < CK * 4 * CPL; base_idx += kRowThreads * 8) {
+        for (int base_idx = 0; base_idx < CK * W; base_idx += NT * 8) {
             float fk[8], fq[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
-                const int idx = base_idx + tid + u * kRowThreads;
-                const int tt = idx / (4 * CPL), c = idx % (4 * CPL);
+                const int idx = base_idx + tid + u * NT;
+                const int tt = idx / W, c = idx % W;
                 const bool ok = tt < tn && c < d;
                 const long long off = base + (long long)(t0 + tt) * rs + c;
                 fk[u] = ok ? ldv(k + off) : 0.0f;
@@ -122,8 +125,8 @@ __global__ void __launch_bounds__(kRowThreads)
             }
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
-                const int idx = base_idx + tid + u * kRowThreads;
-                const int tt = idx / (4 * CPL), c = idx % (4 * CPL);
+                const int idx = base_idx + tid + u * NT;
+                const int tt = idx / W, c = idx % W;
                 if (tt < CK) {
                     const int so_ = tt * RP + (c / CPL) * SP + c % CPL;
                     sk[so_] = fk[u];
@@ -131,7 +134,7 @@ __global__ void __launch_bounds__(kRowThreads)
                 }
             }
         }
-        for (int idx = tid; idx < CK * kRowsPerCta; idx += kRowThreads) {
+        for (int idx = tid; idx < CK * kRowsPerCta; idx += NT) {
             const int tt = idx / kRowsPerCta, r = idx % kRowsPerCta;
             const bool ok = tt < tn && rb + r < d;
             const long long off = base + (long long)(t0 + tt) * rs + rb + r;
@@ -141,7 +144,7 @@ __global__ void __launch_bounds__(kRowThreads)
                                         : ldv(beta + off);
         }
         if (GATED)
-            for (int tt = tid; tt < CK; tt += kRowThreads)
+            for (int tt = tid; tt < CK; tt += NT)
                 sa[tt] = tt < tn ? ldv(alpha + ((long long)b * L + t0 + tt) * H + h) : 1.0f;
         __syncthreads();
         // ---- the chunk's tokens, row by row in registers
@@ -155,8 +158,8 @@ __global__ void __launch_bounds__(kRowThreads)
                 const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
                 r = fmaf(S[c], k4.x, fmaf(S[c + 1], k4.y, fmaf(S[c + 2], k4.z, fmaf(S[c + 3], k4.w, r))));
             }
-            r += __shfl_xor_sync(0xffffffffu, r, 1);
-            r += __shfl_xor_sync(0xffffffffu, r, 2);
+#pragma unroll
+            for (int o2 = 1; o2 < LPR; o2 <<= 1) r += __shfl_xor_sync(0xffffffffu, r, o2);
             const float al = GATED ? sa[tt] : 1.0f;
             const float u = sb[tt * kRowsPerCta + rl] * (sv[tt * kRowsPerCta + rl] - al * r);
             float ov = 0.0f;
@@ -172,12 +175,12 @@ __global__ void __launch_bounds__(kRowThreads)
                     ov = fmaf(sn, qv[e], ov);
                 }
             }
-            ov += __shfl_xor_sync(0xffffffffu, ov, 1);
-            ov += __shfl_xor_sync(0xffffffffu, ov, 2);
+#pragma unroll
+            for (int o2 = 1; o2 < LPR; o2 <<= 1) ov += __shfl_xor_sync(0xffffffffu, ov, o2);
             if (part == 0) so[tt * kRowsPerCta + rl] = ov;
         }
         __syncthreads();
-        for (int idx = tid; idx < tn * kRowsPerCta; idx += kRowThreads) {
+        for (int idx = tid; idx < tn * kRowsPerCta; idx += NT) {
             const int tt = idx / kRowsPerCta, r = idx % kRowsPerCta;
             if (rb + r < d) st_scalar<T>(o + base + (long long)(t0 + tt) * rs + rb + r, so[idx]);
         }
@@ -630,16 +633,16 @@ int launch_bwd_rows(const void* q, const void* k, const void* v, const void* bet
 }
 
 
-template <typename T, int CPL, bool GATED>
+template <typename T, int CPL, int LPR, bool GATED>
 int launch_fwd_rows(const void* q, const void* k, const void* v, const void* beta,
                     const void* alpha, void* o, float* ckpt, int B, int L, int H, int d,
                     int beta_scalar, cudaStream_t st) {
-    constexpr size_t smem = fwd_rows_smem<CPL>();
-    cudaError_t e = cudaFuncSetAttribute(delta_fwd_rows_kernel<T, CPL, GATED>,
+    constexpr size_t smem = fwd_rows_smem<CPL, LPR>();
+    cudaError_t e = cudaFuncSetAttribute(delta_fwd_rows_kernel<T, CPL, LPR, GATED>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return (int)e;
-    delta_fwd_rows_kernel<T, CPL, GATED>
-        <<<dim3(H, B, (d + kRowsPerCta - 1) / kRowsPerCta), kRowThreads, smem, st>>>(
+    delta_fwd_rows_kernel<T, CPL, LPR, GATED>
+        <<<dim3(H, B, (d + kRowsPerCta - 1) / kRowsPerCta), 32 * LPR, smem, st>>>(
             (const T*)q, (const T*)k, (const T*)v, (const T*)beta, (const T*)alpha, (T*)o, ckpt,
             L, H, d, beta_scalar);
     return edb::status_from_cuda(cudaGetLastError());
@@ -651,14 +654,14 @@ int launch_fwd(const void* q, const void* k, const void* v, const void* beta, co
                cudaStream_t st) {
     if (d <= 32)
         return alpha != nullptr
-                   ? launch_fwd_rows<T, 8, true>(q, k, v, beta, alpha, o, ckpt, B, L, H, d,
+                   ? launch_fwd_rows<T, 8, 4, true>(q, k, v, beta, alpha, o, ckpt, B, L, H, d,
                                                  beta_scalar, st)
-                   : launch_fwd_rows<T, 8, false>(q, k, v, beta, alpha, o, ckpt, B, L, H, d,
+                   : launch_fwd_rows<T, 8, 4, false>(q, k, v, beta, alpha, o, ckpt, B, L, H, d,
                                                   beta_scalar, st);
     return alpha != nullptr
-               ? launch_fwd_rows<T, 32, true>(q, k, v, beta, alpha, o, ckpt, B, L, H, d,
+               ? launch_fwd_rows<T, 16, 8, true>(q, k, v, beta, alpha, o, ckpt, B, L, H, d,
                                               beta_scalar, st)
-               : launch_fwd_rows<T, 32, false>(q, k, v, beta, alpha, o, ckpt, B, L, H, d,
+               : launch_fwd_rows<T, 16, 8, false>(q, k, v, beta, alpha, o, ckpt, B, L, H, d,
                                                beta_scalar, st);
 }
 
