@@ -754,9 +754,23 @@ __global__ void __launch_bounds__(256)
     const float add = gm / dtm[row] / (float)D;
     const T* p = dt + row * D;
     T* g = gdt + row * D;
-    for (int i = lane; i < D; i += 32) {
-        const float draw = ldf(p + i);
-        if (draw >= dt_min && draw <= dt_max) st_scalar<T>(g + i, ldf(g + i) + add);
+    constexpr int EPV = 16 / (int)sizeof(T);
+    if (D % EPV == 0 && (reinterpret_cast<uintptr_t>(p) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(g) & 15) == 0) {
+        for (int i = lane * EPV; i < D; i += 32 * EPV) {
+            float fd[EPV], fg[EPV];
+            Vec16<T>::unpack(*reinterpret_cast<const uint4*>(p + i), fd);
+            Vec16<T>::unpack(*reinterpret_cast<const uint4*>(g + i), fg);
+#pragma unroll
+            for (int j = 0; j < EPV; ++j)
+                if (fd[j] >= dt_min && fd[j] <= dt_max) fg[j] += add;
+            *reinterpret_cast<uint4*>(g + i) = Vec16<T>::pack(fg);
+        }
+    } else {
+        for (int i = lane; i < D; i += 32) {
+            const float draw = ldf(p + i);
+            if (draw >= dt_min && draw <= dt_max) st_scalar<T>(g + i, ldf(g + i) + add);
+        }
     }
 }
 
