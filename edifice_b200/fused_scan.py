@@ -231,17 +231,11 @@ class DiagLinearFn(torch.autograd.Function):
 
 
 # --------------------------------------------- scans over host-resident tensors
-_HOST_WS = {}
-
-
 def _host_ws(device, nbytes):
-    """Device workspace for the host entry points, kept per device and grown on
-    demand (the caching allocator would hand back the same block anyway)."""
-    ws = _HOST_WS.get(device)
-    if ws is None or ws.numel() < nbytes:
-        ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
-        _HOST_WS[device] = ws
-    return ws
+    """Device workspace for one host-entry call, from torch's caching allocator on
+    the current stream: stream-ordered, so concurrent calls on different streams
+    never share a ring (a reused block comes back only after its stream is done)."""
+    return torch.empty(nbytes, dtype=torch.uint8, device=device)
 
 
 def _host_train(op, x0, x1, dy, h0, out, device, what):
