@@ -73,6 +73,11 @@ SIGNATURES = {
     "edb_flash_attention_bwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i,
                                      _i, _i, _i, _i, _f, _vp, _sz, _vp]),
 }
+# descriptor form: every op, both directions, takes (const args*, stream, ws, ws_bytes)
+for _op in ("linear_scan", "mingru", "selective_scan", "delta_rule", "flash_attention"):
+    for _dir in ("fwd", "bwd"):
+        SIGNATURES["edb_%s_%s_desc_workspace" % (_op, _dir)] = (_sz, [_vp])
+        SIGNATURES["edb_%s_%s_desc" % (_op, _dir)] = (_i, [_vp, _vp, _vp, _sz])
 
 EDB_F32, EDB_BF16 = 0, 1
 EDB_NATIVE_ELU_GRU, EDB_NATIVE_REAL_GRU, EDB_NATIVE_DIAG_LINEAR = 0, 1, 2

@@ -427,6 +427,141 @@ int edb_selective_scan_bwd_noalloc(int dtype, const void* x, const void* dt, con
                                    int batch, int seq_len, int d_inner, int d_state, float dt_min,
                                    float dt_max, void* stream);
 
+/* ========================================================================
+ * Descriptor form of the ABI.  One argument struct per op carries every tensor
+ * as an edb_tensor (device pointer, dtype, shape, element strides) next to the
+ * op's flags, and each direction has a workspace query and an entry point:
+ *   size_t edb_<op>_{fwd,bwd}_desc_workspace(const edb_<op>_args* args);
+ *   int    edb_<op>_{fwd,bwd}_desc(const edb_<op>_args* args, void* stream,
+ *                                  void* workspace, size_t workspace_bytes);
+ * The entry points compute what the positional entry points above compute.
+ *   - A tensor is used in place when it is dense row-major (strides all zero
+ *     also mean dense) and 16-byte aligned.  Any other input (a transposed or
+ *     sliced view, a broadcast with stride 0, a negative stride, an unaligned
+ *     pointer) is first gathered into a dense copy inside the workspace; any
+ *     other output is computed into a dense copy and scattered back through
+ *     its strides.  Outputs may not have a zero stride on a dimension of
+ *     extent > 1, and outputs must not overlap inputs.
+ *   - The workspace query covers those copies plus the op's own scratch; it
+ *     returns 0 when no workspace is needed or the arguments are invalid (the
+ *     entry point then returns the reason).  A non-empty workspace must be
+ *     256-byte aligned.
+ *   - Residuals the backward reads back (lse, dt_mean, checkpoints) are plain
+ *     dense f32 buffers, as in the positional entry points.
+ *   - Validation (null, dtype, shape, stride, workspace size) happens on the
+ *     host before any GPU work; the codes are the edb_status values.
+ * This is the in-graph boundary the EXLA custom-call handlers
+ * ("exla_fused_<op>_<dtype>", e.g. native/cuda/fused_selective_scan.cu:185-202)
+ * bind: an XLA FFI buffer's dims and layout map onto edb_tensor directly.
+ * ---------------------------------------------------------------------- */
+#define EDB_MAX_DIMS 4
+
+typedef struct {
+    void* data;                      /* device pointer; NULL = absent (optional tensors) */
+    int dtype;                       /* EDB_F32 / EDB_BF16 */
+    int ndim;                        /* 1..EDB_MAX_DIMS */
+    long long shape[EDB_MAX_DIMS];   /* extents, outermost first */
+    long long strides[EDB_MAX_DIMS]; /* in elements; all zero = dense row-major */
+} edb_tensor;
+
+/* Linear scan (edb_linear_scan_fwd / _bwd).  io tensors in `dtype`:
+ * a, b, h, dy, ga, gb [batch, seq_len, hidden]; h0, gh0 [batch, hidden],
+ * optional.  fwd reads a, b, h0 and writes h; bwd reads a, h0, h, dy and writes
+ * ga, gb, gh0. */
+typedef struct {
+    int dtype;
+    edb_tensor a, b, h0, h;
+    edb_tensor dy, ga, gb, gh0;
+} edb_linear_scan_args;
+
+/* MinGRU (edb_mingru_fwd / _bwd): z (sigmoided), c as a, b above. */
+typedef struct {
+    int dtype;
+    edb_tensor z, c, h0, h;
+    edb_tensor dy, gz, gc, gh0;
+} edb_mingru_args;
+
+/* Selective scan.  semantics EDB_SSM_KERNEL: edb_selective_scan_fwd / _bwd
+ * (A required); EDB_SSM_MODEL: edb_selective_scan_model_fwd / _bwd (A optional,
+ * dt_mean required).  x, dt, y, dy, gx, gdt [batch, seq_len, d_inner] and
+ * B, C [batch, seq_len, d_state], A [d_inner, d_state] in `dtype`; gB, gC
+ * [batch, seq_len, d_state] f32.  dt_mean: dense f32 [batch, seq_len];
+ * h_ckpt: optional, edb_selective_scan_ckpt_bytes() bytes. */
+enum { EDB_SSM_KERNEL = 0, EDB_SSM_MODEL = 1 };
+typedef struct {
+    int dtype;
+    int semantics;
+    float dt_min, dt_max;
+    edb_tensor x, dt, A, B, C, y;
+    float* dt_mean;
+    float* h_ckpt;
+    edb_tensor dy, gx, gdt, gB, gC;
+} edb_selective_scan_args;
+
+/* Delta rule: alpha absent = DeltaNet (edb_delta_rule_fwd / _bwd), alpha
+ * present = GatedDeltaNet (edb_gated_delta_net_fwd / _bwd).  q, k, v, o, dO,
+ * gq, gk, gv [batch, seq_len, heads, head_dim]; beta, gbeta [batch, seq_len,
+ * heads] (EDB_BETA_PER_TOKEN) or [batch, seq_len, heads, head_dim]
+ * (EDB_BETA_PER_ELEMENT); alpha, galpha [batch, seq_len, heads]; all in
+ * `dtype`.  s_ckpt: optional, the positional entry points' checkpoint bytes. */
+enum { EDB_BETA_PER_TOKEN = 0, EDB_BETA_PER_ELEMENT = 1 };
+typedef struct {
+    int dtype;
+    int beta_mode;
+    edb_tensor q, k, v, beta, alpha, o;
+    float* s_ckpt;
+    edb_tensor dO, gq, gk, gv, gbeta, galpha;
+} edb_delta_rule_args;
+
+/* Flash attention (edb_flash_attention_fwd / _bwd).  q, o, dO, dq [batch,
+ * q_heads, seq_len, head_dim]; k, v, dk, dv [batch, kv_heads, seq_len,
+ * head_dim]; all in `dtype`.  num_kv_heads: 0 or k's second extent.  lse:
+ * optional dense f32 [batch, q_heads, seq_len] (written by fwd, read by bwd). */
+typedef struct {
+    int dtype;
+    int causal;
+    int num_kv_heads;
+    float scale;
+    edb_tensor q, k, v, o;
+    float* lse;
+    edb_tensor dO, dq, dk, dv;
+} edb_flash_attention_args;
+
+size_t edb_linear_scan_fwd_desc_workspace(const edb_linear_scan_args* args);
+int edb_linear_scan_fwd_desc(const edb_linear_scan_args* args, void* stream, void* workspace,
+                             size_t workspace_bytes);
+size_t edb_linear_scan_bwd_desc_workspace(const edb_linear_scan_args* args);
+int edb_linear_scan_bwd_desc(const edb_linear_scan_args* args, void* stream, void* workspace,
+                             size_t workspace_bytes);
+
+size_t edb_mingru_fwd_desc_workspace(const edb_mingru_args* args);
+int edb_mingru_fwd_desc(const edb_mingru_args* args, void* stream, void* workspace,
+                        size_t workspace_bytes);
+size_t edb_mingru_bwd_desc_workspace(const edb_mingru_args* args);
+int edb_mingru_bwd_desc(const edb_mingru_args* args, void* stream, void* workspace,
+                        size_t workspace_bytes);
+
+size_t edb_selective_scan_fwd_desc_workspace(const edb_selective_scan_args* args);
+int edb_selective_scan_fwd_desc(const edb_selective_scan_args* args, void* stream,
+                                void* workspace, size_t workspace_bytes);
+size_t edb_selective_scan_bwd_desc_workspace(const edb_selective_scan_args* args);
+int edb_selective_scan_bwd_desc(const edb_selective_scan_args* args, void* stream,
+                                void* workspace, size_t workspace_bytes);
+
+size_t edb_delta_rule_fwd_desc_workspace(const edb_delta_rule_args* args);
+int edb_delta_rule_fwd_desc(const edb_delta_rule_args* args, void* stream, void* workspace,
+                            size_t workspace_bytes);
+size_t edb_delta_rule_bwd_desc_workspace(const edb_delta_rule_args* args);
+int edb_delta_rule_bwd_desc(const edb_delta_rule_args* args, void* stream, void* workspace,
+                            size_t workspace_bytes);
+
+size_t edb_flash_attention_fwd_desc_workspace(const edb_flash_attention_args* args);
+int edb_flash_attention_fwd_desc(const edb_flash_attention_args* args, void* stream,
+                                 void* workspace, size_t workspace_bytes);
+size_t edb_flash_attention_bwd_desc_workspace(const edb_flash_attention_args* args);
+int edb_flash_attention_bwd_desc(const edb_flash_attention_args* args, void* stream,
+                                 void* workspace, size_t workspace_bytes);
+
 #ifdef __cplusplus
 }
 #endif

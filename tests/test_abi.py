@@ -81,3 +81,80 @@ def test_host_validation_rejects_bad_arguments():
     assert lib.edb_gated_delta_net_bwd(0, dummy, dummy, dummy, dummy, 1, dummy, dummy, None,
                                        dummy, dummy, dummy, dummy, dummy, 1, 4, 2, 8, dummy,
                                        need - 1, None) == 1004
+
+
+# ---------------------------------------------------------------- descriptor form
+def test_descriptor_workspace_counts_copies_of_non_dense_tensors():
+    from edifice_b200 import descriptor as D
+    base, B, L, H = 1 << 24, 2, 8, 64
+    dense = lambda off=0: D.tensor(base + off, _lib.EDB_BF16, (B, L, H))
+    a = D.make_args("linear_scan", _lib.EDB_BF16)
+    a.a, a.b, a.h = dense(), dense(4096), dense(8192)
+    assert D.workspace_bytes("linear_scan", "fwd", a) == 0
+    # a transposed view of a [B, H, L] buffer needs one dense copy (2 * 8 * 64 bf16 -> 2 KB)
+    a.b = D.tensor(base, _lib.EDB_BF16, (B, L, H), (L * H, 1, L))
+    assert D.workspace_bytes("linear_scan", "fwd", a) == 2048
+    # an unaligned dense pointer is copied too; a broadcast h0 (stride 0) as well
+    a.b = dense(2)
+    a.h0 = D.tensor(base, _lib.EDB_BF16, (B, H), (0, 1))
+    assert D.workspace_bytes("linear_scan", "fwd", a) == 2048 + 256
+    # the backward adds the positional entry point's own scratch on top of the copies
+    f = D.make_args("flash_attention", _lib.EDB_BF16, causal=1)
+    q = D.tensor(base, _lib.EDB_BF16, (1, 4, 256, 128))
+    kv = D.tensor(base, _lib.EDB_BF16, (1, 2, 256, 128))
+    f.q = f.o = f.dO = f.dq = q
+    f.k = f.v = f.dk = f.dv = kv
+    lib = edifice_b200.load()
+    inner = lib.edb_flash_attention_bwd_workspace(1, 1, 4, 2, 256, 128, 0)
+    assert D.workspace_bytes("flash_attention", "bwd", f) == inner
+    f.q = D.tensor(base, _lib.EDB_BF16, (1, 4, 256, 128), (256 * 4 * 128, 128, 4 * 128, 1))
+    assert D.workspace_bytes("flash_attention", "bwd", f) == inner + 4 * 256 * 128 * 2
+
+
+def test_descriptor_validation_before_any_gpu_work():
+    from edifice_b200 import descriptor as D
+    lib = edifice_b200.load()
+    base, B, L, H = 1 << 24, 2, 8, 64
+    dense = lambda dt=_lib.EDB_BF16, shape=(B, L, H): D.tensor(base, dt, shape)
+
+    def st(op, direction, args, ws=None, nbytes=0):
+        fn = getattr(lib, "edb_%s_%s_desc" % (op, direction))
+        return fn(ctypes.byref(args), None, ws, nbytes)
+
+    a = D.make_args("linear_scan", _lib.EDB_BF16)
+    a.a, a.b = dense(), dense()
+    assert st("linear_scan", "fwd", a) == 1000                    # h missing
+    a.h = dense(_lib.EDB_F32)
+    assert st("linear_scan", "fwd", a) == 1002                    # dtype mismatch
+    a.h = dense(shape=(B, L, H + 1))
+    assert st("linear_scan", "fwd", a) == 1001                    # shape mismatch
+    a.h = D.tensor(base, _lib.EDB_BF16, (B, L, H), (L * H, 0, 1))
+    assert st("linear_scan", "fwd", a) == 1001                    # output with a zero stride
+    a.h = D.tensor(base, _lib.EDB_BF16, (B, L, H), (L * H, 1, L))
+    assert st("linear_scan", "fwd", a) == 1004                    # needs a workspace
+    assert st("linear_scan", "fwd", a, base + 16, 1 << 20) == 1003  # not 256-aligned
+    a.dtype = 5
+    assert st("linear_scan", "fwd", a) == 1002
+    # selective scan: A is required in kernel semantics, dt_mean in model semantics
+    s = D.make_args("selective_scan", _lib.EDB_F32, semantics=D.SSM_KERNEL, dt_min=1e-3,
+                    dt_max=0.1)
+    s.x, s.dt, s.y = (dense(_lib.EDB_F32),) * 3
+    s.B = s.C = dense(_lib.EDB_F32, (B, L, 16))
+    assert st("selective_scan", "fwd", s) == 1000
+    s.semantics = D.SSM_MODEL
+    assert st("selective_scan", "fwd", s) == 1000
+    s.semantics = 7
+    assert st("selective_scan", "fwd", s) == 1005
+    # delta rule: beta's rank follows beta_mode; a decay gradient needs a decay
+    d = D.make_args("delta_rule", _lib.EDB_BF16, beta_mode=D.BETA_PER_ELEMENT)
+    d.q = d.k = d.v = d.o = d.dO = d.gq = d.gk = d.gv = dense(shape=(B, L, 2, 32))
+    d.beta = d.gbeta = dense(shape=(B, L, 2))
+    assert st("delta_rule", "fwd", d) == 1001
+    d.beta_mode = D.BETA_PER_TOKEN
+    d.galpha = dense(shape=(B, L, 2))
+    assert st("delta_rule", "bwd", d) == 1005
+    # flash attention: num_kv_heads must agree with k
+    f = D.make_args("flash_attention", _lib.EDB_BF16, num_kv_heads=3)
+    f.q = f.o = dense(shape=(1, 4, 64, 64))
+    f.k = f.v = dense(shape=(1, 2, 64, 64))
+    assert st("flash_attention", "fwd", f) == 1001

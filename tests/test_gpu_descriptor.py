@@ -1,0 +1,237 @@
+"""GPU checks of the descriptor form of the C ABI (edb_<op>_{fwd,bwd}_desc).
+
+Every case feeds the descriptor entry points strided views -- transposed
+layouts, slices of packed buffers, broadcasts, unaligned pointers -- for inputs
+and outputs, and compares with the positional entry points run on contiguous
+copies of the same values.  The descriptor form gathers into dense copies and
+runs the same kernels, so results agree bit for bit wherever the kernels are
+deterministic (every path here but the flash-attention and chunked-DeltaNet
+backwards, whose f32 reductions may land in a different order: checked to
+1e-5 norm-relative).  Absolute correctness of those kernels is the oracle
+parity tests' job.
+"""
+import pytest
+import torch
+
+from edifice_b200 import descriptor as D
+from edifice_b200 import device_errors
+from edifice_b200 import fused_scan as fs
+
+pytestmark = pytest.mark.gpu
+
+
+def _g(seed):
+    return torch.Generator(device="cpu").manual_seed(seed)
+
+
+def _exact(a, b):
+    assert a.shape == b.shape and a.dtype == b.dtype
+    assert torch.equal(a, b), (a.float() - b.float()).abs().max().item()
+
+
+def _close(a, b, tol=1e-5):
+    a, b = a.double(), b.double()
+    assert ((a - b).norm() / b.norm().clamp_min(1e-30)).item() <= tol
+
+
+def _transposed(x, dims):
+    """A non-contiguous view equal to x: x's values stored with `dims` permuted."""
+    inv = [dims.index(i) for i in range(len(dims))]
+    return x.permute(*dims).contiguous().permute(*inv)
+
+
+def _unaligned(x):
+    """A dense view of x's values starting 2 bytes past a 16-byte boundary."""
+    flat = torch.empty(x.numel() + 8, dtype=x.dtype, device=x.device)
+    v = flat[1:1 + x.numel()].view(x.shape)
+    v.copy_(x)
+    return v
+
+
+def _out_view(shape, dtype, dims):
+    """An uninitialised output view with a permuted storage order."""
+    inv = [dims.index(i) for i in range(len(dims))]
+    store = torch.full([shape[d] for d in dims], float("nan"), dtype=dtype, device="cuda")
+    return store.permute(*inv)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_linear_scan_desc_strided(cuda, dtype):
+    g = _g(1)
+    B, L, H = 3, 300, 96
+    a = torch.sigmoid(torch.randn(B, L, H, generator=g)).to(dtype).cuda()
+    b = torch.randn(B, L, H, generator=g).to(dtype).cuda()
+    dy = torch.randn(B, L, H, generator=g).to(dtype).cuda()
+    h0row = torch.randn(1, H, generator=g).to(dtype).cuda()
+    h0 = h0row.expand(B, H)                        # broadcast, stride 0
+    h_ref = fs.linear_scan(a, b, h0.contiguous())
+    ga_r, gb_r, gh0_r = fs.linear_scan_backward(a, h0.contiguous(), h_ref, dy)
+
+    a_v, b_v = _transposed(a, [0, 2, 1]), _unaligned(b)
+    h = _out_view((B, L, H), dtype, [2, 0, 1])
+    args = D.make_args("linear_scan", dtype, a=a_v, b=b_v, h0=h0, h=h)
+    D.run("linear_scan", "fwd", args)
+    ga = _out_view((B, L, H), dtype, [1, 0, 2])
+    gb = torch.empty(B, L, 2 * H, dtype=dtype, device="cuda")[..., H:]   # slice of a wider row
+    gh0 = torch.empty(H, B, dtype=dtype, device="cuda").t()
+    args = D.make_args("linear_scan", dtype, a=a_v, h0=h0, h=_transposed(h_ref, [1, 0, 2]),
+                       dy=_unaligned(dy), ga=ga, gb=gb, gh0=gh0)
+    D.run("linear_scan", "bwd", args)
+    torch.cuda.synchronize()
+    _exact(h.contiguous(), h_ref)
+    for u, r in ((ga, ga_r), (gb, gb_r), (gh0, gh0_r)):
+        _exact(u.contiguous(), r)
+    assert device_errors() == 0
+
+
+def test_linear_scan_desc_dense_runs_in_place(cuda):
+    g = _g(2)
+    B, L, H = 2, 256, 128
+    a = torch.sigmoid(torch.randn(B, L, H, generator=g)).bfloat16().cuda()
+    b = torch.randn(B, L, H, generator=g).bfloat16().cuda()
+    h = torch.empty_like(a)
+    args = D.make_args("linear_scan", torch.bfloat16, a=a, b=b, h=h)
+    assert D.workspace_bytes("linear_scan", "fwd", args) == 0
+    D.run("linear_scan", "fwd", args)
+    _exact(h, fs.linear_scan(a, b))
+
+
+def test_mingru_desc_strided(cuda):
+    g = _g(3)
+    B, L, H = 2, 200, 130
+    z = torch.sigmoid(torch.randn(B, L, H, generator=g)).bfloat16().cuda()
+    c = torch.randn(B, L, H, generator=g).bfloat16().cuda()
+    dy = torch.randn(B, L, H, generator=g).bfloat16().cuda()
+    h_ref = fs.mingru_scan(z, c)
+    gz_r, gc_r, gh0_r = fs.mingru_backward(z, c, None, h_ref, dy)
+    # z and c interleaved in one [B, L, 2, H] buffer, as a fused projection leaves them
+    zc = torch.stack([z, c], dim=2)
+    h = _out_view((B, L, H), torch.bfloat16, [1, 2, 0])
+    D.run("mingru", "fwd", D.make_args("mingru", torch.bfloat16, z=zc[:, :, 0], c=zc[:, :, 1],
+                                       h=h))
+    gz, gc = _out_view((B, L, H), torch.bfloat16, [2, 1, 0]), torch.empty_like(z)
+    gh0 = torch.empty(B, H, dtype=torch.bfloat16, device="cuda")
+    D.run("mingru", "bwd", D.make_args("mingru", torch.bfloat16, z=zc[:, :, 0], c=zc[:, :, 1],
+                                       h=h, dy=_transposed(dy, [2, 1, 0]), gz=gz, gc=gc,
+                                       gh0=gh0))
+    torch.cuda.synchronize()
+    _exact(h.contiguous(), h_ref)
+    for u, r in ((gz, gz_r), (gc, gc_r), (gh0, gh0_r)):
+        _exact(u.contiguous(), r)
+
+
+@pytest.mark.parametrize("semantics", [D.SSM_KERNEL, D.SSM_MODEL])
+def test_selective_scan_desc_strided(cuda, semantics):
+    g = _g(4)
+    B, L, Dn, N = 2, 160, 256, 16
+    dtype = torch.bfloat16
+    x = torch.randn(B, L, Dn, generator=g).to(dtype).cuda()
+    dt = torch.nn.functional.softplus(0.5 * torch.randn(B, L, Dn, generator=g) - 2).to(dtype).cuda()
+    A = (-torch.exp(torch.rand(Dn, N, generator=g) * 2.77)).to(dtype).cuda()
+    Bm = torch.randn(B, L, N, generator=g).to(dtype).cuda()
+    Cm = torch.randn(B, L, N, generator=g).to(dtype).cuda()
+    dy = torch.randn(B, L, Dn, generator=g).to(dtype).cuda()
+    model = semantics == D.SSM_MODEL
+    if model:
+        y_r, dtm_r = fs.selective_scan_model(x, dt, Bm, Cm)
+        gx_r, gdt_r, gB_r, gC_r = fs.selective_scan_model_backward(x, dt, Bm, Cm, dy, dtm_r)
+    else:
+        y_r = fs.selective_scan(x, dt, A, Bm, Cm)
+        gx_r, gdt_r, gB_r, gC_r = fs.selective_scan_backward(x, dt, A, Bm, Cm, dy)
+    # B and C as the two halves of one dense(2N) projection output (common.ex:333-396)
+    BC = torch.cat([Bm, Cm], dim=-1)
+    dt_mean = torch.empty(B, L, dtype=torch.float32, device="cuda")
+    y = _out_view((B, L, Dn), dtype, [2, 0, 1])
+    common = dict(semantics=semantics, dt_min=1e-3, dt_max=0.1, x=_transposed(x, [1, 0, 2]),
+                  dt=_unaligned(dt), A=None if model else _transposed(A, [1, 0]),
+                  B=BC[..., :N], C=BC[..., N:], dt_mean=dt_mean)
+    D.run("selective_scan", "fwd", D.make_args("selective_scan", dtype, y=y, **common))
+    gx, gdt = _out_view((B, L, Dn), dtype, [1, 2, 0]), torch.empty_like(x)
+    gBC = torch.empty(B, L, 2 * N, dtype=torch.float32, device="cuda")
+    D.run("selective_scan", "bwd",
+          D.make_args("selective_scan", dtype, dy=dy, gx=gx, gdt=gdt, gB=gBC[..., :N],
+                      gC=gBC[..., N:], **common))
+    torch.cuda.synchronize()
+    _exact(y.contiguous(), y_r)
+    if model:
+        _exact(dt_mean, dtm_r)
+    for u, r in ((gx, gx_r), (gdt, gdt_r), (gBC[..., :N], gB_r), (gBC[..., N:], gC_r)):
+        _exact(u.contiguous(), r)
+    assert device_errors() == 0
+
+
+def _delta_inputs(B, L, H, d, dtype, seed, per_element=False):
+    g = _g(seed)
+    q, k, v, do = (torch.randn(B, L, H, d, generator=g) for _ in range(4))
+    k = k / torch.sqrt((k * k).sum(-1, keepdim=True) + 1e-6)
+    beta = torch.sigmoid(torch.randn(*((B, L, H, d) if per_element else (B, L, H)), generator=g))
+    alpha = 0.5 + 0.5 * torch.rand(B, L, H, generator=g)
+    return [t.to(dtype).cuda() for t in (q, k, v, beta, alpha, do)]
+
+
+@pytest.mark.parametrize("form", ["chunked", "token_per_element", "gated"])
+def test_delta_rule_desc_packed_qkv(cuda, form):
+    B, L, H, d = 2, 192, 2, (128 if form == "chunked" else 64)
+    dtype = torch.bfloat16
+    q, k, v, beta, alpha, do = _delta_inputs(B, L, H, d, dtype, 5,
+                                             per_element=form == "token_per_element")
+    gated = form == "gated"
+    if gated:
+        o_r = fs.gated_delta_net_scan(q, k, v, beta, alpha)
+        grads_r = fs.gated_delta_net_backward(q, k, v, beta, alpha, do)
+    else:
+        o_r = fs.delta_net_scan(q, k, v, beta)
+        grads_r = fs.delta_rule_backward(q, k, v, beta, do)
+    # q, k, v as slices of one packed [B, L, 3, H, d] projection
+    qkv = torch.stack([q, k, v], dim=2)
+    mode = D.BETA_PER_ELEMENT if beta.dim() == 4 else D.BETA_PER_TOKEN
+    common = dict(beta_mode=mode, q=qkv[:, :, 0], k=qkv[:, :, 1], v=qkv[:, :, 2],
+                  beta=_unaligned(beta), alpha=alpha if gated else None)
+    o = _out_view((B, L, H, d), dtype, [0, 2, 1, 3])
+    D.run("delta_rule", "fwd", D.make_args("delta_rule", dtype, o=o, **common))
+    gqkv = torch.empty(B, L, 3, H, d, dtype=dtype, device="cuda")
+    gbeta = torch.empty_like(beta)
+    galpha = torch.empty(H, B, L, dtype=dtype, device="cuda").permute(1, 2, 0) if gated else None
+    D.run("delta_rule", "bwd",
+          D.make_args("delta_rule", dtype, dO=_transposed(do, [0, 2, 1, 3]), gq=gqkv[:, :, 0],
+                      gk=gqkv[:, :, 1], gv=gqkv[:, :, 2], gbeta=gbeta, galpha=galpha, **common))
+    torch.cuda.synchronize()
+    got = [gqkv[:, :, 0], gqkv[:, :, 1], gqkv[:, :, 2], gbeta] + ([galpha] if gated else [])
+    cmp = _close if form == "chunked" else _exact
+    cmp(o.contiguous(), o_r)
+    for u, r in zip(got, grads_r):
+        cmp(u.contiguous(), r)
+    assert device_errors() == 0
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_flash_attention_desc_blhd_layout(cuda, causal):
+    g = _g(6)
+    B, Hq, Hkv, L, d = 2, 4, 2, 320, 128
+    dtype = torch.bfloat16
+    # the usual projection layout [B, L, H, d], read as [B, H, L, d] views
+    q_blhd = torch.randn(B, L, Hq, d, generator=g).to(dtype).cuda()
+    k_blhd = torch.randn(B, L, Hkv, d, generator=g).to(dtype).cuda()
+    v_blhd = torch.randn(B, L, Hkv, d, generator=g).to(dtype).cuda()
+    do_blhd = torch.randn(B, L, Hq, d, generator=g).to(dtype).cuda()
+    q, k, v, do = (t.transpose(1, 2) for t in (q_blhd, k_blhd, v_blhd, do_blhd))
+    o_r, lse_r = fs.flash_attention(q.contiguous(), k.contiguous(), v.contiguous(), causal=causal,
+                                    return_lse=True)
+    dq_r, dk_r, dv_r = fs.flash_attention_backward(q.contiguous(), k.contiguous(), v.contiguous(),
+                                                   causal, o_r, do.contiguous(), lse_r)
+    lse = torch.empty(B, Hq, L, dtype=torch.float32, device="cuda")
+    o = torch.empty(B, L, Hq, d, dtype=dtype, device="cuda").transpose(1, 2)
+    common = dict(causal=int(causal), num_kv_heads=Hkv, scale=0.0, q=q, k=k, v=v, lse=lse)
+    D.run("flash_attention", "fwd", D.make_args("flash_attention", dtype, o=o, **common))
+    dq = torch.empty(B, L, Hq, d, dtype=dtype, device="cuda").transpose(1, 2)
+    dk = torch.empty(B, L, Hkv, d, dtype=dtype, device="cuda").transpose(1, 2)
+    dv = torch.empty(B, L, Hkv, d, dtype=dtype, device="cuda").transpose(1, 2)
+    D.run("flash_attention", "bwd",
+          D.make_args("flash_attention", dtype, o=o, dO=do, dq=dq, dk=dk, dv=dv, **common))
+    torch.cuda.synchronize()
+    _exact(o.contiguous(), o_r)
+    _exact(lse, lse_r)
+    _close(dq.contiguous(), dq_r)
+    _exact(dk.contiguous(), dk_r)
+    _exact(dv.contiguous(), dv_r)
+    assert device_errors() == 0
