@@ -5,9 +5,10 @@ layouts, slices of packed buffers, broadcasts, unaligned pointers -- for inputs
 and outputs, and compares with the positional entry points run on contiguous
 copies of the same values.  The descriptor form gathers into dense copies and
 runs the same kernels, so results agree bit for bit wherever the kernels are
-deterministic (every path here but the flash-attention and chunked-DeltaNet
-backwards, whose f32 reductions may land in a different order: checked to
-1e-5 norm-relative).  Absolute correctness of those kernels is the oracle
+deterministic (every path here but the flash-attention dQ and the chunked
+DeltaNet, whose f32 reductions may land in a different order before the bf16
+rounding, so a few elements move by one bf16 ulp: checked to 1e-3
+norm-relative, a quarter of bf16's relative resolution).  Absolute correctness of those kernels is the oracle
 parity tests' job.
 """
 import pytest
@@ -29,7 +30,7 @@ def _exact(a, b):
     assert torch.equal(a, b), (a.float() - b.float()).abs().max().item()
 
 
-def _close(a, b, tol=1e-5):
+def _close(a, b, tol=1e-3):
     a, b = a.double(), b.double()
     assert ((a - b).norm() / b.norm().clamp_min(1e-30)).item() <= tol
 
