@@ -278,6 +278,34 @@ class ScanWorkload:
     cpu_what = ("oracle f32 port of the Nx fallbacks (fused_scan.ex:4429-4444, 884-916; "
                 "MinGRU :516-528, 548-581)")
 
+    def ref_cpu_forward(self, budget_s=3.0):
+        """Forward-only tokens/s of the reference's own single-threaded C CPU
+        scan (native/cuda/test_kernels.cu: linear_scan_cpu :166, mingru_scan_cpu
+        :68), built from the reference sources into oracle/_ref; None when that
+        library is absent.  One batch row of the config per repetition."""
+        import numpy as np
+        import oracle as O
+        if O.ref_cpu_lib() is None:
+            return None
+        c = self.cfg
+        self.cpu_step(1)
+        _, a, b, _ = self._cpu
+        h0 = np.zeros((1, c.hidden), np.float32)
+        fn = O.ref_mingru_scan_cpu if c.mingru else O.ref_linear_scan_cpu
+        fn(a, b, h0)
+        t0, reps = time.perf_counter(), 0
+        while True:
+            fn(a, b, h0)
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= budget_s or reps >= 50:
+                break
+        return {"value": reps * c.seq_len / el, "unit": "tokens/s (forward only)", "cores": 1,
+                "sample": "%d repetitions of one batch row [1, %d, %d], %.1f s" % (
+                    reps, c.seq_len, c.hidden, el),
+                "what": "reference native/cuda/test_kernels.cu %s" % (
+                    "mingru_scan_cpu" if c.mingru else "linear_scan_cpu")}
+
 
 class SsmWorkload:
     """Mamba selective scan fwd (with chunk checkpoints) + bwd."""
@@ -867,8 +895,13 @@ def time_cpu(wl, budget_s=12.0):
         el = time.perf_counter() - t0
         if el >= budget_s or reps >= 200:
             break
-    return {"value": tok / el, "unit": "tokens/s", "cores": n, "kind": "port",
-            "sample": "%d repetitions, %.1f s of CPU work: %s" % (reps, el, wl.cpu_what)}
+    out = {"value": tok / el, "unit": "tokens/s", "cores": n, "kind": "port",
+           "sample": "%d repetitions, %.1f s of CPU work: %s" % (reps, el, wl.cpu_what)}
+    if hasattr(wl, "ref_cpu_forward"):
+        ref = wl.ref_cpu_forward()
+        if ref is not None:
+            out["reference_single_thread"] = ref
+    return out
 
 
 # ------------------------------------------------------------------ ours
