@@ -74,8 +74,9 @@ SIGNATURES = {
                                      _i, _i, _i, _i, _f, _vp, _sz, _vp]),
 }
 # descriptor form: every op, both directions, takes (const args*, stream, ws, ws_bytes)
-for _op in ("linear_scan", "mingru", "selective_scan", "delta_rule", "flash_attention"):
-    for _dir in ("fwd", "bwd"):
+for _op in ("linear_scan", "mingru", "selective_scan", "delta_rule", "flash_attention",
+            "native_rec", "laser_attention", "fox_attention"):
+    for _dir in (("fwd",) if _op == "native_rec" else ("fwd", "bwd")):
         SIGNATURES["edb_%s_%s_desc_workspace" % (_op, _dir)] = (_sz, [_vp])
         SIGNATURES["edb_%s_%s_desc" % (_op, _dir)] = (_i, [_vp, _vp, _vp, _sz])
 

@@ -207,8 +207,8 @@ size_t workspace_of(Prepare prepare) {
 // ------------------------------------------------------------ linear / MinGRU
 // The two diagonal scans share their tensor roles: x0 (a or z), x1 (b or c).
 struct ScanIdx {
-    int x0, x1, h0, h, dy, g0, g1, gh0;
-    int B, L, H;
+    int x0 = -1, x1 = -1, h0 = -1, h = -1, dy = -1, g0 = -1, g1 = -1, gh0 = -1;
+    int B = 0, L = 0, H = 0;
 };
 
 template <typename Args>
@@ -241,8 +241,9 @@ int prep_scan(const Args* a, const edb_tensor& x0, const edb_tensor& x1, const e
 
 // ------------------------------------------------------------ selective scan
 struct SsmIdx {
-    int x, dt, A, B, C, y, dy, gx, gdt, gB, gC;
-    int b, L, D, N;
+    int x = -1, dt = -1, A = -1, B = -1, C = -1, y = -1, dy = -1, gx = -1, gdt = -1, gB = -1,
+        gC = -1;
+    int b = 0, L = 0, D = 0, N = 0;
 };
 
 int prep_ssm(const edb_selective_scan_args* a, bool bwd, Plan& p, SsmIdx& ix) {
@@ -278,9 +279,10 @@ int prep_ssm(const edb_selective_scan_args* a, bool bwd, Plan& p, SsmIdx& ix) {
 
 // ------------------------------------------------------------ delta rule
 struct DeltaIdx {
-    int q, k, v, beta, alpha, o, dO, gq, gk, gv, gbeta, galpha;
-    int B, L, H, d;
-    bool gated, bpe;
+    int q = -1, k = -1, v = -1, beta = -1, alpha = -1, o = -1, dO = -1, gq = -1, gk = -1,
+        gv = -1, gbeta = -1, galpha = -1;
+    int B = 0, L = 0, H = 0, d = 0;
+    bool gated = false, bpe = false;
 };
 
 int prep_delta(const edb_delta_rule_args* a, bool bwd, Plan& p, DeltaIdx& ix) {
@@ -318,8 +320,8 @@ int prep_delta(const edb_delta_rule_args* a, bool bwd, Plan& p, DeltaIdx& ix) {
 
 // ------------------------------------------------------------ flash attention
 struct AttnIdx {
-    int q, k, v, o, dO, dq, dk, dv;
-    int B, Hq, Hkv, L, d;
+    int q = -1, k = -1, v = -1, o = -1, dO = -1, dq = -1, dk = -1, dv = -1;
+    int B = 0, Hq = 0, Hkv = 0, L = 0, d = 0;
 };
 
 int prep_attn(const edb_flash_attention_args* a, bool bwd, Plan& p, AttnIdx& ix) {
@@ -593,6 +595,209 @@ extern "C" int edb_flash_attention_bwd_desc(const edb_flash_attention_args* args
                                                   p.ptr(ix.dv), ix.B, ix.Hq, ix.Hkv, ix.L, ix.d,
                                                   args->causal, args->scale, scratch,
                                                   scratch_bytes, stream);
+               },
+               stream, workspace, ws_bytes);
+}
+
+// native-recurrence scans (forward) ----------------------------------------
+extern "C" size_t edb_native_rec_fwd_desc_workspace(const edb_native_rec_args* args) {
+    ScanIdx ix;
+    edb_tensor none = {};
+    return workspace_of([&](Plan& p, size_t& inner) {
+        inner = 0;
+        if (!args) return (int)EDB_ERR_NULL_POINTER;
+        return prep_scan(args, args->x0, args->x1, args->h0, args->h, none, none, none, none,
+                         false, p, ix);
+    });
+}
+extern "C" int edb_native_rec_fwd_desc(const edb_native_rec_args* args, void* stream,
+                                       void* workspace, size_t ws_bytes) {
+    ScanIdx ix;
+    edb_tensor none = {};
+    return run(
+        [&](Plan& p, size_t& inner) {
+            inner = 0;
+            if (!args) return (int)EDB_ERR_NULL_POINTER;
+            return prep_scan(args, args->x0, args->x1, args->h0, args->h, none, none, none, none,
+                             false, p, ix);
+        },
+        [&](Plan& p, void*, size_t) {
+            return edb_native_rec_fwd(args->kind, args->dtype, p.ptr(ix.x0), p.ptr(ix.x1),
+                                      p.ptr(ix.h0), p.ptr(ix.h), ix.B, ix.L, ix.H, stream);
+        },
+        stream, workspace, ws_bytes);
+}
+
+// LASER / FoX attention ----------------------------------------------------
+namespace {
+
+// Shapes shared by the attention variants: q-like [B, Hq, L, d], kv-like
+// [B, Hkv, L, d], per-row [B, Hq, L], per-kv-head [B, Hkv, d].
+struct AttnShapes {
+    long long qs[4], ks[4], bhl[3], bhd[3];
+};
+
+template <typename Args>
+int attn_dims(const Args* a, AttnIdx& x, AttnShapes& s) {
+    if (!a) return EDB_ERR_NULL_POINTER;
+    if (!io_dtype(a->dtype)) return EDB_ERR_BAD_DTYPE;
+    int dq[4], dk[4];
+    if (int st = dims_of(a->q, 4, dq)) return st;
+    if (int st = dims_of(a->k, 4, dk)) return st;
+    x.B = dq[0], x.Hq = dq[1], x.Hkv = dk[1], x.L = dq[2], x.d = dq[3];
+    const long long qs[4] = {dq[0], dq[1], dq[2], dq[3]}, ks[4] = {dq[0], dk[1], dq[2], dq[3]};
+    const long long bhl[3] = {dq[0], dq[1], dq[2]}, bhd[3] = {dq[0], dk[1], dq[3]};
+    for (int i = 0; i < 4; ++i) s.qs[i] = qs[i], s.ks[i] = ks[i];
+    for (int i = 0; i < 3; ++i) s.bhl[i] = bhl[i], s.bhd[i] = bhd[i];
+    return EDB_OK;
+}
+
+struct LaserIdx {
+    AttnIdx a;
+    int vmax = -1;
+};
+
+// fwd reads q, k, v, v_max (optional) and writes o; bwd reads q, k, dO and the
+// residuals, and writes dq, dk, dv.
+int prep_laser(const edb_laser_attention_args* a, bool bwd, Plan& p, LaserIdx& ix) {
+    AttnShapes s;
+    AttnIdx& x = ix.a;
+    if (int st = attn_dims(a, x, s)) return st;
+    if (a->resid == nullptr) return EDB_ERR_NULL_POINTER;
+    const int dt = a->dtype;
+    x.q = p.add(a->q, false, false, dt, 4, s.qs);
+    x.k = p.add(a->k, false, false, dt, 4, s.ks);
+    if (!bwd) {
+        x.v = p.add(a->v, false, false, dt, 4, s.ks);
+        ix.vmax = p.add(a->v_max, false, true, dt, 3, s.bhd);
+        x.o = p.add(a->o, true, false, dt, 4, s.qs);
+    } else {
+        x.dO = p.add(a->dO, false, false, dt, 4, s.qs);
+        x.dq = p.add(a->dq, true, false, dt, 4, s.qs);
+        x.dk = p.add(a->dk, true, false, dt, 4, s.ks);
+        x.dv = p.add(a->dv, true, false, dt, 4, s.ks);
+    }
+    return p.status();
+}
+
+struct FoxIdx {
+    AttnIdx a;
+    int cs = -1, dcs = -1;
+};
+
+int prep_fox(const edb_fox_attention_args* a, bool bwd, Plan& p, FoxIdx& ix) {
+    AttnShapes s;
+    AttnIdx& x = ix.a;
+    if (int st = attn_dims(a, x, s)) return st;
+    if (a->lse == nullptr) return EDB_ERR_NULL_POINTER;
+    const int dt = a->dtype;
+    x.q = p.add(a->q, false, false, dt, 4, s.qs);
+    x.k = p.add(a->k, false, false, dt, 4, s.ks);
+    x.v = p.add(a->v, false, false, dt, 4, s.ks);
+    ix.cs = p.add(a->cs, false, false, EDB_F32, 3, s.bhl);
+    x.o = p.add(a->o, !bwd, false, dt, 4, s.qs);
+    if (bwd) {
+        x.dO = p.add(a->dO, false, false, dt, 4, s.qs);
+        x.dq = p.add(a->dq, true, false, dt, 4, s.qs);
+        x.dk = p.add(a->dk, true, false, dt, 4, s.ks);
+        x.dv = p.add(a->dv, true, false, dt, 4, s.ks);
+        ix.dcs = p.add(a->dcs, true, false, EDB_F32, 3, s.bhl);
+    }
+    return p.status();
+}
+
+}  // namespace
+
+#define PREP_LASER(BWD)                                                                       \
+    [&](Plan& p, size_t& inner) {                                                             \
+        int st = prep_laser(args, BWD, p, ix);                                                \
+        inner = (st == EDB_OK && BWD)                                                         \
+                    ? edb_laser_attention_bwd_workspace(args->dtype, ix.a.B, ix.a.Hq,         \
+                                                        ix.a.Hkv, ix.a.L, ix.a.d)             \
+                    : 0;                                                                      \
+        return st;                                                                            \
+    }
+
+extern "C" size_t edb_laser_attention_fwd_desc_workspace(const edb_laser_attention_args* args) {
+    LaserIdx ix;
+    return workspace_of(PREP_LASER(false));
+}
+extern "C" int edb_laser_attention_fwd_desc(const edb_laser_attention_args* args, void* stream,
+                                            void* workspace, size_t ws_bytes) {
+    LaserIdx ix;
+    return run(PREP_LASER(false),
+               [&](Plan& p, void*, size_t) {
+                   const AttnIdx& x = ix.a;
+                   return edb_laser_attention_fwd(args->dtype, p.ptr(x.q), p.ptr(x.k),
+                                                  p.ptr(x.v), p.ptr(ix.vmax), p.ptr(x.o),
+                                                  args->resid, x.B, x.Hq, x.Hkv, x.L, x.d,
+                                                  args->causal, args->scale, stream);
+               },
+               stream, workspace, ws_bytes);
+}
+extern "C" size_t edb_laser_attention_bwd_desc_workspace(const edb_laser_attention_args* args) {
+    LaserIdx ix;
+    return workspace_of(PREP_LASER(true));
+}
+extern "C" int edb_laser_attention_bwd_desc(const edb_laser_attention_args* args, void* stream,
+                                            void* workspace, size_t ws_bytes) {
+    LaserIdx ix;
+    return run(PREP_LASER(true),
+               [&](Plan& p, void* scratch, size_t scratch_bytes) {
+                   const AttnIdx& x = ix.a;
+                   return edb_laser_attention_bwd(args->dtype, p.ptr(x.q), p.ptr(x.k),
+                                                  p.ptr(x.dO), args->resid, p.ptr(x.dq),
+                                                  p.ptr(x.dk), p.ptr(x.dv), x.B, x.Hq, x.Hkv,
+                                                  x.L, x.d, args->causal, args->scale, scratch,
+                                                  scratch_bytes, stream);
+               },
+               stream, workspace, ws_bytes);
+}
+
+#define PREP_FOX(BWD)                                                                         \
+    [&](Plan& p, size_t& inner) {                                                             \
+        int st = prep_fox(args, BWD, p, ix);                                                  \
+        inner = (st == EDB_OK && BWD)                                                         \
+                    ? edb_fox_attention_bwd_workspace(args->dtype, ix.a.B, ix.a.Hq, ix.a.Hkv, \
+                                                      ix.a.L, ix.a.d)                         \
+                    : 0;                                                                      \
+        return st;                                                                            \
+    }
+
+extern "C" size_t edb_fox_attention_fwd_desc_workspace(const edb_fox_attention_args* args) {
+    FoxIdx ix;
+    return workspace_of(PREP_FOX(false));
+}
+extern "C" int edb_fox_attention_fwd_desc(const edb_fox_attention_args* args, void* stream,
+                                          void* workspace, size_t ws_bytes) {
+    FoxIdx ix;
+    return run(PREP_FOX(false),
+               [&](Plan& p, void*, size_t) {
+                   const AttnIdx& x = ix.a;
+                   return edb_fox_attention_fwd(args->dtype, p.ptr(x.q), p.ptr(x.k), p.ptr(x.v),
+                                                (const float*)p.ptr(ix.cs), p.ptr(x.o),
+                                                args->lse, x.B, x.Hq, x.Hkv, x.L, x.d,
+                                                args->scale, stream);
+               },
+               stream, workspace, ws_bytes);
+}
+extern "C" size_t edb_fox_attention_bwd_desc_workspace(const edb_fox_attention_args* args) {
+    FoxIdx ix;
+    return workspace_of(PREP_FOX(true));
+}
+extern "C" int edb_fox_attention_bwd_desc(const edb_fox_attention_args* args, void* stream,
+                                          void* workspace, size_t ws_bytes) {
+    FoxIdx ix;
+    return run(PREP_FOX(true),
+               [&](Plan& p, void* scratch, size_t scratch_bytes) {
+                   const AttnIdx& x = ix.a;
+                   return edb_fox_attention_bwd(args->dtype, p.ptr(x.q), p.ptr(x.k), p.ptr(x.v),
+                                                (const float*)p.ptr(ix.cs), p.ptr(x.o),
+                                                p.ptr(x.dO), args->lse, p.ptr(x.dq),
+                                                p.ptr(x.dk), p.ptr(x.dv),
+                                                (float*)p.ptr(ix.dcs), x.B, x.Hq, x.Hkv, x.L,
+                                                x.d, args->scale, scratch, scratch_bytes,
+                                                stream);
                },
                stream, workspace, ws_bytes);
 }

@@ -58,9 +58,28 @@ class FlashAttentionArgs(ctypes.Structure):
                 + _t("dO", "dq", "dk", "dv"))
 
 
+class NativeRecArgs(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int), ("kind", ctypes.c_int)] + _t("x0", "x1", "h0", "h")
+
+
+class LaserAttentionArgs(ctypes.Structure):
+    _fields_ = ([("dtype", ctypes.c_int), ("causal", ctypes.c_int), ("scale", ctypes.c_float)]
+                + _t("q", "k", "v", "v_max", "o")
+                + [("resid", ctypes.c_void_p)]
+                + _t("dO", "dq", "dk", "dv"))
+
+
+class FoxAttentionArgs(ctypes.Structure):
+    _fields_ = ([("dtype", ctypes.c_int), ("scale", ctypes.c_float)]
+                + _t("q", "k", "v", "cs", "o")
+                + [("lse", ctypes.c_void_p)]
+                + _t("dO", "dq", "dk", "dv", "dcs"))
+
+
 ARGS = {"linear_scan": LinearScanArgs, "mingru": MinGRUArgs,
         "selective_scan": SelectiveScanArgs, "delta_rule": DeltaRuleArgs,
-        "flash_attention": FlashAttentionArgs}
+        "flash_attention": FlashAttentionArgs, "native_rec": NativeRecArgs,
+        "laser_attention": LaserAttentionArgs, "fox_attention": FoxAttentionArgs}
 
 _DTYPES = {torch.float32: _lib.EDB_F32, torch.bfloat16: _lib.EDB_BF16}
 
@@ -90,7 +109,7 @@ def _ptr(x):
 
 def make_args(op, dtype, **fields):
     """Fill the args struct of `op`: torch tensors become edb_tensor fields, the
-    residual buffers (dt_mean, h_ckpt, s_ckpt, lse) plain pointers, the rest
+    residual buffers (dt_mean, h_ckpt, s_ckpt, lse, resid) plain pointers, the rest
     scalars.  The struct keeps a reference to every tensor it points at, so a
     temporary view's storage is not handed back to the allocator (and reused,
     e.g. as the workspace) while the struct is alive."""

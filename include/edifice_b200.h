@@ -527,6 +527,39 @@ typedef struct {
     edb_tensor dO, dq, dk, dv;
 } edb_flash_attention_args;
 
+/* Native-recurrence scans (edb_native_rec_fwd), forward only (their backwards
+ * are the linear-scan / MinGRU backwards on the activated values): kind is
+ * EDB_NATIVE_*; x0, x1, h [batch, seq_len, hidden], h0 [batch, hidden] optional. */
+typedef struct {
+    int dtype;
+    int kind;
+    edb_tensor x0, x1, h0, h;
+} edb_native_rec_args;
+
+/* LASER attention (edb_laser_attention_fwd / _bwd): q, o, dO, dq as flash;
+ * k, v, dk, dv [batch, kv_heads, seq_len, head_dim]; v_max [batch, kv_heads,
+ * head_dim] optional; resid: dense, edb_laser_attention_resid_bytes() bytes,
+ * 256-byte aligned, written by fwd and read by bwd. */
+typedef struct {
+    int dtype;
+    int causal;
+    float scale;
+    edb_tensor q, k, v, v_max, o;
+    void* resid;
+    edb_tensor dO, dq, dk, dv;
+} edb_laser_attention_args;
+
+/* FoX attention (edb_fox_attention_fwd / _bwd), causal: q, k, v, o, dO, dq,
+ * dk, dv as flash; cs, dcs [batch, q_heads, seq_len] f32; lse: dense f32
+ * [batch, q_heads, seq_len], required (written by fwd, read by bwd). */
+typedef struct {
+    int dtype;
+    float scale;
+    edb_tensor q, k, v, cs, o;
+    float* lse;
+    edb_tensor dO, dq, dk, dv, dcs;
+} edb_fox_attention_args;
+
 size_t edb_linear_scan_fwd_desc_workspace(const edb_linear_scan_args* args);
 int edb_linear_scan_fwd_desc(const edb_linear_scan_args* args, void* stream, void* workspace,
                              size_t workspace_bytes);
@@ -561,6 +594,24 @@ int edb_flash_attention_fwd_desc(const edb_flash_attention_args* args, void* str
 size_t edb_flash_attention_bwd_desc_workspace(const edb_flash_attention_args* args);
 int edb_flash_attention_bwd_desc(const edb_flash_attention_args* args, void* stream,
                                  void* workspace, size_t workspace_bytes);
+
+size_t edb_native_rec_fwd_desc_workspace(const edb_native_rec_args* args);
+int edb_native_rec_fwd_desc(const edb_native_rec_args* args, void* stream, void* workspace,
+                            size_t workspace_bytes);
+
+size_t edb_laser_attention_fwd_desc_workspace(const edb_laser_attention_args* args);
+int edb_laser_attention_fwd_desc(const edb_laser_attention_args* args, void* stream,
+                                 void* workspace, size_t workspace_bytes);
+size_t edb_laser_attention_bwd_desc_workspace(const edb_laser_attention_args* args);
+int edb_laser_attention_bwd_desc(const edb_laser_attention_args* args, void* stream,
+                                 void* workspace, size_t workspace_bytes);
+
+size_t edb_fox_attention_fwd_desc_workspace(const edb_fox_attention_args* args);
+int edb_fox_attention_fwd_desc(const edb_fox_attention_args* args, void* stream,
+                               void* workspace, size_t workspace_bytes);
+size_t edb_fox_attention_bwd_desc_workspace(const edb_fox_attention_args* args);
+int edb_fox_attention_bwd_desc(const edb_fox_attention_args* args, void* stream,
+                               void* workspace, size_t workspace_bytes);
 
 #ifdef __cplusplus
 }

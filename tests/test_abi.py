@@ -158,3 +158,30 @@ def test_descriptor_validation_before_any_gpu_work():
     f.q = f.o = dense(shape=(1, 4, 64, 64))
     f.k = f.v = dense(shape=(1, 2, 64, 64))
     assert st("flash_attention", "fwd", f) == 1001
+
+
+def test_descriptor_attention_variants_need_their_residuals():
+    from edifice_b200 import descriptor as D
+    lib = edifice_b200.load()
+    base = 1 << 24
+    q = D.tensor(base, _lib.EDB_BF16, (1, 4, 64, 64))
+    kv = D.tensor(base, _lib.EDB_BF16, (1, 2, 64, 64))
+    la = D.make_args("laser_attention", _lib.EDB_BF16, causal=1)
+    la.q = la.o = q
+    la.k = la.v = kv
+    assert lib.edb_laser_attention_fwd_desc(ctypes.byref(la), None, None, 0) == 1000  # resid
+    la.resid = base
+    la.v_max = D.tensor(base, _lib.EDB_BF16, (1, 2, 65))
+    assert lib.edb_laser_attention_fwd_desc(ctypes.byref(la), None, None, 0) == 1001
+    fx = D.make_args("fox_attention", _lib.EDB_BF16)
+    fx.q = fx.o = q
+    fx.k = fx.v = kv
+    fx.cs = D.tensor(base, _lib.EDB_F32, (1, 4, 64))
+    assert lib.edb_fox_attention_fwd_desc(ctypes.byref(fx), None, None, 0) == 1000   # lse
+    fx.lse = base
+    fx.cs = D.tensor(base, _lib.EDB_BF16, (1, 4, 64))
+    assert lib.edb_fox_attention_fwd_desc(ctypes.byref(fx), None, None, 0) == 1002   # cs is f32
+    nr = D.make_args("native_rec", _lib.EDB_F32, kind=0)
+    nr.x0 = nr.x1 = D.tensor(base, _lib.EDB_F32, (2, 8, 16))
+    nr.h = D.tensor(base, _lib.EDB_F32, (2, 8, 16), (128, 1, 8))
+    assert lib.edb_native_rec_fwd_desc_workspace(ctypes.byref(nr)) == 1024

@@ -236,3 +236,76 @@ def test_flash_attention_desc_blhd_layout(cuda, causal):
     _exact(dk.contiguous(), dk_r)
     _exact(dv.contiguous(), dv_r)
     assert device_errors() == 0
+
+
+@pytest.mark.parametrize("kind", [0, 1, 2])
+def test_native_rec_desc_strided(cuda, kind):
+    g = _g(7)
+    B, L, H = 2, 257, 192
+    x0 = torch.randn(B, L, H, generator=g).bfloat16().cuda()
+    x1 = torch.randn(B, L, H, generator=g).bfloat16().cuda()
+    h0 = torch.randn(B, H, generator=g).bfloat16().cuda()
+    ref = [fs.elu_gru, fs.real_gru, fs.diag_linear][kind](x0, x1, h0)
+    h = _out_view((B, L, H), torch.bfloat16, [1, 0, 2])
+    D.run("native_rec", "fwd", D.make_args("native_rec", torch.bfloat16, kind=kind,
+                                           x0=_transposed(x0, [2, 1, 0]), x1=_unaligned(x1),
+                                           h0=_transposed(h0, [1, 0]), h=h))
+    torch.cuda.synchronize()
+    _exact(h.contiguous(), ref)
+
+
+def _attn_blhd(B, Hq, Hkv, L, d, seed):
+    g = _g(seed)
+    mk = lambda h: torch.randn(B, L, h, d, generator=g).bfloat16().cuda().transpose(1, 2)
+    return mk(Hq), mk(Hkv), mk(Hkv), mk(Hq)
+
+
+def test_laser_attention_desc_blhd_layout(cuda):
+    B, Hq, Hkv, L, d = 1, 4, 2, 256, 128
+    q, k, v, do = _attn_blhd(B, Hq, Hkv, L, d, 8)
+    qc, kc, vc, doc = (t.contiguous() for t in (q, k, v, do))
+    o_r, resid_r = fs.laser_attention(qc, kc, vc, causal=True, return_resid=True)
+    dq_r, dk_r, dv_r = fs.laser_attention_backward(qc, kc, vc, doc, resid_r, causal=True)
+    resid = torch.empty_like(resid_r)
+    o = torch.empty(B, L, Hq, d, dtype=torch.bfloat16, device="cuda").transpose(1, 2)
+    common = dict(causal=1, scale=0.0, q=q, k=k, resid=resid)
+    D.run("laser_attention", "fwd",
+          D.make_args("laser_attention", torch.bfloat16, v=v, o=o, **common))
+    dq = torch.empty(B, L, Hq, d, dtype=torch.bfloat16, device="cuda").transpose(1, 2)
+    dk, dv = torch.empty_like(kc), _out_view((B, Hkv, L, d), torch.bfloat16, [0, 2, 1, 3])
+    D.run("laser_attention", "bwd",
+          D.make_args("laser_attention", torch.bfloat16, dO=do, dq=dq, dk=dk, dv=dv, **common))
+    torch.cuda.synchronize()
+    _exact(o.contiguous(), o_r)
+    _close(dq.contiguous(), dq_r)
+    _exact(dk, dk_r)
+    _exact(dv.contiguous(), dv_r)
+    assert device_errors() == 0
+
+
+def test_fox_attention_desc_blhd_layout(cuda):
+    B, Hq, Hkv, L, d = 1, 4, 2, 192, 64
+    q, k, v, do = _attn_blhd(B, Hq, Hkv, L, d, 9)
+    qc, kc, vc, doc = (t.contiguous() for t in (q, k, v, do))
+    g = _g(10)
+    cs = torch.cumsum(torch.nn.functional.logsigmoid(torch.randn(B, L, Hq, generator=g)), 1)
+    cs = cs.cuda().transpose(1, 2)                       # [B, Hq, L] view of [B, L, Hq]
+    o_r, lse_r = fs.fox_attention(qc, kc, vc, cs.contiguous(), return_lse=True)
+    dq_r, dk_r, dv_r, dcs_r = fs.fox_attention_backward(qc, kc, vc, cs.contiguous(), o_r, doc,
+                                                        lse_r)
+    lse = torch.empty_like(lse_r)
+    o = torch.empty(B, L, Hq, d, dtype=torch.bfloat16, device="cuda").transpose(1, 2)
+    common = dict(scale=0.0, q=q, k=k, v=v, cs=cs, lse=lse)
+    D.run("fox_attention", "fwd", D.make_args("fox_attention", torch.bfloat16, o=o, **common))
+    dq = torch.empty(B, L, Hq, d, dtype=torch.bfloat16, device="cuda").transpose(1, 2)
+    dk, dv = torch.empty_like(kc), torch.empty_like(vc)
+    dcs = torch.empty(B, L, Hq, dtype=torch.float32, device="cuda").transpose(1, 2)
+    D.run("fox_attention", "bwd",
+          D.make_args("fox_attention", torch.bfloat16, o=o, dO=do, dq=dq, dk=dk, dv=dv,
+                      dcs=dcs, **common))
+    torch.cuda.synchronize()
+    _exact(o.contiguous(), o_r)
+    _exact(lse, lse_r)
+    for u, r in ((dq, dq_r), (dk, dk_r), (dv, dv_r), (dcs, dcs_r)):
+        _close(u.contiguous(), r)
+    assert device_errors() == 0
