@@ -25,6 +25,7 @@ SHAPES = [
     (3, 1000, 96),   # f32: 3 full blocks; bf16: partial channel block
     (2, 130, 200),   # partial channel block, partial tile
     (1, 4096, 256),  # long sequence
+    (40, 64, 512),   # >= 2 CTAs per SM of 128-byte channel blocks (the wide-block path)
 ]
 
 
