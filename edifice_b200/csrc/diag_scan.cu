@@ -12,14 +12,18 @@
 //       linear fwd (a, b)          MinGRU fwd (1-z, z c)
 //       linear bwd (a, a dY)       MinGRU bwd (1-z, (1-z) dY)    [s = dh_acc]
 //     so one engine serves all four; the backward runs time in reverse.
-//   * A CTA owns one 128-byte channel block (64 bf16 / 32 f32 channels) of one
-//     batch row and streams the whole sequence through shared memory in tiles of
-//     ROWS time steps, staged by 2D TMA loads in a STAGES-deep mbarrier ring.
+//   * A CTA owns one channel block of one batch row -- 256 bytes (128 bf16 / 64
+//     f32 channels, 512 threads) when that still gives at least 96 CTAs, else
+//     128 bytes (256 threads) -- and streams the whole sequence through shared
+//     memory in tiles of ROWS time steps, staged by 2D TMA loads in a
+//     STAGES-deep mbarrier ring.  The wide blocks read two full 128-byte lines
+//     per row, which DRAM serves measurably better than one (config 1: 88 % /
+//     93 % of the measured copy bandwidth against 77 % / 81 %); narrower 64-byte
+//     blocks measured slower still.
 //   * Inside a tile: thread (seg, g) owns the 16-byte chunk g (8 bf16 channels)
-//     of ROWS/32 consecutive steps.  Per-thread sequential composition, a 2-step
-//     warp shuffle scan over the 4 segments a warp holds, and a cross-warp
-//     prefix done by one thread per channel that also carries the state from
-//     tile to tile.  Inputs stay in registers between the composition and the
+//     of ROWS/32 consecutive steps.  Per-thread sequential composition, a warp
+//     shuffle scan over the segments a warp holds, and a cross-warp prefix done
+//     by one thread per channel that also carries the state from tile to tile.  Inputs stay in registers between the composition and the
 //     apply pass, so every input byte is read from HBM once and every output
 //     byte written once (16-byte stores, 128 contiguous bytes per 8 lanes).
 //   * The backward needs h_{t-1}: its tile of the forward output is loaded by
@@ -31,8 +35,6 @@
 #include "edb_common.cuh"
 
 namespace {
-
-constexpr int kThreads = 256;
 
 // OP_ELUGRU / OP_REALGRU / OP_DIAGLIN: the native-recurrence scans
 // (lib/edifice/recurrent/native_recurrence.ex:125-230), forward only, with the
@@ -118,28 +120,33 @@ struct ScanMaps {
 };
 
 // NIN inputs:  fwd: [x0, x1]   bwd: [x0, dY, h (shifted -1)] (+ c for MinGRU)
-template <typename T, int OP, bool BWD, int ROWS, int STAGES>
-__global__ void __launch_bounds__(kThreads, 2)
+// CW: 16-byte chunks per channel-block row (8: 128-byte blocks, 256 threads;
+// 16: 256-byte blocks, 512 threads).
+template <typename T, int OP, bool BWD, int ROWS, int STAGES, int CW>
+__global__ void __launch_bounds__(32 * CW, CW >= 16 ? 1 : 2)
     diag_scan_tma_kernel(const __grid_constant__ ScanMaps maps, const T* __restrict__ h0,
                          T* __restrict__ out0, T* __restrict__ out1, T* __restrict__ gh0, int L,
                          int H, unsigned* err) {
     using V = Vec16<T>;
     constexpr int VEC = V::N;
-    constexpr int NCH = 8 * VEC;  // channels per CTA (128 bytes)
+    constexpr int NW = CW;             // warps per CTA (32 segments of CW threads)
+    constexpr int RB = 16 * CW;        // bytes per channel-block row
+    constexpr int NCH = CW * VEC;      // channels per CTA
     constexpr int RPS = ROWS / 32;
     constexpr int NIN = BWD ? (OP == OP_MINGRU ? 4 : 3) : 2;
-    constexpr int TILE = ROWS * 128;
+    constexpr int TILE = ROWS * RB;
+    constexpr int SPW = 32 / CW;       // segments per warp
 
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* stage_base = smem;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * NIN * TILE);
     float* aggA = reinterpret_cast<float*>(full + STAGES);
-    float* aggB = aggA + 8 * NCH;
-    float* cinw = aggB + 8 * NCH;
-    int* s_abort = reinterpret_cast<int*>(cinw + 8 * NCH);
+    float* aggB = aggA + NW * NCH;
+    float* cinw = aggB + NW * NCH;
+    int* s_abort = reinterpret_cast<int*>(cinw + NW * NCH);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = tid & 7, seg = tid >> 3;
+    const int g = tid % CW, seg = tid / CW;
     const int cb = blockIdx.x, b = blockIdx.y;
     const int ch0 = cb * NCH + g * VEC;  // first channel of this thread
     const bool ch_ok = ch0 < H;
@@ -201,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int r = BWD ? ROWS - 1 - p : p;      // physical row in the tile
 #pragma unroll
             for (int k = 0; k < NIN; ++k)
-                rin[k][j] = *reinterpret_cast<const uint4*>(sb + k * TILE + r * 128 + g * 16);
+                rin[k][j] = *reinterpret_cast<const uint4*>(sb + k * TILE + r * RB + g * 16);
         }
 
         // ---- per-thread composition over its RPS steps
@@ -229,9 +236,9 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
         }
 
-        // ---- warp scan over the 4 segments of this warp (lanes 8 apart)
+        // ---- warp scan over the SPW segments of this warp (lanes CW apart)
 #pragma unroll
-        for (int off = 8; off <= 16; off <<= 1) {
+        for (int off = CW; off <= 16; off <<= 1) {
 #pragma unroll
             for (int c = 0; c < VEC; ++c) {
                 const float Ap = __shfl_up_sync(0xffffffffu, A[c], off);
@@ -246,14 +253,14 @@ __global__ void __launch_bounds__(kThreads, 2)
         float Ae[VEC], Be[VEC];
 #pragma unroll
         for (int c = 0; c < VEC; ++c) {
-            Ae[c] = __shfl_up_sync(0xffffffffu, A[c], 8);
-            Be[c] = __shfl_up_sync(0xffffffffu, Bc[c], 8);
-            if (lane < 8) {
+            Ae[c] = __shfl_up_sync(0xffffffffu, A[c], CW);
+            Be[c] = __shfl_up_sync(0xffffffffu, Bc[c], CW);
+            if (lane < CW) {
                 Ae[c] = 1.0f;
                 Be[c] = 0.0f;
             }
         }
-        if ((lane >> 3) == 3) {
+        if (lane / CW == SPW - 1) {
 #pragma unroll
             for (int c = 0; c < VEC; ++c) {
                 aggA[warp * NCH + g * VEC + c] = A[c];
@@ -272,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (tid < NCH) {
             float st = carry;
 #pragma unroll
-            for (int w = 0; w < 8; ++w) {
+            for (int w = 0; w < NW; ++w) {
                 cinw[w * NCH + tid] = st;
                 st = fmaf(aggA[w * NCH + tid], st, aggB[w * NCH + tid]);
             }
@@ -393,11 +400,11 @@ __global__ void diag_scan_simple_kernel(const T* __restrict__ x0p, const T* __re
 }
 
 // ---------------------------------------------------------------- launch
-template <typename T, int OP, bool BWD, int ROWS, int STAGES>
+template <typename T, int OP, bool BWD, int ROWS, int STAGES, int CW>
 size_t tma_smem_bytes() {
     constexpr int NIN = BWD ? (OP == OP_MINGRU ? 4 : 3) : 2;
-    constexpr int NCH = 8 * Vec16<T>::N;
-    return (size_t)STAGES * NIN * ROWS * 128 + STAGES * 8 + 3 * 8 * NCH * 4 + 16;
+    constexpr int NCH = CW * Vec16<T>::N;
+    return (size_t)STAGES * NIN * ROWS * 16 * CW + STAGES * 8 + 3 * CW * NCH * 4 + 16;
 }
 
 template <typename T>
@@ -412,33 +419,46 @@ CUtensorMapDataType tmap_dtype<__nv_bfloat16>() {
 }
 
 template <typename T>
-int make_scan_map(CUtensorMap* m, const void* p, int B, int L, int H, int rows) {
+int make_scan_map(CUtensorMap* m, const void* p, int B, int L, int H, int rows, int row_bytes) {
     const cuuint64_t dims[2] = {(cuuint64_t)H, (cuuint64_t)B * (cuuint64_t)L};
     const cuuint64_t strides[1] = {(cuuint64_t)H * sizeof(T)};
-    const cuuint32_t box[2] = {(cuuint32_t)(128 / sizeof(T)), (cuuint32_t)rows};
+    const cuuint32_t box[2] = {(cuuint32_t)(row_bytes / sizeof(T)), (cuuint32_t)rows};
     CUresult r = edb::encode_tiled(m, tmap_dtype<T>(), 2, const_cast<void*>(p), dims, strides,
                                    box, CU_TENSOR_MAP_SWIZZLE_NONE);
     return r == CUDA_SUCCESS ? EDB_OK : EDB_ERR_UNSUPPORTED;
 }
 
-template <typename T, int OP, bool BWD, int ROWS, int STAGES>
-int launch_tma(const void* const* ins, int nin, const T* h0, T* o0, T* o1, T* gh0, int B, int L,
-               int H, cudaStream_t stream) {
+template <typename T, int OP, bool BWD, int ROWS, int STAGES, int CW>
+int launch_tma_cw(const void* const* ins, int nin, const T* h0, T* o0, T* o1, T* gh0, int B,
+                  int L, int H, cudaStream_t stream) {
     ScanMaps maps;
     for (int k = 0; k < nin; ++k) {
-        int st = make_scan_map<T>(&maps.m[k], ins[k], B, L, H, ROWS);
+        int st = make_scan_map<T>(&maps.m[k], ins[k], B, L, H, ROWS, 16 * CW);
         if (st) return st;
     }
     for (int k = nin; k < 4; ++k) maps.m[k] = maps.m[0];
-    auto kern = diag_scan_tma_kernel<T, OP, BWD, ROWS, STAGES>;
-    const size_t smem = tma_smem_bytes<T, OP, BWD, ROWS, STAGES>();
+    auto kern = diag_scan_tma_kernel<T, OP, BWD, ROWS, STAGES, CW>;
+    const size_t smem = tma_smem_bytes<T, OP, BWD, ROWS, STAGES, CW>();
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return (int)e;
-    constexpr int NCH = 8 * Vec16<T>::N;
+    constexpr int NCH = CW * Vec16<T>::N;
     dim3 grid((H + NCH - 1) / NCH, B);
-    kern<<<grid, kThreads, smem, stream>>>(maps, h0, o0, o1, gh0, L, H, edb::device_error_word());
+    kern<<<grid, 32 * CW, smem, stream>>>(maps, h0, o0, o1, gh0, L, H, edb::device_error_word());
     return edb::status_from_cuda(cudaGetLastError());
+}
+
+// 256-byte channel blocks (one 512-thread CTA per SM) when there are enough of
+// them to cover most SMs and the ring fits; 128-byte blocks otherwise.
+template <typename T, int OP, bool BWD, int ROWS, int STAGES>
+int launch_tma(const void* const* ins, int nin, const T* h0, T* o0, T* o1, T* gh0, int B, int L,
+               int H, cudaStream_t stream) {
+    constexpr int NCH16 = 16 * Vec16<T>::N;
+    if ((long long)B * ((H + NCH16 - 1) / NCH16) >= 96 &&
+        tma_smem_bytes<T, OP, BWD, ROWS, STAGES, 16>() <= 227 * 1024)
+        return launch_tma_cw<T, OP, BWD, ROWS, STAGES, 16>(ins, nin, h0, o0, o1, gh0, B, L, H,
+                                                           stream);
+    return launch_tma_cw<T, OP, BWD, ROWS, STAGES, 8>(ins, nin, h0, o0, o1, gh0, B, L, H, stream);
 }
 
 template <typename T, int OP, bool BWD>
