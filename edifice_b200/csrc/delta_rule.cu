@@ -248,7 +248,7 @@ static __device__ __forceinline__ int halving_base(int lane, int nv) {
 template <int CPL, int LPR>
 struct RowsBwdSmem {
     static constexpr int NT = 32 * LPR, NW = LPR;
-    static constexpr int ROUNDS = LPR == 4 ? 3 : 2;       // halving rounds (rows per warp)
+    static constexpr int ROUNDS = LPR == 4 ? 3 : LPR == 8 ? 2 : 1;  // halving rounds
     static constexpr int SP = CPL + 4, RP = LPR * SP, W = LPR * CPL;  // W: columns per CTA
     // per warp and token: [gq | gk][LPR slices][CPL + 1], the halves LPR (CPL + 1) + 8
     // apart, then galpha and a per-token gbeta: the skews put the 32 lanes' stores of one
@@ -257,7 +257,7 @@ struct RowsBwdSmem {
     static constexpr int RED = 2 * HALF + 2;
     // tokens per cross-warp reduction, and 2 RB slots: a token's gq arrives one step
     // after its gk
-    static constexpr int RB = LPR == 4 ? 8 : 4, NSLOT = 2 * RB;
+    static constexpr int RB = LPR == 4 ? 8 : LPR == 8 ? 4 : 2, NSLOT = 2 * RB;
     static constexpr size_t floats = (size_t)2 * SB * RP + 5 * SB * kRowsPerCta + SB +
                                      (size_t)NSLOT * NW * RED;
     static constexpr size_t bytes = floats * sizeof(float);
@@ -580,7 +580,7 @@ size_t rows_bwd_ws_bytes(int B, int L, int H, int d) {
     const int nz = (d + kRowsPerCta - 1) / kRowsPerCta;
     const size_t rows = (size_t)B * L * H;
     const size_t sc = d <= 32 ? rows_bwd_scratch_bytes<8, 4>(B, H, d)
-                              : rows_bwd_scratch_bytes<16, 8>(B, H, d);
+                              : rows_bwd_scratch_bytes<8, 16>(B, H, d);
     return a256(sc) + a256((size_t)nz * rows * 2 * d * sizeof(float)) +
            a256((size_t)nz * rows * 2 * sizeof(float));
 }
@@ -625,9 +625,9 @@ int launch_bwd_rows(const void* q, const void* k, const void* v, const void* bet
                      : launch_bwd_rows_t<T, 8, 4, false>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk,
                                                       gv, gbeta, galpha, B, L, H, d, beta_scalar,
                                                       st);
-    return alpha ? launch_bwd_rows_t<T, 16, 8, true>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk, gv,
+    return alpha ? launch_bwd_rows_t<T, 8, 16, true>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk, gv,
                                                   gbeta, galpha, B, L, H, d, beta_scalar, st)
-                 : launch_bwd_rows_t<T, 16, 8, false>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk,
+                 : launch_bwd_rows_t<T, 8, 16, false>(q, k, v, beta, alpha, dO, ckpt, ws, gq, gk,
                                                    gv, gbeta, galpha, B, L, H, d, beta_scalar,
                                                    st);
 }
