@@ -411,6 +411,20 @@ class SsmModelWorkload(SsmWorkload):
 
     launches_per_step = 5  # dt mean, fwd, bwd, dB/dC reduce, gdt mean term
 
+    def kernels(self):
+        # With the model's fixed A = -(1..N) the decays are the powers of exp(-dt): one
+        # ex2 per (t, d), not per (t, d, n), so the SFU no longer bounds the path; it is
+        # issue-bound, and HBM is the roofline it is reported against.
+        return {"fwd": ("hbm", self.cfg.bytes_fwd()), "bwd": ("hbm", self.cfg.bytes_bwd())}
+
+    def extra(self, fwd_ms, bwd_ms):
+        c = self.cfg
+        return {"exps_per_s_fwd_algorithmic": round(c.exps_fwd() / (fwd_ms / 1e3) / 1e9, 1),
+                "note": "fixed A = -(1..N): exp(dt A[d,n]) = r^(n+1), r = exp(-dt), one ex2 "
+                        "and NS/2 packed multiplies per (t, d) in the forward, the backward's "
+                        "rebuild and its recompute; issue-bound (forward: a few instructions "
+                        "per (t, d, n)), HBM is the reported roofline"}
+
     def step(self, ev=None):
         from edifice_b200 import fused_scan as fs
         if ev:

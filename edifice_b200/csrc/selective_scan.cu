@@ -41,6 +41,22 @@ static __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+static __device__ __forceinline__ float2 ex2_2(float2 x) { return make_float2(ex2(x.x), ex2(x.y)); }
+
+// Decays of the model's fixed A[d, n] = -(n + 1) (lib/edifice/ssm/common.ex:409):
+// exp(-dtc (n + 1)) = r^(n+1), r = exp(-dtc).  pw starts at (r, r^2) for the pair
+// n = (0, 1); next_power returns the current pair and steps it by r^2.
+static __device__ __forceinline__ void fixa_powers(float dtc, float2& pw, float2& rr2) {
+    const float r = ex2(-dtc * 1.4426950408889634f);
+    pw = make_float2(r, r * r);
+    rr2 = make_float2(r * r, r * r);
+}
+static __device__ __forceinline__ float2 next_power(float2& pw, float2 rr2) {
+    const float2 a = pw;
+    pw = mul2(pw, rr2);
+    return a;
+}
+
 // chunk / sub-chunk lengths per padded state count: TS*NS = 64 state values in
 // registers per sub-chunk, CK/TS = 8 sub-checkpoints (8*NS floats) in smem.
 template <int NS>
@@ -360,7 +376,10 @@ static __device__ __forceinline__ void stage_rows(unsigned char* dst, const T* s
 }
 
 // grid (ceil(D/128), B), block 128; two x/dt tiles of TB steps in flight.
-template <typename T, int NS, bool STATES_ONLY, bool MODEL>
+// FIXA (model semantics with A = NULL): A[d, n] = -(n + 1), so the decays of one
+// (t, d) are the powers r^(n+1) of r = exp(-dtc): one ex2 and NS/2 packed
+// multiplies instead of NS ex2 (relative error ~(n+1) ulp of r, ~4e-6 at n = 15).
+template <typename T, int NS, bool STATES_ONLY, bool MODEL, bool FIXA = false>
 __global__ void __launch_bounds__(kThreads)
     ssm_fwd_staged_kernel(const T* __restrict__ x, const T* __restrict__ dt,
                           const T* __restrict__ A, const T* __restrict__ Bm,
@@ -454,6 +473,8 @@ __global__ void __launch_bounds__(kThreads)
                 const float dti = MODEL ? sDm[(k & 1) * TB + tt] : dtc;
                 const float2 dtc2 = dup2(dtc), dtx2 = dup2(dti * ldf(xs + tt * kThreads));
                 float2 acc = dup2(0.0f);
+                float2 pw, rr2;
+                if (FIXA) fixa_powers(dtc, pw, rr2);
 #pragma unroll
                 for (int p = 0; p < NP; p += 2) {
                     const float4 b4 = *reinterpret_cast<const float4*>(bk + tt * NS + 2 * p);
@@ -462,8 +483,7 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
                         const float2 bq = q ? make_float2(b4.z, b4.w) : make_float2(b4.x, b4.y);
-                        const float2 arg = mul2(dtc2, A2[p + q]);
-                        const float2 a = make_float2(ex2(arg.x), ex2(arg.y));
+                        const float2 a = FIXA ? next_power(pw, rr2) : ex2_2(mul2(dtc2, A2[p + q]));
                         h[p + q] = fma2(a, h[p + q], mul2(dtx2, bq));
                         if (!STATES_ONLY) {
                             const float2 cq = q ? make_float2(c4.z, c4.w) : make_float2(c4.x, c4.y);
@@ -487,7 +507,7 @@ constexpr size_t fwd_staged_smem() {
 
 // grid (ceil(D/128), B), block 128: ssm_bwd_kernel with the chunk's x, dt, dy
 // rows staged in shared memory (one chunk at a time; two CTAs share an SM).
-template <typename T, int NS, bool MODEL>
+template <typename T, int NS, bool MODEL, bool FIXA = false>
 __global__ void __launch_bounds__(kThreads)
     ssm_bwd_staged_kernel(const T* __restrict__ x, const T* __restrict__ dt,
                           const T* __restrict__ A, const T* __restrict__ Bm,
@@ -589,14 +609,15 @@ __global__ void __launch_bounds__(kThreads)
             const float dtc = fminf(fmaxf(ldf(sdt + tt * kThreads), dt_min), dt_max);
             const float2 dtc2 = dup2(dtc),
                          dtx2 = dup2((MODEL ? sDm[tt] : dtc) * ldf(sx + tt * kThreads));
+            float2 pw, rr2;
+            if (FIXA) fixa_powers(dtc, pw, rr2);
 #pragma unroll
             for (int p = 0; p < NP; p += 2) {
                 const float4 b4 = *reinterpret_cast<const float4*>(sB + tt * NS + 2 * p);
 #pragma unroll
                 for (int q = 0; q < 2; ++q) {
                     const float2 bq = q ? make_float2(b4.z, b4.w) : make_float2(b4.x, b4.y);
-                    const float2 arg = mul2(dtc2, A2[p + q]);
-                    const float2 a = make_float2(ex2(arg.x), ex2(arg.y));
+                    const float2 a = FIXA ? next_power(pw, rr2) : ex2_2(mul2(dtc2, A2[p + q]));
                     h[p + q] = fma2(a, h[p + q], mul2(dtx2, bq));
                 }
             }
@@ -616,14 +637,16 @@ __global__ void __launch_bounds__(kThreads)
                 const float dtc = fminf(fmaxf(ldf(sdt + tt * kThreads), dt_min), dt_max);
                 const float2 dtc2 = dup2(dtc),
                              dtx2 = dup2((MODEL ? sDm[tt] : dtc) * ldf(sx + tt * kThreads));
+                float2 pw, rr2;
+                if (FIXA) fixa_powers(dtc, pw, rr2);
 #pragma unroll
                 for (int p = 0; p < NP; p += 2) {
                     const float4 b4 = *reinterpret_cast<const float4*>(sB + tt * NS + 2 * p);
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
                         const float2 bq = q ? make_float2(b4.z, b4.w) : make_float2(b4.x, b4.y);
-                        const float2 arg = mul2(dtc2, A2[p + q]);
-                        as[j][p + q] = make_float2(ex2(arg.x), ex2(arg.y));
+                        as[j][p + q] =
+                            FIXA ? next_power(pw, rr2) : ex2_2(mul2(dtc2, A2[p + q]));
                         h[p + q] = fma2(as[j][p + q], h[p + q], mul2(dtx2, bq));
                         hs[j][p + q] = h[p + q];
                     }
@@ -803,6 +826,9 @@ int launch_fwd(const void* x, const void* dt, const void* A, const void* Bm, con
         constexpr size_t sm = fwd_staged_smem<T, NS>();
         auto kern = states_only ? ssm_fwd_staged_kernel<T, NS, true, MODEL>
                                 : ssm_fwd_staged_kernel<T, NS, false, MODEL>;
+        if (MODEL && A == nullptr)  // the model's fixed A: decays as powers
+            kern = states_only ? ssm_fwd_staged_kernel<T, NS, true, MODEL, MODEL>
+                               : ssm_fwd_staged_kernel<T, NS, false, MODEL, MODEL>;
         cudaError_t ea =
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
         if (ea != cudaSuccess) return (int)ea;
@@ -826,10 +852,12 @@ int launch_bwd(const void* x, const void* dt, const void* A, const void* Bm, con
     if (D % StageGeom<T>::EPC == 0 && edb::aligned16(x) && edb::aligned16(dt) &&
         edb::aligned16(dy)) {
         constexpr size_t sm = bwd_staged_smem<T, NS>();
-        cudaError_t ea = cudaFuncSetAttribute(ssm_bwd_staged_kernel<T, NS, MODEL>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        auto kern = ssm_bwd_staged_kernel<T, NS, MODEL>;
+        if (MODEL && A == nullptr) kern = ssm_bwd_staged_kernel<T, NS, MODEL, MODEL>;
+        cudaError_t ea =
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
         if (ea != cudaSuccess) return (int)ea;
-        ssm_bwd_staged_kernel<T, NS, MODEL><<<grid, kThreads, sm, st>>>(
+        kern<<<grid, kThreads, sm, st>>>(
             (const T*)x, (const T*)dt, (const T*)A, (const T*)Bm, (const T*)Cm, (const T*)dy,
             ckpt, dtm, (T*)gx, (T*)gdt, gpart, B, L, D, N, lo, hi);
     } else {

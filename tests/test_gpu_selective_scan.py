@@ -209,19 +209,22 @@ def test_model_semantics_parity(cuda, dtype, case, use_ckpt, given_a):
 
 def test_model_semantics_fixed_a_is_the_default(cuda):
     """A = None and the explicit fixed -(1..N) matrix (what mamba.ex:187-193
-    passes to the fused path) give identical results."""
-    x, dt, A, Bm, Cm, dy = ssm_inputs(2, 300, 256, 16, torch.bfloat16, seed=5)
+    passes to the fused path) compute the same numbers: with A = None the decays
+    are the powers r^(n+1) of r = exp(-dt) (one exponential per step and
+    channel), with the matrix one exponential per state, so they agree to f32
+    rounding (f32 io here, so that no bf16 output rounding hides a difference)."""
+    x, dt, A, Bm, Cm, dy = ssm_inputs(2, 300, 256, 16, torch.float32, seed=5)
     D, N = A.shape
-    fixed = (-(torch.arange(N, dtype=torch.float32) + 1)).expand(D, N).contiguous()
-    fixed = fixed.to(torch.bfloat16).cuda()
+    fixed = (-(torch.arange(N, dtype=torch.float32) + 1)).expand(D, N).contiguous().cuda()
     y0, m0 = fs.selective_scan_model(x, dt, Bm, Cm)
     y1, m1 = fs.selective_scan_model(x, dt, Bm, Cm, a=fixed)
     torch.cuda.synchronize()
-    assert torch.equal(y0, y1) and torch.equal(m0, m1)
+    assert torch.equal(m0, m1)
+    assert O.norm_rel(_np(y0), _np(y1)) <= 1e-5
     g0 = fs.selective_scan_model_backward(x, dt, Bm, Cm, dy, m0)
     g1 = fs.selective_scan_model_backward(x, dt, Bm, Cm, dy, m1, a=fixed)
     for u, v in zip(g0, g1):
-        assert torch.equal(u, v)
+        assert O.norm_rel(_np(u), _np(v)) <= 1e-5
 
 
 def test_model_semantics_autograd_fn(cuda):
