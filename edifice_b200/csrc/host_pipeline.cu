@@ -49,7 +49,8 @@ int check_shape(int dtype, int B, int L, int H) {
 struct Res {
     cudaStream_t sin = nullptr, sout = nullptr;
     cudaEvent_t start = nullptr, done = nullptr;
-    cudaEvent_t in[kSlots] = {}, comp[kSlots] = {}, free_[kSlots] = {};
+    cudaEvent_t in_fwd[kSlots] = {}, in[kSlots] = {}, fwd[kSlots] = {}, comp[kSlots] = {},
+                free_[kSlots] = {};
     ~Res() {
         // destruction is deferred by the runtime until queued work completes
         if (sin) cudaStreamDestroy(sin);
@@ -57,7 +58,7 @@ struct Res {
         for (cudaEvent_t e : {start, done})
             if (e) cudaEventDestroy(e);
         for (int i = 0; i < kSlots; ++i)
-            for (cudaEvent_t e : {in[i], comp[i], free_[i]})
+            for (cudaEvent_t e : {in_fwd[i], in[i], fwd[i], comp[i], free_[i]})
                 if (e) cudaEventDestroy(e);
     }
     cudaError_t init() {
@@ -67,7 +68,9 @@ struct Res {
         if ((e = cudaEventCreateWithFlags(&start, cudaEventDisableTiming))) return e;
         if ((e = cudaEventCreateWithFlags(&done, cudaEventDisableTiming))) return e;
         for (int i = 0; i < kSlots; ++i) {
+            if ((e = cudaEventCreateWithFlags(&in_fwd[i], cudaEventDisableTiming))) return e;
             if ((e = cudaEventCreateWithFlags(&in[i], cudaEventDisableTiming))) return e;
+            if ((e = cudaEventCreateWithFlags(&fwd[i], cudaEventDisableTiming))) return e;
             if ((e = cudaEventCreateWithFlags(&comp[i], cudaEventDisableTiming))) return e;
             if ((e = cudaEventCreateWithFlags(&free_[i], cudaEventDisableTiming))) return e;
         }
@@ -125,30 +128,38 @@ int run(int op, int dtype, const void* x0, const void* x1, const void* h0, const
         auto hp = [](const void* p, size_t o) { return static_cast<const char*>(p) + o; };
         auto hq = [](void* p, size_t o) { return static_cast<char*>(p) + o; };
 
-        // host -> device, once the slot's previous chunk has been copied out
+        // host -> device, once the slot's previous chunk has been copied out: the
+        // forward's inputs first, so that the forward (and the copy of h back to the
+        // host) can start while dy is still on its way in
         if (i >= kSlots) EDB_TRY(cudaStreamWaitEvent(r.sin, r.free_[slot], 0));
         EDB_TRY(cudaMemcpyAsync(dx0, hp(x0, off), n, cudaMemcpyHostToDevice, r.sin));
         EDB_TRY(cudaMemcpyAsync(dx1, hp(x1, off), n, cudaMemcpyHostToDevice, r.sin));
-        EDB_TRY(cudaMemcpyAsync(ddy, hp(dy, off), n, cudaMemcpyHostToDevice, r.sin));
         if (h0) EDB_TRY(cudaMemcpyAsync(dh0, hp(h0, off0), n0, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaEventRecord(r.in_fwd[slot], r.sin));
+        EDB_TRY(cudaMemcpyAsync(ddy, hp(dy, off), n, cudaMemcpyHostToDevice, r.sin));
         EDB_TRY(cudaEventRecord(r.in[slot], r.sin));
 
-        // forward + backward of the chunk on the caller's stream
-        EDB_TRY(cudaStreamWaitEvent(s, r.in[slot], 0));
+        // forward, then backward, of the chunk on the caller's stream
         const void* ph0 = h0 ? dh0 : nullptr;
         void* pgh0 = gh0 ? dgh0 : nullptr;
-        if (op == HOST_LINEAR) {
+        EDB_TRY(cudaStreamWaitEvent(s, r.in_fwd[slot], 0));
+        if (op == HOST_LINEAR)
             EDB_TRY_ST(edb_linear_scan_fwd(dtype, dx0, dx1, ph0, dh, nr, L, H, s));
-            EDB_TRY_ST(edb_linear_scan_bwd(dtype, dx0, ph0, dh, ddy, dg0, dg1, pgh0, nr, L, H, s));
-        } else {
+        else
             EDB_TRY_ST(edb_mingru_fwd(dtype, dx0, dx1, ph0, dh, nr, L, H, s));
+        EDB_TRY(cudaEventRecord(r.fwd[slot], s));
+        EDB_TRY(cudaStreamWaitEvent(s, r.in[slot], 0));
+        if (op == HOST_LINEAR)
+            EDB_TRY_ST(edb_linear_scan_bwd(dtype, dx0, ph0, dh, ddy, dg0, dg1, pgh0, nr, L, H, s));
+        else
             EDB_TRY_ST(edb_mingru_bwd(dtype, dx0, dx1, ph0, dh, ddy, dg0, dg1, pgh0, nr, L, H, s));
-        }
         EDB_TRY(cudaEventRecord(r.comp[slot], s));
 
-        // device -> host
-        EDB_TRY(cudaStreamWaitEvent(r.sout, r.comp[slot], 0));
+        // device -> host: h as soon as the forward is done, the gradients after the
+        // backward (the backward only reads h, so both may run at once)
+        EDB_TRY(cudaStreamWaitEvent(r.sout, r.fwd[slot], 0));
         EDB_TRY(cudaMemcpyAsync(hq(h, off), dh, n, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaStreamWaitEvent(r.sout, r.comp[slot], 0));
         EDB_TRY(cudaMemcpyAsync(hq(g0, off), dg0, n, cudaMemcpyDeviceToHost, r.sout));
         EDB_TRY(cudaMemcpyAsync(hq(g1, off), dg1, n, cudaMemcpyDeviceToHost, r.sout));
         if (gh0) EDB_TRY(cudaMemcpyAsync(hq(gh0, off0), dgh0, n0, cudaMemcpyDeviceToHost, r.sout));
