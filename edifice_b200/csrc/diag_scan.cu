@@ -228,10 +228,16 @@ __global__ void __launch_bounds__(32 * CW, CW >= 16 ? 1 : 2)
                 V::unpack(rin[1][j], x1);
 #pragma unroll
                 for (int c = 0; c < VEC; ++c) {
-                    float a, bb;
-                    StepMap<OP, BWD>::map(x0[c], x1[c], a, bb);
-                    Bc[c] = fmaf(a, Bc[c], bb);
-                    A[c] *= a;
+                    if (OP == OP_MINGRU && !BWD) {
+                        // (1 - z, z c) composed as A - z A, B + z (c - B): 3 instructions
+                        A[c] = fmaf(-x0[c], A[c], A[c]);
+                        Bc[c] = fmaf(x0[c], x1[c] - Bc[c], Bc[c]);
+                    } else {
+                        float a, bb;
+                        StepMap<OP, BWD>::map(x0[c], x1[c], a, bb);
+                        Bc[c] = fmaf(a, Bc[c], bb);
+                        A[c] *= a;
+                    }
                 }
             }
         }
@@ -305,9 +311,13 @@ __global__ void __launch_bounds__(32 * CW, CW >= 16 ? 1 : 2)
                 if (!BWD) {
 #pragma unroll
                     for (int c = 0; c < VEC; ++c) {
-                        float a, bb;
-                        StepMap<OP, BWD>::map(x0[c], x1[c], a, bb);
-                        sv[c] = fmaf(a, sv[c], bb);
+                        if (OP == OP_MINGRU) {
+                            sv[c] = fmaf(x0[c], x1[c] - sv[c], sv[c]);  // h + z (c - h)
+                        } else {
+                            float a, bb;
+                            StepMap<OP, BWD>::map(x0[c], x1[c], a, bb);
+                            sv[c] = fmaf(a, sv[c], bb);
+                        }
                     }
                     if (ch_ok) st_global_v4(out0 + off, V::pack(sv));
                 } else {
