@@ -2,19 +2,23 @@
 """Benchmark of the fused sequence-mixing hot path on B200 (one JSON line).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config linear|mingru|ssm|attn|delta|gated] [--no-paths]
+                    [--config ssm|linear|mingru|attn|laser|delta|delta_model|gated|
+                              ssm_model|ssm_cfg0] [--scaling strong|weak] [--no-paths]
 
-Headline (default --config linear): BASELINE configs[1] -- the diagonal
-linear-RNN scan h_t = a_t h_{t-1} + b_t, forward + backward, bf16 io / f32
-state, batch 8 x seq 4096 x hidden 2048 per GPU.  A step = one forward + one
-backward pass over the rank's shard; tokens = batch * seq.  Weak scaling: rank r
-owns units [rU, (r+1)U) of a global problem of N shards (batch rows; (batch,
-kv-group) pairs for attention), inputs seeded per unit, no collective on the
-data path.
+Headline (default --config ssm): BASELINE configs[4], the largest single-GPU
+config -- the Mamba selective scan (kernel semantics) forward with chunk-start
+states + backward, bf16 io / f32 state, batch 64 x seq 8192 x d_inner 4096,
+d_state 16.  A step = one forward + one backward pass over the rank's shard;
+tokens = batch * seq.  Strong scaling by default: the fixed configs[4] problem is
+split over the N ranks by batch rows (64/N each); --scaling weak gives every rank
+a full config of its own units.  No collective runs on the data path.
 
-The headline line also carries `paths`: the other configs (MinGRU form of
-configs[1], configs[2] DeltaNet, configs[3] causal GQA attention, configs[4]
-Mamba selective scan), each timed the same way over min(K, 20) steps.
+The line carries `paths`: every other config timed the same way -- configs[1]
+(linear scan, and its MinGRU form), configs[2] (chunked DeltaNet; also the
+per-element-beta model form and GatedDeltaNet), configs[3] (causal GQA flash
+attention, and LASER at its shapes), the Mamba model semantics at configs[4]
+shapes, and configs[0] (the reference's CPU Mamba forward, f32, on the GPU) --
+each with its own roofline, e2e and (N = 1) cpu_baseline.
 
 --impl ours       our kernels (libedifice_b200.so): device-timed with CUDA
                   events, max over ranks; e2e through the public API with host
@@ -38,35 +42,39 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+CONFIGS = ("ssm", "linear", "mingru", "attn", "laser", "delta", "delta_model", "gated",
+           "ssm_model", "ssm_cfg0")
+
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["linear", "mingru", "ssm", "ssm_model", "attn", "laser",
-                                         "delta", "delta_model", "gated"],
-                    default="linear")
-    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--config", choices=CONFIGS, default="ssm")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong")
+    ap.add_argument("--e2e-steps", type=int, default=20,
+                    help="upper bound on the timed e2e steps (each path also stops at ~3 s)")
     ap.add_argument("--replicate", action="store_true",
                     help="N>1: also time the optional all-gather of the forward output "
                          "(a replicated output; never part of the kernel path)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-paths", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
-                    help="override the config's batch per GPU (small cases for ncu captures)")
+                    help="override the config's batch (small cases for ncu captures)")
     ap.add_argument("--seq-len", type=int, default=None,
                     help="override the config's sequence length (small cases for ncu captures)")
     return ap.parse_args()
 
 
-def make_workload(args):
+def make_workload(name, args=None):
     import dataclasses
-    wl = WORKLOADS[args.config]()
-    if args.batch:
+    wl = WORKLOADS[name]()
+    if args is not None and args.batch:
         wl.cfg = dataclasses.replace(wl.cfg, batch=args.batch)
-    if args.seq_len:
+    if args is not None and args.seq_len:
         wl.cfg = dataclasses.replace(wl.cfg, seq_len=args.seq_len)
     return wl
 
@@ -147,12 +155,12 @@ def measured_peaks():
         with open(p) as f:
             d = json.load(f)
         return {"hbm": (float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"),
-                "tensor": (float(d["bf16_tflops_sustained"]),
-                           "measured (MEASURED_PEAKS.json bf16_tflops_sustained: the kernel runs "
-                           "back to back inside a seconds-long step loop)"),
+                "tensor": (float(d["bf16_tflops"]),
+                           "measured (MEASURED_PEAKS.json bf16_tflops, the burst figure: each "
+                           "kernel is timed over a region of tens to hundreds of ms)"),
                 "sfu": sfu, "fp32": fp32}
     return {"hbm": (6650.0, "fallback (6.65 TB/s pool measurement)"),
-            "tensor": (1400.0, "fallback (1.4 PFLOP/s sustained pool measurement)"), "sfu": sfu,
+            "tensor": (1590.0, "fallback (1.59 PFLOP/s burst pool measurement)"), "sfu": sfu,
             "fp32": fp32}
 
 
@@ -179,75 +187,121 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
+def _pinned_like(t):
+    import torch
+    return torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+
+
 # ---------------------------------------------------------------- workloads
-class ScanWorkload:
+class Workload:
+    """One config of the path.  Subclasses set cfg, kname, dtype, api and define
+    _setup, step, kernels, host_inputs, e2e_step (device API after the copies) or
+    e2e_host (a host-tensor entry point), cpu_step and cpu_what."""
+    dtype = "bf16"
+    launches_per_step = 0
+    unit_name = "batch rows"
+
+    def setup(self, dev, rank, world, scaling):
+        from edifice_b200 import shard
+        self.world, self.scaling = world, scaling
+        self.my_units = shard.units_for(self.cfg.units, rank, world, scaling)
+        self.active = len(self.my_units) > 0
+        if self.active:
+            self._setup(dev)
+
+    def total_tokens(self):
+        """Tokens of one step summed over all ranks."""
+        mult = self.world if self.scaling == "weak" else 1
+        return self.cfg.tokens * mult
+
+    def describe(self, world, scaling):
+        from edifice_b200 import shard
+        n = len(shard.units_for(self.cfg.units, 0, world, scaling))
+        total = self.cfg.units * (world if scaling == "weak" else 1)
+        d = {"workload": self.title(), "units": "%s: %d in all, %d on rank 0" % (
+                 self.unit_name, total, n),
+             "scaling": scaling,
+             "parallelism": "dp%d (shards of %s, no collective)" % (world, self.unit_name)}
+        d.update(self.shape_info())
+        d["global_batch"] = self.cfg.batch * (world if scaling == "weak" else 1)
+        d["l2"] = self.l2_note()
+        return d
+
+    def step(self, ev=None):
+        if ev:
+            ev[0].record()
+        r = self.fwd() if self.active else None
+        if ev:
+            ev[1].record()
+        if self.active and self.has_bwd:
+            self.bwd(r)
+        if ev:
+            ev[2].record()
+
+    has_bwd = True
+
+    def e2e_step(self, dev_in):
+        raise NotImplementedError
+
+    def extra(self, fwd_ms, bwd_ms):
+        return {}
+
+
+class ScanWorkload(Workload):
     """linear scan (or its MinGRU form) fwd + bwd."""
 
     def __init__(self, mingru=False):
         from edifice_b200.shard import ScanConfig
         self.cfg = ScanConfig(name="mingru_cfg1", mingru=True) if mingru else ScanConfig()
         self.kname = "mingru" if mingru else "linear_scan"
-        self.dtype = "bf16"
 
-    def describe(self, world):
+    def title(self):
+        return "%s fwd+bwd (BASELINE configs[1]%s)" % (
+            self.cfg.name, ", MinGRU form" if self.cfg.mingru else "")
+
+    def shape_info(self):
         c = self.cfg
-        return {"workload": "%s fwd+bwd (BASELINE configs[1]%s)" %
-                            (c.name, ", MinGRU form" if c.mingru else ""),
-                "batch_per_gpu": c.batch, "global_batch": c.batch * world, "seq_len": c.seq_len,
-                "hidden": c.hidden, "parallelism": "dp%d (batch-row shards, no collective)" % world,
-                "l2": "inputs larger than L2 (%.2f GB touched per step > 126 MB)"
-                      % ((c.bytes_fwd() + c.bytes_bwd()) / 1e9)}
+        return {"batch": c.batch, "seq_len": c.seq_len, "hidden": c.hidden}
 
-    def setup(self, dev, rank):
+    def l2_note(self):
+        c = self.cfg
+        return "inputs larger than L2 (%.2f GB touched per step > 126 MB)" % (
+            (c.bytes_fwd() + c.bytes_bwd()) / 1e9)
+
+    def _setup(self, dev):
         from edifice_b200 import shard
-        self.units = shard.plan_units(self.cfg.units, rank, self._world)
-        self.a, self.b, self.dy = shard.scan_inputs(self.cfg, self.units, dev)
+        self.a, self.b, self.dy = shard.scan_inputs(self.cfg, self.my_units, dev)
 
     def kernels(self):
-        return {"fwd": ("hbm", self.cfg.bytes_fwd()), "bwd": ("hbm", self.cfg.bytes_bwd())}
+        f = len(self.my_units) / self.cfg.units
+        return {"fwd": ("hbm", self.cfg.bytes_fwd() * f), "bwd": ("hbm", self.cfg.bytes_bwd() * f)}
 
     launches_per_step = 2
-    tokens = property(lambda self: self.cfg.tokens)
 
-    def _fwd(self, a, b):
+    def fwd(self):
         from edifice_b200 import fused_scan as fs
-        return fs.mingru_scan(a, b) if self.cfg.mingru else fs.linear_scan(a, b)
+        return fs.mingru_scan(self.a, self.b) if self.cfg.mingru else \
+            fs.linear_scan(self.a, self.b)
 
-    def _bwd(self, a, b, h, dy):
+    def bwd(self, h):
         from edifice_b200 import fused_scan as fs
         if self.cfg.mingru:
-            return fs.mingru_backward(a, b, None, h, dy)
-        return fs.linear_scan_backward(a, None, h, dy)
-
-    def step(self, ev=None):
-        if ev:
-            ev[0].record()
-        h = self._fwd(self.a, self.b)
-        if ev:
-            ev[1].record()
-        self._bwd(self.a, self.b, h, self.dy)
-        if ev:
-            ev[2].record()
+            return fs.mingru_backward(self.a, self.b, None, h, self.dy)
+        return fs.linear_scan_backward(self.a, None, h, self.dy)
 
     def host_inputs(self):
         return [self.a, self.b, self.dy]
 
     def forward_output(self):
-        return self._fwd(self.a, self.b)
+        return self.fwd()
 
-    def e2e_host_shapes(self):
+    def e2e_outputs(self):
         B, L, H = self.a.shape
-        return [(B, L, H)] * 3 + [(B, H)]
-
-    def e2e_step(self, dev_in):
-        a, b, dy = dev_in
-        h = self._fwd(a, b)
-        return (h,) + tuple(self._bwd(a, b, h, dy))
+        return [(B, L, H, self.a.dtype)] * 3 + [(B, H, self.a.dtype)]
 
     def e2e_host(self, pin, outs):
         """One fwd+bwd step over pinned host buffers through the host entry
-        point, which overlaps the copies with the kernels batch-row chunk by chunk.
-        Returns the host outputs (h, ga, gb, gh0)."""
+        point, which overlaps the copies with the kernels batch-row chunk by chunk."""
         from edifice_b200 import fused_scan as fs
         fn = fs.mingru_train_host if self.cfg.mingru else fs.linear_scan_train_host
         return fn(pin[0], pin[1], pin[2], out=outs)
@@ -275,8 +329,9 @@ class ScanWorkload:
             O.linear_scan_bwd(a, None, h, dy, prec=prec)
         return rows * c.seq_len  # tokens processed
 
-    cpu_what = ("oracle f32 port of the Nx fallbacks (fused_scan.ex:4429-4444, 884-916; "
-                "MinGRU :516-528, 548-581)")
+    cpu_what = property(lambda self: (
+        "oracle f32 port of the Nx fallbacks (fused_scan.ex:%s) on the full config" % (
+            "516-528, 548-581" if self.cfg.mingru else "4429-4444, 884-916")))
 
     def ref_cpu_forward(self, budget_s=3.0):
         """Forward-only tokens/s of the reference's own single-threaded C CPU
@@ -307,89 +362,167 @@ class ScanWorkload:
                     "mingru_scan_cpu" if c.mingru else "linear_scan_cpu")}
 
 
-class SsmWorkload:
+def _ssm_cpu_sample(c, ch, L):
+    import numpy as np
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((1, L, ch), dtype=np.float32)
+    dt = np.log1p(np.exp(rng.standard_normal((1, L, ch)) * 0.5 - 2)).astype(np.float32)
+    A = (-np.exp(rng.uniform(0, math.log(16), (ch, c.d_state)))).astype(np.float32)
+    B = rng.standard_normal((1, L, c.d_state), dtype=np.float32)
+    C = rng.standard_normal((1, L, c.d_state), dtype=np.float32)
+    dy = rng.standard_normal((1, L, ch), dtype=np.float32)
+    return x, dt, A, B, C, dy
+
+
+class SsmWorkload(Workload):
     """Mamba selective scan fwd (with chunk checkpoints) + bwd."""
 
     def __init__(self):
         from edifice_b200.shard import SsmConfig
         self.cfg = SsmConfig()
         self.kname = "selective_scan"
-        self.dtype = "bf16"
 
-    def describe(self, world):
+    def title(self):
+        return "%s fwd+bwd (BASELINE configs[4], kernel semantics)" % self.cfg.name
+
+    def shape_info(self):
         c = self.cfg
-        return {"workload": "%s fwd+bwd (BASELINE configs[4])" % c.name,
-                "batch_per_gpu": c.batch, "global_batch": c.batch * world, "seq_len": c.seq_len,
-                "d_inner": c.d_inner, "d_state": c.d_state,
-                "parallelism": "dp%d (batch-row shards, no collective)" % world,
-                "l2": "inputs larger than L2 (%.1f GB per step)"
-                      % ((c.bytes_fwd() + c.bytes_bwd()) / 1e9)}
+        return {"batch": c.batch, "seq_len": c.seq_len, "d_inner": c.d_inner,
+                "d_state": c.d_state}
 
-    def setup(self, dev, rank):
+    def l2_note(self):
+        c = self.cfg
+        return "inputs larger than L2 (%.1f GB per step)" % ((c.bytes_fwd() + c.bytes_bwd()) / 1e9)
+
+    def _setup(self, dev):
         from edifice_b200 import shard
-        self.units = shard.plan_units(self.cfg.units, rank, self._world)
-        self.x, self.dt, self.A, self.B, self.C, self.dy = shard.ssm_inputs(self.cfg, self.units, dev)
+        self.x, self.dt, self.A, self.B, self.C, self.dy = shard.ssm_inputs(
+            self.cfg, self.my_units, dev)
 
     def kernels(self):
         # exp-bound, not HBM-bound: one ex2 per (t, d, n) costs more SFU time
         # (16/clk/SM) than the element's bytes cost HBM time
-        return {"fwd": ("sfu", self.cfg.exps_fwd()), "bwd": ("sfu", self.cfg.exps_bwd())}
+        f = len(self.my_units) / self.cfg.units
+        return {"fwd": ("sfu", self.cfg.exps_fwd() * f), "bwd": ("sfu", self.cfg.exps_bwd() * f)}
 
     launches_per_step = 3  # fwd, bwd, dB/dC reduce
-    tokens = property(lambda self: self.cfg.tokens)
 
-    def step(self, ev=None):
+    def fwd(self):
         from edifice_b200 import fused_scan as fs
-        if ev:
-            ev[0].record()
-        _, ck = fs.selective_scan(self.x, self.dt, self.A, self.B, self.C, with_ckpt=True)
-        if ev:
-            ev[1].record()
-        fs.selective_scan_backward(self.x, self.dt, self.A, self.B, self.C, self.dy, ck)
-        if ev:
-            ev[2].record()
+        return fs.selective_scan(self.x, self.dt, self.A, self.B, self.C, with_ckpt=True)[1]
+
+    def bwd(self, ck):
+        from edifice_b200 import fused_scan as fs
+        return fs.selective_scan_backward(self.x, self.dt, self.A, self.B, self.C, self.dy, ck)
 
     def host_inputs(self):
         return [self.x, self.dt, self.A, self.B, self.C, self.dy]
 
-    def e2e_step(self, dev_in):
-        from edifice_b200 import fused_scan as fs
-        x, dt, A, B, C, dy = dev_in
-        y, ck = fs.selective_scan(x, dt, A, B, C, with_ckpt=True)
-        return (y,) + tuple(fs.selective_scan_backward(x, dt, A, B, C, dy, ck))
+    def e2e_outputs(self):
+        import torch
+        Bsz, L, D = self.x.shape
+        N = self.A.shape[1]
+        return [(Bsz, L, D, self.x.dtype)] * 3 + [(Bsz, L, N, torch.float32)] * 2
 
-    api = "edifice_b200.fused_scan.selective_scan + backward"
+    def e2e_host(self, pin, outs):
+        """One fwd+bwd step over pinned host buffers through the host entry point
+        (batch-row chunks: copies overlapped with the kernels)."""
+        from edifice_b200 import fused_scan as fs
+        return fs.selective_scan_train_host(*pin, out=outs)
+
+    api = "edifice_b200.fused_scan.selective_scan_train_host (host tensors in and out)"
 
     def extra(self, fwd_ms, bwd_ms):
         c = self.cfg
-        hbm_gbs = (c.bytes_fwd() + c.bytes_bwd()) / ((fwd_ms + bwd_ms) / 1e3) / 1e9
+        f = len(self.my_units) / c.units
+        hbm_gbs = (c.bytes_fwd() + c.bytes_bwd()) * f / ((fwd_ms + bwd_ms) / 1e3) / 1e9
         return {"hbm_GB/s_fwd+bwd": round(hbm_gbs, 1),
                 "hbm_frac_of_peak": round(hbm_gbs / measured_peaks()["hbm"][0], 4),
-                "note": "exp-bound, not HBM-bound: one ex2 per (t,d,n) in the forward and two "
-                        "in the recompute-not-store backward; the SFU rate (16/clk/SM) caps the "
-                        "config-4 forward near 7.4 ms at 1965 MHz"}
+                "note": "exp-bound, not HBM-bound: one ex2 per (t,d,n) in the forward, 1.75 "
+                        "in the recompute-not-store backward; the SFU rate (16/clk/SM) caps "
+                        "the configs[4] forward near 7.4 ms at 1965 MHz"}
+
+    CPU_CH, CPU_L = 1024, 8192
+
+    def cpu_step(self, rows=None, prec="f32"):
+        import oracle as O
+        c = self.cfg
+        if not hasattr(self, "_cpu"):
+            self._cpu = _ssm_cpu_sample(c, self.CPU_CH, self.CPU_L)
+        x, dt, A, B, C, dy = self._cpu
+        O.selective_scan_fwd(x, dt, A, B, C, prec=prec)
+        O.selective_scan_bwd(x, dt, A, B, C, dy, prec=prec)
+        # token-equivalents: one batch row, CPU_CH of d_inner channels, CPU_L steps
+        return self.CPU_L * self.CPU_CH / c.d_inner
+
+    cpu_what = property(lambda self: (
+        "oracle f32 port (kernel semantics, backward_kernels_test.exs:1563-1586 + "
+        "fused_scan.ex:1453-1531) on 1 batch row x %d of %d channels x %d steps, scaled "
+        "to tokens by the channel share" % (self.CPU_CH, self.cfg.d_inner, self.CPU_L)))
+
+
+class SsmCfg0Workload(SsmWorkload):
+    """the reference's CPU-backend Mamba forward (f32, batch 2 x seq
+    256 x d_inner 512, d_state 16), timed on the GPU (forward only, as the config
+    is a forward) and through the oracle's f32 port on all host cores."""
+
+    def __init__(self):
+        from edifice_b200.shard import ssm_cfg0
+        self.cfg = ssm_cfg0()
+        self.kname = "selective_scan_cfg0"
+        self.dtype = "f32"
+
+    def title(self):
+        return "%s forward (BASELINE configs[0], f32, kernel semantics)" % self.cfg.name
+
+    def l2_note(self):
+        return "3.25 MB per step: L2-resident (the config is this small)"
+
+    has_bwd = False
+    launches_per_step = 1
+
+    def kernels(self):
+        f = len(self.my_units) / self.cfg.units
+        return {"fwd": ("sfu", self.cfg.exps_fwd() * f), "bwd": ("sfu", 0.0)}
+
+    def fwd(self):
+        from edifice_b200 import fused_scan as fs
+        return fs.selective_scan(self.x, self.dt, self.A, self.B, self.C)
+
+    def host_inputs(self):
+        return [self.x, self.dt, self.A, self.B, self.C]
+
+    e2e_outputs = None
+    e2e_host = None
+
+    def e2e_step(self, dev_in):
+        from edifice_b200 import fused_scan as fs
+        return (fs.selective_scan(*dev_in),)
+
+    api = "edifice_b200.fused_scan.selective_scan (forward; host copies in the timed region)"
+
+    def extra(self, fwd_ms, bwd_ms):
+        return {"note": "configs[0] is a forward-only config: a step is one forward, tokens "
+                        "= batch * seq = 512; launch-bound at this size"}
 
     def cpu_step(self, rows=None, prec="f32"):
         import numpy as np
         import oracle as O
         c = self.cfg
-        ch = 128
-        if not hasattr(self, "_cpu"):
+        if not hasattr(self, "_cpu0"):
             rng = np.random.default_rng(0)
-            x = rng.standard_normal((1, c.seq_len, ch), dtype=np.float32)
-            dt = np.log1p(np.exp(rng.standard_normal((1, c.seq_len, ch)) * 0.5 - 2)).astype(np.float32)
-            A = (-np.exp(rng.uniform(0, math.log(16), (ch, c.d_state)))).astype(np.float32)
-            B = rng.standard_normal((1, c.seq_len, c.d_state), dtype=np.float32)
-            C = rng.standard_normal((1, c.seq_len, c.d_state), dtype=np.float32)
-            dy = rng.standard_normal((1, c.seq_len, ch), dtype=np.float32)
-            self._cpu = (x, dt, A, B, C, dy)
-        x, dt, A, B, C, dy = self._cpu
-        O.selective_scan_fwd(x, dt, A, B, C, prec=prec)
-        O.selective_scan_bwd(x, dt, A, B, C, dy, prec=prec)
-        return c.seq_len * ch / c.d_inner  # token-equivalents (one row, 128 of 4096 channels)
+            shp = (c.batch, c.seq_len, c.d_inner)
+            x = rng.standard_normal(shp, dtype=np.float32)
+            dt = np.log1p(np.exp(rng.standard_normal(shp) * 0.5 - 2)).astype(np.float32)
+            A = (-np.exp(rng.uniform(0, math.log(16), (c.d_inner, c.d_state)))).astype(np.float32)
+            B = rng.standard_normal((c.batch, c.seq_len, c.d_state), dtype=np.float32)
+            C = rng.standard_normal((c.batch, c.seq_len, c.d_state), dtype=np.float32)
+            self._cpu0 = (x, dt, A, B, C)
+        O.selective_scan_fwd(*self._cpu0, prec=prec)
+        return c.tokens
 
-    cpu_what = ("oracle f32 port (kernel semantics, backward_kernels_test.exs:1563-1586 + "
-                "fused_scan.ex:1453-1531) on 1 batch row x 128 of 4096 channels, scaled")
+    cpu_what = "oracle f32 port of the kernel-semantics forward (fused_selective_scan.cu:41-98 == " \
+               "backward_kernels_test.exs:1563-1586) on the full configs[0] problem"
 
 
 class SsmModelWorkload(SsmWorkload):
@@ -403,11 +536,9 @@ class SsmModelWorkload(SsmWorkload):
         self.cfg = dataclasses.replace(self.cfg, name="selective_scan_model_cfg4")
         self.kname = "selective_scan_model"
 
-    def describe(self, world):
-        d = super().describe(world)
-        d["workload"] = ("%s fwd+bwd (configs[4] shapes, Edifice.build(:mamba) semantics: "
-                         "B_bar = mean_d(dt) B, A = -(1..N))" % self.cfg.name)
-        return d
+    def title(self):
+        return ("%s fwd+bwd (configs[4] shapes, Edifice.build(:mamba) semantics: "
+                "B_bar = mean_d(dt) B, A = -(1..N))" % self.cfg.name)
 
     launches_per_step = 5  # dt mean, fwd, bwd, dB/dC reduce, gdt mean term
 
@@ -415,29 +546,33 @@ class SsmModelWorkload(SsmWorkload):
         # With the model's fixed A = -(1..N) the decays are the powers of exp(-dt): one
         # ex2 per (t, d), not per (t, d, n), so the SFU no longer bounds the path; it is
         # issue-bound, and HBM is the roofline it is reported against.
-        return {"fwd": ("hbm", self.cfg.bytes_fwd()), "bwd": ("hbm", self.cfg.bytes_bwd())}
+        f = len(self.my_units) / self.cfg.units
+        return {"fwd": ("hbm", self.cfg.bytes_fwd() * f), "bwd": ("hbm", self.cfg.bytes_bwd() * f)}
 
     def extra(self, fwd_ms, bwd_ms):
         c = self.cfg
-        return {"exps_per_s_fwd_algorithmic": round(c.exps_fwd() / (fwd_ms / 1e3) / 1e9, 1),
+        f = len(self.my_units) / c.units
+        return {"exps_per_s_fwd_algorithmic": round(c.exps_fwd() * f / (fwd_ms / 1e3) / 1e9, 1),
                 "note": "fixed A = -(1..N): exp(dt A[d,n]) = r^(n+1), r = exp(-dt), one ex2 "
                         "and NS/2 packed multiplies per (t, d) in the forward, the backward's "
-                        "rebuild and its recompute; issue-bound (forward: a few instructions "
-                        "per (t, d, n)), HBM is the reported roofline"}
+                        "rebuild and its recompute; issue-bound, HBM is the reported roofline"}
 
-    def step(self, ev=None):
+    def fwd(self):
         from edifice_b200 import fused_scan as fs
-        if ev:
-            ev[0].record()
         _, dtm, ck = fs.selective_scan_model(self.x, self.dt, self.B, self.C, with_ckpt=True)
-        if ev:
-            ev[1].record()
-        fs.selective_scan_model_backward(self.x, self.dt, self.B, self.C, self.dy, dtm, h_ckpt=ck)
-        if ev:
-            ev[2].record()
+        return dtm, ck
+
+    def bwd(self, r):
+        from edifice_b200 import fused_scan as fs
+        dtm, ck = r
+        return fs.selective_scan_model_backward(self.x, self.dt, self.B, self.C, self.dy, dtm,
+                                                h_ckpt=ck)
 
     def host_inputs(self):
         return [self.x, self.dt, self.B, self.C, self.dy]
+
+    e2e_outputs = None
+    e2e_host = None
 
     def e2e_step(self, dev_in):
         from edifice_b200 import fused_scan as fs
@@ -445,7 +580,8 @@ class SsmModelWorkload(SsmWorkload):
         y, dtm, ck = fs.selective_scan_model(x, dt, B, C, with_ckpt=True)
         return (y,) + tuple(fs.selective_scan_model_backward(x, dt, B, C, dy, dtm, h_ckpt=ck))
 
-    api = "edifice_b200.fused_scan.selective_scan_model + backward"
+    api = ("edifice_b200.fused_scan.selective_scan_model + backward (whole-tensor copies "
+           "in the timed region)")
 
     def cpu_step(self, rows=None, prec="f32"):
         import numpy as np
@@ -469,48 +605,50 @@ class SsmModelWorkload(SsmWorkload):
                 "one batch row per thread x 1024 steps x 128 of 4096 channels, scaled")
 
 
-class AttnWorkload:
+class AttnWorkload(Workload):
     """causal GQA attention fwd (with lse) + bwd."""
+    unit_name = "(batch, kv-group) pairs"
 
     def __init__(self):
         from edifice_b200.shard import AttnConfig
         self.cfg = AttnConfig()
         self.kname = "flash_attention"
-        self.dtype = "bf16"
 
-    def describe(self, world):
+    def title(self):
+        return "%s fwd+bwd (BASELINE configs[3])" % self.cfg.name
+
+    def shape_info(self):
         c = self.cfg
-        return {"workload": "%s fwd+bwd (BASELINE configs[3])" % c.name,
-                "batch_per_gpu": c.batch, "global_batch": c.batch * world, "q_heads": c.q_heads,
-                "kv_heads": c.kv_heads, "seq_len": c.seq_len, "head_dim": c.head_dim,
-                "causal": c.causal,
-                "parallelism": "dp%d ((batch, kv-group) shards, no collective)" % world,
-                "l2": "tensor-bound; q/k/v/dO 0.67 GB per step"}
+        return {"batch": c.batch, "q_heads": c.q_heads, "kv_heads": c.kv_heads,
+                "seq_len": c.seq_len, "head_dim": c.head_dim, "causal": c.causal}
 
-    def setup(self, dev, rank):
+    def l2_note(self):
+        return "tensor-bound; q/k/v/dO 0.67 GB per step"
+
+    def _setup(self, dev):
         from edifice_b200 import shard
-        self.units = shard.plan_units(self.cfg.units, rank, self._world)
-        self.q, self.k, self.v, self.do = shard.attn_inputs(self.cfg, self.units, dev)
+        self.q, self.k, self.v, self.do = shard.attn_inputs(self.cfg, self.my_units, dev)
 
     def kernels(self):
-        return {"fwd": ("tensor", self.cfg.flops_fwd()), "bwd": ("tensor", self.cfg.flops_bwd())}
+        f = len(self.my_units) / self.cfg.units
+        return {"fwd": ("tensor", self.cfg.flops_fwd() * f),
+                "bwd": ("tensor", self.cfg.flops_bwd() * f)}
 
     launches_per_step = 4  # fwd, rowdot, bwd, dq convert
-    tokens = property(lambda self: self.cfg.tokens)
 
-    def step(self, ev=None):
+    def fwd(self):
         from edifice_b200 import fused_scan as fs
-        if ev:
-            ev[0].record()
-        o, lse = fs.flash_attention(self.q, self.k, self.v, causal=True, return_lse=True)
-        if ev:
-            ev[1].record()
-        fs.flash_attention_backward(self.q, self.k, self.v, True, o, self.do, lse)
-        if ev:
-            ev[2].record()
+        return fs.flash_attention(self.q, self.k, self.v, causal=True, return_lse=True)
+
+    def bwd(self, r):
+        from edifice_b200 import fused_scan as fs
+        o, lse = r
+        return fs.flash_attention_backward(self.q, self.k, self.v, True, o, self.do, lse)
 
     def host_inputs(self):
         return [self.q, self.k, self.v, self.do]
+
+    e2e_host = None
 
     def e2e_step(self, dev_in):
         from edifice_b200 import fused_scan as fs
@@ -518,7 +656,8 @@ class AttnWorkload:
         o, lse = fs.flash_attention(q, k, v, causal=True, return_lse=True)
         return (o,) + tuple(fs.flash_attention_backward(q, k, v, True, o, do, lse))
 
-    api = "edifice_b200.fused_scan.flash_attention + flash_attention_backward"
+    api = ("edifice_b200.fused_scan.flash_attention + flash_attention_backward (whole-tensor "
+           "copies in the timed region)")
 
     def cpu_step(self, rows=None, prec="f32"):
         import numpy as np
@@ -555,23 +694,18 @@ class LaserWorkload(AttnWorkload):
         self.cfg = dataclasses.replace(self.cfg, name="laser_attention_cfg3")
         self.kname = "laser_attention"
 
-    def describe(self, world):
-        d = super().describe(world)
-        d["workload"] = "%s fwd+bwd (configs[3] shapes)" % self.cfg.name
-        return d
+    def title(self):
+        return "%s fwd+bwd (configs[3] shapes)" % self.cfg.name
 
     launches_per_step = 9  # vmax, exp, flash fwd, log; dR, rowdot, flash bwd, dq convert, dV
 
-    def step(self, ev=None):
+    def fwd(self):
         from edifice_b200 import fused_scan as fs
-        if ev:
-            ev[0].record()
-        _, resid = fs.laser_attention(self.q, self.k, self.v, causal=True, return_resid=True)
-        if ev:
-            ev[1].record()
-        fs.laser_attention_backward(self.q, self.k, self.v, self.do, resid, causal=True)
-        if ev:
-            ev[2].record()
+        return fs.laser_attention(self.q, self.k, self.v, causal=True, return_resid=True)[1]
+
+    def bwd(self, resid):
+        from edifice_b200 import fused_scan as fs
+        return fs.laser_attention_backward(self.q, self.k, self.v, self.do, resid, causal=True)
 
     def e2e_step(self, dev_in):
         from edifice_b200 import fused_scan as fs
@@ -579,7 +713,8 @@ class LaserWorkload(AttnWorkload):
         o, resid = fs.laser_attention(q, k, v, causal=True, return_resid=True)
         return (o,) + tuple(fs.laser_attention_backward(q, k, v, do, resid, causal=True))
 
-    api = "edifice_b200.fused_scan.laser_attention + laser_attention_backward"
+    api = ("edifice_b200.fused_scan.laser_attention + laser_attention_backward (whole-tensor "
+           "copies in the timed region)")
 
     def cpu_step(self, rows=None, prec="f32"):
         import numpy as np
@@ -603,51 +738,53 @@ class LaserWorkload(AttnWorkload):
                 "L=1024, scaled to the step by FLOP share")
 
 
-class DeltaWorkload:
+class DeltaWorkload(Workload):
     """DeltaNet delta rule fwd (with state checkpoints) + bwd."""
+    unit_name = "(batch, head) pairs"
 
     def __init__(self):
         from edifice_b200.shard import DeltaConfig
         self.cfg = DeltaConfig()
         self.kname = "delta_rule"
-        self.dtype = "bf16"
 
-    def describe(self, world):
+    def title(self):
+        return "%s fwd+bwd (BASELINE configs[2])" % self.cfg.name
+
+    def shape_info(self):
         c = self.cfg
-        return {"workload": "%s fwd+bwd (BASELINE configs[2])" % c.name,
-                "batch_per_gpu": c.batch, "global_batch": c.batch * world, "heads": c.heads,
-                "seq_len": c.seq_len, "head_dim": c.head_dim, "chunk": c.chunk,
-                "beta": "one per (token, head)",
-                "parallelism": "dp%d ((batch, head) shards, no collective)" % world,
-                "l2": "inputs larger than L2 (%.2f GB per step)"
-                      % ((c.bytes_fwd() + c.bytes_bwd()) / 1e9)}
+        return {"batch": c.batch, "heads": c.heads, "seq_len": c.seq_len,
+                "head_dim": c.head_dim, "chunk": c.chunk, "beta": "one per (token, head)"}
 
-    def setup(self, dev, rank):
+    def l2_note(self):
+        c = self.cfg
+        return "inputs larger than L2 (%.2f GB per step)" % ((c.bytes_fwd() + c.bytes_bwd()) / 1e9)
+
+    def _setup(self, dev):
         from edifice_b200 import shard
-        self.units = shard.plan_units(self.cfg.units, rank, self._world)
-        self.q, self.k, self.v, self.beta, self.do = shard.delta_inputs(self.cfg, self.units, dev)
+        self.q, self.k, self.v, self.beta, self.do = shard.delta_inputs(self.cfg, self.my_units,
+                                                                        dev)
 
     def kernels(self):
         # dense chunked contractions: measured against the tensor peak
-        return {"fwd": ("tensor", self.cfg.flops_fwd()), "bwd": ("tensor", self.cfg.flops_bwd())}
+        f = len(self.my_units) / self.cfg.units
+        return {"fwd": ("tensor", self.cfg.flops_fwd() * f),
+                "bwd": ("tensor", self.cfg.flops_bwd() * f)}
 
     # chunked path: prep + state (forward), prep + state + post (backward)
     launches_per_step = 5
-    tokens = property(lambda self: self.cfg.tokens)
 
-    def step(self, ev=None):
+    def fwd(self):
         from edifice_b200 import fused_scan as fs
-        if ev:
-            ev[0].record()
-        _, ck = fs.delta_net_scan(self.q, self.k, self.v, self.beta, with_ckpt=True)
-        if ev:
-            ev[1].record()
-        fs.delta_rule_backward(self.q, self.k, self.v, self.beta, self.do, ck)
-        if ev:
-            ev[2].record()
+        return fs.delta_net_scan(self.q, self.k, self.v, self.beta, with_ckpt=True)[1]
+
+    def bwd(self, ck):
+        from edifice_b200 import fused_scan as fs
+        return fs.delta_rule_backward(self.q, self.k, self.v, self.beta, self.do, ck)
 
     def host_inputs(self):
         return [self.q, self.k, self.v, self.beta, self.do]
+
+    e2e_host = None
 
     def e2e_step(self, dev_in):
         from edifice_b200 import fused_scan as fs
@@ -655,13 +792,19 @@ class DeltaWorkload:
         o, ck = fs.delta_net_scan(q, k, v, beta, with_ckpt=True)
         return (o,) + tuple(fs.delta_rule_backward(q, k, v, beta, do, ck))
 
-    api = "edifice_b200.fused_scan.delta_net_scan + delta_rule_backward"
+    api = ("edifice_b200.fused_scan.delta_net_scan + delta_rule_backward (whole-tensor copies "
+           "in the timed region)")
 
     def extra(self, fwd_ms, bwd_ms):
+        c = self.cfg
+        f = len(self.my_units) / c.units
         peak = measured_peaks()["tensor"][0]
-        tf = (self.cfg.flops_fwd() + self.cfg.flops_bwd()) / ((fwd_ms + bwd_ms) / 1e3) / 1e12
+        tf = (c.flops_fwd() + c.flops_bwd()) * f / ((fwd_ms + bwd_ms) / 1e3) / 1e12
+        gbs = (c.bytes_fwd() + c.bytes_bwd()) * f / ((fwd_ms + bwd_ms) / 1e3) / 1e9
         return {"chunked_flops_TFLOP/s": round(tf, 2),
-                "tensor_frac_of_peak": round(tf / peak, 4)}
+                "tensor_frac_of_peak": round(tf / peak, 4),
+                "hbm_GB/s_fwd+bwd": round(gbs, 1),
+                "hbm_frac_of_peak": round(gbs / measured_peaks()["hbm"][0], 4)}
 
     def cpu_step(self, rows=None, prec="f32"):
         import numpy as np
@@ -708,23 +851,26 @@ class DeltaModelWorkload(DeltaWorkload):
         self.cfg = dataclasses.replace(self.cfg, name="delta_net_model_cfg2")
         self.kname = "delta_rule_rows"
 
-    def describe(self, world):
-        d = super().describe(world)
-        d["workload"] = ("%s fwd+bwd (configs[2] shapes, per-element beta as "
-                         "Edifice.build(:delta_net))" % self.cfg.name)
+    def title(self):
+        return ("%s fwd+bwd (configs[2] shapes, per-element beta as Edifice.build(:delta_net))"
+                % self.cfg.name)
+
+    def shape_info(self):
+        d = super().shape_info()
         d["beta"] = "one per (token, head, row) = sigmoid(N(0,1))"
         return d
 
-    def setup(self, dev, rank):
+    def _setup(self, dev):
         import torch
-        super().setup(dev, rank)
-        g = torch.Generator(device=dev).manual_seed(1234 + rank)
+        super()._setup(dev)
+        g = torch.Generator(device=dev).manual_seed(1234 + self.my_units[0])
         self.beta = torch.sigmoid(torch.randn(self.q.shape, generator=g, device=dev)).to(
             self.q.dtype)
 
     def kernels(self):
-        return {"fwd": ("fp32", recurrence_flops(self.cfg, False, False)),
-                "bwd": ("fp32", recurrence_flops(self.cfg, False, True))}
+        f = len(self.my_units) / self.cfg.units
+        return {"fwd": ("fp32", recurrence_flops(self.cfg, False, False) * f),
+                "bwd": ("fp32", recurrence_flops(self.cfg, False, True) * f)}
 
     launches_per_step = 3  # forward (writes the checkpoints), backward, row-sum reduce
 
@@ -758,7 +904,7 @@ class DeltaModelWorkload(DeltaWorkload):
 class GatedDeltaWorkload(DeltaWorkload):
     """GatedDeltaNet (delta rule with a per-token decay alpha) fwd + bwd at the
     configs[2] shapes and distributions, alpha = mean of sigmoid(N(0,1)) gates over
-    head_dim (the model's form).  Token recurrence (SIMT, one CTA per (b, h))."""
+    head_dim (the model's form)."""
 
     def __init__(self):
         import dataclasses
@@ -766,36 +912,36 @@ class GatedDeltaWorkload(DeltaWorkload):
         self.cfg = dataclasses.replace(self.cfg, name="gated_delta_net_cfg2")
         self.kname = "gated_delta_net"
 
-    def describe(self, world):
-        d = super().describe(world)
-        d["workload"] = "%s fwd+bwd (configs[2] shapes, alpha = mean of sigmoid gates)" % (
-            self.cfg.name)
+    def title(self):
+        return "%s fwd+bwd (configs[2] shapes, alpha = mean of sigmoid gates)" % self.cfg.name
+
+    def shape_info(self):
+        d = super().shape_info()
         d["alpha"] = "one per (token, head)"
         return d
 
-    def setup(self, dev, rank):
+    def _setup(self, dev):
         from edifice_b200 import shard
-        super().setup(dev, rank)
-        self.alpha = shard.gated_alpha(self.cfg, self.units, dev)
+        super()._setup(dev)
+        self.alpha = shard.gated_alpha(self.cfg, self.my_units, dev)
 
     def kernels(self):
         # token recurrence on the f32 pipes: algorithmic FLOPs of the recurrence
-        return {"fwd": ("fp32", recurrence_flops(self.cfg, True, False)),
-                "bwd": ("fp32", recurrence_flops(self.cfg, True, True))}
+        f = len(self.my_units) / self.cfg.units
+        return {"fwd": ("fp32", recurrence_flops(self.cfg, True, False) * f),
+                "bwd": ("fp32", recurrence_flops(self.cfg, True, True) * f)}
 
     launches_per_step = 3  # forward (writes the checkpoints), backward, row-sum reduce
 
-    def step(self, ev=None):
+    def fwd(self):
         from edifice_b200 import fused_scan as fs
-        if ev:
-            ev[0].record()
-        _, ck = fs.gated_delta_net_scan(self.q, self.k, self.v, self.beta, self.alpha,
-                                        with_ckpt=True)
-        if ev:
-            ev[1].record()
-        fs.gated_delta_net_backward(self.q, self.k, self.v, self.beta, self.alpha, self.do, ck)
-        if ev:
-            ev[2].record()
+        return fs.gated_delta_net_scan(self.q, self.k, self.v, self.beta, self.alpha,
+                                       with_ckpt=True)[1]
+
+    def bwd(self, ck):
+        from edifice_b200 import fused_scan as fs
+        return fs.gated_delta_net_backward(self.q, self.k, self.v, self.beta, self.alpha,
+                                           self.do, ck)
 
     def host_inputs(self):
         return [self.q, self.k, self.v, self.beta, self.alpha, self.do]
@@ -806,7 +952,8 @@ class GatedDeltaWorkload(DeltaWorkload):
         o, ck = fs.gated_delta_net_scan(q, k, v, beta, alpha, with_ckpt=True)
         return (o,) + tuple(fs.gated_delta_net_backward(q, k, v, beta, alpha, do, ck))
 
-    api = "edifice_b200.fused_scan.gated_delta_net_scan + gated_delta_net_backward"
+    api = ("edifice_b200.fused_scan.gated_delta_net_scan + gated_delta_net_backward "
+           "(whole-tensor copies in the timed region)")
 
     def extra(self, fwd_ms, bwd_ms):
         return {}
@@ -836,17 +983,18 @@ class GatedDeltaWorkload(DeltaWorkload):
                 "pair over 256 tokens, scaled by the head share")
 
 
-WORKLOADS = {"linear": lambda: ScanWorkload(False), "mingru": lambda: ScanWorkload(True),
-             "ssm": SsmWorkload, "ssm_model": SsmModelWorkload, "attn": AttnWorkload,
-             "laser": LaserWorkload,
-             "delta": DeltaWorkload, "delta_model": DeltaModelWorkload,
-             "gated": GatedDeltaWorkload}
+WORKLOADS = {"ssm": SsmWorkload, "linear": lambda: ScanWorkload(False),
+             "mingru": lambda: ScanWorkload(True), "attn": AttnWorkload,
+             "laser": LaserWorkload, "delta": DeltaWorkload, "delta_model": DeltaModelWorkload,
+             "gated": GatedDeltaWorkload, "ssm_model": SsmModelWorkload,
+             "ssm_cfg0": SsmCfg0Workload}
 
 
 def roofline(wl, kern_ms):
     peaks = measured_peaks()
     work = wl.kernels()
-    dom = max(kern_ms, key=kern_ms.get)
+    timed = {k: v for k, v in kern_ms.items() if work[k][1] > 0 and v > 0}
+    dom = max(timed, key=timed.get)
     bound, amount = work[dom]
     peak, src = peaks[bound]
     scale, unit = RATE[bound]
@@ -859,7 +1007,7 @@ def roofline(wl, kern_ms):
             "unit": unit, "frac": round(achieved / peak, 4), "peak_source": src,
             amount_key: amount, "traffic": ncu_traffic(kname)}
     per = {}
-    for k, ms in kern_ms.items():
+    for k, ms in timed.items():
         b_, a_ = work[k]
         sc, un = RATE[b_]
         rate = a_ / (ms / 1e3) / sc
@@ -869,6 +1017,9 @@ def roofline(wl, kern_ms):
 
 
 def time_steps(wl, K, W, world, dist, torch):
+    """W (>= 3) untimed steps, then K steps bracketed by a barrier and a device
+    synchronise on both sides, timed with CUDA events on the launching stream;
+    the elapsed time and the per-direction means are maxed over ranks."""
     for _ in range(max(3, W)):
         wl.step()
     torch.cuda.synchronize()
@@ -896,6 +1047,68 @@ def time_steps(wl, K, W, world, dist, torch):
     return el, {"fwd": fwd, "bwd": bwd}, t0, t1
 
 
+def time_e2e(wl, args, world, dist, torch, budget_s=3.0):
+    """The same metric end to end through the public API: every step copies its
+    inputs from pinned host memory to the device and its results back (the
+    host-tensor entry points overlap those copies with the kernels chunk by
+    chunk).  Returns the e2e dict (max over ranks)."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    pin, dev_in, outs = [], [], []
+    if wl.active:
+        for x in wl.host_inputs():
+            p = _pinned_like(x)
+            p.copy_(x)
+            pin.append(p)
+        if wl.e2e_host is not None:
+            outs = [torch.empty(s[:-1], dtype=s[-1], pin_memory=True) for s in wl.e2e_outputs()]
+        else:
+            dev_in = [torch.empty_like(x) for x in wl.host_inputs()]
+    torch.cuda.synchronize()
+
+    def one():
+        if not wl.active:
+            return
+        if wl.e2e_host is not None:
+            wl.e2e_host(pin, tuple(outs))
+            return
+        for d_, h_ in zip(dev_in, pin):
+            d_.copy_(h_, non_blocking=True)
+        res = wl.e2e_step(dev_in)
+        if not outs:
+            outs.extend(torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res)
+        for o_, r_ in zip(outs, res):
+            o_.copy_(r_, non_blocking=True)
+
+    t_a = time.perf_counter()
+    for _ in range(3):  # warm-up, as for the device-timed steps
+        one()
+    torch.cuda.synchronize()
+    per = (time.perf_counter() - t_a) / 3
+    n = int(max(3, min(args.e2e_steps, budget_s / max(per, 1e-6))))
+    if world > 1:  # every rank times the same number of steps
+        t = torch.tensor([n], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        n = int(t.item())
+        dist.barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(n):
+        one()
+    e2.record()
+    torch.cuda.synchronize()
+    el2 = s2.elapsed_time(e2)
+    if world > 1:
+        t = torch.tensor([el2], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        el2 = t.item()
+    out = {"value": wl.total_tokens() * n / (el2 / 1000.0), "unit": "tokens/s",
+           "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in pin),
+           "d2h_bytes_per_step": sum(x.numel() * x.element_size() for x in outs),
+           "ms_per_step": el2 / n, "steps": n, "api": wl.api,
+           "bytes_note": "per rank (rank 0)"}
+    return out
+
+
 def time_cpu(wl, budget_s=12.0):
     import oracle as O
     n = cpu_threads()
@@ -919,148 +1132,119 @@ def time_cpu(wl, budget_s=12.0):
 
 
 # ------------------------------------------------------------------ ours
+def measure(name, args, dev, rank, world, dist, torch, K, W, e2e_budget, cpu_budget, main):
+    """Time one config: device steps, e2e, (rank 0, N = 1) CPU baseline."""
+    from edifice_b200 import device_errors
+    wl = make_workload(name, args if main else None)
+    wl.setup(dev, rank, world, args.scaling)
+    sampler = ClockSampler(torch.cuda.current_device()) if main else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    el, km, t0, t1 = time_steps(wl, K, W, world, dist, torch)
+    if sampler:
+        sampler.stop()
+    entry = {"value": wl.total_tokens() * K / (el / 1000.0), "unit": "tokens/s",
+             "ms_per_step": el / K, "steps": K, "config": wl.describe(world, args.scaling),
+             "gpu_launches": wl.launches_per_step * K}
+    if rank == 0:
+        entry["roofline"], entry["kernels"] = roofline(wl, km)
+        entry.update(wl.extra(km["fwd"], km["bwd"]))
+    if main:
+        entry["clocks"] = sampler.summary(t0, t1)
+        entry["_timed"] = (t0, t1)
+    # free the device-timed tensors' work before the e2e copies
+    torch.cuda.synchronize()
+    entry["e2e"] = None if args.no_e2e else time_e2e(wl, args, world, dist, torch,
+                                                     budget_s=e2e_budget)
+    replicate = None
+    if main and args.replicate and world > 1 and hasattr(wl, "forward_output"):
+        replicate = time_replicate(wl, world, dist, torch, dev)
+    if replicate:
+        entry["replicate"] = replicate
+    entry["device_errors"] = device_errors()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        entry["cpu_baseline"] = time_cpu(wl, cpu_budget)
+    elif rank == 0:
+        entry["cpu_baseline"] = None
+    del wl
+    torch.cuda.empty_cache()
+    return entry
+
+
+def time_replicate(wl, world, dist, torch, dev):
+    """Optional replicated output (N > 1): all-gather of the forward output, timed
+    on its own; every rank takes the same collective steps."""
+    from edifice_b200 import shard
+    h = wl.forward_output()
+    shard.all_gather_units(h)
+    torch.cuda.synchronize()
+    dist.barrier()
+    reps = 10
+    s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s3.record()
+    for _ in range(reps):
+        shard.all_gather_units(h)
+    e3.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([s3.elapsed_time(e3) / reps], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item()
+    total = world * h.numel() * h.element_size()
+    return {"what": "all-gather of the forward output along the batch (NCCL)",
+            "bytes_gathered_per_rank": total, "ms": ms,
+            "bus_GB/s": (world - 1) / world * total / (ms / 1e3) / 1e9}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
-    from edifice_b200 import device_errors
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
-    wl = make_workload(args)
-    wl._world = world
-    wl.setup(dev, rank)
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.3)
-    K = args.steps
-    elapsed, kern_ms, t0, t1 = time_steps(wl, K, args.warmup, world, dist, torch)
-    sampler.stop()
-    errs = device_errors()
-
-    # ---- e2e through the public API with host buffers
-    e2e = None
-    if args.e2e_steps > 0:
-        pin = [x.cpu().pin_memory() for x in wl.host_inputs()]
-        dev_in = [torch.empty_like(x) for x in wl.host_inputs()]
-        outs_host = []
-
-        def e2e_step():
-            if hasattr(wl, "e2e_host"):
-                if not outs_host:
-                    outs_host.extend(torch.empty(s_, dtype=pin[0].dtype, pin_memory=True)
-                                     for s_ in wl.e2e_host_shapes())
-                wl.e2e_host(pin, tuple(outs_host))
-                return
-            for d_, h_ in zip(dev_in, pin):
-                d_.copy_(h_, non_blocking=True)
-            res = wl.e2e_step(dev_in)
-            if not outs_host:
-                outs_host.extend(torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res)
-            for o_, r_ in zip(outs_host, res):
-                o_.copy_(r_, non_blocking=True)
-
-        for _ in range(3):  # warm-up, as for the device-timed steps
-            e2e_step()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s2.record()
-        for _ in range(args.e2e_steps):
-            e2e_step()
-        e2.record()
-        torch.cuda.synchronize()
-        el2 = s2.elapsed_time(e2)
-        if world > 1:
-            t = torch.tensor([el2], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            el2 = t.item()
-        e2e = {"value": world * wl.tokens * args.e2e_steps / (el2 / 1000.0), "unit": "tokens/s",
-               "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in pin),
-               "d2h_bytes_per_step": sum(x.numel() * x.element_size() for x in outs_host),
-               "ms_per_step": el2 / args.e2e_steps, "steps": args.e2e_steps, "api": wl.api}
-        del pin, dev_in, outs_host
-
-    # ---- optional replicated output (N > 1): all-gather of the forward output,
-    # timed on its own; every rank takes the same collective steps
-    replicate = None
-    if args.replicate and world > 1 and hasattr(wl, "forward_output"):
-        from edifice_b200 import shard
-        h = wl.forward_output()
-        shard.all_gather_units(h)
-        torch.cuda.synchronize()
-        dist.barrier()
-        reps = 10
-        s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s3.record()
-        for _ in range(reps):
-            shard.all_gather_units(h)
-        e3.record()
-        torch.cuda.synchronize()
-        t = torch.tensor([s3.elapsed_time(e3) / reps], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = t.item()
-        total = world * h.numel() * h.element_size()
-        replicate = {"what": "all-gather of the forward output along the batch (NCCL)",
-                     "bytes_gathered_per_rank": total, "ms": ms,
-                     "bus_GB/s": (world - 1) / world * total / (ms / 1e3) / 1e9}
-        del h
-
-    # ---- other paths (same process, smaller step count)
+    head = measure(args.config, args, dev, rank, world, dist, torch, args.steps, args.warmup,
+                   e2e_budget=8.0, cpu_budget=12.0, main=True)
     paths = {}
-    if args.config == "linear" and not args.no_paths:
-        del wl.a, wl.b, wl.dy
-        torch.cuda.empty_cache()
-        for name in ("mingru", "attn", "laser", "delta", "delta_model", "gated", "ssm",
-                     "ssm_model"):
-            pw = WORKLOADS[name]()
-            pw._world = world
-            pw.setup(dev, rank)
-            kp = max(2, min(K, 20))
-            el_p, km, _, _ = time_steps(pw, kp, 3, world, dist, torch)
-            roof_p, per_p = roofline(pw, km)
-            entry = {"value": world * pw.tokens * kp / (el_p / 1000.0), "unit": "tokens/s",
-                     "ms_per_step": el_p / kp, "steps": kp, "config": pw.describe(world),
-                     "roofline": roof_p, "kernels": per_p,
-                     "gpu_launches": pw.launches_per_step * kp}
-            if hasattr(pw, "extra"):
-                entry.update(pw.extra(km["fwd"], km["bwd"]))
-            paths[pw.cfg.name] = entry
-            del pw
-            torch.cuda.empty_cache()
-        errs |= device_errors()
-
+    if not args.no_paths:
+        for name in CONFIGS:
+            if name == args.config:
+                continue
+            kp = max(2, min(args.steps, 20))
+            e = measure(name, args, dev, rank, world, dist, torch, kp, 3, e2e_budget=3.0,
+                        cpu_budget=4.0, main=False)
+            if rank == 0:
+                paths[WORKLOADS[name]().cfg.name] = e
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
-
-    roof, per_kernel = roofline(wl, kern_ms)
-    cpu = None
-    if world == 1 and not args.no_cpu_baseline:
-        cpu = time_cpu(wl)
+    t0, t1 = head.pop("_timed")
+    errs = head.pop("device_errors") | max([p.pop("device_errors") for p in paths.values()],
+                                           default=0)
+    K = args.steps
     line = {
         "metric": "scan/delta/attn fwd+bwd tokens/s",
-        "value": world * wl.tokens * K / (elapsed / 1000.0), "unit": "tokens/s",
+        "value": head["value"], "unit": "tokens/s",
         "n_gpus": world, "steps": K, "warmup": max(3, args.warmup),
-        "ms_per_step": elapsed / K, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
-        "config": wl.describe(world),
-        "roofline": roof, "kernels": per_kernel, "cpu_baseline": cpu, "e2e": e2e,
-        "gpu_launches": wl.launches_per_step * K,
-        "clocks": sampler.summary(t0, t1),
+        "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+        "scaling": args.scaling, "vs_baseline": None,
+        "dtype": WORKLOADS[args.config]().dtype, "data": "synthetic",
+        "config": head["config"],
+        "roofline": head["roofline"], "kernels": head["kernels"],
+        "cpu_baseline": head["cpu_baseline"], "e2e": head["e2e"],
+        "gpu_launches": head["gpu_launches"],
+        "clocks": head["clocks"],
         "device_errors": errs,
     }
-    if hasattr(wl, "extra"):
-        line.update(wl.extra(kern_ms["fwd"], kern_ms["bwd"]))
-    if replicate:
-        line["replicate"] = replicate
+    for k, v in head.items():
+        if k not in line and k not in ("value", "ms_per_step", "steps"):
+            line[k] = v
     if paths:
         line["paths"] = paths
     print(json.dumps(line), flush=True)
@@ -1072,8 +1256,7 @@ def run_reference(args):
     if rank != 0:
         return
     import oracle as O
-    wl = make_workload(args)
-    wl._world = 1
+    wl = make_workload(args.config, args)
     n = cpu_threads()
     O.set_threads(n)
     t0 = time.perf_counter()
@@ -1096,9 +1279,9 @@ def run_reference(args):
         "impl": "reference",
         "metric": "scan/delta/attn fwd+bwd tokens/s", "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": el * 1000.0 / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": wl.describe(1),
+        "ms_per_step": el * 1000.0 / args.steps, "higher_is_better": True,
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": wl.describe(world, args.scaling),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": n, "kind": "port",
                          "sample": sample + "; oracle f32 restatement of the Nx fallbacks (the "
                                    "reference's Nx/EXLA host path needs Erlang/Elixir, absent "

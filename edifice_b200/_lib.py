@@ -30,6 +30,9 @@ SIGNATURES = {
                                         _vp, _sz, _vp]),
     "edb_mingru_train_host": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp,
                                    _sz, _vp]),
+    "edb_selective_scan_train_host_workspace": (_sz, [_i, _i, _i, _i, _i]),
+    "edb_selective_scan_train_host": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                           _vp, _i, _i, _i, _i, _f, _f, _vp, _sz, _vp]),
     "edb_selective_scan_ckpt_bytes": (_sz, [_i, _i, _i, _i]),
     "edb_selective_scan_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f,
                                     _f, _vp]),

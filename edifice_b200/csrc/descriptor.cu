@@ -23,10 +23,10 @@ size_t align_ws(size_t x) { return (x + kWsAlign - 1) & ~(kWsAlign - 1); }
 
 size_t elem_bytes(int dtype) { return dtype == EDB_BF16 ? 2 : 4; }
 
+// Strides are always the tensor's real element strides: all-zero strides on a
+// tensor of more than one element are a broadcast (gathered as an input,
+// rejected as an output), never a shorthand for "dense".
 bool dense_row_major(const edb_tensor& t) {
-    bool all_zero = true;
-    for (int i = 0; i < t.ndim; ++i) all_zero = all_zero && t.strides[i] == 0;
-    if (all_zero) return true;
     long long expect = 1;
     for (int i = t.ndim - 1; i >= 0; --i) {
         if (t.shape[i] != 1 && t.strides[i] != expect) return false;
@@ -108,8 +108,7 @@ class Plan {
         if (t.ndim != ndim || ndim < 1 || ndim > EDB_MAX_DIMS) return fail(EDB_ERR_BAD_SHAPE);
         for (int i = 0; i < ndim; ++i) {
             if (t.shape[i] != shape[i]) return fail(EDB_ERR_BAD_SHAPE);
-            if (output && t.strides[i] == 0 && t.shape[i] > 1 && !dense_row_major(t))
-                return fail(EDB_ERR_BAD_SHAPE);
+            if (output && t.strides[i] == 0 && t.shape[i] > 1) return fail(EDB_ERR_BAD_SHAPE);
         }
         if (n_ == kMaxSlots) return fail(EDB_ERR_UNSUPPORTED);
         Slot& s = slots_[n_];

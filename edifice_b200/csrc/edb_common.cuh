@@ -10,6 +10,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "edifice_b200.h"
 
 // ---------------------------------------------------------------- errors
@@ -248,7 +250,25 @@ inline int dtype_size(int dtype) { return dtype == EDB_BF16 ? 2 : 4; }
 // SM count of the current device (cached per device).
 int sm_count();
 
-// Device address of the current device's error word (cached per device).
+// Per-device cache of one __device__ symbol's address, keyed on the unique id
+// of the context it was looked up in.
+struct SymbolCache {
+    std::mutex m;
+    unsigned long long ctx_id[64] = {};
+    void* addr[64] = {};
+};
+
+// Device address of a __device__ symbol of this library in the current
+// device's current context (0 or a cudaError_t).  The address is cached per
+// device together with the context's unique id (cuCtxGetId, through the
+// runtime's driver entry point), so a cudaDeviceReset or any other re-creation
+// of the context is noticed and the symbol looked up again; when the id cannot
+// be read the symbol is looked up on every call.  The first lookup in a
+// context may load this library's module: it should not happen inside a
+// stream capture.
+int symbol_address(const void* symbol, SymbolCache& cache, void** out);
+
+// Device address of the current device's error word (see symbol_address).
 unsigned int* device_error_word();
 
 // Map a cudaError_t to the ABI's int status.

@@ -1,14 +1,17 @@
 // host_pipeline.cu -- forward + backward of the diagonal scans (linear scan,
-// MinGRU) over HOST-resident tensors: batch rows are streamed through a small
-// ring of device slots so that the host->device copies of chunk i+1, the scan
-// kernels of chunk i and the device->host copies of chunk i-1 run at the same
-// time (the two copy directions use separate copy engines; PCIe is full duplex).
+// MinGRU) and of the Mamba selective scan over HOST-resident tensors: batch
+// rows are streamed through a small ring of device slots so that the
+// host->device copies of chunk i+1, the kernels of chunk i and the
+// device->host copies of chunk i-1 run at the same time (the two copy
+// directions use separate copy engines; PCIe is full duplex).
 //
-// The scans are independent per batch row, so a chunk of rows is a complete
+// Every op here is independent per batch row, so a chunk of rows is a complete
 // sub-problem and the results equal those of one whole-batch call.  Ordering:
 // the helper streams first wait for everything already queued on the caller's
-// stream, and the caller's stream finally waits for the last copy, so the call
-// behaves like any other stream-ordered entry point.
+// stream, and the caller's stream finally waits for both helper streams (on
+// every exit path once a copy was queued, errors included), so the call behaves
+// like any other stream-ordered entry point: once the caller's stream has
+// passed the call, no copy into or out of the caller's host buffers is pending.
 #include <cstdint>
 
 #include "edb_common.cuh"
@@ -22,14 +25,18 @@ enum { HOST_LINEAR = 0, HOST_MINGRU = 1 };
 
 size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-int chunk_rows(int B, int L, int H, int esize) {
-    const size_t row = (size_t)L * H * esize;
-    size_t r = row >= kChunkTarget ? 1 : kChunkTarget / row;
-    // keep at least ~4 chunks in flight when the batch allows it
+// Rows per chunk: about `target` bytes per [rows, L, H] tensor, but at least ~4
+// chunks in flight when the batch allows it.
+int chunk_rows(int B, size_t row_bytes, size_t target) {
+    size_t r = row_bytes >= target ? 1 : target / row_bytes;
     const size_t quarter = ((size_t)B + 3) / 4;
     if (r > quarter) r = quarter;
     if (r < 1) r = 1;
     return (int)r;
+}
+
+int chunk_rows(int B, int L, int H, int esize) {
+    return chunk_rows(B, (size_t)L * H * esize, kChunkTarget);
 }
 
 // One slot: x0, x1, dy, h, g0, g1 ([rows, L, H]) then h0, gh0 ([rows, H]).
@@ -48,14 +55,14 @@ int check_shape(int dtype, int B, int L, int H) {
 
 struct Res {
     cudaStream_t sin = nullptr, sout = nullptr;
-    cudaEvent_t start = nullptr, done = nullptr;
+    cudaEvent_t start = nullptr, done_in = nullptr, done = nullptr;
     cudaEvent_t in_fwd[kSlots] = {}, in[kSlots] = {}, fwd[kSlots] = {}, comp[kSlots] = {},
                 free_[kSlots] = {};
     ~Res() {
         // destruction is deferred by the runtime until queued work completes
         if (sin) cudaStreamDestroy(sin);
         if (sout) cudaStreamDestroy(sout);
-        for (cudaEvent_t e : {start, done})
+        for (cudaEvent_t e : {start, done_in, done})
             if (e) cudaEventDestroy(e);
         for (int i = 0; i < kSlots; ++i)
             for (cudaEvent_t e : {in_fwd[i], in[i], fwd[i], comp[i], free_[i]})
@@ -65,16 +72,27 @@ struct Res {
         cudaError_t e;
         if ((e = cudaStreamCreateWithFlags(&sin, cudaStreamNonBlocking))) return e;
         if ((e = cudaStreamCreateWithFlags(&sout, cudaStreamNonBlocking))) return e;
-        if ((e = cudaEventCreateWithFlags(&start, cudaEventDisableTiming))) return e;
-        if ((e = cudaEventCreateWithFlags(&done, cudaEventDisableTiming))) return e;
-        for (int i = 0; i < kSlots; ++i) {
-            if ((e = cudaEventCreateWithFlags(&in_fwd[i], cudaEventDisableTiming))) return e;
-            if ((e = cudaEventCreateWithFlags(&in[i], cudaEventDisableTiming))) return e;
-            if ((e = cudaEventCreateWithFlags(&fwd[i], cudaEventDisableTiming))) return e;
-            if ((e = cudaEventCreateWithFlags(&comp[i], cudaEventDisableTiming))) return e;
-            if ((e = cudaEventCreateWithFlags(&free_[i], cudaEventDisableTiming))) return e;
-        }
+        for (cudaEvent_t* ev : {&start, &done_in, &done})
+            if ((e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming))) return e;
+        for (int i = 0; i < kSlots; ++i)
+            for (cudaEvent_t* ev : {&in_fwd[i], &in[i], &fwd[i], &comp[i], &free_[i]})
+                if ((e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming))) return e;
         return cudaSuccess;
+    }
+};
+
+// Makes the caller's stream wait for both helper streams when it goes out of
+// scope, on the success path and on every error path after the first copy was
+// queued: a caller that synchronises its stream after an error status then
+// knows that no copy into or out of its host buffers is still pending.
+struct Join {
+    Res& r;
+    cudaStream_t s;
+    bool armed = false;
+    ~Join() {
+        if (!armed) return;
+        if (cudaEventRecord(r.done_in, r.sin) == cudaSuccess) cudaStreamWaitEvent(s, r.done_in, 0);
+        if (cudaEventRecord(r.done, r.sout) == cudaSuccess) cudaStreamWaitEvent(s, r.done, 0);
     }
 };
 
@@ -88,6 +106,9 @@ struct Res {
         int st_ = (expr);           \
         if (st_ != EDB_OK) return st_; \
     } while (0)
+
+const char* hp(const void* p, size_t o) { return static_cast<const char*>(p) + o; }
+char* hq(void* p, size_t o) { return static_cast<char*>(p) + o; }
 
 // x0/x1: (a, b) for the linear scan, (z, c) for MinGRU.  g0/g1 likewise.
 int run(int op, int dtype, const void* x0, const void* x1, const void* h0, const void* dy,
@@ -106,9 +127,11 @@ int run(int op, int dtype, const void* x0, const void* x1, const void* h0, const
     cudaStream_t s = (cudaStream_t)stream;
     Res r;
     EDB_TRY(r.init());
+    Join join{r, s};
     EDB_TRY(cudaEventRecord(r.start, s));
     EDB_TRY(cudaStreamWaitEvent(r.sin, r.start, 0));
     EDB_TRY(cudaStreamWaitEvent(r.sout, r.start, 0));
+    join.armed = true;
 
     const int nchunks = (B + rows - 1) / rows;
     for (int i = 0; i < nchunks; ++i) {
@@ -125,8 +148,6 @@ int run(int op, int dtype, const void* x0, const void* x1, const void* h0, const
         void* dgh0 = base + 6 * tb + hb;
         const size_t off = (size_t)r0 * L * H * es, n = (size_t)nr * L * H * es;
         const size_t off0 = (size_t)r0 * H * es, n0 = (size_t)nr * H * es;
-        auto hp = [](const void* p, size_t o) { return static_cast<const char*>(p) + o; };
-        auto hq = [](void* p, size_t o) { return static_cast<char*>(p) + o; };
 
         // host -> device, once the slot's previous chunk has been copied out: the
         // forward's inputs first, so that the forward (and the copy of h back to the
@@ -165,10 +186,122 @@ int run(int op, int dtype, const void* x0, const void* x1, const void* h0, const
         if (gh0) EDB_TRY(cudaMemcpyAsync(hq(gh0, off0), dgh0, n0, cudaMemcpyDeviceToHost, r.sout));
         EDB_TRY(cudaEventRecord(r.free_[slot], r.sout));
     }
-    // the caller's stream completes only after every result has reached the host
-    EDB_TRY(cudaEventRecord(r.done, r.sout));
-    EDB_TRY(cudaStreamWaitEvent(s, r.done, 0));
+    return EDB_OK;  // `join` makes the caller's stream wait for the last copies
+}
+
+// ------------------------------------------------------------ selective scan
+// A chunk of the selective scan is far more work per byte than a diagonal-scan
+// chunk and its kernels want many rows at once (32 CTAs per row at d_inner =
+// 4096), so its chunks aim at ~256 MiB per [rows, L, D] tensor.
+constexpr size_t kSsmChunkTarget = 256u << 20;
+
+struct SsmSlot {
+    size_t td, tn, tf, ck, ws;  // [rows,L,D] io, [rows,L,N] io, [rows,L,N] f32, ckpt, bwd ws
+    size_t bytes() const { return 6 * td + 2 * tn + 2 * tf + ck + ws; }
+};
+
+int ssm_rows(int B, int L, int D, int es) {
+    return chunk_rows(B, (size_t)L * D * es, kSsmChunkTarget);
+}
+
+SsmSlot ssm_slot(int rows, int L, int D, int N, int es) {
+    SsmSlot g;
+    g.td = a256((size_t)rows * L * D * es);
+    g.tn = a256((size_t)rows * L * N * es);
+    g.tf = a256((size_t)rows * L * N * 4);
+    g.ck = a256(edb_selective_scan_ckpt_bytes(rows, L, D, N));
+    g.ws = a256(edb_selective_scan_bwd_workspace(rows, L, D, N, 1));
+    return g;
+}
+
+int check_ssm(int dtype, int B, int L, int D, int N) {
+    if (dtype != EDB_F32 && dtype != EDB_BF16) return EDB_ERR_BAD_DTYPE;
+    if (B <= 0 || L <= 0 || D <= 0 || N <= 0 || N > 16) return EDB_ERR_BAD_SHAPE;
+    if ((long long)B * L > 0x7fffffffLL) return EDB_ERR_BAD_SHAPE;
     return EDB_OK;
+}
+
+int run_ssm(int dtype, const void* x, const void* dt, const void* A, const void* Bm,
+            const void* Cm, const void* dy, void* y, void* gx, void* gdt, float* gB, float* gC,
+            int B, int L, int D, int N, float dt_min, float dt_max, void* ws, size_t ws_bytes,
+            void* stream) {
+    if (int st = check_ssm(dtype, B, L, D, N)) return st;
+    if (!x || !dt || !A || !Bm || !Cm || !dy || !y || !gx || !gdt || !gB || !gC || !ws)
+        return EDB_ERR_NULL_POINTER;
+    const int es = dtype == EDB_BF16 ? 2 : 4;
+    const int rows = ssm_rows(B, L, D, es);
+    const SsmSlot g = ssm_slot(rows, L, D, N, es);
+    const size_t ab = a256((size_t)D * N * es);
+    if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0) return EDB_ERR_MISALIGNED;
+    if (ws_bytes < ab + kSlots * g.bytes()) return EDB_ERR_WORKSPACE_TOO_SMALL;
+
+    cudaStream_t s = (cudaStream_t)stream;
+    Res r;
+    EDB_TRY(r.init());
+    Join join{r, s};
+    EDB_TRY(cudaEventRecord(r.start, s));
+    EDB_TRY(cudaStreamWaitEvent(r.sin, r.start, 0));
+    EDB_TRY(cudaStreamWaitEvent(r.sout, r.start, 0));
+    join.armed = true;
+
+    // A [D, N] is shared by every row: one copy ahead of the first chunk
+    void* dA = ws;
+    EDB_TRY(cudaMemcpyAsync(dA, A, (size_t)D * N * es, cudaMemcpyHostToDevice, r.sin));
+
+    const int nchunks = (B + rows - 1) / rows;
+    for (int i = 0; i < nchunks; ++i) {
+        const int slot = i % kSlots;
+        const int r0 = i * rows, nr = B - r0 < rows ? B - r0 : rows;
+        char* p = static_cast<char*>(ws) + ab + slot * g.bytes();
+        void* dx = p;
+        void* ddt = p + g.td;
+        void* ddy = p + 2 * g.td;
+        void* dyo = p + 3 * g.td;
+        void* dgx = p + 4 * g.td;
+        void* dgdt = p + 5 * g.td;
+        void* dB = p + 6 * g.td;
+        void* dC = p + 6 * g.td + g.tn;
+        float* dgB = reinterpret_cast<float*>(p + 6 * g.td + 2 * g.tn);
+        float* dgC = reinterpret_cast<float*>(p + 6 * g.td + 2 * g.tn + g.tf);
+        float* dck = reinterpret_cast<float*>(p + 6 * g.td + 2 * g.tn + 2 * g.tf);
+        void* dws = p + 6 * g.td + 2 * g.tn + 2 * g.tf + g.ck;
+        const size_t offd = (size_t)r0 * L * D * es, nd = (size_t)nr * L * D * es;
+        const size_t offn = (size_t)r0 * L * N * es, nn = (size_t)nr * L * N * es;
+        const size_t offf = (size_t)r0 * L * N, nf = (size_t)nr * L * N * 4;
+
+        // host -> device once the slot's previous chunk has left: the forward's
+        // inputs first, dY after them
+        if (i >= kSlots) EDB_TRY(cudaStreamWaitEvent(r.sin, r.free_[slot], 0));
+        EDB_TRY(cudaMemcpyAsync(dx, hp(x, offd), nd, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaMemcpyAsync(ddt, hp(dt, offd), nd, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaMemcpyAsync(dB, hp(Bm, offn), nn, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaMemcpyAsync(dC, hp(Cm, offn), nn, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaEventRecord(r.in_fwd[slot], r.sin));
+        EDB_TRY(cudaMemcpyAsync(ddy, hp(dy, offd), nd, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaEventRecord(r.in[slot], r.sin));
+
+        // forward (writing the chunk-start states), then backward, on the caller's stream
+        EDB_TRY(cudaStreamWaitEvent(s, r.in_fwd[slot], 0));
+        EDB_TRY_ST(edb_selective_scan_fwd(dtype, dx, ddt, dA, dB, dC, dyo, dck, nr, L, D, N,
+                                          dt_min, dt_max, s));
+        EDB_TRY(cudaEventRecord(r.fwd[slot], s));
+        EDB_TRY(cudaStreamWaitEvent(s, r.in[slot], 0));
+        EDB_TRY_ST(edb_selective_scan_bwd(dtype, dx, ddt, dA, dB, dC, ddy, dck, dgx, dgdt, dgB,
+                                          dgC, nr, L, D, N, dt_min, dt_max, dws, g.ws, s));
+        EDB_TRY(cudaEventRecord(r.comp[slot], s));
+
+        // device -> host: y as soon as the forward is done, the gradients after
+        // the backward
+        EDB_TRY(cudaStreamWaitEvent(r.sout, r.fwd[slot], 0));
+        EDB_TRY(cudaMemcpyAsync(hq(y, offd), dyo, nd, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaStreamWaitEvent(r.sout, r.comp[slot], 0));
+        EDB_TRY(cudaMemcpyAsync(hq(gx, offd), dgx, nd, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaMemcpyAsync(hq(gdt, offd), dgdt, nd, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaMemcpyAsync(gB + offf, dgB, nf, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaMemcpyAsync(gC + offf, dgC, nf, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaEventRecord(r.free_[slot], r.sout));
+    }
+    return EDB_OK;  // `join` makes the caller's stream wait for the last copies
 }
 
 }  // namespace
@@ -194,4 +327,24 @@ extern "C" int edb_mingru_train_host(int dtype, const void* z, const void* c, co
                                      size_t workspace_bytes, void* stream) {
     return run(HOST_MINGRU, dtype, z, c, h0, dy, h, gz, gc, gh0, batch, seq_len, hidden,
                workspace, workspace_bytes, stream);
+}
+
+extern "C" size_t edb_selective_scan_train_host_workspace(int dtype, int batch, int seq_len,
+                                                          int d_inner, int d_state) {
+    if (check_ssm(dtype, batch, seq_len, d_inner, d_state) != EDB_OK) return 0;
+    const int es = dtype == EDB_BF16 ? 2 : 4;
+    const int rows = ssm_rows(batch, seq_len, d_inner, es);
+    return a256((size_t)d_inner * d_state * es) +
+           kSlots * ssm_slot(rows, seq_len, d_inner, d_state, es).bytes();
+}
+
+extern "C" int edb_selective_scan_train_host(int dtype, const void* x, const void* dt,
+                                             const void* A, const void* B, const void* C,
+                                             const void* dy, void* y, void* gx, void* gdt,
+                                             float* gB, float* gC, int batch, int seq_len,
+                                             int d_inner, int d_state, float dt_min,
+                                             float dt_max, void* workspace,
+                                             size_t workspace_bytes, void* stream) {
+    return run_ssm(dtype, x, dt, A, B, C, dy, y, gx, gdt, gB, gC, batch, seq_len, d_inner,
+                   d_state, dt_min, dt_max, workspace, workspace_bytes, stream);
 }

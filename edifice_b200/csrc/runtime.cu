@@ -42,16 +42,70 @@ CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t ra
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
-unsigned int* device_error_word() {
-    static unsigned int* cache[64] = {nullptr};
+namespace {
+
+using PFN_ctx_current = CUresult (*)(CUcontext*);
+using PFN_ctx_id = CUresult (*)(CUcontext, unsigned long long*);
+PFN_ctx_current g_ctx_current = nullptr;
+PFN_ctx_id g_ctx_id = nullptr;
+std::once_flag g_ctx_once;
+
+// Unique id of the calling thread's current context, 0 if none or unknown.
+unsigned long long current_context_id() {
+    std::call_once(g_ctx_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) ==
+                cudaSuccess && q == cudaDriverEntryPointSuccess)
+            g_ctx_current = reinterpret_cast<PFN_ctx_current>(fn);
+        fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_ctx_id = reinterpret_cast<PFN_ctx_id>(fn);
+    });
+    if (!g_ctx_current || !g_ctx_id) return 0;
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (g_ctx_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+    if (g_ctx_id(ctx, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
+
+SymbolCache g_error_word_cache;
+
+}  // namespace
+
+int symbol_address(const void* symbol, SymbolCache& cache, void** out) {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    if (!cache[dev]) {
-        void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_edb_device_errors) == cudaSuccess)
-            cache[dev] = static_cast<unsigned int*>(p);
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    const bool cacheable = dev >= 0 && dev < 64;
+    unsigned long long id = current_context_id();
+    if (cacheable && id != 0) {
+        std::lock_guard<std::mutex> lk(cache.m);
+        if (cache.ctx_id[dev] == id && cache.addr[dev] != nullptr) {
+            *out = cache.addr[dev];
+            return EDB_OK;
+        }
     }
-    return cache[dev];
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, symbol);
+    if (e != cudaSuccess) return (int)e;
+    if (p == nullptr) return EDB_ERR_UNSUPPORTED;
+    id = current_context_id();  // the lookup makes the primary context current
+    if (cacheable && id != 0) {
+        std::lock_guard<std::mutex> lk(cache.m);
+        cache.ctx_id[dev] = id;
+        cache.addr[dev] = p;
+    }
+    *out = p;
+    return EDB_OK;
+}
+
+unsigned int* device_error_word() {
+    void* p = nullptr;
+    if (symbol_address(&g_edb_device_errors, g_error_word_cache, &p) != EDB_OK) return nullptr;
+    return static_cast<unsigned int*>(p);
 }
 
 int sm_count() {

@@ -25,8 +25,6 @@
 //     transpose-reduce, cross-warp sum in shared memory, one partial per
 //     (channel block, b, t, n) to the workspace, then a second kernel sums the
 //     channel-block partials in a fixed order.  No atomics.
-#include <atomic>
-
 #include "edb_common.cuh"
 
 namespace {
@@ -1048,29 +1046,18 @@ extern "C" int edb_selective_scan_model_bwd(int dtype, const void* x, const void
 // Scratch of edb_selective_scan_bwd_noalloc: a fixed array inside the library,
 // one per device, so that callers which must not allocate device memory can
 // still run the backward.  Host code cannot use the symbol itself as a device
-// address (on the host it names a host-side stand-in); the address is looked
-// up once per device with cudaGetSymbolAddress, the device being current.
+// address (on the host it names a host-side stand-in): the address comes from
+// cudaGetSymbolAddress with the device current, on the first call in each
+// context (edb::symbol_address caches it per device, keyed on the context's
+// unique id, so a device reset is noticed and the address looked up again).
 static __device__ __align__(256) unsigned char g_ssm_noalloc_scratch[EDB_SSM_NOALLOC_SCRATCH_BYTES];
 
 namespace {
 
-constexpr int kMaxDevices = 64;
-std::atomic<void*> g_ssm_noalloc_addr[kMaxDevices];
+edb::SymbolCache g_ssm_noalloc_cache;
 
 int ssm_noalloc_scratch(void** out) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return (int)e;
-    if (dev < 0 || dev >= kMaxDevices) return EDB_ERR_UNSUPPORTED;
-    void* p = g_ssm_noalloc_addr[dev].load(std::memory_order_acquire);
-    if (p == nullptr) {
-        e = cudaGetSymbolAddress(&p, g_ssm_noalloc_scratch);
-        if (e != cudaSuccess) return (int)e;
-        if (p == nullptr) return EDB_ERR_UNSUPPORTED;
-        g_ssm_noalloc_addr[dev].store(p, std::memory_order_release);
-    }
-    *out = p;
-    return EDB_OK;
+    return edb::symbol_address(g_ssm_noalloc_scratch, g_ssm_noalloc_cache, out);
 }
 
 }  // namespace

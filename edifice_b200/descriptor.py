@@ -84,15 +84,27 @@ ARGS = {"linear_scan": LinearScanArgs, "mingru": MinGRUArgs,
 _DTYPES = {torch.float32: _lib.EDB_F32, torch.bfloat16: _lib.EDB_BF16}
 
 
+def dense_strides(shape):
+    """Element strides of a dense row-major array of `shape`."""
+    out, acc = [], 1
+    for n in reversed(shape):
+        out.append(acc)
+        acc *= n
+    return tuple(reversed(out))
+
+
 def tensor(data, dtype, shape, strides=None):
-    """An edb_tensor from a raw device address (strides in elements; None = dense)."""
+    """An edb_tensor from a raw device address (strides in elements; None = the
+    dense row-major strides of `shape`).  The library reads strides literally: a
+    zero stride on an extent > 1 is a broadcast."""
     t = Tensor()
     t.data = data
     t.dtype = dtype
     t.ndim = len(shape)
+    strides = dense_strides(shape) if strides is None else strides
     for i, n in enumerate(shape):
         t.shape[i] = n
-        t.strides[i] = 0 if strides is None else strides[i]
+        t.strides[i] = strides[i]
     return t
 
 

@@ -334,6 +334,44 @@ def selective_scan_backward(x, dt, a, b, c, grad_output, h_ckpt=None):
     return gx, gdt, gB, gC
 
 
+def selective_scan_train_host(x, dt, a, b, c, grad_output, out=None, device=None):
+    """Forward and backward of the selective scan (kernel semantics) for
+    host-resident tensors, the copies overlapped with the kernels batch-row chunk
+    by chunk.  Returns host tensors (y, grad_x, grad_dt, grad_B, grad_C), written
+    into ``out`` when given (y, grad_x, grad_dt in the input dtype, grad_B and
+    grad_C f32).  Asynchronous on the current stream of ``device``: synchronise it
+    before reading the results.  Inputs and outputs should be pinned for the
+    copies to overlap."""
+    what = "selective_scan_train_host"
+    for t in (x, dt, a, b, c, grad_output):
+        if t.is_cuda or not t.is_contiguous():
+            raise _lib.EdbError("%s: inputs must be contiguous host tensors" % what)
+    Bsz, L, D, N = _ssm_shapes(x, a, b)
+    _same(x.shape, dt.shape, what)
+    _same(x.shape, grad_output.shape, what)
+    _same(b.shape, c.shape, what)
+    if out is None:
+        out = tuple(torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for _ in range(3)) + \
+            tuple(torch.empty((Bsz, L, N), dtype=torch.float32, pin_memory=True)
+                  for _ in range(2))
+    dts = (x.dtype,) * 3 + (torch.float32,) * 2
+    for o, want in zip(out, dts):
+        if o.is_cuda or not o.is_contiguous() or o.dtype != want:
+            raise _lib.EdbError("%s: outputs must be contiguous host tensors (y, gx, gdt in "
+                                "the input dtype, gB, gC f32)" % what)
+    device = torch.device(device if device is not None else "cuda")
+    dt_code = _dtype_code(x, what)
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        nbytes = lib.edb_selective_scan_train_host_workspace(dt_code, Bsz, L, D, N)
+        ws = _host_ws(device, nbytes)
+        _lib.check(lib.edb_selective_scan_train_host(
+            dt_code, _p(x), _p(dt), _p(a), _p(b), _p(c), _p(grad_output), _p(out[0]),
+            _p(out[1]), _p(out[2]), _p(out[3]), _p(out[4]), Bsz, L, D, N, DT_MIN, DT_MAX,
+            _p(ws), nbytes, _stream()), "CUDA fused selective scan over host tensors")
+    return out
+
+
 def _model_shapes(x, a, b):
     Bsz, L, D = x.shape
     N = b.shape[2]

@@ -3,11 +3,15 @@
 One process per GPU.  Every config partitions into independent units (batch
 rows for the scans and Mamba, (batch, head) pairs for DeltaNet, (batch,
 kv-group) for GQA attention); ranks never exchange data on the kernel path.
-Weak scaling: every rank processes a full config-sized shard of its own units,
-so the global problem at N GPUs is N shards of units [rank*U, (rank+1)*U).
+Two plans:
+  strong  the config's fixed problem is split over the ranks: rank r owns the
+          contiguous units split_units(U, N)[r] (configs[4]: 64 batch rows ->
+          8 per GPU at N = 8);
+  weak    every rank processes a full config-sized shard of its own units, so
+          the global problem at N GPUs is N shards of units [r*U, (r+1)*U).
 
 Inputs of unit u are drawn from a generator seeded with (base_seed, u), so a
-unit's data are identical whatever the world size.
+unit's data are identical whatever the world size and plan.
 """
 import dataclasses
 import math
@@ -64,14 +68,18 @@ class SsmConfig:
         return self.batch * self.seq_len
 
     def bytes_fwd(self):
+        """read x, dt, B, C, A; write y"""
+        es = torch.finfo(self.dtype).bits // 8
         e = self.batch * self.seq_len * self.d_inner
         bc = self.batch * self.seq_len * self.d_state
-        return 3 * e * 2 + 2 * bc * 2 + self.d_inner * self.d_state * 2
+        return 3 * e * es + 2 * bc * es + self.d_inner * self.d_state * es
 
     def bytes_bwd(self):
+        """read x, dt, dY, B, C, A; write dx, ddt (io dtype), dB, dC (f32)"""
+        es = torch.finfo(self.dtype).bits // 8
         e = self.batch * self.seq_len * self.d_inner
         bc = self.batch * self.seq_len * self.d_state
-        return 5 * e * 2 + 2 * bc * 2 + 2 * bc * 4 + self.d_inner * self.d_state * 2
+        return 5 * e * es + 2 * bc * es + 2 * bc * 4 + self.d_inner * self.d_state * es
 
     def exps_fwd(self):
         """exp(dt A) evaluations of the forward: one per (b, t, d, n)."""
@@ -82,6 +90,13 @@ class SsmConfig:
         sub-chunk start states from the chunk checkpoint, one to recompute each
         sub-chunk (its exp(dt A) then serves the reverse walk)."""
         return 2 * self.exps_fwd()
+
+
+def ssm_cfg0():
+    """the Mamba selective-scan forward the reference runs on
+    its CPU host backend, f32, batch 2 x seq 256 x d_inner 512, d_state 16."""
+    return SsmConfig(name="selective_scan_cfg0", batch=2, seq_len=256, d_inner=512, d_state=16,
+                     dtype=torch.float32)
 
 
 @dataclasses.dataclass(frozen=True)
@@ -162,6 +177,20 @@ def plan_units(n_units_per_rank, rank, world_size):
     return list(range(lo, lo + n_units_per_rank))
 
 
+def units_for(n_units, rank, world_size, scaling="strong"):
+    """The global unit indices rank `rank` processes under `scaling` ("strong":
+    its contiguous share of the config's n_units; "weak": a full config of its
+    own).  A strong split may leave a rank with no units (world > n_units)."""
+    if scaling == "weak":
+        return plan_units(n_units, rank, world_size)
+    if scaling != "strong":
+        raise ValueError("scaling must be 'strong' or 'weak'")
+    if world_size < 1 or not (0 <= rank < world_size):
+        raise ValueError("bad rank/world_size")
+    start, count = split_units(n_units, world_size)[rank]
+    return list(range(start, start + count))
+
+
 def split_units(n_units, world_size):
     """Strong-scaling split of n_units over world_size ranks (contiguous, sizes
     differ by at most one).  Returns a list of (start, count)."""
@@ -214,29 +243,49 @@ def ssm_inputs(cfg, units, device, base_seed=0):
 
 def attn_inputs(cfg, units, device, base_seed=0):
     """configs[3] per (batch, kv-group) unit: q, k, v, dO ~ N(0,1).  The rank's
-    units are laid out as a [len(units)/kv_heads, heads, L, d] batch."""
+    units are laid out unit-major, q/dO [U, G, L, d] and k/v [U, 1, L, d] (G query
+    heads per kv head), which is byte for byte the reference's [B, Hq, L, d] /
+    [B, Hkv, L, d] layout of whole batches; when the units make whole batches the
+    tensors are returned in that [U/Hkv, Hq, L, d] / [U/Hkv, Hkv, L, d] form."""
     G = cfg.q_heads // cfg.kv_heads
     L, d = cfg.seq_len, cfg.head_dim
-    nb = len(units) // cfg.kv_heads
-    q = torch.empty((nb, cfg.q_heads, L, d), dtype=cfg.dtype, device=device)
+    U = len(units)
+    q = torch.empty((U, G, L, d), dtype=cfg.dtype, device=device)
     do = torch.empty_like(q)
-    k = torch.empty((nb, cfg.kv_heads, L, d), dtype=cfg.dtype, device=device)
+    k = torch.empty((U, 1, L, d), dtype=cfg.dtype, device=device)
     v = torch.empty_like(k)
     for i, u in enumerate(units):
-        b, hk = divmod(i, cfg.kv_heads)
         g = torch.Generator(device=device).manual_seed(unit_seed(base_seed, u))
-        q[b, hk * G:(hk + 1) * G].copy_(torch.randn((G, L, d), generator=g, device=device))
-        k[b, hk].copy_(torch.randn((L, d), generator=g, device=device))
-        v[b, hk].copy_(torch.randn((L, d), generator=g, device=device))
-        do[b, hk * G:(hk + 1) * G].copy_(torch.randn((G, L, d), generator=g, device=device))
+        q[i].copy_(torch.randn((G, L, d), generator=g, device=device))
+        k[i, 0].copy_(torch.randn((L, d), generator=g, device=device))
+        v[i, 0].copy_(torch.randn((L, d), generator=g, device=device))
+        do[i].copy_(torch.randn((G, L, d), generator=g, device=device))
+    if U % cfg.kv_heads == 0 and all(u % cfg.kv_heads == i % cfg.kv_heads
+                                     for i, u in enumerate(units)):
+        nb = U // cfg.kv_heads
+        q, do = (t.view(nb, cfg.q_heads, L, d) for t in (q, do))
+        k, v = (t.view(nb, cfg.kv_heads, L, d) for t in (k, v))
     return q, k, v, do
+
+
+def _delta_heads(cfg, units):
+    """Heads per batch entry of a rank's (batch, head) units: whole batches keep
+    cfg.heads; a run of consecutive heads of one batch becomes one batch entry."""
+    U, H = len(units), cfg.heads
+    if U % H == 0:
+        return H
+    if H % U == 0 and units[0] // H == units[-1] // H:
+        return U
+    raise ValueError("a rank's (batch, head) units must be whole batches or part of one")
 
 
 def delta_inputs(cfg, units, device, base_seed=0):
     """configs[2] per (batch, head) unit: q, k ~ N(0,1), k L2-normalised over d;
     v ~ N(0,1); beta = sigmoid(N(0,1)) per token; dO ~ N(0,1).  The rank's units
-    are laid out as a [len(units)/heads, L, heads, d] batch."""
-    L, H, d = cfg.seq_len, cfg.heads, cfg.head_dim
+    are laid out as a [len(units)/Hl, L, Hl, d] batch, Hl = heads for whole
+    batches, else the number of units (consecutive heads of one batch)."""
+    L, d = cfg.seq_len, cfg.head_dim
+    H = _delta_heads(cfg, units)
     nb = len(units) // H
     q = torch.empty((nb, L, H, d), dtype=cfg.dtype, device=device)
     k, v, do = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
@@ -258,8 +307,9 @@ def gated_alpha(cfg, units, device, base_seed=0):
     heads]: the mean over head_dim of sigmoid(N(0,1)) gates, the model's form
     (lib/edifice/recurrent/gated_delta_net.ex:382-389), drawn after that unit's
     delta_inputs stream (a separate generator offset, so the q/k/v/beta/dO draws
-    are the configs[2] ones)."""
-    L, H, d = cfg.seq_len, cfg.heads, cfg.head_dim
+    are the configs[2] ones).  Laid out as delta_inputs lays out the units."""
+    L, d = cfg.seq_len, cfg.head_dim
+    H = _delta_heads(cfg, units)
     nb = len(units) // H
     alpha = torch.empty((nb, L, H), dtype=cfg.dtype, device=device)
     for i, u in enumerate(units):

@@ -125,7 +125,9 @@ int edb_native_rec_fwd(int kind, int dtype, const void* x0, const void* x1, cons
  * that host->device copies, the kernels above and device->host copies of
  * successive row chunks overlap.  Host buffers should be page-locked
  * (cudaHostAlloc / cudaHostRegister) for the copies to overlap.  Stream-ordered:
- * the results are on the host once `stream` has reached this point.
+ * the results are on the host once `stream` has reached this point; after an
+ * error status no copy into or out of the host buffers is left pending once
+ * `stream` has reached this point either.
  * Results are those of edb_<op>_fwd followed by edb_<op>_bwd on the whole batch.
  * Replaces the host-side round trip a caller with host-resident Nx tensors makes
  * around fused_linear_scan_launch / fused_mingru_scan_launch (and their
@@ -181,6 +183,31 @@ int edb_selective_scan_bwd(int dtype, const void* x, const void* dt, const void*
                            float* gB, float* gC, int batch, int seq_len, int d_inner, int d_state,
                            float dt_min, float dt_max, void* workspace, size_t workspace_bytes,
                            void* stream);
+
+/* Forward (with chunk-start states) + backward of the selective scan over HOST
+ * tensors, kernel semantics as above: x, dt, dy and the outputs y, gx, gdt
+ * [batch, seq_len, d_inner] and B, C [batch, seq_len, d_state] in `dtype`, gB,
+ * gC f32 [batch, seq_len, d_state], A [d_inner, d_state] in `dtype`, all in host
+ * memory (page-locked for the copies to overlap).  Batch rows stream through a
+ * ring of device slots in `workspace`
+ * (edb_selective_scan_train_host_workspace() bytes, 256-byte aligned): the
+ * host->device copies of one row chunk, the kernels of the previous one and the
+ * device->host copies of the one before run at once.  Results equal
+ * edb_selective_scan_fwd + edb_selective_scan_bwd on the whole batch.
+ * Stream-ordered: the results are on the host once `stream` has reached this
+ * point, also after an error status (no copy is left pending).  Replaces the
+ * host-side round trip a caller with host-resident Nx tensors makes around
+ * fused_selective_scan_launch and fused_selective_scan_backward_launch
+ * (native/cuda/fused_selective_scan.cu:105-124, fused_selective_scan_backward.cu:
+ * 198-238); the reference has no single entry point for it. */
+size_t edb_selective_scan_train_host_workspace(int dtype, int batch, int seq_len, int d_inner,
+                                               int d_state);
+
+int edb_selective_scan_train_host(int dtype, const void* x, const void* dt, const void* A,
+                                  const void* B, const void* C, const void* dy, void* y, void* gx,
+                                  void* gdt, float* gB, float* gC, int batch, int seq_len,
+                                  int d_inner, int d_state, float dt_min, float dt_max,
+                                  void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
  * Mamba selective scan, MODEL semantics (what Edifice.build(:mamba) computes:
@@ -412,9 +439,11 @@ int edb_gated_delta_net_bwd(int dtype, const void* q, const void* k, const void*
  * caller still passes every input and output.
  *   - Problems whose workspace (edb_selective_scan_bwd_workspace) exceeds the
  *     array are rejected with EDB_ERR_WORKSPACE_TOO_SMALL before any GPU work.
- *   - The first call on a device looks up the array's device address (once
- *     per device, with that device current); make that first call before any
- *     stream capture.
+ *   - The first call on a device looks up the array's device address, with
+ *     that device current, and caches it together with the unique id of the
+ *     CUDA context it was found in; after a cudaDeviceReset (a new context)
+ *     the next call looks it up again.  Make the first call in each context
+ *     before any stream capture.
  *   - All calls share the one array per device and it keeps the last call's
  *     contents (every byte this backward reads is written first, so nothing
  *     needs clearing); calls that overlap on the GPU -- different streams, or
@@ -435,10 +464,13 @@ int edb_selective_scan_bwd_noalloc(int dtype, const void* x, const void* dt, con
  *   int    edb_<op>_{fwd,bwd}_desc(const edb_<op>_args* args, void* stream,
  *                                  void* workspace, size_t workspace_bytes);
  * The entry points compute what the positional entry points above compute.
- *   - A tensor is used in place when it is dense row-major (strides all zero
- *     also mean dense) and 16-byte aligned.  Any other input (a transposed or
- *     sliced view, a broadcast with stride 0, a negative stride, an unaligned
- *     pointer) is first gathered into a dense copy inside the workspace; any
+ *   - Strides are the tensor's real element strides (a dense row-major
+ *     [B, L, H] tensor has strides {L*H, H, 1}); a zero stride on a dimension
+ *     of extent > 1 is a broadcast, even when every stride is zero.
+ *   - A tensor is used in place when it is dense row-major and 16-byte
+ *     aligned.  Any other input (a transposed or sliced view, a broadcast with
+ *     stride 0, a negative stride, an unaligned pointer) is first gathered
+ *     into a dense copy inside the workspace; any
  *     other output is computed into a dense copy and scattered back through
  *     its strides.  Outputs may not have a zero stride on a dimension of
  *     extent > 1, and outputs must not overlap inputs.
@@ -461,7 +493,7 @@ typedef struct {
     int dtype;                       /* EDB_F32 / EDB_BF16 */
     int ndim;                        /* 1..EDB_MAX_DIMS */
     long long shape[EDB_MAX_DIMS];   /* extents, outermost first */
-    long long strides[EDB_MAX_DIMS]; /* in elements; all zero = dense row-major */
+    long long strides[EDB_MAX_DIMS]; /* in elements (real strides; 0 = broadcast) */
 } edb_tensor;
 
 /* Linear scan (edb_linear_scan_fwd / _bwd).  io tensors in `dtype`:

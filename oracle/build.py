@@ -30,8 +30,23 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_ROOT = os.environ.get("EDIFICE_REFERENCE_ROOT", "/root/reference")
-REF_CUDA = os.path.join(REF_ROOT, "native", "cuda")
+def reference_root():
+    """The reference checkout to compile from: $EDIFICE_REFERENCE_ROOT, else the
+    `reference_path` that the build's BASELINE.json records; None when neither is
+    set.  Nothing at run time needs it (the GPU box uses the prebuilt files)."""
+    env = os.environ.get("EDIFICE_REFERENCE_ROOT")
+    if env:
+        return env
+    try:
+        import json
+        with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+            return json.load(f).get("reference_path") or None
+    except (OSError, ValueError):
+        return None
+
+
+REF_ROOT = reference_root()
+REF_CUDA = os.path.join(REF_ROOT, "native", "cuda") if REF_ROOT else None
 REF_OUT = os.path.join(HERE, "_ref")
 
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
@@ -84,7 +99,7 @@ def build_oracle(force=False):
 
 
 def reference_present():
-    return os.path.isdir(REF_CUDA)
+    return REF_CUDA is not None and os.path.isdir(REF_CUDA)
 
 
 def build_ref(force=False):

@@ -22,7 +22,7 @@ op-level vectors are what the oracle is pinned against:
   gqa_fixture.npz        q [B,Hq,L,d], k, v [B,Hkv,L,d], o (causal) per layer;
                          dq, dk, dv = autograd under seeded dO
 
-Usage:  python tests/golden/make_golden.py [--reference /root/reference]
+Usage:  python tests/golden/make_golden.py --reference <reference checkout>
 """
 import argparse
 import os
@@ -260,8 +260,11 @@ def make_gqa(gen, ref_root):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("EDIFICE_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("EDIFICE_REFERENCE_ROOT"),
+                    help="the reference checkout (default: $EDIFICE_REFERENCE_ROOT)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the reference checkout with --reference or EDIFICE_REFERENCE_ROOT")
     sys.path.insert(0, os.path.join(args.reference, "scripts"))
     import generate_random_weight_fixtures as gen  # the reference's own model classes
     torch.set_grad_enabled(True)

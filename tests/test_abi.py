@@ -130,6 +130,15 @@ def test_descriptor_validation_before_any_gpu_work():
     assert st("linear_scan", "fwd", a) == 1001                    # shape mismatch
     a.h = D.tensor(base, _lib.EDB_BF16, (B, L, H), (L * H, 0, 1))
     assert st("linear_scan", "fwd", a) == 1001                    # output with a zero stride
+    a.h = D.tensor(base, _lib.EDB_BF16, (B, L, H), (0, 0, 0))
+    assert st("linear_scan", "fwd", a) == 1001                    # ... and all strides zero
+    a.h = dense()
+    # an input whose strides are all zero is a broadcast of one element, gathered
+    # into a dense copy (so it needs a workspace), never read as a dense array
+    a.a = D.tensor(base, _lib.EDB_BF16, (B, L, H), (0, 0, 0))
+    assert D.workspace_bytes("linear_scan", "fwd", a) == B * L * H * 2
+    assert st("linear_scan", "fwd", a) == 1004
+    a.a = dense()
     a.h = D.tensor(base, _lib.EDB_BF16, (B, L, H), (L * H, 1, L))
     assert st("linear_scan", "fwd", a) == 1004                    # needs a workspace
     assert st("linear_scan", "fwd", a, base + 16, 1 << 20) == 1003  # not 256-aligned

@@ -309,3 +309,24 @@ def test_fox_attention_desc_blhd_layout(cuda):
     for u, r in ((dq, dq_r), (dk, dk_r), (dv, dv_r), (dcs, dcs_r)):
         _close(u.contiguous(), r)
     assert device_errors() == 0
+
+
+def test_all_zero_strides_are_a_broadcast(cuda):
+    """A one-element tensor expanded to the full shape has every stride zero: as an
+    input it is gathered as the broadcast it is (never read as a dense array past
+    its one element), as an output it is rejected before any GPU work."""
+    g = _g(7)
+    B, L, H = 2, 130, 64
+    dtype = torch.bfloat16
+    a1 = torch.tensor(0.75, dtype=dtype, device="cuda").expand(B, L, H)
+    assert a1.stride() == (0, 0, 0)
+    b = torch.randn(B, L, H, generator=g).to(dtype).cuda()
+    h_ref = fs.linear_scan(a1.contiguous(), b)
+    h = torch.empty(B, L, H, dtype=dtype, device="cuda")
+    D.run("linear_scan", "fwd", D.make_args("linear_scan", dtype, a=a1, b=b, h=h))
+    _exact(h, h_ref)
+    out1 = torch.empty((), dtype=dtype, device="cuda").expand(B, L, H)
+    with pytest.raises(Exception):
+        D.run("linear_scan", "fwd", D.make_args("linear_scan", dtype, a=a1, b=b, h=out1))
+    torch.cuda.synchronize()
+    assert device_errors() == 0

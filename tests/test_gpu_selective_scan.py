@@ -235,3 +235,32 @@ def test_model_semantics_autograd_fn(cuda):
     ref = O.selective_scan_model_bwd(*[_np(t) for t in (x, dt, Bm, Cm)], _np(dy))
     for leaf, r in zip(leaves, ref):
         assert O.norm_rel(_np(leaf.grad), r) <= 1e-4
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(8, 200, 256, 16), (3, 77, 130, 5), (1, 64, 512, 16)])
+def test_train_host_matches_device_path(cuda, dtype, shape):
+    """Forward + backward over pinned host tensors (row chunks streamed through a
+    ring of device slots, copies overlapped with the kernels) equals the device
+    entry points on the whole batch bit for bit (every kernel is independent per
+    batch row and the gB/gC reductions run over channels only), twice in a row."""
+    Bsz, L, D, N = shape
+    x, dt, A, Bm, Cm, dy = ssm_inputs(Bsz, L, D, N, dtype, seed=44)
+    y_r, ck = fs.selective_scan(x, dt, A, Bm, Cm, with_ckpt=True)
+    ref = (y_r,) + tuple(fs.selective_scan_backward(x, dt, A, Bm, Cm, dy, ck))
+    pin = [t.cpu().pin_memory() for t in (x, dt, A, Bm, Cm, dy)]
+    for _ in range(2):
+        out = fs.selective_scan_train_host(*pin)
+        torch.cuda.synchronize()
+        for o, r in zip(out, ref):
+            assert o.dtype == r.dtype and o.shape == r.shape
+            assert torch.equal(o, r.cpu())
+    assert device_errors() == 0
+
+
+def test_train_host_rejects_device_tensors(cuda):
+    x = torch.rand(1, 4, 8, device="cuda")
+    A = torch.rand(8, 4, device="cuda")
+    B = torch.rand(1, 4, 4, device="cuda")
+    with pytest.raises(RuntimeError):
+        fs.selective_scan_train_host(x, x, A, B, B, x)

@@ -1,4 +1,4 @@
-"""Host-side logic of the multi-GPU (weak-scaling) path, on CPU.
+"""Host-side logic of the multi-GPU path (strong and weak plans), on CPU.
 
 Every config partitions into independent units (batch rows; (batch, head);
 (batch, kv group)); a rank owns a contiguous range of global units and draws
@@ -51,6 +51,46 @@ def test_unit_inputs_do_not_depend_on_world_size():
     upper = shard.delta_inputs(dcfg, [2, 3], "cpu")  # (b=1, h=0..1) of the full problem
     for f, u in zip(full, upper):
         assert torch.equal(f[1:], u)
+
+
+def test_units_for_strong_and_weak():
+    # strong: the fixed configs[4] batch of 64 rows, 64/N rows per rank
+    for world in (1, 2, 4, 8):
+        seen = []
+        for r in range(world):
+            u = shard.units_for(64, r, world, "strong")
+            assert len(u) == 64 // world
+            seen += u
+        assert seen == list(range(64))
+        assert shard.units_for(64, 1, world, "weak") == list(range(64, 128)) if world > 1 \
+            else True
+    # more ranks than units: the surplus ranks get none
+    assert [len(shard.units_for(2, r, 8, "strong")) for r in range(8)] == [1, 1] + [0] * 6
+    with pytest.raises(ValueError):
+        shard.units_for(4, 0, 2, "sideways")
+
+
+def test_strong_split_layouts_match_the_full_problem():
+    """A rank's share of a strong split holds exactly the full problem's values of
+    its units, in the layout the kernels take: attention units of part of a batch
+    become a [U, G, L, d] batch (byte for byte the [B, Hq, L, d] layout), delta-rule
+    units of part of a batch a [1, L, U, d] batch."""
+    acfg = shard.AttnConfig(batch=2, q_heads=8, kv_heads=4, seq_len=8, head_dim=16,
+                            dtype=torch.float32)
+    full = shard.attn_inputs(acfg, list(range(8)), "cpu")
+    assert full[0].shape == (2, 8, 8, 16) and full[1].shape == (2, 4, 8, 16)
+    part = shard.attn_inputs(acfg, shard.units_for(8, 3, 4, "strong"), "cpu")  # units 6, 7
+    assert part[0].shape == (2, 2, 8, 16) and part[1].shape == (2, 1, 8, 16)
+    assert torch.equal(part[0].reshape(2 * 2, 8, 16), full[0][1, 4:8])
+    assert torch.equal(part[1].reshape(2, 8, 16), full[1][1, 2:4])
+    dcfg = shard.DeltaConfig(batch=2, heads=4, seq_len=8, head_dim=16, dtype=torch.float32)
+    dfull = shard.delta_inputs(dcfg, list(range(8)), "cpu")
+    dpart = shard.delta_inputs(dcfg, shard.units_for(8, 3, 4, "strong"), "cpu")  # (1, 2..3)
+    assert dpart[0].shape == (1, 8, 2, 16) and dpart[3].shape == (1, 8, 2)
+    for f, u in zip(dfull, dpart):
+        assert torch.equal(f[1:, :, 2:4], u)
+    gfull = shard.gated_alpha(dcfg, list(range(8)), "cpu")
+    assert torch.equal(gfull[1:, :, 2:4], shard.gated_alpha(dcfg, [6, 7], "cpu"))
 
 
 def _free_port():

@@ -76,3 +76,27 @@ def test_noalloc_rejects_problems_beyond_its_scratch(cuda):
     st = lib.edb_selective_scan_bwd_noalloc(1, p, p, p, p, p, p, None, p, p, p, p, Bsz, L, D, N,
                                             0.001, 0.1, None)
     assert st == 1004  # EDB_ERR_WORKSPACE_TOO_SMALL, returned before any GPU work
+
+
+@pytest.mark.parametrize("D", [130, 256])
+def test_noalloc_odd_width_on_a_side_stream(cuda, D):
+    """An odd channel count (the unstaged kernels, no 16-byte copies) and a
+    non-default stream passed through the C ABI, twice in a row, against the
+    workspace entry point."""
+    lib = edifice_b200.load()
+    x, dt, A, Bm, Cm, dy = _inputs(2, 97, D, 16, torch.bfloat16, seed=5)
+    ref = fs.selective_scan_backward(x, dt, A, Bm, Cm, dy)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    for _ in range(2):
+        Bsz, L, _ = x.shape
+        gx, gdt = torch.empty_like(x), torch.empty_like(x)
+        gB = torch.empty(Bsz, L, 16, dtype=torch.float32, device=x.device)
+        gC = torch.empty_like(gB)
+        st = lib.edb_selective_scan_bwd_noalloc(1, P(x), P(dt), P(A), P(Bm), P(Cm), P(dy), P(None),
+                                                P(gx), P(gdt), P(gB), P(gC), Bsz, L, D, 16, 0.001,
+                                                0.1, ctypes.c_void_p(side.cuda_stream))
+        assert st == 0, edifice_b200._lib.status_string(st)
+        side.synchronize()
+        for g, r in zip((gx, gdt, gB, gC), ref):
+            assert O.norm_rel(g.float().cpu().numpy(), r.float().cpu().numpy()) <= 2e-2
