@@ -128,34 +128,16 @@ static __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
 }
 
 // ---------------------------------------------------------------- packed f32 pairs
-// sm_100 executes fma/mul/add on a pair of f32 values as one instruction
-// (.f32x2 on a 64-bit register pair), with the rounding of the scalar forms.
-static __device__ __forceinline__ unsigned long long f2_bits(float2 v) {
-    unsigned long long r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
-    return r;
-}
-static __device__ __forceinline__ float2 bits_f2(unsigned long long r) {
-    float2 v;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
-    return v;
-}
+// sm_100 executes fma/mul/add on a pair of f32 values as one instruction, with
+// the rounding of the scalar forms.  The compiler builtins (not inline PTX) let
+// the register allocator keep pairs in place: wrapping the PTX .f32x2 forms in
+// asm with mov.b64 packing hid the pairs from it and cost register moves.
 // a * b + c, element-wise
 static __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-    unsigned long long d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
-    return bits_f2(d);
+    return __ffma2_rn(a, b, c);
 }
-static __device__ __forceinline__ float2 mul2(float2 a, float2 b) {
-    unsigned long long d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
-    return bits_f2(d);
-}
-static __device__ __forceinline__ float2 add2(float2 a, float2 b) {
-    unsigned long long d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
-    return bits_f2(d);
-}
+static __device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+static __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 static __device__ __forceinline__ float2 dup2(float x) { return make_float2(x, x); }
 
 // ---------------------------------------------------------------- vector I/O

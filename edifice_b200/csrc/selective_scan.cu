@@ -25,7 +25,10 @@
 //     transpose-reduce, cross-warp sum in shared memory, one partial per
 //     (channel block, b, t, n) to the workspace, then a second kernel sums the
 //     channel-block partials in a fixed order.  No atomics.
+#include <type_traits>
+
 #include "edb_common.cuh"
+#include "tc_common.cuh"
 
 namespace {
 
@@ -49,6 +52,16 @@ static __device__ __forceinline__ void fixa_powers(float dtc, float2& pw, float2
     pw = make_float2(r, r * r);
     rr2 = make_float2(r * r, r * r);
 }
+// As fixa_powers for the states of one half of 16: half 1 starts at the pair
+// n = (8, 9), i.e. (r^9, r^10) = (r, r^2) r^8.
+static __device__ __forceinline__ void fixa_powers_half(float dtc, int half, float2& pw,
+                                                        float2& rr2) {
+    fixa_powers(dtc, pw, rr2);
+    if (half) {
+        const float r4 = rr2.x * rr2.x;
+        pw = mul2(pw, make_float2(r4 * r4, r4 * r4));
+    }
+}
 static __device__ __forceinline__ float2 next_power(float2& pw, float2 rr2) {
     const float2 a = pw;
     pw = mul2(pw, rr2);
@@ -56,11 +69,13 @@ static __device__ __forceinline__ float2 next_power(float2& pw, float2 rr2) {
 }
 
 // chunk / sub-chunk lengths per padded state count: TS*NS = 64 state values in
-// registers per sub-chunk, CK/TS = 8 sub-checkpoints (8*NS floats) in smem.
+// registers per sub-chunk.  Checkpoints every CK steps: 8 for 16 states (the
+// tensor-core-reduce backward rebuilds one sub-chunk start per chunk, so 1.5
+// exps per (t, d, n) instead of 2), 8 sub-chunks for 8 states.
 template <int NS>
 struct SsmTiling {
     static constexpr int TS = 64 / NS;
-    static constexpr int CK = 8 * TS;
+    static constexpr int CK = NS == 16 ? 2 * TS : 8 * TS;
 };
 
 template <typename T>
@@ -386,7 +401,7 @@ __global__ void __launch_bounds__(kThreads)
                           float dt_max) {
     constexpr int TB = 32;
     constexpr int CK = SsmTiling<NS>::CK;
-    static_assert(CK % TB == 0, "checkpoints fall on tile starts");
+    static_assert(CK % TB == 0 || TB % CK == 0, "checkpoints fall on tile starts or inside");
     constexpr int TILEB = TB * StageGeom<T>::ROWB;
     constexpr int BCV = TB * NS / kThreads;  // B (and C) values per thread and tile
     extern __shared__ __align__(16) unsigned char smem[];
@@ -459,14 +474,14 @@ __global__ void __launch_bounds__(kThreads)
             const float* bk = sB + (k & 1) * TB * NS;
             const float* ckc = sC + (k & 1) * TB * NS;
             const int t0 = k * TB, tn = min(TB, L - t0);
-            if (ckpt != nullptr && t0 % CK == 0) {
-                float* cp = ckpt + (((long long)b * nck + t0 / CK) * D + d) * NS;
-#pragma unroll
-                for (int p = 0; p < NP; p += 2)
-                    *reinterpret_cast<float4*>(cp + 2 * p) =
-                        make_float4(h[p].x, h[p].y, h[p + 1].x, h[p + 1].y);
-            }
             for (int tt = 0; tt < tn; ++tt) {
+                if (ckpt != nullptr && (t0 + tt) % CK == 0) {
+                    float* cp = ckpt + (((long long)b * nck + (t0 + tt) / CK) * D + d) * NS;
+#pragma unroll
+                    for (int p = 0; p < NP; p += 2)
+                        *reinterpret_cast<float4*>(cp + 2 * p) =
+                            make_float4(h[p].x, h[p].y, h[p + 1].x, h[p + 1].y);
+                }
                 const float dtc = fminf(fmaxf(ldf(dts + tt * kThreads), dt_min), dt_max);
                 const float dti = MODEL ? sDm[(k & 1) * TB + tt] : dtc;
                 const float2 dtc2 = dup2(dtc), dtx2 = dup2(dti * ldf(xs + tt * kThreads));
@@ -729,6 +744,376 @@ constexpr size_t bwd_staged_smem() {
            (size_t)(kThreads / 32) * CK * 2 * NS * sizeof(float) + (size_t)CK * sizeof(float);
 }
 
+// ------------------------------------------------ backward, tensor-core reduce
+// bf16 io, 16 states: the same recompute-not-store backward (one thread per
+// channel, its 16 states in registers) with the two sums over channels
+// (gB = sum_d dh x dtc, gC = sum_d dY h) taken by the tensor core.  Each step's
+// per-channel products go to shared memory as bf16 and tcgen05.mma.kind::f16
+// adds them up, 16 channels per instruction:
+//   D[m][*] = sum_k P[k][m] * 1,  m = (step j of a 4-step sub-chunk, gB|gC, n)
+// with P (128 values x 128 channels, MN-major: a channel's values contiguous,
+// so a thread stores its own products with 16-byte vectors) as operand A and a
+// tile of ones as operand B; D (128 TMEM lanes x 16 columns, all columns
+// equal) is read back one value per thread.  That replaces the warp
+// transpose-reduce (~7.75 instructions per (t, d, n)) with ~0.5 (bf16x2
+// converts and 16-byte stores).  Each product is rounded to bf16 (relative
+// error <= 2^-9, unbiased) before the f32 sum, so gB/gC carry ~1e-3 relative
+// error; the f32-io path keeps the exact SIMT reduce.  (The tensor core reads
+// no MN-major tf32 operand, so f32 products would need one scalar store each.)
+// Chunks of CK = 8 steps run last to first; the x/dt/dY tiles and the chunk
+// checkpoint arrive by cp.async one chunk ahead.  Per chunk: rebuild the
+// second sub-chunk's start state from the checkpoint, then per 4-step
+// sub-chunk recompute h and exp(dt A) into registers and walk back writing P
+// (all 8 steps of the chunk: 256 values), gx and gdt.  A warp that has written
+// its P rows counts itself in with one shared-memory atomic and the last of
+// the four issues the chunk's two MMAs (steps 0-3 and 4-7, into TMEM columns
+// 0-15 and 16-31); the sums are read once per chunk,
+// after the next chunk's first recompute, so the MMA latency stays hidden and
+// no CTA barrier runs inside a chunk.
+namespace sstc {
+constexpr int THREADS = kThreads;       // one thread per channel
+constexpr int WARPS = THREADS / 32;
+constexpr int NS = 16, NP = 8;          // states, state pairs per thread
+constexpr int TS = 4, CK = 8;
+constexpr int ROWB = kThreads * 2;      // bytes of one bf16 tile row (128 channels)
+constexpr int TILEB = CK * ROWB;        // one [CK][128] bf16 tile
+constexpr int CHS = 20;                 // floats per channel of a state row (16 + bank skew)
+constexpr int P_BYTES = 64 * 1024;      // 16 K-groups x 4 M-blocks x 1 KB atoms
+constexpr int OFF_P = 0;                // the chunk's products
+constexpr int OFF_ONES = OFF_P + P_BYTES;  // B: 2 KB of bf16 1.0 (16 rows x 128 B)
+constexpr int OFF_CK = OFF_ONES + 2048;           // [2][128][CHS] f32 chunk checkpoints
+constexpr int OFF_S1 = OFF_CK + 2 * kThreads * CHS * 4;  // [128][CHS] sub-chunk 1 start
+constexpr int OFF_TILE = OFF_S1 + kThreads * CHS * 4;    // [2][x|dt|dy][CK][128] bf16
+constexpr int OFF_BC = OFF_TILE + 2 * 3 * TILEB;         // [2][B|C][CK][NS] f32
+constexpr int OFF_DM = OFF_BC + 2 * 2 * CK * NS * 4;     // [2][CK] f32 (model mode)
+constexpr int OFF_BAR = OFF_DM + 2 * CK * 4;  // mbarrier, TMEM address, arrival counter
+constexpr int SMEM = OFF_BAR + 32;
+constexpr int SMEM_ALLOC = SMEM;  // the dynamic base is 1 KB aligned (checked in the kernel)
+static_assert(2 * (SMEM_ALLOC + 1024) <= 228 * 1024, "two CTAs per SM");
+constexpr int TMEM_COLS = 32;            // D: columns 0-15 = steps 0-3, 16-31 = steps 4-7
+// kind::f16, bf16 x bf16 -> f32, M = 128, N = 16, A MN-major, B K-major
+constexpr uint32_t IDESC = tc::idesc_bf16(128, 16, 1, 0);
+
+// Byte offset of the 16-byte chunk holding values m8..m8+7 (m8 % 8 == 0) of
+// channel k in P: K-group k/8 (4 KB), M-block m8/64 (1 KB atom of 8 channel
+// rows x 128 B), row k%8, chunk (m8%64)/8 swizzled by the row (SWIZZLE_128B).
+static __device__ __forceinline__ uint32_t p_off(int k, int m8) {
+    return (uint32_t)(k >> 3) * 4096u + (uint32_t)(m8 >> 6) * 1024u +
+           tc::sw128_off((uint32_t)(k & 7), (uint32_t)((m8 & 63) >> 3));
+}
+
+static __device__ __forceinline__ float bf16_at(const unsigned char* tile, int row, int ch) {
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(tile + row * ROWB)[ch]);
+}
+static __device__ __forceinline__ uint4 pack8(float2 a, float2 b, float2 c, float2 d) {
+    return make_uint4(tc::pack_bf16x2(a.x, a.y), tc::pack_bf16x2(b.x, b.y),
+                      tc::pack_bf16x2(c.x, c.y), tc::pack_bf16x2(d.x, d.y));
+}
+static __device__ __forceinline__ void load16(const float* p, float2 (&h)[NP]) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float4 v = *reinterpret_cast<const float4*>(p + 4 * q);
+        h[2 * q] = make_float2(v.x, v.y);
+        h[2 * q + 1] = make_float2(v.z, v.w);
+    }
+}
+static __device__ __forceinline__ void bq16(const float* p, float2 (&v)[NP]) { load16(p, v); }
+}  // namespace sstc
+
+// grid (ceil(D/128), B), block 128, two CTAs per SM.  D % 8 == 0 and x, dt, dy
+// 16-byte aligned (the staged geometry).  gpart as ssm_bwd_kernel's.
+template <bool MODEL, bool FIXA>
+__global__ void __launch_bounds__(sstc::THREADS, 2)
+    ssm_bwd_tc_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ dt,
+                      const __nv_bfloat16* __restrict__ A, const __nv_bfloat16* __restrict__ Bm,
+                      const __nv_bfloat16* __restrict__ Cm, const __nv_bfloat16* __restrict__ dy,
+                      const float* __restrict__ ckpt, const float* __restrict__ dtm,
+                      __nv_bfloat16* __restrict__ gx, __nv_bfloat16* __restrict__ gdt,
+                      float* __restrict__ gpart, int Bsz, int L, int D, int N, float dt_min,
+                      float dt_max, unsigned* err) {
+    using namespace sstc;
+    using T = __nv_bfloat16;
+    extern __shared__ __align__(1024) unsigned char smem[];
+    float* sCk = reinterpret_cast<float*>(smem + OFF_CK);
+    float* sS1 = reinterpret_cast<float*>(smem + OFF_S1);
+    float* sBC = reinterpret_cast<float*>(smem + OFF_BC);
+    float* sDm = reinterpret_cast<float*>(smem + OFF_DM);
+    uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BAR + 8);
+    unsigned* arrivals = reinterpret_cast<unsigned*>(smem + OFF_BAR + 12);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int d0 = blockIdx.x * kThreads, d = d0 + tid;
+    const int b = blockIdx.y;
+    const bool live = d < D;
+    const int nck = (L + CK - 1) / CK;
+    const int nblk = gridDim.x;
+    const long long row0 = (long long)b * L;
+    if ((smem_u32(smem) & 1023u) != 0) {  // SWIZZLE_128B operands need 1 KB alignment
+        if (tid == 0) edb_flag_error(err, EDB_DEVERR_SSM_PIPE);
+        return;
+    }
+
+    // ---- set-up: TMEM columns for D, the MMA barriers, the ones tile
+    if (warp == 0) {
+        tc::tmem_alloc(tmem_slot, TMEM_COLS);
+        tc::tmem_relinquish();
+    }
+    if (tid == 0) {
+        mbar_init(mbar, 1);
+        fence_mbar_init();
+        *arrivals = 0;
+    }
+    for (int i = tid; i < 512; i += THREADS)  // 1024 bf16 ones = 512 words of 0x3F80 pairs
+        reinterpret_cast<uint32_t*>(smem + OFF_ONES)[i] = 0x3F803F80u;
+    fence_proxy_async();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    // exp(dtc A) = 2^(dtc A log2 e); the ln 2 of d/d dtc is applied to the sum
+    float2 A2[NP], dh[NP];
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+        const int n = 2 * p;
+        A2[p].x = (live && n < N) ? a_at<MODEL>(A, d, n, N) * kLog2e : 0.0f;
+        A2[p].y = (live && n + 1 < N) ? a_at<MODEL>(A, d, n + 1, N) * kLog2e : 0.0f;
+        dh[p] = dup2(0.0f);
+    }
+
+    // staging of chunk c into buffer c & 1: x | dt | dy rows and the chunk's
+    // checkpoint (zeros for channels past D), one cp.async group
+    auto issue_chunk = [&](int c) {
+        unsigned char* base = smem + OFF_TILE + (c & 1) * 3 * TILEB;
+        const T* src[3] = {x, dt, dy};
+        constexpr int PER = CK * (ROWB / 16);  // 16-byte copies per tile
+        static_assert(PER == THREADS, "one copy per thread and tile");
+        const int r = tid / (ROWB / 16), c16 = tid % (ROWB / 16);
+        const int t = c * CK + r, dd = d0 + c16 * 8;
+        const bool ok = t < L && dd < D;
+#pragma unroll
+        for (int q = 0; q < 3; ++q)
+            cp_async16(base + q * TILEB + r * ROWB + c16 * 16,
+                       src[q] + (ok ? (row0 + t) * D + dd : 0), ok ? 16u : 0u);
+        float* ck_dst = sCk + (c & 1) * kThreads * CHS;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {  // 4 x 16 bytes per channel
+            const int i = tid + k * THREADS, ch = i >> 2, q4 = i & 3;
+            const bool okc = d0 + ch < D;
+            cp_async16(ck_dst + ch * CHS + q4 * 4,
+                       ckpt + (okc ? (((long long)b * nck + c) * D + d0 + ch) * NS + q4 * 4 : 0),
+                       okc ? 16u : 0u);
+        }
+        cp_async_commit();
+    };
+    // B, C (and the mean dt) of chunk c: two values per thread, to registers
+    float rbc0 = 0.0f, rbc1 = 0.0f, rdm = 0.0f;
+    auto load_bc = [&](int c) {
+        const int t = c * CK + tid / NS, n = tid % NS;  // tid < CK * NS = 128
+        const bool ok = t < L && n < N;
+        rbc0 = ok ? ldf(Bm + (row0 + t) * N + n) : 0.0f;
+        rbc1 = ok ? ldf(Cm + (row0 + t) * N + n) : 0.0f;
+        if (MODEL && tid < CK) {
+            const int tt = c * CK + tid;
+            rdm = tt < L ? dtm[row0 + tt] : 0.0f;
+        }
+    };
+    auto store_bc = [&](int c) {
+        sBC[(c & 1) * 2 * CK * NS + tid] = rbc0;
+        sBC[(c & 1) * 2 * CK * NS + CK * NS + tid] = rbc1;
+        if (MODEL && tid < CK) sDm[(c & 1) * CK + tid] = rdm;
+    };
+
+    issue_chunk(nck - 1);
+    load_bc(nck - 1);
+    store_bc(nck - 1);
+
+    int n_mma = 0;            // chunks handed to the tensor core
+    int pend_t = 0, pend_tn = 0;  // first step and step count of the last one
+    bool failed = false, wfailed = false;  // CTA-wide (at chunk starts) / this warp's
+    // Waits for the last chunk's MMAs (P is then free) and reads its sums (two
+    // values per thread: steps warp and 4 + warp) into gpart.  Returns false if
+    // the wait gave up.
+    auto drain = [&]() -> bool {
+        bool ok = mbar_wait_bounded(mbar, (unsigned)((n_mma - 1) & 1), err, EDB_DEVERR_SSM_PIPE);
+        // warp-uniform, so that the .sync.aligned TMEM load below runs on whole warps
+        if (!__all_sync(0xffffffffu, ok)) return false;
+        tc::fence_after_sync();
+        uint32_t v0, v1;
+        const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16);
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(v0) : "r"(ta));
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(v1) : "r"(ta + 16));
+        tc::tmem_wait_ld();
+        const int which = lane >> 4, n = lane & 15;  // value 32 warp + lane of each half
+        const long long o = (((long long)which * nblk + blockIdx.x) * Bsz + b) * L + pend_t;
+        if (warp < pend_tn) gpart[(o + warp) * NS + n] = __uint_as_float(v0);
+        if (4 + warp < pend_tn) gpart[(o + 4 + warp) * NS + n] = __uint_as_float(v1);
+        return true;
+    };
+
+    for (int c = nck - 1; c >= 0; --c) {
+        const int t0 = c * CK, tn = min(CK, L - t0);
+        const unsigned char* tx = smem + OFF_TILE + (c & 1) * 3 * TILEB;
+        const unsigned char* tdt = tx + TILEB;
+        const unsigned char* tdy = tx + 2 * TILEB;
+        const float* sB = sBC + (c & 1) * 2 * CK * NS;
+        const float* sC = sB + CK * NS;
+        const float* dm = sDm + (c & 1) * CK;
+        const float* ck0 = sCk + (c & 1) * kThreads * CHS + tid * CHS;
+        float* s1 = sS1 + tid * CHS;
+
+        cp_async_wait<0>();
+        // chunk c's tiles, checkpoint, B/C visible; every warp is done with chunk c+1
+        failed = __syncthreads_or(wfailed) != 0;
+        if (failed) break;
+        if (c > 0) {
+            issue_chunk(c - 1);
+            load_bc(c - 1);
+        }
+
+        // ---- start state of sub-chunk 1: TS steps on from the checkpoint.  Rows
+        // past L were staged as zeros, so the walk needs no bound on the step.
+        const int nsub = (tn + TS - 1) / TS;
+        float2 h[NP];
+        if (nsub > 1) {
+            load16(ck0, h);
+#pragma unroll
+            for (int tt = 0; tt < TS; ++tt) {
+                const float dtc = fminf(fmaxf(bf16_at(tdt, tt, tid), dt_min), dt_max);
+                const float2 dtc2 = dup2(dtc),
+                             dtx2 = dup2((MODEL ? dm[tt] : dtc) * bf16_at(tx, tt, tid));
+                float2 pw, rr2;
+                if (FIXA) fixa_powers(dtc, pw, rr2);
+                float2 bq[NP];
+                bq16(sB + tt * NS, bq);
+#pragma unroll
+                for (int p = 0; p < NP; ++p) {
+                    const float2 a = FIXA ? next_power(pw, rr2) : ex2_2(mul2(dtc2, A2[p]));
+                    h[p] = fma2(a, h[p], mul2(dtx2, bq[p]));
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                *reinterpret_cast<float4*>(s1 + 4 * q) =
+                    make_float4(h[2 * q].x, h[2 * q].y, h[2 * q + 1].x, h[2 * q + 1].y);
+        }
+
+#pragma unroll
+        for (int s = 1; s >= 0; --s) {  // sub-chunks of the chunk, last first
+            if (s >= nsub) continue;
+            const int u0 = s * TS, un = min(TS, tn - u0);
+            float2 hs[TS][NP], as[TS][NP];
+            load16(s ? s1 : ck0, h);
+#pragma unroll
+            for (int j = 0; j < TS; ++j) {
+                const int tt = u0 + j;
+                const float dtc = fminf(fmaxf(bf16_at(tdt, tt, tid), dt_min), dt_max);
+                const float2 dtc2 = dup2(dtc),
+                             dtx2 = dup2((MODEL ? dm[tt] : dtc) * bf16_at(tx, tt, tid));
+                float2 pw, rr2;
+                if (FIXA) fixa_powers(dtc, pw, rr2);
+                float2 bq[NP];
+                bq16(sB + tt * NS, bq);
+#pragma unroll
+                for (int p = 0; p < NP; ++p) {
+                    as[j][p] = FIXA ? next_power(pw, rr2) : ex2_2(mul2(dtc2, A2[p]));
+                    h[p] = fma2(as[j][p], h[p], mul2(dtx2, bq[p]));
+                    hs[j][p] = h[p];
+                }
+            }
+            // P is free once the previous chunk's MMAs are done and read
+            if (s == nsub - 1 && n_mma > 0 && !drain()) wfailed = true;
+            unsigned char* P = smem + OFF_P;
+#pragma unroll
+            for (int j = TS - 1; j >= 0; --j) {
+                if (j >= un) continue;
+                const int tt = u0 + j;
+                const float draw = bf16_at(tdt, tt, tid);
+                const float dtc = fminf(fmaxf(draw, dt_min), dt_max);
+                const float xv = bf16_at(tx, tt, tid);
+                const float dyv = live ? bf16_at(tdy, tt, tid) : 0.0f;
+                const float dti = MODEL ? dm[tt] : dtc;  // dt of the input term
+                const float dtx = dti * xv;
+                const float2 dy2 = dup2(dyv), dtx2 = dup2(dtx), ndtx2 = dup2(-dtx);
+                float2 bq[NP], cq[NP];
+                bq16(sB + tt * NS, bq);
+                bq16(sC + tt * NS, cq);
+                // two partial sums each (even / odd pairs): shorter dependency chains
+                float2 gxa[2] = {dup2(0.0f), dup2(0.0f)}, gda[2] = {dup2(0.0f), dup2(0.0f)};
+                float2 pb[NP], pc[NP];
+#pragma unroll
+                for (int p = 0; p < NP; ++p) {
+                    const float2 hc = hs[j][p];
+                    const float2 dht = fma2(dy2, cq[p], dh[p]);
+                    pc[p] = mul2(dy2, hc);
+                    pb[p] = mul2(dht, dtx2);
+                    gxa[p & 1] = fma2(dht, bq[p], gxa[p & 1]);
+                    // d h_t / d dtc = A (a h_{t-1}) + B x with a h_{t-1} = h_t - dtc x B
+                    // (A in log2 units here; the B x part is summed once below)
+                    gda[p & 1] = fma2(mul2(dht, A2[p]), fma2(ndtx2, bq[p], hc), gda[p & 1]);
+                    dh[p] = mul2(dht, as[j][p]);
+                }
+                const int m0 = tt * 32;  // this step's values: {gB 0..15 | gC 16..31}
+                *reinterpret_cast<uint4*>(P + p_off(tid, m0)) = pack8(pb[0], pb[1], pb[2], pb[3]);
+                *reinterpret_cast<uint4*>(P + p_off(tid, m0 + 8)) = pack8(pb[4], pb[5], pb[6], pb[7]);
+                *reinterpret_cast<uint4*>(P + p_off(tid, m0 + 16)) = pack8(pc[0], pc[1], pc[2], pc[3]);
+                *reinterpret_cast<uint4*>(P + p_off(tid, m0 + 24)) = pack8(pc[4], pc[5], pc[6], pc[7]);
+                const float gxs = (gxa[0].x + gxa[0].y) + (gxa[1].x + gxa[1].y);
+                const float gdl = kLn2 * ((gda[0].x + gda[0].y) + (gda[1].x + gda[1].y));
+                // model mode: the input term's dt is the channel mean, whose
+                // gradient ssm_model_gdt_kernel adds afterwards
+                const float gds = MODEL ? gdl : fmaf(xv, gxs, gdl);
+                if (live) {
+                    const long long o = (row0 + t0 + tt) * D + d;
+                    st_scalar<T>(gx + o, gxs * dti);
+                    st_scalar<T>(gdt + o, (draw >= dt_min && draw <= dt_max) ? gds : 0.0f);
+                }
+            }
+        }
+        // Hand P to the tensor core: each warp makes its stores visible to the
+        // async proxy and counts itself in; the warp that arrives last issues
+        // the chunk's MMAs.  The counter only grows (WARPS per chunk): a warp
+        // writes the next chunk's P only after draining these MMAs.
+        tc::fence_before_sync();  // this warp's TMEM reads of D before the count
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+            __threadfence_block();
+            const unsigned prev = atomicAdd(arrivals, 1u);
+            if (prev % WARPS == WARPS - 1) {
+                __threadfence_block();
+                tc::fence_after_sync();
+                const uint64_t bdesc = tc::sdesc_sw128(smem + OFF_ONES, 16, 1024);
+                // steps 0-3 (M-blocks 0, 1) into columns 0-15, steps 4-7 (M-blocks 2, 3)
+                // into columns 16-31
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+                    for (int kk = 0; kk < kThreads / 16; ++kk)
+                        tc::mma_bf16_ss(tmem + (uint32_t)(hf * 16),
+                                        tc::sdesc_sw128(smem + OFF_P + kk * 8192 + hf * 2048, 1024,
+                                                        4096),
+                                        bdesc, IDESC, kk > 0);
+                tc::commit(mbar);
+            }
+        }
+        __syncwarp();
+        pend_t = t0;
+        pend_tn = tn;
+        ++n_mma;
+        if (c > 0) store_bc(c - 1);
+    }
+    cp_async_wait<0>();  // nothing may land after the CTA has left
+    if (!failed && !wfailed && n_mma > 0) drain();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
 // ------------------------------------------------------------ model semantics
 // lib/edifice/ssm/common.ex:402-444 (discretize_ssm): B_bar = mean_d(clip(dt)) B.
 // dtm[row] = mean over d_inner of the clamped dt, one warp per (b, t) row, summed
@@ -847,8 +1232,27 @@ int launch_bwd(const void* x, const void* dt, const void* A, const void* Bm, con
                cudaStream_t st) {
     const int nblk = (D + kThreads - 1) / kThreads;
     dim3 grid(nblk, B);
-    if (D % StageGeom<T>::EPC == 0 && edb::aligned16(x) && edb::aligned16(dt) &&
-        edb::aligned16(dy)) {
+    bool tc_done = false;
+    if constexpr (std::is_same<T, __nv_bfloat16>::value && NS == 16) {
+        // bf16 io, 16 states: the tensor-core channel reduce (gx/gdt leave in
+        // 16-byte rows, so they must be 16-byte aligned as well)
+        if (D % 8 == 0 && edb::aligned16(x) && edb::aligned16(dt) && edb::aligned16(dy) &&
+            edb::aligned16(gx) && edb::aligned16(gdt)) {
+            auto kern = ssm_bwd_tc_kernel<MODEL, false>;
+            if (MODEL && A == nullptr) kern = ssm_bwd_tc_kernel<MODEL, MODEL>;
+            cudaError_t ea = cudaFuncSetAttribute(
+                kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sstc::SMEM_ALLOC);
+            if (ea != cudaSuccess) return (int)ea;
+            kern<<<grid, sstc::THREADS, sstc::SMEM_ALLOC, st>>>(
+                (const T*)x, (const T*)dt, (const T*)A, (const T*)Bm, (const T*)Cm,
+                (const T*)dy, ckpt, dtm, (T*)gx, (T*)gdt, gpart, B, L, D, N, lo, hi,
+                edb::device_error_word());
+            tc_done = true;
+        }
+    }
+    if (tc_done) {
+    } else if (D % StageGeom<T>::EPC == 0 && edb::aligned16(x) && edb::aligned16(dt) &&
+               edb::aligned16(dy)) {
         constexpr size_t sm = bwd_staged_smem<T, NS>();
         auto kern = ssm_bwd_staged_kernel<T, NS, MODEL>;
         if (MODEL && A == nullptr) kern = ssm_bwd_staged_kernel<T, NS, MODEL, MODEL>;

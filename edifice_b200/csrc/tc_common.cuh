@@ -56,6 +56,19 @@ static __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t a_d
         : "memory");
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::tf32 (f32 operands read with
+// 10 explicit mantissa bits); the layouts (K- or MN-major) are in `idesc`.
+static __device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc,
+                                                   uint64_t b_desc, uint32_t idesc,
+                                                   uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // All MMAs issued so far by this thread arrive on `bar` when complete.
 static __device__ __forceinline__ void commit(uint64_t* bar) {
     asm volatile(

@@ -43,6 +43,8 @@ CASES = [
     (2, 100, 200, 8),   # partial channel block, N = 8
     (3, 77, 130, 5),    # odd everything
     (1, 1000, 256, 16), # many chunks
+    (2, 61, 136, 16),   # bf16: the tensor-core reduce with a partial channel block and chunk
+    (1, 3, 8, 16),      # one partial chunk, one live octet of channels
 ]
 
 
