@@ -20,6 +20,7 @@ SIGNATURES = {
     "edb_version": (ctypes.c_char_p, []),
     "edb_status_string": (ctypes.c_char_p, [_i]),
     "edb_get_device_errors": (_i, [ctypes.POINTER(ctypes.c_uint), _i]),
+    "edb_set_wait_limit_ns": (_i, [ctypes.c_longlong]),
     "edb_linear_scan_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "edb_linear_scan_bwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "edb_mingru_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),

@@ -126,7 +126,7 @@ template <typename T, int OP, bool BWD, int ROWS, int STAGES, int CW>
 __global__ void __launch_bounds__(32 * CW, CW >= 16 ? 1 : 2)
     diag_scan_tma_kernel(const __grid_constant__ ScanMaps maps, const T* __restrict__ h0,
                          T* __restrict__ out0, T* __restrict__ out1, T* __restrict__ gh0, int L,
-                         int H, unsigned* err) {
+                         int H, unsigned* err, unsigned long long wait_ns) {
     using V = Vec16<T>;
     constexpr int VEC = V::N;
     constexpr int NW = CW;             // warps per CTA (32 segments of CW threads)
@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(32 * CW, CW >= 16 ? 1 : 2)
         const int pt = BWD ? ntiles - 1 - i : i;
         const int t0 = pt * ROWS;
 
-        if (!mbar_wait_bounded(&full[s], par, err, EDB_DEVERR_SCAN_PIPE)) *s_abort = 1;
+        if (!mbar_wait_limited(&full[s], par, err, EDB_DEVERR_SCAN_PIPE, wait_ns)) *s_abort = 1;
 
         // ---- registers <- this thread's RPS rows of every input
         uint4 rin[NIN][RPS];
@@ -353,7 +353,8 @@ __global__ void __launch_bounds__(32 * CW, CW >= 16 ? 1 : 2)
 
     if (abort_tile >= 0) {
         // drain the copies this CTA still has in flight (tiles abort_tile ..
-        // abort_tile + STAGES - 1), each wait bounded by EDB_WAIT_NS, then leave
+        // abort_tile + STAGES - 1), each wait bounded by EDB_WAIT_NS whatever the
+        // host's limit (the copies are real and land), then leave
         if (tid == 0) {
             const int last = abort_tile + STAGES < ntiles ? abort_tile + STAGES : ntiles;
             for (int i = abort_tile; i < last; ++i)
@@ -454,7 +455,8 @@ int launch_tma_cw(const void* const* ins, int nin, const T* h0, T* o0, T* o1, T*
     if (e != cudaSuccess) return (int)e;
     constexpr int NCH = CW * Vec16<T>::N;
     dim3 grid((H + NCH - 1) / NCH, B);
-    kern<<<grid, 32 * CW, smem, stream>>>(maps, h0, o0, o1, gh0, L, H, edb::device_error_word());
+    kern<<<grid, 32 * CW, smem, stream>>>(maps, h0, o0, o1, gh0, L, H, edb::device_error_word(),
+                                          edb::wait_limit_ns());
     return edb::status_from_cuda(cudaGetLastError());
 }
 

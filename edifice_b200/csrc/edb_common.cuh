@@ -63,6 +63,19 @@ static __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned par
     return ok != 0;
 }
 
+// Non-blocking probe of an mbarrier phase (never suspends the thread).
+static __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, unsigned parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 static __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -84,6 +97,20 @@ static __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned
         if (mbar_try_wait(bar, parity)) return true;
         if (global_ns() - t0 > EDB_WAIT_NS) break;
     }
+    edb_flag_error(err, errbit);
+    return false;
+}
+
+// As mbar_wait_bounded with a caller-chosen limit (edb_set_wait_limit_ns):
+// limit_ns = 0 gives up as soon as one probe finds the phase incomplete, which
+// is how a test makes a wait run out on purpose.
+static __device__ __forceinline__ bool mbar_wait_limited(uint64_t* bar, unsigned parity,
+                                                         unsigned* err, unsigned errbit,
+                                                         uint64_t limit_ns) {
+    if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (limit_ns != 0 && global_ns() - t0 <= limit_ns)
+        if (mbar_try_wait(bar, parity)) return true;
     edb_flag_error(err, errbit);
     return false;
 }
@@ -252,6 +279,10 @@ int symbol_address(const void* symbol, SymbolCache& cache, void** out);
 
 // Device address of the current device's error word (see symbol_address).
 unsigned int* device_error_word();
+
+// Wall-clock limit of the waits that take one (edb_set_wait_limit_ns): the
+// default EDB_WAIT_NS unless the host set another.
+unsigned long long wait_limit_ns();
 
 // Map a cudaError_t to the ABI's int status.
 inline int status_from_cuda(cudaError_t e) { return e == cudaSuccess ? EDB_OK : (int)e; }

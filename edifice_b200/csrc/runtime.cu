@@ -3,6 +3,7 @@
 // runtime's driver entry point, and the per-device SM-count cache.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "edb_common.cuh"
@@ -108,6 +109,15 @@ unsigned int* device_error_word() {
     return static_cast<unsigned int*>(p);
 }
 
+namespace {
+std::atomic<long long> g_wait_limit{-1};  // < 0: EDB_WAIT_NS
+}  // namespace
+
+unsigned long long wait_limit_ns() {
+    const long long v = g_wait_limit.load(std::memory_order_relaxed);
+    return v < 0 ? EDB_WAIT_NS : (unsigned long long)v;
+}
+
 int sm_count() {
     static int cache[64] = {0};
     int dev = 0;
@@ -139,6 +149,11 @@ extern "C" const char* edb_status_string(int status) {
             if (status > 0 && status < 1000) return cudaGetErrorString((cudaError_t)status);
             return "unknown status";
     }
+}
+
+extern "C" int edb_set_wait_limit_ns(long long limit_ns) {
+    edb::g_wait_limit.store(limit_ns < 0 ? -1 : limit_ns, std::memory_order_relaxed);
+    return EDB_OK;
 }
 
 extern "C" int edb_get_device_errors(unsigned int* flags_out, int clear) {

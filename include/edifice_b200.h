@@ -63,6 +63,15 @@ const char* edb_status_string(int status);
  * Synchronises the current device.  Returns 0 or a cudaError_t. */
 int edb_get_device_errors(unsigned int* flags_out, int clear);
 
+/* Wall-clock limit of the waits of the diagonal-scan TMA pipeline (linear scan,
+ * MinGRU and the native-recurrence scans), read at each launch.  limit_ns < 0
+ * restores the default (2 s); 0 means a wait that finds its copy not yet landed
+ * gives up at once -- that is how a test makes the pipeline give up on purpose.
+ * A CTA that gives up sets EDB_DEVERR_SCAN_PIPE, writes no outputs from that
+ * tile on, waits (2 s at most) for the copies it has in flight, and exits.  Process-wide;
+ * returns 0.  No counterpart in the reference (its kernels have no waits). */
+int edb_set_wait_limit_ns(long long limit_ns);
+
 /* ------------------------------------------------------------------------
  * Diagonal linear recurrence  h_t = a_t * h_{t-1} + b_t   (h_{-1} = h0)
  * a, b, h: [batch, seq_len, hidden]; h0: [batch, hidden] or NULL (= zeros).

@@ -210,3 +210,30 @@ def test_train_host_rejects_device_tensors(cuda):
     a = torch.rand(1, 4, 8, device="cuda")
     with pytest.raises(RuntimeError):
         fs.linear_scan_train_host(a, a, a)
+
+
+@pytest.mark.parametrize("op", ["linear", "mingru"])
+def test_bounded_wait_gives_up_reports_and_recovers(cuda, op):
+    """A wait of the TMA pipeline that runs out (limit 0: the first probe of a
+    tile that has not landed gives up) makes the kernel flag EDB_DEVERR_SCAN_PIPE
+    in the device error word and exit -- after its in-flight copies land -- rather
+    than hang; the next call with the default limit is exact."""
+    import edifice_b200
+    lib = edifice_b200.load()
+    a, b, dy, _ = _inputs((2, 512, 256), torch.bfloat16, 5, mingru=op == "mingru")
+    fwd = fs.linear_scan if op == "linear" else fs.mingru_scan
+    ref = fwd(a, b)
+    torch.cuda.synchronize()
+    assert device_errors() == 0
+    assert lib.edb_set_wait_limit_ns(0) == 0
+    try:
+        fwd(a, b)
+        torch.cuda.synchronize()  # the kernel has exited: the call did not hang
+        flags = device_errors()
+    finally:
+        assert lib.edb_set_wait_limit_ns(-1) == 0
+    assert flags & 0x1, flags  # EDB_DEVERR_SCAN_PIPE
+    again = fwd(a, b)
+    torch.cuda.synchronize()
+    assert torch.equal(again, ref)
+    assert device_errors() == 0
