@@ -158,6 +158,15 @@ __global__ void __launch_bounds__(sf::THREADS, 1)
         *s_abort = 1;
         return false;
     };
+    // The same decisions taken by a whole warp: the .sync.aligned TMEM loads and
+    // stores that follow them need every lane, so no lane may leave alone.
+    auto wait_w = [&](uint64_t* bar, uint32_t parity) {
+        const bool ok = mbar_wait_bounded(bar, parity, err, EDB_DEVERR_DELTA_PIPE);
+        if (__all_sync(0xffffffffu, ok)) return true;
+        *s_abort = 1;
+        return false;
+    };
+    auto abort_w = [&]() { return __any_sync(0xffffffffu, *s_abort != 0u); };
 
     if (warp == 8) {
         // ---------------------------------------------------------- TMA + MMA
@@ -240,8 +249,8 @@ __global__ void __launch_bounds__(sf::THREADS, 1)
     } else if (warp < 4) {
         // ---------------------------------------------------------- S^T residual
         for (int c = 0; c <= NC; ++c) {
-            if (c > 0 && !wait(&p2[(c - 1) & 1], ((c - 1) >> 1) & 1)) break;
-            if (*s_abort) break;
+            if (c > 0 && !wait_w(&p2[(c - 1) & 1], ((c - 1) >> 1) & 1)) break;
+            if (abort_w()) break;
             tc::fence_after_sync();
             if (st_T != nullptr)
                 store_rows_transposed<D>(st_T + (long long)c * D * D + i, tmem + TM_S + lane_base);
@@ -283,8 +292,8 @@ __global__ void __launch_bounds__(sf::THREADS, 1)
             const int bf = c & 1;
             // P1(c - 1) was issued, so u0_ready[bf ^ 1] is consumed and the
             // buffer pair bf (last used by chunk c - 2, read out already) is free
-            if (c > 0 && !wait(&p1[bf ^ 1], ((c - 1) >> 1) & 1)) break;
-            if (*s_abort) break;
+            if (c > 0 && !wait_w(&p1[bf ^ 1], ((c - 1) >> 1) & 1)) break;
+            if (abort_w()) break;
             {
                 uint32_t r[32];
 #pragma unroll
@@ -304,14 +313,14 @@ __global__ void __launch_bounds__(sf::THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&u0_ready[bf]);
             if (c > 0) {
-                if (!wait(&p2[bf ^ 1], ((c - 1) >> 1) & 1)) break;
+                if (!wait_w(&p2[bf ^ 1], ((c - 1) >> 1) & 1)) break;
                 tc::fence_after_sync();
                 readout(c - 1);
             }
             // the next rows land while P1(c) runs
             if (c + 1 < NC) load_u0(c + 1);
         }
-        if (!*s_abort && wait(&p2[(NC - 1) & 1], ((NC - 1) >> 1) & 1)) {
+        if (!abort_w() && wait_w(&p2[(NC - 1) & 1], ((NC - 1) >> 1) & 1)) {
             tc::fence_after_sync();
             readout(NC - 1);
         }

@@ -166,6 +166,15 @@ __global__ void __launch_bounds__(sb::THREADS, 1)
         *s_abort = 1;
         return false;
     };
+    // The same decisions taken by a whole warp: the .sync.aligned TMEM loads and
+    // stores that follow them need every lane, so no lane may leave alone.
+    auto wait_w = [&](uint64_t* bar, uint32_t parity) {
+        const bool ok = mbar_wait_bounded(bar, parity, err, EDB_DEVERR_DELTA_PIPE);
+        if (__all_sync(0xffffffffu, ok)) return true;
+        *s_abort = 1;
+        return false;
+    };
+    auto abort_w = [&]() { return __any_sync(0xffffffffu, *s_abort != 0u); };
 
     if (warp == 8) {
         // ---------------------------------------------------------- TMA + MMA
@@ -264,8 +273,8 @@ __global__ void __launch_bounds__(sb::THREADS, 1)
     } else if (warp < 4) {
         // ---------------------------------------------------------- dS_C^T
         for (int n = 0; n < NC; ++n) {
-            if (n > 0 && !wait(&p2[(n - 1) & 1], ((n - 1) >> 1) & 1)) break;
-            if (*s_abort) break;
+            if (n > 0 && !wait_w(&p2[(n - 1) & 1], ((n - 1) >> 1) & 1)) break;
+            if (abort_w()) break;
             tc::fence_after_sync();
             store_rows_transposed<D>(dSCT + (ch0 + NC - 1 - n) * D * D + i, tmem + TM_S + lane_base);
             tc::fence_before_sync();
@@ -276,8 +285,8 @@ __global__ void __launch_bounds__(sb::THREADS, 1)
         // ---------------------------------------------------------- dU~, dU~^T
         for (int n = 0; n < NC; ++n) {
             // D_U[n & 1] is final once P1(n) is done (P2(n) only reads it)
-            if (!wait(&p1[n & 1], (n >> 1) & 1)) break;
-            if (*s_abort) break;
+            if (!wait_w(&p1[n & 1], (n >> 1) & 1)) break;
+            if (abort_w()) break;
             tc::fence_after_sync();
             // D_U row i -> dU~[c][t][i] (coalesced over i) and dU~^T[c][i][t]
             const int c = NC - 1 - n;

@@ -13,7 +13,8 @@
 //   warps 0-3  softmax: thread r owns query row r = TMEM lane r; reads S with
 //              tcgen05.ld, online softmax in the log2 domain (one ex2.approx per
 //              score), lazy O rescale (only when the running max grows by more
-//              than 8, i.e. P <= 256), writes P (bf16, swizzled) to shared
+//              than 8, i.e. P <= 256; decided per warp, since the TMEM load and
+//              store need the whole warp), writes P (bf16, swizzled) to shared
 //              memory, and at the end normalises O and stores it with TMA;
 //   warp 4     TMA producer: Q once, then K_j / V_j through a 2-stage ring;
 //   warp 5     MMA issuer (one thread): S_{j+1} = Q K_{j+1}^T is issued as soon
@@ -66,10 +67,16 @@ struct FwdSmem {
 // ------------------------------------------------------------ tcgen05 forward
 // STORE_O = false: only the row log-sum-exp is written (the backward's
 // recompute when the caller has no lse from the forward).
-template <int HD, bool CAUSAL, bool STORE_O = true>
+// FOX: FoX attention (lib/edifice/cuda/fused_scan.ex:3796-3870), the score of
+// key j less cs[b, h, j] (the cs_i of the query row cancels in the softmax and
+// is left out of lse as well).  The bias is register arithmetic on values the
+// softmax threads read with plain loads; the pipeline and its waits are the
+// same as without it.
+template <int HD, bool CAUSAL, bool STORE_O = true, bool FOX = false>
 __global__ void __launch_bounds__(kFwdThreads, 2)
     attn_fwd_tc_kernel(const __grid_constant__ AttnMaps maps, float* __restrict__ lse, int L,
-                       int Hq, int Hkv, float scale_log2, unsigned* err) {
+                       int Hq, int Hkv, float scale_log2, unsigned* err,
+                       const float* __restrict__ cs = nullptr) {
     using S = FwdSmem<HD>;
     constexpr int NB = S::NB;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -232,8 +239,12 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
         const uint32_t tO = tmem + S::TMEM_O + lane_base;
         float m_used = -INFINITY, l = 0.0f;
         bool ok = true;
+        // Every go / give-up decision below is taken by the whole warp (__all_sync):
+        // a lane that left the loop alone would leave the others in tcgen05.ld.
         for (int j = 0; j < nkv; ++j) {
-            if (*(volatile int*)s_abort || !mbar_wait_bounded(s_full, j & 1, err, EDB_DEVERR_ATTN_PIPE)) {
+            const bool got = !*(volatile int*)s_abort &&
+                             mbar_wait_bounded(s_full, j & 1, err, EDB_DEVERR_ATTN_PIPE);
+            if (!__all_sync(0xffffffffu, got)) {
                 ok = false;
                 break;
             }
@@ -261,23 +272,49 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
 #pragma unroll
                 for (int c = 0; c < BN; ++c) x[c] = __uint_as_float(sr[c >> 5][c & 31]) * scale_log2;
             }
+            if (FOX) {
+                // x_j -= cs_j log2(e); 16-byte loads when the row is aligned and the
+                // tile lies inside L (the same addresses for every thread: broadcast)
+                const float* cr = cs + (long long)bh * L + kv0;
+                if (kv0 + BN <= L && ((reinterpret_cast<uintptr_t>(cr) & 15) == 0)) {
+#pragma unroll
+                    for (int c4 = 0; c4 < BN / 4; ++c4) {
+                        const float4 v = __ldg(reinterpret_cast<const float4*>(cr) + c4);
+                        x[4 * c4 + 0] = fmaf(-v.x, kLog2e, x[4 * c4 + 0]);
+                        x[4 * c4 + 1] = fmaf(-v.y, kLog2e, x[4 * c4 + 1]);
+                        x[4 * c4 + 2] = fmaf(-v.z, kLog2e, x[4 * c4 + 2]);
+                        x[4 * c4 + 3] = fmaf(-v.w, kLog2e, x[4 * c4 + 3]);
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < BN; ++c)
+                        if (kv0 + c < L) x[c] = fmaf(-__ldg(cr + c), kLog2e, x[c]);
+                }
+            }
             // 4 independent max chains
             float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
             for (int c = 0; c < BN; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
             const float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
             const float m_new = fmaxf(m_used, mt);
-            bool rescale = false;
+            // Each row decides for itself whether its max grew by more than 8; the
+            // O rescale below is tcgen05.ld/st, which the whole warp must execute
+            // together (.sync.aligned), so the warp rescales when any of its rows
+            // needs it and the other rows multiply by alpha = 1.  A lane-divergent
+            // rescale leaves the warp stalled in tcgen05.ld.
             float alpha = 1.0f;
+            bool grow = false;
             if (j == 0) {
                 m_used = m_new;
             } else if (m_new > m_used + 8.0f) {
                 alpha = tc::ex2(m_used - m_new);
                 m_used = m_new;
-                rescale = true;
+                grow = true;
             }
+            const bool rescale = __any_sync(0xffffffffu, grow);
             // P buffer and O are free once PV_{j-1} has completed
-            if (j > 0 && !mbar_wait_bounded(pv_done, (j - 1) & 1, err, EDB_DEVERR_ATTN_PIPE)) {
+            if (j > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(pv_done, (j - 1) & 1, err,
+                                                                    EDB_DEVERR_ATTN_PIPE))) {
                 ok = false;
                 break;
             }
@@ -317,7 +354,8 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
             if (lane == 0) mbar_arrive(p_full);
         }
         // ---- epilogue: O / l -> bf16 -> smem (Q tile region, swizzled) -> TMA store
-        if (ok && mbar_wait_bounded(pv_done, (nkv - 1) & 1, err, EDB_DEVERR_ATTN_PIPE)) {
+        if (__all_sync(0xffffffffu,
+                       ok && mbar_wait_bounded(pv_done, (nkv - 1) & 1, err, EDB_DEVERR_ATTN_PIPE))) {
             tc::fence_after_sync();
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
 #pragma unroll
@@ -424,22 +462,22 @@ int make_map3(CUtensorMap* m, const void* p, int d, int L, int nbh, int box_rows
     return tc::make_attn_map(m, p, d, L, nbh, box_rows);
 }
 
-template <int HD, bool CAUSAL, bool STORE_O = true>
+template <int HD, bool CAUSAL, bool STORE_O = true, bool FOX = false>
 int launch_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
-                  int Hkv, int L, float scale, cudaStream_t st) {
+                  int Hkv, int L, float scale, cudaStream_t st, const float* cs = nullptr) {
     AttnMaps maps;
     int s;
     if ((s = make_map3(&maps.q, q, HD, L, B * Hq, BM))) return s;
     if ((s = make_map3(&maps.k, k, HD, L, B * Hkv, BN))) return s;
     if ((s = make_map3(&maps.v, v, HD, L, B * Hkv, BN))) return s;
     if ((s = make_map3(&maps.o, o, HD, L, B * Hq, BM))) return s;
-    auto kern = attn_fwd_tc_kernel<HD, CAUSAL, STORE_O>;
+    auto kern = attn_fwd_tc_kernel<HD, CAUSAL, STORE_O, FOX>;
     const int smem = FwdSmem<HD>::TOTAL;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
     dim3 grid((L + BM - 1) / BM, Hq, B);
     kern<<<grid, kFwdThreads, smem, st>>>(maps, lse, L, Hq, Hkv, scale * kLog2e,
-                                          edb::device_error_word());
+                                          edb::device_error_word(), cs);
     return edb::status_from_cuda(cudaGetLastError());
 }
 
@@ -515,6 +553,13 @@ extern "C" int edb_flash_attention_fwd(int dtype, const void* q, const void* k, 
 }
 
 // ------------------------------------------------------------ FoX attention forward
+// The shapes FoX runs on tensor cores (the plain flash kernels' condition).
+static bool fox_tc_shape(int dtype, int d, const void* q, const void* k, const void* v,
+                         const void* o) {
+    return dtype == EDB_BF16 && (d == 64 || d == 128) && edb::aligned16(q) && edb::aligned16(k) &&
+           edb::aligned16(v) && edb::aligned16(o);
+}
+
 extern "C" int edb_fox_attention_fwd(int dtype, const void* q, const void* k, const void* v,
                                      const float* cs, void* o, float* lse, int B, int Hq, int Hkv,
                                      int L, int d, float scale, void* stream) {
@@ -525,8 +570,13 @@ extern "C" int edb_fox_attention_fwd(int dtype, const void* q, const void* k, co
     if (!q || !k || !v || !cs || !o || !lse) return EDB_ERR_NULL_POINTER;
     if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)d);
     cudaStream_t st = (cudaStream_t)stream;
-    // SIMT kernels: a tcgen05 variant with the bias in the softmax warps did not
-    // complete on the B200 and is not built
+    // bf16, head_dim 64/128: the tcgen05 kernel with the bias in its softmax warps
+    if (fox_tc_shape(dtype, d, q, k, v, o)) {
+        return d == 128 ? launch_fwd_tc<128, true, true, true>(q, k, v, o, lse, B, Hq, Hkv, L,
+                                                               scale, st, cs)
+                        : launch_fwd_tc<64, true, true, true>(q, k, v, o, lse, B, Hq, Hkv, L,
+                                                              scale, st, cs);
+    }
     return dtype == EDB_BF16
                ? launch_fwd_simt<__nv_bfloat16>(q, k, v, o, lse, B, Hq, Hkv, L, d, 1, scale, st,
                                                 cs)

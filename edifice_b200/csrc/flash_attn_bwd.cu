@@ -72,12 +72,19 @@ struct BwdSmem {
     static constexpr int TMEM_COLS = 512;
 };
 
-template <int HD, bool CAUSAL>
+// FOX: FoX attention (fused_scan.ex:3870-3984): P of key row j takes the bias
+// -cs[b, h, j] of its query head h (one plain load per head and thread), and
+// each compute thread adds up the dS of its key row over its 32 query columns of
+// every tile of a head, storing that partial (half hf of the query columns) to
+// cs_part[hf][b, h, j]; fox_dcs_kernel then forms grad_cs = -(sum) / scale.  No
+// wait or barrier is added.
+template <int HD, bool CAUSAL, bool FOX = false>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ BwdMaps maps, const float* __restrict__ lse,
                        const float* __restrict__ Dv, float* __restrict__ dq_acc,
                        __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv, int L,
-                       int Hq, int Hkv, float scale, unsigned* err) {
+                       int Hq, int Hkv, float scale, unsigned* err,
+                       const float* __restrict__ cs = nullptr, float* __restrict__ cs_part = nullptr) {
     using S = BwdSmem<HD>;
     constexpr int NB = S::NB;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -274,12 +281,24 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const uint32_t lb = (uint32_t)(qw * 32) << 16;
         const int c0 = hf * 32;
         const float2 sl2 = dup2(scale_log2), sc2 = dup2(scale);
+        float2 nb2 = dup2(0.0f);  // FoX: -cs[b, h, kv] log2(e) of the current query head
+        float dsum = 0.0f;        // FoX: this thread's dS sum over the head's query columns
+        const long long rows_all = (long long)gridDim.z * Hq * L;
         for (int n = 0; n < N; ++n) {
             const int s = n % QD_STAGES;
             const int i = i0 + n % nqi;
-            if (*abort_flag ||
-                !mbar_wait_bounded(&qd_full[s], (n / QD_STAGES) & 1, err, EDB_DEVERR_ATTN_PIPE) ||
-                !mbar_wait_bounded(sdp_full, n & 1, err, EDB_DEVERR_ATTN_PIPE)) {
+            const int gq = n / nqi;
+            if (FOX && n % nqi == 0)
+                nb2 = dup2(kv_idx < L ? -__ldg(cs + ((long long)b * Hq + hk * G + gq) * L + kv_idx) *
+                                            kLog2e
+                                      : 0.0f);
+            // go / give-up decisions are the whole warp's (__all_sync): a lane that
+            // left the loop alone would leave the others in tcgen05.ld
+            const bool got =
+                !*abort_flag &&
+                mbar_wait_bounded(&qd_full[s], (n / QD_STAGES) & 1, err, EDB_DEVERR_ATTN_PIPE) &&
+                mbar_wait_bounded(sdp_full, n & 1, err, EDB_DEVERR_ATTN_PIPE);
+            if (!__all_sync(0xffffffffu, got)) {
                 *abort_flag = 1;
                 break;
             }
@@ -291,7 +310,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(sdp_free);
-            if (n > 0 && !mbar_wait_bounded(mm2_done, (n - 1) & 1, err, EDB_DEVERR_ATTN_PIPE)) {
+            if (n > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(mm2_done, (n - 1) & 1, err,
+                                                                    EDB_DEVERR_ATTN_PIPE))) {
                 *abort_flag = 1;
                 break;
             }
@@ -316,7 +336,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     const int cc = ch * 8 + 2 * e;  // column within this warp's 32
                     const float2 sv = make_float2(__uint_as_float(sr[cc]), __uint_as_float(sr[cc + 1]));
                     const float2 dp = make_float2(__uint_as_float(dr[cc]), __uint_as_float(dr[cc + 1]));
-                    const float2 arg = fma2(sv, sl2, lv[e]);
+                    const float2 arg = fma2(sv, sl2, FOX ? add2(lv[e], nb2) : lv[e]);
                     float2 p = make_float2(tc::ex2(arg.x), tc::ex2(arg.y));
                     if (need_mask) {
                         const int q_idx = i * BQ + c0 + cc;
@@ -325,6 +345,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                         if (!ok || (CAUSAL && q_idx + 1 < kv_idx)) p.y = 0.0f;
                     }
                     const float2 ds = mul2(p, fma2(dp, sc2, dv2[e]));
+                    if (FOX) dsum += ds.x + ds.y;
                     pk[e] = tc::pack_bf16x2(p.x, p.y);
                     dk2[e] = tc::pack_bf16x2(ds.x, ds.y);
                 }
@@ -337,6 +358,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             fence_proxy_async();
             __syncwarp();
             if (lane == 0) mbar_arrive(pds_full);
+            if (FOX && n % nqi == nqi - 1) {  // the head's last query tile
+                if (kv_idx < L)
+                    cs_part[hf * rows_all + ((long long)b * Hq + hk * G + gq) * L + kv_idx] = dsum;
+                dsum = 0.0f;
+            }
         }
     } else {
         // ------------------------------------------------ dQ reduction + dK/dV epilogue (warps 4-7)
@@ -348,7 +374,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int n = 0; n < N; ++n) {
             const int g = n / nqi, i = i0 + n % nqi;
             const int bh = b * Hq + hk * G + g;
-            if (ok && (*abort_flag || !mbar_wait_bounded(dq_full, n & 1, err, EDB_DEVERR_ATTN_PIPE))) {
+            if (ok && !__all_sync(0xffffffffu, !*abort_flag && mbar_wait_bounded(dq_full, n & 1, err,
+                                                                                 EDB_DEVERR_ATTN_PIPE))) {
                 *abort_flag = 1;
                 ok = false;
             }
@@ -395,7 +422,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
         }
         if (w == 0 && lane == 0) tc::tma_store_wait_all();
-        if (ok && mbar_wait_bounded(all_done, 0, err, EDB_DEVERR_ATTN_PIPE)) {
+        if (ok && __all_sync(0xffffffffu, mbar_wait_bounded(all_done, 0, err, EDB_DEVERR_ATTN_PIPE))) {
             tc::fence_after_sync();
             const int r = w * 32 + lane;
             const int kv_idx = kt * BKV + r;
@@ -584,10 +611,11 @@ bool tc_shape(int dtype, int head_dim) {
     return dtype == EDB_BF16 && (head_dim == 64 || head_dim == 128);
 }
 
-template <int HD, bool CAUSAL>
+template <int HD, bool CAUSAL, bool FOX = false>
 int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dO, const float* lse,
                   const float* D, float* dq_acc, void* dk, void* dv, int B, int Hq, int Hkv, int L,
-                  float scale, cudaStream_t st) {
+                  float scale, cudaStream_t st, const float* cs = nullptr,
+                  float* cs_part = nullptr) {
     BwdMaps maps;
     int s;
     if ((s = tc::make_attn_map(&maps.q, q, HD, L, B * Hq, BQ))) return s;
@@ -595,14 +623,14 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const void* dO, c
     if ((s = tc::make_attn_map(&maps.k, k, HD, L, B * Hkv, BKV))) return s;
     if ((s = tc::make_attn_map(&maps.v, v, HD, L, B * Hkv, BKV))) return s;
     if ((s = tc::make_attn_map_f32(&maps.dq, dq_acc, HD, L, B * Hq, BQ))) return s;
-    auto kern = attn_bwd_tc_kernel<HD, CAUSAL>;
+    auto kern = attn_bwd_tc_kernel<HD, CAUSAL, FOX>;
     const int smem = BwdSmem<HD>::TOTAL;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
     dim3 grid((L + BKV - 1) / BKV, Hkv, B);
     kern<<<grid, kBwdThreads, smem, st>>>(maps, lse, D, dq_acc, (__nv_bfloat16*)dk,
                                           (__nv_bfloat16*)dv, L, Hq, Hkv, scale,
-                                          edb::device_error_word());
+                                          edb::device_error_word(), cs, cs_part);
     return edb::status_from_cuda(cudaGetLastError());
 }
 
@@ -755,7 +783,9 @@ extern "C" size_t edb_fox_attention_bwd_workspace(int dtype, int batch, int q_he
                                                   int kv_heads, int seq_len, int head_dim) {
     if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || seq_len <= 0 || head_dim <= 0) return 0;
     const size_t rows = (size_t)batch * q_heads * seq_len;
-    return a256(rows * 4) + a256(2 * rows * 4);  // D, the two cs partial halves
+    size_t ws = a256(rows * 4) + a256(2 * rows * 4);  // D, the two cs partial halves
+    if (tc_shape(dtype, head_dim)) ws += a256(rows * head_dim * 4);  // f32 dQ accumulator
+    return ws;
 }
 
 extern "C" int edb_fox_attention_bwd(int dtype, const void* q, const void* k, const void* v,
@@ -794,7 +824,30 @@ extern "C" int edb_fox_attention_bwd(int dtype, const void* q, const void* k, co
                                                               (long long)rows, head_dim);
         if (cudaError_t e = cudaGetLastError()) return (int)e;
     }
-    // SIMT kernels (the tcgen05 forward variant did not complete; see flash_attn.cu)
+    if (tc_shape(dtype, head_dim) && edb::aligned16(q) && edb::aligned16(k) &&
+        edb::aligned16(v) && edb::aligned16(dO) && edb::aligned16(dk) && edb::aligned16(dv)) {
+        // the tcgen05 kernel with the per-key-row bias and the dS column sums
+        float* acc = reinterpret_cast<float*>(w);
+        const size_t nel = rows * head_dim;
+        cudaError_t e = cudaMemsetAsync(acc, 0, nel * 4, st);
+        if (e != cudaSuccess) return (int)e;
+        const int s = head_dim == 128
+                          ? launch_bwd_tc<128, true, true>(q, k, v, dO, lse, D, acc, dk, dv, batch,
+                                                           q_heads, kv_heads, seq_len, scale, st,
+                                                           cs, part)
+                          : launch_bwd_tc<64, true, true>(q, k, v, dO, lse, D, acc, dk, dv, batch,
+                                                          q_heads, kv_heads, seq_len, scale, st,
+                                                          cs, part);
+        if (s) return s;
+        const unsigned nb = (unsigned)((nel / 4 + 255) / 256);
+        dq_convert_kernel<__nv_bfloat16><<<nb, 256, 0, st>>>(acc, (__nv_bfloat16*)dq,
+                                                            (long long)nel);
+        if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
+        fox_dcs_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(part, dcs, (long long)rows,
+                                                                     1.0f / scale);
+        return edb::status_from_cuda(cudaGetLastError());
+    }
+    // SIMT kernels: other dtypes and head dims
     const int s =
         dtype == EDB_BF16
             ? launch_bwd_simt<__nv_bfloat16>(q, k, v, dO, lse, D, dq, dk, dv, batch, q_heads,
