@@ -252,12 +252,28 @@ __global__ void __launch_bounds__(sf::THREADS, 1)
             if (c > 0 && !wait_w(&p2[(c - 1) & 1], ((c - 1) >> 1) & 1)) break;
             if (abort_w()) break;
             tc::fence_after_sync();
-            if (st_T != nullptr)
-                store_rows_transposed<D>(st_T + (long long)c * D * D + i, tmem + TM_S + lane_base);
+            // S is read into registers and released (s_read) before its 64 KB of
+            // stores are issued, so P2 never waits on the global store queue
+            uint32_t x[D / 32][32];
+            if (st_T != nullptr) {
+#pragma unroll
+                for (int cc = 0; cc < D / 32; ++cc)
+                    tc::tmem_ld32(tmem + TM_S + lane_base + cc * 32, x[cc]);
+                tc::tmem_wait_ld();
+            }
+            if (c < NC) {
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(s_read);
+            }
+            if (st_T != nullptr) {
+                float* dst = st_T + (long long)c * D * D + i;
+#pragma unroll
+                for (int cc = 0; cc < D / 32; ++cc)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) dst[(cc * 32 + e) * D] = __uint_as_float(x[cc][e]);
+            }
             if (c == NC) break;
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(s_read);
         }
     } else {
         // ---------------------------------------------------------- U0^T in, O / U~ out
@@ -312,13 +328,13 @@ __global__ void __launch_bounds__(sf::THREADS, 1)
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(&u0_ready[bf]);
+            // the next rows are in flight while P1(c) runs and chunk c - 1 is read out
+            if (c + 1 < NC) load_u0(c + 1);
             if (c > 0) {
                 if (!wait_w(&p2[bf ^ 1], ((c - 1) >> 1) & 1)) break;
                 tc::fence_after_sync();
                 readout(c - 1);
             }
-            // the next rows land while P1(c) runs
-            if (c + 1 < NC) load_u0(c + 1);
         }
         if (!abort_w() && wait_w(&p2[(NC - 1) & 1], ((NC - 1) >> 1) & 1)) {
             tc::fence_after_sync();

@@ -276,10 +276,21 @@ __global__ void __launch_bounds__(sb::THREADS, 1)
             if (n > 0 && !wait_w(&p2[(n - 1) & 1], ((n - 1) >> 1) & 1)) break;
             if (abort_w()) break;
             tc::fence_after_sync();
-            store_rows_transposed<D>(dSCT + (ch0 + NC - 1 - n) * D * D + i, tmem + TM_S + lane_base);
+            // dS is read into registers and released (s_read) before its 64 KB of
+            // stores are issued, so P2 never waits on the global store queue
+            uint32_t x[D / 32][32];
+#pragma unroll
+            for (int cc = 0; cc < D / 32; ++cc)
+                tc::tmem_ld32(tmem + TM_S + lane_base + cc * 32, x[cc]);
+            tc::tmem_wait_ld();
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(s_read);
+            float* dst = dSCT + (ch0 + NC - 1 - n) * D * D + i;
+#pragma unroll
+            for (int cc = 0; cc < D / 32; ++cc)
+#pragma unroll
+                for (int e = 0; e < 32; ++e) dst[(cc * 32 + e) * D] = __uint_as_float(x[cc][e]);
         }
     } else {
         // ---------------------------------------------------------- dU~, dU~^T

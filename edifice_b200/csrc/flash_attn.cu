@@ -258,7 +258,11 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
             if (lane == 0) mbar_arrive(s_free);
 
             const int kv0 = j * BN;
+            // x: the raw scores (FoX: already in the log2 domain with the bias);
+            // xs scales x into the log2 domain inside the exponent's FFMA, so the
+            // max runs on x and no separate multiply is spent per score
             float x[BN];
+            const float xs = FOX ? 1.0f : scale_log2;
             // only the diagonal tiles and a ragged last tile need a mask (CTA-uniform)
             const bool need_mask = (kv0 + BN > L) || (CAUSAL && kv0 + BN - 1 > q0);
             if (need_mask) {
@@ -266,13 +270,15 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                 for (int c = 0; c < BN; ++c) {
                     const int kv = kv0 + c;
                     const bool masked = kv >= L || (CAUSAL && kv > qrow);
-                    x[c] = masked ? -INFINITY : __uint_as_float(sr[c >> 5][c & 31]) * scale_log2;
+                    x[c] = masked ? -INFINITY : __uint_as_float(sr[c >> 5][c & 31]);
                 }
             } else {
 #pragma unroll
-                for (int c = 0; c < BN; ++c) x[c] = __uint_as_float(sr[c >> 5][c & 31]) * scale_log2;
+                for (int c = 0; c < BN; ++c) x[c] = __uint_as_float(sr[c >> 5][c & 31]);
             }
             if (FOX) {
+#pragma unroll
+                for (int c = 0; c < BN; ++c) x[c] *= scale_log2;
                 // x_j -= cs_j log2(e); 16-byte loads when the row is aligned and the
                 // tile lies inside L (the same addresses for every thread: broadcast)
                 const float* cr = cs + (long long)bh * L + kv0;
@@ -291,11 +297,11 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                         if (kv0 + c < L) x[c] = fmaf(-__ldg(cr + c), kLog2e, x[c]);
                 }
             }
-            // 4 independent max chains
+            // 4 independent max chains, two scores per three-input max
             float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int c = 0; c < BN; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
-            const float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+            for (int c = 0; c < BN; c += 2) mx4[(c >> 1) & 3] = tc::fmax3(mx4[(c >> 1) & 3], x[c], x[c + 1]);
+            const float mt = tc::fmax3(fmaxf(mx4[0], mx4[1]), mx4[2], mx4[3]) * xs;
             const float m_new = fmaxf(m_used, mt);
             // Each row decides for itself whether its max grew by more than 8; the
             // O rescale below is tcgen05.ld/st, which the whole warp must execute
@@ -312,6 +318,26 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                 grow = true;
             }
             const bool rescale = __any_sync(0xffffffffu, grow);
+            // P_j in registers first: its exps overlap P_{j-1} V_{j-1} on the tensor
+            // core; only the O rescale and the P stores wait for that product
+            const float nmu = m_used == -INFINITY ? 0.0f : -m_used;
+            // exponent arguments and row sums in packed f32x2 arithmetic
+            const float2 xs2 = dup2(xs), nmu2 = dup2(nmu);
+            float2 rs2[2] = {dup2(0.0f), dup2(0.0f)};
+            uint4 pv[BN / 8];
+#pragma unroll
+            for (int ch = 0; ch < BN / 8; ++ch) {
+                float p[8];
+#pragma unroll
+                for (int e = 0; e < 8; e += 2) {
+                    const float2 a = fma2(make_float2(x[ch * 8 + e], x[ch * 8 + e + 1]), xs2, nmu2);
+                    p[e] = tc::ex2(a.x);
+                    p[e + 1] = tc::ex2(a.y);
+                    rs2[(e >> 1) & 1] = add2(rs2[(e >> 1) & 1], make_float2(p[e], p[e + 1]));
+                }
+                pv[ch] = make_uint4(tc::pack_bf16x2(p[0], p[1]), tc::pack_bf16x2(p[2], p[3]),
+                                    tc::pack_bf16x2(p[4], p[5]), tc::pack_bf16x2(p[6], p[7]));
+            }
             // P buffer and O are free once PV_{j-1} has completed
             if (j > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(pv_done, (j - 1) & 1, err,
                                                                     EDB_DEVERR_ATTN_PIPE))) {
@@ -332,22 +358,11 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                 }
                 tc::tmem_wait_st();
             }
-            const float mu = m_used == -INFINITY ? 0.0f : m_used;
-            float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             uint8_t* prow = sP;
 #pragma unroll
-            for (int ch = 0; ch < BN / 8; ++ch) {
-                float p[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    p[e] = tc::ex2(x[ch * 8 + e] - mu);
-                    rs4[e & 3] += p[e];
-                }
-                const uint4 v = make_uint4(tc::pack_bf16x2(p[0], p[1]), tc::pack_bf16x2(p[2], p[3]),
-                                           tc::pack_bf16x2(p[4], p[5]), tc::pack_bf16x2(p[6], p[7]));
-                *reinterpret_cast<uint4*>(prow + tc::sw128_off(row, ch)) = v;
-            }
-            l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+            for (int ch = 0; ch < BN / 8; ++ch)
+                *reinterpret_cast<uint4*>(prow + tc::sw128_off(row, ch)) = pv[ch];
+            l += (rs2[0].x + rs2[0].y) + (rs2[1].x + rs2[1].y);
             fence_proxy_async();
             tc::fence_before_sync();
             __syncwarp();

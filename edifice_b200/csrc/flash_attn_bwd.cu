@@ -165,6 +165,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
         }
         int issued = 0;
+        // this lane's rows of -lse log2(e) and -D scale for a tile, loaded one tile
+        // ahead so their latency hides behind the wait for a free stage
+        float pl[BQ / 32], pd[BQ / 32];
+        auto fetch = [&](int n) {
+            const int g = n / nqi, i = i0 + n % nqi;
+            const long long row0 = (long long)(b * Hq + hk * G + g) * L;
+#pragma unroll
+            for (int r = 0; r < BQ / 32; ++r) {
+                const int qr = i * BQ + lane + 32 * r;
+                const bool ok = qr < L;
+                // stored as -lse log2(e) and -D scale: P = ex2(S scale log2(e) + .),
+                // dS = P (dP scale + .); rows past L give P = 0
+                pl[r] = ok ? -lse[row0 + qr] * kLog2e : -INFINITY;
+                pd[r] = ok ? -Dv[row0 + qr] * scale : 0.0f;
+            }
+        };
+        if (N > 0) fetch(0);
         for (int n = 0; n < N; ++n) {
             const int s = n % QD_STAGES;
             int go = 1;
@@ -180,13 +197,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             if (!go) break;
             const int g = n / nqi, i = i0 + n % nqi;
             const int bh = b * Hq + hk * G + g;
-            for (int c = lane; c < BQ; c += 32) {
-                const int qr = i * BQ + c;
-                const bool ok = qr < L;
-                // stored as -lse log2(e) and -D scale: P = ex2(S scale log2(e) + .),
-                // dS = P (dP scale + .); rows past L give P = 0
-                sLse[s * BQ + c] = ok ? -lse[(long long)bh * L + qr] * kLog2e : -INFINITY;
-                sD[s * BQ + c] = ok ? -Dv[(long long)bh * L + qr] * scale : 0.0f;
+#pragma unroll
+            for (int r = 0; r < BQ / 32; ++r) {
+                sLse[s * BQ + lane + 32 * r] = pl[r];
+                sD[s * BQ + lane + 32 * r] = pd[r];
             }
             __syncwarp();
             if (lane == 0) {
@@ -199,6 +213,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 }
             }
             issued = n + 1;
+            if (n + 1 < N) fetch(n + 1);
         }
         if (lane == 0) {
             for (int n = max(0, issued - QD_STAGES); n < issued; ++n)
@@ -211,7 +226,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (lane == 0) {
             constexpr uint32_t idSP = tc::idesc_bf16(BKV, BQ, 0, 0);   // S^T, dP^T
             constexpr uint32_t idKV = tc::idesc_bf16(BKV, HD, 0, 1);   // dV, dK
-            constexpr uint32_t idQ = tc::idesc_bf16(BQ, HD, 1, 1);     // dQ
+            constexpr uint32_t idQ = tc::idesc_bf16(BQ, HD, 1, 1);     // dQ (head_dim 64)
+            constexpr uint32_t idQt = tc::idesc_bf16(HD, BQ, 1, 1);    // dQ^T (head_dim 128)
             auto issue_sdp = [&](int n) {
                 const int s = n % QD_STAGES;
                 const uint8_t* q = sQ + s * S::QD_BYTES;
@@ -250,6 +266,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 const int s = n % QD_STAGES;
                 const uint8_t* q = sQ + s * S::QD_BYTES;
                 const uint8_t* o = sdO + s * S::QD_BYTES;
+                // dQ first, its barrier committed at once: the dQ warps drain it while
+                // dV and dK run.  head_dim 128 computes dQ^T = K^T dS^T, M = 128 (the
+                // head dim): the tensor core's full-rate shape, where dS K would be
+                // M = 64 (half rate); both operands are MN-major in the same tiles.
+                if constexpr (HD == 128) {
+#pragma unroll
+                    for (int kk = 0; kk < BKV / 16; ++kk)
+                        tc::mma_bf16_ss(tmem + S::TM_DQ, tc::sdesc_sw128(sK + kk * 2048, BKV * 128, 1024),
+                                        tc::sdesc_sw128(sDs + kk * 2048, BQ * 128, 1024), idQt,
+                                        kk > 0);
+                } else {
+#pragma unroll
+                    for (int kk = 0; kk < BKV / 16; ++kk)
+                        tc::mma_bf16_ss(tmem + S::TM_DQ, tc::sdesc_sw128(sDs + kk * 2048, BQ * 128, 1024),
+                                        tc::sdesc_sw128(sK + kk * 2048, BKV * 128, 1024), idQ, kk > 0);
+                }
+                tc::commit(dq_full);
 #pragma unroll
                 for (int kk = 0; kk < BQ / 16; ++kk) {
                     tc::mma_bf16_ss(tmem + S::TM_DV, tc::sdesc_sw128(sPt + kk * 32, 16, 1024),
@@ -259,13 +292,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                     tc::sdesc_sw128(q + kk * 2048, BQ * 128, 1024), idKV,
                                     (n > 0 || kk > 0));
                 }
-#pragma unroll
-                for (int kk = 0; kk < BKV / 16; ++kk)
-                    tc::mma_bf16_ss(tmem + S::TM_DQ, tc::sdesc_sw128(sDs + kk * 2048, BQ * 128, 1024),
-                                    tc::sdesc_sw128(sK + kk * 2048, BKV * 128, 1024), idQ, kk > 0);
                 tc::commit(mm2_done);
                 tc::commit(&qd_empty[s]);
-                tc::commit(dq_full);
             }
             if (!ok) *abort_flag = 1;
             tc::commit(all_done);
@@ -310,16 +338,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(sdp_free);
-            if (n > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(mm2_done, (n - 1) & 1, err,
-                                                                    EDB_DEVERR_ATTN_PIPE))) {
-                *abort_flag = 1;
-                break;
-            }
             const float* nl2 = sLse + s * BQ + c0;   // -lse log2(e)
             const float* ndd = sD + s * BQ + c0;     // -D scale
             // masks only on the diagonal and for a ragged last kv tile; query rows
             // past L carry -lse = -inf and give P = 0 by themselves
             const bool need_mask = (kt * BKV + BKV > L) || (CAUSAL && i * BQ < kt * BKV + BKV);
+            // P and dS in registers first: this math overlaps the previous tile's
+            // dV / dK / dQ products, which still read P^T and dS^T in shared memory;
+            // only the stores below wait for them (mm2_done)
+            uint4 pt4[4], ds4[4];
 #pragma unroll
             for (int ch = 0; ch < 4; ++ch) {
                 const float4 la = *reinterpret_cast<const float4*>(nl2 + ch * 8);
@@ -349,11 +376,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     pk[e] = tc::pack_bf16x2(p.x, p.y);
                     dk2[e] = tc::pack_bf16x2(ds.x, ds.y);
                 }
+                pt4[ch] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                ds4[ch] = make_uint4(dk2[0], dk2[1], dk2[2], dk2[3]);
+            }
+            if (n > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(mm2_done, (n - 1) & 1, err,
+                                                                    EDB_DEVERR_ATTN_PIPE))) {
+                *abort_flag = 1;
+                break;
+            }
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
                 const int chunk = hf * 4 + ch;  // 16-byte chunk of the 128-byte row
-                *reinterpret_cast<uint4*>(sPt + tc::sw128_off(r, chunk)) =
-                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                *reinterpret_cast<uint4*>(sDs + tc::sw128_off(r, chunk)) =
-                    make_uint4(dk2[0], dk2[1], dk2[2], dk2[3]);
+                *reinterpret_cast<uint4*>(sPt + tc::sw128_off(r, chunk)) = pt4[ch];
+                *reinterpret_cast<uint4*>(sDs + tc::sw128_off(r, chunk)) = ds4[ch];
             }
             fence_proxy_async();
             __syncwarp();
@@ -386,6 +421,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
             tc::named_bar(2, 128);
             if (ok) {
+                if constexpr (HD == 128) {
+                    // dQ^T: TMEM lane 32 w + lane is head-dim column d, its 64 columns the
+                    // tile's query rows; the thread writes column d of every row into
+                    // staging box w (float `lane` of each 128-byte row, conflict free)
+                    uint32_t qv[2][32];
+                    tc::tmem_ld32(tmem + S::TM_DQ + lb, qv[0]);
+                    tc::tmem_ld32(tmem + S::TM_DQ + lb + 32, qv[1]);
+                    tc::tmem_wait_ld();
+                    uint8_t* box = sDq + w * (BQ * 128) + (lane & 3) * 4;
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            *reinterpret_cast<uint32_t*>(box + tc::sw128_off(h2 * 32 + e, lane >> 2)) =
+                                qv[h2][e];
+                } else
                 // dQ_i in two halves of HD/2 columns (register budget); M = 64
                 // accumulator: lanes 32w + t (t < 16) hold query row 16w + t of the tile
 #pragma unroll

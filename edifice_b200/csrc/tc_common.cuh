@@ -174,6 +174,13 @@ static __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// max(a, b, c) in one instruction (three-input max.f32, sm_100).
+static __device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 static __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
