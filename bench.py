@@ -66,6 +66,9 @@ def parse():
                     help="override the config's batch (small cases for ncu captures)")
     ap.add_argument("--seq-len", type=int, default=None,
                     help="override the config's sequence length (small cases for ncu captures)")
+    ap.add_argument("--probe", choices=["host-copies"], default=None,
+                    help="instead of the bench line: per-rank pinned host<->device copy "
+                         "bandwidth, rank 0 alone and then all ranks at once")
     return ap.parse_args()
 
 
@@ -1292,8 +1295,92 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def probe_host_copies(args):
+    """Pinned host<->device copy bandwidth per rank: host to device, device to
+    host, and both directions at once (two streams), first on rank 0 alone (the
+    others wait at a barrier) and then on every rank at the same time.  Rank 0
+    prints one JSON line with each rank's GB/s, PCI bus id and CPU affinity:
+    the e2e figures at N GPUs are bounded by what these copies reach together."""
+    import torch
+    import torch.distributed as dist
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    nbytes, reps = 256 << 20, 8
+    h_in = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    h_out = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    d_in = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    d_out = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    s_h2d, s_d2h = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def run(kind):
+        evs = []
+        for st, dst, src, on in ((s_h2d, d_in, h_in, kind in ("h2d", "both")),
+                                 (s_d2h, h_out, d_out, kind in ("d2h", "both"))):
+            if not on:
+                continue
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(st):
+                a.record()
+                for _ in range(reps):
+                    dst.copy_(src, non_blocking=True)
+                b.record()
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        return [nbytes * reps / (a.elapsed_time(b) / 1e3) / 1e9 for a, b in evs]
+
+    def sweep(active):
+        out = {}
+        for kind in ("h2d", "d2h", "both"):
+            if world > 1:
+                dist.barrier()
+            if active:
+                run(kind)  # warm
+                r = run(kind)
+                if kind == "both":
+                    out["both_h2d_gbs"], out["both_d2h_gbs"] = r
+                else:
+                    out[kind + "_gbs"] = r[0]
+        return out
+
+    solo = sweep(rank == 0)
+    together = sweep(True)
+    props = torch.cuda.get_device_properties(dev)
+    bus = "%04x:%02x:%02x" % (getattr(props, "pci_domain_id", 0), getattr(props, "pci_bus_id", 0),
+                              getattr(props, "pci_device_id", 0))
+    me = [together.get("h2d_gbs", 0.0), together.get("d2h_gbs", 0.0),
+          together.get("both_h2d_gbs", 0.0), together.get("both_d2h_gbs", 0.0)]
+    table = [me]
+    if world > 1:
+        t = torch.tensor(me, device=dev, dtype=torch.float64)
+        got = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(got, t)
+        table = [g.tolist() for g in got]
+        names = [None] * world
+        dist.all_gather_object(names, {"bus": bus, "cpus": len(os.sched_getaffinity(0))})
+        dist.barrier()
+        dist.destroy_process_group()
+    else:
+        names = [{"bus": bus, "cpus": len(os.sched_getaffinity(0))}]
+    if rank != 0:
+        return
+    per = [dict(rank=i, h2d_gbs=r[0], d2h_gbs=r[1], both_h2d_gbs=r[2], both_d2h_gbs=r[3], **names[i])
+           for i, r in enumerate(table)]
+    print(json.dumps({"probe": "host-copies", "n_gpus": world, "bytes_per_copy": nbytes,
+                      "copies": reps, "rank0_alone": solo, "all_ranks": per,
+                      "sum_h2d_gbs": sum(r[0] for r in table),
+                      "sum_d2h_gbs": sum(r[1] for r in table),
+                      "sum_both_gbs": sum(r[2] + r[3] for r in table)}), flush=True)
+
+
 def main():
     args = parse()
+    if args.probe == "host-copies":
+        probe_host_copies(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
