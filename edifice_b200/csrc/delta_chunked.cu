@@ -25,8 +25,8 @@
 //                           kind::tf32 with every operand K-major.  S lives in
 //                           TMEM (lanes = value dim, columns = key dim) as the f32
 //                           accumulator and is fed back as the A operand:
-//                             D_U  = U0^T + S (-W)^T        M=128, N=64,  K=128
-//                             D_O  = S Q^T + D_U M^T        M=128, N=64,  K=128/64
+//                             [D_U | D_O] = [U0^T | 0] + S [-W; Q]^T   M=128, N=128, K=128
+//                             D_O += D_U M^T                M=128, N=64,  K=64
 //                             S   += D_U (K^T)^T            M=128, N=128, K=64
 //                           -W, Q, K^T, M arrive by TMA (SWIZZLE_128B f32 boxes)
 //                           in a 2-stage ring; U0^T rows are stored into TMEM
@@ -81,21 +81,25 @@ struct StateMaps {
 // The TMEM accumulators U and O are double-buffered by chunk parity, so the
 // read-out of chunk c - 1 and the S^T store of chunk c run while the tensor
 // core works on chunk c:
-//   P1(c): D_U[b] = U0^T + S (-W)^T,  D_O[b] = S Q^T      (S read as A from TMEM)
+//   P1(c): [D_U | D_O][b] = [U0^T | 0] + S [-W; Q]^T      (S read as A from TMEM)
 //   P2(c): D_O[b] += D_U[b] M^T,  S += D_U[b] (K^T)^T      (after S^T is read out)
 // mbarriers (per buffer where two chunks could otherwise alias one phase):
 //   full[s]       TMA stage s landed          u0_ready[b]  U0^T rows in D_U[b]
 //   p1[b], p2[b]  tcgen05.commit of P1 / P2   s_read       S^T of this chunk read
 namespace sf {
 constexpr int THREADS = 288;
-constexpr int OFF_W = 0;
-constexpr int OFF_Q = OFF_W + 4 * BOX_C;
-constexpr int OFF_KT = OFF_Q + 4 * BOX_C;
+// -W and Q share their K slices: box bx of -W (rows 0-63) is followed by box bx of
+// Q (rows 64-127), so each 128-byte K slice of the pair is one N = 128 operand
+// and P1 is a single product S [-W; Q]^T = [D_U | D_O]
+constexpr int OFF_WQ = 0;
+constexpr int OFF_KT = OFF_WQ + 8 * BOX_C;
 constexpr int OFF_M = OFF_KT + 2 * BOX_D;
 constexpr int STAGE_BYTES = OFF_M + 2 * BOX_C;  // 112 KB
 constexpr int OFF_BARS = 2 * STAGE_BYTES;
 constexpr int SMEM = OFF_BARS + 128;
-constexpr int TM_S = 0, TM_U = 128, TM_O = 256, TM_COLS = 512;  // U, O: 2 x 64 columns
+// TMEM: S, then two buffers of [D_U (64 columns) | D_O (64 columns)]
+constexpr int TM_S = 0, TM_U = 128, TM_COLS = 512;
+constexpr int TM_BUF = 128, TM_OFF_O = 64;
 }  // namespace sf
 
 __global__ void __launch_bounds__(sf::THREADS, 1)
@@ -177,8 +181,8 @@ __global__ void __launch_bounds__(sf::THREADS, 1)
                 const int rc = (int)((ch0 + c) * C), rd = (int)((ch0 + c) * D);
                 mbar_arrive_expect_tx(bar, STAGE_BYTES);
                 for (int bx = 0; bx < 4; ++bx) {
-                    tma_load_2d(st + OFF_W + bx * BOX_C, &maps.Wn, bar, bx * 32, rc);
-                    tma_load_2d(st + OFF_Q + bx * BOX_C, &maps.Q, bar, bx * 32, rc);
+                    tma_load_2d(st + OFF_WQ + (2 * bx) * BOX_C, &maps.Wn, bar, bx * 32, rc);
+                    tma_load_2d(st + OFF_WQ + (2 * bx + 1) * BOX_C, &maps.Q, bar, bx * 32, rc);
                 }
                 for (int bx = 0; bx < 2; ++bx) {
                     tma_load_2d(st + OFF_KT + bx * BOX_D, &maps.KT, bar, bx * 32, rd);
@@ -202,16 +206,17 @@ __global__ void __launch_bounds__(sf::THREADS, 1)
                 const int bf = c & 1;
                 const uint32_t par = (c >> 1) & 1;
                 const uint8_t* st = smem + bf * STAGE_BYTES;
-                const uint32_t tU = tmem + TM_U + bf * 64, tO = tmem + TM_O + bf * 64;
+                const uint32_t tU = tmem + TM_U + bf * TM_BUF, tO = tU + TM_OFF_O;
                 if (!wait(&full[bf], par)) break;
                 landed = c + 1;
                 if (!wait(&u0_ready[bf], par)) break;
                 tc::fence_after_sync();
 #pragma unroll
                 for (int kk = 0; kk < D / 8; ++kk) {
-                    mma_tf32_ts(tU, tmem + TM_S + kk * 8, kdesc(st + OFF_W, BOX_C, kk), idN64, 1);
-                    mma_tf32_ts(tO, tmem + TM_S + kk * 8, kdesc(st + OFF_Q, BOX_C, kk), idN64,
-                                kk > 0);
+                    // [D_U | D_O] += S [-W; Q]^T: D_U holds U0^T, D_O zeros (the
+                    // U0 warps store both halves), so every step accumulates
+                    mma_tf32_ts(tU, tmem + TM_S + kk * 8, kdesc(st + OFF_WQ, 2 * BOX_C, kk),
+                                idN128, 1);
                 }
                 tc::commit(&p1[bf]);
                 committed = 2 * c + 1;
@@ -289,7 +294,7 @@ __global__ void __launch_bounds__(sf::THREADS, 1)
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 uint32_t x[32];
-                tc::tmem_ld32(tmem + TM_O + bf * 64 + lane_base + half * 32, x);
+                tc::tmem_ld32(tmem + TM_U + bf * TM_BUF + TM_OFF_O + lane_base + half * 32, x);
                 tc::tmem_wait_ld();
                 __nv_bfloat16* op =
                     o + (((long long)b * L + c * C + half * 32) * H + h) * D + i;
@@ -301,7 +306,7 @@ __global__ void __launch_bounds__(sf::THREADS, 1)
             }
             if (ures != nullptr)
                 store_rows_transposed<C>(ures + (long long)c * C * D + i,
-                                         tmem + TM_U + bf * 64 + lane_base);
+                                         tmem + TM_U + bf * TM_BUF + lane_base);
         };
         load_u0(0);
         for (int c = 0; c < NC; ++c) {
@@ -321,8 +326,14 @@ __global__ void __launch_bounds__(sf::THREADS, 1)
                         r[4 * e + 2] = __float_as_uint(u[8 * half + e].z);
                         r[4 * e + 3] = __float_as_uint(u[8 * half + e].w);
                     }
-                    tc::tmem_st32(tmem + TM_U + bf * 64 + lane_base + half * 32, r);
+                    tc::tmem_st32(tmem + TM_U + bf * TM_BUF + lane_base + half * 32, r);
                 }
+                uint32_t z[32];
+#pragma unroll
+                for (int e = 0; e < 32; ++e) z[e] = 0u;
+#pragma unroll
+                for (int half = 0; half < 2; ++half)
+                    tc::tmem_st32(tmem + TM_U + bf * TM_BUF + TM_OFF_O + lane_base + half * 32, z);
                 tc::tmem_wait_st();
             }
             tc::fence_before_sync();
