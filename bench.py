@@ -42,7 +42,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-CONFIGS = ("ssm", "linear", "mingru", "attn", "laser", "delta", "delta_model", "gated",
+CONFIGS = ("ssm", "linear", "mingru", "attn", "laser", "fox", "delta", "delta_model", "gated",
            "ssm_model", "ssm_cfg0")
 
 
@@ -741,6 +741,81 @@ class LaserWorkload(AttnWorkload):
                 "L=1024, scaled to the step by FLOP share")
 
 
+class FoxWorkload(AttnWorkload):
+    """FoX attention (fused_scan.ex:3796-3984) fwd + bwd at the configs[3] shapes: the
+    flash kernels with the forget bias -cs_j in the softmax warps and grad_cs from the
+    dS column sums; cs = cumsum(log sigmoid(f)), f ~ N(0, 1), per query head (seeded
+    per unit, so every split of the units computes the same numbers)."""
+
+    def __init__(self):
+        import dataclasses
+        super().__init__()
+        self.cfg = dataclasses.replace(self.cfg, name="fox_attention_cfg3")
+        self.kname = "fox_attention"
+
+    def title(self):
+        return "%s fwd+bwd (configs[3] shapes)" % self.cfg.name
+
+    launches_per_step = 5  # fwd; rowdot, bwd, dq convert, grad_cs
+
+    def _setup(self, dev):
+        import torch
+        from edifice_b200 import shard
+        super()._setup(dev)
+        c = self.cfg
+        G, L = c.q_heads // c.kv_heads, c.seq_len
+        cs = torch.empty((len(self.my_units), G, L), dtype=torch.float32, device=dev)
+        for i, u in enumerate(self.my_units):
+            g = torch.Generator(device=dev).manual_seed(shard.unit_seed(7, u))
+            f = torch.randn((G, L), generator=g, device=dev)
+            cs[i].copy_(torch.cumsum(torch.nn.functional.logsigmoid(f), -1))
+        self.cs = cs.view(self.q.shape[0], self.q.shape[1], L)
+
+    def fwd(self):
+        from edifice_b200 import fused_scan as fs
+        return fs.fox_attention(self.q, self.k, self.v, self.cs, return_lse=True)
+
+    def bwd(self, r):
+        from edifice_b200 import fused_scan as fs
+        o, lse = r
+        return fs.fox_attention_backward(self.q, self.k, self.v, self.cs, o, self.do, lse)
+
+    def host_inputs(self):
+        return [self.q, self.k, self.v, self.cs, self.do]
+
+    def e2e_step(self, dev_in):
+        from edifice_b200 import fused_scan as fs
+        q, k, v, cs, do = dev_in
+        o, lse = fs.fox_attention(q, k, v, cs, return_lse=True)
+        return (o,) + tuple(fs.fox_attention_backward(q, k, v, cs, o, do, lse))
+
+    api = ("edifice_b200.fused_scan.fox_attention + fox_attention_backward (whole-tensor "
+           "copies in the timed region)")
+
+    def cpu_step(self, rows=None, prec="f32"):
+        import numpy as np
+        import oracle as O
+        c = self.cfg
+        Ls = 1024
+        if not hasattr(self, "_cpu_f"):
+            rng = np.random.default_rng(0)
+            q = rng.standard_normal((1, 4, Ls, c.head_dim), dtype=np.float32)
+            k = rng.standard_normal((1, 1, Ls, c.head_dim), dtype=np.float32)
+            v = rng.standard_normal((1, 1, Ls, c.head_dim), dtype=np.float32)
+            do = rng.standard_normal((1, 4, Ls, c.head_dim), dtype=np.float32)
+            f = rng.standard_normal((1, 4, Ls))
+            cs = np.cumsum(-np.logaddexp(0.0, -f), -1).astype(np.float32)
+            self._cpu_f = (q, k, v, cs, do)
+        q, k, v, cs, do = self._cpu_f
+        O.fox_fwd(q, k, v, cs)
+        O.fox_bwd(q, k, v, cs, do)
+        f_sample = 4.0 * 4 * Ls * Ls * c.head_dim / 2 * 3.5
+        return c.tokens * f_sample / (c.flops_fwd() + c.flops_bwd())
+
+    cpu_what = ("oracle port (fused_scan.ex:3796-3984, dense f64) on one kv group (4 q heads) "
+                "at L=1024, scaled to the step by FLOP share")
+
+
 class DeltaWorkload(Workload):
     """DeltaNet delta rule fwd (with state checkpoints) + bwd."""
     unit_name = "(batch, head) pairs"
@@ -988,7 +1063,7 @@ class GatedDeltaWorkload(DeltaWorkload):
 
 WORKLOADS = {"ssm": SsmWorkload, "linear": lambda: ScanWorkload(False),
              "mingru": lambda: ScanWorkload(True), "attn": AttnWorkload,
-             "laser": LaserWorkload, "delta": DeltaWorkload, "delta_model": DeltaModelWorkload,
+             "laser": LaserWorkload, "fox": FoxWorkload, "delta": DeltaWorkload, "delta_model": DeltaModelWorkload,
              "gated": GatedDeltaWorkload, "ssm_model": SsmModelWorkload,
              "ssm_cfg0": SsmCfg0Workload}
 

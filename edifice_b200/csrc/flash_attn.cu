@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                 mbar_arrive_expect_tx(&full[s], S::KV_BYTES);
                 for (int bx = 0; bx < NB; ++bx)
                     tma_load_3d(ring + s * S::KV_BYTES + bx * (BN * 128), map, &full[s], bx * 64,
-                                j * BN, bhk);
+                                (FOX ? nkv - 1 - j : j) * BN, bhk);
                 issued = j + 1;
             }
             // make sure no copy is still landing when the CTA leaves (bounded)
@@ -257,12 +257,15 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
             __syncwarp();
             if (lane == 0) mbar_arrive(s_free);
 
-            const int kv0 = j * BN;
-            // x: the raw scores (FoX: already in the log2 domain with the bias);
-            // xs scales x into the log2 domain inside the exponent's FFMA, so the
-            // max runs on x and no separate multiply is spent per score
+            // FoX visits the kv tiles newest first: its bias -cs_j grows with j, so
+            // the first tile sets each row's max and later tiles rarely raise it
+            // (oldest first, every tile would rescale O)
+            const int kv0 = (FOX ? nkv - 1 - j : j) * BN;
+            // x: the raw scores (FoX: s scale - cs_j, natural units); xs scales x
+            // into the log2 domain inside the exponent's FFMA, so the max runs on x
+            // and no separate multiply is spent per score
             float x[BN];
-            const float xs = FOX ? 1.0f : scale_log2;
+            const float xs = FOX ? kLog2e : scale_log2;
             // only the diagonal tiles and a ragged last tile need a mask (CTA-uniform)
             const bool need_mask = (kv0 + BN > L) || (CAUSAL && kv0 + BN - 1 > q0);
             if (need_mask) {
@@ -277,24 +280,27 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                 for (int c = 0; c < BN; ++c) x[c] = __uint_as_float(sr[c >> 5][c & 31]);
             }
             if (FOX) {
-#pragma unroll
-                for (int c = 0; c < BN; ++c) x[c] *= scale_log2;
-                // x_j -= cs_j log2(e); 16-byte loads when the row is aligned and the
-                // tile lies inside L (the same addresses for every thread: broadcast)
+                // x_j = s_j scale - cs_j, one FFMA per score; 16-byte loads when the
+                // row is aligned and the tile lies inside L (the same addresses for
+                // every thread: broadcast).  Masked scores stay -inf.
+                const float sc = scale_log2 * kLn2;
                 const float* cr = cs + (long long)bh * L + kv0;
+                // the next tile's 256 bytes of cs into L1 ahead of use
+                if (lane < 2 && kv0 >= BN)
+                    asm volatile("prefetch.global.L1 [%0];" ::"l"(cr - BN + 32 * lane));
                 if (kv0 + BN <= L && ((reinterpret_cast<uintptr_t>(cr) & 15) == 0)) {
 #pragma unroll
                     for (int c4 = 0; c4 < BN / 4; ++c4) {
                         const float4 v = __ldg(reinterpret_cast<const float4*>(cr) + c4);
-                        x[4 * c4 + 0] = fmaf(-v.x, kLog2e, x[4 * c4 + 0]);
-                        x[4 * c4 + 1] = fmaf(-v.y, kLog2e, x[4 * c4 + 1]);
-                        x[4 * c4 + 2] = fmaf(-v.z, kLog2e, x[4 * c4 + 2]);
-                        x[4 * c4 + 3] = fmaf(-v.w, kLog2e, x[4 * c4 + 3]);
+                        x[4 * c4 + 0] = fmaf(x[4 * c4 + 0], sc, -v.x);
+                        x[4 * c4 + 1] = fmaf(x[4 * c4 + 1], sc, -v.y);
+                        x[4 * c4 + 2] = fmaf(x[4 * c4 + 2], sc, -v.z);
+                        x[4 * c4 + 3] = fmaf(x[4 * c4 + 3], sc, -v.w);
                     }
                 } else {
 #pragma unroll
                     for (int c = 0; c < BN; ++c)
-                        if (kv0 + c < L) x[c] = fmaf(-__ldg(cr + c), kLog2e, x[c]);
+                        x[c] = kv0 + c < L ? fmaf(x[c], sc, -__ldg(cr + c)) : -INFINITY;
                 }
             }
             // 4 independent max chains, two scores per three-input max
