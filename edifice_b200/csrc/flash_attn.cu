@@ -289,13 +289,18 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                 if (lane < 2 && kv0 >= BN)
                     asm volatile("prefetch.global.L1 [%0];" ::"l"(cr - BN + 32 * lane));
                 if (kv0 + BN <= L && ((reinterpret_cast<uintptr_t>(cr) & 15) == 0)) {
+                    const float2 sc2 = dup2(sc);
 #pragma unroll
                     for (int c4 = 0; c4 < BN / 4; ++c4) {
                         const float4 v = __ldg(reinterpret_cast<const float4*>(cr) + c4);
-                        x[4 * c4 + 0] = fmaf(x[4 * c4 + 0], sc, -v.x);
-                        x[4 * c4 + 1] = fmaf(x[4 * c4 + 1], sc, -v.y);
-                        x[4 * c4 + 2] = fmaf(x[4 * c4 + 2], sc, -v.z);
-                        x[4 * c4 + 3] = fmaf(x[4 * c4 + 3], sc, -v.w);
+                        const float2 lo = fma2(make_float2(x[4 * c4], x[4 * c4 + 1]), sc2,
+                                               make_float2(-v.x, -v.y));
+                        const float2 hi = fma2(make_float2(x[4 * c4 + 2], x[4 * c4 + 3]), sc2,
+                                               make_float2(-v.z, -v.w));
+                        x[4 * c4] = lo.x;
+                        x[4 * c4 + 1] = lo.y;
+                        x[4 * c4 + 2] = hi.x;
+                        x[4 * c4 + 3] = hi.y;
                     }
                 } else {
 #pragma unroll
