@@ -100,7 +100,10 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nq = (L + BM - 1) / BM;
-    const int qt = CAUSAL ? nq - 1 - (int)blockIdx.x : (int)blockIdx.x;  // longest first
+    // longest causal query tiles first within each (head, batch); taking the query
+    // tile as the grid's slowest index instead (longest first across all heads)
+    // measured no faster for causal attention and 9 % slower for FoX
+    const int qt = CAUSAL ? nq - 1 - (int)blockIdx.x : (int)blockIdx.x;
     const int hq = blockIdx.y, b = blockIdx.z;
     const int hk = hq / (Hq / Hkv);
     const int bh = b * Hq + hq, bhk = b * Hkv + hk;

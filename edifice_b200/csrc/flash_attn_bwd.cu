@@ -112,7 +112,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     int* s_abort = reinterpret_cast<int*>(s_tmem + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int kt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+    // Blocks launch in linear-index order (x fastest).  The kv tile is taken as the
+    // slowest index: with a causal mask kv tile 0 has the most query tiles, so the
+    // longest CTAs of every (kv head, batch) go first and the short ones fill the
+    // tail (FoX backward 7.73 -> 7.27 ms at the configs[3] shapes; causal attention
+    // unchanged)
+    const int nrow = gridDim.y * gridDim.z;
+    const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    const int kt = lin / nrow, rem = lin - kt * nrow;
+    const int hk = rem % Hkv, b = rem / Hkv;
     const int G = Hq / Hkv;
     const int bhk = b * Hkv + hk;
     const int nq = (L + BQ - 1) / BQ;
