@@ -115,8 +115,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // Blocks launch in linear-index order (x fastest).  The kv tile is taken as the
     // slowest index: with a causal mask kv tile 0 has the most query tiles, so the
     // longest CTAs of every (kv head, batch) go first and the short ones fill the
-    // tail (FoX backward 7.73 -> 7.27 ms at the configs[3] shapes; causal attention
-    // unchanged)
+    // tail (FoX backward 7.78 -> 7.47 ms at the configs[3] shapes; causal attention
+    // 7.83-7.97 -> 7.78-7.83 ms)
     const int nrow = gridDim.y * gridDim.z;
     const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
     const int kt = lin / nrow, rem = lin - kt * nrow;
