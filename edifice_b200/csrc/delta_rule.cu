@@ -478,17 +478,22 @@ __global__ void __launch_bounds__(32 * LPR, 2)
             w[CPL + 2 * p] = g.x;
             w[CPL + 2 * p + 1] = g.y;
             const float2 x = fma2(nbd, krow(tt, p), dS[p]);
-            ga2 = fma2(x, P[p], ga2);
+            if (GATED) ga2 = fma2(x, P[p], ga2);
             dS[p] = GATED ? mul2(al2, x) : x;
         }
         reduce_rows(w, tt - 1, tt);
-        // scalars: galpha, and a per-token beta's gradient (one lane per row)
-        float ga = ga2.x + ga2.y;
-        float bsum = (part_ix == 0 && row_ok) ? err * dsk : 0.0f;
+        // scalars: galpha (gated only), and a per-token beta's gradient (one lane per
+        // row; a per-element beta's goes out per row above)
+        float ga = 0.0f, bsum = 0.0f;
+        if (GATED) {
+            ga = ga2.x + ga2.y;
 #pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) {
-            ga += __shfl_xor_sync(0xffffffffu, ga, o);
-            bsum += __shfl_xor_sync(0xffffffffu, bsum, o);
+            for (int o = 16; o >= 1; o >>= 1) ga += __shfl_xor_sync(0xffffffffu, ga, o);
+        }
+        if (beta_scalar) {
+            bsum = (part_ix == 0 && row_ok) ? err * dsk : 0.0f;
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) bsum += __shfl_xor_sync(0xffffffffu, bsum, o);
         }
         if (lane == 0) {
             red[((tt % NSLOT) * NW + warp) * RED + 2 * HALF] = ga;
