@@ -152,29 +152,41 @@ __global__ void __launch_bounds__(32 * LPR)
             if (tt % CKP == 0) save_state((t0 + tt) / CKP);
             const float* kr = sk + tt * RP + part * SP;
             const float* qr = sq + tt * RP + part * SP;
-            float r = 0.0f;
+            // row dots as packed f32x2 FMAs into two accumulators: short dependency
+            // chains ahead of the shuffles (the per-token step is latency-bound)
+            float2 ra = make_float2(0.0f, 0.0f), rc = make_float2(0.0f, 0.0f);
 #pragma unroll
             for (int c = 0; c < CPL; c += 4) {
                 const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
-                r = fmaf(S[c], k4.x, fmaf(S[c + 1], k4.y, fmaf(S[c + 2], k4.z, fmaf(S[c + 3], k4.w, r))));
+                ra = fma2(make_float2(S[c], S[c + 1]), make_float2(k4.x, k4.y), ra);
+                rc = fma2(make_float2(S[c + 2], S[c + 3]), make_float2(k4.z, k4.w), rc);
             }
+            float r = (ra.x + ra.y) + (rc.x + rc.y);
 #pragma unroll
             for (int o2 = 1; o2 < LPR; o2 <<= 1) r += __shfl_xor_sync(0xffffffffu, r, o2);
             const float al = GATED ? sa[tt] : 1.0f;
             const float u = sb[tt * kRowsPerCta + rl] * (sv[tt * kRowsPerCta + rl] - al * r);
-            float ov = 0.0f;
+            const float2 u2 = make_float2(u, u), al2 = make_float2(al, al);
+            float2 oa = make_float2(0.0f, 0.0f), oc = make_float2(0.0f, 0.0f);
 #pragma unroll
             for (int c = 0; c < CPL; c += 4) {
                 const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
                 const float4 q4 = *reinterpret_cast<const float4*>(qr + c);
-                const float kv[4] = {k4.x, k4.y, k4.z, k4.w}, qv[4] = {q4.x, q4.y, q4.z, q4.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float sn = fmaf(u, kv[e], GATED ? al * S[c + e] : S[c + e]);
-                    S[c + e] = sn;
-                    ov = fmaf(sn, qv[e], ov);
+                float2 s0 = make_float2(S[c], S[c + 1]), s1 = make_float2(S[c + 2], S[c + 3]);
+                if (GATED) {
+                    s0 = mul2(al2, s0);
+                    s1 = mul2(al2, s1);
                 }
+                s0 = fma2(u2, make_float2(k4.x, k4.y), s0);
+                s1 = fma2(u2, make_float2(k4.z, k4.w), s1);
+                S[c] = s0.x;
+                S[c + 1] = s0.y;
+                S[c + 2] = s1.x;
+                S[c + 3] = s1.y;
+                oa = fma2(s0, make_float2(q4.x, q4.y), oa);
+                oc = fma2(s1, make_float2(q4.z, q4.w), oc);
             }
+            float ov = (oa.x + oa.y) + (oc.x + oc.y);
 #pragma unroll
             for (int o2 = 1; o2 < LPR; o2 <<= 1) ov += __shfl_xor_sync(0xffffffffu, ov, o2);
             if (part == 0) so[tt * kRowsPerCta + rl] = ov;
