@@ -982,7 +982,9 @@ class DeltaModelWorkload(DeltaWorkload):
 class GatedDeltaWorkload(DeltaWorkload):
     """GatedDeltaNet (delta rule with a per-token decay alpha) fwd + bwd at the
     configs[2] shapes and distributions, alpha = mean of sigmoid(N(0,1)) gates over
-    head_dim (the model's form)."""
+    head_dim (the model's form).  bf16, one beta per token, d = 128: the chunked
+    tensor-core kernels with the decay, so the FLOP and launch accounting is the
+    delta rule's."""
 
     def __init__(self):
         import dataclasses
@@ -1002,14 +1004,6 @@ class GatedDeltaWorkload(DeltaWorkload):
         from edifice_b200 import shard
         super()._setup(dev)
         self.alpha = shard.gated_alpha(self.cfg, self.my_units, dev)
-
-    def kernels(self):
-        # token recurrence on the f32 pipes: algorithmic FLOPs of the recurrence
-        f = len(self.my_units) / self.cfg.units
-        return {"fwd": ("fp32", recurrence_flops(self.cfg, True, False) * f),
-                "bwd": ("fp32", recurrence_flops(self.cfg, True, True) * f)}
-
-    launches_per_step = 3  # forward (writes the checkpoints), backward, row-sum reduce
 
     def fwd(self):
         from edifice_b200 import fused_scan as fs
@@ -1032,9 +1026,6 @@ class GatedDeltaWorkload(DeltaWorkload):
 
     api = ("edifice_b200.fused_scan.gated_delta_net_scan + gated_delta_net_backward "
            "(whole-tensor copies in the timed region)")
-
-    def extra(self, fwd_ms, bwd_ms):
-        return {}
 
     def cpu_step(self, rows=None, prec="f32"):
         import numpy as np

@@ -58,6 +58,9 @@ SIGNATURES = {
     "edb_gated_delta_net_ckpt_bytes": (_sz, [_i, _i, _i, _i, _i, _i]),
     "edb_gated_delta_net_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i,
                                      _vp]),
+    "edb_gated_delta_net_fwd_workspace": (_sz, [_i, _i, _i, _i, _i, _i]),
+    "edb_gated_delta_net_fwd_ws": (_i, [_i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i,
+                                        _i, _vp, _sz, _vp]),
     "edb_gated_delta_net_bwd_workspace": (_sz, [_i, _i, _i, _i, _i, _i, _i]),
     "edb_gated_delta_net_bwd": (_i, [_i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp,
                                      _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),

@@ -34,6 +34,16 @@
 //                           stores S^T at every chunk start (and the final S^T)
 //                           and each chunk's U~ for the backward.  TF32
 //                           operands (10-bit mantissa), f32 accumulation.
+//
+// GatedDeltaNet (one decay alpha per token and head; fused_scan.ex:2256-2284,
+// gated_delta_net.ex:382-394), same kernels with GATED: inside a chunk
+// gamma_t = prod_{s<=t} alpha_s, Gamma_ts = gamma_t / gamma_s (s <= t), and
+//   A = tril(diag(beta)(K K^T o Gamma), -1),  W = T diag(beta gamma) K,  U0 = T diag(beta) V
+//   U~ = U0 - W S_0^T,  O = diag(gamma) Q S_0^T + (tril(Q K^T) o Gamma) U~
+//   S_C = gamma_C S_0 + U~^T diag(gamma_C / gamma) K
+// (the recurrence S_t = alpha_t S_{t-1} + beta_t (v_t - alpha_t S_{t-1} k_t) k_t^T
+// unrolled over the chunk).  The prep folds every gamma into its operands; the
+// state kernel scales S by gamma_C between P1 (which needs S_0) and P2.
 #include <math.h>
 
 #include "delta_chunked.cuh"
@@ -50,10 +60,12 @@ struct FwdScratch {
     float* KT;   // [nch][D][C]
     float* U0T;  // [nch][D][C]
     float* M;    // [nch][C][C]  tril(Q K^T), diagonal included
+    float* gl;   // [nch][C]     gated: in-chunk log-decay cumsum
 };
 
 size_t fwd_scratch_bytes(long long nch) {
-    return 4 * a256((size_t)nch * C * D * 4) + a256((size_t)nch * C * C * 4);
+    return 4 * a256((size_t)nch * C * D * 4) + a256((size_t)nch * C * C * 4) +
+           a256((size_t)nch * C * 4);
 }
 
 FwdScratch carve_fwd(void* ws, long long nch) {
@@ -65,6 +77,7 @@ FwdScratch carve_fwd(void* ws, long long nch) {
     s.KT = reinterpret_cast<float*>(p + 2 * cd);
     s.U0T = reinterpret_cast<float*>(p + 3 * cd);
     s.M = reinterpret_cast<float*>(p + 4 * cd);
+    s.gl = reinterpret_cast<float*>(p + 4 * cd + a256((size_t)nch * C * C * 4));
     return s;
 }
 
@@ -102,10 +115,11 @@ constexpr int TM_S = 0, TM_U = 128, TM_COLS = 512;
 constexpr int TM_BUF = 128, TM_OFF_O = 64;
 }  // namespace sf
 
+template <bool GATED>
 __global__ void __launch_bounds__(sf::THREADS, 1)
     delta_state_fwd_kernel(const __grid_constant__ StateMaps maps, const float* __restrict__ U0T,
-                           float* __restrict__ resid, __nv_bfloat16* __restrict__ o, int L, int H,
-                           int NC, unsigned* err) {
+                           const float* __restrict__ gl, float* __restrict__ resid,
+                           __nv_bfloat16* __restrict__ o, int L, int H, int NC, unsigned* err) {
     using namespace sf;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BARS);
@@ -260,11 +274,28 @@ __global__ void __launch_bounds__(sf::THREADS, 1)
             // S is read into registers and released (s_read) before its 64 KB of
             // stores are issued, so P2 never waits on the global store queue
             uint32_t x[D / 32][32];
-            if (st_T != nullptr) {
+            if (GATED || st_T != nullptr) {
 #pragma unroll
                 for (int cc = 0; cc < D / 32; ++cc)
                     tc::tmem_ld32(tmem + TM_S + lane_base + cc * 32, x[cc]);
                 tc::tmem_wait_ld();
+            }
+            if (GATED && c < NC) {
+                // S <- gamma_C S once P1(c) has read S_0
+                const float gC = __expf(gl[(ch0 + c) * C + C - 1]);
+                if (!wait_w(&p1[c & 1], (c >> 1) & 1)) break;
+                tc::fence_after_sync();
+#pragma unroll
+                for (int cc = 0; cc < D / 32; ++cc)
+#pragma unroll
+                    for (int g8 = 0; g8 < 4; ++g8) {
+                        uint32_t y[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            y[e] = __float_as_uint(gC * __uint_as_float(x[cc][8 * g8 + e]));
+                        tc::tmem_st8(tmem + TM_S + lane_base + cc * 32 + 8 * g8, y);
+                    }
+                tc::tmem_wait_st();
             }
             if (c < NC) {
                 tc::fence_before_sync();
@@ -375,8 +406,9 @@ size_t edb_delta_chunked_fwd_ws(int B, int L, int H) {
     return fwd_scratch_bytes((long long)B * H * ((L + C - 1) / C));
 }
 
-int edb_delta_chunked_fwd(const void* q, const void* k, const void* v, const void* beta, void* o,
-                          float* resid, int B, int L, int H, void* ws, cudaStream_t st) {
+int edb_delta_chunked_fwd(const void* q, const void* k, const void* v, const void* beta,
+                          const void* alpha, void* o, float* resid, int B, int L, int H, void* ws,
+                          cudaStream_t st) {
     const int NC = (L + C - 1) / C;
     const long long nch = (long long)B * H * NC;
     if (nch * D > 0x7fffffffLL) return EDB_ERR_UNSUPPORTED;  // TMA row coordinate is int32
@@ -387,17 +419,19 @@ int edb_delta_chunked_fwd(const void* q, const void* k, const void* v, const voi
     po.M = w.M;
     po.Wn = w.Wn;
     po.U0T = w.U0T;
-    int s = launch_delta_prep<true>(q, k, v, beta, po, B, L, H, st);
+    po.gl = w.gl;
+    int s = launch_delta_prep<true>(q, k, v, beta, alpha, po, B, L, H, st);
     if (s != EDB_OK) return s;
     StateMaps maps;
     if ((s = make_box_map(&maps.Wn, w.Wn, nch * C, D, C))) return s;
     if ((s = make_box_map(&maps.Q, w.Q, nch * C, D, C))) return s;
     if ((s = make_box_map(&maps.KT, w.KT, nch * D, C, D))) return s;
     if ((s = make_box_map(&maps.M, w.M, nch * C, C, C))) return s;
-    cudaError_t e = cudaFuncSetAttribute(delta_state_fwd_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, sf::SMEM);
+    auto kern = alpha != nullptr ? delta_state_fwd_kernel<true> : delta_state_fwd_kernel<false>;
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sf::SMEM);
     if (e != cudaSuccess) return (int)e;
-    delta_state_fwd_kernel<<<dim3(H, B), sf::THREADS, sf::SMEM, st>>>(
-        maps, w.U0T, resid, (__nv_bfloat16*)o, L, H, NC, edb::device_error_word());
+    kern<<<dim3(H, B), sf::THREADS, sf::SMEM, st>>>(maps, w.U0T, w.gl, resid, (__nv_bfloat16*)o,
+                                                     L, H, NC, edb::device_error_word());
     return edb::status_from_cuda(cudaGetLastError());
 }

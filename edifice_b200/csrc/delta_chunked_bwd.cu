@@ -27,6 +27,21 @@
 //   delta_post_kernel       (delta_chunked_post.cu) per chunk: the products
 //                           with S_0 / dS_C, dT_b, dQ, dK, dV on tcgen05, the
 //                           C x C chain (dA, dbeta) SIMT.
+//
+// GatedDeltaNet (GATED; fused_scan.ex:1347-1431 is the reference's backward):
+// with the forward's gamma_t, Gamma, K' = diag(gamma) K, K~ = diag(gamma_C/gamma) K,
+// Q~ = diag(gamma) Q, M = tril(Q K^T) o Gamma, W = T diag(beta) K':
+//   dU~  = M^T dO + K~ dS_C^T
+//   dS_0 = gamma_C dS_C + dO^T Q~ - dU~^T W
+//   dT_b = dW K'^T + dU~ V^T,  dM~ = dM o Gamma,  dG = (diag(beta) dA) o Gamma
+//   dQ   = diag(gamma) dO S_0 + dM~ K
+//   dK   = diag(gamma_C/gamma) U~ dS_C + dM~^T Q + diag(gamma) T_b^T dW + (dG + dG^T) K
+//   dg_t = <dQ~_t, q~_t> + <dK'_t, k'_t> - <dK~_t, k~_t> + rowsum - colsum of dM o M
+//          and of dA o A (A = tril(diag(beta)(K K^T o Gamma), -1)), and at t = C - 1
+//          also sum_s <dK~_s, k~_s> + gamma_C <dS_C, S_0>
+//   dalpha_s = (sum_{t >= s} dg_t) / alpha_s        (g_t = sum_{s<=t} log alpha_s)
+// The prep writes K' (Kf), K~ (Kd), Q~^T (QdT) and g; the state kernel reads K~,
+// Q~^T and -W^T, and scales dS by gamma_C between P1 (which needs dS_C) and P2.
 #include <math.h>
 
 #include "delta_chunked.cuh"
@@ -51,14 +66,19 @@ struct BwdScratch {
     float* dSCT;  // [nch][D][D]  dS_C^T
     float* dU;    // [nch][C][D]  dU~
     float* dUT;   // [nch][D][C]  dU~^T
+    // gated only
+    float* Kd;    // [nch][C][D]  K~ = diag(gamma_C / gamma) K
+    float* QdT;   // [nch][D][C]  Q~^T
+    float* gl;    // [nch][C]     g
 };
 
-size_t bwd_scratch_bytes(long long nch) {
+size_t bwd_scratch_bytes(long long nch, bool gated) {
     return 7 * a256((size_t)nch * C * D * 4) + 3 * a256((size_t)nch * C * C * 4) +
-           a256((size_t)nch * D * D * 4);
+           a256((size_t)nch * D * D * 4) +
+           (gated ? 2 * a256((size_t)nch * C * D * 4) + a256((size_t)nch * C * 4) : 0);
 }
 
-BwdScratch carve_bwd(void* ws, long long nch) {
+BwdScratch carve_bwd(void* ws, long long nch, bool gated) {
     char* p = static_cast<char*>(ws);
     const size_t cd = a256((size_t)nch * C * D * 4), cc = a256((size_t)nch * C * C * 4);
     auto take = [&](size_t bytes) {
@@ -78,6 +98,9 @@ BwdScratch carve_bwd(void* ws, long long nch) {
     s.T = take(cc);
     s.G = take(cc);
     s.dSCT = take(a256((size_t)nch * D * D * 4));
+    s.Kd = gated ? take(cd) : nullptr;
+    s.QdT = gated ? take(cd) : nullptr;
+    s.gl = gated ? take(a256((size_t)nch * C * 4)) : nullptr;
     return s;
 }
 
@@ -112,10 +135,11 @@ constexpr int SMEM = OFF_BARS + 128;
 constexpr int TM_S = 0, TM_U = 128, TM_COLS = 256;  // D_U: 2 x 64 columns
 }  // namespace sb
 
+template <bool GATED>
 __global__ void __launch_bounds__(sb::THREADS, 1)
-    delta_state_bwd_kernel(const __grid_constant__ StateBwdMaps maps, float* __restrict__ dSCT,
-                           float* __restrict__ dU, float* __restrict__ dUT, int H, int NC,
-                           unsigned* err) {
+    delta_state_bwd_kernel(const __grid_constant__ StateBwdMaps maps, const float* __restrict__ gl,
+                           float* __restrict__ dSCT, float* __restrict__ dU,
+                           float* __restrict__ dUT, int H, int NC, unsigned* err) {
     using namespace sb;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BARS);
@@ -283,6 +307,23 @@ __global__ void __launch_bounds__(sb::THREADS, 1)
             for (int cc = 0; cc < D / 32; ++cc)
                 tc::tmem_ld32(tmem + TM_S + lane_base + cc * 32, x[cc]);
             tc::tmem_wait_ld();
+            if (GATED) {
+                // dS <- gamma_C dS once P1(n) has read dS_C
+                const float gC = __expf(gl[(ch0 + NC - 1 - n) * C + C - 1]);
+                if (!wait_w(&p1[n & 1], (n >> 1) & 1)) break;
+                tc::fence_after_sync();
+#pragma unroll
+                for (int cc = 0; cc < D / 32; ++cc)
+#pragma unroll
+                    for (int g8 = 0; g8 < 4; ++g8) {
+                        uint32_t y[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            y[e] = __float_as_uint(gC * __uint_as_float(x[cc][8 * g8 + e]));
+                        tc::tmem_st8(tmem + TM_S + lane_base + cc * 32 + 8 * g8, y);
+                    }
+                tc::tmem_wait_st();
+            }
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(s_read);
@@ -333,22 +374,25 @@ __global__ void __launch_bounds__(sb::THREADS, 1)
 
 // ---------------------------------------------------------------- library-internal
 int edb_delta_chunked_post(const float* resid, const void* dO, const void* v, const void* beta,
-                           const float* dSCT, const float* dU, const float* dUT, const float* Kf,
-                           const float* KT, const float* QT, const float* T, const float* G,
-                           void* gq, void* gk, void* gv, void* gbeta, int B, int L, int H,
+                           const void* alpha, const float* dSCT, const float* dU, const float* dUT,
+                           const float* Kf, const float* KT, const float* QT, const float* T,
+                           const float* G, const float* MT, const float* gl, void* gq, void* gk,
+                           void* gv, void* gbeta, void* galpha, int B, int L, int H,
                            cudaStream_t st);
 
-size_t edb_delta_chunked_bwd_ws(int B, int L, int H) {
-    return bwd_scratch_bytes((long long)B * H * ((L + C - 1) / C));
+size_t edb_delta_chunked_bwd_ws(int B, int L, int H, int gated) {
+    return bwd_scratch_bytes((long long)B * H * ((L + C - 1) / C), gated != 0);
 }
 
 int edb_delta_chunked_bwd(const void* q, const void* k, const void* v, const void* beta,
-                          const void* dO, const float* resid, void* gq, void* gk, void* gv,
-                          void* gbeta, int B, int L, int H, void* ws, cudaStream_t st) {
+                          const void* alpha, const void* dO, const float* resid, void* gq,
+                          void* gk, void* gv, void* gbeta, void* galpha, int B, int L, int H,
+                          void* ws, cudaStream_t st) {
     const int NC = (L + C - 1) / C;
     const long long units = (long long)B * H, nch = units * NC;
     if ((units * (NC + 1)) * D > 0x7fffffffLL) return EDB_ERR_UNSUPPORTED;
-    BwdScratch w = carve_bwd(ws, nch);
+    const bool gated = alpha != nullptr;
+    BwdScratch w = carve_bwd(ws, nch, gated);
     unsigned* err = edb::device_error_word();
     cudaError_t e;
     PrepOut po{};
@@ -360,23 +404,27 @@ int edb_delta_chunked_bwd(const void* q, const void* k, const void* v, const voi
     po.WnT = w.WnT;
     po.T = w.T;
     po.G = w.G;
-    int s = launch_delta_prep<false>(q, k, dO, beta, po, B, L, H, st);
+    po.Kd = w.Kd;
+    po.QdT = w.QdT;
+    po.gl = w.gl;
+    int s = launch_delta_prep<false>(q, k, dO, beta, alpha, po, B, L, H, st);
     if (s != EDB_OK) return s;
 
+    // gated: the state kernel takes K~ and Q~^T, the post kernel K' (in Kf), K^T, Q^T
     StateBwdMaps sm;
-    if ((s = make_box_map(&sm.Kf, w.Kf, nch * C, D, C))) return s;
+    if ((s = make_box_map(&sm.Kf, gated ? w.Kd : w.Kf, nch * C, D, C))) return s;
     if ((s = make_box_map(&sm.dOT, w.dOT, nch * D, C, D))) return s;
     if ((s = make_box_map(&sm.MT, w.MT, nch * C, C, C))) return s;
-    if ((s = make_box_map(&sm.QT, w.QT, nch * D, C, D))) return s;
+    if ((s = make_box_map(&sm.QT, gated ? w.QdT : w.QT, nch * D, C, D))) return s;
     if ((s = make_box_map(&sm.WnT, w.WnT, nch * D, C, D))) return s;
-    if ((e = cudaFuncSetAttribute(delta_state_bwd_kernel,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, sb::SMEM)) !=
-        cudaSuccess)
+    auto kern = gated ? delta_state_bwd_kernel<true> : delta_state_bwd_kernel<false>;
+    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  sb::SMEM)) != cudaSuccess)
         return (int)e;
-    delta_state_bwd_kernel<<<dim3(H, B), sb::THREADS, sb::SMEM, st>>>(sm, w.dSCT, w.dU, w.dUT, H,
-                                                                       NC, err);
+    kern<<<dim3(H, B), sb::THREADS, sb::SMEM, st>>>(sm, w.gl, w.dSCT, w.dU, w.dUT, H, NC, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
 
-    return edb_delta_chunked_post(resid, dO, v, beta, w.dSCT, w.dU, w.dUT, w.Kf, w.KT, w.QT, w.T,
-                                  w.G, gq, gk, gv, gbeta, B, L, H, st);
+    return edb_delta_chunked_post(resid, dO, v, beta, alpha, w.dSCT, w.dU, w.dUT, w.Kf, w.KT,
+                                  w.QT, w.T, w.G, w.MT, w.gl, gq, gk, gv, gbeta, galpha, B, L, H,
+                                  st);
 }

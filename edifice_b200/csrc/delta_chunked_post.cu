@@ -21,6 +21,17 @@
 // operand is a K-major f32 SWIZZLE_128B tile; the tiles of the later products
 // load (TMA) into the space of the first products' operands while the
 // threads work.
+//
+// GATED (GatedDeltaNet): the prep hands over K' = diag(gamma) K rows (Kf),
+// K K^T o Gamma (G), (M o Gamma)^T and g; the same products then give
+// dQa~ = dO S_0 and dK~ = U~ dS_C unscaled, and three more accumulators keep
+// the parts of dQ and dK whose row scale differs:
+//   dQ = gamma (.) dQa~ + dM~ K                         (dM~ = dM o Gamma)
+//   dK = dM~^T Q + E K + (gamma_C/gamma) (.) dK~ + gamma (.) T_b^T dW
+// with E = dG~ + dG~^T, dG~ = (diag(beta) dA) o Gamma.  The log-decay gradient dg
+// gathers in shared memory (row and column sums of dM o M and dA o A, the row
+// dots with q and k at the read-out, gamma_C <dS_C, S_0> from the phase-A tiles)
+// and dalpha_s = (sum_{t>=s} dg_t) / alpha_s.
 #include <math.h>
 
 #include "delta_chunked.cuh"
@@ -44,11 +55,15 @@ constexpr int OFF_DW = OFF_R1, OFF_DUT = OFF_R1 + 2 * BOX_D;
 constexpr int OFF_TBT = OFF_R1, OFF_E = OFF_R1 + 2 * BOX_C;
 constexpr int OFF_DM = OFF_R4, OFF_DMT = OFF_R4 + 2 * BOX_C;
 constexpr int OFF_BS = OFF_R4 + 4 * BOX_C;  // beta [C]
-constexpr int OFF_BAR = OFF_BS + C * 4;
+constexpr int OFF_GS = OFF_BS + C * 4;      // gated: g [C]
+constexpr int OFF_DG = OFF_GS + C * 4;      // gated: dg [C]
+constexpr int OFF_BAR = OFF_DG + C * 4;
 constexpr int SMEM = OFF_BAR + 64;
 constexpr int PHASE_A_TX = 8 * BOX_D + 8 * BOX_C;  // S_0^T, dS_C^T, U~, dU~
 constexpr int TM_Q = 0, TM_W = 64, TM_K = 128, TM_M = 192, TM_DTB = 256, TM_V = 320,
               TM_COLS = 512;
+// gated: dM~ K (dQ), dM~^T Q + E K (dK) and T_b^T dW (dK, in dM's columns once read)
+constexpr int TM_Q2 = 384, TM_KB = 448, TM_KW = TM_M;
 // SIMT scratch of the C x C chain (floats, in R2..R3): three [C][PS] arrays
 // and one [C]
 constexpr int PS = C + 4;
@@ -67,16 +82,40 @@ static __device__ __forceinline__ void st_f32(uint8_t* base, uint32_t off, float
     *reinterpret_cast<float*>(base + off) = v;
 }
 
+// Butterfly transpose-reduce over the lanes: v[N] per lane, offsets N/2 ... 1
+// (lanes l and l ^ o swap complementary halves and add).  Afterwards lane l's
+// v[0] (N = 32) is the sum over the 32 lanes of element l; for N = 64 over 16
+// lanes, v[0..3] are the sums of elements base + 0..3, base = 32 b3 + 16 b2 +
+// 8 b1 + 4 b0 (b = the lane's bits).
+template <int N, int FIRST>
+static __device__ __forceinline__ void xreduce(float (&v)[N], int lane) {
+#pragma unroll
+    for (int o = FIRST, half = N / 2; o >= 1; o >>= 1, half >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float keep = up ? v[i + half] : v[i];
+            const float send = up ? v[i] : v[i + half];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+}
+
+template <bool GATED>
 __global__ void __launch_bounds__(THREADS, 1)
     delta_post_kernel(const __grid_constant__ PostMaps maps, const __nv_bfloat16* __restrict__ dO,
                       const __nv_bfloat16* __restrict__ v, const __nv_bfloat16* __restrict__ beta,
-                      const float* __restrict__ Tg, const float* __restrict__ Gg,
-                      __nv_bfloat16* __restrict__ gq, __nv_bfloat16* __restrict__ gk,
-                      __nv_bfloat16* __restrict__ gv, __nv_bfloat16* __restrict__ gbeta, int L,
+                      const __nv_bfloat16* __restrict__ alpha, const float* __restrict__ Tg,
+                      const float* __restrict__ Gg, const float* __restrict__ MTg,
+                      const float* __restrict__ glg, __nv_bfloat16* __restrict__ gq,
+                      __nv_bfloat16* __restrict__ gk, __nv_bfloat16* __restrict__ gv,
+                      __nv_bfloat16* __restrict__ gbeta, __nv_bfloat16* __restrict__ galpha, int L,
                       int H, int NC, unsigned* err) {
     extern __shared__ __align__(1024) uint8_t smem[];
     float* sc = reinterpret_cast<float*>(smem + OFF_R2);
     float* bs = reinterpret_cast<float*>(smem + OFF_BS);
+    float* gs = reinterpret_cast<float*>(smem + OFF_GS);
+    float* dg = reinterpret_cast<float*>(smem + OFF_DG);
     uint64_t* bar_ld = reinterpret_cast<uint64_t*>(smem + OFF_BAR);  // [3] TMA groups
     uint64_t* bar_mma = bar_ld + 3;
     uint32_t* s_misc = reinterpret_cast<uint32_t*>(bar_mma + 1);  // [0] tmem, [1] abort
@@ -137,6 +176,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (tid < C)
         bs[tid] = tid < nvalid ? __bfloat162float(beta[((long long)b * L + t0 + tid) * H + h])
                                : 0.0f;
+    if (GATED && tid < C) {
+        gs[tid] = glg[ch * C + tid];
+        dg[tid] = 0.0f;
+    }
     constexpr int NT = C * C / 4 / THREADS;
     float4 tv[NT];
 #pragma unroll
@@ -173,7 +216,30 @@ __global__ void __launch_bounds__(THREADS, 1)
                 ok = false;
             }
         }
-        if (ok) {
+        if (!ok) s_misc[1] = 1;
+    }
+    if (GATED) {
+        // dg_{C-1} += gamma_C <dS_C, S_0>: the two phase-A tiles share one
+        // (swizzled) layout, so the dot runs over their bytes in order.  Warps
+        // 1-7, while warp 0's lane 0 waits on the products.
+        float acc = 0.0f;
+        if (warp > 0) {
+            if (mbar_wait_bounded(&bar_ld[0], 0, err, EDB_DEVERR_DELTA_PIPE)) {
+                const float4* a4 = reinterpret_cast<const float4*>(smem + OFF_R0);
+                const float4* b4 = reinterpret_cast<const float4*>(smem + OFF_R1);
+#pragma unroll 4
+                for (int i = tid - 32; i < R_BYTES / 16; i += THREADS - 32) acc = dot4(a4[i], b4[i], acc);
+            } else {
+                s_misc[1] = 1;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0 && warp > 0) atomicAdd(&dg[C - 1], __expf(gs[C - 1]) * acc);
+        __syncthreads();  // the phase-A tiles are read: their space takes the next loads
+    }
+    if (tid == 0) {
+        if (!s_misc[1]) {
             const int rd = (int)(ch * D), rc = (int)(ch * C);
             mbar_arrive_expect_tx(&bar_ld[1], 4 * BOX_C);
             for (int bx = 0; bx < 4; ++bx)
@@ -185,8 +251,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tma_load_2d(smem + OFF_DUT + bx * BOX_D, &maps.dUT, &bar_ld[2], bx * 32, rd);
             }
             ld_issued = 7;
-        } else {
-            s_misc[1] = 1;
         }
     }
     tc::fence_before_sync();
@@ -276,10 +340,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                                     __uint_as_float(x1[s4 + 2]), __uint_as_float(x1[s4 + 3])));
                 }
             }
+            // gated: M_ts = (M o Gamma)^T[s][t], for the dM o M sums (loads in flight
+            // across the TMEM read)
+            float mv[GATED ? C : 1];
+            if constexpr (GATED) {
+#pragma unroll
+                for (int s = 0; s < C; ++s)
+                    mv[s] = lane < 16 ? MTg[(ch * C + s) * C + t] : 0.0f;
+            }
             tc::tmem_ld32(tmem + TM_M + lane_base, x0);
             tc::tmem_ld32(tmem + TM_M + lane_base + 32, x1);
             tc::tmem_wait_ld();
-            if (lane < 16) {
+            if (!GATED && lane < 16) {
 #pragma unroll
                 for (int s4 = 0; s4 < C; s4 += 4) {
                     float m[4];
@@ -291,6 +363,37 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     st4(reinterpret_cast<float*>(smem + OFF_DM + kmaj_off4(t, s4, C)),
                         make_float4(m[0], m[1], m[2], m[3]));
+                }
+            }
+            if constexpr (GATED) {
+                // dM~ = dM o Gamma into the B tiles; dg_t += rowsum(dM o M),
+                // dg_s -= colsum(dM o M)
+                const float gt = lane < 16 ? gs[t] : 0.0f;
+                float rsum = 0.0f;
+#pragma unroll
+                for (int s4 = 0; s4 < C; s4 += 4) {
+                    float m[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int s = s4 + e;
+                        const float raw = lane < 16 && s <= t ? __uint_as_float(s < 32 ? x0[s] : x1[s - 32]) : 0.0f;
+                        mv[s] *= raw;
+                        rsum += mv[s];
+                        m[e] = s <= t ? raw * __expf(gt - gs[s]) : 0.0f;
+                        if (lane < 16)
+                            st_f32(smem + OFF_DMT, kmaj_off4(s, t & ~3, C) + (t & 3) * 4, m[e]);
+                    }
+                    if (lane < 16)
+                        st4(reinterpret_cast<float*>(smem + OFF_DM + kmaj_off4(t, s4, C)),
+                            make_float4(m[0], m[1], m[2], m[3]));
+                }
+                if (lane < 16) atomicAdd(&dg[t], rsum);
+                xreduce<C, 8>(mv, lane);
+                if (lane < 16) {
+                    const int s0 = 32 * ((lane >> 3) & 1) + 16 * ((lane >> 2) & 1) + 8 * ((lane >> 1) & 1) +
+                                   4 * (lane & 1);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) atomicAdd(&dg[s0 + e], -mv[e]);
                 }
             }
         }
@@ -363,13 +466,34 @@ __global__ void __launch_bounds__(THREADS, 1)
             st4(Ds + (4 * a + r) * PS + 4 * bq, make_float4(dA[r][0], dA[r][1], dA[r][2], dA[r][3]));
         // dbeta_t = sum_s dT_b[t][s]-term (diagonal of X') + sum_{s<t} dA[t][s] (K K^T)[t][s]
         {
-            float p[4];
+            // gated: G holds K K^T o Gamma below the diagonal, A = diag(beta) G there;
+            // dg_t += rowsum(dA o A), dg_s -= colsum(dA o A)
+            float p[4], cs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
                 const float4 g = f4(Gg + (ch * C + 4 * a + r) * C + 4 * bq);
                 p[r] = dA[r][0] * g.x + dA[r][1] * g.y + dA[r][2] * g.z + dA[r][3] * g.w;
+                if (GATED) {
+                    const float bt = bs[4 * a + r];
+                    cs[0] = fmaf(bt * dA[r][0], g.x, cs[0]);
+                    cs[1] = fmaf(bt * dA[r][1], g.y, cs[1]);
+                    cs[2] = fmaf(bt * dA[r][2], g.z, cs[2]);
+                    cs[3] = fmaf(bt * dA[r][3], g.w, cs[3]);
+                }
 #pragma unroll
                 for (int o = 1; o < 16; o <<= 1) p[r] += __shfl_xor_sync(0xffffffffu, p[r], o);
+            }
+            if (GATED) {
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) cs[cc] += __shfl_xor_sync(0xffffffffu, cs[cc], 16);
+                if (lane < 16) {
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc) atomicAdd(&dg[4 * bq + cc], -cs[cc]);
+                }
+                if (bq == 0) {
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) atomicAdd(&dg[4 * a + r], bs[4 * a + r] * p[r]);
+                }
             }
             __syncthreads();  // dA and dbT complete
             if (bq == 0) {
@@ -388,7 +512,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             const float trv[4] = {tr.x, tr.y, tr.z, tr.w};
             const float bc = bs[4 * bq + cc];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) dA[r][cc] = bs[4 * a + r] * dA[r][cc] + bc * trv[r];
+            for (int r = 0; r < 4; ++r) {
+                dA[r][cc] = bs[4 * a + r] * dA[r][cc] + bc * trv[r];
+                if (GATED) {
+                    // one of the two terms is nonzero: Gamma of the pair, later index first
+                    const int t = 4 * a + r, s2 = 4 * bq + cc;
+                    dA[r][cc] *= __expf(t >= s2 ? gs[t] - gs[s2] : gs[s2] - gs[t]);
+                }
+            }
         }
 #pragma unroll
         for (int r = 0; r < 4; ++r)
@@ -413,11 +544,19 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint64_t TbT = kdesc(smem + OFF_TBT, BOX_C, kk);
                 const uint64_t E = kdesc(smem + OFF_E, BOX_C, kk);
                 const uint64_t kA = kdesc(smem + OFF_KT, BOX_D, kk);
-                mma_tf32_ss(tmem + TM_Q, kA, dM, id128, 1);
-                mma_tf32_ss(tmem + TM_V, kdesc(smem + OFF_DUT, BOX_D, kk), TbT, id128, kk > 0);
-                mma_tf32_ss(tmem + TM_K, kdesc(smem + OFF_QT, BOX_D, kk), dMT, id128, 1);
-                mma_tf32_ts(tmem + TM_K, tmem + TM_W + kk * 8, TbT, id128, 1);
-                mma_tf32_ss(tmem + TM_K, kA, E, id128, 1);
+                if (!GATED) {
+                    mma_tf32_ss(tmem + TM_Q, kA, dM, id128, 1);
+                    mma_tf32_ss(tmem + TM_V, kdesc(smem + OFF_DUT, BOX_D, kk), TbT, id128, kk > 0);
+                    mma_tf32_ss(tmem + TM_K, kdesc(smem + OFF_QT, BOX_D, kk), dMT, id128, 1);
+                    mma_tf32_ts(tmem + TM_K, tmem + TM_W + kk * 8, TbT, id128, 1);
+                    mma_tf32_ss(tmem + TM_K, kA, E, id128, 1);
+                } else {
+                    mma_tf32_ss(tmem + TM_Q2, kA, dM, id128, kk > 0);
+                    mma_tf32_ss(tmem + TM_V, kdesc(smem + OFF_DUT, BOX_D, kk), TbT, id128, kk > 0);
+                    mma_tf32_ss(tmem + TM_KB, kdesc(smem + OFF_QT, BOX_D, kk), dMT, id128, kk > 0);
+                    mma_tf32_ss(tmem + TM_KB, kA, E, id128, 1);
+                    mma_tf32_ts(tmem + TM_KW, tmem + TM_W + kk * 8, TbT, id128, kk > 0);
+                }
             }
             tc::commit(bar_mma);
             if (!mbar_wait_bounded(bar_mma, 0, err, EDB_DEVERR_DELTA_PIPE)) {
@@ -436,7 +575,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
-    if (!s_misc[1]) {
+    if (!GATED && !s_misc[1]) {
         // thread (lane quarter, half) -> column j = TMEM lane, tokens [32 hf, 32 hf + 32)
         const int j = (warp & 3) * 32 + lane;
         uint32_t xq[32], xv[32], xk[32];
@@ -457,8 +596,90 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
     }
+    if (GATED && !s_misc[1]) {
+        // thread (lane quarter, half) -> column j = TMEM lane, tokens t = 32 hf + e;
+        // q_t[j], k_t[j] from the Q^T, K^T tiles; dg partials per token, summed
+        // over j by a transpose-reduce and the four warps of the half
+        const int j = (warp & 3) * 32 + lane;
+        const float gC = gs[C - 1];
+        float dgp[32];
+        float k1tot = 0.0f;
+        {
+            uint32_t xa[32], xb[32];
+            tc::tmem_ld32(tmem + TM_Q + lane_base + hf * 32, xa);
+            tc::tmem_ld32(tmem + TM_Q2 + lane_base + hf * 32, xb);
+            tc::tmem_wait_ld();
+            __nv_bfloat16* oq = gq + row0 + j;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                const int t = hf * 32 + e;
+                const float gam = __expf(gs[t]);
+                const float qv = *reinterpret_cast<const float*>(
+                    smem + OFF_QT + kmaj_off4(j, t & ~3, D) + (t & 3) * 4);
+                const float dqa = gam * __uint_as_float(xa[e]);
+                dgp[e] = dqa * qv;
+                if (t < nvalid) oq[t * ts] = __float2bfloat16(dqa + __uint_as_float(xb[e]));
+            }
+        }
+        {
+            uint32_t xa[32];
+            tc::tmem_ld32(tmem + TM_V + lane_base + hf * 32, xa);
+            tc::tmem_wait_ld();
+            __nv_bfloat16* ov = gv + row0 + j;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                const int t = hf * 32 + e;
+                if (t < nvalid) ov[t * ts] = __float2bfloat16(__uint_as_float(xa[e]));
+            }
+        }
+        {
+            uint32_t xa[32], xb[32], xc[32];
+            tc::tmem_ld32(tmem + TM_K + lane_base + hf * 32, xa);
+            tc::tmem_ld32(tmem + TM_KB + lane_base + hf * 32, xb);
+            tc::tmem_ld32(tmem + TM_KW + lane_base + hf * 32, xc);
+            tc::tmem_wait_ld();
+            __nv_bfloat16* ok_ = gk + row0 + j;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                const int t = hf * 32 + e;
+                const float gam = __expf(gs[t]), kap = __expf(gC - gs[t]);
+                const float kv = *reinterpret_cast<const float*>(
+                    smem + OFF_KT + kmaj_off4(j, t & ~3, D) + (t & 3) * 4);
+                const float k1 = kap * __uint_as_float(xa[e]);  // (gamma_C/gamma) dK~
+                const float kw = gam * __uint_as_float(xc[e]);  // gamma T_b^T dW
+                dgp[e] = fmaf(kv, kw - k1, dgp[e]);
+                k1tot = fmaf(kv, k1, k1tot);
+                if (t < nvalid) ok_[t * ts] = __float2bfloat16(__uint_as_float(xb[e]) + k1 + kw);
+            }
+        }
+        xreduce<32, 16>(dgp, lane);
+        atomicAdd(&dg[hf * 32 + lane], dgp[0]);
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) k1tot += __shfl_xor_sync(0xffffffffu, k1tot, o);
+        if (lane == 0) atomicAdd(&dg[C - 1], k1tot);
+    }
     tc::fence_before_sync();
     __syncthreads();
+    if (GATED && !s_misc[1] && warp < 2) {
+        // dlog alpha_s = sum_{t >= s} dg_t (a reverse scan), dalpha_s = that / alpha_s
+        const int s = tid;
+        float acc = dg[s];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_down_sync(0xffffffffu, acc, o);
+            if (lane + o < 32) acc += y;
+        }
+        if (warp == 0) {
+            float tail = dg[32 + lane];
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) tail += __shfl_xor_sync(0xffffffffu, tail, o);
+            acc += tail;
+        }
+        if (s < nvalid) {
+            const long long ai = ((long long)b * L + t0 + s) * H + h;
+            galpha[ai] = __float2bfloat16(acc / __bfloat162float(alpha[ai]));
+        }
+    }
     if (warp == 0) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, TM_COLS);
@@ -469,9 +690,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // Library-internal launcher (called by edb_delta_chunked_bwd).
 int edb_delta_chunked_post(const float* resid, const void* dO, const void* v, const void* beta,
-                           const float* dSCT, const float* dU, const float* dUT, const float* Kf,
-                           const float* KT, const float* QT, const float* T, const float* G,
-                           void* gq, void* gk, void* gv, void* gbeta, int B, int L, int H,
+                           const void* alpha, const float* dSCT, const float* dU, const float* dUT,
+                           const float* Kf, const float* KT, const float* QT, const float* T,
+                           const float* G, const float* MT, const float* gl, void* gq, void* gk,
+                           void* gv, void* gbeta, void* galpha, int B, int L, int H,
                            cudaStream_t st) {
     const int NC = (L + C - 1) / C;
     const long long units = (long long)B * H, nch = units * NC;
@@ -485,12 +707,13 @@ int edb_delta_chunked_post(const float* resid, const void* dO, const void* v, co
     if ((s = make_box_map(&m.KT, KT, nch * D, C, D))) return s;
     if ((s = make_box_map(&m.QT, QT, nch * D, C, D))) return s;
     if ((s = make_box_map(&m.dUT, dUT, nch * D, C, D))) return s;
-    cudaError_t e = cudaFuncSetAttribute(delta_post_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    auto kern = alpha != nullptr ? delta_post_kernel<true> : delta_post_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (e != cudaSuccess) return (int)e;
-    delta_post_kernel<<<dim3(NC, H, B), THREADS, SMEM, st>>>(
-        m, (const __nv_bfloat16*)dO, (const __nv_bfloat16*)v, (const __nv_bfloat16*)beta, T, G,
-        (__nv_bfloat16*)gq, (__nv_bfloat16*)gk, (__nv_bfloat16*)gv, (__nv_bfloat16*)gbeta, L, H,
-        NC, edb::device_error_word());
+    kern<<<dim3(NC, H, B), THREADS, SMEM, st>>>(
+        m, (const __nv_bfloat16*)dO, (const __nv_bfloat16*)v, (const __nv_bfloat16*)beta,
+        (const __nv_bfloat16*)alpha, T, G, MT, gl, (__nv_bfloat16*)gq, (__nv_bfloat16*)gk,
+        (__nv_bfloat16*)gv, (__nv_bfloat16*)gbeta, (__nv_bfloat16*)galpha, L, H, NC,
+        edb::device_error_word());
     return edb::status_from_cuda(cudaGetLastError());
 }

@@ -695,12 +695,14 @@ int check(int dtype, int B, int L, int H, int d) {
 bool edb_delta_chunked_ok(int dtype, int beta_per_element, int head_dim);
 size_t edb_delta_chunked_ckpt_bytes(int B, int L, int H);
 size_t edb_delta_chunked_fwd_ws(int B, int L, int H);
-size_t edb_delta_chunked_bwd_ws(int B, int L, int H);
-int edb_delta_chunked_fwd(const void* q, const void* k, const void* v, const void* beta, void* o,
-                          float* resid, int B, int L, int H, void* ws, cudaStream_t st);
+size_t edb_delta_chunked_bwd_ws(int B, int L, int H, int gated);
+int edb_delta_chunked_fwd(const void* q, const void* k, const void* v, const void* beta,
+                          const void* alpha, void* o, float* resid, int B, int L, int H, void* ws,
+                          cudaStream_t st);
 int edb_delta_chunked_bwd(const void* q, const void* k, const void* v, const void* beta,
-                          const void* dO, const float* resid, void* gq, void* gk, void* gv,
-                          void* gbeta, int B, int L, int H, void* ws, cudaStream_t st);
+                          const void* alpha, const void* dO, const float* resid, void* gq,
+                          void* gk, void* gv, void* gbeta, void* galpha, int B, int L, int H,
+                          void* ws, cudaStream_t st);
 
 extern "C" size_t edb_delta_rule_ckpt_bytes(int dtype, int beta_per_element, int batch,
                                             int seq_len, int heads, int head_dim) {
@@ -732,8 +734,8 @@ extern "C" int edb_delta_rule_fwd(int dtype, const void* q, const void* k, const
             !edb::aligned16(workspace) ||
             (reinterpret_cast<uintptr_t>(s_ckpt) & 15u))
             return EDB_ERR_MISALIGNED;
-        return edb_delta_chunked_fwd(q, k, v, beta, o, s_ckpt, batch, seq_len, heads, workspace,
-                                     st);
+        return edb_delta_chunked_fwd(q, k, v, beta, nullptr, o, s_ckpt, batch, seq_len, heads,
+                                     workspace, st);
     }
     const int bs = beta_per_element ? 0 : 1;
     return dtype == EDB_BF16
@@ -753,7 +755,7 @@ extern "C" size_t edb_delta_rule_bwd_workspace(int dtype, int beta_per_element, 
     if (edb_delta_chunked_ok(dtype, beta_per_element, head_dim)) {
         // residuals (when not passed), then the forward's or the backward's scratch
         const size_t f = edb_delta_chunked_fwd_ws(batch, seq_len, heads);
-        const size_t b = edb_delta_chunked_bwd_ws(batch, seq_len, heads);
+        const size_t b = edb_delta_chunked_bwd_ws(batch, seq_len, heads, 0);
         return ck + (have_ckpt ? b : (f > b ? f : b));
     }
     // checkpoints (when not passed), then the row-parallel backward's scratch
@@ -785,13 +787,13 @@ extern "C" int edb_delta_rule_bwd(int dtype, const void* q, const void* k, const
         if (!resid) {
             // residuals into the workspace; o goes to gq, which the backward overwrites
             float* r = static_cast<float*>(workspace);
-            int s = edb_delta_chunked_fwd(q, k, v, beta, gq, r, batch, seq_len, heads, scratch,
-                                          st);
+            int s = edb_delta_chunked_fwd(q, k, v, beta, nullptr, gq, r, batch, seq_len, heads,
+                                          scratch, st);
             if (s) return s;
             resid = r;
         }
-        return edb_delta_chunked_bwd(q, k, v, beta, dO, resid, gq, gk, gv, gbeta, batch, seq_len,
-                                     heads, scratch, st);
+        return edb_delta_chunked_bwd(q, k, v, beta, nullptr, dO, resid, gq, gk, gv, gbeta,
+                                     nullptr, batch, seq_len, heads, scratch, st);
     }
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return EDB_ERR_MISALIGNED;
     const int bs = beta_per_element ? 0 : 1;
@@ -814,12 +816,48 @@ extern "C" int edb_delta_rule_bwd(int dtype, const void* q, const void* k, const
 }
 
 // ------------------------------------------------------------------ GatedDeltaNet
-// Token recurrence only (the chunked tensor-core form serves the ungated rule).
+// bf16 io, one beta per (token, head), head_dim 128: the chunked tensor-core form
+// (delta_chunked*.cu with the decay); every other case the token recurrence.
+// The residual (s_ckpt) format follows the path, as for the delta rule.
 extern "C" size_t edb_gated_delta_net_ckpt_bytes(int dtype, int beta_per_element, int batch,
                                                  int seq_len, int heads, int head_dim) {
-    (void)beta_per_element;
     if (check(dtype, batch, seq_len, heads, head_dim)) return 0;
-    return ckpt_bytes(batch, seq_len, heads, head_dim);
+    return edb_delta_chunked_ok(dtype, beta_per_element, head_dim)
+               ? edb_delta_chunked_ckpt_bytes(batch, seq_len, heads)
+               : ckpt_bytes(batch, seq_len, heads, head_dim);
+}
+
+extern "C" size_t edb_gated_delta_net_fwd_workspace(int dtype, int beta_per_element, int batch,
+                                                    int seq_len, int heads, int head_dim) {
+    if (check(dtype, batch, seq_len, heads, head_dim)) return 0;
+    return edb_delta_chunked_ok(dtype, beta_per_element, head_dim)
+               ? edb_delta_chunked_fwd_ws(batch, seq_len, heads)
+               : 0;
+}
+
+extern "C" int edb_gated_delta_net_fwd_ws(int dtype, const void* q, const void* k, const void* v,
+                                          const void* beta, int beta_per_element,
+                                          const void* alpha, void* o, float* s_ckpt, int batch,
+                                          int seq_len, int heads, int head_dim, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+    if (int s = check(dtype, batch, seq_len, heads, head_dim)) return s;
+    if (!q || !k || !v || !beta || !alpha || !o) return EDB_ERR_NULL_POINTER;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (edb_delta_chunked_ok(dtype, beta_per_element, head_dim)) {
+        const size_t need = edb_delta_chunked_fwd_ws(batch, seq_len, heads);
+        if (workspace_bytes < need || !workspace) return EDB_ERR_WORKSPACE_TOO_SMALL;
+        if (!edb::aligned16(q) || !edb::aligned16(k) || !edb::aligned16(v) ||
+            !edb::aligned16(workspace) || (reinterpret_cast<uintptr_t>(s_ckpt) & 15u))
+            return EDB_ERR_MISALIGNED;
+        return edb_delta_chunked_fwd(q, k, v, beta, alpha, o, s_ckpt, batch, seq_len, heads,
+                                     workspace, st);
+    }
+    const int bs = beta_per_element ? 0 : 1;
+    return dtype == EDB_BF16
+               ? launch_fwd<__nv_bfloat16>(q, k, v, beta, alpha, o, s_ckpt, batch, seq_len,
+                                           heads, head_dim, bs, st)
+               : launch_fwd<float>(q, k, v, beta, alpha, o, s_ckpt, batch, seq_len, heads,
+                                   head_dim, bs, st);
 }
 
 extern "C" int edb_gated_delta_net_fwd(int dtype, const void* q, const void* k, const void* v,
@@ -828,13 +866,22 @@ extern "C" int edb_gated_delta_net_fwd(int dtype, const void* q, const void* k, 
                                        int head_dim, void* stream) {
     if (int s = check(dtype, batch, seq_len, heads, head_dim)) return s;
     if (!q || !k || !v || !beta || !alpha || !o) return EDB_ERR_NULL_POINTER;
-    const int bs = beta_per_element ? 0 : 1;
+    const size_t wsb = edb_gated_delta_net_fwd_workspace(dtype, beta_per_element, batch,
+                                                         seq_len, heads, head_dim);
+    if (wsb == 0)
+        return edb_gated_delta_net_fwd_ws(dtype, q, k, v, beta, beta_per_element, alpha, o,
+                                          s_ckpt, batch, seq_len, heads, head_dim, nullptr, 0,
+                                          stream);
+    // the chunked form's scratch, taken stream-ordered (no workspace argument here)
     cudaStream_t st = (cudaStream_t)stream;
-    return dtype == EDB_BF16
-               ? launch_fwd<__nv_bfloat16>(q, k, v, beta, alpha, o, s_ckpt, batch, seq_len,
-                                           heads, head_dim, bs, st)
-               : launch_fwd<float>(q, k, v, beta, alpha, o, s_ckpt, batch, seq_len, heads,
-                                   head_dim, bs, st);
+    void* ws = nullptr;
+    cudaError_t e = cudaMallocAsync(&ws, wsb, st);
+    if (e != cudaSuccess) return (int)e;
+    const int s = edb_gated_delta_net_fwd_ws(dtype, q, k, v, beta, beta_per_element, alpha, o,
+                                             s_ckpt, batch, seq_len, heads, head_dim, ws, wsb,
+                                             stream);
+    cudaFreeAsync(ws, st);
+    return s;
 }
 
 extern "C" size_t edb_gated_delta_net_bwd_workspace(int dtype, int beta_per_element, int batch,
@@ -845,6 +892,11 @@ extern "C" size_t edb_gated_delta_net_bwd_workspace(int dtype, int beta_per_elem
                                 : a256(edb_gated_delta_net_ckpt_bytes(dtype, beta_per_element,
                                                                       batch, seq_len, heads,
                                                                       head_dim));
+    if (edb_delta_chunked_ok(dtype, beta_per_element, head_dim)) {
+        const size_t f = edb_delta_chunked_fwd_ws(batch, seq_len, heads);
+        const size_t b = edb_delta_chunked_bwd_ws(batch, seq_len, heads, 1);
+        return ck + (have_ckpt ? b : (f > b ? f : b));
+    }
     return ck + rows_bwd_ws_bytes(batch, seq_len, heads, head_dim);
 }
 
@@ -864,17 +916,37 @@ extern "C" int edb_gated_delta_net_bwd(int dtype, const void* q, const void* k, 
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return EDB_ERR_MISALIGNED;
     cudaStream_t st = (cudaStream_t)stream;
     char* p = static_cast<char*>(workspace);
+    const size_t ckb = s_ckpt ? 0
+                              : a256(edb_gated_delta_net_ckpt_bytes(dtype, beta_per_element,
+                                                                    batch, seq_len, heads,
+                                                                    head_dim));
+    if (edb_delta_chunked_ok(dtype, beta_per_element, head_dim)) {
+        if (!edb::aligned16(q) || !edb::aligned16(k) || !edb::aligned16(v) ||
+            !edb::aligned16(dO) || (reinterpret_cast<uintptr_t>(s_ckpt) & 15u))
+            return EDB_ERR_MISALIGNED;
+        const float* resid = s_ckpt;
+        char* scratch = p + ckb;
+        if (!resid) {
+            // residuals into the workspace; o goes to gq, which the backward overwrites
+            float* r = reinterpret_cast<float*>(p);
+            int s = edb_delta_chunked_fwd(q, k, v, beta, alpha, gq, r, batch, seq_len, heads,
+                                          scratch, st);
+            if (s) return s;
+            resid = r;
+        }
+        return edb_delta_chunked_bwd(q, k, v, beta, alpha, dO, resid, gq, gk, gv, gbeta, galpha,
+                                     batch, seq_len, heads, scratch, st);
+    }
     const float* ck = s_ckpt;
     if (!ck) {
         // states only: the forward writes o into gq, which the backward overwrites
         float* w = reinterpret_cast<float*>(p);
-        p += a256(edb_gated_delta_net_ckpt_bytes(dtype, beta_per_element, batch, seq_len, heads,
-                                                 head_dim));
-        int s = edb_gated_delta_net_fwd(dtype, q, k, v, beta, beta_per_element, alpha, gq, w,
-                                        batch, seq_len, heads, head_dim, stream);
+        int s = edb_gated_delta_net_fwd_ws(dtype, q, k, v, beta, beta_per_element, alpha, gq, w,
+                                           batch, seq_len, heads, head_dim, nullptr, 0, stream);
         if (s) return s;
         ck = w;
     }
+    p += ckb;
     const int bs = beta_per_element ? 0 : 1;
     return dtype == EDB_BF16
                ? launch_bwd_rows<__nv_bfloat16>(q, k, v, beta, alpha, dO, ck, p, gq, gk, gv,

@@ -500,9 +500,11 @@ extern "C" int edb_selective_scan_bwd_desc(const edb_selective_scan_args* args, 
                                                                      ck)                      \
                                  : edb_delta_rule_bwd_workspace(args->dtype, ix.bpe, ix.B,    \
                                                                 ix.L, ix.H, ix.d, ck);        \
-            else if (!ix.gated)                                                               \
-                inner = edb_delta_rule_fwd_workspace(args->dtype, ix.bpe, ix.B, ix.L, ix.H,   \
-                                                     ix.d);                                   \
+            else                                                                              \
+                inner = ix.gated ? edb_gated_delta_net_fwd_workspace(args->dtype, ix.bpe,     \
+                                                                     ix.B, ix.L, ix.H, ix.d)  \
+                                 : edb_delta_rule_fwd_workspace(args->dtype, ix.bpe, ix.B,    \
+                                                                ix.L, ix.H, ix.d);            \
         }                                                                                     \
         return st;                                                                            \
     }
@@ -517,10 +519,10 @@ extern "C" int edb_delta_rule_fwd_desc(const edb_delta_rule_args* args, void* st
     return run(PREP_DELTA(false),
                [&](Plan& p, void* scratch, size_t scratch_bytes) {
                    if (ix.gated)
-                       return edb_gated_delta_net_fwd(args->dtype, p.ptr(ix.q), p.ptr(ix.k),
-                                                      p.ptr(ix.v), p.ptr(ix.beta), ix.bpe,
-                                                      p.ptr(ix.alpha), p.ptr(ix.o), args->s_ckpt,
-                                                      ix.B, ix.L, ix.H, ix.d, stream);
+                       return edb_gated_delta_net_fwd_ws(
+                           args->dtype, p.ptr(ix.q), p.ptr(ix.k), p.ptr(ix.v), p.ptr(ix.beta),
+                           ix.bpe, p.ptr(ix.alpha), p.ptr(ix.o), args->s_ckpt, ix.B, ix.L, ix.H,
+                           ix.d, scratch, scratch_bytes, stream);
                    return edb_delta_rule_fwd(args->dtype, p.ptr(ix.q), p.ptr(ix.k), p.ptr(ix.v),
                                              p.ptr(ix.beta), ix.bpe, p.ptr(ix.o), args->s_ckpt,
                                              ix.B, ix.L, ix.H, ix.d, scratch, scratch_bytes,

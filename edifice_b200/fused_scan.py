@@ -519,8 +519,9 @@ def _gated_shapes(q, k, v, beta, alpha):
 def gated_delta_net_scan(q, k, v, beta, alpha, with_ckpt=False):
     """FusedScan.gated_delta_net_scan/5 (fused_scan.ex:219-233): q, k (L2-normalised),
     v [B, L, H, d]; beta (post-sigmoid) [B, L, H, d] or [B, L, H]; alpha (decay)
-    [B, L, H] -> o [B, L, H, d].  with_ckpt=True also returns the f32 chunk-start
-    states the backward can reuse."""
+    [B, L, H] -> o [B, L, H, d].  with_ckpt=True also returns the f32 residuals the
+    backward can reuse (the chunk-start states; for the chunked form, bf16 with a
+    per-token beta and d = 128, transposed and followed by the chunk errors)."""
     _dev(q, k, v, beta, alpha, what="gated_delta_net_scan")
     B, L, H, d, per_el = _gated_shapes(q, k, v, beta, alpha)
     o = torch.empty_like(q)
@@ -530,8 +531,12 @@ def gated_delta_net_scan(q, k, v, beta, alpha, with_ckpt=False):
     if with_ckpt:
         ck = torch.empty(lib.edb_gated_delta_net_ckpt_bytes(dt, per_el, B, L, H, d) // 4,
                          dtype=torch.float32, device=q.device)
-    _lib.check(lib.edb_gated_delta_net_fwd(dt, _p(q), _p(k), _p(v), _p(beta), per_el, _p(alpha),
-                                           _p(o), _p(ck), B, L, H, d, _stream()),
+    # the chunked tensor-core form (bf16, one beta per token, d = 128) takes a workspace
+    wsb = lib.edb_gated_delta_net_fwd_workspace(dt, per_el, B, L, H, d)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=q.device) if wsb else None
+    _lib.check(lib.edb_gated_delta_net_fwd_ws(dt, _p(q), _p(k), _p(v), _p(beta), per_el,
+                                              _p(alpha), _p(o), _p(ck), B, L, H, d, _p(ws), wsb,
+                                              _stream()),
                "CUDA fused GatedDeltaNet scan")
     return (o, ck) if with_ckpt else o
 

@@ -357,8 +357,9 @@ int edb_convert(int src_dtype, const void* src, int dst_dtype, void* dst, size_t
  * s_ckpt (optional, f32, edb_delta_rule_ckpt_bytes() bytes): residuals the
  * forward leaves for edb_delta_rule_bwd of the same dtype, beta form and shape.
  * Token recurrence: S ([head_dim][head_dim], value index first) at the start
- * of every 64-token chunk and the final S, [batch][heads][nchunks + 1][d][d].
- * Chunked form: the same states transposed (key index first), followed by the
+ * of every 16-token piece and the final S, [batch][heads][npieces + 1][d][d].
+ * Chunked form: S^T (key index first) at the start of every 64-token chunk
+ * and the final one, [batch * heads][nchunks + 1][d][d], followed by the
  * per-chunk errors U~ = U0 - W S_0^T, [batch * heads][nchunks][64][d].
  * Replaces fused_delta_net_scan_launch / fused_delta_rule_scan_launch with
  * alpha = NULL (native/cuda/fused_delta_rule_scan.cu:213-258); Nx semantics
@@ -399,10 +400,15 @@ int edb_delta_rule_bwd(int dtype, const void* q, const void* k, const void* v, c
  * S_t = S_d + (beta_t (.) (v_t - r)) k_t^T; o_t = S_t q_t (S_0 = 0).
  * q, k, v, o, beta as edb_delta_rule_fwd; alpha: [batch, seq_len, heads]
  * (one decay per token and head, Edifice.build(:gated_delta_net)'s form,
- * lib/edifice/recurrent/gated_delta_net.ex:389-394).  head_dim <= 128; token
- * recurrence for every dtype and beta form.  s_ckpt (optional, f32,
- * edb_gated_delta_net_ckpt_bytes() bytes): S at the start of every 64-token
- * chunk and the final S, [batch][heads][nchunks + 1][d][d].
+ * lib/edifice/recurrent/gated_delta_net.ex:389-394).  head_dim <= 128.
+ * bf16 with one beta per (token, head) and head_dim 128 takes the chunked
+ * tensor-core form (64-token chunks, the decay folded into the chunk products);
+ * every other case the token recurrence.  s_ckpt (optional, f32,
+ * edb_gated_delta_net_ckpt_bytes() bytes) follows the path as for
+ * edb_delta_rule_fwd: token recurrence, S at the start of every 16-token piece
+ * and the final S, [batch][heads][npieces + 1][d][d]; chunked form, S^T at the
+ * start of every 64-token chunk and the final one, followed by the per-chunk
+ * errors U~.
  * Replaces fused_gated_delta_net_scan_launch / fused_delta_rule_scan_launch
  * with alpha (native/cuda/fused_delta_rule_scan.cu:213-258); Nx semantics
  * lib/edifice/cuda/fused_scan.ex:2256-2284.
@@ -410,13 +416,27 @@ int edb_delta_rule_bwd(int dtype, const void* q, const void* k, const void* v, c
 size_t edb_gated_delta_net_ckpt_bytes(int dtype, int beta_per_element, int batch, int seq_len,
                                       int heads, int head_dim);
 
+/* Workspace bytes edb_gated_delta_net_fwd_ws needs (0 for the token recurrence). */
+size_t edb_gated_delta_net_fwd_workspace(int dtype, int beta_per_element, int batch,
+                                         int seq_len, int heads, int head_dim);
+
+/* The forward with a caller-owned workspace (16-byte aligned, at least
+ * edb_gated_delta_net_fwd_workspace() bytes): no allocation inside. */
+int edb_gated_delta_net_fwd_ws(int dtype, const void* q, const void* k, const void* v,
+                               const void* beta, int beta_per_element, const void* alpha, void* o,
+                               float* s_ckpt, int batch, int seq_len, int heads, int head_dim,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* The same forward without a workspace argument: the chunked form takes its
+ * scratch stream-ordered (cudaMallocAsync / cudaFreeAsync on `stream`). */
 int edb_gated_delta_net_fwd(int dtype, const void* q, const void* k, const void* v,
                             const void* beta, int beta_per_element, const void* alpha, void* o,
                             float* s_ckpt, int batch, int seq_len, int heads, int head_dim,
                             void* stream);
 
-/* Workspace bytes edb_gated_delta_net_bwd needs (a buffer of one chunk's 64
- * states per (batch, head), plus the checkpoints when have_ckpt == 0). */
+/* Workspace bytes edb_gated_delta_net_bwd needs (the token recurrence: a buffer
+ * of one chunk's 64 states per (batch, head); the chunked form: its per-chunk
+ * scratch; plus the residuals when have_ckpt == 0). */
 size_t edb_gated_delta_net_bwd_workspace(int dtype, int beta_per_element, int batch,
                                          int seq_len, int heads, int head_dim, int have_ckpt);
 

@@ -194,3 +194,28 @@ def test_descriptor_attention_variants_need_their_residuals():
     nr.x0 = nr.x1 = D.tensor(base, _lib.EDB_F32, (2, 8, 16))
     nr.h = D.tensor(base, _lib.EDB_F32, (2, 8, 16), (128, 1, 8))
     assert lib.edb_native_rec_fwd_desc_workspace(ctypes.byref(nr)) == 1024
+
+
+def test_gated_chunked_form_sizes():
+    """bf16 with one beta per token and head_dim 128 takes the chunked form: a
+    forward workspace and the chunked residual layout (S^T per chunk start and the
+    final one, then the chunk errors U~); the token recurrence needs none."""
+    lib = edifice_b200.load()
+    B, L, H, d, C = 2, 130, 3, 128, 64
+    nc = (L + C - 1) // C
+    assert lib.edb_gated_delta_net_fwd_workspace(1, 0, B, L, H, d) > 0
+    assert lib.edb_gated_delta_net_ckpt_bytes(1, 0, B, L, H, d) == \
+        4 * B * H * ((nc + 1) * d * d + nc * C * d)
+    assert lib.edb_gated_delta_net_ckpt_bytes(1, 0, B, L, H, d) == \
+        lib.edb_delta_rule_ckpt_bytes(1, 0, B, L, H, d)
+    for dt, per_el, dd in ((0, 0, 128), (1, 1, 128), (1, 0, 64)):
+        assert lib.edb_gated_delta_net_fwd_workspace(dt, per_el, B, L, H, dd) == 0
+        # token recurrence: S every 16 tokens and the final S
+        assert lib.edb_gated_delta_net_ckpt_bytes(dt, per_el, B, L, H, dd) == \
+            4 * B * H * ((L + 15) // 16 + 1) * dd * dd
+    dummy = ctypes.c_void_p(16)
+    # a chunked-form call with a null alpha is refused before any allocation
+    assert lib.edb_gated_delta_net_fwd(1, dummy, dummy, dummy, dummy, 0, None, dummy, None, B,
+                                       L, H, d, None) == 1000
+    assert lib.edb_gated_delta_net_fwd_ws(1, dummy, dummy, dummy, dummy, 0, dummy, dummy, None,
+                                          B, L, H, d, None, 0, None) == 1004

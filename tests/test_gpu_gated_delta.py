@@ -133,3 +133,80 @@ def test_gated_autograd_fn(cuda):
     ref = O.gated_delta_net_bwd(*[_np(t) for t in (q, k, v, beta, alpha)], _np(do))
     for leaf, r in zip(leaves, ref):
         assert O.norm_rel(_np(leaf.grad), r) <= 1e-4
+
+
+# ---------------------------------------------------------------- chunked form
+# bf16, one beta per (token, head), head_dim 128: the chunked tensor-core kernels
+# with the decay folded into the chunk products (tf32 operands, f32 accumulation).
+CHUNKED = [
+    (1, 64, 1),     # one full chunk
+    (2, 130, 3),    # ragged last chunk
+    (1, 300, 2),
+    (2, 1000, 2),   # sixteen chunks per (batch, head)
+]
+
+
+def _chunked(B, L, H):
+    from edifice_b200 import _lib
+    return _lib.load().edb_gated_delta_net_fwd_workspace(1, 0, B, L, H, 128) > 0
+
+
+@pytest.mark.parametrize("case", CHUNKED)
+@pytest.mark.parametrize("alpha_lo", [0.05, 0.01])
+@pytest.mark.parametrize("use_ckpt", [False, True])
+def test_chunked_gated_parity(cuda, case, alpha_lo, use_ckpt):
+    B, L, H = case
+    assert _chunked(B, L, H)
+    q, k, v, beta, alpha, do = gated_inputs(B, L, H, 128, torch.bfloat16, seed=70 + L,
+                                            scalar_beta=True, alpha_lo=alpha_lo)
+    if use_ckpt:
+        o, ck = fs.gated_delta_net_scan(q, k, v, beta, alpha, with_ckpt=True)
+    else:
+        o, ck = fs.gated_delta_net_scan(q, k, v, beta, alpha), None
+    grads = fs.gated_delta_net_backward(q, k, v, beta, alpha, do, ck)
+    torch.cuda.synchronize()
+    args = [_np(t) for t in (q, k, v, beta, alpha)]
+    assert O.norm_rel(_np(o), O.gated_delta_net_fwd(*args)) <= TOL[torch.bfloat16]
+    ref = O.gated_delta_net_bwd(*args, _np(do))
+    for name, got, r in zip(("q", "k", "v", "beta", "alpha"), grads, ref):
+        assert got.shape == torch.Size(r.shape)
+        assert torch.isfinite(got.float()).all(), name
+        err = O.norm_rel(_np(got), r)
+        assert err <= TOL[torch.bfloat16], (name, err)
+    assert device_errors() == 0
+
+
+def test_chunked_gated_alpha_one_is_the_delta_rule(cuda):
+    """alpha == 1 through the chunked gated kernels equals the chunked delta rule
+    (gamma = 1 everywhere, so every product matches up to summation order)."""
+    q, k, v, beta, alpha, do = gated_inputs(2, 200, 2, 128, torch.bfloat16, seed=71,
+                                            scalar_beta=True)
+    one = torch.ones_like(alpha)
+    o = fs.gated_delta_net_scan(q, k, v, beta, one)
+    g = fs.gated_delta_net_backward(q, k, v, beta, one, do)
+    o_ref = fs.delta_net_scan(q, k, v, beta)
+    g_ref = fs.delta_rule_backward(q, k, v, beta, do)
+    torch.cuda.synchronize()
+    assert O.norm_rel(_np(o), _np(o_ref)) <= 1e-2
+    for a, b_ in zip(g[:4], g_ref):
+        assert O.norm_rel(_np(a), _np(b_)) <= 1e-2
+
+
+def test_chunked_gated_no_workspace_entry(cuda):
+    """edb_gated_delta_net_fwd (no workspace argument, stream-ordered scratch) gives
+    the same bits as the workspace entry point."""
+    from edifice_b200 import _lib
+    lib = _lib.load()
+    B, L, H, d = 1, 150, 2, 128
+    q, k, v, beta, alpha, do = gated_inputs(B, L, H, d, torch.bfloat16, seed=72,
+                                            scalar_beta=True)
+    o_ref, ck_ref = fs.gated_delta_net_scan(q, k, v, beta, alpha, with_ckpt=True)
+    o = torch.empty_like(q)
+    ck = torch.empty_like(ck_ref)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert lib.edb_gated_delta_net_fwd(1, P(q), P(k), P(v), P(beta), 0, P(alpha), P(o), P(ck),
+                                       B, L, H, d, st) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(o, o_ref)
+    assert torch.equal(ck, ck_ref)
