@@ -64,6 +64,9 @@ constexpr int TM_Q = 0, TM_W = 64, TM_K = 128, TM_M = 192, TM_DTB = 256, TM_V = 
               TM_COLS = 512;
 // gated: dM~ K (dQ), dM~^T Q + E K (dK) and T_b^T dW (dK, in dM's columns once read)
 constexpr int TM_Q2 = 384, TM_KB = 448, TM_KW = TM_M;
+// gated read-out: per-(token, column) dg partials [C][DGP] in the chain scratch
+constexpr int DGP = D + 4;
+static_assert(C * DGP * 4 <= 8 * BOX_C, "dg partials fit R2-R3");
 // SIMT scratch of the C x C chain (floats, in R2..R3): three [C][PS] arrays
 // and one [C]
 constexpr int PS = C + 4;
@@ -80,25 +83,6 @@ static __device__ __forceinline__ float4 f4(const float* p) {
 }
 static __device__ __forceinline__ void st_f32(uint8_t* base, uint32_t off, float v) {
     *reinterpret_cast<float*>(base + off) = v;
-}
-
-// Butterfly transpose-reduce over the lanes: v[N] per lane, offsets N/2 ... 1
-// (lanes l and l ^ o swap complementary halves and add).  Afterwards lane l's
-// v[0] (N = 32) is the sum over the 32 lanes of element l; for N = 64 over 16
-// lanes, v[0..3] are the sums of elements base + 0..3, base = 32 b3 + 16 b2 +
-// 8 b1 + 4 b0 (b = the lane's bits).
-template <int N, int FIRST>
-static __device__ __forceinline__ void xreduce(float (&v)[N], int lane) {
-#pragma unroll
-    for (int o = FIRST, half = N / 2; o >= 1; o >>= 1, half >>= 1) {
-        const bool up = (lane & o) != 0;
-#pragma unroll
-        for (int i = 0; i < half; ++i) {
-            const float keep = up ? v[i + half] : v[i];
-            const float send = up ? v[i] : v[i + half];
-            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-        }
-    }
 }
 
 template <bool GATED>
@@ -200,7 +184,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             ld_landed = 1;
             tc::fence_after_sync();
             constexpr uint32_t id128 = idesc_tf32(128, C), id64 = idesc_tf32(64, C);
-#pragma unroll
+#pragma unroll 1
             for (int kk = 0; kk < D / 8; ++kk) {
                 const uint64_t s0 = kdesc(smem + OFF_R0, BOX_D, kk);
                 const uint64_t dof = kdesc(smem + OFF_R4, BOX_C, kk);
@@ -293,7 +277,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             ld_landed |= 2;
             tc::fence_after_sync();
             constexpr uint32_t id64 = idesc_tf32(64, C);
-#pragma unroll
+#pragma unroll 1
             for (int kk = 0; kk < D / 8; ++kk) {
                 mma_tf32_ss(tmem + TM_DTB, kdesc(smem + OFF_DW, BOX_C, kk),
                             kdesc(smem + OFF_R2, BOX_C, kk), id64, kk > 0);
@@ -340,18 +324,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                                     __uint_as_float(x1[s4 + 2]), __uint_as_float(x1[s4 + 3])));
                 }
             }
-            // gated: M_ts = (M o Gamma)^T[s][t], for the dM o M sums (loads in flight
-            // across the TMEM read)
-            float mv[GATED ? C : 1];
-            if constexpr (GATED) {
-#pragma unroll
-                for (int s = 0; s < C; ++s)
-                    mv[s] = lane < 16 ? MTg[(ch * C + s) * C + t] : 0.0f;
-            }
             tc::tmem_ld32(tmem + TM_M + lane_base, x0);
             tc::tmem_ld32(tmem + TM_M + lane_base + 32, x1);
             tc::tmem_wait_ld();
-            if (!GATED && lane < 16) {
+            if (lane < 16) {
 #pragma unroll
                 for (int s4 = 0; s4 < C; s4 += 4) {
                     float m[4];
@@ -359,41 +335,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int e = 0; e < 4; ++e) {
                         const int s = s4 + e;
                         m[e] = s <= t ? __uint_as_float(s < 32 ? x0[s] : x1[s - 32]) : 0.0f;
-                        st_f32(smem + OFF_DMT, kmaj_off4(s, t & ~3, C) + (t & 3) * 4, m[e]);
+                        if (!GATED)
+                            st_f32(smem + OFF_DMT, kmaj_off4(s, t & ~3, C) + (t & 3) * 4, m[e]);
                     }
                     st4(reinterpret_cast<float*>(smem + OFF_DM + kmaj_off4(t, s4, C)),
                         make_float4(m[0], m[1], m[2], m[3]));
-                }
-            }
-            if constexpr (GATED) {
-                // dM~ = dM o Gamma into the B tiles; dg_t += rowsum(dM o M),
-                // dg_s -= colsum(dM o M)
-                const float gt = lane < 16 ? gs[t] : 0.0f;
-                float rsum = 0.0f;
-#pragma unroll
-                for (int s4 = 0; s4 < C; s4 += 4) {
-                    float m[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int s = s4 + e;
-                        const float raw = lane < 16 && s <= t ? __uint_as_float(s < 32 ? x0[s] : x1[s - 32]) : 0.0f;
-                        mv[s] *= raw;
-                        rsum += mv[s];
-                        m[e] = s <= t ? raw * __expf(gt - gs[s]) : 0.0f;
-                        if (lane < 16)
-                            st_f32(smem + OFF_DMT, kmaj_off4(s, t & ~3, C) + (t & 3) * 4, m[e]);
-                    }
-                    if (lane < 16)
-                        st4(reinterpret_cast<float*>(smem + OFF_DM + kmaj_off4(t, s4, C)),
-                            make_float4(m[0], m[1], m[2], m[3]));
-                }
-                if (lane < 16) atomicAdd(&dg[t], rsum);
-                xreduce<C, 8>(mv, lane);
-                if (lane < 16) {
-                    const int s0 = 32 * ((lane >> 3) & 1) + 16 * ((lane >> 2) & 1) + 8 * ((lane >> 1) & 1) +
-                                   4 * (lane & 1);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) atomicAdd(&dg[s0 + e], -mv[e]);
                 }
             }
         }
@@ -410,7 +356,59 @@ __global__ void __launch_bounds__(THREADS, 1)
                 st_f32(smem + OFF_TBT, kmaj_off4(s0 + e, t & ~3, C) + (t & 3) * 4, tb);
             }
         }
+        // gated: M[4a + r][4bq + cc] = (M o Gamma)^T[4bq + cc][4a + r], in flight
+        // across the barrier
+        float4 mt4[GATED ? 4 : 1];
+        if constexpr (GATED) {
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) mt4[cc] = f4(MTg + (ch * C + 4 * bq + cc) * C + 4 * a);
+        }
         __syncthreads();
+        if constexpr (GATED) {
+            // this thread's 4 x 4 block of dM (raw, masked): dM~ = dM o Gamma into both
+            // B tiles; dg_t += rowsum(dM o M), dg_s -= colsum(dM o M)
+            float dmv[4][4], rs[4], cs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const float4 x = ld4(reinterpret_cast<const float*>(smem + OFF_DM + kmaj_off4(4 * a + r, 4 * bq, C)));
+                dmv[r][0] = x.x, dmv[r][1] = x.y, dmv[r][2] = x.z, dmv[r][3] = x.w;
+                const float mr[4] = {r == 0 ? mt4[0].x : r == 1 ? mt4[0].y : r == 2 ? mt4[0].z : mt4[0].w,
+                                     r == 0 ? mt4[1].x : r == 1 ? mt4[1].y : r == 2 ? mt4[1].z : mt4[1].w,
+                                     r == 0 ? mt4[2].x : r == 1 ? mt4[2].y : r == 2 ? mt4[2].z : mt4[2].w,
+                                     r == 0 ? mt4[3].x : r == 1 ? mt4[3].y : r == 2 ? mt4[3].z : mt4[3].w};
+                const int t = 4 * a + r;
+                rs[r] = 0.0f;
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    const float pr = dmv[r][cc] * mr[cc];
+                    rs[r] += pr;
+                    cs[cc] += pr;
+                    const int s2 = 4 * bq + cc;
+                    dmv[r][cc] = s2 <= t ? dmv[r][cc] * __expf(gs[t] - gs[s2]) : 0.0f;
+                }
+                st4(reinterpret_cast<float*>(smem + OFF_DM + kmaj_off4(t, 4 * bq, C)),
+                    make_float4(dmv[r][0], dmv[r][1], dmv[r][2], dmv[r][3]));
+            }
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc)
+                st4(reinterpret_cast<float*>(smem + OFF_DMT + kmaj_off4(4 * bq + cc, 4 * a, C)),
+                    make_float4(dmv[0][cc], dmv[1][cc], dmv[2][cc], dmv[3][cc]));
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+#pragma unroll
+                for (int o = 1; o < 16; o <<= 1) rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], o);
+            }
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) cs[cc] += __shfl_xor_sync(0xffffffffu, cs[cc], 16);
+            if (bq == 0) {
+#pragma unroll
+                for (int r = 0; r < 4; ++r) atomicAdd(&dg[4 * a + r], rs[r]);
+            }
+            if (lane < 16) {
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) atomicAdd(&dg[4 * bq + cc], -cs[cc]);
+            }
+        }
         float2 acc[4][2];
         // X' = T^T dT_b (T[t][s] = 0 for t < s); its diagonal is the dbeta term of T_b
 #pragma unroll
@@ -537,7 +535,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             ld_landed |= 4;
             tc::fence_after_sync();
             constexpr uint32_t id128 = idesc_tf32(128, C);
-#pragma unroll
+#pragma unroll 1
             for (int kk = 0; kk < C / 8; ++kk) {
                 const uint64_t dM = kdesc(smem + OFF_DM, BOX_C, kk);
                 const uint64_t dMT = kdesc(smem + OFF_DMT, BOX_C, kk);
@@ -597,69 +595,65 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     }
     if (GATED && !s_misc[1]) {
-        // thread (lane quarter, half) -> column j = TMEM lane, tokens t = 32 hf + e;
-        // q_t[j], k_t[j] from the Q^T, K^T tiles; dg partials per token, summed
-        // over j by a transpose-reduce and the four warps of the half
+        // thread (lane quarter, half) -> column j = TMEM lane, tokens t = 32 hf + 8 g + e
+        // (eight columns of each accumulator at a time); q_t[j], k_t[j] from the Q^T,
+        // K^T tiles; the dg partial of (t, j) into scratch (the chain's, dead now)
         const int j = (warp & 3) * 32 + lane;
         const float gC = gs[C - 1];
-        float dgp[32];
         float k1tot = 0.0f;
-        {
-            uint32_t xa[32], xb[32];
-            tc::tmem_ld32(tmem + TM_Q + lane_base + hf * 32, xa);
-            tc::tmem_ld32(tmem + TM_Q2 + lane_base + hf * 32, xb);
+        __nv_bfloat16* oq = gq + row0 + j;
+        __nv_bfloat16* ov = gv + row0 + j;
+        __nv_bfloat16* ok_ = gk + row0 + j;
+#pragma unroll 1
+        for (int g8 = 0; g8 < 4; ++g8) {
+            const uint32_t col = lane_base + hf * 32 + 8 * g8;
+            uint32_t xq[8], xq2[8], xv[8], xk1[8], xkb[8], xkw[8];
+            tc::tmem_ld8(tmem + TM_Q + col, xq);
+            tc::tmem_ld8(tmem + TM_Q2 + col, xq2);
+            tc::tmem_ld8(tmem + TM_V + col, xv);
+            tc::tmem_ld8(tmem + TM_K + col, xk1);
+            tc::tmem_ld8(tmem + TM_KB + col, xkb);
+            tc::tmem_ld8(tmem + TM_KW + col, xkw);
             tc::tmem_wait_ld();
-            __nv_bfloat16* oq = gq + row0 + j;
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const int t = hf * 32 + e;
-                const float gam = __expf(gs[t]);
-                const float qv = *reinterpret_cast<const float*>(
-                    smem + OFF_QT + kmaj_off4(j, t & ~3, D) + (t & 3) * 4);
-                const float dqa = gam * __uint_as_float(xa[e]);
-                dgp[e] = dqa * qv;
-                if (t < nvalid) oq[t * ts] = __float2bfloat16(dqa + __uint_as_float(xb[e]));
-            }
-        }
-        {
-            uint32_t xa[32];
-            tc::tmem_ld32(tmem + TM_V + lane_base + hf * 32, xa);
-            tc::tmem_wait_ld();
-            __nv_bfloat16* ov = gv + row0 + j;
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const int t = hf * 32 + e;
-                if (t < nvalid) ov[t * ts] = __float2bfloat16(__uint_as_float(xa[e]));
-            }
-        }
-        {
-            uint32_t xa[32], xb[32], xc[32];
-            tc::tmem_ld32(tmem + TM_K + lane_base + hf * 32, xa);
-            tc::tmem_ld32(tmem + TM_KB + lane_base + hf * 32, xb);
-            tc::tmem_ld32(tmem + TM_KW + lane_base + hf * 32, xc);
-            tc::tmem_wait_ld();
-            __nv_bfloat16* ok_ = gk + row0 + j;
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const int t = hf * 32 + e;
+            for (int e = 0; e < 8; ++e) {
+                const int t = hf * 32 + 8 * g8 + e;
                 const float gam = __expf(gs[t]), kap = __expf(gC - gs[t]);
-                const float kv = *reinterpret_cast<const float*>(
-                    smem + OFF_KT + kmaj_off4(j, t & ~3, D) + (t & 3) * 4);
-                const float k1 = kap * __uint_as_float(xa[e]);  // (gamma_C/gamma) dK~
-                const float kw = gam * __uint_as_float(xc[e]);  // gamma T_b^T dW
-                dgp[e] = fmaf(kv, kw - k1, dgp[e]);
+                const uint32_t to = (t & 3) * 4;
+                const float qv = *reinterpret_cast<const float*>(smem + OFF_QT + kmaj_off4(j, t & ~3, D) + to);
+                const float kv = *reinterpret_cast<const float*>(smem + OFF_KT + kmaj_off4(j, t & ~3, D) + to);
+                const float dqa = gam * __uint_as_float(xq[e]);        // gamma dQa~
+                const float k1 = kap * __uint_as_float(xk1[e]);        // (gamma_C/gamma) dK~
+                const float kw = gam * __uint_as_float(xkw[e]);        // gamma T_b^T dW
+                sc[t * DGP + j] = fmaf(dqa, qv, kv * (kw - k1));
                 k1tot = fmaf(kv, k1, k1tot);
-                if (t < nvalid) ok_[t * ts] = __float2bfloat16(__uint_as_float(xb[e]) + k1 + kw);
+                if (t < nvalid) {
+                    oq[t * ts] = __float2bfloat16(dqa + __uint_as_float(xq2[e]));
+                    ov[t * ts] = __float2bfloat16(__uint_as_float(xv[e]));
+                    ok_[t * ts] = __float2bfloat16(__uint_as_float(xkb[e]) + k1 + kw);
+                }
             }
         }
-        xreduce<32, 16>(dgp, lane);
-        atomicAdd(&dg[hf * 32 + lane], dgp[0]);
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) k1tot += __shfl_xor_sync(0xffffffffu, k1tot, o);
         if (lane == 0) atomicAdd(&dg[C - 1], k1tot);
     }
     tc::fence_before_sync();
     __syncthreads();
+    if (GATED) {
+        if (!s_misc[1]) {
+            // dg_t += sum_j of the partials: four threads per token, j = 4 jj + quarter
+            // (bank-conflict free), then a two-step shuffle
+            const int t = tid >> 2, qq = tid & 3;
+            float acc = 0.0f;
+#pragma unroll 8
+            for (int jj = 0; jj < D / 4; ++jj) acc += sc[t * DGP + 4 * jj + qq];
+            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+            if (qq == 0) atomicAdd(&dg[t], acc);
+        }
+        __syncthreads();
+    }
     if (GATED && !s_misc[1] && warp < 2) {
         // dlog alpha_s = sum_{t >= s} dg_t (a reverse scan), dalpha_s = that / alpha_s
         const int s = tid;
