@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             ld_landed = 1;
             tc::fence_after_sync();
             constexpr uint32_t id128 = idesc_tf32(128, C), id64 = idesc_tf32(64, C);
-#pragma unroll 1
+#pragma unroll
             for (int kk = 0; kk < D / 8; ++kk) {
                 const uint64_t s0 = kdesc(smem + OFF_R0, BOX_D, kk);
                 const uint64_t dof = kdesc(smem + OFF_R4, BOX_C, kk);
@@ -277,7 +277,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             ld_landed |= 2;
             tc::fence_after_sync();
             constexpr uint32_t id64 = idesc_tf32(64, C);
-#pragma unroll 1
+#pragma unroll
             for (int kk = 0; kk < D / 8; ++kk) {
                 mma_tf32_ss(tmem + TM_DTB, kdesc(smem + OFF_DW, BOX_C, kk),
                             kdesc(smem + OFF_R2, BOX_C, kk), id64, kk > 0);
@@ -535,7 +535,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             ld_landed |= 4;
             tc::fence_after_sync();
             constexpr uint32_t id128 = idesc_tf32(128, C);
-#pragma unroll 1
+#pragma unroll
             for (int kk = 0; kk < C / 8; ++kk) {
                 const uint64_t dM = kdesc(smem + OFF_DM, BOX_C, kk);
                 const uint64_t dMT = kdesc(smem + OFF_DMT, BOX_C, kk);
