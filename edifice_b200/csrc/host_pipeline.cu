@@ -1,6 +1,6 @@
 // host_pipeline.cu -- forward + backward of the diagonal scans (linear scan,
-// MinGRU) and of the Mamba selective scan over HOST-resident tensors: batch
-// rows are streamed through a small ring of device slots so that the
+// MinGRU), of the Mamba selective scan and of flash attention over
+// HOST-resident tensors: batch rows (attention: (batch, kv head) units) are streamed through a small ring of device slots so that the
 // host->device copies of chunk i+1, the kernels of chunk i and the
 // device->host copies of chunk i-1 run at the same time (the two copy
 // directions use separate copy engines; PCIe is full duplex).
@@ -304,7 +304,130 @@ int run_ssm(int dtype, const void* x, const void* dt, const void* A, const void*
     return EDB_OK;  // `join` makes the caller's stream wait for the last copies
 }
 
+// ------------------------------------------------------------ flash attention
+// Units are (batch, kv head) pairs: unit u = b * Hkv + hk owns q / o / dO / dq
+// heads [u G, u G + G) (G = Hq / Hkv) and k / v / dk / dv head u, contiguous in
+// the [B, H, L, d] layouts, so a run of consecutive units is a complete
+// sub-problem that the device kernels take as `batch = units, kv_heads = 1,
+// q_heads = G`.  About eight chunks per call: copies dominate at these sizes
+// (two bytes in and two out per FLOP-heavy element), and each chunk's backward
+// grid still covers several waves.
+struct AttnSlot {
+    size_t tq, tk, lse, ws;  // [units, G, L, d] io, [units, L, d] io, lse f32, bwd ws
+    size_t bytes() const { return 4 * tq + 4 * tk + lse + ws; }
+};
+
+int attn_units_per_chunk(int units) { return units < 8 ? 1 : (units + 7) / 8; }
+
+AttnSlot attn_slot(int dtype, int nu, int G, int L, int d) {
+    const int es = dtype == EDB_BF16 ? 2 : 4;
+    AttnSlot g;
+    g.tq = a256((size_t)nu * G * L * d * es);
+    g.tk = a256((size_t)nu * L * d * es);
+    g.lse = a256((size_t)nu * G * L * 4);
+    g.ws = a256(edb_flash_attention_bwd_workspace(dtype, nu, G, 1, L, d, 1));
+    return g;
+}
+
+int check_attn(int dtype, int B, int Hq, int Hkv, int L, int d) {
+    if (dtype != EDB_F32 && dtype != EDB_BF16) return EDB_ERR_BAD_DTYPE;
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || L <= 0 || d <= 0 || Hq % Hkv != 0)
+        return EDB_ERR_BAD_SHAPE;
+    return EDB_OK;
+}
+
+int run_attn(int dtype, const void* q, const void* k, const void* v, const void* dO, void* o,
+             void* dq, void* dk, void* dv, int B, int Hq, int Hkv, int L, int d, int causal,
+             float scale, void* ws, size_t ws_bytes, void* stream) {
+    if (int st = check_attn(dtype, B, Hq, Hkv, L, d)) return st;
+    if (!q || !k || !v || !dO || !o || !dq || !dk || !dv || !ws) return EDB_ERR_NULL_POINTER;
+    const int es = dtype == EDB_BF16 ? 2 : 4;
+    const int G = Hq / Hkv, units = B * Hkv;
+    const int nu = attn_units_per_chunk(units);
+    const AttnSlot g = attn_slot(dtype, nu, G, L, d);
+    if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0) return EDB_ERR_MISALIGNED;
+    if (ws_bytes < kSlots * g.bytes()) return EDB_ERR_WORKSPACE_TOO_SMALL;
+
+    cudaStream_t s = (cudaStream_t)stream;
+    Res r;
+    EDB_TRY(r.init());
+    Join join{r, s};
+    EDB_TRY(cudaEventRecord(r.start, s));
+    EDB_TRY(cudaStreamWaitEvent(r.sin, r.start, 0));
+    EDB_TRY(cudaStreamWaitEvent(r.sout, r.start, 0));
+    join.armed = true;
+
+    const int nchunks = (units + nu - 1) / nu;
+    for (int i = 0; i < nchunks; ++i) {
+        const int slot = i % kSlots;
+        const int u0 = i * nu, n = units - u0 < nu ? units - u0 : nu;
+        char* p = static_cast<char*>(ws) + slot * g.bytes();
+        void* dqi = p;
+        void* ddo = p + g.tq;
+        void* dout = p + 2 * g.tq;
+        void* ddq = p + 3 * g.tq;
+        void* dki = p + 4 * g.tq;
+        void* dvi = p + 4 * g.tq + g.tk;
+        void* ddk = p + 4 * g.tq + 2 * g.tk;
+        void* ddv = p + 4 * g.tq + 3 * g.tk;
+        float* dlse = reinterpret_cast<float*>(p + 4 * g.tq + 4 * g.tk);
+        void* dws = p + 4 * g.tq + 4 * g.tk + g.lse;
+        const size_t offq = (size_t)u0 * G * L * d * es, nq = (size_t)n * G * L * d * es;
+        const size_t offk = (size_t)u0 * L * d * es, nk = (size_t)n * L * d * es;
+
+        // host -> device once the slot's previous chunk has left: q, k, v, then dO
+        if (i >= kSlots) EDB_TRY(cudaStreamWaitEvent(r.sin, r.free_[slot], 0));
+        EDB_TRY(cudaMemcpyAsync(dqi, hp(q, offq), nq, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaMemcpyAsync(dki, hp(k, offk), nk, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaMemcpyAsync(dvi, hp(v, offk), nk, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaEventRecord(r.in_fwd[slot], r.sin));
+        EDB_TRY(cudaMemcpyAsync(ddo, hp(dO, offq), nq, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaEventRecord(r.in[slot], r.sin));
+
+        // forward (with lse), then backward, on the caller's stream
+        EDB_TRY(cudaStreamWaitEvent(s, r.in_fwd[slot], 0));
+        EDB_TRY_ST(edb_flash_attention_fwd(dtype, dqi, dki, dvi, dout, dlse, n, G, 1, L, d,
+                                           causal, scale, s));
+        EDB_TRY(cudaEventRecord(r.fwd[slot], s));
+        EDB_TRY(cudaStreamWaitEvent(s, r.in[slot], 0));
+        EDB_TRY_ST(edb_flash_attention_bwd(dtype, dqi, dki, dvi, dout, ddo, dlse, ddq, ddk, ddv,
+                                           n, G, 1, L, d, causal, scale, dws, g.ws, s));
+        EDB_TRY(cudaEventRecord(r.comp[slot], s));
+
+        // device -> host: o as soon as the forward is done, the gradients after the
+        // backward
+        EDB_TRY(cudaStreamWaitEvent(r.sout, r.fwd[slot], 0));
+        EDB_TRY(cudaMemcpyAsync(hq(o, offq), dout, nq, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaStreamWaitEvent(r.sout, r.comp[slot], 0));
+        EDB_TRY(cudaMemcpyAsync(hq(dq, offq), ddq, nq, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaMemcpyAsync(hq(dk, offk), ddk, nk, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaMemcpyAsync(hq(dv, offk), ddv, nk, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaEventRecord(r.free_[slot], r.sout));
+    }
+    return EDB_OK;  // `join` makes the caller's stream wait for the last copies
+}
+
 }  // namespace
+
+extern "C" size_t edb_flash_attention_train_host_workspace(int dtype, int batch, int q_heads,
+                                                           int kv_heads, int seq_len,
+                                                           int head_dim) {
+    if (check_attn(dtype, batch, q_heads, kv_heads, seq_len, head_dim) != EDB_OK) return 0;
+    const int units = batch * kv_heads;
+    return kSlots * attn_slot(dtype, attn_units_per_chunk(units), q_heads / kv_heads, seq_len,
+                              head_dim)
+                        .bytes();
+}
+
+extern "C" int edb_flash_attention_train_host(int dtype, const void* q, const void* k,
+                                              const void* v, const void* dO, void* o, void* dq,
+                                              void* dk, void* dv, int batch, int q_heads,
+                                              int kv_heads, int seq_len, int head_dim,
+                                              int causal, float scale, void* workspace,
+                                              size_t workspace_bytes, void* stream) {
+    return run_attn(dtype, q, k, v, dO, o, dq, dk, dv, batch, q_heads, kv_heads, seq_len,
+                    head_dim, causal, scale, workspace, workspace_bytes, stream);
+}
 
 extern "C" size_t edb_scan_train_host_workspace(int dtype, int batch, int seq_len, int hidden) {
     if (check_shape(dtype, batch, seq_len, hidden) != EDB_OK) return 0;

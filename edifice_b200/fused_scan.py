@@ -621,6 +621,42 @@ def flash_attention_backward(q, k, v, causal, forward_out, grad_output, lse=None
     return dq, dk, dv
 
 
+def flash_attention_train_host(q, k, v, grad_output, causal=True, scale=None, out=None,
+                               device=None):
+    """Forward and backward of flash attention for host-resident q, k, v [B, Hq, L, d] /
+    [B, Hkv, L, d] and grad_output [B, Hq, L, d]: (batch, kv head) units stream through
+    the device with their copies overlapped with the kernels.  Returns host tensors
+    (o, grad_q, grad_k, grad_v), written into ``out`` when given.  Asynchronous on the
+    current stream of ``device``: synchronise it before reading the results.  Inputs
+    and outputs should be pinned for the copies to overlap."""
+    what = "flash_attention_train_host"
+    for t in (q, k, v, grad_output):
+        if t.is_cuda or not t.is_contiguous():
+            raise _lib.EdbError("%s: inputs must be contiguous host tensors" % what)
+    B, Hq, Hkv, L, d = _attn_shapes(q, k, v)
+    _same(q.shape, grad_output.shape, what)
+    if out is None:
+        out = (torch.empty(q.shape, dtype=q.dtype, pin_memory=True),
+               torch.empty(q.shape, dtype=q.dtype, pin_memory=True),
+               torch.empty(k.shape, dtype=k.dtype, pin_memory=True),
+               torch.empty(v.shape, dtype=v.dtype, pin_memory=True))
+    for o_, ref in zip(out, (q, q, k, v)):
+        if o_.is_cuda or not o_.is_contiguous() or o_.shape != ref.shape or o_.dtype != ref.dtype:
+            raise _lib.EdbError("%s: outputs must be contiguous host tensors shaped like "
+                                "(q, q, k, v)" % what)
+    device = torch.device(device if device is not None else "cuda")
+    code = _dtype_code(q, what)
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        nbytes = lib.edb_flash_attention_train_host_workspace(code, B, Hq, Hkv, L, d)
+        ws = _host_ws(device, nbytes)
+        _lib.check(lib.edb_flash_attention_train_host(
+            code, _p(q), _p(k), _p(v), _p(grad_output), _p(out[0]), _p(out[1]), _p(out[2]),
+            _p(out[3]), B, Hq, Hkv, L, d, int(bool(causal)), float(scale or 0.0), _p(ws), nbytes,
+            _stream()), "CUDA flash attention over host tensors")
+    return out
+
+
 class FlashAttentionFn(torch.autograd.Function):
     """custom_grad wiring of flash_attention_custom_call/4 (fused_scan.ex:3427-3443):
     gradients to q, k, v."""

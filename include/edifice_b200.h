@@ -280,6 +280,27 @@ int edb_flash_attention_bwd(int dtype, const void* q, const void* k, const void*
                             int causal, float scale, void* workspace, size_t workspace_bytes,
                             void* stream);
 
+/* Forward + backward of flash attention for HOST-resident q, k, v, dO (page-
+ * locked for the copies to overlap): returns o, dq, dk, dv in host memory.
+ * (batch, kv head) units stream through a ring of device slots in `workspace`
+ * (edb_flash_attention_train_host_workspace() bytes, 256-byte aligned): the
+ * host->device copies of one chunk of units, the kernels of the previous one and
+ * the device->host copies of the one before run at once.  Results equal
+ * edb_flash_attention_fwd + edb_flash_attention_bwd on the whole problem.
+ * Stream-ordered as edb_selective_scan_train_host.  The reference has no single
+ * entry point for it: a caller with host-resident Nx tensors makes the round trip
+ * around fused_flash_attention_launch / _backward_launch
+ * (native/cuda/fused_flash_attention.cu:168-191, fused_flash_attention_backward.cu:
+ * 355-408). */
+size_t edb_flash_attention_train_host_workspace(int dtype, int batch, int q_heads,
+                                                int kv_heads, int seq_len, int head_dim);
+
+int edb_flash_attention_train_host(int dtype, const void* q, const void* k, const void* v,
+                                   const void* dO, void* o, void* dq, void* dk, void* dv,
+                                   int batch, int q_heads, int kv_heads, int seq_len,
+                                   int head_dim, int causal, float scale, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------
  * LASER attention (attention over exp(V)):
  *   A = softmax(Q K^T scale (+ causal mask)) exp(V - v_max);  O = log(max(A, 1e-7)) + v_max

@@ -456,3 +456,24 @@ def test_fox_shim_symbols(cuda, prec, dtype):
     for i, w in enumerate(want[:3]):
         assert torch.equal(cat[i * n:(i + 1) * n].view_as(w), w)
     assert torch.equal(cat[3 * n:].view(B, H, L), want[3].to(dtype))
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("B,Hq,Hkv,L,d", [(2, 4, 2, 256, 64), (3, 8, 2, 384, 128),
+                                          (4, 8, 4, 200, 128), (1, 2, 1, 130, 64)])
+def test_flash_attention_train_host(cuda, causal, B, Hq, Hkv, L, d):
+    """The host-tensor entry point ((batch, kv head) units streamed through a ring of
+    three device slots, copies overlapped with the kernels) against the device entry
+    points on the same inputs: four to eight chunks, so the ring wraps."""
+    q, k, v, do = attn_inputs(B, Hq, Hkv, L, d, torch.bfloat16, seed=90 + L)
+    pin = [t.cpu().pin_memory() for t in (q, k, v, do)]
+    o, dq, dk, dv = fs.flash_attention_train_host(*pin, causal=causal)
+    torch.cuda.synchronize()
+    o_r, lse = fs.flash_attention(q, k, v, causal=causal, return_lse=True)
+    dq_r, dk_r, dv_r = fs.flash_attention_backward(q, k, v, causal, o_r, do, lse)
+    torch.cuda.synchronize()
+    assert torch.equal(o, o_r.cpu())
+    for got, ref in ((dq, dq_r), (dk, dk_r), (dv, dv_r)):
+        ref = ref.cpu().double()
+        assert ((got.double() - ref).norm() / ref.norm()).item() <= 1e-3
+    assert device_errors() == 0

@@ -170,13 +170,13 @@ def _delta_inputs(B, L, H, d, dtype, seed, per_element=False):
     return [t.to(dtype).cuda() for t in (q, k, v, beta, alpha, do)]
 
 
-@pytest.mark.parametrize("form", ["chunked", "token_per_element", "gated"])
+@pytest.mark.parametrize("form", ["chunked", "token_per_element", "gated", "gated_chunked"])
 def test_delta_rule_desc_packed_qkv(cuda, form):
-    B, L, H, d = 2, 192, 2, (128 if form == "chunked" else 64)
+    B, L, H, d = 2, 192, 2, (128 if form in ("chunked", "gated_chunked") else 64)
     dtype = torch.bfloat16
     q, k, v, beta, alpha, do = _delta_inputs(B, L, H, d, dtype, 5,
                                              per_element=form == "token_per_element")
-    gated = form == "gated"
+    gated = form.startswith("gated")
     if gated:
         o_r = fs.gated_delta_net_scan(q, k, v, beta, alpha)
         grads_r = fs.gated_delta_net_backward(q, k, v, beta, alpha, do)
@@ -198,7 +198,7 @@ def test_delta_rule_desc_packed_qkv(cuda, form):
                       gk=gqkv[:, :, 1], gv=gqkv[:, :, 2], gbeta=gbeta, galpha=galpha, **common))
     torch.cuda.synchronize()
     got = [gqkv[:, :, 0], gqkv[:, :, 1], gqkv[:, :, 2], gbeta] + ([galpha] if gated else [])
-    cmp = _close if form == "chunked" else _exact
+    cmp = _close if form in ("chunked", "gated_chunked") else _exact
     cmp(o.contiguous(), o_r)
     for u, r in zip(got, grads_r):
         cmp(u.contiguous(), r)
