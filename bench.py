@@ -172,6 +172,11 @@ RATE = {"hbm": (1e9, "GB/s"), "tensor": (1e12, "TFLOP/s"), "sfu": (1e9, "Gexp/s"
         "fp32": (1e12, "TFLOP/s")}
 
 
+def torch_f32():
+    import torch
+    return torch.float32
+
+
 def ncu_traffic(kernel_key):
     """Per-launch DRAM bytes of a kernel from the committed ncu summary, if any."""
     p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
@@ -718,9 +723,11 @@ class LaserWorkload(AttnWorkload):
         from edifice_b200 import fused_scan as fs
         return fs.laser_attention_backward(self.q, self.k, self.v, self.do, resid, causal=True)
 
-    # whole-tensor copies around the device entry points
-    e2e_host = None
-    e2e_outputs = None
+    def e2e_host(self, pin, outs):
+        """One fwd+bwd step over pinned host buffers through the host entry point."""
+        from edifice_b200 import fused_scan as fs
+        return fs.laser_attention_train_host(pin[0], pin[1], pin[2], pin[3], causal=True,
+                                             out=outs)
 
     def e2e_step(self, dev_in):
         from edifice_b200 import fused_scan as fs
@@ -728,8 +735,7 @@ class LaserWorkload(AttnWorkload):
         o, resid = fs.laser_attention(q, k, v, causal=True, return_resid=True)
         return (o,) + tuple(fs.laser_attention_backward(q, k, v, do, resid, causal=True))
 
-    api = ("edifice_b200.fused_scan.laser_attention + laser_attention_backward (whole-tensor "
-           "copies in the timed region)")
+    api = "edifice_b200.fused_scan.laser_attention_train_host (host tensors in and out)"
 
     def cpu_step(self, rows=None, prec="f32"):
         import numpy as np
@@ -795,9 +801,13 @@ class FoxWorkload(AttnWorkload):
     def host_inputs(self):
         return [self.q, self.k, self.v, self.cs, self.do]
 
-    # whole-tensor copies around the device entry points
-    e2e_host = None
-    e2e_outputs = None
+    def e2e_outputs(self):
+        return super().e2e_outputs() + [tuple(self.cs.shape) + (torch_f32(),)]
+
+    def e2e_host(self, pin, outs):
+        """One fwd+bwd step over pinned host buffers through the host entry point."""
+        from edifice_b200 import fused_scan as fs
+        return fs.fox_attention_train_host(pin[0], pin[1], pin[2], pin[3], pin[4], out=outs)
 
     def e2e_step(self, dev_in):
         from edifice_b200 import fused_scan as fs
@@ -805,8 +815,7 @@ class FoxWorkload(AttnWorkload):
         o, lse = fs.fox_attention(q, k, v, cs, return_lse=True)
         return (o,) + tuple(fs.fox_attention_backward(q, k, v, cs, o, do, lse))
 
-    api = ("edifice_b200.fused_scan.fox_attention + fox_attention_backward (whole-tensor "
-           "copies in the timed region)")
+    api = "edifice_b200.fused_scan.fox_attention_train_host (host tensors in and out)"
 
     def cpu_step(self, rows=None, prec="f32"):
         import numpy as np

@@ -1,5 +1,5 @@
 // host_pipeline.cu -- forward + backward of the diagonal scans (linear scan,
-// MinGRU), of the Mamba selective scan and of flash attention over
+// MinGRU), of the Mamba selective scan and of attention (flash, FoX, LASER) over
 // HOST-resident tensors: batch rows (attention: (batch, kv head) units) are streamed through a small ring of device slots so that the
 // host->device copies of chunk i+1, the kernels of chunk i and the
 // device->host copies of chunk i-1 run at the same time (the two copy
@@ -304,28 +304,37 @@ int run_ssm(int dtype, const void* x, const void* dt, const void* A, const void*
     return EDB_OK;  // `join` makes the caller's stream wait for the last copies
 }
 
-// ------------------------------------------------------------ flash attention
+// ------------------------------------------------------------ attention
 // Units are (batch, kv head) pairs: unit u = b * Hkv + hk owns q / o / dO / dq
-// heads [u G, u G + G) (G = Hq / Hkv) and k / v / dk / dv head u, contiguous in
-// the [B, H, L, d] layouts, so a run of consecutive units is a complete
-// sub-problem that the device kernels take as `batch = units, kv_heads = 1,
-// q_heads = G`.  About eight chunks per call: copies dominate at these sizes
-// (two bytes in and two out per FLOP-heavy element), and each chunk's backward
-// grid still covers several waves.
+// heads [u G, u G + G) (G = Hq / Hkv; FoX's cs / dcs rows likewise) and k / v /
+// dk / dv head u, contiguous in the [B, H, L, d] layouts, so a run of consecutive
+// units is a complete sub-problem that the device kernels take as `batch = units,
+// kv_heads = 1, q_heads = G` (LASER's v_max is per (b, kv head, column), so per
+// unit too).  About eight chunks per call: copies dominate at these sizes, and
+// each chunk's backward grid still covers several waves.
+enum { ATTN_FLASH = 0, ATTN_FOX = 1, ATTN_LASER = 2 };
+
 struct AttnSlot {
-    size_t tq, tk, lse, ws;  // [units, G, L, d] io, [units, L, d] io, lse f32, bwd ws
-    size_t bytes() const { return 4 * tq + 4 * tk + lse + ws; }
+    // [units, G, L, d] io, [units, L, d] io, lse f32 (flash, FoX), cs and dcs f32
+    // (FoX), the forward's residual (LASER), the backward's workspace
+    size_t tq, tk, lse, cs, resid, ws;
+    size_t bytes() const { return 4 * tq + 4 * tk + lse + 2 * cs + resid + ws; }
 };
 
 int attn_units_per_chunk(int units) { return units < 8 ? 1 : (units + 7) / 8; }
 
-AttnSlot attn_slot(int dtype, int nu, int G, int L, int d) {
+AttnSlot attn_slot(int op, int dtype, int nu, int G, int L, int d) {
     const int es = dtype == EDB_BF16 ? 2 : 4;
-    AttnSlot g;
+    AttnSlot g{};
     g.tq = a256((size_t)nu * G * L * d * es);
     g.tk = a256((size_t)nu * L * d * es);
-    g.lse = a256((size_t)nu * G * L * 4);
-    g.ws = a256(edb_flash_attention_bwd_workspace(dtype, nu, G, 1, L, d, 1));
+    const size_t rows = a256((size_t)nu * G * L * 4);
+    if (op != ATTN_LASER) g.lse = rows;
+    if (op == ATTN_FOX) g.cs = rows;
+    if (op == ATTN_LASER) g.resid = a256(edb_laser_attention_resid_bytes(dtype, nu, G, 1, L, d));
+    g.ws = a256(op == ATTN_FLASH ? edb_flash_attention_bwd_workspace(dtype, nu, G, 1, L, d, 1)
+                : op == ATTN_FOX ? edb_fox_attention_bwd_workspace(dtype, nu, G, 1, L, d)
+                                 : edb_laser_attention_bwd_workspace(dtype, nu, G, 1, L, d));
     return g;
 }
 
@@ -336,15 +345,23 @@ int check_attn(int dtype, int B, int Hq, int Hkv, int L, int d) {
     return EDB_OK;
 }
 
-int run_attn(int dtype, const void* q, const void* k, const void* v, const void* dO, void* o,
-             void* dq, void* dk, void* dv, int B, int Hq, int Hkv, int L, int d, int causal,
-             float scale, void* ws, size_t ws_bytes, void* stream) {
+size_t attn_workspace(int op, int dtype, int B, int Hq, int Hkv, int L, int d) {
+    if (check_attn(dtype, B, Hq, Hkv, L, d) != EDB_OK) return 0;
+    return kSlots * attn_slot(op, dtype, attn_units_per_chunk(B * Hkv), Hq / Hkv, L, d).bytes();
+}
+
+// cs / dcs: FoX only (f32 [B, Hq, L]).
+int run_attn(int op, int dtype, const void* q, const void* k, const void* v, const float* cs,
+             const void* dO, void* o, void* dq, void* dk, void* dv, float* dcs, int B, int Hq,
+             int Hkv, int L, int d, int causal, float scale, void* ws, size_t ws_bytes,
+             void* stream) {
     if (int st = check_attn(dtype, B, Hq, Hkv, L, d)) return st;
     if (!q || !k || !v || !dO || !o || !dq || !dk || !dv || !ws) return EDB_ERR_NULL_POINTER;
+    if (op == ATTN_FOX && (!cs || !dcs)) return EDB_ERR_NULL_POINTER;
     const int es = dtype == EDB_BF16 ? 2 : 4;
     const int G = Hq / Hkv, units = B * Hkv;
     const int nu = attn_units_per_chunk(units);
-    const AttnSlot g = attn_slot(dtype, nu, G, L, d);
+    const AttnSlot g = attn_slot(op, dtype, nu, G, L, d);
     if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0) return EDB_ERR_MISALIGNED;
     if (ws_bytes < kSlots * g.bytes()) return EDB_ERR_WORKSPACE_TOO_SMALL;
 
@@ -366,32 +383,55 @@ int run_attn(int dtype, const void* q, const void* k, const void* v, const void*
         void* ddo = p + g.tq;
         void* dout = p + 2 * g.tq;
         void* ddq = p + 3 * g.tq;
-        void* dki = p + 4 * g.tq;
-        void* dvi = p + 4 * g.tq + g.tk;
-        void* ddk = p + 4 * g.tq + 2 * g.tk;
-        void* ddv = p + 4 * g.tq + 3 * g.tk;
-        float* dlse = reinterpret_cast<float*>(p + 4 * g.tq + 4 * g.tk);
-        void* dws = p + 4 * g.tq + 4 * g.tk + g.lse;
+        char* pk = p + 4 * g.tq;
+        void* dki = pk;
+        void* dvi = pk + g.tk;
+        void* ddk = pk + 2 * g.tk;
+        void* ddv = pk + 3 * g.tk;
+        char* pr = pk + 4 * g.tk;
+        float* dlse = reinterpret_cast<float*>(pr);
+        float* dcsi = reinterpret_cast<float*>(pr + g.lse);
+        float* ddcs = reinterpret_cast<float*>(pr + g.lse + g.cs);
+        void* dres = pr + g.lse + 2 * g.cs;
+        void* dws = pr + g.lse + 2 * g.cs + g.resid;
         const size_t offq = (size_t)u0 * G * L * d * es, nq = (size_t)n * G * L * d * es;
         const size_t offk = (size_t)u0 * L * d * es, nk = (size_t)n * L * d * es;
+        const size_t offr = (size_t)u0 * G * L, nr = (size_t)n * G * L * 4;
 
-        // host -> device once the slot's previous chunk has left: q, k, v, then dO
+        // host -> device once the slot's previous chunk has left: the forward's
+        // inputs, then dO
         if (i >= kSlots) EDB_TRY(cudaStreamWaitEvent(r.sin, r.free_[slot], 0));
         EDB_TRY(cudaMemcpyAsync(dqi, hp(q, offq), nq, cudaMemcpyHostToDevice, r.sin));
         EDB_TRY(cudaMemcpyAsync(dki, hp(k, offk), nk, cudaMemcpyHostToDevice, r.sin));
         EDB_TRY(cudaMemcpyAsync(dvi, hp(v, offk), nk, cudaMemcpyHostToDevice, r.sin));
+        if (op == ATTN_FOX)
+            EDB_TRY(cudaMemcpyAsync(dcsi, cs + offr, nr, cudaMemcpyHostToDevice, r.sin));
         EDB_TRY(cudaEventRecord(r.in_fwd[slot], r.sin));
         EDB_TRY(cudaMemcpyAsync(ddo, hp(dO, offq), nq, cudaMemcpyHostToDevice, r.sin));
         EDB_TRY(cudaEventRecord(r.in[slot], r.sin));
 
-        // forward (with lse), then backward, on the caller's stream
+        // forward, then backward, on the caller's stream
         EDB_TRY(cudaStreamWaitEvent(s, r.in_fwd[slot], 0));
-        EDB_TRY_ST(edb_flash_attention_fwd(dtype, dqi, dki, dvi, dout, dlse, n, G, 1, L, d,
-                                           causal, scale, s));
+        if (op == ATTN_FLASH)
+            EDB_TRY_ST(edb_flash_attention_fwd(dtype, dqi, dki, dvi, dout, dlse, n, G, 1, L, d,
+                                               causal, scale, s));
+        else if (op == ATTN_FOX)
+            EDB_TRY_ST(edb_fox_attention_fwd(dtype, dqi, dki, dvi, dcsi, dout, dlse, n, G, 1, L,
+                                             d, scale, s));
+        else
+            EDB_TRY_ST(edb_laser_attention_fwd(dtype, dqi, dki, dvi, nullptr, dout, dres, n, G,
+                                               1, L, d, causal, scale, s));
         EDB_TRY(cudaEventRecord(r.fwd[slot], s));
         EDB_TRY(cudaStreamWaitEvent(s, r.in[slot], 0));
-        EDB_TRY_ST(edb_flash_attention_bwd(dtype, dqi, dki, dvi, dout, ddo, dlse, ddq, ddk, ddv,
-                                           n, G, 1, L, d, causal, scale, dws, g.ws, s));
+        if (op == ATTN_FLASH)
+            EDB_TRY_ST(edb_flash_attention_bwd(dtype, dqi, dki, dvi, dout, ddo, dlse, ddq, ddk,
+                                               ddv, n, G, 1, L, d, causal, scale, dws, g.ws, s));
+        else if (op == ATTN_FOX)
+            EDB_TRY_ST(edb_fox_attention_bwd(dtype, dqi, dki, dvi, dcsi, dout, ddo, dlse, ddq,
+                                             ddk, ddv, ddcs, n, G, 1, L, d, scale, dws, g.ws, s));
+        else
+            EDB_TRY_ST(edb_laser_attention_bwd(dtype, dqi, dki, ddo, dres, ddq, ddk, ddv, n, G,
+                                               1, L, d, causal, scale, dws, g.ws, s));
         EDB_TRY(cudaEventRecord(r.comp[slot], s));
 
         // device -> host: o as soon as the forward is done, the gradients after the
@@ -402,6 +442,8 @@ int run_attn(int dtype, const void* q, const void* k, const void* v, const void*
         EDB_TRY(cudaMemcpyAsync(hq(dq, offq), ddq, nq, cudaMemcpyDeviceToHost, r.sout));
         EDB_TRY(cudaMemcpyAsync(hq(dk, offk), ddk, nk, cudaMemcpyDeviceToHost, r.sout));
         EDB_TRY(cudaMemcpyAsync(hq(dv, offk), ddv, nk, cudaMemcpyDeviceToHost, r.sout));
+        if (op == ATTN_FOX)
+            EDB_TRY(cudaMemcpyAsync(dcs + offr, ddcs, nr, cudaMemcpyDeviceToHost, r.sout));
         EDB_TRY(cudaEventRecord(r.free_[slot], r.sout));
     }
     return EDB_OK;  // `join` makes the caller's stream wait for the last copies
@@ -412,11 +454,7 @@ int run_attn(int dtype, const void* q, const void* k, const void* v, const void*
 extern "C" size_t edb_flash_attention_train_host_workspace(int dtype, int batch, int q_heads,
                                                            int kv_heads, int seq_len,
                                                            int head_dim) {
-    if (check_attn(dtype, batch, q_heads, kv_heads, seq_len, head_dim) != EDB_OK) return 0;
-    const int units = batch * kv_heads;
-    return kSlots * attn_slot(dtype, attn_units_per_chunk(units), q_heads / kv_heads, seq_len,
-                              head_dim)
-                        .bytes();
+    return attn_workspace(ATTN_FLASH, dtype, batch, q_heads, kv_heads, seq_len, head_dim);
 }
 
 extern "C" int edb_flash_attention_train_host(int dtype, const void* q, const void* k,
@@ -425,8 +463,42 @@ extern "C" int edb_flash_attention_train_host(int dtype, const void* q, const vo
                                               int kv_heads, int seq_len, int head_dim,
                                               int causal, float scale, void* workspace,
                                               size_t workspace_bytes, void* stream) {
-    return run_attn(dtype, q, k, v, dO, o, dq, dk, dv, batch, q_heads, kv_heads, seq_len,
-                    head_dim, causal, scale, workspace, workspace_bytes, stream);
+    return run_attn(ATTN_FLASH, dtype, q, k, v, nullptr, dO, o, dq, dk, dv, nullptr, batch,
+                    q_heads, kv_heads, seq_len, head_dim, causal, scale, workspace,
+                    workspace_bytes, stream);
+}
+
+extern "C" size_t edb_fox_attention_train_host_workspace(int dtype, int batch, int q_heads,
+                                                         int kv_heads, int seq_len,
+                                                         int head_dim) {
+    return attn_workspace(ATTN_FOX, dtype, batch, q_heads, kv_heads, seq_len, head_dim);
+}
+
+extern "C" int edb_fox_attention_train_host(int dtype, const void* q, const void* k,
+                                            const void* v, const float* cs, const void* dO,
+                                            void* o, void* dq, void* dk, void* dv, float* dcs,
+                                            int batch, int q_heads, int kv_heads, int seq_len,
+                                            int head_dim, float scale, void* workspace,
+                                            size_t workspace_bytes, void* stream) {
+    return run_attn(ATTN_FOX, dtype, q, k, v, cs, dO, o, dq, dk, dv, dcs, batch, q_heads,
+                    kv_heads, seq_len, head_dim, 1, scale, workspace, workspace_bytes, stream);
+}
+
+extern "C" size_t edb_laser_attention_train_host_workspace(int dtype, int batch, int q_heads,
+                                                           int kv_heads, int seq_len,
+                                                           int head_dim) {
+    return attn_workspace(ATTN_LASER, dtype, batch, q_heads, kv_heads, seq_len, head_dim);
+}
+
+extern "C" int edb_laser_attention_train_host(int dtype, const void* q, const void* k,
+                                              const void* v, const void* dO, void* o, void* dq,
+                                              void* dk, void* dv, int batch, int q_heads,
+                                              int kv_heads, int seq_len, int head_dim,
+                                              int causal, float scale, void* workspace,
+                                              size_t workspace_bytes, void* stream) {
+    return run_attn(ATTN_LASER, dtype, q, k, v, nullptr, dO, o, dq, dk, dv, nullptr, batch,
+                    q_heads, kv_heads, seq_len, head_dim, causal, scale, workspace,
+                    workspace_bytes, stream);
 }
 
 extern "C" size_t edb_scan_train_host_workspace(int dtype, int batch, int seq_len, int hidden) {

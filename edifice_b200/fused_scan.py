@@ -621,6 +621,50 @@ def flash_attention_backward(q, k, v, causal, forward_out, grad_output, lse=None
     return dq, dk, dv
 
 
+def _attn_host(kind, q, k, v, cs, grad_output, causal, scale, out, device):
+    """Shared body of the three host-tensor attention entry points (kind: "flash",
+    "fox", "laser")."""
+    what = "%s_attention_train_host" % kind
+    for t in (q, k, v, cs, grad_output):
+        if t is not None and (t.is_cuda or not t.is_contiguous()):
+            raise _lib.EdbError("%s: inputs must be contiguous host tensors" % what)
+    B, Hq, Hkv, L, d = _attn_shapes(q, k, v)
+    _same(q.shape, grad_output.shape, what)
+    fox = kind == "fox"
+    if fox and (cs is None or tuple(cs.shape) != (B, Hq, L) or cs.dtype != torch.float32):
+        raise _lib.EdbError("%s: cs must be f32 [B, Hq, L]" % what)
+    want = [(q.shape, q.dtype), (q.shape, q.dtype), (k.shape, k.dtype), (v.shape, v.dtype)]
+    if fox:
+        want.append((cs.shape, torch.float32))
+    if out is None:
+        out = tuple(torch.empty(sh, dtype=dt, pin_memory=True) for sh, dt in want)
+    if len(out) != len(want):
+        raise _lib.EdbError("%s: expected %d outputs" % (what, len(want)))
+    for o_, (sh, dt) in zip(out, want):
+        if o_.is_cuda or not o_.is_contiguous() or o_.shape != sh or o_.dtype != dt:
+            raise _lib.EdbError("%s: outputs must be contiguous host tensors shaped like "
+                                "(q, q, k, v%s)" % (what, ", cs" if fox else ""))
+    device = torch.device(device if device is not None else "cuda")
+    code = _dtype_code(q, what)
+    lib = _lib.load()
+    sc = float(scale or 0.0)
+    with torch.cuda.device(device):
+        nbytes = getattr(lib, "edb_%s_attention_train_host_workspace" % kind)(code, B, Hq, Hkv,
+                                                                              L, d)
+        ws = _host_ws(device, nbytes)
+        if fox:
+            st = lib.edb_fox_attention_train_host(
+                code, _p(q), _p(k), _p(v), _p(cs), _p(grad_output), _p(out[0]), _p(out[1]),
+                _p(out[2]), _p(out[3]), _p(out[4]), B, Hq, Hkv, L, d, sc, _p(ws), nbytes,
+                _stream())
+        else:
+            st = getattr(lib, "edb_%s_attention_train_host" % kind)(
+                code, _p(q), _p(k), _p(v), _p(grad_output), _p(out[0]), _p(out[1]), _p(out[2]),
+                _p(out[3]), B, Hq, Hkv, L, d, int(bool(causal)), sc, _p(ws), nbytes, _stream())
+        _lib.check(st, "CUDA %s attention over host tensors" % kind)
+    return out
+
+
 def flash_attention_train_host(q, k, v, grad_output, causal=True, scale=None, out=None,
                                device=None):
     """Forward and backward of flash attention for host-resident q, k, v [B, Hq, L, d] /
@@ -629,32 +673,20 @@ def flash_attention_train_host(q, k, v, grad_output, causal=True, scale=None, ou
     (o, grad_q, grad_k, grad_v), written into ``out`` when given.  Asynchronous on the
     current stream of ``device``: synchronise it before reading the results.  Inputs
     and outputs should be pinned for the copies to overlap."""
-    what = "flash_attention_train_host"
-    for t in (q, k, v, grad_output):
-        if t.is_cuda or not t.is_contiguous():
-            raise _lib.EdbError("%s: inputs must be contiguous host tensors" % what)
-    B, Hq, Hkv, L, d = _attn_shapes(q, k, v)
-    _same(q.shape, grad_output.shape, what)
-    if out is None:
-        out = (torch.empty(q.shape, dtype=q.dtype, pin_memory=True),
-               torch.empty(q.shape, dtype=q.dtype, pin_memory=True),
-               torch.empty(k.shape, dtype=k.dtype, pin_memory=True),
-               torch.empty(v.shape, dtype=v.dtype, pin_memory=True))
-    for o_, ref in zip(out, (q, q, k, v)):
-        if o_.is_cuda or not o_.is_contiguous() or o_.shape != ref.shape or o_.dtype != ref.dtype:
-            raise _lib.EdbError("%s: outputs must be contiguous host tensors shaped like "
-                                "(q, q, k, v)" % what)
-    device = torch.device(device if device is not None else "cuda")
-    code = _dtype_code(q, what)
-    lib = _lib.load()
-    with torch.cuda.device(device):
-        nbytes = lib.edb_flash_attention_train_host_workspace(code, B, Hq, Hkv, L, d)
-        ws = _host_ws(device, nbytes)
-        _lib.check(lib.edb_flash_attention_train_host(
-            code, _p(q), _p(k), _p(v), _p(grad_output), _p(out[0]), _p(out[1]), _p(out[2]),
-            _p(out[3]), B, Hq, Hkv, L, d, int(bool(causal)), float(scale or 0.0), _p(ws), nbytes,
-            _stream()), "CUDA flash attention over host tensors")
-    return out
+    return _attn_host("flash", q, k, v, None, grad_output, causal, scale, out, device)
+
+
+def laser_attention_train_host(q, k, v, grad_output, causal=True, scale=None, out=None,
+                               device=None):
+    """LASER attention over host tensors, as flash_attention_train_host: returns
+    (o, grad_q, grad_k, grad_v) (v_max computed per (batch, kv head))."""
+    return _attn_host("laser", q, k, v, None, grad_output, causal, scale, out, device)
+
+
+def fox_attention_train_host(q, k, v, cs, grad_output, scale=None, out=None, device=None):
+    """FoX attention over host tensors, as flash_attention_train_host; cs f32
+    [B, Hq, L].  Returns (o, grad_q, grad_k, grad_v, grad_cs)."""
+    return _attn_host("fox", q, k, v, cs, grad_output, True, scale, out, device)
 
 
 class FlashAttentionFn(torch.autograd.Function):

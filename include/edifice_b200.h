@@ -332,6 +332,18 @@ int edb_laser_attention_bwd(int dtype, const void* q, const void* k, const void*
                             int q_heads, int kv_heads, int seq_len, int head_dim, int causal,
                             float scale, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Forward + backward of LASER attention for host-resident q, k, v, dO, as
+ * edb_flash_attention_train_host (v_max computed per unit, the residual kept on the
+ * device): returns o, dq, dk, dv in host memory. */
+size_t edb_laser_attention_train_host_workspace(int dtype, int batch, int q_heads,
+                                                int kv_heads, int seq_len, int head_dim);
+
+int edb_laser_attention_train_host(int dtype, const void* q, const void* k, const void* v,
+                                   const void* dO, void* o, void* dq, void* dk, void* dv,
+                                   int batch, int q_heads, int kv_heads, int seq_len,
+                                   int head_dim, int causal, float scale, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------
  * FoX attention (forgetting attention), always causal:
  *   S_ij = q_i.k_j scale + cs_i - cs_j (j <= i);  O = softmax(S) V
@@ -360,6 +372,18 @@ int edb_fox_attention_bwd(int dtype, const void* q, const void* k, const void* v
                           void* dq, void* dk, void* dv, float* dcs, int batch, int q_heads,
                           int kv_heads, int seq_len, int head_dim, float scale, void* workspace,
                           size_t workspace_bytes, void* stream);
+
+/* Forward + backward of FoX attention for host-resident q, k, v, cs (f32
+ * [B, Hq, L]) and dO, as edb_flash_attention_train_host: returns o, dq, dk, dv and
+ * dcs (f32) in host memory. */
+size_t edb_fox_attention_train_host_workspace(int dtype, int batch, int q_heads, int kv_heads,
+                                              int seq_len, int head_dim);
+
+int edb_fox_attention_train_host(int dtype, const void* q, const void* k, const void* v,
+                                 const float* cs, const void* dO, void* o, void* dq, void* dk,
+                                 void* dv, float* dcs, int batch, int q_heads, int kv_heads,
+                                 int seq_len, int head_dim, float scale, void* workspace,
+                                 size_t workspace_bytes, void* stream);
 
 /* Element-wise storage conversion of n values (EDB_F32 <-> EDB_BF16, or a copy);
  * the shims use it for the reference's io-typed cs arguments. */

@@ -477,3 +477,36 @@ def test_flash_attention_train_host(cuda, causal, B, Hq, Hkv, L, d):
         ref = ref.cpu().double()
         assert ((got.double() - ref).norm() / ref.norm()).item() <= 1e-3
     assert device_errors() == 0
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,L,d", [(2, 4, 2, 256, 128), (3, 8, 2, 384, 64)])
+def test_fox_and_laser_train_host(cuda, B, Hq, Hkv, L, d):
+    """FoX and LASER over host tensors (the same unit ring as flash attention)
+    against their device entry points on the same inputs."""
+    q, k, v, do = attn_inputs(B, Hq, Hkv, L, d, torch.bfloat16, seed=95 + L)
+    g = torch.Generator(device="cpu").manual_seed(96 + L)
+    cs = torch.cumsum(torch.nn.functional.logsigmoid(torch.randn(B, Hq, L, generator=g)), -1)
+    pin = [t.cpu().pin_memory() for t in (q, k, v, do)]
+    cs_p = cs.pin_memory()
+    cs = cs.cuda()
+    # FoX
+    got = fs.fox_attention_train_host(pin[0], pin[1], pin[2], cs_p, pin[3])
+    torch.cuda.synchronize()
+    o_r, lse = fs.fox_attention(q, k, v, cs, return_lse=True)
+    ref = (o_r,) + tuple(fs.fox_attention_backward(q, k, v, cs, o_r, do, lse))
+    torch.cuda.synchronize()
+    assert torch.equal(got[0], ref[0].cpu())
+    for a, r in zip(got[1:], ref[1:]):
+        r = r.cpu().double()
+        assert ((a.double() - r).norm() / r.norm()).item() <= 1e-3
+    # LASER
+    got = fs.laser_attention_train_host(*pin, causal=True)
+    torch.cuda.synchronize()
+    o_r, resid = fs.laser_attention(q, k, v, causal=True, return_resid=True)
+    ref = (o_r,) + tuple(fs.laser_attention_backward(q, k, v, do, resid, causal=True))
+    torch.cuda.synchronize()
+    assert torch.equal(got[0], ref[0].cpu())
+    for a, r in zip(got[1:], ref[1:]):
+        r = r.cpu().double()
+        assert ((a.double() - r).norm() / r.norm()).item() <= 1e-3
+    assert device_errors() == 0
