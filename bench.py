@@ -579,8 +579,11 @@ class SsmModelWorkload(SsmWorkload):
     def host_inputs(self):
         return [self.x, self.dt, self.B, self.C, self.dy]
 
-    e2e_outputs = None
-    e2e_host = None
+    def e2e_host(self, pin, outs):
+        """One fwd+bwd step over pinned host buffers through the host entry point
+        (batch-row chunks: copies overlapped with the kernels)."""
+        from edifice_b200 import fused_scan as fs
+        return fs.selective_scan_model_train_host(*pin, out=outs)
 
     def e2e_step(self, dev_in):
         from edifice_b200 import fused_scan as fs
@@ -588,8 +591,7 @@ class SsmModelWorkload(SsmWorkload):
         y, dtm, ck = fs.selective_scan_model(x, dt, B, C, with_ckpt=True)
         return (y,) + tuple(fs.selective_scan_model_backward(x, dt, B, C, dy, dtm, h_ckpt=ck))
 
-    api = ("edifice_b200.fused_scan.selective_scan_model + backward (whole-tensor copies "
-           "in the timed region)")
+    api = "edifice_b200.fused_scan.selective_scan_model_train_host (host tensors in and out)"
 
     def cpu_step(self, rows=None, prec="f32"):
         import numpy as np

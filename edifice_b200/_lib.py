@@ -34,6 +34,10 @@ SIGNATURES = {
     "edb_selective_scan_train_host_workspace": (_sz, [_i, _i, _i, _i, _i]),
     "edb_selective_scan_train_host": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                            _vp, _i, _i, _i, _i, _f, _f, _vp, _sz, _vp]),
+    "edb_selective_scan_model_train_host_workspace": (_sz, [_i, _i, _i, _i, _i]),
+    "edb_selective_scan_model_train_host": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                                 _vp, _vp, _vp, _i, _i, _i, _i, _f, _f, _vp,
+                                                 _sz, _vp]),
     "edb_selective_scan_ckpt_bytes": (_sz, [_i, _i, _i, _i]),
     "edb_selective_scan_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f,
                                     _f, _vp]),

@@ -196,16 +196,19 @@ int run(int op, int dtype, const void* x0, const void* x1, const void* h0, const
 constexpr size_t kSsmChunkTarget = 256u << 20;
 
 struct SsmSlot {
-    size_t td, tn, tf, ck, ws;  // [rows,L,D] io, [rows,L,N] io, [rows,L,N] f32, ckpt, bwd ws
-    size_t bytes() const { return 6 * td + 2 * tn + 2 * tf + ck + ws; }
+    // [rows,L,D] io, [rows,L,N] io, [rows,L,N] f32, ckpt, bwd ws, dt mean [rows,L] f32
+    // (model semantics)
+    size_t td, tn, tf, ck, ws, dm;
+    size_t bytes() const { return 6 * td + 2 * tn + 2 * tf + ck + ws + dm; }
 };
 
 int ssm_rows(int B, int L, int D, int es) {
     return chunk_rows(B, (size_t)L * D * es, kSsmChunkTarget);
 }
 
-SsmSlot ssm_slot(int rows, int L, int D, int N, int es) {
+SsmSlot ssm_slot(int rows, int L, int D, int N, int es, bool model = false) {
     SsmSlot g;
+    g.dm = model ? a256((size_t)rows * L * 4) : 0;
     g.td = a256((size_t)rows * L * D * es);
     g.tn = a256((size_t)rows * L * N * es);
     g.tf = a256((size_t)rows * L * N * 4);
@@ -221,16 +224,19 @@ int check_ssm(int dtype, int B, int L, int D, int N) {
     return EDB_OK;
 }
 
-int run_ssm(int dtype, const void* x, const void* dt, const void* A, const void* Bm,
-            const void* Cm, const void* dy, void* y, void* gx, void* gdt, float* gB, float* gC,
-            int B, int L, int D, int N, float dt_min, float dt_max, void* ws, size_t ws_bytes,
-            void* stream) {
+// model: the model semantics (edb_selective_scan_model_*); A may then be NULL (the
+// fixed -(n+1) diagonal).
+int run_ssm(bool model, int dtype, const void* x, const void* dt, const void* A,
+            const void* Bm, const void* Cm, const void* dy, void* y, void* gx, void* gdt,
+            float* gB, float* gC, int B, int L, int D, int N, float dt_min, float dt_max,
+            void* ws, size_t ws_bytes, void* stream) {
     if (int st = check_ssm(dtype, B, L, D, N)) return st;
-    if (!x || !dt || !A || !Bm || !Cm || !dy || !y || !gx || !gdt || !gB || !gC || !ws)
+    if (!x || !dt || (!A && !model) || !Bm || !Cm || !dy || !y || !gx || !gdt || !gB || !gC ||
+        !ws)
         return EDB_ERR_NULL_POINTER;
     const int es = dtype == EDB_BF16 ? 2 : 4;
     const int rows = ssm_rows(B, L, D, es);
-    const SsmSlot g = ssm_slot(rows, L, D, N, es);
+    const SsmSlot g = ssm_slot(rows, L, D, N, es, model);
     const size_t ab = a256((size_t)D * N * es);
     if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0) return EDB_ERR_MISALIGNED;
     if (ws_bytes < ab + kSlots * g.bytes()) return EDB_ERR_WORKSPACE_TOO_SMALL;
@@ -245,8 +251,8 @@ int run_ssm(int dtype, const void* x, const void* dt, const void* A, const void*
     join.armed = true;
 
     // A [D, N] is shared by every row: one copy ahead of the first chunk
-    void* dA = ws;
-    EDB_TRY(cudaMemcpyAsync(dA, A, (size_t)D * N * es, cudaMemcpyHostToDevice, r.sin));
+    void* dA = A ? ws : nullptr;
+    if (A) EDB_TRY(cudaMemcpyAsync(dA, A, (size_t)D * N * es, cudaMemcpyHostToDevice, r.sin));
 
     const int nchunks = (B + rows - 1) / rows;
     for (int i = 0; i < nchunks; ++i) {
@@ -265,6 +271,7 @@ int run_ssm(int dtype, const void* x, const void* dt, const void* A, const void*
         float* dgC = reinterpret_cast<float*>(p + 6 * g.td + 2 * g.tn + g.tf);
         float* dck = reinterpret_cast<float*>(p + 6 * g.td + 2 * g.tn + 2 * g.tf);
         void* dws = p + 6 * g.td + 2 * g.tn + 2 * g.tf + g.ck;
+        float* ddm = reinterpret_cast<float*>(p + 6 * g.td + 2 * g.tn + 2 * g.tf + g.ck + g.ws);
         const size_t offd = (size_t)r0 * L * D * es, nd = (size_t)nr * L * D * es;
         const size_t offn = (size_t)r0 * L * N * es, nn = (size_t)nr * L * N * es;
         const size_t offf = (size_t)r0 * L * N, nf = (size_t)nr * L * N * 4;
@@ -282,12 +289,22 @@ int run_ssm(int dtype, const void* x, const void* dt, const void* A, const void*
 
         // forward (writing the chunk-start states), then backward, on the caller's stream
         EDB_TRY(cudaStreamWaitEvent(s, r.in_fwd[slot], 0));
-        EDB_TRY_ST(edb_selective_scan_fwd(dtype, dx, ddt, dA, dB, dC, dyo, dck, nr, L, D, N,
-                                          dt_min, dt_max, s));
+        if (model)
+            EDB_TRY_ST(edb_selective_scan_model_fwd(dtype, dx, ddt, dA, dB, dC, dyo, ddm, dck, nr,
+                                                    L, D, N, dt_min, dt_max, s));
+        else
+            EDB_TRY_ST(edb_selective_scan_fwd(dtype, dx, ddt, dA, dB, dC, dyo, dck, nr, L, D, N,
+                                              dt_min, dt_max, s));
         EDB_TRY(cudaEventRecord(r.fwd[slot], s));
         EDB_TRY(cudaStreamWaitEvent(s, r.in[slot], 0));
-        EDB_TRY_ST(edb_selective_scan_bwd(dtype, dx, ddt, dA, dB, dC, ddy, dck, dgx, dgdt, dgB,
-                                          dgC, nr, L, D, N, dt_min, dt_max, dws, g.ws, s));
+        if (model)
+            EDB_TRY_ST(edb_selective_scan_model_bwd(dtype, dx, ddt, dA, dB, dC, ddy, ddm, dck, dgx,
+                                                    dgdt, dgB, dgC, nr, L, D, N, dt_min, dt_max,
+                                                    dws, g.ws, s));
+        else
+            EDB_TRY_ST(edb_selective_scan_bwd(dtype, dx, ddt, dA, dB, dC, ddy, dck, dgx, dgdt,
+                                              dgB, dgC, nr, L, D, N, dt_min, dt_max, dws, g.ws,
+                                              s));
         EDB_TRY(cudaEventRecord(r.comp[slot], s));
 
         // device -> host: y as soon as the forward is done, the gradients after
@@ -540,6 +557,27 @@ extern "C" int edb_selective_scan_train_host(int dtype, const void* x, const voi
                                              int d_inner, int d_state, float dt_min,
                                              float dt_max, void* workspace,
                                              size_t workspace_bytes, void* stream) {
-    return run_ssm(dtype, x, dt, A, B, C, dy, y, gx, gdt, gB, gC, batch, seq_len, d_inner,
-                   d_state, dt_min, dt_max, workspace, workspace_bytes, stream);
+    return run_ssm(false, dtype, x, dt, A, B, C, dy, y, gx, gdt, gB, gC, batch, seq_len,
+                   d_inner, d_state, dt_min, dt_max, workspace, workspace_bytes, stream);
+}
+
+extern "C" size_t edb_selective_scan_model_train_host_workspace(int dtype, int batch,
+                                                                int seq_len, int d_inner,
+                                                                int d_state) {
+    if (check_ssm(dtype, batch, seq_len, d_inner, d_state) != EDB_OK) return 0;
+    const int es = dtype == EDB_BF16 ? 2 : 4;
+    const int rows = ssm_rows(batch, seq_len, d_inner, es);
+    return a256((size_t)d_inner * d_state * es) +
+           kSlots * ssm_slot(rows, seq_len, d_inner, d_state, es, true).bytes();
+}
+
+extern "C" int edb_selective_scan_model_train_host(int dtype, const void* x, const void* dt,
+                                                   const void* A, const void* B, const void* C,
+                                                   const void* dy, void* y, void* gx, void* gdt,
+                                                   float* gB, float* gC, int batch, int seq_len,
+                                                   int d_inner, int d_state, float dt_min,
+                                                   float dt_max, void* workspace,
+                                                   size_t workspace_bytes, void* stream) {
+    return run_ssm(true, dtype, x, dt, A, B, C, dy, y, gx, gdt, gB, gC, batch, seq_len,
+                   d_inner, d_state, dt_min, dt_max, workspace, workspace_bytes, stream);
 }

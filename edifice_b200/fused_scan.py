@@ -372,6 +372,42 @@ def selective_scan_train_host(x, dt, a, b, c, grad_output, out=None, device=None
     return out
 
 
+def selective_scan_model_train_host(x, dt, b, c, grad_output, a=None, out=None,
+                                    device=None):
+    """Forward and backward of the model semantics (selective_scan_model) for
+    host-resident tensors, as selective_scan_train_host: batch-row chunks with the
+    copies overlapped with the kernels; ``a`` None is the model's fixed -(1..N)
+    diagonal.  Returns host tensors (y, grad_x, grad_dt, grad_B, grad_C)."""
+    what = "selective_scan_model_train_host"
+    for t in (x, dt, a, b, c, grad_output):
+        if t is not None and (t.is_cuda or not t.is_contiguous()):
+            raise _lib.EdbError("%s: inputs must be contiguous host tensors" % what)
+    Bsz, L, D, N = _model_shapes(x, a, b)
+    _same(x.shape, dt.shape, what)
+    _same(x.shape, grad_output.shape, what)
+    _same(b.shape, c.shape, what)
+    if out is None:
+        out = tuple(torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for _ in range(3)) + \
+            tuple(torch.empty((Bsz, L, N), dtype=torch.float32, pin_memory=True)
+                  for _ in range(2))
+    dts = (x.dtype,) * 3 + (torch.float32,) * 2
+    for o, want in zip(out, dts):
+        if o.is_cuda or not o.is_contiguous() or o.dtype != want:
+            raise _lib.EdbError("%s: outputs must be contiguous host tensors (y, gx, gdt in "
+                                "the input dtype, gB, gC f32)" % what)
+    device = torch.device(device if device is not None else "cuda")
+    code = _dtype_code(x, what)
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        nbytes = lib.edb_selective_scan_model_train_host_workspace(code, Bsz, L, D, N)
+        ws = _host_ws(device, nbytes)
+        _lib.check(lib.edb_selective_scan_model_train_host(
+            code, _p(x), _p(dt), _p(a), _p(b), _p(c), _p(grad_output), _p(out[0]), _p(out[1]),
+            _p(out[2]), _p(out[3]), _p(out[4]), Bsz, L, D, N, DT_MIN, DT_MAX, _p(ws), nbytes,
+            _stream()), "CUDA selective scan (model semantics) over host tensors")
+    return out
+
+
 def _model_shapes(x, a, b):
     Bsz, L, D = x.shape
     N = b.shape[2]

@@ -246,6 +246,19 @@ int edb_selective_scan_model_bwd(int dtype, const void* x, const void* dt, const
                                  int d_state, float dt_min, float dt_max, void* workspace,
                                  size_t workspace_bytes, void* stream);
 
+/* Forward + backward of the model semantics for host-resident tensors, as
+ * edb_selective_scan_train_host (A may be NULL: the fixed -(n+1) diagonal; the
+ * dt means stay on the device). */
+size_t edb_selective_scan_model_train_host_workspace(int dtype, int batch, int seq_len,
+                                                     int d_inner, int d_state);
+
+int edb_selective_scan_model_train_host(int dtype, const void* x, const void* dt, const void* A,
+                                        const void* B, const void* C, const void* dy, void* y,
+                                        void* gx, void* gdt, float* gB, float* gC, int batch,
+                                        int seq_len, int d_inner, int d_state, float dt_min,
+                                        float dt_max, void* workspace, size_t workspace_bytes,
+                                        void* stream);
+
 /* ------------------------------------------------------------------------
  * Scaled-dot-product attention, causal or full, with grouped KV heads (GQA).
  *   O = softmax(Q K^T * scale [+ -inf above the diagonal if causal]) V

@@ -260,6 +260,29 @@ def test_train_host_matches_device_path(cuda, dtype, shape):
     assert device_errors() == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(8, 200, 256, 16), (3, 77, 130, 5)])
+@pytest.mark.parametrize("given_a", [False, True])
+def test_model_train_host_matches_device_path(cuda, dtype, shape, given_a):
+    """The model semantics over pinned host tensors (the same row ring) equal the
+    device entry points on the whole batch bit for bit: the dt mean and its gradient
+    term reduce over channels only, so every batch row is independent."""
+    Bsz, L, D, N = shape
+    x, dt, A, Bm, Cm, dy = ssm_inputs(Bsz, L, D, N, dtype, seed=45)
+    a = A if given_a else None
+    y_r, dtm, ck = fs.selective_scan_model(x, dt, Bm, Cm, a=a, with_ckpt=True)
+    ref = (y_r,) + tuple(fs.selective_scan_model_backward(x, dt, Bm, Cm, dy, dtm, a=a,
+                                                          h_ckpt=ck))
+    pin = [t.cpu().pin_memory() for t in (x, dt, Bm, Cm, dy)]
+    a_p = A.cpu().pin_memory() if given_a else None
+    out = fs.selective_scan_model_train_host(*pin, a=a_p)
+    torch.cuda.synchronize()
+    for o, r in zip(out, ref):
+        assert o.dtype == r.dtype and o.shape == r.shape
+        assert torch.equal(o, r.cpu())
+    assert device_errors() == 0
+
+
 def test_train_host_rejects_device_tensors(cuda):
     x = torch.rand(1, 4, 8, device="cuda")
     A = torch.rand(8, 4, device="cuda")
