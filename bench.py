@@ -889,7 +889,15 @@ class DeltaWorkload(Workload):
     def host_inputs(self):
         return [self.q, self.k, self.v, self.beta, self.do]
 
-    e2e_host = None
+    def e2e_outputs(self):
+        return [tuple(t.shape) + (t.dtype,) for t in (self.q, self.q, self.k, self.v,
+                                                       self.beta)]
+
+    def e2e_host(self, pin, outs):
+        """One fwd+bwd step over pinned host buffers through the host entry point
+        (batch-row chunks, copies overlapped with the kernels)."""
+        from edifice_b200 import fused_scan as fs
+        return fs.delta_rule_train_host(pin[0], pin[1], pin[2], pin[3], pin[4], out=outs)
 
     def e2e_step(self, dev_in):
         from edifice_b200 import fused_scan as fs
@@ -897,8 +905,7 @@ class DeltaWorkload(Workload):
         o, ck = fs.delta_net_scan(q, k, v, beta, with_ckpt=True)
         return (o,) + tuple(fs.delta_rule_backward(q, k, v, beta, do, ck))
 
-    api = ("edifice_b200.fused_scan.delta_net_scan + delta_rule_backward (whole-tensor copies "
-           "in the timed region)")
+    api = "edifice_b200.fused_scan.delta_rule_train_host (host tensors in and out)"
 
     def extra(self, fwd_ms, bwd_ms):
         c = self.cfg
@@ -1045,14 +1052,22 @@ class GatedDeltaWorkload(DeltaWorkload):
     def host_inputs(self):
         return [self.q, self.k, self.v, self.beta, self.alpha, self.do]
 
+    def e2e_outputs(self):
+        return [tuple(t.shape) + (t.dtype,) for t in (self.q, self.q, self.k, self.v,
+                                                       self.beta, self.alpha)]
+
+    def e2e_host(self, pin, outs):
+        """One fwd+bwd step over pinned host buffers through the host entry point."""
+        from edifice_b200 import fused_scan as fs
+        return fs.gated_delta_net_train_host(*pin, out=outs)
+
     def e2e_step(self, dev_in):
         from edifice_b200 import fused_scan as fs
         q, k, v, beta, alpha, do = dev_in
         o, ck = fs.gated_delta_net_scan(q, k, v, beta, alpha, with_ckpt=True)
         return (o,) + tuple(fs.gated_delta_net_backward(q, k, v, beta, alpha, do, ck))
 
-    api = ("edifice_b200.fused_scan.gated_delta_net_scan + gated_delta_net_backward "
-           "(whole-tensor copies in the timed region)")
+    api = "edifice_b200.fused_scan.gated_delta_net_train_host (host tensors in and out)"
 
     def cpu_step(self, rows=None, prec="f32"):
         import numpy as np

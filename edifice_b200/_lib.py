@@ -77,6 +77,13 @@ SIGNATURES = {
     "edb_fox_attention_train_host_workspace": (_sz, [_i, _i, _i, _i, _i, _i]),
     "edb_fox_attention_train_host": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                           _i, _i, _i, _i, _i, _f, _vp, _sz, _vp]),
+    "edb_delta_rule_train_host_workspace": (_sz, [_i, _i, _i, _i, _i, _i]),
+    "edb_delta_rule_train_host": (_i, [_i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp,
+                                       _i, _i, _i, _i, _vp, _sz, _vp]),
+    "edb_gated_delta_net_train_host_workspace": (_sz, [_i, _i, _i, _i, _i, _i]),
+    "edb_gated_delta_net_train_host": (_i, [_i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp,
+                                            _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz,
+                                            _vp]),
     "edb_laser_attention_resid_bytes": (_sz, [_i, _i, _i, _i, _i, _i]),
     "edb_laser_attention_fwd": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
                                      _f, _vp]),

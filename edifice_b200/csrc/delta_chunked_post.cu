@@ -56,9 +56,12 @@ constexpr int OFF_TBT = OFF_R1, OFF_E = OFF_R1 + 2 * BOX_C;
 constexpr int OFF_DM = OFF_R4, OFF_DMT = OFF_R4 + 2 * BOX_C;
 constexpr int OFF_BS = OFF_R4 + 4 * BOX_C;  // beta [C]
 constexpr int OFF_GS = OFF_BS + C * 4;      // gated: g [C]
-constexpr int OFF_DG = OFF_GS + C * 4;      // gated: dg [C]
-constexpr int OFF_BAR = OFF_DG + C * 4;
+// gated: dg partials per warp [THREADS / 32][C], summed in a fixed order at the end
+// (no atomics: the gradient is the same bits every run)
+constexpr int OFF_DG = OFF_GS + C * 4;
+constexpr int OFF_BAR = OFF_DG + (THREADS / 32) * C * 4;
 constexpr int SMEM = OFF_BAR + 64;
+static_assert(SMEM <= 227 * 1024, "fits the per-CTA shared-memory limit");
 constexpr int PHASE_A_TX = 8 * BOX_D + 8 * BOX_C;  // S_0^T, dS_C^T, U~, dU~
 constexpr int TM_Q = 0, TM_W = 64, TM_K = 128, TM_M = 192, TM_DTB = 256, TM_V = 320,
               TM_COLS = 512;
@@ -99,7 +102,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     float* sc = reinterpret_cast<float*>(smem + OFF_R2);
     float* bs = reinterpret_cast<float*>(smem + OFF_BS);
     float* gs = reinterpret_cast<float*>(smem + OFF_GS);
-    float* dg = reinterpret_cast<float*>(smem + OFF_DG);
+    float* dgw = reinterpret_cast<float*>(smem + OFF_DG);
     uint64_t* bar_ld = reinterpret_cast<uint64_t*>(smem + OFF_BAR);  // [3] TMA groups
     uint64_t* bar_mma = bar_ld + 3;
     uint32_t* s_misc = reinterpret_cast<uint32_t*>(bar_mma + 1);  // [0] tmem, [1] abort
@@ -160,9 +163,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (tid < C)
         bs[tid] = tid < nvalid ? __bfloat162float(beta[((long long)b * L + t0 + tid) * H + h])
                                : 0.0f;
-    if (GATED && tid < C) {
-        gs[tid] = glg[ch * C + tid];
-        dg[tid] = 0.0f;
+    if (GATED) {
+        if (tid < C) gs[tid] = glg[ch * C + tid];
+        for (int i = tid; i < (THREADS / 32) * C; i += THREADS) dgw[i] = 0.0f;
     }
     constexpr int NT = C * C / 4 / THREADS;
     float4 tv[NT];
@@ -219,7 +222,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0 && warp > 0) atomicAdd(&dg[C - 1], __expf(gs[C - 1]) * acc);
+        if (lane == 0 && warp > 0) dgw[warp * C + C - 1] += __expf(gs[C - 1]) * acc;
         __syncthreads();  // the phase-A tiles are read: their space takes the next loads
     }
     if (tid == 0) {
@@ -400,13 +403,16 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) cs[cc] += __shfl_xor_sync(0xffffffffu, cs[cc], 16);
-            if (bq == 0) {
-#pragma unroll
-                for (int r = 0; r < 4; ++r) atomicAdd(&dg[4 * a + r], rs[r]);
-            }
+            // this warp's row of partials: column sums, then (other lanes, maybe the
+            // same entries) row sums
             if (lane < 16) {
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc) atomicAdd(&dg[4 * bq + cc], -cs[cc]);
+                for (int cc = 0; cc < 4; ++cc) dgw[warp * C + 4 * bq + cc] -= cs[cc];
+            }
+            __syncwarp();
+            if (bq == 0) {
+#pragma unroll
+                for (int r = 0; r < 4; ++r) dgw[warp * C + 4 * a + r] += rs[r];
             }
         }
         float2 acc[4][2];
@@ -486,11 +492,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int cc = 0; cc < 4; ++cc) cs[cc] += __shfl_xor_sync(0xffffffffu, cs[cc], 16);
                 if (lane < 16) {
 #pragma unroll
-                    for (int cc = 0; cc < 4; ++cc) atomicAdd(&dg[4 * bq + cc], -cs[cc]);
+                    for (int cc = 0; cc < 4; ++cc) dgw[warp * C + 4 * bq + cc] -= cs[cc];
                 }
+                __syncwarp();
                 if (bq == 0) {
 #pragma unroll
-                    for (int r = 0; r < 4; ++r) atomicAdd(&dg[4 * a + r], bs[4 * a + r] * p[r]);
+                    for (int r = 0; r < 4; ++r) dgw[warp * C + 4 * a + r] += bs[4 * a + r] * p[r];
                 }
             }
             __syncthreads();  // dA and dbT complete
@@ -636,7 +643,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) k1tot += __shfl_xor_sync(0xffffffffu, k1tot, o);
-        if (lane == 0) atomicAdd(&dg[C - 1], k1tot);
+        if (lane == 0) dgw[warp * C + C - 1] += k1tot;
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -650,21 +657,26 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int jj = 0; jj < D / 4; ++jj) acc += sc[t * DGP + 4 * jj + qq];
             acc += __shfl_xor_sync(0xffffffffu, acc, 1);
             acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-            if (qq == 0) atomicAdd(&dg[t], acc);
+            if (qq == 0) dgw[warp * C + t] += acc;
         }
         __syncthreads();
     }
     if (GATED && !s_misc[1] && warp < 2) {
         // dlog alpha_s = sum_{t >= s} dg_t (a reverse scan), dalpha_s = that / alpha_s
+        // dg_s: the warps' partials in a fixed order
         const int s = tid;
-        float acc = dg[s];
+        float acc = 0.0f;
+#pragma unroll
+        for (int w = 0; w < THREADS / 32; ++w) acc += dgw[w * C + s];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const float y = __shfl_down_sync(0xffffffffu, acc, o);
             if (lane + o < 32) acc += y;
         }
         if (warp == 0) {
-            float tail = dg[32 + lane];
+            float tail = 0.0f;
+#pragma unroll
+            for (int w = 0; w < THREADS / 32; ++w) tail += dgw[w * C + 32 + lane];
 #pragma unroll
             for (int o = 16; o >= 1; o >>= 1) tail += __shfl_xor_sync(0xffffffffu, tail, o);
             acc += tail;

@@ -1,5 +1,6 @@
 // host_pipeline.cu -- forward + backward of the diagonal scans (linear scan,
-// MinGRU), of the Mamba selective scan and of attention (flash, FoX, LASER) over
+// MinGRU), of the Mamba selective scan, of attention (flash, FoX, LASER) and of
+// the delta rule (DeltaNet, GatedDeltaNet) over
 // HOST-resident tensors: batch rows (attention: (batch, kv head) units) are streamed through a small ring of device slots so that the
 // host->device copies of chunk i+1, the kernels of chunk i and the
 // device->host copies of chunk i-1 run at the same time (the two copy
@@ -466,7 +467,236 @@ int run_attn(int op, int dtype, const void* q, const void* k, const void* v, con
     return EDB_OK;  // `join` makes the caller's stream wait for the last copies
 }
 
+// ------------------------------------------------------------ delta rule
+// DeltaNet / GatedDeltaNet: every [B, L, H, ...] tensor is contiguous per batch row
+// and a row's (b, h) recurrences are complete sub-problems, so chunks of rows go
+// through the same ring.  Each slot runs its chunk's kernels on a compute stream of
+// its own: a chunk's state passes (chunked form) or token recurrence (the other
+// forms) are serial chains over the sequence that occupy a fraction of the GPU,
+// so consecutive chunks' kernels overlap instead of queueing behind each other.
+size_t delta_row_elems(int L, int H, int d) { return (size_t)L * H * d; }
+
+struct DeltaSlot {
+    // [rows, L, H, d] io (q, k, v, dO, o, dq, dk, dv), beta and its gradient,
+    // alpha and its gradient (gated), the forward's residual, the scratch of the
+    // forward and of the backward (one after the other on the slot's stream)
+    size_t t, tb, ta, resid, ws;
+    size_t bytes() const { return 8 * t + 2 * tb + 2 * ta + resid + ws; }
+};
+
+// Whether the call takes the chunked tensor-core form (a forward workspace) or the
+// token recurrence.
+bool delta_chunked(bool gated, int dtype, int bpe, int L, int H, int d) {
+    return (gated ? edb_gated_delta_net_fwd_workspace(dtype, bpe, 1, L, H, d)
+                  : edb_delta_rule_fwd_workspace(dtype, bpe, 1, L, H, d)) > 0;
+}
+
+// The token recurrence's chunks are long serial chains (each about as long as the
+// whole batch's), so it takes at most one chunk per slot, all in flight at once;
+// the chunked form's chunks are short next to their copies.
+int delta_rows(bool gated, int dtype, int bpe, int B, int L, int H, int d) {
+    const int es = dtype == EDB_BF16 ? 2 : 4;
+    if (!delta_chunked(gated, dtype, bpe, L, H, d)) return (B + kSlots - 1) / kSlots;
+    return chunk_rows(B, delta_row_elems(L, H, d) * es, 64u << 20);
+}
+
+DeltaSlot delta_slot(bool gated, int dtype, int bpe, int rows, int L, int H, int d) {
+    const int es = dtype == EDB_BF16 ? 2 : 4;
+    DeltaSlot g{};
+    g.t = a256((size_t)rows * delta_row_elems(L, H, d) * es);
+    g.tb = a256((size_t)rows * L * H * (bpe ? d : 1) * es);
+    g.ta = gated ? a256((size_t)rows * L * H * es) : 0;
+    size_t fw, bw;
+    if (gated) {
+        g.resid = a256(edb_gated_delta_net_ckpt_bytes(dtype, bpe, rows, L, H, d));
+        fw = edb_gated_delta_net_fwd_workspace(dtype, bpe, rows, L, H, d);
+        bw = edb_gated_delta_net_bwd_workspace(dtype, bpe, rows, L, H, d, 1);
+    } else {
+        g.resid = a256(edb_delta_rule_ckpt_bytes(dtype, bpe, rows, L, H, d));
+        fw = edb_delta_rule_fwd_workspace(dtype, bpe, rows, L, H, d);
+        bw = edb_delta_rule_bwd_workspace(dtype, bpe, rows, L, H, d, 1);
+    }
+    g.ws = a256(fw > bw ? fw : bw);
+    return g;
+}
+
+int check_delta(int dtype, int B, int L, int H, int d) {
+    if (dtype != EDB_F32 && dtype != EDB_BF16) return EDB_ERR_BAD_DTYPE;
+    if (B <= 0 || L <= 0 || H <= 0 || d <= 0 || d > 128) return EDB_ERR_BAD_SHAPE;
+    return EDB_OK;
+}
+
+size_t delta_workspace(bool gated, int dtype, int bpe, int B, int L, int H, int d) {
+    if (check_delta(dtype, B, L, H, d) != EDB_OK) return 0;
+    return kSlots * delta_slot(gated, dtype, bpe, delta_rows(gated, dtype, bpe, B, L, H, d), L,
+                               H, d).bytes();
+}
+
+// The slots' compute streams, joined into the caller's stream on every exit path
+// once work was queued on them.
+struct SlotStreams {
+    cudaStream_t cs[kSlots] = {};
+    cudaEvent_t done[kSlots] = {};
+    cudaStream_t s = nullptr;
+    bool armed = false;
+    cudaError_t init(cudaStream_t caller) {
+        s = caller;
+        cudaError_t e;
+        for (int i = 0; i < kSlots; ++i) {
+            if ((e = cudaStreamCreateWithFlags(&cs[i], cudaStreamNonBlocking))) return e;
+            if ((e = cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming))) return e;
+        }
+        return cudaSuccess;
+    }
+    ~SlotStreams() {
+        for (int i = 0; i < kSlots; ++i) {
+            if (armed && cs[i] && done[i] && cudaEventRecord(done[i], cs[i]) == cudaSuccess)
+                cudaStreamWaitEvent(s, done[i], 0);
+            if (cs[i]) cudaStreamDestroy(cs[i]);
+            if (done[i]) cudaEventDestroy(done[i]);
+        }
+    }
+};
+
+// alpha / galpha: GatedDeltaNet when alpha is not null.
+int run_delta(int dtype, const void* q, const void* k, const void* v, const void* beta,
+              int bpe, const void* alpha, const void* dO, void* o, void* gq, void* gk, void* gv,
+              void* gbeta, void* galpha, int B, int L, int H, int d, void* ws, size_t ws_bytes,
+              void* stream) {
+    if (int st = check_delta(dtype, B, L, H, d)) return st;
+    const bool gated = alpha != nullptr;
+    if (!q || !k || !v || !beta || !dO || !o || !gq || !gk || !gv || !gbeta || !ws ||
+        (gated && !galpha))
+        return EDB_ERR_NULL_POINTER;
+    const int es = dtype == EDB_BF16 ? 2 : 4;
+    const int rows = delta_rows(gated, dtype, bpe, B, L, H, d);
+    const DeltaSlot g = delta_slot(gated, dtype, bpe, rows, L, H, d);
+    if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0) return EDB_ERR_MISALIGNED;
+    if (ws_bytes < kSlots * g.bytes()) return EDB_ERR_WORKSPACE_TOO_SMALL;
+
+    cudaStream_t s = (cudaStream_t)stream;
+    Res r;
+    EDB_TRY(r.init());
+    SlotStreams ss;
+    EDB_TRY(ss.init(s));
+    Join join{r, s};
+    EDB_TRY(cudaEventRecord(r.start, s));
+    EDB_TRY(cudaStreamWaitEvent(r.sin, r.start, 0));
+    EDB_TRY(cudaStreamWaitEvent(r.sout, r.start, 0));
+    for (int i = 0; i < kSlots; ++i) EDB_TRY(cudaStreamWaitEvent(ss.cs[i], r.start, 0));
+    join.armed = true;
+    ss.armed = true;
+
+    const int nchunks = (B + rows - 1) / rows;
+    for (int i = 0; i < nchunks; ++i) {
+        const int slot = i % kSlots;
+        cudaStream_t c = ss.cs[slot];
+        const int r0 = i * rows, nr = B - r0 < rows ? B - r0 : rows;
+        char* p = static_cast<char*>(ws) + slot * g.bytes();
+        void* dq_ = p;
+        void* dk_ = p + g.t;
+        void* dv_ = p + 2 * g.t;
+        void* ddo = p + 3 * g.t;
+        void* dout = p + 4 * g.t;
+        void* dgq = p + 5 * g.t;
+        void* dgk = p + 6 * g.t;
+        void* dgv = p + 7 * g.t;
+        void* dbeta = p + 8 * g.t;
+        void* dgbeta = p + 8 * g.t + g.tb;
+        void* dalpha = p + 8 * g.t + 2 * g.tb;
+        void* dgalpha = p + 8 * g.t + 2 * g.tb + g.ta;
+        float* dres = reinterpret_cast<float*>(p + 8 * g.t + 2 * g.tb + 2 * g.ta);
+        void* dws = p + 8 * g.t + 2 * g.tb + 2 * g.ta + g.resid;
+        const size_t row_t = delta_row_elems(L, H, d) * es;
+        const size_t row_b = (size_t)L * H * (bpe ? d : 1) * es, row_a = (size_t)L * H * es;
+        const size_t ot = r0 * row_t, nt = nr * row_t;
+        const size_t ob = r0 * row_b, nb = nr * row_b, oa = r0 * row_a, na = nr * row_a;
+
+        // host -> device once the slot's previous chunk has left: the forward's
+        // inputs, then dO
+        if (i >= kSlots) EDB_TRY(cudaStreamWaitEvent(r.sin, r.free_[slot], 0));
+        EDB_TRY(cudaMemcpyAsync(dq_, hp(q, ot), nt, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaMemcpyAsync(dk_, hp(k, ot), nt, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaMemcpyAsync(dv_, hp(v, ot), nt, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaMemcpyAsync(dbeta, hp(beta, ob), nb, cudaMemcpyHostToDevice, r.sin));
+        if (gated)
+            EDB_TRY(cudaMemcpyAsync(dalpha, hp(alpha, oa), na, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaEventRecord(r.in_fwd[slot], r.sin));
+        EDB_TRY(cudaMemcpyAsync(ddo, hp(dO, ot), nt, cudaMemcpyHostToDevice, r.sin));
+        EDB_TRY(cudaEventRecord(r.in[slot], r.sin));
+
+        // forward (leaving its residual), then backward, on the slot's stream
+        EDB_TRY(cudaStreamWaitEvent(c, r.in_fwd[slot], 0));
+        if (gated)
+            EDB_TRY_ST(edb_gated_delta_net_fwd_ws(dtype, dq_, dk_, dv_, dbeta, bpe, dalpha, dout,
+                                                  dres, nr, L, H, d, dws, g.ws, c));
+        else
+            EDB_TRY_ST(edb_delta_rule_fwd(dtype, dq_, dk_, dv_, dbeta, bpe, dout, dres, nr, L, H,
+                                          d, dws, g.ws, c));
+        EDB_TRY(cudaEventRecord(r.fwd[slot], c));
+        EDB_TRY(cudaStreamWaitEvent(c, r.in[slot], 0));
+        if (gated)
+            EDB_TRY_ST(edb_gated_delta_net_bwd(dtype, dq_, dk_, dv_, dbeta, bpe, dalpha, ddo, dres,
+                                               dgq, dgk, dgv, dgbeta, dgalpha, nr, L, H, d, dws,
+                                               g.ws, c));
+        else
+            EDB_TRY_ST(edb_delta_rule_bwd(dtype, dq_, dk_, dv_, dbeta, bpe, ddo, dres, dgq, dgk,
+                                          dgv, dgbeta, nr, L, H, d, dws, g.ws, c));
+        EDB_TRY(cudaEventRecord(r.comp[slot], c));
+
+        // device -> host: o once the forward is done, the gradients after the backward
+        EDB_TRY(cudaStreamWaitEvent(r.sout, r.fwd[slot], 0));
+        EDB_TRY(cudaMemcpyAsync(hq(o, ot), dout, nt, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaStreamWaitEvent(r.sout, r.comp[slot], 0));
+        EDB_TRY(cudaMemcpyAsync(hq(gq, ot), dgq, nt, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaMemcpyAsync(hq(gk, ot), dgk, nt, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaMemcpyAsync(hq(gv, ot), dgv, nt, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaMemcpyAsync(hq(gbeta, ob), dgbeta, nb, cudaMemcpyDeviceToHost, r.sout));
+        if (gated)
+            EDB_TRY(cudaMemcpyAsync(hq(galpha, oa), dgalpha, na, cudaMemcpyDeviceToHost, r.sout));
+        EDB_TRY(cudaEventRecord(r.free_[slot], r.sout));
+    }
+    return EDB_OK;  // `ss` and `join` make the caller's stream wait for the rest
+}
+
 }  // namespace
+
+extern "C" size_t edb_delta_rule_train_host_workspace(int dtype, int beta_per_element,
+                                                      int batch, int seq_len, int heads,
+                                                      int head_dim) {
+    return delta_workspace(false, dtype, beta_per_element, batch, seq_len, heads, head_dim);
+}
+
+extern "C" int edb_delta_rule_train_host(int dtype, const void* q, const void* k, const void* v,
+                                         const void* beta, int beta_per_element,
+                                         const void* dO, void* o, void* gq, void* gk, void* gv,
+                                         void* gbeta, int batch, int seq_len, int heads,
+                                         int head_dim, void* workspace, size_t workspace_bytes,
+                                         void* stream) {
+    return run_delta(dtype, q, k, v, beta, beta_per_element, nullptr, dO, o, gq, gk, gv, gbeta,
+                     nullptr, batch, seq_len, heads, head_dim, workspace, workspace_bytes,
+                     stream);
+}
+
+extern "C" size_t edb_gated_delta_net_train_host_workspace(int dtype, int beta_per_element,
+                                                           int batch, int seq_len, int heads,
+                                                           int head_dim) {
+    return delta_workspace(true, dtype, beta_per_element, batch, seq_len, heads, head_dim);
+}
+
+extern "C" int edb_gated_delta_net_train_host(int dtype, const void* q, const void* k,
+                                              const void* v, const void* beta,
+                                              int beta_per_element, const void* alpha,
+                                              const void* dO, void* o, void* gq, void* gk,
+                                              void* gv, void* gbeta, void* galpha, int batch,
+                                              int seq_len, int heads, int head_dim,
+                                              void* workspace, size_t workspace_bytes,
+                                              void* stream) {
+    if (!alpha) return EDB_ERR_NULL_POINTER;
+    return run_delta(dtype, q, k, v, beta, beta_per_element, alpha, dO, o, gq, gk, gv, gbeta,
+                     galpha, batch, seq_len, heads, head_dim, workspace, workspace_bytes,
+                     stream);
+}
 
 extern "C" size_t edb_flash_attention_train_host_workspace(int dtype, int batch, int q_heads,
                                                            int kv_heads, int seq_len,

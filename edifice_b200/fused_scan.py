@@ -544,6 +544,62 @@ class DeltaNetFn(torch.autograd.Function):
         return delta_rule_backward(q, k, v, beta, grad_output.contiguous(), ck)
 
 
+def _delta_host(q, k, v, beta, alpha, grad_output, out, device):
+    """Shared body of delta_rule_train_host / gated_delta_net_train_host."""
+    gated = alpha is not None
+    what = "gated_delta_net_train_host" if gated else "delta_rule_train_host"
+    for t in (q, k, v, beta, alpha, grad_output):
+        if t is not None and (t.is_cuda or not t.is_contiguous()):
+            raise _lib.EdbError("%s: inputs must be contiguous host tensors" % what)
+    B, L, H, d, per_el = _gated_shapes(q, k, v, beta, alpha) if gated else \
+        _delta_shapes(q, k, v, beta)
+    _same(q.shape, grad_output.shape, what)
+    want = [q, q, k, v, beta] + ([alpha] if gated else [])
+    if out is None:
+        out = tuple(torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in want)
+    if len(out) != len(want):
+        raise _lib.EdbError("%s: expected %d outputs" % (what, len(want)))
+    for o_, t in zip(out, want):
+        if o_.is_cuda or not o_.is_contiguous() or o_.shape != t.shape or o_.dtype != t.dtype:
+            raise _lib.EdbError("%s: outputs must be contiguous host tensors shaped like "
+                                "(q, q, k, v, beta%s)" % (what, ", alpha" if gated else ""))
+    device = torch.device(device if device is not None else "cuda")
+    code = _dtype_code(q, what)
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        if gated:
+            nbytes = lib.edb_gated_delta_net_train_host_workspace(code, per_el, B, L, H, d)
+            ws = _host_ws(device, nbytes)
+            st = lib.edb_gated_delta_net_train_host(
+                code, _p(q), _p(k), _p(v), _p(beta), per_el, _p(alpha), _p(grad_output),
+                _p(out[0]), _p(out[1]), _p(out[2]), _p(out[3]), _p(out[4]), _p(out[5]), B, L,
+                H, d, _p(ws), nbytes, _stream())
+        else:
+            nbytes = lib.edb_delta_rule_train_host_workspace(code, per_el, B, L, H, d)
+            ws = _host_ws(device, nbytes)
+            st = lib.edb_delta_rule_train_host(
+                code, _p(q), _p(k), _p(v), _p(beta), per_el, _p(grad_output), _p(out[0]),
+                _p(out[1]), _p(out[2]), _p(out[3]), _p(out[4]), B, L, H, d, _p(ws), nbytes,
+                _stream())
+        _lib.check(st, "CUDA %s over host tensors" % what)
+    return out
+
+
+def delta_rule_train_host(q, k, v, beta, grad_output, out=None, device=None):
+    """Forward and backward of the delta rule (DeltaNet) for host-resident q, k, v,
+    beta and grad_output: batch-row chunks stream through the device with the copies
+    overlapped with the kernels.  Returns host tensors (o, grad_q, grad_k, grad_v,
+    grad_beta), written into ``out`` when given.  Asynchronous on the current stream
+    of ``device``: synchronise it before reading the results."""
+    return _delta_host(q, k, v, beta, None, grad_output, out, device)
+
+
+def gated_delta_net_train_host(q, k, v, beta, alpha, grad_output, out=None, device=None):
+    """GatedDeltaNet over host tensors, as delta_rule_train_host; returns
+    (o, grad_q, grad_k, grad_v, grad_beta, grad_alpha)."""
+    return _delta_host(q, k, v, beta, alpha, grad_output, out, device)
+
+
 def _gated_shapes(q, k, v, beta, alpha):
     B, L, H, d, per_el = _delta_shapes(q, k, v, beta)
     if tuple(alpha.shape) != (B, L, H) or alpha.dtype != q.dtype:

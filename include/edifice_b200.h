@@ -512,6 +512,36 @@ int edb_gated_delta_net_bwd(int dtype, const void* q, const void* k, const void*
                             void* gbeta, void* galpha, int batch, int seq_len, int heads,
                             int head_dim, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Forward + backward of the delta rule / GatedDeltaNet for host-resident q, k, v,
+ * beta (, alpha) and dO (page-locked for the copies to overlap): returns o, gq, gk,
+ * gv, gbeta (, galpha) in host memory.  Batch rows stream through a ring of device
+ * slots in `workspace` (edb_{delta_rule,gated_delta_net}_train_host_workspace()
+ * bytes, 256-byte aligned) as in edb_selective_scan_train_host; each slot runs its
+ * chunk's forward (with residual) and backward on a stream of its own, so the
+ * chunks' serial recurrences overlap.  Results equal the device entry points on the
+ * whole batch.  The reference has no single entry point for it (a host-resident Nx
+ * caller round-trips around fused_delta_rule_scan_launch / _backward_launch,
+ * native/cuda/fused_delta_rule_scan.cu:213-258, fused_delta_rule_scan_backward.cu:
+ * 277-318). */
+size_t edb_delta_rule_train_host_workspace(int dtype, int beta_per_element, int batch,
+                                           int seq_len, int heads, int head_dim);
+
+int edb_delta_rule_train_host(int dtype, const void* q, const void* k, const void* v,
+                              const void* beta, int beta_per_element, const void* dO, void* o,
+                              void* gq, void* gk, void* gv, void* gbeta, int batch, int seq_len,
+                              int heads, int head_dim, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+size_t edb_gated_delta_net_train_host_workspace(int dtype, int beta_per_element, int batch,
+                                                int seq_len, int heads, int head_dim);
+
+int edb_gated_delta_net_train_host(int dtype, const void* q, const void* k, const void* v,
+                                   const void* beta, int beta_per_element, const void* alpha,
+                                   const void* dO, void* o, void* gq, void* gk, void* gv,
+                                   void* gbeta, void* galpha, int batch, int seq_len, int heads,
+                                   int head_dim, void* workspace, size_t workspace_bytes,
+                                   void* stream);
+
 /* Capacity of the library's built-in scratch array used by
  * edb_selective_scan_bwd_noalloc (16 MiB; every GPU that loads the library
  * holds it until the process exits). */

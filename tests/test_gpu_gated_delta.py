@@ -210,3 +210,21 @@ def test_chunked_gated_no_workspace_entry(cuda):
     torch.cuda.synchronize()
     assert torch.equal(o, o_ref)
     assert torch.equal(ck, ck_ref)
+
+
+@pytest.mark.parametrize("dtype,scalar_beta,d", [(torch.bfloat16, True, 128),
+                                                 (torch.bfloat16, False, 64)])
+def test_gated_train_host(cuda, dtype, scalar_beta, d):
+    """GatedDeltaNet over pinned host tensors (the delta rule's row ring) equals the
+    device entry points on the whole batch bit for bit."""
+    B, L, H = 5, 150, 2
+    q, k, v, beta, alpha, do = gated_inputs(B, L, H, d, dtype, seed=73, scalar_beta=scalar_beta)
+    o_r, ck = fs.gated_delta_net_scan(q, k, v, beta, alpha, with_ckpt=True)
+    ref = (o_r,) + tuple(fs.gated_delta_net_backward(q, k, v, beta, alpha, do, ck))
+    pin = [t.cpu().pin_memory() for t in (q, k, v, beta, alpha, do)]
+    out = fs.gated_delta_net_train_host(*pin)
+    torch.cuda.synchronize()
+    for o, r in zip(out, ref):
+        assert o.dtype == r.dtype and o.shape == r.shape
+        assert torch.equal(o, r.cpu())
+    assert device_errors() == 0
