@@ -219,3 +219,47 @@ def test_gated_chunked_form_sizes():
                                        L, H, d, None) == 1000
     assert lib.edb_gated_delta_net_fwd_ws(1, dummy, dummy, dummy, dummy, 0, dummy, dummy, None,
                                           B, L, H, d, None, 0, None) == 1004
+
+
+def test_host_tensor_entry_points_validate_on_host():
+    """The host-tensor pipelines reject bad arguments before any CUDA call: null
+    pointers, bad shapes (query heads not a multiple of kv heads), a workspace that
+    is too small or not 256-byte aligned."""
+    lib = edifice_b200.load()
+    d = ctypes.c_void_p(256)
+    odd = ctypes.c_void_p(272)
+    B, Hq, Hkv, L, hd = 2, 4, 2, 128, 64
+    for kind in ("flash", "laser"):
+        fn = getattr(lib, "edb_%s_attention_train_host" % kind)
+        need = getattr(lib, "edb_%s_attention_train_host_workspace" % kind)(1, B, Hq, Hkv, L, hd)
+        assert need > 0
+        assert getattr(lib, "edb_%s_attention_train_host_workspace" % kind)(1, B, 3, 2, L, hd) == 0
+        assert fn(1, None, d, d, d, d, d, d, d, B, Hq, Hkv, L, hd, 1, 0.0, d, need, None) == 1000
+        assert fn(1, d, d, d, d, d, d, d, d, B, 3, 2, L, hd, 1, 0.0, d, need, None) == 1001
+        assert fn(1, d, d, d, d, d, d, d, d, B, Hq, Hkv, L, hd, 1, 0.0, d, need - 1, None) == 1004
+        assert fn(1, d, d, d, d, d, d, d, d, B, Hq, Hkv, L, hd, 1, 0.0, odd, need, None) == 1003
+    need = lib.edb_fox_attention_train_host_workspace(1, B, Hq, Hkv, L, hd)
+    assert need > 0
+    # FoX: cs and dcs are required
+    assert lib.edb_fox_attention_train_host(1, d, d, d, None, d, d, d, d, d, d, B, Hq, Hkv, L,
+                                            hd, 0.0, d, need, None) == 1000
+    for gated in (False, True):
+        name = "gated_delta_net" if gated else "delta_rule"
+        need = getattr(lib, "edb_%s_train_host_workspace" % name)(1, 0, 4, 130, 2, 128)
+        assert need > 0
+        args = [1, d, d, d, d, 0] + ([d] if gated else []) + [d, d, d, d, d, d] + \
+            ([d] if gated else [])
+        fn = getattr(lib, "edb_%s_train_host" % name)
+        assert fn(*args, 4, 130, 2, 128, d, need - 1, None) == 1004
+        assert fn(*args, 4, 130, 2, 128, odd, need, None) == 1003
+        bad = list(args)
+        bad[1] = None
+        assert fn(*bad, 4, 130, 2, 128, d, need, None) == 1000
+    assert lib.edb_gated_delta_net_train_host(1, d, d, d, d, 0, None, d, d, d, d, d, d, d, 4,
+                                              130, 2, 128, d, 1 << 30, None) == 1000
+    need = lib.edb_selective_scan_model_train_host_workspace(1, 4, 64, 256, 16)
+    assert need > 0
+    # model semantics: A may be NULL (the fixed diagonal); a null x is refused
+    assert lib.edb_selective_scan_model_train_host(1, None, d, None, d, d, d, d, d, d, d, d, 4,
+                                                   64, 256, 16, 1e-3, 0.1, d, need,
+                                                   None) == 1000
