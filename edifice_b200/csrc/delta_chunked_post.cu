@@ -55,10 +55,11 @@ constexpr int OFF_DW = OFF_R1, OFF_DUT = OFF_R1 + 2 * BOX_D;
 constexpr int OFF_TBT = OFF_R1, OFF_E = OFF_R1 + 2 * BOX_C;
 constexpr int OFF_DM = OFF_R4, OFF_DMT = OFF_R4 + 2 * BOX_C;
 constexpr int OFF_BS = OFF_R4 + 4 * BOX_C;  // beta [C]
-constexpr int OFF_GS = OFF_BS + C * 4;      // gated: g [C]
+constexpr int OFF_GS = OFF_BS + C * 4;      // gated: g [C] in log2 units
+constexpr int OFF_GAM = OFF_GS + C * 4;     // gated: gamma [C]
 // gated: dg partials per warp [THREADS / 32][C], summed in a fixed order at the end
 // (no atomics: the gradient is the same bits every run)
-constexpr int OFF_DG = OFF_GS + C * 4;
+constexpr int OFF_DG = OFF_GAM + C * 4;
 constexpr int OFF_BAR = OFF_DG + (THREADS / 32) * C * 4;
 constexpr int SMEM = OFF_BAR + 64;
 static_assert(SMEM <= 227 * 1024, "fits the per-CTA shared-memory limit");
@@ -102,6 +103,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     float* sc = reinterpret_cast<float*>(smem + OFF_R2);
     float* bs = reinterpret_cast<float*>(smem + OFF_BS);
     float* gs = reinterpret_cast<float*>(smem + OFF_GS);
+    float* gam_s = reinterpret_cast<float*>(smem + OFF_GAM);
     float* dgw = reinterpret_cast<float*>(smem + OFF_DG);
     uint64_t* bar_ld = reinterpret_cast<uint64_t*>(smem + OFF_BAR);  // [3] TMA groups
     uint64_t* bar_mma = bar_ld + 3;
@@ -164,7 +166,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         bs[tid] = tid < nvalid ? __bfloat162float(beta[((long long)b * L + t0 + tid) * H + h])
                                : 0.0f;
     if (GATED) {
-        if (tid < C) gs[tid] = glg[ch * C + tid];
+        if (tid < C) {
+            // log2 units: every decay ratio below is one ex2
+            const float g2 = glg[ch * C + tid] * 1.4426950408889634f;
+            gs[tid] = g2;
+            gam_s[tid] = tc::ex2(g2);
+        }
         for (int i = tid; i < (THREADS / 32) * C; i += THREADS) dgw[i] = 0.0f;
     }
     constexpr int NT = C * C / 4 / THREADS;
@@ -222,7 +229,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0 && warp > 0) dgw[warp * C + C - 1] += __expf(gs[C - 1]) * acc;
+        if (lane == 0 && warp > 0) dgw[warp * C + C - 1] += gam_s[C - 1] * acc;
         __syncthreads();  // the phase-A tiles are read: their space takes the next loads
     }
     if (tid == 0) {
@@ -387,7 +394,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     rs[r] += pr;
                     cs[cc] += pr;
                     const int s2 = 4 * bq + cc;
-                    dmv[r][cc] = s2 <= t ? dmv[r][cc] * __expf(gs[t] - gs[s2]) : 0.0f;
+                    dmv[r][cc] = s2 <= t ? dmv[r][cc] * tc::ex2(gs[t] - gs[s2]) : 0.0f;
                 }
                 st4(reinterpret_cast<float*>(smem + OFF_DM + kmaj_off4(t, 4 * bq, C)),
                     make_float4(dmv[r][0], dmv[r][1], dmv[r][2], dmv[r][3]));
@@ -522,7 +529,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (GATED) {
                     // one of the two terms is nonzero: Gamma of the pair, later index first
                     const int t = 4 * a + r, s2 = 4 * bq + cc;
-                    dA[r][cc] *= __expf(t >= s2 ? gs[t] - gs[s2] : gs[s2] - gs[t]);
+                    dA[r][cc] *= tc::ex2(t >= s2 ? gs[t] - gs[s2] : gs[s2] - gs[t]);
                 }
             }
         }
@@ -602,8 +609,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     }
     if (GATED && !s_misc[1]) {
-        // thread (lane quarter, half) -> column j = TMEM lane, tokens t = 32 hf + 8 g + e
-        // (eight columns of each accumulator at a time); q_t[j], k_t[j] from the Q^T,
+        // thread (lane quarter, half) -> column j = TMEM lane, tokens t = 32 hf + 16 g + e
+        // (sixteen columns of each accumulator at a time); q_t[j], k_t[j] from the Q^T,
         // K^T tiles; the dg partial of (t, j) into scratch (the chain's, dead now)
         const int j = (warp & 3) * 32 + lane;
         const float gC = gs[C - 1];
@@ -612,20 +619,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         __nv_bfloat16* ov = gv + row0 + j;
         __nv_bfloat16* ok_ = gk + row0 + j;
 #pragma unroll 1
-        for (int g8 = 0; g8 < 4; ++g8) {
-            const uint32_t col = lane_base + hf * 32 + 8 * g8;
-            uint32_t xq[8], xq2[8], xv[8], xk1[8], xkb[8], xkw[8];
-            tc::tmem_ld8(tmem + TM_Q + col, xq);
-            tc::tmem_ld8(tmem + TM_Q2 + col, xq2);
-            tc::tmem_ld8(tmem + TM_V + col, xv);
-            tc::tmem_ld8(tmem + TM_K + col, xk1);
-            tc::tmem_ld8(tmem + TM_KB + col, xkb);
-            tc::tmem_ld8(tmem + TM_KW + col, xkw);
+        for (int g16 = 0; g16 < 2; ++g16) {
+            const uint32_t col = lane_base + hf * 32 + 16 * g16;
+            uint32_t xq[16], xq2[16], xv[16], xk1[16], xkb[16], xkw[16];
+            tc::tmem_ld16(tmem + TM_Q + col, xq);
+            tc::tmem_ld16(tmem + TM_Q2 + col, xq2);
+            tc::tmem_ld16(tmem + TM_V + col, xv);
+            tc::tmem_ld16(tmem + TM_K + col, xk1);
+            tc::tmem_ld16(tmem + TM_KB + col, xkb);
+            tc::tmem_ld16(tmem + TM_KW + col, xkw);
             tc::tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const int t = hf * 32 + 8 * g8 + e;
-                const float gam = __expf(gs[t]), kap = __expf(gC - gs[t]);
+            for (int e = 0; e < 16; ++e) {
+                const int t = hf * 32 + 16 * g16 + e;
+                const float gam = gam_s[t], kap = tc::ex2(gC - gs[t]);
                 const uint32_t to = (t & 3) * 4;
                 const float qv = *reinterpret_cast<const float*>(smem + OFF_QT + kmaj_off4(j, t & ~3, D) + to);
                 const float kv = *reinterpret_cast<const float*>(smem + OFF_KT + kmaj_off4(j, t & ~3, D) + to);
