@@ -139,6 +139,8 @@ def test_gated_autograd_fn(cuda):
 # bf16, one beta per (token, head), head_dim 128: the chunked tensor-core kernels
 # with the decay folded into the chunk products (tf32 operands, f32 accumulation).
 CHUNKED = [
+    (1, 1, 1),      # one token
+    (1, 65, 2),     # one token past a chunk
     (1, 64, 1),     # one full chunk
     (2, 130, 3),    # ragged last chunk
     (1, 300, 2),
