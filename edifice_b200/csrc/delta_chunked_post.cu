@@ -423,30 +423,56 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
         float2 acc[4][2];
-        // X' = T^T dT_b (T[t][s] = 0 for t < s); its diagonal is the dbeta term of T_b
+        {
+            // X' = T^T dT_b (T[t][s] = 0 for t < s): the rows of block a need t in
+            // [4a, 64), so warp w takes row blocks w and 15 - w (64 - 4w + 4 + 4w = 68
+            // steps in all, the same for every warp) and its half-warps each walk half
+            // of both ranges; one xor-16 round adds the halves.  Half 0 then owns
+            // block w, half 1 block 15 - w.  The diagonal of X' is dbeta's T_b term.
+            const int hh = lane >> 4;
+            const int aA = warp, aB = 15 - warp;
+            const int mA = 2 * aA + C / 2, mB = 2 * aB + C / 2;  // midpoints of [4a, 64)
+            float2 xa[4][2], xb[4][2];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) acc[r][0] = acc[r][1] = make_float2(0.0f, 0.0f);
-        for (int t = 4 * a; t < C; ++t) {
-            const float4 tt = ld4(Ts + t * PS + 4 * a), dd = ld4(Ds + t * PS + 4 * bq);
-            const float2 d01 = make_float2(dd.x, dd.y), d23 = make_float2(dd.z, dd.w);
-            const float tr[4] = {tt.x, tt.y, tt.z, tt.w};
+            for (int r = 0; r < 4; ++r)
+                xa[r][0] = xa[r][1] = xb[r][0] = xb[r][1] = make_float2(0.0f, 0.0f);
+            auto walk = [&](int blk, int t0, int t1, float2 (&x)[4][2]) {
+                for (int t = t0; t < t1; ++t) {
+                    const float4 tt = ld4(Ts + t * PS + 4 * blk), dd = ld4(Ds + t * PS + 4 * bq);
+                    const float2 d01 = make_float2(dd.x, dd.y), d23 = make_float2(dd.z, dd.w);
+                    const float tr[4] = {tt.x, tt.y, tt.z, tt.w};
 #pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                acc[r][0] = fma2(dup2(tr[r]), d01, acc[r][0]);
-                acc[r][1] = fma2(dup2(tr[r]), d23, acc[r][1]);
-            }
+                    for (int r = 0; r < 4; ++r) {
+                        x[r][0] = fma2(dup2(tr[r]), d01, x[r][0]);
+                        x[r][1] = fma2(dup2(tr[r]), d23, x[r][1]);
+                    }
+                }
+            };
+            walk(aA, hh ? mA : 4 * aA, hh ? C : mA, xa);
+            walk(aB, hh ? mB : 4 * aB, hh ? C : mB, xb);
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    xa[r][k].x += __shfl_xor_sync(0xffffffffu, xa[r][k].x, 16);
+                    xa[r][k].y += __shfl_xor_sync(0xffffffffu, xa[r][k].y, 16);
+                    xb[r][k].x += __shfl_xor_sync(0xffffffffu, xb[r][k].x, 16);
+                    xb[r][k].y += __shfl_xor_sync(0xffffffffu, xb[r][k].y, 16);
+                    acc[r][k] = hh ? xb[r][k] : xa[r][k];
+                }
         }
-        if (a == bq) {
-            dbT[4 * a] = acc[0][0].x;
-            dbT[4 * a + 1] = acc[1][0].y;
-            dbT[4 * a + 2] = acc[2][1].x;
-            dbT[4 * a + 3] = acc[3][1].y;
+        const int ax = lane >> 4 ? 15 - warp : warp;  // row block of this thread's X'
+        if (ax == bq) {
+            dbT[4 * ax] = acc[0][0].x;
+            dbT[4 * ax + 1] = acc[1][0].y;
+            dbT[4 * ax + 2] = acc[2][1].x;
+            dbT[4 * ax + 3] = acc[3][1].y;
         }
         __syncthreads();  // T is no longer read: X'^T goes in its place
-        st4(Ts + (4 * bq) * PS + 4 * a, make_float4(acc[0][0].x, acc[1][0].x, acc[2][0].x, acc[3][0].x));
-        st4(Ts + (4 * bq + 1) * PS + 4 * a, make_float4(acc[0][0].y, acc[1][0].y, acc[2][0].y, acc[3][0].y));
-        st4(Ts + (4 * bq + 2) * PS + 4 * a, make_float4(acc[0][1].x, acc[1][1].x, acc[2][1].x, acc[3][1].x));
-        st4(Ts + (4 * bq + 3) * PS + 4 * a, make_float4(acc[0][1].y, acc[1][1].y, acc[2][1].y, acc[3][1].y));
+        st4(Ts + (4 * bq) * PS + 4 * ax, make_float4(acc[0][0].x, acc[1][0].x, acc[2][0].x, acc[3][0].x));
+        st4(Ts + (4 * bq + 1) * PS + 4 * ax, make_float4(acc[0][0].y, acc[1][0].y, acc[2][0].y, acc[3][0].y));
+        st4(Ts + (4 * bq + 2) * PS + 4 * ax, make_float4(acc[0][1].x, acc[1][1].x, acc[2][1].x, acc[3][1].x));
+        st4(Ts + (4 * bq + 3) * PS + 4 * ax, make_float4(acc[0][1].y, acc[1][1].y, acc[2][1].y, acc[3][1].y));
         __syncthreads();
         // dA = -X' T_b^T, strictly lower (T_b[col][s] = 0 for s > col): only
         // blocks with b <= a are nonzero
