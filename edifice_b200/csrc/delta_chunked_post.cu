@@ -474,33 +474,65 @@ __global__ void __launch_bounds__(THREADS, 1)
         st4(Ts + (4 * bq + 2) * PS + 4 * ax, make_float4(acc[0][1].x, acc[1][1].x, acc[2][1].x, acc[3][1].x));
         st4(Ts + (4 * bq + 3) * PS + 4 * ax, make_float4(acc[0][1].y, acc[1][1].y, acc[2][1].y, acc[3][1].y));
         __syncthreads();
-        // dA = -X' T_b^T, strictly lower (T_b[col][s] = 0 for s > col): only
-        // blocks with b <= a are nonzero
+        // this thread's 4 x 4 block of K K^T (o Gamma, gated), in flight across dA
+        float4 g4[4];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) acc[r][0] = acc[r][1] = make_float2(0.0f, 0.0f);
-        if (bq <= a) {
-            for (int s = 0; s <= 4 * bq + 3; ++s) {
-                const float4 xv = ld4(Ts + s * PS + 4 * a), tb = ld4(Tb + s * PS + 4 * bq);
-                const float2 t01 = make_float2(tb.x, tb.y), t23 = make_float2(tb.z, tb.w);
-                const float xr[4] = {xv.x, xv.y, xv.z, xv.w};
+        for (int r = 0; r < 4; ++r) g4[r] = f4(Gg + (ch * C + 4 * a + r) * C + 4 * bq);
+        {
+            // dA = -X' T_b^T, strictly lower (T_b[col][s] = 0 for s > col): block
+            // (a, bq) is nonzero for bq <= a only and sums s in [0, 4 bq + 4).  Balanced
+            // as X' above (warp w: row blocks w and 15 - w, half-warps split each range),
+            // then masked, negated and written over dT_b (no longer read), from where
+            // every thread takes back its own (a, bq) block.
+            const int hh = lane >> 4;
+            const int aA = warp, aB = 15 - warp;
+            const int n = 4 * bq + 4, mid = 2 * bq + 2;
+            float2 ya[4][2], yb[4][2];
 #pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    acc[r][0] = fma2(dup2(xr[r]), t01, acc[r][0]);
-                    acc[r][1] = fma2(dup2(xr[r]), t23, acc[r][1]);
+            for (int r = 0; r < 4; ++r)
+                ya[r][0] = ya[r][1] = yb[r][0] = yb[r][1] = make_float2(0.0f, 0.0f);
+            auto walk = [&](int blk, float2 (&y)[4][2]) {
+                if (bq > blk) return;
+                for (int s2 = hh ? mid : 0; s2 < (hh ? n : mid); ++s2) {
+                    const float4 xv = ld4(Ts + s2 * PS + 4 * blk), tb = ld4(Tb + s2 * PS + 4 * bq);
+                    const float2 t01 = make_float2(tb.x, tb.y), t23 = make_float2(tb.z, tb.w);
+                    const float xr[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        y[r][0] = fma2(dup2(xr[r]), t01, y[r][0]);
+                        y[r][1] = fma2(dup2(xr[r]), t23, y[r][1]);
+                    }
                 }
+            };
+            walk(aA, ya);
+            walk(aB, yb);
+            const int ax = hh ? aB : aA;
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                float v4[4];
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    ya[r][k].x += __shfl_xor_sync(0xffffffffu, ya[r][k].x, 16);
+                    ya[r][k].y += __shfl_xor_sync(0xffffffffu, ya[r][k].y, 16);
+                    yb[r][k].x += __shfl_xor_sync(0xffffffffu, yb[r][k].x, 16);
+                    yb[r][k].y += __shfl_xor_sync(0xffffffffu, yb[r][k].y, 16);
+                    const float2 y2 = hh ? yb[r][k] : ya[r][k];
+                    v4[2 * k] = y2.x;
+                    v4[2 * k + 1] = y2.y;
+                }
+                float m[4];
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) m[cc] = 4 * bq + cc < 4 * ax + r ? -v4[cc] : 0.0f;
+                st4(Ds + (4 * ax + r) * PS + 4 * bq, make_float4(m[0], m[1], m[2], m[3]));
             }
         }
+        __syncthreads();  // dA complete in Ds
         float dA[4][4];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-            const float v4[4] = {acc[r][0].x, acc[r][0].y, acc[r][1].x, acc[r][1].y};
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) dA[r][cc] = 4 * bq + cc < 4 * a + r ? -v4[cc] : 0.0f;
+            const float4 v = ld4(Ds + (4 * a + r) * PS + 4 * bq);
+            dA[r][0] = v.x, dA[r][1] = v.y, dA[r][2] = v.z, dA[r][3] = v.w;
         }
-        // dT_b is no longer read (its last reader was X'): dA goes in its place
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-            st4(Ds + (4 * a + r) * PS + 4 * bq, make_float4(dA[r][0], dA[r][1], dA[r][2], dA[r][3]));
         // dbeta_t = sum_s dT_b[t][s]-term (diagonal of X') + sum_{s<t} dA[t][s] (K K^T)[t][s]
         {
             // gated: G holds K K^T o Gamma below the diagonal, A = diag(beta) G there;
@@ -508,7 +540,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             float p[4], cs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
-                const float4 g = f4(Gg + (ch * C + 4 * a + r) * C + 4 * bq);
+                const float4 g = g4[r];
                 p[r] = dA[r][0] * g.x + dA[r][1] * g.y + dA[r][2] * g.z + dA[r][3] * g.w;
                 if (GATED) {
                     const float bt = bs[4 * a + r];
